@@ -1,0 +1,363 @@
+"""Decode tokens/s of the cuda-b200 plugin (Llama hot path), one JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload tinyllama-bf16-bs1]
+
+Workload (default): TinyLlama-1.1B shape, bf16 weights, random init, batch 1,
+128-token prompt then greedy decode with a 384-row KV cache (the reference's
+``context = prompt + 256`` rule).  A *step* is one decode step (one token).
+With N GPUs (torchrun, one process per GPU) every rank decodes its own
+sequence: independent replicas, weak scaling, no collective on the data path.
+
+Reported:
+  value      device-resident decode: the captured decode graph replayed K
+             times with the next step's inputs written on the device from the
+             previous argmax (no host round trip), CUDA-event timed, max over
+             ranks;  value = N * K / time.
+  e2e        the reference's own loop through the public API: per step build
+             the host inputs, device.array(...) them, program.run(bindings),
+             device.argmax(logits) -- host<->device copies inside the timing.
+  roofline   the fused gate/up GEMV (largest weight stream) timed alone over
+             all layers' weights (> L2), vs the measured HBM copy bandwidth;
+             step_roofline: weight+KV bytes per token x tokens/s vs the same.
+  cpu_baseline  the parity oracle (restated reference cpu compiler, NumPy +
+             ml_dtypes) timing real decode steps of the same model on the host.
+Inputs are larger than L2 (2.07 GB of weights per step), so no flush is needed.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from pathlib import Path
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "chomik-grad_b200", ROOT):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
+
+METRIC = "decode tokens/sec (bs=1) and % of HBM roofline"
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+
+
+def measured_peaks():
+    try:
+        data = json.loads(PEAKS.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def dist_setup(gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def reduce_max(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    import torch
+
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def weight_bytes(config, itemsize: int) -> int:
+    from cuda_b200.frontend.llama import required_weight_shapes
+
+    total = sum(int(np.prod(s)) for n, s in required_weight_shapes(config).items()
+                if n != "model.embed_tokens.weight")
+    return total * itemsize
+
+
+def cpu_baseline(wl, weights, budget_s: float = 25.0):
+    """Oracle decode steps of the same model on host cores (bounded sample)."""
+    from oracle import numpy_compiler
+
+    numpy_compiler.install()
+    from cuda_b200.runtime import LlamaRuntime
+
+    cfg = wl.config
+    rt = LlamaRuntime(cfg, weights, compiler="cpu")
+    context = wl.context
+    shape = (1, cfg.num_key_value_heads, context, cfg.head_size)
+    caches = [np.zeros(shape, np.float32) for _ in range(2 * cfg.num_hidden_layers)]
+    position = wl.prompt_tokens
+    times = []
+    started = time.perf_counter()
+    token = 1
+    while True:
+        t0 = time.perf_counter()
+        logits, caches = rt.decode(token, position, context, caches)
+        token = rt.device.argmax(logits)
+        times.append(time.perf_counter() - t0)
+        position += 1
+        if time.perf_counter() - started > budget_s or len(times) >= 50:
+            break
+    warm = times[1:] if len(times) > 1 else times
+    per_token = statistics.median(warm)
+    return {"value": 1.0 / per_token, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{len(times)} decode steps (first excluded if >1) of {wl.name} at context "
+                      f"{context} through the restated reference cpu compiler (NumPy {np.__version__}, "
+                      f"ml_dtypes bf16 matmuls run single-threaded); {os.cpu_count()} host cores present",
+            "seconds_per_token": per_token}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from cuda_b200.models import WORKLOADS, synthetic_weights
+
+    wl = WORKLOADS[args.workload]
+    weights = synthetic_weights(wl.config, dtype=wl.np_dtype)
+    budget = float(os.environ.get("CB_REFERENCE_BUDGET_S", "150"))
+    base = cpu_baseline(wl, weights, budget_s=budget)
+    line = {
+        "metric": METRIC, "value": base["value"], "unit": "tokens/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * base["seconds_per_token"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": wl.name, "model": "TinyLlama-1.1B-shape (random init)", "global_batch": 1,
+                   "prompt_tokens": wl.prompt_tokens, "context": wl.context},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def gemv_roofline(program, rounds: int = 20):
+    """Average duration of the fused gate/up GEMV, all layers' weights in turn."""
+    import torch
+
+    from cuda_b200 import _lib
+
+    steps = [s for s in program.plan.steps if s.name == "gemv" and s.args["epilogue"] == _lib.EPI_SILU_MUL]
+    stream = program.device.stream()
+    for s in steps:
+        program._step_gemv(s, stream)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(rounds):
+        for s in steps:
+            program._step_gemv(s, stream)
+    end.record()
+    end.synchronize()
+    per_launch_ms = start.elapsed_time(end) / (rounds * len(steps))
+    nbytes = sum(v.buf.size * v.dtype.itemsize for v in steps[0].args["weights"])
+    return nbytes, per_launch_ms, len(steps)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    parser.add_argument("--workload", default="tinyllama-bf16-bs1")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+
+    rank, world, local = dist_setup(args.gpus)
+    import cuda_b200  # noqa: F401
+    from cuda_b200.models import WORKLOADS, synthetic_prompt, synthetic_weights
+    from cuda_b200.runtime import LlamaRuntime
+
+    wl = WORKLOADS[args.workload]
+    cfg = wl.config
+    weights = synthetic_weights(cfg, dtype=wl.np_dtype)
+    rt = LlamaRuntime(cfg, weights, compiler="cuda-b200")
+    prompt = list(synthetic_prompt(cfg, wl.prompt_tokens, seed=rank)[0])
+    context = wl.context
+    start_pos = len(prompt)
+    per_chunk = context - start_pos - 2  # decode steps available per pass over the cache
+
+    logits, caches = rt.prefill(prompt, context)
+    first = rt.device.argmax(logits)
+    program, nodes = rt.decode_program(context, caches, first, start_pos)
+
+    # ---- value: device-resident decode (graph replays, device-side inputs) ----
+    def device_pass(n_steps: int):
+        return rt.decode_on_device(first, start_pos, context, caches, n_steps + 1, timed=True)
+
+    device_pass(min(args.warmup, per_chunk))
+    barrier(world)
+    elapsed_ms, done = 0.0, 0
+    with ClockSampler(local) as clocks:
+        while done < args.steps:
+            n = min(per_chunk, args.steps - done)
+            _, ms = device_pass(n)
+            elapsed_ms += ms
+            done += n
+    barrier(world)
+    slowest = reduce_max(elapsed_ms, world)
+    tokens_total = args.steps * world
+    value = tokens_total / (slowest / 1000.0)
+
+    # ---- e2e: the reference's host loop through the public API ----
+    def host_steps(n: int):
+        nonlocal caches
+        token, position = first, start_pos
+        for _ in range(n):
+            out, caches = rt.decode(token, position, context, caches)
+            token = rt.device.argmax(out)
+            position += 1
+            if position >= context - 1:
+                token, position = first, start_pos
+
+    host_steps(args.warmup)
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    host_steps(args.steps)
+    t1.record()
+    t1.synchronize()
+    e2e_ms = reduce_max(t0.elapsed_time(t1), world)
+    e2e_value = tokens_total / (e2e_ms / 1000.0)
+    host = rt.step_inputs(first, start_pos, context)
+    h2d = int(sum(a.nbytes for a in host))
+    d2h = 16
+
+    # ---- roofline of the dominant kernel and of the whole step ----
+    gemv_bytes, gemv_ms, gemv_layers = gemv_roofline(program)
+    peak, peak_kind = measured_peaks()
+    achieved = gemv_bytes / (gemv_ms / 1000.0) / 1e9
+    itemsize = wl.np_dtype.itemsize
+    avg_ctx = start_pos + min(args.steps, per_chunk) / 2
+    kv_bytes = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * 4 * context
+    step_bytes = weight_bytes(cfg, itemsize) + cfg.hidden_size * itemsize + kv_bytes
+    step_gbs = step_bytes * (value / world) / 1e9
+
+    launches_per_step = len(program.plan.steps) + 1  # + cb_decode_advance
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": slowest / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02), uniform random prompt ids)",
+        "config": {"workload": wl.name, "model": "TinyLlama-1.1B-shape", "global_batch": world,
+                   "seq_len": context, "prompt_tokens": wl.prompt_tokens, "kv_cache": "float32",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (2.07 GB weights per step)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel": f"cb_gemv silu_mul (gate/up {gemv_bytes / 1e6:.1f} MB per launch, "
+                               f"{gemv_layers} layers cycled)", "peak_source": peak_kind},
+        "step_roofline": {"bytes_per_token": step_bytes, "achieved": step_gbs, "peak": peak,
+                          "unit": "GB/s", "frac": step_gbs / peak, "avg_context": avg_ctx},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, weights).items()
+                                if k in ("value", "unit", "cores", "kind", "sample")}
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

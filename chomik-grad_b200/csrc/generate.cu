@@ -1,0 +1,48 @@
+// On-device greedy decode driver: advances the per-step inputs of a decode
+// program (token ids, position, attention mask, cache write mask) from the
+// previous step's argmax, so K decode steps can be replayed back to back
+// without a host round trip per token.  It writes exactly what the host loop
+// of generate_tinyllama.py:772-786 builds for the next step.
+#include "common.cuh"
+
+namespace cb {
+namespace {
+
+__global__ void decode_advance_kernel(const long long* argmax, void* ids, int ids_dtype, void* position,
+                                      int position_dtype, void* mask, int mask_dtype, void* write_mask,
+                                      int write_mask_dtype, long long context, long long* token_log,
+                                      long long step, int* error_flag) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const long long token = argmax[0];
+  const long long pos = load_index(position, 0, position_dtype);
+  const long long next = pos + 1;
+  if (token_log != nullptr) token_log[step] = token;
+  if (next >= context || pos < 0) {
+    if (error_flag != nullptr) atomicExch(error_flag, 3);
+    return;
+  }
+  if (ids_dtype == CB_I64) static_cast<long long*>(ids)[0] = token;
+  else static_cast<int32_t*>(ids)[0] = static_cast<int32_t>(token);
+  if (position_dtype == CB_I64) static_cast<long long*>(position)[0] = next;
+  else static_cast<int32_t*>(position)[0] = static_cast<int32_t>(next);
+  store_from_f32(mask, next, mask_dtype, 0.0f);
+  store_from_f32(write_mask, pos, write_mask_dtype, 0.0f);
+  store_from_f32(write_mask, next, write_mask_dtype, 1.0f);
+}
+
+}  // namespace
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" int cb_decode_advance(const long long* argmax, void* ids, int ids_dtype, void* position,
+                                 int position_dtype, void* mask, int mask_dtype, void* write_mask,
+                                 int write_mask_dtype, long long context, long long* token_log,
+                                 long long step, int* error_flag, cb_stream_t stream) {
+  CB_REQUIRE(ids_dtype == CB_I32 || ids_dtype == CB_I64, "decode advance: ids must be int32/int64");
+  CB_REQUIRE(position_dtype == CB_I32 || position_dtype == CB_I64, "decode advance: bad position dtype");
+  decode_advance_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      argmax, ids, ids_dtype, position, position_dtype, mask, mask_dtype, write_mask, write_mask_dtype,
+      context, token_log, step, error_flag);
+  return check_launch("cb_decode_advance");
+}

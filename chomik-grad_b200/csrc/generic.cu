@@ -1,0 +1,297 @@
+// Generic six-op kernels: fused elementwise, reductions, strided copies,
+// gather and row argmax.  These carry any graph the plugin cannot pattern-
+// match; the Llama hot path uses the fused kernels in gemv.cu/attention.cu.
+#include "common.cuh"
+
+namespace cb {
+namespace {
+
+constexpr int kThreads = 256;
+
+inline int grid_for(long long n, int per_block = kThreads) {
+  long long blocks = (n + per_block - 1) / per_block;
+  long long cap = static_cast<long long>(sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+__device__ __forceinline__ float apply_op(int op, float a, float b) {
+  switch (op) {
+    case CB_OP_ADD: return __fadd_rn(a, b);
+    case CB_OP_SUB: return __fsub_rn(a, b);
+    case CB_OP_MUL: return __fmul_rn(a, b);
+    case CB_OP_DIV: return __fdiv_rn(a, b);
+    case CB_OP_EQUAL: return a == b ? 1.0f : 0.0f;
+    case CB_OP_NEG: return -a;
+    case CB_OP_EXP: return expf(a);
+    case CB_OP_LOG: return logf(a);
+    case CB_OP_SQRT: return __fsqrt_rn(a);
+    case CB_OP_RELU: return (a >= 0.0f || a != a) ? a : 0.0f;  // np.maximum(a, 0)
+    case CB_OP_STEP: return a > 0.0f ? 1.0f : 0.0f;
+    default: return 0.0f;
+  }
+}
+
+__global__ void elementwise_kernel(const cb_elementwise_args a, long long total) {
+  float reg[CB_EW_MAX_INPUTS + CB_EW_MAX_INSTR];
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long offs[CB_EW_MAX_INPUTS];
+    for (int j = 0; j < a.n_inputs; ++j) offs[j] = a.in_offset[j];
+    long long rest = i;
+    for (int d = a.ndim - 1; d >= 0; --d) {
+      const long long c = rest % a.shape[d];
+      rest /= a.shape[d];
+      for (int j = 0; j < a.n_inputs; ++j) offs[j] += c * a.in_strides[j][d];
+    }
+    for (int j = 0; j < a.n_inputs; ++j) reg[j] = load_as_f32(a.inputs[j], offs[j], a.in_dtype[j]);
+    float result = reg[0];
+    for (int t = 0; t < a.n_instr; ++t) {
+      result = round_to(apply_op(a.op[t], reg[a.lhs[t]], a.rhs[t] >= 0 ? reg[a.rhs[t]] : 0.0f),
+                        a.round[t]);
+      reg[a.n_inputs + t] = result;
+    }
+    store_from_f32(a.out, i, a.out_dtype, result);
+  }
+}
+
+__device__ __forceinline__ float nan_max(float a, float b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  return fmaxf(a, b);
+}
+
+__device__ __forceinline__ long long red_offset(const cb_reduce_args& a, long long r) {
+  long long off = 0;
+  for (int d = a.n_red - 1; d >= 0; --d) {
+    const long long c = r % a.red_shape[d];
+    r /= a.red_shape[d];
+    off += c * a.red_strides[d];
+  }
+  return off;
+}
+
+__device__ __forceinline__ long long keep_offset(const cb_reduce_args& a, long long o) {
+  long long off = a.in_offset;
+  for (int d = a.n_keep - 1; d >= 0; --d) {
+    const long long c = o % a.keep_shape[d];
+    o /= a.keep_shape[d];
+    off += c * a.keep_strides[d];
+  }
+  return off;
+}
+
+// One thread per output, accumulating in index order (NumPy's reduce loop for
+// non-native float types rounds the accumulator after every add).
+__global__ void reduce_sequential_kernel(const cb_reduce_args a, long long n_out, long long n_red) {
+  for (long long o = blockIdx.x * (long long)blockDim.x + threadIdx.x; o < n_out;
+       o += (long long)gridDim.x * blockDim.x) {
+    const long long base = keep_offset(a, o);
+    float acc = load_as_f32(a.in, base + red_offset(a, 0), a.in_dtype);
+    for (long long r = 1; r < n_red; ++r) {
+      const float v = load_as_f32(a.in, base + red_offset(a, r), a.in_dtype);
+      acc = a.kind == CB_REDUCE_SUM ? round_to(__fadd_rn(acc, v), a.acc_dtype) : nan_max(acc, v);
+    }
+    store_from_f32(a.out, o, a.out_dtype, acc);
+  }
+}
+
+// One warp per output, tree order (float32 sums; any max).
+__global__ void reduce_warp_kernel(const cb_reduce_args a, long long n_out, long long n_red) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long o = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); o < n_out;
+       o += warps) {
+    const long long base = keep_offset(a, o);
+    float acc = a.kind == CB_REDUCE_SUM ? 0.0f : -INFINITY;
+    for (long long r = lane; r < n_red; r += 32) {
+      const float v = load_as_f32(a.in, base + red_offset(a, r), a.in_dtype);
+      acc = a.kind == CB_REDUCE_SUM ? acc + v : nan_max(acc, v);
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      const float other = __shfl_xor_sync(0xffffffffu, acc, s);
+      acc = a.kind == CB_REDUCE_SUM ? acc + other : nan_max(acc, other);
+    }
+    if (lane == 0) store_from_f32(a.out, o, a.out_dtype, acc);
+  }
+}
+
+struct CopyShape {
+  long long shape[CB_MAX_DIMS];
+  long long strides[CB_MAX_DIMS];
+};
+
+template <typename T>
+__global__ void copy_strided_kernel(const T* in, T* out, int ndim, CopyShape s, long long total) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long rest = i, off = 0;
+    for (int d = ndim - 1; d >= 0; --d) {
+      const long long c = rest % s.shape[d];
+      rest /= s.shape[d];
+      off += c * s.strides[d];
+    }
+    out[i] = in[off];
+  }
+}
+
+template <typename T>
+__global__ void gather_kernel(const T* table, long long rows, long long row_units, const void* idx,
+                              int idx_dtype, long long n, T* out, int* error_flag) {
+  const long long total = n * row_units;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long which = i / row_units;
+    const long long unit = i - which * row_units;
+    long long row = load_index(idx, which, idx_dtype);
+    if (row < 0) row += rows;
+    if (row < 0 || row >= rows) {
+      if (error_flag != nullptr) atomicExch(error_flag, 1);
+      out[i] = T{};
+      continue;
+    }
+    out[i] = table[row * row_units + unit];
+  }
+}
+
+__global__ void argmax_rows_kernel(const void* x, int dtype, long long width, long long* out) {
+  __shared__ float best_v[kThreads];
+  __shared__ long long best_i[kThreads];
+  const long long row = blockIdx.x;
+  float bv = -INFINITY;
+  long long bi = width;  // sentinel: loses to any real index
+  for (long long j = threadIdx.x; j < width; j += blockDim.x) {
+    const float v = load_as_f32(x, row * width + j, dtype);
+    if (bi == width || argmax_better(v, j, bv, bi)) {
+      bv = v;
+      bi = j;
+    }
+  }
+  best_v[threadIdx.x] = bv;
+  best_i[threadIdx.x] = bi;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) {
+      const float ov = best_v[threadIdx.x + s];
+      const long long oi = best_i[threadIdx.x + s];
+      if (oi != width && (best_i[threadIdx.x] == width ||
+                          argmax_better(ov, oi, best_v[threadIdx.x], best_i[threadIdx.x]))) {
+        best_v[threadIdx.x] = ov;
+        best_i[threadIdx.x] = oi;
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[row] = best_i[0] == width ? 0 : best_i[0];
+}
+
+}  // namespace
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" {
+
+int cb_elementwise(const cb_elementwise_args* a, cb_stream_t stream) {
+  CB_REQUIRE(a->ndim >= 0 && a->ndim <= CB_MAX_DIMS, "elementwise: bad ndim %d", a->ndim);
+  CB_REQUIRE(a->n_inputs >= 1 && a->n_inputs <= CB_EW_MAX_INPUTS, "elementwise: bad input count");
+  CB_REQUIRE(a->n_instr >= 0 && a->n_instr <= CB_EW_MAX_INSTR, "elementwise: bad instruction count");
+  for (int t = 0; t < a->n_instr; ++t) {
+    const int limit = a->n_inputs + t;
+    CB_REQUIRE(a->lhs[t] >= 0 && a->lhs[t] < limit && a->rhs[t] < limit,
+               "elementwise: instruction %d reads an undefined register", t);
+  }
+  long long total = 1;
+  for (int d = 0; d < a->ndim; ++d) total *= a->shape[d];
+  if (total == 0) return CB_OK;
+  elementwise_kernel<<<grid_for(total), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(*a, total);
+  return check_launch("cb_elementwise");
+}
+
+int cb_reduce(const cb_reduce_args* a, cb_stream_t stream) {
+  CB_REQUIRE(a->n_keep >= 0 && a->n_keep <= CB_MAX_DIMS && a->n_red >= 0 && a->n_red <= CB_MAX_DIMS,
+             "reduce: bad dims");
+  long long n_out = 1, n_red = 1;
+  for (int d = 0; d < a->n_keep; ++d) n_out *= a->keep_shape[d];
+  for (int d = 0; d < a->n_red; ++d) n_red *= a->red_shape[d];
+  if (n_out == 0) return CB_OK;
+  CB_REQUIRE(n_red > 0 || a->kind == CB_REDUCE_SUM,
+             "zero-size array to reduction operation maximum which has no identity");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_red == 0) {
+    cudaMemsetAsync(a->out, 0, n_out * (a->out_dtype == CB_F32 ? 4 : 2), s);
+    return check_launch("cb_reduce(empty)");
+  }
+  if (a->sequential) {
+    reduce_sequential_kernel<<<grid_for(n_out), kThreads, 0, s>>>(*a, n_out, n_red);
+  } else {
+    reduce_warp_kernel<<<grid_for(n_out * 32), kThreads, 0, s>>>(*a, n_out, n_red);
+  }
+  return check_launch("cb_reduce");
+}
+
+int cb_copy_strided(const void* in, long long in_offset, void* out, int elem_bytes, int ndim,
+                    const long long* shape, const long long* in_strides, cb_stream_t stream) {
+  CB_REQUIRE(ndim >= 0 && ndim <= CB_MAX_DIMS, "copy: bad ndim %d", ndim);
+  CopyShape s{};
+  long long total = 1;
+  for (int d = 0; d < ndim; ++d) {
+    s.shape[d] = shape[d];
+    s.strides[d] = in_strides[d];
+    total *= shape[d];
+  }
+  if (total == 0) return CB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int g = grid_for(total);
+  switch (elem_bytes) {
+    case 1: copy_strided_kernel<<<g, kThreads, 0, st>>>(static_cast<const uint8_t*>(in) + in_offset,
+                                                         static_cast<uint8_t*>(out), ndim, s, total); break;
+    case 2: copy_strided_kernel<<<g, kThreads, 0, st>>>(static_cast<const uint16_t*>(in) + in_offset,
+                                                         static_cast<uint16_t*>(out), ndim, s, total); break;
+    case 4: copy_strided_kernel<<<g, kThreads, 0, st>>>(static_cast<const uint32_t*>(in) + in_offset,
+                                                         static_cast<uint32_t*>(out), ndim, s, total); break;
+    case 8: copy_strided_kernel<<<g, kThreads, 0, st>>>(static_cast<const uint64_t*>(in) + in_offset,
+                                                         static_cast<uint64_t*>(out), ndim, s, total); break;
+    default: CB_REQUIRE(false, "copy: unsupported element size %d", elem_bytes);
+  }
+  return check_launch("cb_copy_strided");
+}
+
+int cb_gather(const void* table, long long rows, long long row_bytes, const void* idx, int idx_dtype,
+              long long n, void* out, int* error_flag, cb_stream_t stream) {
+  CB_REQUIRE(idx_dtype == CB_I32 || idx_dtype == CB_I64, "gather: indices must be int32/int64");
+  CB_REQUIRE(rows >= 0 && row_bytes >= 0 && n >= 0, "gather: negative size");
+  if (n == 0 || row_bytes == 0) return CB_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uintptr_t align = reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(out) |
+                          static_cast<uintptr_t>(row_bytes);
+  if ((align & 15) == 0) {
+    const long long units = row_bytes / 16;
+    gather_kernel<<<grid_for(n * units), kThreads, 0, s>>>(static_cast<const uint4*>(table), rows, units,
+                                                           idx, idx_dtype, n, static_cast<uint4*>(out),
+                                                           error_flag);
+  } else if ((align & 3) == 0) {
+    const long long units = row_bytes / 4;
+    gather_kernel<<<grid_for(n * units), kThreads, 0, s>>>(static_cast<const uint32_t*>(table), rows,
+                                                           units, idx, idx_dtype, n,
+                                                           static_cast<uint32_t*>(out), error_flag);
+  } else {
+    gather_kernel<<<grid_for(n * row_bytes), kThreads, 0, s>>>(static_cast<const uint8_t*>(table), rows,
+                                                               row_bytes, idx, idx_dtype, n,
+                                                               static_cast<uint8_t*>(out), error_flag);
+  }
+  return check_launch("cb_gather");
+}
+
+int cb_argmax_rows(const void* x, int dtype, long long rows, long long width, long long* out_index,
+                   cb_stream_t stream) {
+  CB_REQUIRE(width > 0, "attempt to get argmax of an empty sequence");
+  if (rows == 0) return CB_OK;
+  CB_REQUIRE(rows < (1LL << 31), "argmax: too many rows");
+  argmax_rows_kernel<<<static_cast<unsigned>(rows), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, dtype, width, out_index);
+  return check_launch("cb_argmax_rows");
+}
+
+}  // extern "C"

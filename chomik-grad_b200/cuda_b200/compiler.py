@@ -1,0 +1,78 @@
+"""``CudaB200Compiler``: the ``cuda-b200`` plugin's ``Compiler``.
+
+Implements ``Compiler.compile(outputs, dynamic_inputs=())``
+(chomikgrad/lazy.py:172-183) with the reference CUDA plugin's conventions
+(``cache_size``, ``close()``, errors: cuda_backend.py:385-453):
+
+* ``ValueError`` for an empty output list, a non-leaf dynamic input, or a
+  dynamic input that is not a leaf of the compiled graph (dynamic inputs that
+  a lowering prunes, e.g. the decode RoPE ``rotation``, are accepted and
+  ignored, like mlx_backend.py:249-258);
+* ``TypeError`` for dtypes the kernels do not implement (float64, ...);
+* ``RuntimeError`` when no B200 is present -- never a CPU fallback.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import numpy as np
+
+from .device import CudaB200Device, DeviceArray
+from .frontend.lazy import Compiler
+from .planner import Planner
+from .program import CudaB200Program
+
+
+class CudaB200Compiler(Compiler):
+    """Lower chomik-grad graphs to sm_100a kernels (see cuda_b200.planner)."""
+
+    name = "cuda-b200"
+
+    def __init__(self, device_index: Optional[int] = None, *, use_graphs: bool = True,
+                 pdl: bool = True, fuse_decode: bool = True, alias_caches: bool = True,
+                 max_positions: int = 8192, gemv_grid: int = 0) -> None:
+        self.device = CudaB200Device(device_index)
+        self.use_graphs = use_graphs
+        self.pdl = pdl
+        self.fuse_decode = fuse_decode
+        self.alias_caches = alias_caches
+        self.max_positions = max_positions
+        self.gemv_grid = gemv_grid
+        self._tables: dict = {}
+        self._programs: list = []
+
+    @property
+    def cache_size(self) -> int:
+        return 0
+
+    def close(self) -> None:
+        self.device.synchronize()
+        for program in self._programs:
+            program.close()
+        self._programs.clear()
+        self._tables.clear()
+
+    def _leaf_dtype(self, node) -> np.dtype:
+        native = node.native_values.get(self.device.name)
+        if isinstance(native, DeviceArray):
+            return native.dtype
+        if node.value is not None:
+            return np.asarray(node.value).dtype
+        return np.asarray(node.numpy_value()).dtype
+
+    def plan(self, outputs: Sequence[object], dynamic_inputs: Sequence[object] = ()):
+        """Planning only (host side); exposed for inspection and tests."""
+        if not outputs:
+            raise ValueError("at least one output is required")
+        if any(node.op is not None for node in dynamic_inputs):
+            raise ValueError("dynamic inputs must be graph leaves")
+        return Planner(outputs, dynamic_inputs, backend=self.device.name,
+                       leaf_dtype=self._leaf_dtype, max_positions=self.max_positions,
+                       fuse_decode=self.fuse_decode, alias_caches=self.alias_caches,
+                       table_cache=self._tables).build()
+
+    def compile(self, outputs: Sequence[object],
+                dynamic_inputs: Sequence[object] = ()) -> CudaB200Program:
+        program = CudaB200Program(self.plan(outputs, dynamic_inputs), self)
+        return program

@@ -1,0 +1,222 @@
+"""Device storage and the ``DeviceAdapter`` of the ``cuda-b200`` backend.
+
+Native values are :class:`DeviceArray` objects: a dense, C-contiguous CUDA
+buffer (owned by a ``torch.Tensor``, which supplies the allocator and the
+current stream) plus NumPy metadata (``shape``, ``dtype`` -- bfloat16 is
+``ml_dtypes.bfloat16``), the attributes chomik-grad callers read from native
+values (``Tensor.from_native(value, shape=value.shape, ...)``,
+generate_tinyllama.py:796-804).
+
+The adapter follows ``DeviceAdapter`` (chomikgrad/lazy.py:107-151):
+``argmax`` has ``np.argmax`` semantics (first maximum, NaN wins) and returns
+a Python int after a 8-byte read-back; there is no host fallback.
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+from typing import Any, Dict, Mapping, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from .frontend.lazy import DeviceAdapter
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _bf16() -> np.dtype:
+    import ml_dtypes
+
+    return np.dtype(ml_dtypes.bfloat16)
+
+
+def torch_dtype(dtype: np.dtype):
+    torch = _torch()
+    dtype = np.dtype(dtype)
+    table = {
+        "float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16,
+        "int32": torch.int32, "int64": torch.int64, "uint8": torch.uint8, "bool": torch.bool,
+        "int16": torch.int16, "int8": torch.int8, "float64": torch.float64,
+    }
+    try:
+        return table[dtype.name]
+    except KeyError as error:
+        raise TypeError(f"cuda-b200 cannot store dtype {dtype}") from error
+
+
+def numpy_dtype(tdtype) -> np.dtype:
+    torch = _torch()
+    if tdtype == torch.bfloat16:
+        return _bf16()
+    return np.dtype(str(tdtype).replace("torch.", ""))
+
+
+class DeviceArray:
+    """A dense device buffer with NumPy shape/dtype metadata."""
+
+    __slots__ = ("tensor", "shape", "dtype", "argmax_value", "__weakref__")
+
+    def __init__(self, tensor: Any, shape: Optional[Sequence[int]] = None,
+                 dtype: Optional[np.dtype] = None) -> None:
+        self.tensor = tensor
+        self.shape = tuple(int(n) for n in (shape if shape is not None else tensor.shape))
+        self.dtype = np.dtype(dtype) if dtype is not None else numpy_dtype(tensor.dtype)
+        # Optional device int64 holding argmax(self) computed by the program
+        # that produced this array (saves a reduction in DeviceAdapter.argmax).
+        self.argmax_value = None
+
+    @property
+    def size(self) -> int:
+        return int(np.prod(self.shape)) if self.shape else 1
+
+    @property
+    def ndim(self) -> int:
+        return len(self.shape)
+
+    @property
+    def nbytes(self) -> int:
+        return self.size * self.dtype.itemsize
+
+    def data_ptr(self) -> int:
+        return int(self.tensor.data_ptr())
+
+    def __repr__(self) -> str:
+        return f"DeviceArray(shape={self.shape}, dtype={self.dtype}, device={self.tensor.device})"
+
+
+def empty(shape: Sequence[int], dtype: np.dtype, device: Any) -> DeviceArray:
+    torch = _torch()
+    count = int(np.prod(shape)) if len(shape) else 1
+    tensor = torch.empty(max(count, 1), dtype=torch_dtype(dtype), device=device)
+    return DeviceArray(tensor, tuple(shape), dtype)
+
+
+def upload(value: np.ndarray, device: Any) -> DeviceArray:
+    """Copy a host array to a new dense device buffer."""
+    torch = _torch()
+    host = np.ascontiguousarray(value)
+    dtype = host.dtype
+    if dtype.name == "bfloat16":
+        tensor = torch.from_numpy(host.reshape(-1).view(np.int16)).to(device).view(torch.bfloat16)
+    elif dtype == np.bool_:
+        tensor = torch.from_numpy(host.reshape(-1)).to(device)
+    else:
+        tensor = torch.from_numpy(host.reshape(-1)).to(device)
+    if tensor.numel() == 0:
+        tensor = torch.empty(1, dtype=torch_dtype(dtype), device=device)
+    return DeviceArray(tensor, host.shape, dtype)
+
+
+def download(array: DeviceArray) -> np.ndarray:
+    torch = _torch()
+    flat = array.tensor[: array.size] if array.size else array.tensor[:0]
+    if array.dtype.name == "bfloat16":
+        host = flat.view(torch.int16).cpu().numpy().view(np.uint16).view(_bf16())
+    else:
+        host = flat.cpu().numpy()
+    return host.reshape(array.shape).copy()
+
+
+class CudaB200Device(DeviceAdapter):
+    """``DeviceAdapter`` over one B200 (the current CUDA device by default)."""
+
+    name = "cuda-b200"
+
+    def __init__(self, index: Optional[int] = None) -> None:
+        torch = _torch()
+        if not torch.cuda.is_available():
+            raise RuntimeError("the cuda-b200 backend requires a working NVIDIA driver and CUDA GPU")
+        self.index = torch.cuda.current_device() if index is None else int(index)
+        self.torch_device = torch.device("cuda", self.index)
+        major, minor = torch.cuda.get_device_capability(self.index)
+        if (major, minor) != (10, 0):
+            raise RuntimeError(f"cuda-b200 kernels are built for sm_100a; device {self.index} "
+                               f"is sm_{major}{minor}")
+        _lib.load()
+        self.inference_dtype = _bf16()
+
+    # -- stream ------------------------------------------------------------
+    def stream(self) -> int:
+        torch = _torch()
+        return int(torch.cuda.current_stream(self.torch_device).cuda_stream)
+
+    # -- DeviceAdapter -----------------------------------------------------
+    def array(self, value: object) -> DeviceArray:
+        if isinstance(value, DeviceArray):
+            return value
+        torch = _torch()
+        if isinstance(value, torch.Tensor):
+            tensor = value.detach().to(self.torch_device).contiguous().reshape(-1)
+            return DeviceArray(tensor, tuple(value.shape), numpy_dtype(value.dtype))
+        with torch.cuda.device(self.torch_device):
+            return upload(np.asarray(value), self.torch_device)
+
+    def evaluate(self, values: Sequence[object]) -> None:
+        self.synchronize()
+
+    def synchronize(self) -> None:
+        _torch().cuda.synchronize(self.torch_device)
+
+    def to_numpy(self, value: object) -> np.ndarray:
+        if isinstance(value, DeviceArray):
+            return download(value)
+        return np.asarray(value)
+
+    def argmax(self, value: object) -> int:
+        """Index of the first maximum of the flattened array (np.argmax)."""
+        array = self.array(value)
+        if array.argmax_value is not None:
+            index, status = array.argmax_value.tolist()
+            if status:
+                raise IndexError("a kernel of the program that produced these logits flagged an "
+                                 f"out-of-range index (code {status})")
+            return int(index)
+        if array.size == 0:
+            raise ValueError("attempt to get argmax of an empty sequence")
+        result = _torch().empty(1, dtype=_torch().int64, device=self.torch_device)
+        _lib.call("cb_argmax_rows", array.data_ptr(), _lib.dtype_code(array.dtype), 1,
+                  array.size, result.data_ptr(), self.stream())
+        return int(result.item())
+
+    def argmax_last_axis(self, value: object) -> np.ndarray:
+        array = self.array(value)
+        width = array.shape[-1] if array.shape else 1
+        if width == 0:
+            raise ValueError("attempt to get argmax of an empty sequence")
+        rows = array.size // width
+        result = _torch().empty(max(rows, 1), dtype=_torch().int64, device=self.torch_device)
+        if rows:
+            _lib.call("cb_argmax_rows", array.data_ptr(), _lib.dtype_code(array.dtype), rows, width,
+                      result.data_ptr(), self.stream())
+        return result[:rows].cpu().numpy().reshape(array.shape[:-1])
+
+    def dtype(self, value: object) -> np.dtype:
+        if isinstance(value, DeviceArray):
+            return value.dtype
+        return np.asarray(value).dtype
+
+    def load_safetensors(self, path: Path, *,
+                         dtype: Optional[np.dtype] = None) -> Mapping[str, DeviceArray]:
+        """Read a safetensors file straight into device buffers (casting if asked)."""
+        from safetensors import safe_open
+
+        torch = _torch()
+        result: Dict[str, DeviceArray] = {}
+        with safe_open(str(path), framework="pt", device="cpu") as handle:
+            for key in handle.keys():
+                tensor = handle.get_tensor(key)
+                if dtype is not None:
+                    tensor = tensor.to(torch_dtype(np.dtype(dtype)))
+                result[key] = self.array(tensor)
+        return result
+
+    def reset_peak_memory(self) -> None:
+        _torch().cuda.reset_peak_memory_stats(self.torch_device)
+
+    def peak_memory_bytes(self) -> Optional[int]:
+        return int(_torch().cuda.max_memory_allocated(self.torch_device))

@@ -1,0 +1,100 @@
+"""Named model shapes and seeded synthetic weights for the Llama hot path.
+
+There are no checkpoints on the benchmark machines, so every configuration is
+random-initialised: non-norm weights ~ N(0, 0.02) drawn in float32 and cast to
+the model dtype, RMSNorm weights = 1.  Each tensor has its own generator,
+``default_rng(SeedSequence(seed).spawn(n)[k])`` with ``k`` the tensor's index
+in ``required_weight_shapes`` order, so tensors are reproducible one by one
+and can be drawn on several host threads at once (NumPy releases the GIL while
+filling).  Prompts are uniform token ids from ``default_rng(seed + 1)``.
+"""
+
+from __future__ import annotations
+
+from concurrent.futures import ThreadPoolExecutor
+from dataclasses import dataclass
+import os
+from typing import Dict, Optional
+
+import numpy as np
+
+from .frontend.llama import LlamaConfig, required_weight_shapes
+
+
+def bfloat16() -> np.dtype:
+    import ml_dtypes
+
+    return np.dtype(ml_dtypes.bfloat16)
+
+
+@dataclass(frozen=True)
+class Workload:
+    """One benchmark/parity configuration of the Llama hot path."""
+
+    name: str
+    config: LlamaConfig
+    dtype: str              # "float32" | "bfloat16"
+    batch: int
+    prompt_tokens: int
+    decode_steps: int
+
+    @property
+    def np_dtype(self) -> np.dtype:
+        return np.dtype(np.float32) if self.dtype == "float32" else bfloat16()
+
+    @property
+    def context(self) -> int:
+        """KV rows per sequence: prompt + generated (generate_tinyllama.py:692)."""
+        return self.prompt_tokens + self.decode_steps
+
+
+TINY = LlamaConfig(vocab_size=4096, hidden_size=256, intermediate_size=688,
+                   num_hidden_layers=4, num_attention_heads=8, num_key_value_heads=2,
+                   max_position_embeddings=128, rope_theta=10_000.0)
+TINYLLAMA = LlamaConfig(vocab_size=32000, hidden_size=2048, intermediate_size=5632,
+                        num_hidden_layers=22, num_attention_heads=32,
+                        num_key_value_heads=4, max_position_embeddings=2048,
+                        rope_theta=10_000.0)
+LLAMA3_8B = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336,
+                        num_hidden_layers=32, num_attention_heads=32,
+                        num_key_value_heads=8, max_position_embeddings=8192,
+                        rope_theta=500_000.0)
+
+WORKLOADS: Dict[str, Workload] = {
+    w.name: w
+    for w in (
+        Workload("tiny-fp32", TINY, "float32", 1, 16, 32),
+        Workload("tiny-bf16", TINY, "bfloat16", 1, 16, 32),
+        Workload("tinyllama-bf16-bs1", TINYLLAMA, "bfloat16", 1, 128, 256),
+        Workload("tinyllama-bf16-bs32", TINYLLAMA, "bfloat16", 32, 512, 256),
+        Workload("tinyllama-bf16-prefill-bs8", TINYLLAMA, "bfloat16", 8, 2048, 0),
+        Workload("llama3-8b-bf16-bs16", LLAMA3_8B, "bfloat16", 16, 1024, 256),
+    )
+}
+
+
+def synthetic_weights(config: LlamaConfig, *, dtype: np.dtype, seed: int = 0,
+                      std: float = 0.02, threads: Optional[int] = None) -> Dict[str, np.ndarray]:
+    """Seeded random-init weights in HF layout (see module docstring)."""
+    dtype = np.dtype(dtype)
+    shapes = list(required_weight_shapes(config).items())
+    seeds = np.random.SeedSequence(seed).spawn(len(shapes))
+
+    def draw(index: int) -> np.ndarray:
+        name, shape = shapes[index]
+        if name.endswith("norm.weight"):
+            return np.ones(shape, dtype=dtype)
+        values = np.random.default_rng(seeds[index]).normal(0.0, std, shape)
+        return values.astype(np.float32).astype(dtype)
+
+    workers = threads or min(32, os.cpu_count() or 1)
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        arrays = list(pool.map(draw, range(len(shapes))))
+    return {name: array for (name, _), array in zip(shapes, arrays)}
+
+
+def synthetic_prompt(config: LlamaConfig, length: int, *, seed: int = 0,
+                     batch: int = 1) -> np.ndarray:
+    """(batch, length) uniform token ids in [0, vocab)."""
+    rng = np.random.default_rng(seed + 1)
+    return rng.integers(0, config.vocab_size, size=(batch, length)).astype(np.int32)

@@ -1,0 +1,803 @@
+"""Graph -> kernel plan for the ``cuda-b200`` compiler (host-only, no GPU).
+
+The planner turns a chomik-grad output list into a straight-line list of
+kernel launches over a static set of device buffers:
+
+1. **Lowerings.**  Nodes whose intrinsic ``lowering`` the plugin supports
+   (``rms_norm``, ``rope``, ``sdpa``; hints attached by chomikgrad/llama.py
+   :13-25) are replaced by one kernel, *after* checking that the portable
+   sub-graph under the node has the exact shape the reference builds
+   (llama.py:279-287, :293-323, :355-364).  The scalar constants of that
+   sub-graph (mean divisor, epsilon, attention divisor) and the dtype of
+   every intermediate are read from it, so the kernel repeats the arithmetic
+   the reference's ``cpu`` compiler performs -- including bfloat16
+   intermediates and NumPy's sequential bfloat16 sums.  A lowering whose
+   sub-graph does not match is simply not used.
+2. **Runtime dtypes.**  Each value gets the dtype NumPy/ml_dtypes would give
+   it at run time (bf16 @ bf16 -> float32, bf16 + f32 -> f32, ...), which can
+   differ from the node's metadata dtype.
+3. **Decode fusion.**  Single-token Llama structures become fused kernels:
+   rms_norm -> q/k/v GEMV, RoPE + write-mask cache update + attention,
+   O-proj + residual, rms_norm -> gate/up GEMV + SwiGLU, down + residual,
+   final norm -> lm_head + argmax.  KV caches bound as dynamic inputs are
+   updated in place (the caller rebinds the returned cache,
+   generate_tinyllama.py:857).
+4. **Generic lowering** of everything else: fused elementwise trees, views
+   for RESHAPE/PERMUTE, reductions, batched matmul, gather.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Set, Tuple
+
+import numpy as np
+
+from . import _lib
+
+# --------------------------------------------------------------------------
+# node helpers (duck-typed: work for the mirror and the real chomikgrad)
+
+
+def kind(node) -> Optional[str]:
+    return None if node.op is None else node.op.value
+
+
+def is_ew(node, name: Optional[str] = None) -> bool:
+    return kind(node) == "elementwise" and (name is None or str(node.arg) == name)
+
+
+def bf16() -> np.dtype:
+    import ml_dtypes
+
+    return np.dtype(ml_dtypes.bfloat16)
+
+
+F32 = np.dtype(np.float32)
+FLOATS = ("float32", "bfloat16", "float16")
+
+
+def dt_code(dtype: np.dtype) -> int:
+    return _lib.dtype_code(dtype)
+
+
+def contiguous_strides(shape: Sequence[int]) -> Tuple[int, ...]:
+    strides, step = [], 1
+    for n in reversed(shape):
+        strides.append(step)
+        step *= max(int(n), 1)
+    return tuple(reversed(strides))
+
+
+class PlanError(TypeError):
+    """The graph uses a dtype or construct the plugin cannot run."""
+
+
+# --------------------------------------------------------------------------
+# buffers and views
+
+
+@dataclass(eq=False)
+class Buffer:
+    """One device allocation of the program."""
+
+    kind: str                 # input | tmp | aux
+    shape: Tuple[int, ...]
+    dtype: np.dtype
+    node: object = None       # the leaf, for inputs
+    name: str = ""
+    host: Optional[np.ndarray] = None   # aux: initial contents
+    zero: bool = False        # aux: zero-initialised
+    bind: str = "copy"        # inputs: copy | pointer (dynamic caches, constants)
+
+    @property
+    def size(self) -> int:
+        return int(np.prod(self.shape)) if self.shape else 1
+
+
+@dataclass(eq=False)
+class View:
+    buf: Buffer
+    shape: Tuple[int, ...]
+    strides: Tuple[int, ...]
+    offset: int = 0
+
+    @property
+    def dtype(self) -> np.dtype:
+        return self.buf.dtype
+
+    @property
+    def size(self) -> int:
+        return int(np.prod(self.shape)) if self.shape else 1
+
+    def is_contiguous(self) -> bool:
+        expected = contiguous_strides(self.shape)
+        return all(n == 1 or s == e for n, s, e in zip(self.shape, self.strides, expected))
+
+    @staticmethod
+    def whole(buf: Buffer) -> "View":
+        return View(buf, tuple(buf.shape), contiguous_strides(buf.shape), 0)
+
+
+def reshape_strides(shape: Sequence[int], strides: Sequence[int],
+                    new_shape: Sequence[int]) -> Optional[Tuple[int, ...]]:
+    """Strides viewing ``shape/strides`` as ``new_shape`` without a copy, or None.
+
+    Same contract as NumPy's no-copy reshape: groups of old axes that are
+    contiguous among themselves can be split/merged freely.
+    """
+    old = [(int(n), int(s)) for n, s in zip(shape, strides) if int(n) != 1]
+    new = [int(n) for n in new_shape]
+    if int(np.prod([n for n, _ in old], dtype=np.int64)) != int(np.prod(new, dtype=np.int64)):
+        return None
+    if any(n == 0 for n in new):
+        return contiguous_strides(new)
+    result = [0] * len(new)
+    oi, ni = 0, 0
+    # indices of new dims that are not 1
+    while ni < len(new) and oi < len(old):
+        if new[ni] == 1:
+            result[ni] = 0
+            ni += 1
+            continue
+        op, np_ = old[oi][0], new[ni]
+        oj, nj = oi + 1, ni + 1
+        while op != np_:
+            if np_ < op:
+                while nj < len(new) and new[nj] == 1:
+                    nj += 1
+                if nj >= len(new):
+                    return None
+                np_ *= new[nj]
+                nj += 1
+            else:
+                if oj >= len(old):
+                    return None
+                op *= old[oj][0]
+                oj += 1
+        for k in range(oi, oj - 1):
+            if old[k][1] != old[k + 1][0] * old[k + 1][1]:
+                return None
+        stride = old[oj - 1][1]
+        for k in range(nj - 1, ni - 1, -1):
+            if new[k] == 1:
+                result[k] = 0
+                continue
+            result[k] = stride
+            stride *= new[k]
+        oi, ni = oj, nj
+    while ni < len(new):
+        result[ni] = 0
+        ni += 1
+    return tuple(result)
+
+
+# --------------------------------------------------------------------------
+# steps (one kernel launch each)
+
+
+@dataclass(eq=False)
+class Step:
+    name: str
+    out: Optional[View]
+    args: Dict[str, object] = field(default_factory=dict)
+    text: str = ""
+
+
+# --------------------------------------------------------------------------
+# the plan
+
+
+@dataclass
+class RmsSpec:
+    divisor: float
+    eps: float
+    dts: Tuple[np.dtype, ...]  # sq, sum, mean, t, d, y
+    out_dtype: np.dtype
+
+
+class Plan:
+    """Result of planning: buffers, steps, outputs and the program source."""
+
+    def __init__(self) -> None:
+        self.buffers: List[Buffer] = []
+        self.steps: List[Step] = []
+        self.leaves: List[object] = []            # all leaves the plan reads
+        self.inputs: Tuple[object, ...] = ()      # CompiledProgram.inputs
+        self.input_buffers: Dict[object, Buffer] = {}
+        self.outputs: List[Tuple[object, View]] = []
+        self.aliases: Dict[int, object] = {}      # output index -> dynamic leaf updated in place
+        self.argmax_of: Dict[int, Buffer] = {}    # output index -> int64 argmax buffer
+        self.error_flag: Optional[Buffer] = None
+        self.init_steps: List[dict] = []          # run once when the program is built
+        self.guards: List[Tuple[object, np.ndarray]] = []  # non-cached leaves assumed constant
+        self.lowered: Dict[str, int] = {}
+        self.source = ""
+
+    def buffer(self, kind_: str, shape, dtype, **kw) -> Buffer:
+        buf = Buffer(kind_, tuple(int(n) for n in shape), np.dtype(dtype), **kw)
+        buf.name = f"{kind_[0]}{len(self.buffers)}"
+        self.buffers.append(buf)
+        return buf
+
+
+class Planner:
+    """Builds a :class:`Plan` from output nodes (see module docstring)."""
+
+    SUPPORTED_LOWERINGS = frozenset({"rms_norm", "rope", "sdpa"})
+
+    def __init__(self, outputs: Sequence[object], dynamic_inputs: Sequence[object], *,
+                 backend: str, leaf_dtype, max_positions: int = 8192,
+                 fuse_decode: bool = True, alias_caches: bool = True,
+                 table_cache: Optional[dict] = None) -> None:
+        self.outputs = tuple(outputs)
+        self.dynamic = set(dynamic_inputs)
+        self.backend = backend
+        self.leaf_dtype = leaf_dtype
+        self.max_positions = max_positions
+        self.fuse_decode = fuse_decode
+        self.alias_caches = alias_caches
+        self.table_cache = table_cache if table_cache is not None else {}
+        self.plan = Plan()
+        self._rdt: Dict[object, np.dtype] = {}
+        self._val: Dict[object, View] = {}
+        self._low: Dict[object, Tuple[str, tuple, object]] = {}
+        self._rms: Dict[object, RmsSpec] = {}
+        self._sdpa: Dict[object, float] = {}
+        self._rope: Dict[object, object] = {}
+        self.units: Dict[object, object] = {}
+
+    # ---------------------------------------------------------------- dtypes
+    def rdt(self, node) -> np.dtype:
+        """Runtime dtype NumPy/ml_dtypes produce for ``node`` (iterative)."""
+        if node in self._rdt:
+            return self._rdt[node]
+        stack = [node]
+        while stack:
+            top = stack[-1]
+            if top in self._rdt:
+                stack.pop()
+                continue
+            pending = [p for p in top.inputs if p not in self._rdt]
+            if pending:
+                stack.extend(pending)
+                continue
+            stack.pop()
+            self._rdt[top] = self._infer(top)
+        return self._rdt[node]
+
+    def _infer(self, node) -> np.dtype:
+        k = kind(node)
+        if k is None:
+            return np.dtype(self.leaf_dtype(node))
+        ins = [self._rdt[p] for p in node.inputs]
+        if k == "elementwise":
+            name = str(node.arg)
+            if name == "equal":
+                return ins[0]
+            if len(ins) == 2:
+                return np.result_type(ins[0], ins[1])
+            return ins[0]
+        if k == "matmul":
+            if ins[0].name == "bfloat16" and ins[1].name == "bfloat16":
+                return F32
+            return np.result_type(ins[0], ins[1])
+        if k in ("reshape", "permute", "reduce"):
+            return ins[0]
+        if k == "gather":
+            return ins[0]
+        raise PlanError(f"unsupported operation: {node.op}")
+
+    # ------------------------------------------------------- graph analysis
+    def _lowering_of(self, node):
+        low = node.lowering
+        if low is None or low[0] not in self.SUPPORTED_LOWERINGS:
+            return None
+        kind_ = low[0]
+        if kind_ == "rms_norm" and self._match_rms(node, low):
+            return low
+        if kind_ == "rope" and self._match_rope(node, low):
+            return low
+        if kind_ == "sdpa" and self._match_sdpa(node, low):
+            return low
+        return None
+
+    def _parents(self, node):
+        low = self._low.get(node)
+        return low[1] if low is not None else node.inputs
+
+    def _order(self) -> List[object]:
+        order, seen = [], set()
+        for root in self.outputs:
+            if root in seen:
+                continue
+            seen.add(root)
+            stack = [(root, None)]
+            while stack:
+                node, it = stack[-1]
+                if it is None:
+                    low = self._lowering_of(node) if node.op is not None else None
+                    if low is not None:
+                        self._low[node] = low
+                    it = iter(self._parents(node))
+                    stack[-1] = (node, it)
+                advanced = False
+                for parent in it:
+                    if parent not in seen:
+                        seen.add(parent)
+                        stack.append((parent, None))
+                        advanced = True
+                        break
+                if not advanced:
+                    stack.pop()
+                    order.append(node)
+        return order
+
+    # --- structural matchers of the reference's portable sub-graphs -------
+    def _const(self, node) -> Optional[float]:
+        """Value of a constant scalar leaf (immutable: cached native)."""
+        if node.op is not None or node in self.dynamic or not node.cache_native:
+            return None
+        if int(np.prod(node.shape)) != 1:
+            return None
+        try:
+            value = np.asarray(node.numpy_value())
+        except Exception:
+            return None
+        return float(value.reshape(-1)[0].astype(np.float32))
+
+    def _match_rms(self, node, low) -> bool:
+        """out = x / sqrt(sum(x*x, -1, keepdims)/c + eps) * w (llama.py:279-287)."""
+        x, w = low[1]
+        if not is_ew(node, "mul") or node.inputs[1] is not w:
+            return False
+        a = node.inputs[0]
+        if not is_ew(a, "div") or a.inputs[0] is not x:
+            return False
+        s = a.inputs[1]
+        if not is_ew(s, "sqrt"):
+            return False
+        t = s.inputs[0]
+        if not is_ew(t, "add"):
+            return False
+        m, e = t.inputs
+        if not is_ew(m, "div"):
+            return False
+        total, c = m.inputs
+        if kind(total) != "reduce":
+            return False
+        how, axes, keep = total.arg
+        if how != "sum" or tuple(axes) != (len(x.shape) - 1,) or not keep:
+            return False
+        q = total.inputs[0]
+        if not is_ew(q, "mul") or q.inputs[0] is not x or q.inputs[1] is not x:
+            return False
+        divisor, eps = self._const(c), self._const(e)
+        if divisor is None or eps is None or len(w.shape) != 1 or w.shape[0] != x.shape[-1]:
+            return False
+        # the constants enter the arithmetic in their own runtime dtype
+        divisor = float(np.asarray(divisor, dtype=np.float32).astype(self.rdt(c)).astype(np.float32))
+        eps = float(np.asarray(eps, dtype=np.float32).astype(self.rdt(e)).astype(np.float32))
+        dts = tuple(self.rdt(n) for n in (q, total, m, t, s, a))
+        if any(d.name not in FLOATS for d in dts) or self.rdt(node).name not in FLOATS:
+            return False
+        self._rms[node] = RmsSpec(divisor, eps, dts, self.rdt(node))
+        return True
+
+    def _match_rope(self, node, low) -> bool:
+        """out = reshape(reshape(x) @ R) with R (1,1,T,hd,hd) (llama.py:293-323)."""
+        inputs, (hd, theta, offset) = low[1], low[2]
+        x = inputs[0]
+        if kind(node) != "reshape" or len(x.shape) != 4:
+            return False
+        mm = node.inputs[0]
+        if kind(mm) != "matmul" or kind(mm.inputs[0]) != "reshape" or mm.inputs[0].inputs[0] is not x:
+            return False
+        rot = mm.inputs[1]
+        b, h, t, d = x.shape
+        if d != hd or d % 2 or rot.op is not None or tuple(rot.shape) != (1, 1, t, d, d):
+            return False
+        if self.rdt(node).name not in FLOATS or int(offset) != 0:
+            return False
+        position = inputs[1] if len(inputs) == 2 else None
+        if position is None:
+            # constant rotation table: read cos/sin straight from it
+            if rot in self.dynamic or not rot.cache_native:
+                return False
+            table = np.asarray(rot.numpy_value()).astype(np.float32)[0, 0]
+            half = d // 2
+            j = np.arange(half)
+            cos = table[:, j, j][None]          # [1][T][half]
+            sin = table[:, j, j + half][None]
+            self._rope[node] = ("table", cos.copy(), sin.copy())
+        else:
+            if position.shape != () or np.dtype(self.rdt(position)).kind not in "iu":
+                return False
+            self._rope[node] = ("position", float(theta), self.rdt(rot), t, d)
+        return True
+
+    def _repeat_source(self, node, heads: int):
+        """k for reshape(reshape(k) * ones(1,1,G,1,1)) (llama.py:325-330), else None."""
+        if kind(node) != "reshape":
+            return None
+        mul = node.inputs[0]
+        if not is_ew(mul, "mul"):
+            return None
+        inner, ones = mul.inputs
+        if kind(inner) != "reshape" or ones.op is not None or ones in self.dynamic:
+            return None
+        src = inner.inputs[0]
+        if len(src.shape) != 4:
+            return None
+        b, kvh, t, d = src.shape
+        if tuple(inner.shape) != (b, kvh, 1, t, d) or kvh == 0 or heads % kvh:
+            return None
+        if tuple(ones.shape) != (1, 1, heads // kvh, 1, 1):
+            return None
+        try:
+            ones_value = np.asarray(ones.numpy_value())
+        except Exception:
+            return None
+        if not np.all(ones_value == 1):
+            return None
+        if not ones.cache_native:
+            self.plan.guards.append((ones, ones_value.copy()))
+        return src
+
+    def _match_sdpa(self, node, low) -> bool:
+        """out = softmax((q @ rep(k)^T) / c + mask) @ rep(v) (llama.py:355-364)."""
+        q, k, v, mask = low[1]
+        if kind(node) != "matmul" or len(q.shape) != 4:
+            return False
+        heads = q.shape[1]
+        probs, rep_v = node.inputs
+        if self._repeat_source(rep_v, heads) is not v:
+            return False
+        # softmax portable form: div(exp(sub(x, max)), sum(...)), hint ("softmax", (x,), axis)
+        slow = probs.lowering
+        if slow is None or slow[0] != "softmax" or int(slow[2]) != 3:
+            return False
+        scores = slow[1][0]
+        if not is_ew(scores, "add") or scores.inputs[1] is not mask:
+            return False
+        scaled = scores.inputs[0]
+        if not is_ew(scaled, "div"):
+            return False
+        qk, c = scaled.inputs
+        if kind(qk) != "matmul" or qk.inputs[0] is not q:
+            return False
+        kt = qk.inputs[1]
+        if kind(kt) != "permute" or tuple(kt.arg) != (0, 1, 3, 2):
+            return False
+        if self._repeat_source(kt.inputs[0], heads) is not k:
+            return False
+        divisor = self._const(c)
+        if divisor is None or len(mask.shape) != 4:
+            return False
+        divisor = float(np.asarray(divisor, dtype=np.float32).astype(self.rdt(c)).astype(np.float32))
+        if any(self.rdt(n) != F32 for n in (scaled, scores, probs, node)):
+            return False
+        self._sdpa[node] = divisor
+        return True
+
+    # ------------------------------------------------------------ planning
+    def build(self) -> Plan:
+        plan = self.plan
+        order = self._order()
+        self.order = order
+        for node in order:
+            dt = self.rdt(node)
+            if node.op is not None and dt.name not in FLOATS + ("int32", "int64"):
+                raise PlanError(f"cuda-b200 does not support runtime dtype {dt} "
+                                f"(node {kind(node)} {node.arg!r})")
+        leaves = [n for n in order if n.op is None]
+        if not self.dynamic.issubset(set(leaves) | self._pruned_leaves()):
+            raise ValueError("dynamic input is not a leaf of the compiled graph")
+        plan.leaves = leaves
+        plan.dynamic = set(self.dynamic)
+        plan.inputs = tuple(n for n in leaves if n in self.dynamic) if self.dynamic else tuple(leaves)
+        self.consumers: Dict[object, List[object]] = {}
+        for node in order:
+            for parent in self._parents(node):
+                self.consumers.setdefault(parent, []).append(node)
+        self.output_set = set(self.outputs)
+        self.claimed: Set[object] = set()
+        for leaf in leaves:
+            self._bind_leaf(leaf)
+        if self.fuse_decode:
+            from .fusion import DecodeFusion
+
+            DecodeFusion(self).apply()
+        self._fuse_elementwise_groups()
+        for node in order:
+            if node.op is None or node in self._val:
+                continue
+            unit = self.units.get(node)
+            if unit is not None:
+                unit()
+            elif node not in self.claimed:
+                self._emit_generic(node)
+        for index, node in enumerate(self.outputs):
+            plan.outputs.append((node, self.value(node)))
+        from .fusion import assign_prefetch
+
+        assign_prefetch(plan.steps)
+        plan.source = self._source()
+        return plan
+
+    def _pruned_leaves(self) -> Set[object]:
+        """Leaves only reachable through portable sub-graphs of used lowerings."""
+        seen, stack = set(), list(self.outputs)
+        while stack:
+            n = stack.pop()
+            if n in seen:
+                continue
+            seen.add(n)
+            stack.extend(n.inputs)
+        return {n for n in seen if n.op is None}
+
+    def _bind_leaf(self, leaf) -> None:
+        dt = self.rdt(leaf)
+        dynamic = leaf in self.dynamic
+        cached = (not dynamic) and leaf.cache_native
+        buf = self.plan.buffer("input", leaf.shape, dt, node=leaf,
+                               bind="pointer" if cached else "copy")
+        self.plan.input_buffers[leaf] = buf
+        self._val[leaf] = View.whole(buf)
+
+    def value(self, node) -> View:
+        if node not in self._val:
+            self._emit_generic(node)
+        return self._val[node]
+
+    def set_value(self, node, view: View) -> None:
+        self._val[node] = view
+
+    def tmp(self, shape, dtype) -> View:
+        return View.whole(self.plan.buffer("tmp", shape, dtype))
+
+    def aux(self, host: Optional[np.ndarray] = None, *, shape=None, dtype=None, zero=False) -> Buffer:
+        if host is not None:
+            return self.plan.buffer("aux", host.shape, host.dtype, host=host)
+        return self.plan.buffer("aux", shape, dtype, zero=zero)
+
+    def error_flag(self) -> Buffer:
+        if self.plan.error_flag is None:
+            self.plan.error_flag = self.aux(shape=(1,), dtype=np.int32, zero=True)
+        return self.plan.error_flag
+
+    def add_step(self, name: str, out: Optional[View], text: str, **args) -> Step:
+        step = Step(name, out, args, text)
+        self.plan.steps.append(step)
+        return step
+
+    def contiguous(self, view: View) -> View:
+        if view.is_contiguous():
+            return view
+        out = self.tmp(view.shape, view.dtype)
+        self.add_step("copy", out, f"copy({self._name(view)})", src=view)
+        return out
+
+    def _name(self, view: View) -> str:
+        return view.buf.name + (f"[+{view.offset}]" if view.offset else "")
+
+    # ------------------------------------------------- generic emission
+    def _emit_generic(self, node) -> None:
+        if node in self._val:
+            return
+        # make sure parents exist first (iterative to avoid deep recursion)
+        pending = [node]
+        while pending:
+            top = pending[-1]
+            missing = [p for p in self._parents(top) if p not in self._val]
+            if missing:
+                pending.extend(missing)
+                continue
+            pending.pop()
+            if top not in self._val:
+                self._emit_one(top)
+
+    def _emit_one(self, node) -> None:
+        low = self._low.get(node)
+        if low is not None:
+            getattr(self, f"_emit_{low[0]}")(node, low)
+            return
+        k = kind(node)
+        getattr(self, f"_emit_{k}")(node)
+
+    def _emit_reshape(self, node) -> None:
+        src = self.value(node.inputs[0])
+        strides = reshape_strides(src.shape, src.strides, node.arg)
+        if strides is None:
+            src = self.contiguous(src)
+            strides = contiguous_strides(node.arg)
+        self.set_value(node, View(src.buf, tuple(node.arg), strides, src.offset))
+
+    def _emit_permute(self, node) -> None:
+        src = self.value(node.inputs[0])
+        axes = tuple(node.arg)
+        self.set_value(node, View(src.buf, tuple(src.shape[a] for a in axes),
+                                  tuple(src.strides[a] for a in axes), src.offset))
+
+    def _emit_elementwise(self, node) -> None:
+        group = self._ew_groups.get(node)
+        if group is None:
+            group = self._ew_tree(node, set())
+        inputs, instrs = group
+        views = [self.value(p) for p in inputs]
+        out = self.tmp(node.shape, self.rdt(node))
+        self.add_step("elementwise", out,
+                      f"elementwise({', '.join(self._name(v) for v in views)}; "
+                      f"{' '.join(i[0] for i in instrs)})",
+                      inputs=views, instrs=instrs, shape=tuple(node.shape))
+        self.set_value(node, out)
+
+    def _ew_tree(self, root, absorbed: Set[object]):
+        inputs: List[object] = []
+        slot: Dict[object, int] = {}
+        instrs: List[Tuple[str, int, int, np.dtype]] = []
+        reg: Dict[object, int] = {}
+
+        order: List[object] = []
+        stack = [(root, False)]
+        while stack:
+            n, done = stack.pop()
+            if done:
+                order.append(n)
+                continue
+            if n in reg:
+                continue
+            if n is root or n in absorbed:
+                stack.append((n, True))
+                for p in reversed(n.inputs):
+                    stack.append((p, False))
+        for n in order:
+            if n in reg:
+                continue
+            operands = []
+            for p in n.inputs:
+                if p is root or p in absorbed:
+                    operands.append(("r", p))
+                else:
+                    if p not in slot:
+                        slot[p] = len(inputs)
+                        inputs.append(p)
+                    operands.append(("i", p))
+            reg[n] = len(instrs)
+            instrs.append((str(n.arg), operands, self.rdt(n)))
+        n_in = len(inputs)
+        encoded = []
+        for name, operands, dt in instrs:
+            idx = []
+            for tag, p in operands:
+                idx.append(slot[p] if tag == "i" else n_in + reg[p])
+            encoded.append((name, idx[0], idx[1] if len(idx) > 1 else -1, dt))
+        return inputs, encoded
+
+    def _fuse_elementwise_groups(self) -> None:
+        """Inline single-consumer elementwise parents of the same shape."""
+        self._ew_groups: Dict[object, tuple] = {}
+        candidates = [n for n in self.order
+                      if is_ew(n) and n not in self._low and n not in self._val
+                      and n not in self.claimed and n not in self.units]
+        cand = set(candidates)
+        absorbed: Set[object] = set()
+        for child in candidates:
+            for p in child.inputs:
+                if (p in cand and p.shape == child.shape and p not in self.output_set
+                        and len(self.consumers.get(p, ())) == 1):
+                    absorbed.add(p)
+        for root in candidates:
+            if root in absorbed:
+                continue
+            mine = set()
+            stack = [root]
+            while stack:
+                n = stack.pop()
+                for p in n.inputs:
+                    if p in absorbed and p not in mine:
+                        mine.add(p)
+                        stack.append(p)
+            inputs, instrs = self._ew_tree(root, mine)
+            while len(inputs) > _lib.EW_MAX_INPUTS or len(instrs) > _lib.EW_MAX_INSTR:
+                # too big: stop absorbing the root's direct parents
+                for p in root.inputs:
+                    mine.discard(p)
+                    absorbed.discard(p)
+                inputs, instrs = self._ew_tree(root, mine)
+                if len(inputs) > _lib.EW_MAX_INPUTS:
+                    raise PlanError("elementwise node with too many operands")
+            self._ew_groups[root] = (inputs, instrs)
+        for n in absorbed:
+            self.claimed.add(n)
+
+    def _emit_reduce(self, node) -> None:
+        src = self.value(node.inputs[0])
+        how, axes, keepdims = node.arg
+        axes = tuple(axes)
+        keep = [d for d in range(len(src.shape)) if d not in axes]
+        dt = self.rdt(node)
+        out = self.tmp(node.shape, dt)
+        sequential = how == "sum" and dt.name in ("bfloat16", "float16")
+        self.add_step("reduce", out, f"reduce_{how}({self._name(src)}, axis={axes})",
+                      src=src, how=how, keep=keep, red=list(axes), sequential=sequential)
+        self.set_value(node, out)
+
+    def _emit_matmul(self, node) -> None:
+        a, b = (self.value(p) for p in node.inputs)
+        out = self.tmp(node.shape, self.rdt(node))
+        self.add_step("matmul", out, f"matmul({self._name(a)}, {self._name(b)})", a=a, b=b)
+        self.set_value(node, out)
+
+    def _emit_gather(self, node) -> None:
+        table = self.contiguous(self.value(node.inputs[0]))
+        idx = self.contiguous(self.value(node.inputs[1]))
+        if np.dtype(idx.dtype).name not in ("int32", "int64"):
+            raise PlanError("gather indices must be int32 or int64 on cuda-b200")
+        out = self.tmp(node.shape, self.rdt(node))
+        self.add_step("gather", out, f"gather({self._name(table)}, {self._name(idx)})",
+                      table=table, idx=idx, flag=self.error_flag())
+        self.set_value(node, out)
+
+    # lowerings --------------------------------------------------------
+    def _emit_rms_norm(self, node, low) -> None:
+        x, w = (self.contiguous(self.value(p)) for p in low[1])
+        spec = self._rms[node]
+        out = self.tmp(node.shape, spec.out_dtype)
+        self.plan.lowered["rms_norm"] = self.plan.lowered.get("rms_norm", 0) + 1
+        self.add_step("rms_norm", out, f"rms_norm({self._name(x)}, {self._name(w)}, "
+                      f"eps={spec.eps!r}, divisor={spec.divisor!r})", x=x, w=w, spec=spec)
+        self.set_value(node, out)
+
+    def rope_tables(self, node) -> Tuple[Buffer, Buffer, int]:
+        info = self._rope[node]
+        if info[0] == "table":
+            _, cos, sin = info
+            return self.aux(cos), self.aux(sin), 1
+        _, theta, dtype, tokens, hd = info
+        key = ("rope", theta, np.dtype(dtype).str, tokens, hd, self.max_positions)
+        cached = self.table_cache.get(key)
+        if cached is None:
+            from .frontend.llama import rope_angles
+
+            angles = rope_angles(self.max_positions + tokens - 1, hd, theta)
+            cos = np.cos(angles).astype(dtype).astype(np.float32)
+            sin = np.sin(angles).astype(dtype).astype(np.float32)
+            # row p of offset o is angle o + p: [n_offsets][T][half]
+            idx = np.arange(self.max_positions)[:, None] + np.arange(tokens)[None, :]
+            cached = (cos[idx].copy(), sin[idx].copy())
+            self.table_cache[key] = cached
+        return self.aux(cached[0]), self.aux(cached[1]), self.max_positions
+
+    def _emit_rope(self, node, low) -> None:
+        x = self.value(low[1][0])
+        cos, sin, n_off = self.rope_tables(node)
+        offset = self.contiguous(self.value(low[1][1])) if len(low[1]) == 2 else None
+        out = self.tmp(node.shape, self.rdt(node))
+        self.plan.lowered["rope"] = self.plan.lowered.get("rope", 0) + 1
+        self.add_step("rope", out, f"rope({self._name(x)}, theta={low[2][1]!r})", x=x, cos=cos,
+                      sin=sin, n_offsets=n_off, offset=offset, flag=self.error_flag())
+        self.set_value(node, out)
+
+    def _emit_sdpa(self, node, low) -> None:
+        q, k, v, mask = (self.value(p) for p in low[1])
+        out = self.tmp(node.shape, F32)
+        self.plan.lowered["sdpa"] = self.plan.lowered.get("sdpa", 0) + 1
+        self.add_step("sdpa", out, f"sdpa({self._name(q)}, {self._name(k)}, {self._name(v)}, "
+                      f"mask={self._name(mask)}, divisor={self._sdpa[node]!r})",
+                      q=q, k=k, v=v, mask=mask, divisor=self._sdpa[node])
+        self.set_value(node, out)
+
+    # ------------------------------------------------------------ source
+    def _source(self) -> str:
+        lines = ["def run(inputs):"]
+        for buf in self.plan.buffers:
+            if buf.kind == "input":
+                lines.append(f"    {buf.name} = input({buf.bind}) {buf.shape} {buf.dtype}")
+        for step in self.plan.steps:
+            target = self._name(step.out) if step.out is not None else "_"
+            lines.append(f"    {target} = {step.text}")
+        outs = ", ".join(self._name(v) + (" (in place)" if i in self.plan.aliases else "")
+                         for i, (_, v) in enumerate(self.plan.outputs))
+        lines.append(f"    return ({outs},)")
+        return "\n".join(lines)

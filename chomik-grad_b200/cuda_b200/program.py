@@ -1,0 +1,517 @@
+"""Execution of a :class:`~cuda_b200.planner.Plan` on the GPU.
+
+A program owns a static set of device buffers (intermediates, tables,
+scratch, and slots for inputs that are copied in), so its launch sequence has
+fixed pointers and is recorded once into a CUDA graph and replayed: one
+``cudaGraphLaunch`` per ``run`` instead of the reference's per-node Python
+dispatch (chomikgrad/lazy.py:487-492, cuda_backend.py:55-69).
+
+Input binding follows ``CompiledProgram.run`` (chomikgrad/lazy.py:158-165):
+bound dynamic inputs are used for this run only, unbound leaves use their
+cached native value or upload their host value (cache_native leaves once,
+others every run, so host mutation of ``copy=False`` tensors is observed).
+Small inputs are copied into program-owned slots; KV caches that the plan
+updates in place are bound by pointer and returned as the same objects.
+Other outputs are fresh arrays owned by the caller.
+
+Graphs are keyed by the addresses of pointer-bound inputs; a key seen twice
+is captured and replayed from then on.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Mapping, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import _lib
+from .device import DeviceArray, torch_dtype
+from .frontend.lazy import CompiledProgram
+from .planner import Buffer, Plan, Step, View, contiguous_strides
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+class CudaB200Program(CompiledProgram):
+    """A compiled graph: static buffers + a replayable launch sequence."""
+
+    def __init__(self, plan: Plan, compiler) -> None:
+        self.plan = plan
+        self.source = plan.source
+        self.inputs = plan.inputs
+        self.device = compiler.device
+        self._compiler = compiler
+        self._built = False
+        self._tensors: Dict[Buffer, object] = {}
+        self._ptr: Dict[Buffer, int] = {}
+        self._graphs: Dict[tuple, int] = {}
+        self._seen: Dict[tuple, int] = {}
+        self._capture_stream: Optional[int] = None
+        self.use_graphs = compiler.use_graphs
+        self.launches = 0  # kernels launched by the last eager run (graph replays re-run them)
+
+    # ------------------------------------------------------------ build
+    def _build(self) -> None:
+        torch = _torch()
+        dev = self.device.torch_device
+        for buf in self.plan.buffers:
+            if buf.kind == "input" and buf.bind == "pointer":
+                continue  # bound per run
+            if buf.kind == "aux" and buf.host is not None:
+                arr = self.device.array(buf.host)
+                self._tensors[buf] = arr.tensor
+            else:
+                count = max(buf.size, 1)
+                tensor = (torch.zeros if buf.zero else torch.empty)(
+                    count, dtype=torch_dtype(buf.dtype), device=dev)
+                self._tensors[buf] = tensor
+            self._ptr[buf] = int(self._tensors[buf].data_ptr())
+        self._bind_constants()
+        stream = self.device.stream()
+        for init in self.plan.init_steps:
+            if init["name"] == "rms_table":
+                self._rms_table(init, stream)
+        self._built = True
+
+    def _rms_table(self, init, stream: int) -> None:
+        table: View = init["table"]
+        spec = init["spec"]
+        leaf_ptr = self._leaf_pointer(table.buf)
+        args = self._rms_args(leaf_ptr, table.dtype, table.shape[0], table.shape[1], spec)
+        _lib.call("cb_rmsnorm_row_table", ctypes.byref(args), self._ptr[init["out"]], stream)
+
+    # ------------------------------------------------------------ inputs
+    def _load(self, leaf) -> DeviceArray:
+        """Native value of an unbound leaf (lazy.py:94-104; cuda_backend.py:395-401)."""
+        name = self.device.name
+        native = leaf.native_values.get(name)
+        if native is not None:
+            return native
+        arr = self.device.array(leaf.numpy_value())
+        if leaf.cache_native:
+            leaf.native_values[name] = arr
+        return arr
+
+    def _leaf_pointer(self, buf: Buffer) -> int:
+        if buf in self._ptr:
+            return self._ptr[buf]
+        return self._load(buf.node).data_ptr()
+
+    def _bind_constants(self) -> None:
+        """Resolve immutable (cache_native, non-dynamic) leaves once per program."""
+        self._constants = {}
+        self._per_run = []
+        for leaf, buf in self.plan.input_buffers.items():
+            if buf.bind == "pointer" and leaf.cache_native and leaf not in self.plan.dynamic:
+                arr = self._load(leaf)
+                self._check(arr, buf)
+                self._constants[leaf] = arr
+                self._ptr[buf] = arr.data_ptr()
+            else:
+                self._per_run.append((leaf, buf))
+
+    @staticmethod
+    def _check(arr: DeviceArray, buf: Buffer) -> None:
+        if tuple(arr.shape) != tuple(buf.shape):
+            raise ValueError(f"input bound with shape {arr.shape}, program expects {buf.shape}")
+        if np.dtype(arr.dtype) != np.dtype(buf.dtype):
+            raise TypeError(f"input bound with dtype {arr.dtype}, program was compiled for "
+                            f"{buf.dtype}; compile a new program for this dtype")
+
+    def _bind(self, bindings: Mapping) -> Tuple[Dict[object, DeviceArray], tuple]:
+        bound: Dict[object, DeviceArray] = dict(self._constants)
+        key = []
+        for leaf, buf in self._per_run:
+            if leaf in bindings:
+                arr = self.device.array(bindings[leaf])
+            else:
+                arr = self._load(leaf)
+            self._check(arr, buf)
+            bound[leaf] = arr
+            if buf.bind == "pointer":
+                self._ptr[buf] = arr.data_ptr()
+                key.append(self._ptr[buf])
+            else:
+                slot = self._tensors[buf]
+                n = max(buf.size, 1)
+                if arr.size:
+                    slot[:n].copy_(arr.tensor[:n], non_blocking=True)
+        return bound, tuple(key)
+
+    # ------------------------------------------------------------ run
+    def run(self, bindings: Optional[Mapping] = None, *, synchronize: bool = False) -> Tuple[object, ...]:
+        torch = _torch()
+        with torch.cuda.device(self.device.torch_device):
+            if not self._built:
+                self._build()
+            for leaf, expected in self.plan.guards:
+                if not np.array_equal(np.asarray(leaf.numpy_value()), expected):
+                    raise RuntimeError("a constant the program was specialised on has changed; "
+                                       "compile the graph again")
+            bound, key = self._bind(bindings or {})
+            self._last_key = key
+            stream = self.device.stream()
+            exec_ = self._graphs.get(key)
+            if exec_ is not None:
+                _lib.call("cb_graph_launch", exec_, stream)
+            else:
+                self._seen[key] = self._seen.get(key, 0) + 1
+                if self.use_graphs and self._seen[key] >= 2 and len(self._graphs) < 8:
+                    exec_ = self._capture()
+                    self._graphs[key] = exec_
+                    _lib.call("cb_graph_launch", exec_, stream)
+                else:
+                    self._launch_all(stream)
+            outputs = self._collect(bound)
+            if synchronize:
+                self.device.synchronize()
+                self.check_errors()
+        return outputs
+
+    # ------------------------------------------------ device-side driving
+    def slot_pointer(self, leaf) -> int:
+        """Device address of the program-owned slot a small dynamic input is copied into."""
+        buf = self.plan.input_buffers[leaf]
+        if buf.bind != "copy":
+            raise ValueError("this input is bound by pointer, it has no slot")
+        return self._ptr[buf]
+
+    def argmax_pointer(self, output_index: int = 0) -> int:
+        """Device address of the int64 argmax the program computes for an output."""
+        return self._ptr[self.plan.argmax_of[output_index]]
+
+    def error_pointer(self) -> int:
+        return self._ptr[self.plan.error_flag] if self.plan.error_flag is not None else 0
+
+    def replay(self, stream: Optional[int] = None) -> None:
+        """Re-run the captured graph of the last ``run`` on the current slot contents.
+
+        No inputs are bound and no outputs are copied out: device-side drivers
+        (cb_decode_advance) update the slots between replays.
+        """
+        exec_ = self._graphs.get(getattr(self, "_last_key", None))
+        if exec_ is None:
+            raise RuntimeError("replay() needs a captured graph: run() the program twice first")
+        _lib.call("cb_graph_launch", exec_, self.device.stream() if stream is None else stream)
+
+    def _capture(self) -> int:
+        if self._capture_stream is None:
+            s = ctypes.c_void_p()
+            _lib.call("cb_stream_create", ctypes.byref(s))
+            self._capture_stream = s.value
+        # the capture stream must see all prior work of the current stream
+        self.device.synchronize()
+        _lib.call("cb_capture_begin", self._capture_stream)
+        try:
+            self._launch_all(self._capture_stream)
+        finally:
+            exec_ = ctypes.c_void_p()
+            status = _lib.load().cb_capture_end(self._capture_stream, ctypes.byref(exec_))
+        _lib.check(status, "cb_capture_end")
+        return exec_.value
+
+    def _collect(self, bound: Dict[object, DeviceArray]) -> Tuple[object, ...]:
+        torch = _torch()
+        outs: List[DeviceArray] = []
+        for index, (node, view) in enumerate(self.plan.outputs):
+            alias = self.plan.aliases.get(index)
+            if alias is not None:
+                outs.append(bound[alias])
+                continue
+            if node.op is None and node in bound:
+                outs.append(bound[node])
+                continue
+            outs.append(self._copy_out(view, node.shape))
+            argmax = self.plan.argmax_of.get(index)
+            if argmax is not None:
+                status = torch.zeros(2, dtype=torch.int64, device=self.device.torch_device)
+                status[:1].copy_(self._tensors[argmax][:1])
+                if self.plan.error_flag is not None:
+                    status[1:].copy_(self._tensors[self.plan.error_flag][:1])
+                outs[-1].argmax_value = status
+        return tuple(outs)
+
+    def _copy_out(self, view: View, shape) -> DeviceArray:
+        torch = _torch()
+        count = int(np.prod(shape)) if len(shape) else 1
+        out = torch.empty(max(count, 1), dtype=torch_dtype(view.dtype), device=self.device.torch_device)
+        base = self._ptr.get(view.buf)
+        if base is None:
+            base = self._leaf_pointer(view.buf)
+        if count:
+            if view.is_contiguous():
+                src = self._tensors.get(view.buf)
+                if src is not None:
+                    out[:count].copy_(src[view.offset: view.offset + count])
+                else:
+                    _lib.call("cb_copy_strided", base, view.offset, out.data_ptr(),
+                              view.dtype.itemsize, 1, _lib.ll_array([count]), _lib.ll_array([1]),
+                              self.device.stream())
+            else:
+                _lib.call("cb_copy_strided", base, view.offset, out.data_ptr(), view.dtype.itemsize,
+                          len(view.shape), _lib.ll_array(view.shape), _lib.ll_array(view.strides),
+                          self.device.stream())
+        return DeviceArray(out, tuple(shape), view.dtype)
+
+    def check_errors(self) -> None:
+        """Raise if a kernel flagged an out-of-range index (gather, position)."""
+        if self.plan.error_flag is None:
+            return
+        flag = self._tensors[self.plan.error_flag]
+        value = int(flag[0].item())
+        if value:
+            flag.zero_()
+            if value == 1:
+                raise IndexError("gather index is outside the first dimension")
+            raise IndexError("RoPE position is outside the precomputed table")
+
+    # ------------------------------------------------------------ launches
+    def ptr(self, view: View) -> int:
+        base = self._ptr.get(view.buf)
+        if base is None:
+            base = self._leaf_pointer(view.buf)
+        return base + view.offset * view.dtype.itemsize
+
+    def _launch_all(self, stream: int) -> None:
+        for step in self.plan.steps:
+            getattr(self, f"_step_{step.name}")(step, stream)
+        self.launches = len(self.plan.steps)
+
+    def _step_copy(self, step: Step, stream: int) -> None:
+        src: View = step.args["src"]
+        if src.size == 0:
+            return
+        _lib.call("cb_copy_strided", self.ptr(src), 0, self.ptr(step.out), src.dtype.itemsize,
+                  len(src.shape), _lib.ll_array(src.shape), _lib.ll_array(src.strides), stream)
+
+    def _step_elementwise(self, step: Step, stream: int) -> None:
+        shape = step.args["shape"]
+        nd = len(shape)
+        a = _lib.ElementwiseArgs()
+        a.ndim = nd
+        a.out_dtype = _lib.dtype_code(step.out.dtype)
+        for d, n in enumerate(shape):
+            a.shape[d] = n
+        views: Sequence[View] = step.args["inputs"]
+        a.n_inputs = len(views)
+        for i, v in enumerate(views):
+            a.inputs[i] = self.ptr(v)
+            a.in_dtype[i] = _lib.dtype_code(v.dtype)
+            a.in_offset[i] = 0
+            lead = nd - len(v.shape)
+            for d in range(nd):
+                j = d - lead
+                a.in_strides[i][d] = 0 if j < 0 or v.shape[j] == 1 else v.strides[j]
+        instrs = step.args["instrs"]
+        a.n_instr = len(instrs)
+        for t, (name, lhs, rhs, dt) in enumerate(instrs):
+            a.op[t] = _lib.OPS[name]
+            a.lhs[t] = lhs
+            a.rhs[t] = rhs
+            a.round[t] = _lib.dtype_code(dt)
+        a.out = self.ptr(step.out)
+        _lib.call("cb_elementwise", ctypes.byref(a), stream)
+
+    def _step_reduce(self, step: Step, stream: int) -> None:
+        src: View = step.args["src"]
+        a = _lib.ReduceArgs()
+        a.in_ = self.ptr(src)
+        a.in_dtype = _lib.dtype_code(src.dtype)
+        a.out = self.ptr(step.out)
+        a.out_dtype = _lib.dtype_code(step.out.dtype)
+        a.kind = _lib.REDUCE_SUM if step.args["how"] == "sum" else _lib.REDUCE_MAX
+        a.sequential = int(step.args["sequential"])
+        a.acc_dtype = _lib.dtype_code(step.out.dtype)
+        keep, red = step.args["keep"], step.args["red"]
+        a.n_keep, a.n_red = len(keep), len(red)
+        for i, d in enumerate(keep):
+            a.keep_shape[i] = src.shape[d]
+            a.keep_strides[i] = src.strides[d]
+        for i, d in enumerate(red):
+            a.red_shape[i] = src.shape[d]
+            a.red_strides[i] = src.strides[d]
+        _lib.call("cb_reduce", ctypes.byref(a), stream)
+
+    def _step_matmul(self, step: Step, stream: int) -> None:
+        av: View = step.args["a"]
+        bv: View = step.args["b"]
+        out = step.out
+        batch = tuple(out.shape[:-2])
+        if len(batch) > _lib.MM_MAX_BATCH:
+            raise _lib.KernelError("matmul: too many batch dimensions")
+        a = _lib.MatmulArgs()
+        a.a, a.a_dtype = self.ptr(av), _lib.dtype_code(av.dtype)
+        a.b, a.b_dtype = self.ptr(bv), _lib.dtype_code(bv.dtype)
+        a.c, a.c_dtype = self.ptr(out), _lib.dtype_code(out.dtype)
+        a.m, a.k = av.shape[-2], av.shape[-1]
+        a.n = bv.shape[-1]
+        a.a_rs, a.a_cs = av.strides[-2], av.strides[-1]
+        a.b_rs, a.b_cs = bv.strides[-2], bv.strides[-1]
+        a.batch_ndim = len(batch)
+        for d, n in enumerate(batch):
+            a.batch_shape[d] = n
+            for view, target in ((av, a.a_bstride), (bv, a.b_bstride)):
+                j = d - (len(batch) - (len(view.shape) - 2))
+                target[d] = 0 if j < 0 or view.shape[j] == 1 else view.strides[j]
+        _lib.call("cb_matmul", ctypes.byref(a), stream)
+
+    def _step_gather(self, step: Step, stream: int) -> None:
+        table: View = step.args["table"]
+        idx: View = step.args["idx"]
+        rows = table.shape[0]
+        row_bytes = int(np.prod(table.shape[1:])) * table.dtype.itemsize
+        _lib.call("cb_gather", self.ptr(table), rows, row_bytes, self.ptr(idx),
+                  _lib.dtype_code(idx.dtype), idx.size, self.ptr(step.out),
+                  self._ptr[step.args["flag"]], stream)
+
+    def _rms_args(self, x_ptr: int, x_dtype, rows: int, width: int, spec) -> _lib.RmsNormArgs:
+        a = _lib.RmsNormArgs()
+        a.x, a.x_dtype = x_ptr, _lib.dtype_code(x_dtype)
+        a.rows, a.width, a.x_row_stride, a.x_offset = rows, width, width, 0
+        a.divisor, a.eps = spec.divisor, spec.eps
+        (a.dt_sq, a.dt_sum, a.dt_mean, a.dt_t, a.dt_d, a.dt_y) = (_lib.dtype_code(d) for d in spec.dts)
+        return a
+
+    def _step_rms_norm(self, step: Step, stream: int) -> None:
+        x: View = step.args["x"]
+        w: View = step.args["w"]
+        width = x.shape[-1] if x.shape else 1
+        rows = x.size // max(width, 1)
+        a = self._rms_args(self.ptr(x), x.dtype, rows, width, step.args["spec"])
+        a.w, a.w_dtype = self.ptr(w), _lib.dtype_code(w.dtype)
+        a.out, a.out_dtype = self.ptr(step.out), _lib.dtype_code(step.out.dtype)
+        _lib.call("cb_rmsnorm", ctypes.byref(a), stream)
+
+    def _step_rope(self, step: Step, stream: int) -> None:
+        x: View = step.args["x"]
+        a = _lib.RopeArgs()
+        a.x, a.x_dtype, a.x_offset = self.ptr(x), _lib.dtype_code(x.dtype), 0
+        for d in range(4):
+            a.x_strides[d] = x.strides[d]
+        a.out, a.out_dtype = self.ptr(step.out), _lib.dtype_code(step.out.dtype)
+        a.batch, a.heads, a.tokens, a.head_size = x.shape
+        a.cos_table = self._ptr[step.args["cos"]]
+        a.sin_table = self._ptr[step.args["sin"]]
+        a.n_offsets = step.args["n_offsets"]
+        offset = step.args["offset"]
+        if offset is not None:
+            a.offset, a.offset_dtype = self.ptr(offset), _lib.dtype_code(offset.dtype)
+        a.error_flag = self._ptr[step.args["flag"]]
+        _lib.call("cb_rope", ctypes.byref(a), stream)
+
+    def _step_sdpa(self, step: Step, stream: int) -> None:
+        q, k, v, mask = (step.args[n] for n in ("q", "k", "v", "mask"))
+        a = _lib.SdpaArgs()
+        for name, view in (("q", q), ("k", k), ("v", v)):
+            setattr(a, name, self.ptr(view))
+            setattr(a, f"{name}_dtype", _lib.dtype_code(view.dtype))
+            target = getattr(a, f"{name}_strides")
+            for d in range(4):
+                target[d] = 0 if view.shape[d] == 1 else view.strides[d]
+        a.mask, a.mask_dtype = self.ptr(mask), _lib.dtype_code(mask.dtype)
+        for d in range(4):
+            a.mask_strides[d] = 0 if mask.shape[d] == 1 else mask.strides[d]
+        a.out = self.ptr(step.out)
+        a.batch, a.heads, a.tq, a.head_size = q.shape
+        a.kv_heads, a.tk = k.shape[1], k.shape[2]
+        a.divisor = step.args["divisor"]
+        _lib.call("cb_sdpa", ctypes.byref(a), stream)
+
+    def _prefetch(self, args, target: Tuple[int, int]) -> None:
+        index, cap = target
+        weights: Sequence[View] = self.plan.steps[index].args["weights"]
+        left = cap
+        for i, w in enumerate(weights[:3]):
+            size = min(w.buf.size * w.dtype.itemsize, left) & ~15
+            if size <= 0:
+                break
+            args.prefetch_ptr[i] = self.ptr(w)
+            args.prefetch_bytes[i] = size
+            left -= size
+
+    def _step_gemv(self, step: Step, stream: int) -> None:
+        g = step.args
+        a = _lib.GemvArgs()
+        weights: Sequence[View] = g["weights"]
+        a.n_w = len(weights)
+        for i, w in enumerate(weights):
+            a.w[i] = self.ptr(w)
+            a.w_rows[i] = g["rows"][i]
+        a.w_dtype = _lib.dtype_code(weights[0].dtype)
+        a.k = g["k"]
+        x: View = g["x"]
+        a.x, a.x_dtype = self.ptr(x), _lib.dtype_code(x.dtype)
+        if g.get("x_index") is not None:
+            a.x_index, a.x_index_dtype = self.ptr(g["x_index"]), _lib.dtype_code(g["x_index"].dtype)
+        spec = g.get("norm")
+        if spec is not None:
+            a.norm = _lib.NORM_RMS_TABLE if g.get("norm_table") is not None else _lib.NORM_RMS
+            a.norm_w, a.norm_w_dtype = self.ptr(g["norm_w"]), _lib.dtype_code(g["norm_w"].dtype)
+            a.divisor, a.eps = spec.divisor, spec.eps
+            (a.dt_sq, a.dt_sum, a.dt_mean, a.dt_t, a.dt_d, a.dt_y) = (_lib.dtype_code(d) for d in spec.dts)
+            a.dt_norm_out = _lib.dtype_code(spec.out_dtype)
+            if g.get("norm_table") is not None:
+                a.norm_table = self._ptr[g["norm_table"]]
+        a.epilogue = g["epilogue"]
+        if g.get("residual") is not None:
+            a.residual, a.residual_dtype = self.ptr(g["residual"]), _lib.dtype_code(g["residual"].dtype)
+            if g.get("residual_index") is not None:
+                a.residual_index = self.ptr(g["residual_index"])
+                a.residual_index_dtype = _lib.dtype_code(g["residual_index"].dtype)
+        a.out = self.ptr(step.out)
+        if g["epilogue"] == _lib.EPI_ARGMAX:
+            a.scratch_val = self._ptr[g["scratch_val"]]
+            a.scratch_idx = self._ptr[g["scratch_idx"]]
+            a.counter = self._ptr[g["counter"]]
+            a.argmax_out = self._ptr[g["argmax"]]
+        if g.get("prefetch") is not None:
+            self._prefetch(a, g["prefetch"])
+        a.grid = self._compiler.gemv_grid
+        a.pdl = int(self._compiler.pdl)
+        _lib.call("cb_gemv", ctypes.byref(a), stream)
+
+    def _step_decode_attention(self, step: Step, stream: int) -> None:
+        g = step.args
+        a = _lib.DecodeAttentionArgs()
+        a.qkv = self.ptr(g["qkv"])
+        a.q_off, a.k_off, a.v_off = g["q_off"], g["k_off"], g["v_off"]
+        a.heads, a.kv_heads, a.head_size, a.context = g["heads"], g["kv_heads"], g["head_size"], g["context"]
+        a.position, a.position_dtype = self.ptr(g["position"]), _lib.dtype_code(g["position"].dtype)
+        a.cos_table, a.sin_table = self._ptr[g["cos"]], self._ptr[g["sin"]]
+        a.n_positions = g["n_positions"]
+        a.k_cache, a.v_cache = self.ptr(g["k_cache"]), self.ptr(g["v_cache"])
+        a.write_mask = self.ptr(g["write_mask"])
+        a.write_mask_dtype = _lib.dtype_code(g["write_mask"].dtype)
+        a.one_minus_dtype = _lib.dtype_code(g["one_minus"])
+        a.mask, a.mask_dtype = self.ptr(g["mask"]), _lib.dtype_code(g["mask"].dtype)
+        a.divisor = g["divisor"]
+        a.out = self.ptr(step.out)
+        a.scratch = self._ptr[g["scratch"]]
+        a.counters = self._ptr[g["counters"]]
+        a.error_flag = self._ptr[g["flag"]]
+        if g.get("prefetch") is not None:
+            self._prefetch(a, g["prefetch"])
+        a.split = 32
+        a.pdl = int(self._compiler.pdl)
+        _lib.call("cb_decode_attention", ctypes.byref(a), stream)
+
+    # ------------------------------------------------------------ cleanup
+    def close(self) -> None:
+        lib = _lib.load()
+        for exec_ in self._graphs.values():
+            lib.cb_graph_destroy(exec_)
+        self._graphs.clear()
+        if self._capture_stream is not None:
+            lib.cb_stream_destroy(self._capture_stream)
+            self._capture_stream = None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,343 @@
+/*
+ * chomik_b200.h -- C ABI of libchomik_b200.so, the sm_100a kernel library
+ * behind chomik-grad's `cuda-b200` compiler plugin.
+ *
+ * Everything here takes raw device pointers, element counts/strides, a dtype
+ * code and a cudaStream_t (passed as void*), and returns an int status:
+ * CB_OK (0) or an error code whose text is available from cb_last_error().
+ * No function allocates device memory; callers own every buffer.
+ *
+ * Each entry point replaces the reference behaviour cited beside it (paths
+ * are inside the chomik-grad project).  The reference runs these operations
+ * through its NumPy `cpu` compiler (chomikgrad/lazy.py:609-636) or CuPy
+ * (chomikgrad/cuda_backend.py:619-701); the Python plugin in
+ * cuda_b200/program.py binds these symbols with ctypes.
+ */
+#ifndef CHOMIK_B200_H
+#define CHOMIK_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes: float32, bfloat16, float16, int32, int64 */
+enum { CB_F32 = 0, CB_BF16 = 1, CB_F16 = 2, CB_I32 = 3, CB_I64 = 4 };
+
+/* status codes */
+enum { CB_OK = 0, CB_ERR_INVALID = 1, CB_ERR_CUDA = 2 };
+
+#define CB_MAX_DIMS 8
+#define CB_EW_MAX_INPUTS 8
+#define CB_EW_MAX_INSTR 40
+#define CB_MM_MAX_BATCH 6
+
+typedef void* cb_stream_t; /* cudaStream_t */
+
+#if defined(__GNUC__)
+#define CB_API __attribute__((visibility("default")))
+#else
+#define CB_API
+#endif
+
+/* ---- library / runtime --------------------------------------------------*/
+CB_API int cb_abi_version(void);
+/* Text of the last error raised on the calling thread ("" if none). */
+CB_API const char* cb_last_error(void);
+/* Number of streaming multiprocessors of the current device. */
+CB_API int cb_sm_count(int* count);
+
+/* Stream-capture helpers for CUDA-graph replay of a compiled program.
+ * Replaces the per-node Python dispatch of build_python_program's generated
+ * `run` (chomikgrad/lazy.py:389-499; CUDAProgram.run cuda_backend.py:55-69). */
+CB_API int cb_stream_create(cb_stream_t* stream);
+CB_API int cb_stream_destroy(cb_stream_t stream);
+CB_API int cb_capture_begin(cb_stream_t stream);
+CB_API int cb_capture_end(cb_stream_t stream, void** graph_exec);
+CB_API int cb_graph_launch(void* graph_exec, cb_stream_t stream);
+CB_API int cb_graph_destroy(void* graph_exec);
+
+/* ---- ELEMENTWISE ---------------------------------------------------------
+ * Fused elementwise expression over a broadcast output shape.
+ * Replaces NumpyCompiler._BINARY/_UNARY (chomikgrad/lazy.py:554-568) and the
+ * CuPy fused elementwise kernel (chomikgrad/cuda_backend.py:703-748).
+ * Register r < n_inputs is input r (converted to float32); register
+ * n_inputs + i is the result of instruction i, rounded to round[i]'s dtype
+ * (CB_F32 = no rounding).  The output is the last instruction's register
+ * (or input 0 when n_instr == 0), stored contiguously as out_dtype. */
+enum {
+  CB_OP_ADD = 0, CB_OP_SUB = 1, CB_OP_MUL = 2, CB_OP_DIV = 3, CB_OP_EQUAL = 4,
+  CB_OP_NEG = 5, CB_OP_EXP = 6, CB_OP_LOG = 7, CB_OP_SQRT = 8, CB_OP_RELU = 9,
+  CB_OP_STEP = 10
+};
+typedef struct {
+  int ndim;
+  int n_inputs;
+  int n_instr;
+  int out_dtype;
+  long long shape[CB_MAX_DIMS];
+  const void* inputs[CB_EW_MAX_INPUTS];
+  int in_dtype[CB_EW_MAX_INPUTS];
+  long long in_strides[CB_EW_MAX_INPUTS][CB_MAX_DIMS]; /* elements; 0 = broadcast */
+  long long in_offset[CB_EW_MAX_INPUTS];
+  int op[CB_EW_MAX_INSTR];
+  int lhs[CB_EW_MAX_INSTR];
+  int rhs[CB_EW_MAX_INSTR];
+  int round[CB_EW_MAX_INSTR];
+  void* out;
+} cb_elementwise_args;
+CB_API int cb_elementwise(const cb_elementwise_args* args, cb_stream_t stream);
+
+/* ---- REDUCE --------------------------------------------------------------
+ * sum / max over `red` dims for every element of the `keep` dims.
+ * Replaces np.sum / np.max(axis, keepdims) (chomikgrad/lazy.py:618-622).
+ * sequential != 0 accumulates in index order rounding to acc_dtype after each
+ * add -- NumPy's loop for bfloat16/float16 data; otherwise a tree order. */
+enum { CB_REDUCE_SUM = 0, CB_REDUCE_MAX = 1 };
+typedef struct {
+  const void* in;
+  int in_dtype;
+  void* out; /* contiguous over keep dims */
+  int out_dtype;
+  int kind;
+  int sequential;
+  int acc_dtype;
+  int n_keep;
+  int n_red;
+  long long in_offset;
+  long long keep_shape[CB_MAX_DIMS];
+  long long keep_strides[CB_MAX_DIMS];
+  long long red_shape[CB_MAX_DIMS];
+  long long red_strides[CB_MAX_DIMS];
+} cb_reduce_args;
+CB_API int cb_reduce(const cb_reduce_args* args, cb_stream_t stream);
+
+/* ---- RESHAPE / PERMUTE materialisation -----------------------------------
+ * out (contiguous) <- strided view of `in`; elem_bytes in {1,2,4,8}.
+ * Replaces the copies np.reshape/np.transpose make for non-viewable layouts
+ * (chomikgrad/lazy.py:624-628). */
+CB_API int cb_copy_strided(const void* in, long long in_offset, void* out, int elem_bytes, int ndim,
+                    const long long* shape, const long long* in_strides, cb_stream_t stream);
+
+/* ---- GATHER --------------------------------------------------------------
+ * out[i, :] = table[idx[i], :] (rows of row_bytes bytes); negative indices
+ * wrap once, out-of-range indices set *error_flag = 1 and write zeros.
+ * Replaces np.take(table, idx, axis=0) (chomikgrad/lazy.py:633-634) and
+ * cp.take (chomikgrad/cuda_backend.py:699-700). */
+CB_API int cb_gather(const void* table, long long rows, long long row_bytes, const void* idx,
+              int idx_dtype, long long n, void* out, int* error_flag, cb_stream_t stream);
+
+/* ---- MATMUL --------------------------------------------------------------
+ * Batched, broadcast C = A @ B with float32 accumulation; C contiguous
+ * (batch..., m, n).  bf16 @ bf16 returns float32 like ml_dtypes.
+ * Replaces np.matmul (chomikgrad/lazy.py:630-631) and cp.matmul/cuBLAS
+ * (chomikgrad/cuda_backend.py:678-698). */
+typedef struct {
+  const void* a;
+  int a_dtype;
+  const void* b;
+  int b_dtype;
+  void* c;
+  int c_dtype;
+  long long m, n, k;
+  long long a_offset, b_offset;
+  long long a_rs, a_cs, b_rs, b_cs; /* element strides of the matrix dims */
+  int batch_ndim;
+  long long batch_shape[CB_MM_MAX_BATCH];
+  long long a_bstride[CB_MM_MAX_BATCH];
+  long long b_bstride[CB_MM_MAX_BATCH];
+} cb_matmul_args;
+CB_API int cb_matmul(const cb_matmul_args* args, cb_stream_t stream);
+
+/* ---- rms_norm lowering ---------------------------------------------------
+ * out = x / sqrt(sum(x*x)/divisor + eps) * w per row, each op rounded to the
+ * dtype the reference graph gives it (dt_*), with a sequential sum when the
+ * square is bf16/f16.  divisor and eps are the values of the graph's constant
+ * leaves.  Replaces LlamaForCausalLM._rms_norm's portable chain
+ * (chomikgrad/llama.py:279-287; MLX lowering mlx_backend.py:410-414).
+ * With d_table != NULL the per-row sqrt term is read from d_table[d_index[r]]
+ * (see cb_rmsnorm_row_table). */
+typedef struct {
+  const void* x;
+  int x_dtype;
+  long long rows, width, x_row_stride, x_offset;
+  const void* x_index; /* optional: row r reads x row x_index[r] */
+  int x_index_dtype;
+  const void* w;
+  int w_dtype;
+  void* out;
+  int out_dtype;
+  float divisor, eps;
+  int dt_sq, dt_sum, dt_mean, dt_t, dt_d, dt_y;
+  const float* d_table;
+} cb_rmsnorm_args;
+CB_API int cb_rmsnorm(const cb_rmsnorm_args* args, cb_stream_t stream);
+/* d_out[r] = rounded sqrt(mean(x_r^2) + eps) for each row of a constant
+ * table, so that rms_norm(gather(table, ids)) costs a lookup at decode time. */
+CB_API int cb_rmsnorm_row_table(const cb_rmsnorm_args* args, float* d_out, cb_stream_t stream);
+
+/* ---- rope lowering -------------------------------------------------------
+ * Rotate-half RoPE of x (B, H, T, hd) with cos/sin rows already rounded to the
+ * rotation matrix dtype: out_j = x_j c_j - x_{j+h} s_j, out_{j+h} =
+ * x_j s_j + x_{j+h} c_j.  Table layout [n_offsets][T][hd/2]; the offset is
+ * read from a device scalar (NULL = 0).  Replaces the dense rotation matmul of
+ * LlamaForCausalLM._apply_rope/_apply_rotation (chomikgrad/llama.py:293-323)
+ * and its table _rope_rotations (:127-152). */
+typedef struct {
+  const void* x;
+  int x_dtype;
+  long long x_offset;
+  long long x_strides[4];
+  void* out; /* contiguous (B, H, T, hd) */
+  int out_dtype;
+  long long batch, heads, tokens, head_size;
+  const float* cos_table;
+  const float* sin_table;
+  long long n_offsets;
+  const void* offset;
+  int offset_dtype;
+  int* error_flag;
+} cb_rope_args;
+CB_API int cb_rope(const cb_rope_args* args, cb_stream_t stream);
+
+/* ---- sdpa lowering -------------------------------------------------------
+ * softmax((q @ k^T) / divisor + mask) @ v with grouped KV heads, float32
+ * accumulation, online softmax.  q (B,H,Tq,D), k/v (B,Hkv,Tk,D), mask
+ * broadcast to (B,H,Tq,Tk) via strides (mask == NULL: none); out contiguous
+ * (B,H,Tq,D) float32.  Replaces the portable attention of
+ * chomikgrad/llama.py:355-364 / :514-525 (repeat_kv :325-330, softmax
+ * chomikgrad/tensor.py:325-334; MLX lowering mlx_backend.py:423-428). */
+typedef struct {
+  const void* q;
+  int q_dtype;
+  long long q_offset, q_strides[4];
+  const void* k;
+  int k_dtype;
+  long long k_offset, k_strides[4];
+  const void* v;
+  int v_dtype;
+  long long v_offset, v_strides[4];
+  const void* mask;
+  int mask_dtype;
+  long long mask_offset, mask_strides[4];
+  float* out;
+  long long batch, heads, kv_heads, tq, tk, head_size;
+  float divisor;
+} cb_sdpa_args;
+CB_API int cb_sdpa(const cb_sdpa_args* args, cb_stream_t stream);
+
+/* ---- decode hot path -----------------------------------------------------*/
+
+/* Streaming GEMV y = x W^T for one token, W in HF (out, in) row-major layout,
+ * with an optional fused rms_norm prologue and a fused epilogue.  Up to three
+ * weight matrices are processed as one logical matrix (rows concatenated),
+ * e.g. q/k/v or gate/up.  Replaces the decode MATMULs of
+ * LlamaForCausalLM._linear (chomikgrad/llama.py:275-277) plus the fused
+ * chains that follow them: residual add (:529-535), SwiGLU silu(gate)*up
+ * (:289-291, :371-380), and greedy argmax of the logits (DeviceAdapter.argmax,
+ * chomikgrad/lazy.py:128-129; cuda_backend.py:37-38).
+ * Scratch (argmax epilogue): scratch_val/scratch_idx hold one entry per CTA
+ * and *counter must be 0 before the first launch (the kernel leaves it 0). */
+enum { CB_NORM_NONE = 0, CB_NORM_RMS = 1, CB_NORM_RMS_TABLE = 2 };
+enum { CB_EPI_STORE = 0, CB_EPI_RESIDUAL = 1, CB_EPI_SILU_MUL = 2, CB_EPI_ARGMAX = 3 };
+typedef struct {
+  const void* w[3];
+  long long w_rows[3];
+  int n_w;
+  int w_dtype;
+  long long k;
+  const void* x;
+  int x_dtype;
+  const void* x_index; /* optional: x row = x + x_index[0] * k */
+  int x_index_dtype;
+  int norm;
+  const void* norm_w;
+  int norm_w_dtype;
+  float divisor, eps;
+  int dt_sq, dt_sum, dt_mean, dt_t, dt_d, dt_y;
+  int dt_norm_out;         /* dtype of the rms_norm output row */
+  const float* norm_table; /* CB_NORM_RMS_TABLE: d per x_index row */
+  int epilogue;
+  const void* residual;
+  int residual_dtype;
+  const void* residual_index; /* optional: residual row = residual + idx * n_out */
+  int residual_index_dtype;
+  float* out;
+  float* scratch_val;
+  long long* scratch_idx;
+  unsigned int* counter;
+  long long* argmax_out;
+  /* L2 prefetch of the NEXT kernel's weights, shared across this grid's
+   * CTAs (16-byte aligned ranges; NULL = none). */
+  const void* prefetch_ptr[3];
+  long long prefetch_bytes[3];
+  int grid; /* 0 = library default */
+  int pdl;  /* launch with programmatic dependent launch */
+} cb_gemv_args;
+CB_API int cb_gemv(const cb_gemv_args* args, cb_stream_t stream);
+/* CTAs cb_gemv launches for these args (size of the argmax scratch). */
+CB_API int cb_gemv_grid(const cb_gemv_args* args, int* grid);
+
+/* Single-token GQA attention over the bound KV cache, fused with RoPE of the
+ * new q/k rows and the in-place cache update.  Replaces, per decode layer,
+ * _apply_rotation for q and k (chomikgrad/llama.py:509-510), the write-mask
+ * blend cache*(1-wm) + key*wm (:511-512), repeat_kv + masked softmax
+ * attention (:514-525).  Rows r with wm[r] != 0 are rewritten with the
+ * blend's float32 arithmetic; every other row is left untouched.
+ * Split-K over the context; partials in `scratch` (splits * heads * (hd + 2)
+ * floats) are combined by the last CTA of each KV group, which resets
+ * counters[g] to 0 (counters must be 0 before the first launch). */
+typedef struct {
+  const float* qkv; /* raw q | k | v projections, float32 */
+  long long q_off, k_off, v_off;
+  long long heads, kv_heads, head_size, context;
+  const void* position;
+  int position_dtype;
+  const float* cos_table; /* [n_positions][hd/2] */
+  const float* sin_table;
+  long long n_positions;
+  float* k_cache; /* (kv_heads, context, hd) float32, updated in place */
+  float* v_cache;
+  const void* write_mask; /* context values */
+  int write_mask_dtype;
+  int one_minus_dtype; /* dtype of (1 - write_mask) in the graph */
+  const void* mask; /* additive attention mask, context values */
+  int mask_dtype;
+  float divisor;
+  float* out; /* heads * hd float32 */
+  float* scratch;
+  unsigned int* counters; /* kv_heads */
+  int* error_flag;
+  const void* prefetch_ptr[3]; /* next kernel's weights, see cb_gemv_args */
+  long long prefetch_bytes[3];
+  int split; /* positions per CTA (0 = default) */
+  int pdl;
+} cb_decode_attention_args;
+CB_API int cb_decode_attention(const cb_decode_attention_args* args, cb_stream_t stream);
+/* Scratch floats cb_decode_attention needs for these args. */
+CB_API long long cb_decode_attention_scratch(const cb_decode_attention_args* args);
+
+/* On-device greedy step driver for back-to-back decode replays: from the
+ * previous step's argmax it writes the next step's token id, position + 1,
+ * attention mask row (position+1 -> 0) and write mask (one-hot at the new
+ * position), exactly what the host loop of
+ * examples/generate_tinyllama.py:772-786 builds each step; token_log[step]
+ * records the token.  Sets *error_flag = 3 instead of writing past the
+ * context. */
+CB_API int cb_decode_advance(const long long* argmax, void* ids, int ids_dtype, void* position,
+                      int position_dtype, void* mask, int mask_dtype, void* write_mask,
+                      int write_mask_dtype, long long context, long long* token_log, long long step,
+                      int* error_flag, cb_stream_t stream);
+
+/* Row-wise argmax with np.argmax semantics (first max, NaN wins).
+ * Replaces DeviceAdapter.argmax / argmax_last_axis (chomikgrad/lazy.py:128-134,
+ * cuda_backend.py:37-41). */
+CB_API int cb_argmax_rows(const void* x, int dtype, long long rows, long long width,
+                   long long* out_index, cb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CHOMIK_B200_H */

@@ -1,0 +1,135 @@
+"""GPU parity of the generic six-op lowering and the rms_norm/rope/sdpa kernels.
+
+Patterns follow the reference's backend tests (tests/test_cuda.py:32-138,
+tests/test_lazy.py:49-63): every result is compared with the reference
+``cpu`` compiler's output -- the golden fixtures for the known answers, the
+restated oracle for random cases.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import golden
+from cuda_b200.frontend.tensor import Tensor, compile_graph
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16():
+    import ml_dtypes
+
+    return np.dtype(ml_dtypes.bfloat16)
+
+
+def test_six_ir_operations_and_gather_match_golden(gpu, oracle):
+    g = golden("six_ops")
+    left, right = Tensor(g["chain_left"]), Tensor(g["chain_right"])
+    result = ((left @ right).relu() + 0.25).permute(1, 0).reshape(1, 4).sum(axis=1)
+    program = compile_graph(result, compiler="cuda-b200")
+    np.testing.assert_allclose(program()[0], g["chain_out"], rtol=1e-5, atol=1e-6)
+    assert "matmul" in program.source and "elementwise" in program.source
+    gathered = Tensor(g["gather_table"]).gather(Tensor(g["gather_idx"], copy=False))
+    out = gathered.numpy(compiler="cuda-b200")
+    assert np.array_equal(out, g["gather_out"])  # bit-exact
+
+
+def test_batched_and_broadcast_matmul_match_golden(gpu, oracle):
+    g = golden("six_ops")
+    np.testing.assert_allclose((Tensor(g["bmm_a"]) @ Tensor(g["bmm_b"])).numpy(compiler="cuda-b200"),
+                               g["bmm_out"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose((Tensor(g["proj_x"]) @ Tensor(g["proj_w"])).numpy(compiler="cuda-b200"),
+                               g["proj_out"], rtol=1e-5, atol=1e-6)
+
+
+def test_softmax_portable_path_matches_golden(gpu, oracle):
+    g = golden("six_ops")
+    np.testing.assert_allclose(Tensor(g["softmax_x"]).softmax(axis=-1).numpy(compiler="cuda-b200"),
+                               g["softmax_out"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(Tensor(g["softmax_x"]).softmax(axis=1).numpy(compiler="cuda-b200"),
+                               g["softmax1_out"], rtol=1e-5, atol=1e-6)
+
+
+def test_bf16_sum_accumulates_sequentially_like_numpy(gpu, oracle):
+    g = golden("six_ops")
+    x = g["bf16_sumsq_x"].view(bf16())
+    t = Tensor(x)
+    out = (t * t).sum(axis=-1, keepdims=True).numpy(compiler="cuda-b200")
+    assert np.array_equal(out.view(np.uint16), g["bf16_sumsq_out"])  # bit-exact
+
+
+def test_dynamic_input_and_deferred_synchronization(gpu):
+    source = Tensor([1.0, 2.0], dtype=np.float32)
+    program = compile_graph(source * 2.0, compiler="cuda-b200", dynamic_inputs=(source,))
+    replacement = program.device.array(np.array([3.0, 4.0], dtype=np.float32))
+    native = program.run({source._node: replacement}, synchronize=False)[0]
+    program.device.synchronize()
+    np.testing.assert_allclose(program.device.to_numpy(native), [6.0, 8.0])
+    assert program.inputs == (source._node,)
+    assert program.device.argmax(native) == 1
+    np.testing.assert_allclose(program()[0], [2.0, 4.0])
+
+
+def test_copy_false_observes_host_mutation(gpu):
+    source = np.array([1.0, 2.0], dtype=np.float32)
+    tensor = Tensor(source, copy=False)
+    np.testing.assert_allclose(tensor.numpy(compiler="cuda-b200"), [1.0, 2.0])
+    source[0] = 9.0
+    np.testing.assert_allclose(tensor.numpy(compiler="cuda-b200"), [9.0, 2.0])
+
+
+def test_repeated_runs_replay_a_graph_and_stay_bit_identical(gpu, oracle):
+    rng = np.random.default_rng(3)
+    x = Tensor(rng.normal(size=(4, 33)).astype(np.float32))
+    w = Tensor(rng.normal(size=(33, 17)).astype(np.float32))
+    out = ((x @ w).exp() / 3.0 - 1.0).max(axis=0)
+    program = compile_graph(out, compiler="cuda-b200")
+    first = program()[0]
+    for _ in range(3):
+        assert np.array_equal(program()[0], first)
+    assert program._graphs, "second and later runs should replay a CUDA graph"
+    np.testing.assert_allclose(first, out.numpy(compiler="cpu"), rtol=1e-5, atol=1e-6)
+
+
+def test_argmax_first_occurrence_and_nan(gpu):
+    device = gpu.device
+    values = np.array([[1.0, 5.0, 5.0, -2.0]], dtype=np.float32)
+    assert device.argmax(device.array(values)) == 1
+    with_nan = np.array([1.0, np.nan, 7.0, np.nan], dtype=np.float32)
+    assert device.argmax(device.array(with_nan)) == int(np.argmax(with_nan))
+    rows = np.random.default_rng(5).normal(size=(6, 100)).astype(np.float32)
+    np.testing.assert_array_equal(device.argmax_last_axis(device.array(rows)), rows.argmax(axis=-1))
+
+
+def test_gather_out_of_range_raises(gpu):
+    table = Tensor(np.arange(6, dtype=np.float32).reshape(3, 2))
+    bad = Tensor(np.array([[0, 3]], dtype=np.int32), copy=False)
+    with pytest.raises(IndexError):
+        table.gather(bad).numpy(compiler="cuda-b200")
+
+
+def test_float64_is_rejected_without_fallback(gpu):
+    with pytest.raises(TypeError):
+        (Tensor([1.0, 2.0]) * 2.0).numpy(compiler="cuda-b200")
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_llama_lowerings_match_portable_cpu_graph(gpu, oracle, dtype):
+    """rms_norm/rope/sdpa lowerings on a 1-layer model (pattern of test_mlx.py:120-158)."""
+    from cuda_b200.frontend.llama import LlamaConfig, LlamaForCausalLM, position_selector, required_weight_shapes
+
+    dt = np.dtype(np.float32) if dtype == "float32" else bf16()
+    config = LlamaConfig(vocab_size=64, hidden_size=64, intermediate_size=96, num_hidden_layers=1,
+                         num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=16)
+    rng = np.random.default_rng(23)
+    weights = {name: Tensor(np.ones(shape, np.float32).astype(dt) if "norm.weight" in name
+                            else rng.normal(0, 0.05, shape).astype(np.float32).astype(dt))
+               for name, shape in required_weight_shapes(config).items()}
+    model = LlamaForCausalLM(config, weights, sequence_length=5, dtype=dt)
+    output = model(Tensor(np.array([[1, 3, 4, 9, 2]], dtype=np.int32), copy=False),
+                   Tensor(position_selector(4, 5, dtype=dt), copy=False))
+    program = compile_graph(output, compiler="cuda-b200")
+    for name in ("rms_norm", "rope", "sdpa", "gather"):
+        assert name in program.source
+    np.testing.assert_allclose(program()[0], output.numpy(compiler="cpu"), rtol=2e-4, atol=2e-5)
