@@ -89,7 +89,11 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const cb_gemv_args a, lo
   pdl_launch_dependents();
 
   // ---- stage (and normalise) the input row ----
-  const long long xrow = a.x_index != nullptr ? load_index(a.x_index, 0, a.x_index_dtype) : 0;
+  long long xrow = a.x_index != nullptr ? load_index(a.x_index, 0, a.x_index_dtype) : 0;
+  if (a.x_index != nullptr && (xrow < 0 || xrow >= a.index_rows)) {
+    if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 1);
+    xrow = 0;
+  }
   for (long long i = tid; i < K; i += kThreads) xs[i] = load_as_f32(a.x, xrow * K + i, a.x_dtype);
   __syncthreads();
   if (a.norm != CB_NORM_NONE) {
@@ -170,9 +174,15 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const cb_gemv_args a, lo
       if (a.epilogue == CB_EPI_STORE) {
         a.out[u] = v;
       } else if (a.epilogue == CB_EPI_RESIDUAL) {
-        const long long rrow = a.residual_index != nullptr
-                                   ? load_index(a.residual_index, 0, a.residual_index_dtype) * units
-                                   : 0;
+        long long rrow = 0;
+        if (a.residual_index != nullptr) {
+          rrow = load_index(a.residual_index, 0, a.residual_index_dtype);
+          if (rrow < 0 || rrow >= a.index_rows) {
+            if (a.error_flag != nullptr) atomicExch(a.error_flag, 1);
+            rrow = 0;
+          }
+          rrow *= units;
+        }
         a.out[u] = __fadd_rn(load_as_f32(a.residual, rrow + u, a.residual_dtype), v);
       } else if ((tid & 1) == 0) {  // CB_EPI_SILU_MUL: even unit = gate, odd = up
         const float up = tot[tid + 1];
@@ -249,6 +259,8 @@ int plan_gemv(const cb_gemv_args& a, Plan* p) {
   if (a.epilogue == CB_EPI_RESIDUAL) CB_REQUIRE(a.residual != nullptr, "gemv: residual missing");
   if (a.norm != CB_NORM_NONE) CB_REQUIRE(a.norm_w != nullptr, "gemv: norm weight missing");
   if (a.norm == CB_NORM_RMS_TABLE) CB_REQUIRE(a.norm_table && a.x_index, "gemv: norm table needs x_index");
+  if (a.x_index != nullptr || a.residual_index != nullptr)
+    CB_REQUIRE(a.index_rows > 0, "gemv: indexed rows need index_rows");
   return CB_OK;
 }
 

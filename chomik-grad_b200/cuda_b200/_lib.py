@@ -115,6 +115,7 @@ class GemvArgs(ctypes.Structure):
         ("w", c_void_p * 3), ("w_rows", c_longlong * 3), ("n_w", c_int), ("w_dtype", c_int),
         ("k", c_longlong),
         ("x", c_void_p), ("x_dtype", c_int), ("x_index", c_void_p), ("x_index_dtype", c_int),
+        ("index_rows", c_longlong), ("error_flag", c_void_p),
         ("norm", c_int), ("norm_w", c_void_p), ("norm_w_dtype", c_int),
         ("divisor", c_float), ("eps", c_float),
         ("dt_sq", c_int), ("dt_sum", c_int), ("dt_mean", c_int), ("dt_t", c_int),

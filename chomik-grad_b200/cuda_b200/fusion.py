@@ -421,6 +421,8 @@ class DecodeFusion:
                 rv = p.contiguous(p.value(residual))
                 args.update(residual=rv)
                 text.append(f"residual={p._name(rv)}")
+        if "x_index" in args or "residual_index" in args:
+            p.error_flag()  # out-of-range token ids are reported, not read
         if epilogue == _lib.EPI_ARGMAX:
             args.update(scratch_val=p.aux(shape=(2048,), dtype=np.float32),
                         scratch_idx=p.aux(shape=(2048,), dtype=np.int64),

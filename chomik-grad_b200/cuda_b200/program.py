@@ -448,6 +448,11 @@ class CudaB200Program(CompiledProgram):
         a.x, a.x_dtype = self.ptr(x), _lib.dtype_code(x.dtype)
         if g.get("x_index") is not None:
             a.x_index, a.x_index_dtype = self.ptr(g["x_index"]), _lib.dtype_code(g["x_index"].dtype)
+            a.index_rows = x.shape[0]
+        if g.get("residual_index") is not None:
+            a.index_rows = g["residual"].shape[0]
+        if self.plan.error_flag is not None:
+            a.error_flag = self._ptr[self.plan.error_flag]
         spec = g.get("norm")
         if spec is not None:
             a.norm = _lib.NORM_RMS_TABLE if g.get("norm_table") is not None else _lib.NORM_RMS

@@ -251,6 +251,8 @@ typedef struct {
   int x_dtype;
   const void* x_index; /* optional: x row = x + x_index[0] * k */
   int x_index_dtype;
+  long long index_rows; /* rows of the tables x_index/residual_index select from */
+  int* error_flag;      /* set to 1 (and row 0 used) when an index is out of range */
   int norm;
   const void* norm_w;
   int norm_w_dtype;
