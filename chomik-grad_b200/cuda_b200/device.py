@@ -99,17 +99,16 @@ def empty(shape: Sequence[int], dtype: np.dtype, device: Any) -> DeviceArray:
 def upload(value: np.ndarray, device: Any) -> DeviceArray:
     """Copy a host array to a new dense device buffer."""
     torch = _torch()
-    host = np.ascontiguousarray(value)
-    dtype = host.dtype
+    host = np.asarray(value)
+    shape, dtype = host.shape, host.dtype
+    flat = np.ascontiguousarray(host).reshape(-1)  # (ascontiguousarray makes 0-d arrays 1-d)
     if dtype.name == "bfloat16":
-        tensor = torch.from_numpy(host.reshape(-1).view(np.int16)).to(device).view(torch.bfloat16)
-    elif dtype == np.bool_:
-        tensor = torch.from_numpy(host.reshape(-1)).to(device)
+        tensor = torch.from_numpy(flat.view(np.int16)).to(device).view(torch.bfloat16)
     else:
-        tensor = torch.from_numpy(host.reshape(-1)).to(device)
+        tensor = torch.from_numpy(flat).to(device)
     if tensor.numel() == 0:
         tensor = torch.empty(1, dtype=torch_dtype(dtype), device=device)
-    return DeviceArray(tensor, host.shape, dtype)
+    return DeviceArray(tensor, shape, dtype)
 
 
 def download(array: DeviceArray) -> np.ndarray:

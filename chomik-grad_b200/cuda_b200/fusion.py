@@ -260,7 +260,7 @@ class DecodeFusion:
             cos, sin, n_pos = p.rope_tables(q)
             splits = -(-ctx // 32)
             scratch = p.aux(shape=(splits * heads * (hd + 2),), dtype=np.float32)
-            counters = p.aux(shape=(kvh,), dtype=np.uint32, zero=True)
+            counters = p.aux(shape=(kvh,), dtype=np.int32, zero=True)  # used as unsigned
             p.add_step(
                 "decode_attention", out,
                 f"decode_attention(qkv={p._name(qkv)}, kv=({p._name(kview)}, {p._name(vview)}), "
@@ -426,7 +426,7 @@ class DecodeFusion:
         if epilogue == _lib.EPI_ARGMAX:
             args.update(scratch_val=p.aux(shape=(2048,), dtype=np.float32),
                         scratch_idx=p.aux(shape=(2048,), dtype=np.int64),
-                        counter=p.aux(shape=(1,), dtype=np.uint32, zero=True),
+                        counter=p.aux(shape=(1,), dtype=np.int32, zero=True),
                         argmax=p.aux(shape=(1,), dtype=np.int64, zero=True))
             for i, o in enumerate(p.outputs):
                 if o is lins[0].node:
