@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const cb_dec
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, warps = blockDim.x >> 5;
 
   prefetch_share(a.prefetch_ptr, a.prefetch_bytes, static_cast<long long>(g) * splits + split,
-                 static_cast<long long>(splits) * gridDim.y);
+                 static_cast<long long>(splits) * gridDim.y, tid, blockDim.x);
   pdl_wait();
   pdl_launch_dependents();
 

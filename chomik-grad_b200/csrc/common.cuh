@@ -112,10 +112,10 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 }
 
 // This CTA's 1/ncta share of up to three byte ranges, prefetched into L2 in
-// 64 KiB pieces by the block's threads.  Ranges must be 16-byte aligned; the
-// caller uses it to stream the NEXT kernel's weights while this one runs.
+// 64 KiB pieces by threads t = 0..nt-1 of the caller.  Ranges must be 16-byte
+// aligned; used to stream the NEXT kernel's weights while this one runs.
 __device__ __forceinline__ void prefetch_share(const void* const* ptrs, const long long* bytes,
-                                               long long cta, long long ncta) {
+                                               long long cta, long long ncta, int t, int nt) {
   long long total = 0;
 #pragma unroll
   for (int i = 0; i < 3; ++i) total += ptrs[i] != nullptr ? bytes[i] : 0;
@@ -130,7 +130,7 @@ __device__ __forceinline__ void prefetch_share(const void* const* ptrs, const lo
     const long long seg_end = seg_start + bytes[i];
     const long long a = lo > seg_start ? lo : seg_start;
     const long long b = hi < seg_end ? hi : seg_end;
-    for (long long p = a + threadIdx.x * kPiece; p < b; p += blockDim.x * kPiece) {
+    for (long long p = a + t * kPiece; p < b; p += static_cast<long long>(nt) * kPiece) {
       const long long n = b - p < kPiece ? b - p : kPiece;
       const long long n16 = n & ~15LL;
       if (n16 > 0)
