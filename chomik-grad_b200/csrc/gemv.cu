@@ -3,63 +3,32 @@
 // Decode is bound by reading every weight byte once from HBM.  Design:
 //  * one CTA per SM owns a contiguous range of "units" (weight rows); a
 //    producer warp streams them with bulk copies (TMA engine,
-//    cp.async.bulk + mbarrier transaction counts) into a ring of ~8 KiB
-//    shared-memory stages -- up to ~96 KiB per SM in flight without any
-//    register cost;
-//  * the producer starts streaming BEFORE the kernel waits on its producer
-//    kernel (programmatic dependent launch: weights never depend on it), and
-//    the CTA also issues an L2 prefetch of its share of the NEXT kernel's
+//    cp.async.bulk + mbarrier transaction counts) into a shared-memory ring
+//    of multi-row stages (>= 16 KiB each, ~128-180 KiB in flight per SM);
+//  * the CTA also issues an L2 prefetch of its share of the NEXT kernel's
 //    weights, so HBM keeps streaming across kernel boundaries;
-//  * eight consumer warps each own whole stages (round robin), so a row's dot
-//    product is reduced inside one warp -- no block-wide barrier in the loop
-//    and a fixed summation order (deterministic results);
+//  * consumer warps own ring slots (slot s belongs to warp s % consumers, so
+//    parity waits are never more than one phase behind) and multiply all R
+//    rows of a stage at once: each 16-byte chunk of x is read from shared
+//    memory once for R rows (x is stored as two conflict-free planes), R
+//    independent FMA chains, one warp reduction per row, fixed order
+//    (deterministic results);
 //  * the input row x (optionally gathered by a device index and rms-normed
-//    with the reference's roundings) is staged once per CTA in shared memory;
+//    with the reference's roundings) is staged once per CTA;
 //  * epilogues fuse the consumers the reference graph applies next:
-//    residual add, SwiGLU silu(gate)*up (gate/up rows interleaved in a
-//    stage), or logits + greedy argmax (last-CTA merge in CTA order).
+//    residual add, SwiGLU silu(gate)*up (stage = [gate rows | up rows]), or
+//    logits + greedy argmax (last-CTA merge in CTA order).
 #include "norm.cuh"
 #include "sync.cuh"
 
 namespace cb {
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + producer warp
-constexpr int kStageTarget = 8 * 1024;                // bytes per ring stage
-constexpr int kRingTarget = 96 * 1024;                // bytes in flight per CTA
-
-template <typename WT>
-struct Vec;
-template <>
-struct Vec<uint16_t> {  // bfloat16 weights: 8 per 16-byte chunk
-  static constexpr int kElems = 8;
-  __device__ static float dot(const uint4& w, const float* xs, float acc) {
-    const float4 x0 = *reinterpret_cast<const float4*>(xs);
-    const float4 x1 = *reinterpret_cast<const float4*>(xs + 4);
-    acc = fmaf(__uint_as_float(w.x << 16), x0.x, acc);
-    acc = fmaf(__uint_as_float(w.x & 0xffff0000u), x0.y, acc);
-    acc = fmaf(__uint_as_float(w.y << 16), x0.z, acc);
-    acc = fmaf(__uint_as_float(w.y & 0xffff0000u), x0.w, acc);
-    acc = fmaf(__uint_as_float(w.z << 16), x1.x, acc);
-    acc = fmaf(__uint_as_float(w.z & 0xffff0000u), x1.y, acc);
-    acc = fmaf(__uint_as_float(w.w << 16), x1.z, acc);
-    acc = fmaf(__uint_as_float(w.w & 0xffff0000u), x1.w, acc);
-    return acc;
-  }
-};
-template <>
-struct Vec<float> {  // float32 weights: 4 per chunk
-  static constexpr int kElems = 4;
-  __device__ static float dot(const uint4& w, const float* xs, float acc) {
-    const float4 x0 = *reinterpret_cast<const float4*>(xs);
-    acc = fmaf(__uint_as_float(w.x), x0.x, acc);
-    acc = fmaf(__uint_as_float(w.y), x0.y, acc);
-    acc = fmaf(__uint_as_float(w.z), x0.z, acc);
-    acc = fmaf(__uint_as_float(w.w), x0.w, acc);
-    return acc;
-  }
-};
+constexpr int kMaxConsumerWarps = 8;
+constexpr int kThreads = (kMaxConsumerWarps + 1) * 32;  // + producer warp
+constexpr int kMaxRows = 8;                               // rows per stage
+constexpr long long kRingBudget = 180 * 1024;
+constexpr long long kSmemBudget = 210 * 1024;
 
 // Weight row of logical unit u.  SwiGLU interleaves gate (even) / up (odd).
 __device__ __forceinline__ const char* unit_row(const cb_gemv_args& a, long long u, long long row_bytes) {
@@ -74,31 +43,115 @@ __device__ __forceinline__ const char* unit_row(const cb_gemv_args& a, long long
 
 struct Layout {
   long long units, per_cta;
-  int grid, stage_units, slots;
+  int grid, rows, slots, consumers;
   long long row_bytes, stage_bytes;
-  size_t ring_bytes, smem;
+  size_t ring_bytes, x_bytes, smem;
 };
 
+// x for chunk c (VE elements) from the two planes: xa = elements 0..3 of each
+// chunk, xb = 4..7 (bf16 chunks only).  Consecutive lanes read consecutive
+// 16-byte words: no bank conflicts.
 template <typename WT>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const cb_gemv_args a, const Layout L) {
+struct Chunk;
+template <>
+struct Chunk<uint16_t> {
+  static constexpr int kElems = 8;
+  float4 a, b;
+  __device__ void load(const float4* xa, const float4* xb, long long c) {
+    a = xa[c];
+    b = xb[c];
+  }
+  __device__ float dot(const uint4& w, float acc) const {
+    acc = fmaf(__uint_as_float(w.x << 16), a.x, acc);
+    acc = fmaf(__uint_as_float(w.x & 0xffff0000u), a.y, acc);
+    acc = fmaf(__uint_as_float(w.y << 16), a.z, acc);
+    acc = fmaf(__uint_as_float(w.y & 0xffff0000u), a.w, acc);
+    acc = fmaf(__uint_as_float(w.z << 16), b.x, acc);
+    acc = fmaf(__uint_as_float(w.z & 0xffff0000u), b.y, acc);
+    acc = fmaf(__uint_as_float(w.w << 16), b.z, acc);
+    acc = fmaf(__uint_as_float(w.w & 0xffff0000u), b.w, acc);
+    return acc;
+  }
+};
+template <>
+struct Chunk<float> {
+  static constexpr int kElems = 4;
+  float4 a;
+  __device__ void load(const float4* xa, const float4*, long long c) { a = xa[c]; }
+  __device__ float dot(const uint4& w, float acc) const {
+    acc = fmaf(__uint_as_float(w.x), a.x, acc);
+    acc = fmaf(__uint_as_float(w.y), a.y, acc);
+    acc = fmaf(__uint_as_float(w.z), a.z, acc);
+    acc = fmaf(__uint_as_float(w.w), a.w, acc);
+    return acc;
+  }
+};
+
+__device__ __forceinline__ void consumers_sync(int n) {
+  asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory");
+}
+
+// R rows of one stage against x: totals[r] (valid on every lane).
+template <typename WT, int R>
+__device__ __forceinline__ void stage_dot(const unsigned char* stage, const long long* row_at,
+                                          long long row_bytes, const float4* xa, const float4* xb,
+                                          long long chunks, int lane, float* totals) {
+  float acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+  const uint4* rows[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) rows[r] = reinterpret_cast<const uint4*>(stage + row_at[r] * row_bytes);
+  long long c = lane;
+  // two chunks per iteration: twice the shared loads in flight
+  for (; c + 32 < chunks; c += 64) {
+    Chunk<WT> x0, x1;
+    x0.load(xa, xb, c);
+    x1.load(xa, xb, c + 32);
+    uint4 w0[R], w1[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      w0[r] = rows[r][c];
+      w1[r] = rows[r][c + 32];
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = x1.dot(w1[r], x0.dot(w0[r], acc[r]));
+  }
+  if (c < chunks) {
+    Chunk<WT> x;
+    x.load(xa, xb, c);
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = x.dot(rows[r][c], acc[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) totals[r] = warp_sum(acc[r]);
+}
+
+template <typename WT>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const cb_gemv_args a, const Layout L) {
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* ring = smem;
-  float* xs = reinterpret_cast<float*>(smem + L.ring_bytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.ring_bytes + ((a.k * 4 + 15) & ~15LL));
+  float* xs = reinterpret_cast<float*>(smem + L.ring_bytes);  // staged x (k floats)
+  float4* xa = reinterpret_cast<float4*>(smem + L.ring_bytes + L.x_bytes);
+  float4* xb = xa + (a.k / 8 + 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.ring_bytes + 2 * L.x_bytes + 32);
   uint64_t* empty = full + L.slots;
-  __shared__ float norm_red[kConsumerWarps + 1];
-  __shared__ float warp_best_v[kConsumerWarps];
-  __shared__ long long warp_best_i[kConsumerWarps];
+  __shared__ float norm_red[kMaxConsumerWarps];
+  __shared__ float total_sq;
+  __shared__ float warp_best_v[kMaxConsumerWarps];
+  __shared__ long long warp_best_i[kMaxConsumerWarps];
   __shared__ int is_last;
 
-  constexpr int VE = Vec<WT>::kElems;
+  constexpr int VE = Chunk<WT>::kElems;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ncons = L.consumers * 32;
   const long long K = a.k;
   const long long chunks = K / VE;
   const long long u0 = static_cast<long long>(blockIdx.x) * L.per_cta;
   const long long u1 = u0 + L.per_cta < L.units ? u0 + L.per_cta : L.units;
   const long long n_units = u1 > u0 ? u1 - u0 : 0;
-  const long long n_stages = (n_units + L.stage_units - 1) / L.stage_units;
+  const long long n_stages = (n_units + L.rows - 1) / L.rows;
+  const bool pairs = a.epilogue == CB_EPI_SILU_MUL;
 
   if (tid == 0) {
     for (int s = 0; s < L.slots; ++s) {
@@ -109,132 +162,173 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const cb_gemv_args a, co
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
+  if (warp == kMaxConsumerWarps) {
     // ---------------- producer: stream this CTA's rows into the ring ----
     pdl_launch_dependents();
-    if (lane == 0) {
-      for (long long s = 0; s < n_stages; ++s) {
+    // Producer lane j feeds consumer warp j: it issues stages j, j + C, ...
+    // into the slots that warp owns, so C lanes issue copies in parallel.
+    if (lane < L.consumers) {
+      for (long long s = lane; s < n_stages; s += L.consumers) {
         const int slot = static_cast<int>(s % L.slots);
         const long long round = s / L.slots;
-        if (s == L.slots)  // ring primed: now ask L2 for the next kernel's weights
+        if (lane == 0 && s == L.slots)  // ring primed: ask L2 for the next kernel's weights
           prefetch_share(a.prefetch_ptr, a.prefetch_bytes, blockIdx.x, gridDim.x, 0, 1);
         if (round > 0 && !mbar_wait(empty + slot, static_cast<uint32_t>((round - 1) & 1))) {
           if (a.error_flag != nullptr) atomicExch(a.error_flag, 4);
           break;
         }
-        const long long first = u0 + s * L.stage_units;
-        const long long last = first + L.stage_units < u1 ? first + L.stage_units : u1;
+        const long long first = u0 + s * L.rows;
+        const long long last = first + L.rows < u1 ? first + L.rows : u1;
         mbar_arrive_expect_tx(full + slot, static_cast<uint32_t>((last - first) * L.row_bytes));
         unsigned char* dst = ring + slot * L.stage_bytes;
-        for (long long u = first; u < last; ++u)
-          bulk_load(dst + (u - first) * L.row_bytes, unit_row(a, u, L.row_bytes),
-                    static_cast<uint32_t>(L.row_bytes), full + slot);
+        if (pairs) {
+          // [gate rows | up rows] of the stage's pairs: two contiguous copies
+          const uint32_t bytes = static_cast<uint32_t>((last - first) / 2 * L.row_bytes);
+          bulk_load(dst, unit_row(a, first, L.row_bytes), bytes, full + slot);
+          bulk_load(dst + (L.rows / 2) * L.row_bytes, unit_row(a, first + 1, L.row_bytes), bytes, full + slot);
+        } else {
+          // one copy per run of rows inside the same weight matrix
+          long long u = first;
+          while (u < last) {
+            long long end = a.w_rows[0];
+            if (u >= end) end += a.w_rows[1];
+            if (u >= end) end += a.w_rows[2];
+            if (end > last) end = last;
+            bulk_load(dst + (u - first) * L.row_bytes, unit_row(a, u, L.row_bytes),
+                      static_cast<uint32_t>((end - u) * L.row_bytes), full + slot);
+            u = end;
+          }
+        }
       }
-      if (n_stages <= L.slots)
+      if (lane == 0 && n_stages <= L.slots)
         prefetch_share(a.prefetch_ptr, a.prefetch_bytes, blockIdx.x, gridDim.x, 0, 1);
     }
     return;
   }
+  if (warp >= L.consumers) return;
 
-  // ---------------- consumers ----------------
+  // ---------------- consumers: stage x (+ norm) ----------------
   pdl_wait();
   pdl_launch_dependents();
-  const int ctid = tid;  // 0 .. 255
-  constexpr int kConsumers = kConsumerWarps * 32;
   long long xrow = a.x_index != nullptr ? load_index(a.x_index, 0, a.x_index_dtype) : 0;
   if (a.x_index != nullptr && (xrow < 0 || xrow >= a.index_rows)) {
-    if (ctid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 1);
+    if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 1);
     xrow = 0;
   }
-  for (long long i = ctid; i < K; i += kConsumers) xs[i] = load_as_f32(a.x, xrow * K + i, a.x_dtype);
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-  if (a.norm != CB_NORM_NONE) {
-    const NormSpec n{a.divisor, a.eps, a.dt_sq, a.dt_sum, a.dt_mean, a.dt_t, a.dt_d, a.dt_y};
-    float d;
-    if (a.norm == CB_NORM_RMS_TABLE) {
-      d = a.norm_table[xrow];
-    } else {
-      // consumer-only version of norm_block_sum (named barrier 1)
-      __shared__ float total_sq;
-      if (n.dt_sum != CB_F32) {
-        if (ctid == 0) {
-          float acc = round_to(__fmul_rn(xs[0], xs[0]), n.dt_sq);
-          for (long long i = 1; i < K; ++i)
-            acc = round_to(__fadd_rn(acc, round_to(__fmul_rn(xs[i], xs[i]), n.dt_sq)), n.dt_sum);
-          total_sq = acc;
-        }
-      } else {
-        float part = 0.0f;
-        for (long long i = ctid; i < K; i += kConsumers)
-          part = __fadd_rn(part, round_to(__fmul_rn(xs[i], xs[i]), n.dt_sq));
-        part = warp_sum(part);
-        if (lane == 0) norm_red[warp] = part;
-        asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-        if (ctid == 0) {
-          float acc = 0.0f;
-          for (int w = 0; w < kConsumerWarps; ++w) acc += norm_red[w];
-          total_sq = acc;
-        }
+  for (long long i = tid; i < K; i += ncons) xs[i] = load_as_f32(a.x, xrow * K + i, a.x_dtype);
+  consumers_sync(ncons);
+  float d = 0.0f;
+  NormSpec n{a.divisor, a.eps, a.dt_sq, a.dt_sum, a.dt_mean, a.dt_t, a.dt_d, a.dt_y};
+  if (a.norm == CB_NORM_RMS_TABLE) {
+    d = a.norm_table[xrow];
+  } else if (a.norm == CB_NORM_RMS) {
+    if (n.dt_sum != CB_F32) {  // NumPy's sequential 16-bit-float sum
+      if (tid == 0) {
+        float acc = round_to(__fmul_rn(xs[0], xs[0]), n.dt_sq);
+        for (long long i = 1; i < K; ++i)
+          acc = round_to(__fadd_rn(acc, round_to(__fmul_rn(xs[i], xs[i]), n.dt_sq)), n.dt_sum);
+        total_sq = acc;
       }
-      asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-      d = norm_finish_d(n, total_sq);
+    } else {
+      float part = 0.0f;
+      for (long long i = tid; i < K; i += ncons) part = __fadd_rn(part, round_to(__fmul_rn(xs[i], xs[i]), n.dt_sq));
+      part = warp_sum(part);
+      if (lane == 0) norm_red[warp] = part;
+      consumers_sync(ncons);
+      if (tid == 0) {
+        float acc = 0.0f;
+        for (int w = 0; w < L.consumers; ++w) acc += norm_red[w];
+        total_sq = acc;
+      }
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-    for (long long i = ctid; i < K; i += kConsumers)
-      xs[i] = norm_apply(n, xs[i], d, load_as_f32(a.norm_w, i, a.norm_w_dtype), a.dt_norm_out);
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
+    consumers_sync(ncons);
+    d = norm_finish_d(n, total_sq);
   }
+  // normalise and split into the two x planes
+  for (long long c = tid; c < chunks; c += ncons) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < VE; ++e) {
+      const long long i = c * VE + e;
+      v[e] = a.norm != CB_NORM_NONE
+                 ? norm_apply(n, xs[i], d, load_as_f32(a.norm_w, i, a.norm_w_dtype), a.dt_norm_out)
+                 : xs[i];
+    }
+    xa[c] = make_float4(v[0], v[1], v[2], v[3]);
+    if (VE == 8) xb[c] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  consumers_sync(ncons);
+
   long long rrow = 0;
   if (a.epilogue == CB_EPI_RESIDUAL && a.residual_index != nullptr) {
     rrow = load_index(a.residual_index, 0, a.residual_index_dtype);
     if (rrow < 0 || rrow >= a.index_rows) {
-      if (ctid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 1);
+      if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 1);
       rrow = 0;
     }
     rrow *= L.units;
   }
 
-  float best_v = 0.0f, gate = 0.0f;
+  // ---------------- consumers: this warp's stages ----------------
+  float best_v = 0.0f;
   long long best_i = -1;
-  for (long long s = warp; s < n_stages; s += kConsumerWarps) {
+  for (long long s = warp; s < n_stages; s += L.consumers) {
     const int slot = static_cast<int>(s % L.slots);
     if (!mbar_wait(full + slot, static_cast<uint32_t>((s / L.slots) & 1))) {
       if (lane == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 4);
       break;
     }
     const unsigned char* stage = ring + slot * L.stage_bytes;
-    const long long first = u0 + s * L.stage_units;
-    const long long last = first + L.stage_units < u1 ? first + L.stage_units : u1;
-    for (long long u = first; u < last; ++u) {
-      const uint4* row = reinterpret_cast<const uint4*>(stage + (u - first) * L.row_bytes);
-      float acc = 0.0f;
-      for (long long c = lane; c < chunks; c += 32) acc = Vec<WT>::dot(row[c], xs + c * VE, acc);
-      const float total = warp_sum(acc);
-      if (lane == 0) {
-        switch (a.epilogue) {
-          case CB_EPI_STORE: a.out[u] = total; break;
-          case CB_EPI_RESIDUAL:
-            a.out[u] = __fadd_rn(load_as_f32(a.residual, rrow + u, a.residual_dtype), total);
-            break;
-          case CB_EPI_SILU_MUL:
-            if ((u & 1) == 0) {
-              gate = total;
-            } else {
-              const float silu = __fdiv_rn(gate, __fadd_rn(expf(-gate), 1.0f));
-              a.out[u >> 1] = __fmul_rn(silu, total);
-            }
-            break;
-          default:  // CB_EPI_ARGMAX
-            a.out[u] = total;
-            if (best_i < 0 || argmax_better(total, u, best_v, best_i)) {
-              best_v = total;
-              best_i = u;
-            }
+    const long long first = u0 + s * L.rows;
+    const int in_stage = static_cast<int>(first + L.rows < u1 ? L.rows : u1 - first);
+    long long row_at[kMaxRows];
+    float totals[kMaxRows];
+#pragma unroll
+    for (int r = 0; r < kMaxRows; ++r) {
+      const int i = r < in_stage ? r : 0;  // pad with row 0 (result unused)
+      row_at[r] = pairs ? (i & 1) * (L.rows / 2) + (i >> 1) : i;
+    }
+    switch (L.rows) {
+      case 1: stage_dot<WT, 1>(stage, row_at, L.row_bytes, xa, xb, chunks, lane, totals); break;
+      case 2: stage_dot<WT, 2>(stage, row_at, L.row_bytes, xa, xb, chunks, lane, totals); break;
+      case 4: stage_dot<WT, 4>(stage, row_at, L.row_bytes, xa, xb, chunks, lane, totals); break;
+      default: stage_dot<WT, 8>(stage, row_at, L.row_bytes, xa, xb, chunks, lane, totals); break;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);  // slot free: reads are done
+    // epilogue: lane i finishes row i (every lane holds every total)
+    float mine = totals[0], next = 0.0f;
+#pragma unroll
+    for (int r = 1; r < kMaxRows; ++r) {
+      if (lane == r) mine = totals[r];
+      if (lane + 1 == r) next = totals[r];
+    }
+    if (lane < in_stage) {
+      const long long u = first + lane;
+      switch (a.epilogue) {
+        case CB_EPI_STORE: a.out[u] = mine; break;
+        case CB_EPI_RESIDUAL:
+          a.out[u] = __fadd_rn(load_as_f32(a.residual, rrow + u, a.residual_dtype), mine);
+          break;
+        case CB_EPI_SILU_MUL:
+          if ((lane & 1) == 0) {
+            const float silu = __fdiv_rn(mine, __fadd_rn(expf(-mine), 1.0f));
+            a.out[u >> 1] = __fmul_rn(silu, next);
+          }
+          break;
+        default:  // CB_EPI_ARGMAX
+          a.out[u] = mine;
+      }
+    }
+    if (a.epilogue == CB_EPI_ARGMAX && lane == 0) {
+      for (int i = 0; i < in_stage; ++i) {
+        const long long u = first + i;
+        if (best_i < 0 || argmax_better(totals[i], u, best_v, best_i)) {
+          best_v = totals[i];
+          best_i = u;
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty + slot);
   }
 
   if (a.epilogue != CB_EPI_ARGMAX) return;
@@ -243,11 +337,11 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const cb_gemv_args a, co
     warp_best_v[warp] = best_v;
     warp_best_i[warp] = best_i;
   }
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-  if (ctid == 0) {
+  consumers_sync(ncons);
+  if (tid == 0) {
     float bv = 0.0f;
     long long bi = -1;
-    for (int w = 0; w < kConsumerWarps; ++w) {
+    for (int w = 0; w < L.consumers; ++w) {
       if (warp_best_i[w] >= 0 && (bi < 0 || argmax_better(warp_best_v[w], warp_best_i[w], bv, bi))) {
         bv = warp_best_v[w];
         bi = warp_best_i[w];
@@ -259,8 +353,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const cb_gemv_args a, co
     const unsigned ticket = atomicAdd(a.counter, 1u);
     is_last = ticket == gridDim.x - 1;
   }
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-  if (!is_last || ctid != 0) return;
+  consumers_sync(ncons);
+  if (!is_last || tid != 0) return;
   __threadfence();
   float bv = 0.0f;
   long long bi = -1;
@@ -292,31 +386,55 @@ int plan_gemv(const cb_gemv_args& a, Layout* L) {
   }
   CB_REQUIRE(units > 0, "gemv: no rows");
   const long long row_bytes = a.k * (a.w_dtype == CB_BF16 ? 2 : 4);
-  CB_REQUIRE(row_bytes <= 64 * 1024, "gemv: rows longer than 64 KiB are not supported");
-  int stage_units = static_cast<int>(kStageTarget / row_bytes);
-  if (stage_units < 1) stage_units = 1;
-  if (a.epilogue == CB_EPI_SILU_MUL) stage_units = stage_units < 2 ? 2 : stage_units & ~1;
-  const long long stage_bytes = stage_units * row_bytes;
   const size_t x_bytes = (static_cast<size_t>(a.k) * 4 + 15) & ~size_t(15);
-  // two CTAs (this kernel + the next one, launched early) must fit an SM
-  long long ring = kRingTarget;
-  const long long budget = 110 * 1024 - static_cast<long long>(x_bytes);
-  if (ring > budget) ring = budget;
-  int slots = static_cast<int>(ring / stage_bytes);
-  if (slots < 2) slots = 2;
+  const bool pairs = a.epilogue == CB_EPI_SILU_MUL;
+  long long ring = kRingBudget;
+  if (ring + 2 * static_cast<long long>(x_bytes) + 1024 > kSmemBudget)
+    ring = kSmemBudget - 2 * static_cast<long long>(x_bytes) - 1024;
+  // Ring shape: C consumer warps, each owning m >= 2 slots (its next stage is
+  // in flight while it multiplies the current one), stages of `rows` rows
+  // (power of two <= 8, even for SwiGLU).  Pick the shape with the most bytes
+  // in flight, preferring more consumer warps, then stages of >= 8 KiB.
+  int rows = 0, consumers = 0, slots = 0;
+  long long best = -1;
+  for (int c = kMaxConsumerWarps; c >= 2; c /= 2) {
+    for (int r = pairs ? 2 : 1; r <= kMaxRows; r *= 2) {
+      const long long stage = r * row_bytes;
+      long long m = ring / (c * stage);
+      if (m > 4) m = 4;
+      if (m < 2) continue;
+      const long long score = c * m * stage * 4 + (stage >= 8 * 1024 ? 2 : 0) + (c >= 4 ? 1 : 0);
+      if (score > best) {
+        best = score;
+        rows = r;
+        consumers = c;
+        slots = static_cast<int>(c * m);
+      }
+    }
+  }
+  if (best < 0) {  // very long rows: single-buffered fallback
+    rows = pairs ? 2 : 1;
+    consumers = 2;
+    while (consumers > 1 && consumers * rows * row_bytes > ring) consumers /= 2;
+    slots = consumers;
+  }
+  CB_REQUIRE(slots * rows * row_bytes <= ring, "gemv: rows of %lld bytes do not fit the ring", row_bytes);
+  const long long stage_bytes = rows * row_bytes;
   int grid = a.grid > 0 ? a.grid : sm_count();
   long long per = (units + grid - 1) / grid;
-  if (a.epilogue == CB_EPI_SILU_MUL) per += per & 1;  // whole gate/up pairs per CTA
+  if (pairs) per += per & 1;  // whole gate/up pairs per CTA
   grid = static_cast<int>((units + per - 1) / per);
   L->units = units;
   L->per_cta = per;
   L->grid = grid;
-  L->stage_units = stage_units;
+  L->rows = rows;
   L->slots = slots;
+  L->consumers = consumers;
   L->row_bytes = row_bytes;
   L->stage_bytes = stage_bytes;
   L->ring_bytes = static_cast<size_t>(slots) * stage_bytes;
-  L->smem = L->ring_bytes + x_bytes + 2 * slots * sizeof(uint64_t);
+  L->x_bytes = x_bytes;
+  L->smem = L->ring_bytes + 2 * x_bytes + 32 + 2 * slots * sizeof(uint64_t);
   CB_REQUIRE(L->smem <= 220 * 1024, "gemv: k too large for shared memory");
   if (a.epilogue == CB_EPI_ARGMAX)
     CB_REQUIRE(a.scratch_val && a.scratch_idx && a.counter && a.argmax_out, "gemv: argmax needs scratch");

@@ -31,8 +31,12 @@ class CudaB200Compiler(Compiler):
 
     def __init__(self, device_index: Optional[int] = None, *, use_graphs: bool = True,
                  pdl: bool = True, fuse_decode: bool = True, alias_caches: bool = True,
-                 max_positions: int = 8192, gemv_grid: int = 0) -> None:
+                 max_positions: int = 8192, gemv_grid: Optional[int] = None) -> None:
+        import os
+
         self.device = CudaB200Device(device_index)
+        if gemv_grid is None:  # CTAs per decode GEMV (0 = one per SM)
+            gemv_grid = int(os.environ.get("CUDA_B200_GEMV_GRID", "0"))
         self.use_graphs = use_graphs
         self.pdl = pdl
         self.fuse_decode = fuse_decode

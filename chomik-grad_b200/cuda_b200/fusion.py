@@ -213,7 +213,7 @@ class DecodeFusion:
         if len(kn.shape) != 4:
             return None
         _, kvh, ctx, hd2 = kn.shape
-        if hd2 != hd or hd % 32 or hd > 256 or heads % kvh:
+        if hd2 != hd or hd not in (32, 64, 128, 256) or heads % kvh:
             return None
         if tuple(mask.shape) != (1, 1, 1, ctx) or p.rdt(mask).name not in ("float32", "bfloat16", "float16"):
             return None
