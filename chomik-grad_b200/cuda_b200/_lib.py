@@ -180,6 +180,7 @@ _SIGNATURES = {
     "cb_gemv_grid": ([POINTER(GemvArgs), POINTER(c_int)], c_int),
     "cb_decode_attention": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
     "cb_decode_attention_scratch": ([POINTER(DecodeAttentionArgs)], c_longlong),
+    "cb_decode_attention_noalloc": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
     "cb_argmax_rows": ([c_void_p, c_int, c_longlong, c_longlong, c_void_p, c_void_p], c_int),
     "cb_decode_advance": ([c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
                            c_int, c_longlong, c_void_p, c_longlong, c_void_p, c_void_p], c_int),

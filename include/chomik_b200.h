@@ -320,6 +320,19 @@ CB_API int cb_decode_attention(const cb_decode_attention_args* args, cb_stream_t
 /* Scratch floats cb_decode_attention needs for these args. */
 CB_API long long cb_decode_attention_scratch(const cb_decode_attention_args* args);
 
+/* cb_decode_attention for callers that cannot allocate device memory (an FFI
+ * binding that owns only the graph's bound arrays, a process whose arena
+ * already holds all of HBM, a decode loop that cannot afford the device
+ * synchronisation cudaFree brings).  This entry point has no counterpart in
+ * the reference.  `scratch` and `counters` in args are ignored: the library
+ * uses its own fixed device arrays (4 Mi floats of partials, 256 counters).
+ * The first call on a device, with that device current, sets them up (symbol
+ * lookup, counters cleared, device synchronised); make it before any stream
+ * capture.  Larger requests (splits * heads * (head_size + 2) > 4 Mi floats,
+ * kv_heads > 256) return CB_ERR_INVALID before any launch.  All calls on a
+ * device share the arrays: calls that overlap on the GPU race. */
+CB_API int cb_decode_attention_noalloc(const cb_decode_attention_args* args, cb_stream_t stream);
+
 /* On-device greedy step driver for back-to-back decode replays: from the
  * previous step's argmax it writes the next step's token id, position + 1,
  * attention mask row (position+1 -> 0) and write mask (one-hot at the new
