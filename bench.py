@@ -45,6 +45,8 @@ for _p in (ROOT / "chomik-grad_b200", ROOT):
 import numpy as np  # noqa: E402
 
 METRIC = "decode tokens/sec (bs=1) and % of HBM roofline"
+# DRAM bytes of one gate/up GEMV launch from an ncu capture, per workload
+GATEUP_TRAFFIC = {"tinyllama-bf16-bs1": 56_449_792 + 45_312}
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
@@ -337,7 +339,11 @@ def main() -> None:
                    "parallelism": f"replicas x{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (2.07 GB weights per step)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak,
+                     "traffic": GATEUP_TRAFFIC.get(wl.name),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate/up "
+                                       "launch (profiles/gemv_tinyllama_bf16_bs1.txt; cold cache, "
+                                       "includes its L2 prefetch of the next launch's weights)",
                      "kernel": f"cb_gemv silu_mul (gate/up {gemv_bytes / 1e6:.1f} MB per launch, "
                                f"{gemv_layers} layers cycled)", "peak_source": peak_kind},
         "step_roofline": {"bytes_per_token": step_bytes, "achieved": step_gbs, "peak": peak,

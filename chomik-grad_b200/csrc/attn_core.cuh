@@ -46,7 +46,7 @@ __device__ void attention_item(const cb_decode_attention_args& a, int g, int spl
 
   long long pos = load_index(a.position, 0, a.position_dtype);
   if (pos < 0 || pos >= a.n_positions) {
-    if (tid == 0 && split == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 2);
+    if (tid == 0 && split == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_POSITION);
     pos = pos < 0 ? 0 : a.n_positions - 1;
   }
   const float* cs = a.cos_table + pos * half;

@@ -77,13 +77,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const cb_gemv_args a,
     // Producer lane j feeds consumer warp j: it issues stages j, j + C, ...
     // into the slots that warp owns, so C lanes issue copies in parallel.
     if (lane < L.consumers) {
-      for (long long s = lane; s < n_stages; s += L.consumers) {
+      long long s = lane;
+      for (; s < n_stages; s += L.consumers) {
         const int slot = static_cast<int>(s % L.slots);
         const long long round = s / L.slots;
         if (lane == 0 && s == L.slots)  // ring primed: ask L2 for the next kernel's weights
           prefetch_share(a.prefetch_ptr, a.prefetch_bytes, blockIdx.x, gridDim.x, 0, 1);
         if (round > 0 && !mbar_wait(empty + slot, static_cast<uint32_t>((round - 1) & 1))) {
-          if (a.error_flag != nullptr) atomicExch(a.error_flag, 4);
+          if (a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_WAIT_SLOT);
           break;
         }
         const long long first = u0 + s * L.rows;
@@ -111,6 +112,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const cb_gemv_args a,
       }
       if (lane == 0 && n_stages <= L.slots)
         prefetch_share(a.prefetch_ptr, a.prefetch_bytes, blockIdx.x, gridDim.x, 0, 1);
+      // Drain: this lane issued stages lane, lane + C, ..., s - C.  The last
+      // one in each of its slots must have landed before the lane exits, so
+      // no copy still writes this block's shared memory when it retires --
+      // also after a consumer or producer wait gave up.  No later stage uses
+      // these slots, so each wait is for exactly that copy's phase.
+      const int per_lane = L.slots / L.consumers;
+      for (int i = 1; i <= per_lane; ++i) {
+        const long long t = s - static_cast<long long>(i) * L.consumers;
+        if (t < lane) break;
+        if (!mbar_wait(full + t % L.slots, static_cast<uint32_t>((t / L.slots) & 1))) {
+          if (a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_WAIT_DRAIN);
+          break;
+        }
+      }
     }
     return;
   }
@@ -121,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const cb_gemv_args a,
   pdl_launch_dependents();
   long long xrow = a.x_index != nullptr ? load_index(a.x_index, 0, a.x_index_dtype) : 0;
   if (a.x_index != nullptr && (xrow < 0 || xrow >= a.index_rows)) {
-    if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 1);
+    if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_INDEX);
     xrow = 0;
   }
   for (long long i = tid; i < K; i += ncons) xs[i] = load_as_f32(a.x, xrow * K + i, a.x_dtype);
@@ -172,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const cb_gemv_args a,
   if (a.epilogue == CB_EPI_RESIDUAL && a.residual_index != nullptr) {
     rrow = load_index(a.residual_index, 0, a.residual_index_dtype);
     if (rrow < 0 || rrow >= a.index_rows) {
-      if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 1);
+      if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_INDEX);
       rrow = 0;
     }
     rrow *= L.units;
@@ -184,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const cb_gemv_args a,
   for (long long s = warp; s < n_stages; s += L.consumers) {
     const int slot = static_cast<int>(s % L.slots);
     if (!mbar_wait(full + slot, static_cast<uint32_t>((s / L.slots) & 1))) {
-      if (lane == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 4);
+      if (lane == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_WAIT_DATA);
       break;
     }
     const unsigned char* stage = ring + slot * L.stage_bytes;

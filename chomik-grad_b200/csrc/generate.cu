@@ -18,7 +18,7 @@ __global__ void decode_advance_kernel(const long long* argmax, void* ids, int id
   const long long next = pos + 1;
   if (token_log != nullptr) token_log[step] = token;
   if (next >= context || pos < 0) {
-    if (error_flag != nullptr) atomicExch(error_flag, 3);
+    if (error_flag != nullptr) atomicExch(error_flag, CB_FLAG_CONTEXT);
     return;
   }
   if (ids_dtype == CB_I64) static_cast<long long*>(ids)[0] = token;

@@ -147,7 +147,7 @@ __global__ void gather_kernel(const T* table, long long rows, long long row_unit
     long long row = load_index(idx, which, idx_dtype);
     if (row < 0) row += rows;
     if (row < 0 || row >= rows) {
-      if (error_flag != nullptr) atomicExch(error_flag, 1);
+      if (error_flag != nullptr) atomicExch(error_flag, CB_FLAG_INDEX);
       out[i] = T{};
       continue;
     }

@@ -68,7 +68,7 @@ __global__ void rope_kernel(const cb_rope_args a) {
   long long offset = 0;
   if (a.offset != nullptr) offset = load_index(a.offset, 0, a.offset_dtype);
   if (offset < 0 || offset >= a.n_offsets) {
-    if (blockIdx.x == 0 && threadIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, 2);
+    if (blockIdx.x == 0 && threadIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_POSITION);
     offset = offset < 0 ? 0 : a.n_offsets - 1;
   }
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;

@@ -1,14 +1,24 @@
 // mbarrier + bulk-copy (TMA engine) helpers for sm_100a kernels.
 //
-// Every wait is bounded: after `limit` unsuccessful polls it returns false so
-// the caller can record an error and leave instead of spinning forever.
+// Every wait is bounded: after kWaitNs of wall time (read from %globaltimer),
+// or kWaitPolls polls if the timer does not advance, it returns false so the
+// caller can record an error, drain its copies in flight and leave instead of
+// spinning forever.  A kernel whose bulk copies have been issued must not
+// exit before they land: see gemv.cu's producer drain.
 #pragma once
 
 #include <stdint.h>
 
 namespace cb {
 
-constexpr uint32_t kWaitLimit = 1u << 24;
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
+constexpr uint32_t kWaitPolls = 1u << 28;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -45,9 +55,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = kWaitLimit) {
-  for (uint32_t i = 0; i < limit; ++i)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitNs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  for (uint32_t i = 1; i < kWaitPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && global_ns() - start > limit_ns) return false;
+  }
   return false;
 }
 

@@ -207,6 +207,26 @@ def load() -> ctypes.CDLL:
     return lib
 
 
+FLAG_INDEX, FLAG_POSITION, FLAG_CONTEXT = 1, 2, 3
+FLAG_WAIT_DATA, FLAG_WAIT_SLOT, FLAG_WAIT_DRAIN = 4, 5, 6
+
+
+def flag_error(value: int) -> Exception:
+    """The exception for a kernel error-flag value (CB_FLAG_* in the header)."""
+    if value == FLAG_INDEX:
+        return IndexError("gather index is outside the first dimension")
+    if value == FLAG_POSITION:
+        return IndexError("RoPE position is outside the precomputed table")
+    if value == FLAG_CONTEXT:
+        return IndexError("decode step would write past the KV-cache context")
+    waits = {FLAG_WAIT_DATA: "a consumer waiting for weight data",
+             FLAG_WAIT_SLOT: "a producer waiting for a free ring slot",
+             FLAG_WAIT_DRAIN: "the end-of-kernel drain of bulk copies"}
+    if value in waits:
+        return KernelError(f"kernel timed out in {waits[value]} (results are invalid)")
+    return KernelError(f"kernel error flag {value}")
+
+
 def check(status: int, what: str = "") -> None:
     if status != 0:
         message = load().cb_last_error().decode(errors="replace")

@@ -29,7 +29,7 @@ class CudaB200Compiler(Compiler):
 
     name = "cuda-b200"
 
-    def __init__(self, device_index: Optional[int] = None, *, use_graphs: bool = True,
+    def __init__(self, device_index: Optional[int] = None, *, use_graphs: Optional[bool] = None,
                  pdl: bool = True, fuse_decode: bool = True, alias_caches: bool = True,
                  max_positions: int = 8192, gemv_grid: Optional[int] = None) -> None:
         import os
@@ -37,6 +37,8 @@ class CudaB200Compiler(Compiler):
         self.device = CudaB200Device(device_index)
         if gemv_grid is None:  # CTAs per decode GEMV (0 = one per SM)
             gemv_grid = int(os.environ.get("CUDA_B200_GEMV_GRID", "0"))
+        if use_graphs is None:  # CUDA graphs for repeated runs (CUDA_B200_GRAPHS=0: launch one by one)
+            use_graphs = os.environ.get("CUDA_B200_GRAPHS", "1") != "0"
         self.use_graphs = use_graphs
         self.pdl = pdl
         self.fuse_decode = fuse_decode

@@ -171,9 +171,8 @@ class CudaB200Device(DeviceAdapter):
         array = self.array(value)
         if array.argmax_value is not None:
             index, status = array.argmax_value.tolist()
-            if status:
-                raise IndexError("a kernel of the program that produced these logits flagged an "
-                                 f"out-of-range index (code {status})")
+            if status:  # the producing program's error flag, read with the index
+                raise _lib.flag_error(int(status))
             return int(index)
         if array.size == 0:
             raise ValueError("attempt to get argmax of an empty sequence")

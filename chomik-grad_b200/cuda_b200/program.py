@@ -194,10 +194,14 @@ class CudaB200Program(CompiledProgram):
         No inputs are bound and no outputs are copied out: device-side drivers
         (cb_decode_advance) update the slots between replays.
         """
+        stream = self.device.stream() if stream is None else stream
+        if not self.use_graphs:  # graphs switched off: launch the same kernels one by one
+            self._launch_all(stream)
+            return
         exec_ = self._graphs.get(getattr(self, "_last_key", None))
         if exec_ is None:
             raise RuntimeError("replay() needs a captured graph: run() the program twice first")
-        _lib.call("cb_graph_launch", exec_, self.device.stream() if stream is None else stream)
+        _lib.call("cb_graph_launch", exec_, stream)
 
     def _capture(self) -> int:
         if self._capture_stream is None:
@@ -259,16 +263,14 @@ class CudaB200Program(CompiledProgram):
         return DeviceArray(out, tuple(shape), view.dtype)
 
     def check_errors(self) -> None:
-        """Raise if a kernel flagged an out-of-range index (gather, position)."""
+        """Raise if a kernel set the program's error flag (cb_gemv_args.error_flag)."""
         if self.plan.error_flag is None:
             return
         flag = self._tensors[self.plan.error_flag]
         value = int(flag[0].item())
         if value:
             flag.zero_()
-            if value == 1:
-                raise IndexError("gather index is outside the first dimension")
-            raise IndexError("RoPE position is outside the precomputed table")
+            raise _lib.flag_error(value)
 
     # ------------------------------------------------------------ launches
     def ptr(self, view: View) -> int:

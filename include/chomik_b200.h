@@ -28,6 +28,19 @@ enum { CB_F32 = 0, CB_BF16 = 1, CB_F16 = 2, CB_I32 = 3, CB_I64 = 4 };
 /* status codes */
 enum { CB_OK = 0, CB_ERR_INVALID = 1, CB_ERR_CUDA = 2 };
 
+/* values kernels store in an `error_flag` (0 = no error): an index outside
+ * its table, a RoPE position outside the table, a decode step past the
+ * context, and bounded waits that gave up (a consumer waiting for data, a
+ * producer waiting for a free slot, the end-of-kernel drain of copies) */
+enum {
+  CB_FLAG_INDEX = 1,
+  CB_FLAG_POSITION = 2,
+  CB_FLAG_CONTEXT = 3,
+  CB_FLAG_WAIT_DATA = 4,
+  CB_FLAG_WAIT_SLOT = 5,
+  CB_FLAG_WAIT_DRAIN = 6
+};
+
 #define CB_MAX_DIMS 8
 #define CB_EW_MAX_INPUTS 8
 #define CB_EW_MAX_INSTR 40
