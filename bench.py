@@ -47,6 +47,8 @@ import numpy as np  # noqa: E402
 METRIC = "decode tokens/sec (bs=1) and % of HBM roofline"
 # DRAM bytes of one gate/up GEMV launch from an ncu capture, per workload
 GATEUP_TRAFFIC = {"tinyllama-bf16-bs1": 56_449_792 + 45_312}
+# DRAM bytes of one cb_decode_step launch from an ncu capture, per workload
+STEP_TRAFFIC: dict = {}
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
@@ -276,8 +278,11 @@ def main() -> None:
     program, nodes = rt.decode_program(context, caches, first, start_pos)
 
     # ---- value: device-resident decode (graph replays, device-side inputs) ----
-    def device_pass(n_steps: int):
-        return rt.decode_on_device(first, start_pos, context, caches, n_steps + 1, timed=True)
+    replay_ms = []  # device time of each replayed step (CUDA events on the launching stream)
+
+    def device_pass(n_steps: int, times=None):
+        return rt.decode_on_device(first, start_pos, context, caches, n_steps + 1, timed=True,
+                                   replay_times=times)
 
     device_pass(min(args.warmup, per_chunk))
     barrier(world)
@@ -285,7 +290,7 @@ def main() -> None:
     with ClockSampler(local) as clocks:
         while done < args.steps:
             n = min(per_chunk, args.steps - done)
-            _, ms = device_pass(n)
+            _, ms = device_pass(n, replay_ms)
             elapsed_ms += ms
             done += n
     barrier(world)
@@ -319,16 +324,35 @@ def main() -> None:
     d2h = 16
 
     # ---- roofline of the dominant kernel and of the whole step ----
-    gemv_bytes, gemv_ms, gemv_layers = gemv_roofline(program)
     peak, peak_kind = measured_peaks()
-    achieved = gemv_bytes / (gemv_ms / 1000.0) / 1e9
     itemsize = wl.np_dtype.itemsize
     avg_ctx = start_pos + min(args.steps, per_chunk) / 2
     kv_bytes = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * 4 * context
     step_bytes = weight_bytes(cfg, itemsize) + cfg.hidden_size * itemsize + kv_bytes
     step_gbs = step_bytes * (value / world) / 1e9
+    if program.step_mode:
+        # the whole step is one cb_decode_step launch: its bytes over its own time
+        kernel_ms = statistics.fmean(replay_ms)
+        achieved = step_bytes / (kernel_ms / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": STEP_TRAFFIC.get(wl.name),
+                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                      "decode-step launch (profiles/decode_step_tinyllama_bf16_bs1.txt)",
+                    "kernel": f"cb_decode_step (whole decode step, {step_bytes / 1e9:.3f} GB per launch: "
+                              f"weights + K/V over the {context}-row cache + embedding row)",
+                    "kernel_ms": kernel_ms, "peak_source": peak_kind}
+    else:
+        gemv_bytes, gemv_ms, gemv_layers = gemv_roofline(program)
+        achieved = gemv_bytes / (gemv_ms / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": GATEUP_TRAFFIC.get(wl.name),
+                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate/up "
+                                      "launch (profiles/gemv_tinyllama_bf16_bs1.txt; cold cache, "
+                                      "includes its L2 prefetch of the next launch's weights)",
+                    "kernel": f"cb_gemv silu_mul (gate/up {gemv_bytes / 1e6:.1f} MB per launch, "
+                              f"{gemv_layers} layers cycled)", "peak_source": peak_kind}
 
-    launches_per_step = len(program.plan.steps) + 1  # + cb_decode_advance
+    launches_per_step = program.launches + 1  # + cb_decode_advance
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": slowest / args.steps,
@@ -338,14 +362,7 @@ def main() -> None:
                    "seq_len": context, "prompt_tokens": wl.prompt_tokens, "kv_cache": "float32",
                    "parallelism": f"replicas x{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (2.07 GB weights per step)"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak,
-                     "traffic": GATEUP_TRAFFIC.get(wl.name),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate/up "
-                                       "launch (profiles/gemv_tinyllama_bf16_bs1.txt; cold cache, "
-                                       "includes its L2 prefetch of the next launch's weights)",
-                     "kernel": f"cb_gemv silu_mul (gate/up {gemv_bytes / 1e6:.1f} MB per launch, "
-                               f"{gemv_layers} layers cycled)", "peak_source": peak_kind},
+        "roofline": roofline,
         "step_roofline": {"bytes_per_token": step_bytes, "achieved": step_gbs, "peak": peak,
                           "unit": "GB/s", "frac": step_gbs / peak, "avg_context": avg_ctx},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,

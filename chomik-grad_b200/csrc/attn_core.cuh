@@ -1,15 +1,19 @@
 // Single-token decode attention for one (context split, KV head) work item,
 // shared by the standalone cb_decode_attention kernel and the decode-step
-// megakernel.  256 threads (8 warps) execute it; `bar` synchronises them
-// (named barrier 1) so it also runs inside a block that has extra warps.
+// megakernel.  256 threads (8 warps) execute it; `attn_sync` synchronises
+// them (named barrier 1) so it also runs inside a block that has extra warps.
 //
-// The item ropes the new q/k rows, stages its split's K/V rows in shared
-// memory -- applying the write-mask blend cache*(1-wm) + new*wm (float32, as
-// llama.py:511-512 computes it) to the rows it owns and writing them back --
-// computes every (query head, position) score in one pass
-// (x = q.k / divisor + mask), and writes its partial softmax state.  The last
-// item of each KV group merges the splits in split order (deterministic) and
-// resets the group counter.
+// The item has two halves:
+//  * attention_stage_cache: the split's K/V cache rows, write-mask and mask
+//    values into shared memory.  Nothing here depends on this step's q/k/v,
+//    so the megakernel runs it before waiting for the QKV phase;
+//  * attention_finish: rope the new q/k rows, apply the write-mask blend
+//    cache*(1-wm) + new*wm (float32, as llama.py:511-512 computes it) to the
+//    rows with wm != 0 and write them back, compute every (query head,
+//    position) score in one pass (x = q.k / divisor + mask), and write the
+//    split's partial softmax state.  With `merge`, the last item of each KV
+//    group then merges the splits in split order (deterministic) and resets
+//    the group counter; without it the caller merges (attention_merge_chunk).
 #pragma once
 
 #include "common.cuh"
@@ -23,24 +27,67 @@ __device__ __forceinline__ void attn_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kAttnThreads) : "memory");
 }
 
-// Shared floats the item needs.
+// Shared floats an item needs.
 __host__ __device__ inline long long attn_smem_floats(long long group, long long hd) {
-  return (group + 2) * hd + kAttnSplit * (hd + 1) + kAttnSplit * hd + group * kAttnSplit + 2 * group;
+  return (group + 2) * hd + kAttnSplit * (hd + 1) + kAttnSplit * hd + group * kAttnSplit + 2 * group +
+         2 * kAttnSplit;
 }
 
 template <int HD>
-__device__ void attention_item(const cb_decode_attention_args& a, int g, int split, int splits, float* smem,
-                               int* s_last, int tid) {
+struct AttnSmem {
+  float *q_rot, *k_new, *v_new, *ks, *vs, *probs, *stats, *wm, *maskv;
+  __device__ AttnSmem(float* smem, int group) {
+    q_rot = smem;
+    k_new = q_rot + group * HD;
+    v_new = k_new + HD;
+    ks = v_new + HD;                   // [kAttnSplit][HD + 1] (padded: conflict-free scores)
+    vs = ks + kAttnSplit * (HD + 1);   // [kAttnSplit][HD]
+    probs = vs + kAttnSplit * HD;      // [group][kAttnSplit]
+    stats = probs + group * kAttnSplit;  // [group][2]: max, sum
+    wm = stats + 2 * group;            // [kAttnSplit]
+    maskv = wm + kAttnSplit;           // [kAttnSplit]
+  }
+};
+
+__device__ __forceinline__ int attn_rows(const cb_decode_attention_args& a, int split) {
+  const long long lo = static_cast<long long>(split) * kAttnSplit;
+  return static_cast<int>(a.context - lo < kAttnSplit ? a.context - lo : kAttnSplit);
+}
+
+template <int HD>
+__device__ void attention_stage_cache(const cb_decode_attention_args& a, int g, int split, float* smem,
+                                      int tid) {
+  const int group = static_cast<int>(a.heads / a.kv_heads);
+  AttnSmem<HD> s(smem, group);
+  const long long lo_pos = static_cast<long long>(split) * kAttnSplit;
+  const int n = attn_rows(a, split);
+  const float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
+  const float* vc = a.v_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
+  for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
+    const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
+    const float4 kv = __ldcg(reinterpret_cast<const float4*>(kc) + e);
+    const float4 vv = __ldcg(reinterpret_cast<const float4*>(vc) + e);
+    float* kd = s.ks + r * (HD + 1) + d4;
+    kd[0] = kv.x;
+    kd[1] = kv.y;
+    kd[2] = kv.z;
+    kd[3] = kv.w;
+    *reinterpret_cast<float4*>(s.vs + r * HD + d4) = vv;
+  }
+  for (int r = tid; r < n; r += kAttnThreads) {
+    s.wm[r] = load_as_f32(a.write_mask, lo_pos + r, a.write_mask_dtype);
+    s.maskv[r] = load_as_f32(a.mask, lo_pos + r, a.mask_dtype);
+  }
+}
+
+// Needs attention_stage_cache's shared memory (and an attn_sync after it).
+template <int HD>
+__device__ void attention_finish(const cb_decode_attention_args& a, int g, int split, int splits, float* smem,
+                                 int* s_last, int tid, bool merge) {
   const int group = static_cast<int>(a.heads / a.kv_heads);
   constexpr int half = HD / 2;
   constexpr int KS = HD + 1;
-  float* q_rot = smem;
-  float* k_new = q_rot + group * HD;
-  float* v_new = k_new + HD;
-  float* ks = v_new + HD;
-  float* vs = ks + kAttnSplit * KS;
-  float* probs = vs + kAttnSplit * HD;
-  float* stats = probs + group * kAttnSplit;
+  AttnSmem<HD> s(smem, group);
   const int warp = tid >> 5, lane = tid & 31;
   constexpr int warps = kAttnThreads / 32;
 
@@ -54,48 +101,47 @@ __device__ void attention_item(const cb_decode_attention_args& a, int g, int spl
   for (int i = tid; i < group * half; i += kAttnThreads) {
     const int h = i / half, j = i % half;
     const float* src = a.qkv + a.q_off + (static_cast<long long>(g) * group + h) * HD;
-    const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = cs[j], s = sn[j];
-    q_rot[h * HD + j] = fmaf(-hi, s, __fmul_rn(lo, c));
-    q_rot[h * HD + j + half] = fmaf(hi, c, __fmul_rn(lo, s));
+    const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = cs[j], sv = sn[j];
+    s.q_rot[h * HD + j] = fmaf(-hi, sv, __fmul_rn(lo, c));
+    s.q_rot[h * HD + j + half] = fmaf(hi, c, __fmul_rn(lo, sv));
   }
   for (int j = tid; j < half; j += kAttnThreads) {
     const float* src = a.qkv + a.k_off + static_cast<long long>(g) * HD;
-    const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = cs[j], s = sn[j];
-    k_new[j] = fmaf(-hi, s, __fmul_rn(lo, c));
-    k_new[j + half] = fmaf(hi, c, __fmul_rn(lo, s));
+    const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = cs[j], sv = sn[j];
+    s.k_new[j] = fmaf(-hi, sv, __fmul_rn(lo, c));
+    s.k_new[j + half] = fmaf(hi, c, __fmul_rn(lo, sv));
   }
   for (int d = tid; d < HD; d += kAttnThreads)
-    v_new[d] = __ldcg(a.qkv + a.v_off + static_cast<long long>(g) * HD + d);
+    s.v_new[d] = __ldcg(a.qkv + a.v_off + static_cast<long long>(g) * HD + d);
   attn_sync();
 
-  // stage this split's K/V rows; rows with wm != 0 get the blend
+  // rows with wm != 0 get the blend, in shared memory and in the cache
   const long long lo_pos = static_cast<long long>(split) * kAttnSplit;
-  const int n = static_cast<int>(a.context - lo_pos < kAttnSplit ? a.context - lo_pos : kAttnSplit);
+  const int n = attn_rows(a, split);
   float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
   float* vc = a.v_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
   for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
     const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
-    float4 kv = __ldcg(reinterpret_cast<const float4*>(kc) + e);
-    float4 vv = __ldcg(reinterpret_cast<const float4*>(vc) + e);
-    const float wm = load_as_f32(a.write_mask, lo_pos + r, a.write_mask_dtype);
-    if (wm != 0.0f) {
-      const float keep = round_to(__fsub_rn(1.0f, wm), a.one_minus_dtype);
-      float* kf = &kv.x;
-      float* vf = &vv.x;
+    const float wm = s.wm[r];
+    if (wm == 0.0f) continue;
+    const float keep = round_to(__fsub_rn(1.0f, wm), a.one_minus_dtype);
+    float* kd = s.ks + r * KS + d4;
+    float4 vv = *reinterpret_cast<float4*>(s.vs + r * HD + d4);
+    float4 kv = make_float4(kd[0], kd[1], kd[2], kd[3]);
+    float* kf = &kv.x;
+    float* vf = &vv.x;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        kf[i] = __fadd_rn(__fmul_rn(kf[i], keep), __fmul_rn(k_new[d4 + i], wm));
-        vf[i] = __fadd_rn(__fmul_rn(vf[i], keep), __fmul_rn(v_new[d4 + i], wm));
-      }
-      reinterpret_cast<float4*>(kc)[e] = kv;
-      reinterpret_cast<float4*>(vc)[e] = vv;
+    for (int i = 0; i < 4; ++i) {
+      kf[i] = __fadd_rn(__fmul_rn(kf[i], keep), __fmul_rn(s.k_new[d4 + i], wm));
+      vf[i] = __fadd_rn(__fmul_rn(vf[i], keep), __fmul_rn(s.v_new[d4 + i], wm));
     }
-    float* kd = ks + r * KS + d4;
+    reinterpret_cast<float4*>(kc)[e] = kv;
+    reinterpret_cast<float4*>(vc)[e] = vv;
     kd[0] = kv.x;
     kd[1] = kv.y;
     kd[2] = kv.z;
     kd[3] = kv.w;
-    *reinterpret_cast<float4*>(vs + r * HD + d4) = vv;
+    *reinterpret_cast<float4*>(s.vs + r * HD + d4) = vv;
   }
   attn_sync();
 
@@ -103,23 +149,23 @@ __device__ void attention_item(const cb_decode_attention_args& a, int g, int spl
   for (int h = warp; h < group; h += warps) {
     float x = -INFINITY;
     if (lane < n) {
-      const float* q = q_rot + h * HD;
-      const float* k = ks + lane * KS;
+      const float* q = s.q_rot + h * HD;
+      const float* k = s.ks + lane * KS;
       float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
       for (int d = 0; d < HD; d += 2) {
         s0 = fmaf(q[d], k[d], s0);
         s1 = fmaf(q[d + 1], k[d + 1], s1);
       }
-      x = __fadd_rn(__fdiv_rn(s0 + s1, a.divisor), load_as_f32(a.mask, lo_pos + lane, a.mask_dtype));
+      x = __fadd_rn(__fdiv_rn(s0 + s1, a.divisor), s.maskv[lane]);
     }
     const float m = warp_max(x);
     const float p = lane < n ? expf(x - m) : 0.0f;
     const float l = warp_sum(p);
-    probs[h * kAttnSplit + lane] = p;
+    s.probs[h * kAttnSplit + lane] = p;
     if (lane == 0) {
-      stats[2 * h] = m;
-      stats[2 * h + 1] = l;
+      s.stats[2 * h] = m;
+      s.stats[2 * h + 1] = l;
     }
   }
   attn_sync();
@@ -127,21 +173,22 @@ __device__ void attention_item(const cb_decode_attention_args& a, int g, int spl
   // p @ v for every (head, dim) of the group; partials to scratch
   for (int i = tid; i < group * HD; i += kAttnThreads) {
     const int h = i / HD, d = i % HD;
-    const float* p = probs + h * kAttnSplit;
+    const float* p = s.probs + h * kAttnSplit;
     float acc0 = 0.0f, acc1 = 0.0f;
     int j = 0;
     for (; j + 1 < n; j += 2) {
-      acc0 = fmaf(p[j], vs[j * HD + d], acc0);
-      acc1 = fmaf(p[j + 1], vs[(j + 1) * HD + d], acc1);
+      acc0 = fmaf(p[j], s.vs[j * HD + d], acc0);
+      acc1 = fmaf(p[j + 1], s.vs[(j + 1) * HD + d], acc1);
     }
-    if (j < n) acc0 = fmaf(p[j], vs[j * HD + d], acc0);
+    if (j < n) acc0 = fmaf(p[j], s.vs[j * HD + d], acc0);
     float* part = a.scratch + (static_cast<long long>(split) * a.heads + g * group + h) * (HD + 2);
     part[2 + d] = acc0 + acc1;
     if (d == 0) {
-      part[0] = stats[2 * h];
-      part[1] = stats[2 * h + 1];
+      part[0] = s.stats[2 * h];
+      part[1] = s.stats[2 * h + 1];
     }
   }
+  if (!merge) return;
 
   // merge the splits of this KV group in split order
   __threadfence();
@@ -170,6 +217,53 @@ __device__ void attention_item(const cb_decode_attention_args& a, int g, int spl
     a.out[head * HD + d] = __fdiv_rn(acc, lsum);
   }
   if (tid == 0) a.counters[g] = 0u;
+}
+
+// The whole item: stage, then finish with the in-kernel merge.
+template <int HD>
+__device__ void attention_item(const cb_decode_attention_args& a, int g, int split, int splits, float* smem,
+                               int* s_last, int tid) {
+  attention_stage_cache<HD>(a, g, split, smem, tid);
+  attn_sync();
+  attention_finish<HD>(a, g, split, splits, smem, s_last, tid, true);
+}
+
+// Merged attention output for elements [e0, e0 + n) of one head (n <= 8,
+// inside one head) from the split partials (scratch layout above).  Online
+// over splits: the same value as the in-kernel merge up to the last bits.
+// Loads go through L1 (the partials are written once per launch, before the
+// caller's phase): a lane's eight values share sectors the L1 fetches once.
+__device__ __forceinline__ void attention_merge_chunk(const float* parts, long long heads, int hd, int splits,
+                                                      long long e0, int n, float* out) {
+  const long long head = e0 / hd;
+  const int d0 = static_cast<int>(e0 % hd);
+  const long long stride = heads * (hd + 2);
+  const float* base = parts + head * (hd + 2);
+  float m = -INFINITY, lsum = 0.0f, acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll 4
+  for (int sp = 0; sp < splits; ++sp) {
+    const float* part = base + sp * stride;
+    const float ms = __ldca(part), ls = __ldca(part + 1);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = i < n ? __ldca(part + 2 + d0 + i) : 0.0f;
+    if (ms > m) {
+      const float rescale = expf(m - ms);  // 0 on the first split (m = -inf)
+      lsum *= rescale;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] *= rescale;
+      m = ms;
+    }
+    const float scale = expf(ms - m);
+    lsum = fmaf(ls, scale, lsum);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = fmaf(v[i], scale, acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < n) out[i] = __fdiv_rn(acc[i], lsum);
 }
 
 }  // namespace cb

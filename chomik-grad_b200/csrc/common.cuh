@@ -50,6 +50,19 @@ __device__ __forceinline__ float load_as_f32(const void* base, long long i, int 
   }
 }
 
+// load_as_f32 through L2 only (ld.global.cg): for values other blocks of the
+// same launch wrote, which this SM's L1 may hold stale copies of.
+__device__ __forceinline__ float load_cg_f32(const void* base, long long i, int dtype) {
+  switch (dtype) {
+    case CB_F32: return __ldcg(static_cast<const float*>(base) + i);
+    case CB_BF16: return bf16_bits_to_f32(__ldcg(static_cast<const unsigned short*>(base) + i));
+    case CB_F16: return __half2float(__ushort_as_half(__ldcg(static_cast<const unsigned short*>(base) + i)));
+    case CB_I32: return static_cast<float>(__ldcg(static_cast<const int*>(base) + i));
+    case CB_I64: return static_cast<float>(__ldcg(static_cast<const long long*>(base) + i));
+    default: return 0.0f;
+  }
+}
+
 __device__ __forceinline__ void store_from_f32(void* base, long long i, int dtype, float v) {
   switch (dtype) {
     case CB_F32: static_cast<float*>(base)[i] = v; break;

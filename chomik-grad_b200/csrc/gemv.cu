@@ -198,7 +198,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const cb_gemv_args a,
   long long best_i = -1;
   for (long long s = warp; s < n_stages; s += L.consumers) {
     const int slot = static_cast<int>(s % L.slots);
-    if (!mbar_wait(full + slot, static_cast<uint32_t>((s / L.slots) & 1))) {
+    const bool ok = mbar_wait(full + slot, static_cast<uint32_t>((s / L.slots) & 1));
+    if (!__all_sync(0xffffffffu, ok)) {  // the warp leaves together (shuffles follow)
       if (lane == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_WAIT_DATA);
       break;
     }

@@ -27,6 +27,8 @@ BINARY = {"add", "sub", "mul", "div", "equal"}
 REDUCE_SUM, REDUCE_MAX = 0, 1
 NORM_NONE, NORM_RMS, NORM_RMS_TABLE = 0, 1, 2
 EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
+PHASE_GEMV, PHASE_ATTENTION = 0, 1
+X_PLAIN, X_SILU_MUL = 0, 1
 
 LL8 = c_longlong * MAX_DIMS
 
@@ -149,6 +151,17 @@ class DecodeAttentionArgs(ctypes.Structure):
     ]
 
 
+class StepPhase(ctypes.Structure):
+    _fields_ = [("kind", c_int), ("x_mode", c_int), ("gemv", GemvArgs), ("attention", DecodeAttentionArgs)]
+
+
+class DecodeStepConfig(ctypes.Structure):
+    _fields_ = [("grid", c_int), ("n_phases", c_int), ("w_dtype", c_int), ("head_size", c_int),
+                ("slot_bytes", c_longlong), ("x_bytes", c_longlong), ("norm_bytes", c_longlong),
+                ("smem", c_longlong),
+                ("prefetch_bytes", c_longlong), ("lane_inflight", c_int), ("timeline", c_void_p)]
+
+
 class KernelError(RuntimeError):
     """A libchomik_b200 entry point returned a non-zero status."""
 
@@ -181,6 +194,10 @@ _SIGNATURES = {
     "cb_decode_attention": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
     "cb_decode_attention_scratch": ([POINTER(DecodeAttentionArgs)], c_longlong),
     "cb_decode_attention_noalloc": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
+    "cb_decode_step_table_bytes": ([c_int], c_longlong),
+    "cb_decode_step_prepare": ([POINTER(StepPhase), c_int, c_void_p, c_longlong, POINTER(DecodeStepConfig)],
+                               c_int),
+    "cb_decode_step": ([c_void_p, POINTER(DecodeStepConfig), c_void_p, c_void_p, c_void_p], c_int),
     "cb_argmax_rows": ([c_void_p, c_int, c_longlong, c_longlong, c_void_p, c_void_p], c_int),
     "cb_decode_advance": ([c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
                            c_int, c_longlong, c_void_p, c_longlong, c_void_p, c_void_p], c_int),
@@ -208,7 +225,7 @@ def load() -> ctypes.CDLL:
 
 
 FLAG_INDEX, FLAG_POSITION, FLAG_CONTEXT = 1, 2, 3
-FLAG_WAIT_DATA, FLAG_WAIT_SLOT, FLAG_WAIT_DRAIN = 4, 5, 6
+FLAG_WAIT_DATA, FLAG_WAIT_SLOT, FLAG_WAIT_DRAIN, FLAG_WAIT_PHASE = 4, 5, 6, 7
 
 
 def flag_error(value: int) -> Exception:
@@ -221,7 +238,8 @@ def flag_error(value: int) -> Exception:
         return IndexError("decode step would write past the KV-cache context")
     waits = {FLAG_WAIT_DATA: "a consumer waiting for weight data",
              FLAG_WAIT_SLOT: "a producer waiting for a free ring slot",
-             FLAG_WAIT_DRAIN: "the end-of-kernel drain of bulk copies"}
+             FLAG_WAIT_DRAIN: "the end-of-kernel drain of bulk copies",
+             FLAG_WAIT_PHASE: "a block waiting for the previous phase of the decode step"}
     if value in waits:
         return KernelError(f"kernel timed out in {waits[value]} (results are invalid)")
     return KernelError(f"kernel error flag {value}")

@@ -31,7 +31,8 @@ class CudaB200Compiler(Compiler):
 
     def __init__(self, device_index: Optional[int] = None, *, use_graphs: Optional[bool] = None,
                  pdl: bool = True, fuse_decode: bool = True, alias_caches: bool = True,
-                 max_positions: int = 8192, gemv_grid: Optional[int] = None) -> None:
+                 max_positions: int = 8192, gemv_grid: Optional[int] = None,
+                 decode_step: Optional[bool] = None) -> None:
         import os
 
         self.device = CudaB200Device(device_index)
@@ -39,6 +40,9 @@ class CudaB200Compiler(Compiler):
             gemv_grid = int(os.environ.get("CUDA_B200_GEMV_GRID", "0"))
         if use_graphs is None:  # CUDA graphs for repeated runs (CUDA_B200_GRAPHS=0: launch one by one)
             use_graphs = os.environ.get("CUDA_B200_GRAPHS", "1") != "0"
+        if decode_step is None:  # fused decode steps as one persistent launch (cb_decode_step)
+            decode_step = os.environ.get("CUDA_B200_DECODE_STEP", "1") != "0"
+        self.decode_step = decode_step
         self.use_graphs = use_graphs
         self.pdl = pdl
         self.fuse_decode = fuse_decode

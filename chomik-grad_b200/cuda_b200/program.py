@@ -16,6 +16,13 @@ Other outputs are fresh arrays owned by the caller.
 
 Graphs are keyed by the addresses of pointer-bound inputs; a key seen twice
 is captured and replayed from then on.
+
+A fused decode step (only GEMV and decode-attention steps) runs as ONE
+persistent launch, ``cb_decode_step``, instead of one launch per step: the
+steps become the phases of its table (prepared per key, since the table holds
+the bound pointers).  The SwiGLU epilogue of a gate/up GEMV becomes a plain
+store of [gate | up] into a program buffer plus the SwiGLU x mode of the
+down-projection phase that reads it.
 """
 
 from __future__ import annotations
@@ -54,6 +61,14 @@ class CudaB200Program(CompiledProgram):
         self._capture_stream: Optional[int] = None
         self.use_graphs = compiler.use_graphs
         self.launches = 0  # kernels launched by the last eager run (graph replays re-run them)
+        self.step_mode = bool(getattr(compiler, "decode_step", False)) and self._fusable(plan)
+        self._step_tables: Dict[tuple, Tuple[object, _lib.DecodeStepConfig]] = {}
+
+    @staticmethod
+    def _fusable(plan: Plan) -> bool:
+        """Whether the plan is a fused decode step cb_decode_step can run whole."""
+        names = {s.name for s in plan.steps}
+        return bool(plan.steps) and names <= {"gemv", "decode_attention"} and "gemv" in names
 
     # ------------------------------------------------------------ build
     def _build(self) -> None:
@@ -76,6 +91,16 @@ class CudaB200Program(CompiledProgram):
         for init in self.plan.init_steps:
             if init["name"] == "rms_table":
                 self._rms_table(init, stream)
+        if self.step_mode:
+            n = len(self.plan.steps)
+            self._step_counters = torch.zeros(n, dtype=torch.int32, device=dev)
+            self._step_flag = (self._tensors[self.plan.error_flag] if self.plan.error_flag is not None
+                               else torch.zeros(1, dtype=torch.int32, device=dev))
+            # a [gate | up] buffer per SwiGLU: every buffer the step writes is
+            # written once per launch (its x staging reads them through L1)
+            self._gate_up = {s.out.buf: torch.empty(2 * s.args["rows"][0], dtype=torch.float32, device=dev)
+                             for s in self.plan.steps
+                             if s.name == "gemv" and s.args["epilogue"] == _lib.EPI_SILU_MUL}
         self._built = True
 
     def _rms_table(self, init, stream: int) -> None:
@@ -264,12 +289,17 @@ class CudaB200Program(CompiledProgram):
 
     def check_errors(self) -> None:
         """Raise if a kernel set the program's error flag (cb_gemv_args.error_flag)."""
-        if self.plan.error_flag is None:
+        if self.step_mode and self._built:
+            flag = self._step_flag
+        elif self.plan.error_flag is not None:
+            flag = self._tensors[self.plan.error_flag]
+        else:
             return
-        flag = self._tensors[self.plan.error_flag]
         value = int(flag[0].item())
         if value:
             flag.zero_()
+            if value >= _lib.FLAG_WAIT_DATA:
+                self._reset_counters()
             raise _lib.flag_error(value)
 
     # ------------------------------------------------------------ launches
@@ -280,6 +310,9 @@ class CudaB200Program(CompiledProgram):
         return base + view.offset * view.dtype.itemsize
 
     def _launch_all(self, stream: int) -> None:
+        if self.step_mode:
+            self._launch_step(stream)
+            return
         for step in self.plan.steps:
             getattr(self, f"_step_{step.name}")(step, stream)
         self.launches = len(self.plan.steps)
@@ -437,6 +470,9 @@ class CudaB200Program(CompiledProgram):
             left -= size
 
     def _step_gemv(self, step: Step, stream: int) -> None:
+        _lib.call("cb_gemv", ctypes.byref(self._gemv_args(step)), stream)
+
+    def _gemv_args(self, step: Step) -> _lib.GemvArgs:
         g = step.args
         a = _lib.GemvArgs()
         weights: Sequence[View] = g["weights"]
@@ -480,9 +516,12 @@ class CudaB200Program(CompiledProgram):
             self._prefetch(a, g["prefetch"])
         a.grid = self._compiler.gemv_grid
         a.pdl = int(self._compiler.pdl)
-        _lib.call("cb_gemv", ctypes.byref(a), stream)
+        return a
 
     def _step_decode_attention(self, step: Step, stream: int) -> None:
+        _lib.call("cb_decode_attention", ctypes.byref(self._attention_args(step)), stream)
+
+    def _attention_args(self, step: Step) -> _lib.DecodeAttentionArgs:
         g = step.args
         a = _lib.DecodeAttentionArgs()
         a.qkv = self.ptr(g["qkv"])
@@ -505,7 +544,59 @@ class CudaB200Program(CompiledProgram):
             self._prefetch(a, g["prefetch"])
         a.split = 32
         a.pdl = int(self._compiler.pdl)
-        _lib.call("cb_decode_attention", ctypes.byref(a), stream)
+        return a
+
+    # ------------------------------------------------------------ whole decode step
+    def _step_table(self) -> Tuple[object, _lib.DecodeStepConfig]:
+        """The prepared cb_decode_step table of the current bindings (one per key)."""
+        key = getattr(self, "_last_key", ())
+        entry = self._step_tables.get(key)
+        if entry is not None:
+            return entry
+        steps = self.plan.steps
+        phases = (_lib.StepPhase * len(steps))()
+        gate_up = {buf: int(t.data_ptr()) for buf, t in self._gate_up.items()}
+        for phase, step in zip(phases, steps):
+            if step.name == "decode_attention":
+                phase.kind = _lib.PHASE_ATTENTION
+                phase.attention = self._attention_args(step)
+                continue
+            a = self._gemv_args(step)
+            phase.kind = _lib.PHASE_GEMV
+            if a.epilogue == _lib.EPI_SILU_MUL:  # store [gate | up]; the down phase applies SwiGLU
+                a.epilogue, a.out = _lib.EPI_STORE, gate_up[step.out.buf]
+            x_buf = step.args["x"].buf
+            if x_buf in gate_up:
+                a.x, a.x_dtype = gate_up[x_buf], _lib.F32
+                phase.x_mode = _lib.X_SILU_MUL
+            phase.gemv = a
+        lib = _lib.load()
+        torch = _torch()
+        table = torch.empty(lib.cb_decode_step_table_bytes(len(steps)), dtype=torch.uint8,
+                            device=self.device.torch_device)
+        config = _lib.DecodeStepConfig()
+        _lib.check(lib.cb_decode_step_prepare(phases, len(steps), table.data_ptr(), table.numel(),
+                                              ctypes.byref(config)), "cb_decode_step_prepare")
+        if len(self._step_tables) >= 8:
+            self._step_tables.pop(next(iter(self._step_tables)))
+        self._step_tables[key] = (table, config)
+        return table, config
+
+    def _launch_step(self, stream: int) -> None:
+        table, config = self._step_table()
+        _lib.call("cb_decode_step", table.data_ptr(), ctypes.byref(config), self._step_counters.data_ptr(),
+                  self._step_flag.data_ptr(), stream)
+        self.launches = 1
+
+    def _reset_counters(self) -> None:
+        """Zero every arrival/ticket counter after a kernel wait gave up."""
+        if self.step_mode:
+            self._step_counters.zero_()
+        for step in self.plan.steps:
+            for name in ("counters", "counter"):
+                buf = step.args.get(name)
+                if buf is not None and buf in self._tensors:
+                    self._tensors[buf].zero_()
 
     # ------------------------------------------------------------ cleanup
     def close(self) -> None:

@@ -135,7 +135,7 @@ class LlamaRuntime:
         return produced[0], list(produced[1:])
 
     def decode_on_device(self, token: int, position: int, context: int, caches: List[Any],
-                         steps: int, *, timed: bool = False):
+                         steps: int, *, timed: bool = False, replay_times: Optional[List[float]] = None):
         """Greedy-decode ``steps`` tokens with no host round trip per token.
 
         The decode program runs once normally (binding ``token``/``position``
@@ -143,6 +143,9 @@ class LlamaRuntime:
         ``cb_decode_advance`` writing each next step's inputs from the
         previous argmax.  Only for the ``cuda-b200`` compiler.  Returns the
         tokens (and, with ``timed``, the device milliseconds of the replays).
+        With ``replay_times``, CUDA events around every replay append each
+        replay's device milliseconds (the decode-step kernel alone when the
+        program runs as one cb_decode_step launch).
         """
         import torch
 
@@ -165,17 +168,25 @@ class LlamaRuntime:
                 code(program.plan.input_buffers[write].dtype), context, log.data_ptr())
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
+        marks = ([(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(1, steps)] if replay_times is not None else None)
         start.record()
         # advance i logs the token of the step that just ran (position + i - 1)
         for i in range(1, steps):
             _lib.check(lib.cb_decode_advance(*args, i - 1, program.error_pointer(), stream),
                        "cb_decode_advance")
+            if marks is not None:
+                marks[i - 1][0].record()
             program.replay(stream)
+            if marks is not None:
+                marks[i - 1][1].record()
         end.record()
         final = program._tensors[program.plan.argmax_of[0]]
         log[steps - 1:steps].copy_(final[:1])
         end.synchronize()
         program.check_errors()
+        if marks is not None:
+            replay_times.extend(a.elapsed_time(b) for a, b in marks)
         tokens = [int(t) for t in log[:steps].tolist()]
         return (tokens, start.elapsed_time(end)) if timed else tokens
 

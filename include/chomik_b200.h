@@ -38,7 +38,8 @@ enum {
   CB_FLAG_CONTEXT = 3,
   CB_FLAG_WAIT_DATA = 4,
   CB_FLAG_WAIT_SLOT = 5,
-  CB_FLAG_WAIT_DRAIN = 6
+  CB_FLAG_WAIT_DRAIN = 6,
+  CB_FLAG_WAIT_PHASE = 7 /* cb_decode_step: a block waiting for the previous phase */
 };
 
 #define CB_MAX_DIMS 8
@@ -345,6 +346,64 @@ CB_API long long cb_decode_attention_scratch(const cb_decode_attention_args* arg
  * kv_heads > 256) return CB_ERR_INVALID before any launch.  All calls on a
  * device share the arrays: calls that overlap on the GPU race. */
 CB_API int cb_decode_attention_noalloc(const cb_decode_attention_args* args, cb_stream_t stream);
+
+/* ---- whole decode step in one launch --------------------------------------
+ * The fused decode step of LlamaDecoderStep (chomikgrad/llama.py:469-543)
+ * -- per layer the norm->QKV GEMV, RoPE + cache blend + attention, O GEMV +
+ * residual, norm->gate/up GEMV, SwiGLU->down GEMV + residual, then the final
+ * norm->lm_head GEMV + greedy argmax -- as phases of ONE persistent,
+ * cooperative launch (one block per SM) instead of one launch per kernel.
+ * Each block streams its rows of every phase through a shared-memory ring
+ * (bulk copies, continuing across phase boundaries, with L2 prefetch of the
+ * next phase), and waits (bounded) for the previous phase on a grid-wide
+ * counter before it stages x.  Results equal cb_gemv / cb_decode_attention
+ * run one after another with the same arguments. */
+enum { CB_PHASE_GEMV = 0, CB_PHASE_ATTENTION = 1 };
+/* x of a GEMV phase: as given, or the SwiGLU of a [gate | up] vector of
+ * 2*k float32 values: x[i] = silu(v[i]) * v[k + i] (llama.py:289-291,371-380) */
+enum { CB_X_PLAIN = 0, CB_X_SILU_MUL = 1 };
+typedef struct {
+  int kind;   /* CB_PHASE_* */
+  int x_mode; /* CB_X_*, GEMV phases */
+  cb_gemv_args gemv;           /* epilogue STORE, RESIDUAL or ARGMAX; grid, pdl
+                                  and prefetch fields are ignored */
+  cb_decode_attention_args attention; /* split 0 or 32; pdl, prefetch ignored */
+} cb_step_phase;
+/* Launch shape of a prepared step (filled by cb_decode_step_prepare). */
+typedef struct {
+  int grid;      /* blocks per step: one per SM */
+  int n_phases;
+  int w_dtype;   /* weight dtype of every GEMV phase */
+  int head_size; /* of the attention phases (0: none) */
+  long long slot_bytes, x_bytes, norm_bytes, smem; /* shared-memory layout */
+  /* L2 lookahead: bytes of its rows of the next GEMV phase each block asks L2
+   * to prefetch when it starts streaming a phase (prepare sets the default) */
+  long long prefetch_bytes;
+  /* ring copies each producer lane keeps in flight (1 or 2; prepare sets 2):
+   * fewer queue less data ahead of the consumers' latency-critical loads */
+  int lane_inflight;
+  /* optional (NULL = off): grid * n_phases * 12 nanosecond stamps
+   * (%globaltimer) per block and phase, for tuning the schedule: wait begins,
+   * wait ends, x staged, phase done, producer issued the phase's last stage,
+   * thread 0's x loads returned, norm sum done, the last warp's x loads
+   * returned, thread 0 normalised x, the last warp finished staging, 2 spare */
+  unsigned long long* timeline;
+} cb_decode_step_config;
+/* Device bytes of the schedule table cb_decode_step_prepare writes. */
+CB_API long long cb_decode_step_table_bytes(int n_phases);
+/* Check the phases and write their schedule to `table` (device memory of
+ * cb_decode_step_table_bytes bytes; synchronous, so not during stream
+ * capture).  The table holds the phases' pointers: prepare again when any
+ * changes.  An argmax phase's scratch must hold config->grid entries. */
+CB_API int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* table,
+                                  long long table_bytes, cb_decode_step_config* config);
+/* Run the prepared step.  `counters`: n_phases unsigned ints, zero before
+ * the first launch; a step that completes leaves them zero (after a wait
+ * gave up -- *error_flag >= CB_FLAG_WAIT_DATA -- the caller zeroes them and
+ * the attention/argmax counters of the phases).  Launches of one table must
+ * not overlap on the GPU. */
+CB_API int cb_decode_step(const void* table, const cb_decode_step_config* config, unsigned int* counters,
+                          int* error_flag, cb_stream_t stream);
 
 /* On-device greedy step driver for back-to-back decode replays: from the
  * previous step's argmax it writes the next step's token id, position + 1,
