@@ -44,7 +44,7 @@ constexpr int kStepConsumers = 8;                        // = attention's 8 warp
 constexpr int kStepThreads = (kStepConsumers + 1) * 32;  // + producer warp
 constexpr int kStepSlots = 2 * kStepConsumers;           // slot s owned by warp s % 8
 constexpr long long kStepSmemMax = 227 * 1024 - 3 * 1024;  // dynamic; the rest is static
-constexpr int kResidualMax = 256;                          // residual values staged per block
+constexpr int kRowValsMax = 256;  // per-block row values: staged residuals, or SwiGLU gate/up totals
 constexpr long long kNormStageMax = 16 * 1024;             // largest norm-weight vector staged
 constexpr long long kPrefetchDefault = 0;  // L2 lookahead per block and phase (measured: none is best)
 constexpr int kThreadChunks = 3;                         // x chunks per consumer thread
@@ -65,6 +65,7 @@ struct alignas(16) PhaseDesc {
   // phase's ordinal among such phases (-1: read from global memory), and the
   // copy this phase's start issues -- the NEXT staged phase's weights.
   int norm_ord, next_norm_slot;
+  int paired;  // SwiGLU: units are gate/up pairs; a block streams its gate rows, then the same up rows
   const void* next_norm_w;
   long long next_norm_bytes;
   const void* first_norm_w;  // phase 0 only: the copy issued at kernel start
@@ -109,6 +110,8 @@ enum {
   kStampLastLoad = 7,  // the last warp's x loads returned (latest over warps)
   kStampNormed = 8,    // thread 0 normalised its x values
   kStampLastArrive = 9,  // the last warp reached the end of x staging
+  kStampW0First = 10,    // warp 0's first stage of the phase had landed
+  kStampW0Last = 11,     // warp 0 finished its last stage of the phase
   kStamps = 12
 };
 
@@ -178,7 +181,8 @@ __device__ __forceinline__ void unit_range(const PhaseDesc& P, long long cta, lo
 __device__ __forceinline__ long long block_stages(const PhaseDesc& P, long long cta) {
   long long u0, u1;
   unit_range(P, cta, &u0, &u1);
-  return (u1 - u0 + P.rows - 1) / P.rows;
+  const long long n_local = P.paired ? 2 * (u1 - u0) : u1 - u0;
+  return (n_local + P.rows - 1) / P.rows;
 }
 
 // End of the run of rows starting at u that lies inside one weight matrix.
@@ -259,7 +263,7 @@ struct StepShared {
   // latency-critical loads of the window (phase counter, x, residual) do not
   // queue behind up to a ring of bulk data on the way to this SM.
   int quiet;
-  float residual[kResidualMax];  // this block's residual values of the phase
+  float row_vals[kRowValsMax];  // this block's residual values, or its SwiGLU gate | up totals
 };
 
 // A load issued before the phase wait and consumed after it.  As volatile
@@ -335,9 +339,9 @@ __device__ void stage_x(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>& p
   const int warp = tid >> 5, lane = tid & 31;
   const bool vec = P.x_vec != 0;
   // the block's residual values ride along with the x loads
-  float res[kResidualMax / kAttnThreads];
+  float res[kRowValsMax / kAttnThreads];
 #pragma unroll
-  for (int j = 0; j < kResidualMax / kAttnThreads; ++j) {
+  for (int j = 0; j < kRowValsMax / kAttnThreads; ++j) {
     const int i = tid + j * N;
     if (i < n_res) res[j] = load_cg_f32(a.residual, res_first + i, a.residual_dtype);
   }
@@ -456,9 +460,9 @@ __device__ void stage_x(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>& p
     }
   }
 #pragma unroll
-  for (int j = 0; j < kResidualMax / kAttnThreads; ++j) {
+  for (int j = 0; j < kRowValsMax / kAttnThreads; ++j) {
     const int i = tid + j * N;
-    if (i < n_res) sh.residual[i] = res[j];
+    if (i < n_res) sh.row_vals[i] = res[j];
   }
   if (lane == 0 && S.timeline != nullptr)
     atomicMax(S.timeline + (static_cast<long long>(blockIdx.x) * S.n_phases + p) * kStamps + kStampLastArrive,
@@ -478,7 +482,11 @@ __device__ void gemv_phase(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>
   const int warp = tid >> 5, lane = tid & 31;
   long long u0, u1;
   unit_range(P, blockIdx.x, &u0, &u1);
-  const long long n_stages = (u1 - u0 + P.rows - 1) / P.rows;
+  // the block's rows in stream order: its units, or for SwiGLU its gate rows
+  // then the same up rows (block-local index j)
+  const long long n_units = u1 - u0;
+  const long long n_local = P.paired ? 2 * n_units : n_units;
+  const long long n_stages = (n_local + P.rows - 1) / P.rows;
   const long long chunks = a.k / VE;
   float4* xb = xa + (chunks + 1);
   float best_v = 0.0f;
@@ -495,8 +503,8 @@ __device__ void gemv_phase(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>
       rrow *= P.units;
     }
     // residual values of this block's rows, staged with x when they fit
-    const bool res_staged = a.epilogue == CB_EPI_RESIDUAL && u1 - u0 <= kResidualMax;
-    stage_x<WT>(P, pre, xa, xb, sh, tid, rrow + u0, res_staged ? static_cast<int>(u1 - u0) : 0, S, p, norm_smem,
+    const bool res_staged = a.epilogue == CB_EPI_RESIDUAL && n_units <= kRowValsMax;
+    stage_x<WT>(P, pre, xa, xb, sh, tid, rrow + u0, res_staged ? static_cast<int>(n_units) : 0, S, p, norm_smem,
                 norm_bar);
     if (tid == 0) {
       stamp(S, p, kStampStaged);
@@ -514,9 +522,10 @@ __device__ void gemv_phase(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>
         }
         break;
       }
+      if (tid == 0 && s < C) stamp(S, p, kStampW0First);
       const unsigned char* stage = ring + slot * S.slot_bytes;
-      const long long first = u0 + s * P.rows;
-      const int in_stage = static_cast<int>(first + P.rows < u1 ? P.rows : u1 - first);
+      const long long first = s * P.rows;  // block-local
+      const int in_stage = static_cast<int>(first + P.rows < n_local ? P.rows : n_local - first);
       long long row_at[kMaxStageRows];
       float totals[kMaxStageRows];
 #pragma unroll
@@ -535,21 +544,33 @@ __device__ void gemv_phase(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>
       for (int r = 1; r < kMaxStageRows; ++r)
         if (lane == r) mine = totals[r];
       if (lane < in_stage) {
-        const long long u = first + lane;
-        if (a.epilogue == CB_EPI_RESIDUAL)
-          a.out[u] = __fadd_rn(res_staged ? sh.residual[u - u0] : load_cg_f32(a.residual, rrow + u, a.residual_dtype),
+        const long long j = first + lane;
+        if (P.paired) {  // gate / up totals of the block's rows, combined below
+          sh.row_vals[j] = mine;
+        } else if (a.epilogue == CB_EPI_RESIDUAL) {
+          const long long u = u0 + j;
+          a.out[u] = __fadd_rn(res_staged ? sh.row_vals[j] : load_cg_f32(a.residual, rrow + u, a.residual_dtype),
                                mine);
-        else  // CB_EPI_STORE, CB_EPI_ARGMAX (logits)
-          a.out[u] = mine;
+        } else {  // CB_EPI_STORE, CB_EPI_ARGMAX (logits)
+          a.out[u0 + j] = mine;
+        }
       }
       if (a.epilogue == CB_EPI_ARGMAX && lane == 0) {
         for (int i = 0; i < in_stage; ++i) {
-          const long long u = first + i;
+          const long long u = u0 + first + i;
           if (best_i < 0 || argmax_better(totals[i], u, best_v, best_i)) {
             best_v = totals[i];
             best_i = u;
           }
         }
+      }
+    }
+    if (tid == 0) stamp(S, p, kStampW0Last);
+    if (P.paired) {  // SwiGLU: silu(gate) * up, as the gemv epilogue computes it
+      consumers_sync(N);
+      for (long long t = tid; t < n_units; t += N) {
+        const float gate = sh.row_vals[t], up = sh.row_vals[n_units + t];
+        a.out[u0 + t] = __fmul_rn(__fdiv_rn(gate, __fadd_rn(expf(-gate), 1.0f)), up);
       }
     }
   }
@@ -577,20 +598,14 @@ __device__ void gemv_phase(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>
     sh.last = ticket == gridDim.x - 1;
   }
   consumers_sync(N);
-  if (!sh.last || tid != 0) return;
+  if (!sh.last) return;  // block-uniform: the last block merges with all its consumer threads
   __threadfence();
-  float bv = 0.0f;
-  long long bi = -1;
-  for (unsigned c = 0; c < gridDim.x; ++c) {
-    const long long ci = __ldcg(a.scratch_idx + c);
-    const float cv = __ldcg(a.scratch_val + c);
-    if (ci >= 0 && (bi < 0 || argmax_better(cv, ci, bv, bi))) {
-      bv = cv;
-      bi = ci;
-    }
+  const long long bi = argmax_merge(a.scratch_val, a.scratch_idx, static_cast<int>(gridDim.x), tid, N,
+                                    sh.warp_best_v, sh.warp_best_i);
+  if (tid == 0) {
+    a.argmax_out[0] = bi;
+    *a.counter = 0u;
   }
-  a.argmax_out[0] = bi;
-  *a.counter = 0u;
 }
 
 template <typename WT, int HD>
@@ -638,12 +653,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         const char* w0 = static_cast<const char*>(Pp->g.w[0]);
         const char* w1 = static_cast<const char*>(Pp->g.w[1]);
         const char* w2 = static_cast<const char*>(Pp->g.w[2]);
-        if (lane == 1 && Pp->g.norm != CB_NORM_NONE) {
-          // the phase's norm weights into L2 now: the consumers ask for them only
-          // at the phase's start, and a cold read waits behind the weight stream
-          const long long bytes = Pp->g.k * (Pp->g.norm_w_dtype == CB_BF16 || Pp->g.norm_w_dtype == CB_F16 ? 2 : 4);
-          if (Pp->nw_vec && bytes % 16 == 0) prefetch_l2(Pp->g.norm_w, static_cast<uint32_t>(bytes));
-        }
+        const bool paired = Pp->paired != 0;
         if (lane == 0 && S.prefetch_bytes > 0) {  // L2 lookahead: the next GEMV phase (wrapping)
           int q = p + 1;
           while (q < S.n_phases && S.phases[q].kind != CB_PHASE_GEMV) ++q;
@@ -656,7 +666,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         const long long lo = static_cast<long long>(blockIdx.x) * per_cta;
         const long long u0 = lo < units ? lo : units;
         const long long u1 = lo + per_cta < units ? lo + per_cta : units;
-        const long long n_stages = (u1 - u0 + rows - 1) / rows;
+        // block-local rows j: its units in order, or (SwiGLU) its gate rows then its up rows
+        const long long n_units = u1 - u0;
+        const long long n_local = paired ? 2 * n_units : n_units;
+        const long long n_stages = (n_local + rows - 1) / rows;
         for (long long s = ((lane - g) % C + C) % C; s < n_stages; s += C) {
           const long long gs = g + s;
           const int slot = static_cast<int>(gs % kStepSlots);
@@ -679,26 +692,37 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             stop = true;
             break;
           }
-          const long long first = u0 + s * rows;
-          const long long end = first + rows < u1 ? first + rows : u1;
+          const long long first = s * rows;
+          const long long end = first + rows < n_local ? first + rows : n_local;
           unsigned char* dst = ring + slot * S.slot_bytes;
           mbar_arrive_expect_tx(full + slot, static_cast<uint32_t>((end - first) * row_bytes));
-          for (long long u = first; u < end;) {  // one copy per run of rows inside one matrix
-            long long stop_u;
+          for (long long j = first; j < end;) {  // one copy per run of rows inside one matrix
+            long long stop_j;
             const char* src;
-            if (u < r0) {
-              stop_u = r0 < end ? r0 : end;
-              src = w0 + u * row_bytes;
-            } else if (u < r01) {
-              stop_u = r01 < end ? r01 : end;
-              src = w1 + (u - r0) * row_bytes;
+            if (paired) {
+              if (j < n_units) {
+                stop_j = n_units < end ? n_units : end;
+                src = w0 + (u0 + j) * row_bytes;
+              } else {
+                stop_j = end;
+                src = w1 + (u0 + j - n_units) * row_bytes;
+              }
             } else {
-              stop_u = end;
-              src = w2 + (u - r01) * row_bytes;
+              const long long u = u0 + j;
+              if (u < r0) {
+                stop_j = r0 - u0 < end ? r0 - u0 : end;
+                src = w0 + u * row_bytes;
+              } else if (u < r01) {
+                stop_j = r01 - u0 < end ? r01 - u0 : end;
+                src = w1 + (u - r0) * row_bytes;
+              } else {
+                stop_j = end;
+                src = w2 + (u - r01) * row_bytes;
+              }
             }
-            bulk_load(dst + (u - first) * row_bytes, src, static_cast<uint32_t>((stop_u - u) * row_bytes),
+            bulk_load(dst + (j - first) * row_bytes, src, static_cast<uint32_t>((stop_j - j) * row_bytes),
                       full + slot);
-            u = stop_u;
+            j = stop_j;
           }
           last = gs;
         }
@@ -875,7 +899,7 @@ long long cb_decode_step_table_bytes(int n_phases) {
 }
 
 int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* table, long long table_bytes,
-                           cb_decode_step_config* config) {
+                           int flags, cb_decode_step_config* config) {
   CB_REQUIRE(phases != nullptr && n_phases > 0 && table != nullptr && config != nullptr,
              "decode step: phases, table and config are required");
   CB_REQUIRE(table_bytes >= cb_decode_step_table_bytes(n_phases), "decode step: table of %lld bytes is too small",
@@ -910,8 +934,18 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
         units += a.w_rows[w];
       }
       for (int w = a.n_w; w < 3; ++w) CB_REQUIRE(a.w_rows[w] == 0, "decode step phase %d: unused w_rows must be 0", i);
-      CB_REQUIRE(a.epilogue == CB_EPI_STORE || a.epilogue == CB_EPI_RESIDUAL || a.epilogue == CB_EPI_ARGMAX,
-                 "decode step phase %d: epilogue must be store, residual or argmax (SwiGLU is an x mode)", i);
+      CB_REQUIRE(a.epilogue == CB_EPI_STORE || a.epilogue == CB_EPI_RESIDUAL || a.epilogue == CB_EPI_ARGMAX ||
+                     a.epilogue == CB_EPI_SILU_MUL,
+                 "decode step phase %d: unknown epilogue %d", i, a.epilogue);
+      if (a.epilogue == CB_EPI_SILU_MUL) {  // gate/up pairs: units are pairs
+        CB_REQUIRE(a.n_w == 2 && a.w_rows[0] == a.w_rows[1], "decode step phase %d: SwiGLU needs gate/up of equal rows",
+                   i);
+        units = a.w_rows[0];
+        CB_REQUIRE((units + grid - 1) / grid * 2 <= kRowValsMax,
+                   "decode step phase %d: %lld SwiGLU rows per block exceed %d", i, (units + grid - 1) / grid,
+                   kRowValsMax / 2);
+        d.paired = 1;
+      }
       CB_REQUIRE(ph.x_mode == CB_X_PLAIN || ph.x_mode == CB_X_SILU_MUL, "decode step phase %d: bad x mode", i);
       CB_REQUIRE(a.x != nullptr && a.out != nullptr, "decode step phase %d: x and out are required", i);
       if (ph.x_mode == CB_X_SILU_MUL)
@@ -960,9 +994,10 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
     }
   }
   CB_REQUIRE(n_gemv > 0, "decode step: no GEMV phase");
-  // An attention output read only by the next phase's x (the O projection) is
-  // never materialised: that phase merges the split partials while staging.
-  for (int i = 0; i + 1 < n_phases; ++i) {
+  // With CB_STEP_MERGE_IN_STAGE, an attention output read only by the next
+  // phase's x (the O projection) is never materialised: that phase merges
+  // the split partials while staging.  Otherwise the attention phase merges.
+  for (int i = 0; (flags & CB_STEP_MERGE_IN_STAGE) != 0 && i + 1 < n_phases; ++i) {
     PhaseDesc& at = desc[static_cast<size_t>(i)];
     PhaseDesc& o = desc[static_cast<size_t>(i) + 1];
     if (at.kind != CB_PHASE_ATTENTION || o.kind != CB_PHASE_GEMV) continue;

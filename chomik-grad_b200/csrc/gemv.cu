@@ -279,20 +279,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const cb_gemv_args a,
     is_last = ticket == gridDim.x - 1;
   }
   consumers_sync(ncons);
-  if (!is_last || tid != 0) return;
+  if (!is_last) return;  // block-uniform: the last block merges with all its consumer threads
   __threadfence();
-  float bv = 0.0f;
-  long long bi = -1;
-  for (unsigned c = 0; c < gridDim.x; ++c) {
-    const long long ci = __ldcg(a.scratch_idx + c);
-    const float cv = __ldcg(a.scratch_val + c);
-    if (ci >= 0 && (bi < 0 || argmax_better(cv, ci, bv, bi))) {
-      bv = cv;
-      bi = ci;
-    }
+  const long long bi = argmax_merge(a.scratch_val, a.scratch_idx, static_cast<int>(gridDim.x), tid, ncons,
+                                    warp_best_v, warp_best_i);
+  if (tid == 0) {
+    a.argmax_out[0] = bi;
+    *a.counter = 0u;
   }
-  a.argmax_out[0] = bi;
-  *a.counter = 0u;
 }
 
 int plan_gemv(const cb_gemv_args& a, Layout* L) {

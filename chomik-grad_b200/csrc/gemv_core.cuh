@@ -65,6 +65,50 @@ __device__ __forceinline__ void consumers_sync(int n) {
   asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory");
 }
 
+// Winner of the per-block argmax partials [0, n) (written by other blocks,
+// read through L2), merged by all `nthreads` consumer threads: strided
+// loads, warp shuffles, then thread 0 over the warps.  argmax_better is a
+// total order (NaN first, then the larger value, then the lower index), so
+// the merge order does not change the result.  Valid in thread 0; red_v and
+// red_i hold nthreads / 32 entries.
+__device__ __forceinline__ long long argmax_merge(const float* vals, const long long* idx, int n, int tid,
+                                                  int nthreads, float* red_v, long long* red_i) {
+  float bv = 0.0f;
+  long long bi = -1;
+  for (int c = tid; c < n; c += nthreads) {
+    const long long ci = __ldcg(idx + c);
+    const float cv = __ldcg(vals + c);
+    if (ci >= 0 && (bi < 0 || argmax_better(cv, ci, bv, bi))) {
+      bv = cv;
+      bi = ci;
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, bv, off);
+    const long long oi = __shfl_down_sync(0xffffffffu, bi, off);
+    if (oi >= 0 && (bi < 0 || argmax_better(ov, oi, bv, bi))) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((tid & 31) == 0) {
+    red_v[tid >> 5] = bv;
+    red_i[tid >> 5] = bi;
+  }
+  consumers_sync(nthreads);
+  if (tid == 0) {
+    bv = 0.0f;
+    bi = -1;
+    for (int w = 0; w < nthreads / 32; ++w) {
+      if (red_i[w] >= 0 && (bi < 0 || argmax_better(red_v[w], red_i[w], bv, bi))) {
+        bv = red_v[w];
+        bi = red_i[w];
+      }
+    }
+  }
+  return bi;
+}
+
 // R rows of one stage against x: totals[r] (valid on every lane).
 template <typename WT, int R>
 __device__ __forceinline__ void stage_dot(const unsigned char* stage, const long long* row_at,

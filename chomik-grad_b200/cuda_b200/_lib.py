@@ -29,6 +29,7 @@ NORM_NONE, NORM_RMS, NORM_RMS_TABLE = 0, 1, 2
 EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
 PHASE_GEMV, PHASE_ATTENTION = 0, 1
 X_PLAIN, X_SILU_MUL = 0, 1
+STEP_MERGE_IN_STAGE = 1
 
 LL8 = c_longlong * MAX_DIMS
 
@@ -195,8 +196,8 @@ _SIGNATURES = {
     "cb_decode_attention_scratch": ([POINTER(DecodeAttentionArgs)], c_longlong),
     "cb_decode_attention_noalloc": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
     "cb_decode_step_table_bytes": ([c_int], c_longlong),
-    "cb_decode_step_prepare": ([POINTER(StepPhase), c_int, c_void_p, c_longlong, POINTER(DecodeStepConfig)],
-                               c_int),
+    "cb_decode_step_prepare": ([POINTER(StepPhase), c_int, c_void_p, c_longlong, c_int,
+                                POINTER(DecodeStepConfig)], c_int),
     "cb_decode_step": ([c_void_p, POINTER(DecodeStepConfig), c_void_p, c_void_p, c_void_p], c_int),
     "cb_argmax_rows": ([c_void_p, c_int, c_longlong, c_longlong, c_void_p, c_void_p], c_int),
     "cb_decode_advance": ([c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,

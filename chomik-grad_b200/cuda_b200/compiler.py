@@ -18,6 +18,7 @@ from typing import Optional, Sequence
 
 import numpy as np
 
+from . import _lib
 from .device import CudaB200Device, DeviceArray
 from .frontend.lazy import Compiler
 from .planner import Planner
@@ -43,6 +44,11 @@ class CudaB200Compiler(Compiler):
         if decode_step is None:  # fused decode steps as one persistent launch (cb_decode_step)
             decode_step = os.environ.get("CUDA_B200_DECODE_STEP", "1") != "0"
         self.decode_step = decode_step
+        # cb_decode_step_prepare flags: attention splits are merged in the O
+        # projection's x staging (measured faster on TinyLlama); set
+        # CUDA_B200_STEP_MERGE=attention to merge them in the attention phase
+        self.step_flags = (0 if os.environ.get("CUDA_B200_STEP_MERGE") == "attention"
+                           else _lib.STEP_MERGE_IN_STAGE)
         self.use_graphs = use_graphs
         self.pdl = pdl
         self.fuse_decode = fuse_decode

@@ -96,11 +96,6 @@ class CudaB200Program(CompiledProgram):
             self._step_counters = torch.zeros(n, dtype=torch.int32, device=dev)
             self._step_flag = (self._tensors[self.plan.error_flag] if self.plan.error_flag is not None
                                else torch.zeros(1, dtype=torch.int32, device=dev))
-            # a [gate | up] buffer per SwiGLU: every buffer the step writes is
-            # written once per launch (its x staging reads them through L1)
-            self._gate_up = {s.out.buf: torch.empty(2 * s.args["rows"][0], dtype=torch.float32, device=dev)
-                             for s in self.plan.steps
-                             if s.name == "gemv" and s.args["epilogue"] == _lib.EPI_SILU_MUL}
         self._built = True
 
     def _rms_table(self, init, stream: int) -> None:
@@ -547,35 +542,29 @@ class CudaB200Program(CompiledProgram):
         return a
 
     # ------------------------------------------------------------ whole decode step
-    def _step_table(self) -> Tuple[object, _lib.DecodeStepConfig]:
+    def _step_table(self, flags: Optional[int] = None) -> Tuple[object, _lib.DecodeStepConfig]:
         """The prepared cb_decode_step table of the current bindings (one per key)."""
-        key = getattr(self, "_last_key", ())
+        if flags is None:
+            flags = self._compiler.step_flags
+        key = (getattr(self, "_last_key", ()), flags)
         entry = self._step_tables.get(key)
         if entry is not None:
             return entry
         steps = self.plan.steps
         phases = (_lib.StepPhase * len(steps))()
-        gate_up = {buf: int(t.data_ptr()) for buf, t in self._gate_up.items()}
         for phase, step in zip(phases, steps):
             if step.name == "decode_attention":
                 phase.kind = _lib.PHASE_ATTENTION
                 phase.attention = self._attention_args(step)
-                continue
-            a = self._gemv_args(step)
-            phase.kind = _lib.PHASE_GEMV
-            if a.epilogue == _lib.EPI_SILU_MUL:  # store [gate | up]; the down phase applies SwiGLU
-                a.epilogue, a.out = _lib.EPI_STORE, gate_up[step.out.buf]
-            x_buf = step.args["x"].buf
-            if x_buf in gate_up:
-                a.x, a.x_dtype = gate_up[x_buf], _lib.F32
-                phase.x_mode = _lib.X_SILU_MUL
-            phase.gemv = a
+            else:
+                phase.kind = _lib.PHASE_GEMV
+                phase.gemv = self._gemv_args(step)
         lib = _lib.load()
         torch = _torch()
         table = torch.empty(lib.cb_decode_step_table_bytes(len(steps)), dtype=torch.uint8,
                             device=self.device.torch_device)
         config = _lib.DecodeStepConfig()
-        _lib.check(lib.cb_decode_step_prepare(phases, len(steps), table.data_ptr(), table.numel(),
+        _lib.check(lib.cb_decode_step_prepare(phases, len(steps), table.data_ptr(), table.numel(), flags,
                                               ctypes.byref(config)), "cb_decode_step_prepare")
         if len(self._step_tables) >= 8:
             self._step_tables.pop(next(iter(self._step_tables)))

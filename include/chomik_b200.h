@@ -365,8 +365,7 @@ enum { CB_X_PLAIN = 0, CB_X_SILU_MUL = 1 };
 typedef struct {
   int kind;   /* CB_PHASE_* */
   int x_mode; /* CB_X_*, GEMV phases */
-  cb_gemv_args gemv;           /* epilogue STORE, RESIDUAL or ARGMAX; grid, pdl
-                                  and prefetch fields are ignored */
+  cb_gemv_args gemv;           /* grid, pdl and prefetch fields are ignored */
   cb_decode_attention_args attention; /* split 0 or 32; pdl, prefetch ignored */
 } cb_step_phase;
 /* Launch shape of a prepared step (filled by cb_decode_step_prepare). */
@@ -391,12 +390,18 @@ typedef struct {
 } cb_decode_step_config;
 /* Device bytes of the schedule table cb_decode_step_prepare writes. */
 CB_API long long cb_decode_step_table_bytes(int n_phases);
+/* prepare flags: merge an attention phase's splits while the next phase (the
+ * O projection reading its output) stages x, instead of in the attention
+ * phase itself (the output is then never written) */
+enum { CB_STEP_MERGE_IN_STAGE = 1 };
 /* Check the phases and write their schedule to `table` (device memory of
  * cb_decode_step_table_bytes bytes; synchronous, so not during stream
  * capture).  The table holds the phases' pointers: prepare again when any
- * changes.  An argmax phase's scratch must hold config->grid entries. */
+ * changes.  An argmax phase's scratch must hold config->grid entries.
+ * SwiGLU (CB_EPI_SILU_MUL) phases: each block streams the same rows of gate
+ * and up, at most 128 rows per block. */
 CB_API int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* table,
-                                  long long table_bytes, cb_decode_step_config* config);
+                                  long long table_bytes, int flags, cb_decode_step_config* config);
 /* Run the prepared step.  `counters`: n_phases unsigned ints, zero before
  * the first launch; a step that completes leaves them zero (after a wait
  * gave up -- *error_flag >= CB_FLAG_WAIT_DATA -- the caller zeroes them and
