@@ -17,6 +17,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "sync.cuh"
 
 namespace cb {
 
@@ -29,23 +30,26 @@ __device__ __forceinline__ void attn_sync() {
 
 // Shared floats an item needs.
 __host__ __device__ inline long long attn_smem_floats(long long group, long long hd) {
-  return (group + 2) * hd + kAttnSplit * (hd + 1) + kAttnSplit * hd + group * kAttnSplit + 2 * group +
-         2 * kAttnSplit;
+  return (group + 2) * hd + kAttnSplit * (hd + 4) + kAttnSplit * hd + group * kAttnSplit + 2 * group +
+         2 * kAttnSplit + hd;
 }
 
 template <int HD>
 struct AttnSmem {
-  float *q_rot, *k_new, *v_new, *ks, *vs, *probs, *stats, *wm, *maskv;
+  static constexpr int KS = HD + 4;  // padded K rows: conflict-free float4 score loads
+  float *q_rot, *k_new, *v_new, *ks, *vs, *probs, *stats, *wm, *maskv, *cs, *sn;
   __device__ AttnSmem(float* smem, int group) {
-    q_rot = smem;
-    k_new = q_rot + group * HD;
-    v_new = k_new + HD;
-    ks = v_new + HD;                   // [kAttnSplit][HD + 1] (padded: conflict-free scores)
-    vs = ks + kAttnSplit * (HD + 1);   // [kAttnSplit][HD]
-    probs = vs + kAttnSplit * HD;      // [group][kAttnSplit]
+    q_rot = smem;                        // [group][HD]
+    k_new = q_rot + group * HD;          // [HD]
+    v_new = k_new + HD;                  // [HD]
+    ks = v_new + HD;                     // [kAttnSplit][KS]
+    vs = ks + kAttnSplit * KS;           // [kAttnSplit][HD]
+    probs = vs + kAttnSplit * HD;        // [group][kAttnSplit]
     stats = probs + group * kAttnSplit;  // [group][2]: max, sum
-    wm = stats + 2 * group;            // [kAttnSplit]
-    maskv = wm + kAttnSplit;           // [kAttnSplit]
+    wm = stats + 2 * group;              // [kAttnSplit]
+    maskv = wm + kAttnSplit;             // [kAttnSplit]
+    cs = maskv + kAttnSplit;             // [HD / 2]: the position's RoPE cosines
+    sn = cs + HD / 2;                    // [HD / 2]: sines
   }
 };
 
@@ -59,6 +63,7 @@ __device__ void attention_stage_cache(const cb_decode_attention_args& a, int g, 
                                       int tid) {
   const int group = static_cast<int>(a.heads / a.kv_heads);
   AttnSmem<HD> s(smem, group);
+  constexpr int half = HD / 2;
   const long long lo_pos = static_cast<long long>(split) * kAttnSplit;
   const int n = attn_rows(a, split);
   const float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
@@ -67,37 +72,37 @@ __device__ void attention_stage_cache(const cb_decode_attention_args& a, int g, 
     const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
     const float4 kv = __ldcg(reinterpret_cast<const float4*>(kc) + e);
     const float4 vv = __ldcg(reinterpret_cast<const float4*>(vc) + e);
-    float* kd = s.ks + r * (HD + 1) + d4;
-    kd[0] = kv.x;
-    kd[1] = kv.y;
-    kd[2] = kv.z;
-    kd[3] = kv.w;
+    *reinterpret_cast<float4*>(s.ks + r * AttnSmem<HD>::KS + d4) = kv;
     *reinterpret_cast<float4*>(s.vs + r * HD + d4) = vv;
   }
   for (int r = tid; r < n; r += kAttnThreads) {
     s.wm[r] = load_as_f32(a.write_mask, lo_pos + r, a.write_mask_dtype);
     s.maskv[r] = load_as_f32(a.mask, lo_pos + r, a.mask_dtype);
   }
-}
-
-// Needs attention_stage_cache's shared memory (and an attn_sync after it).
-template <int HD>
-__device__ void attention_finish(const cb_decode_attention_args& a, int g, int split, int splits, float* smem,
-                                 int* s_last, int tid, bool merge) {
-  const int group = static_cast<int>(a.heads / a.kv_heads);
-  constexpr int half = HD / 2;
-  constexpr int KS = HD + 1;
-  AttnSmem<HD> s(smem, group);
-  const int warp = tid >> 5, lane = tid & 31;
-  constexpr int warps = kAttnThreads / 32;
-
+  // the position's RoPE row (the position is an input of the step, not of q/k/v)
   long long pos = load_index(a.position, 0, a.position_dtype);
   if (pos < 0 || pos >= a.n_positions) {
     if (tid == 0 && split == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_POSITION);
     pos = pos < 0 ? 0 : a.n_positions - 1;
   }
-  const float* cs = a.cos_table + pos * half;
-  const float* sn = a.sin_table + pos * half;
+  for (int j = tid; j < half; j += kAttnThreads) {
+    s.cs[j] = a.cos_table[pos * half + j];
+    s.sn[j] = a.sin_table[pos * half + j];
+  }
+}
+
+// Needs attention_stage_cache's shared memory (and an attn_sync after it).
+template <int HD>
+__device__ void attention_finish(const cb_decode_attention_args& a, int g, int split, int splits, float* smem,
+                                 int* s_last, int tid, bool merge, unsigned long long* stamps = nullptr) {
+  const int group = static_cast<int>(a.heads / a.kv_heads);
+  constexpr int half = HD / 2;
+  constexpr int KS = AttnSmem<HD>::KS;
+  AttnSmem<HD> s(smem, group);
+  const int warp = tid >> 5, lane = tid & 31;
+  constexpr int warps = kAttnThreads / 32;
+  const float* cs = s.cs;
+  const float* sn = s.sn;
   for (int i = tid; i < group * half; i += kAttnThreads) {
     const int h = i / half, j = i % half;
     const float* src = a.qkv + a.q_off + (static_cast<long long>(g) * group + h) * HD;
@@ -114,6 +119,7 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
   for (int d = tid; d < HD; d += kAttnThreads)
     s.v_new[d] = __ldcg(a.qkv + a.v_off + static_cast<long long>(g) * HD + d);
   attn_sync();
+  if (stamps != nullptr && tid == 0) stamps[0] = global_ns();
 
   // rows with wm != 0 get the blend, in shared memory and in the cache
   const long long lo_pos = static_cast<long long>(split) * kAttnSplit;
@@ -125,9 +131,8 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
     const float wm = s.wm[r];
     if (wm == 0.0f) continue;
     const float keep = round_to(__fsub_rn(1.0f, wm), a.one_minus_dtype);
-    float* kd = s.ks + r * KS + d4;
+    float4 kv = *reinterpret_cast<float4*>(s.ks + r * KS + d4);
     float4 vv = *reinterpret_cast<float4*>(s.vs + r * HD + d4);
-    float4 kv = make_float4(kd[0], kd[1], kd[2], kd[3]);
     float* kf = &kv.x;
     float* vf = &vv.x;
 #pragma unroll
@@ -137,27 +142,28 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
     }
     reinterpret_cast<float4*>(kc)[e] = kv;
     reinterpret_cast<float4*>(vc)[e] = vv;
-    kd[0] = kv.x;
-    kd[1] = kv.y;
-    kd[2] = kv.z;
-    kd[3] = kv.w;
+    *reinterpret_cast<float4*>(s.ks + r * KS + d4) = kv;
     *reinterpret_cast<float4*>(s.vs + r * HD + d4) = vv;
   }
   attn_sync();
+  if (stamps != nullptr && tid == 0) stamps[1] = global_ns();
 
   // scores: warp = query head (looping), lane = position
   for (int h = warp; h < group; h += warps) {
     float x = -INFINITY;
     if (lane < n) {
-      const float* q = s.q_rot + h * HD;
-      const float* k = s.ks + lane * KS;
-      float s0 = 0.0f, s1 = 0.0f;
+      const float4* q = reinterpret_cast<const float4*>(s.q_rot + h * HD);
+      const float4* k = reinterpret_cast<const float4*>(s.ks + lane * KS);
+      float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
 #pragma unroll
-      for (int d = 0; d < HD; d += 2) {
-        s0 = fmaf(q[d], k[d], s0);
-        s1 = fmaf(q[d + 1], k[d + 1], s1);
+      for (int d = 0; d < HD / 4; ++d) {
+        const float4 qa = q[d], ka = k[d];
+        s0 = fmaf(qa.x, ka.x, s0);
+        s1 = fmaf(qa.y, ka.y, s1);
+        s2 = fmaf(qa.z, ka.z, s2);
+        s3 = fmaf(qa.w, ka.w, s3);
       }
-      x = __fadd_rn(__fdiv_rn(s0 + s1, a.divisor), s.maskv[lane]);
+      x = __fadd_rn(__fdiv_rn((s0 + s1) + (s2 + s3), a.divisor), s.maskv[lane]);
     }
     const float m = warp_max(x);
     const float p = lane < n ? expf(x - m) : 0.0f;
@@ -169,25 +175,36 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
     }
   }
   attn_sync();
+  if (stamps != nullptr && tid == 0) stamps[2] = global_ns();
 
-  // p @ v for every (head, dim) of the group; partials to scratch
-  for (int i = tid; i < group * HD; i += kAttnThreads) {
-    const int h = i / HD, d = i % HD;
+  // p @ v: two dims of one head per thread; partials to scratch
+  for (int i = tid; i < group * half; i += kAttnThreads) {
+    const int h = i / half, d = (i % half) * 2;
     const float* p = s.probs + h * kAttnSplit;
-    float acc0 = 0.0f, acc1 = 0.0f;
+    float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
     int j = 0;
     for (; j + 1 < n; j += 2) {
-      acc0 = fmaf(p[j], s.vs[j * HD + d], acc0);
-      acc1 = fmaf(p[j + 1], s.vs[(j + 1) * HD + d], acc1);
+      const float p0 = p[j], p1 = p[j + 1];
+      const float2 v0 = *reinterpret_cast<const float2*>(s.vs + j * HD + d);
+      const float2 v1 = *reinterpret_cast<const float2*>(s.vs + (j + 1) * HD + d);
+      acc0.x = fmaf(p0, v0.x, acc0.x);
+      acc0.y = fmaf(p0, v0.y, acc0.y);
+      acc1.x = fmaf(p1, v1.x, acc1.x);
+      acc1.y = fmaf(p1, v1.y, acc1.y);
     }
-    if (j < n) acc0 = fmaf(p[j], s.vs[j * HD + d], acc0);
+    if (j < n) {
+      const float2 v0 = *reinterpret_cast<const float2*>(s.vs + j * HD + d);
+      acc0.x = fmaf(p[j], v0.x, acc0.x);
+      acc0.y = fmaf(p[j], v0.y, acc0.y);
+    }
     float* part = a.scratch + (static_cast<long long>(split) * a.heads + g * group + h) * (HD + 2);
-    part[2 + d] = acc0 + acc1;
+    *reinterpret_cast<float2*>(part + 2 + d) = make_float2(acc0.x + acc1.x, acc0.y + acc1.y);
     if (d == 0) {
       part[0] = s.stats[2 * h];
       part[1] = s.stats[2 * h + 1];
     }
   }
+  if (stamps != nullptr && tid == 0) stamps[3] = global_ns();
   if (!merge) return;
 
   // merge the splits of this KV group in split order

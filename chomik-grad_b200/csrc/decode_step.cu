@@ -97,6 +97,7 @@ struct StepParams {
   unsigned long long* timeline;  // optional stamps, see cb_decode_step_config
   long long prefetch_bytes;      // L2 lookahead per block and phase
   int lane_inflight;             // ring copies in flight per producer lane (1 or 2)
+  int quiet_window;              // pause ring copies from a phase's wait until its x is staged
 };
 
 enum {
@@ -633,7 +634,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     mbar_fence_init();
     sh.stop = 0;
     sh.last = 0;
-    sh.quiet = 1;  // phase 0 stages x first
+    sh.quiet = S.quiet_window;  // phase 0 stages x first
   }
   __syncthreads();
 
@@ -773,7 +774,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       ++norm_issued;
     }
     // before the wait: everything that does not depend on phase p-1
-    if (tid == 0) *reinterpret_cast<volatile int*>(&sh.quiet) = 1;
+    if (tid == 0 && S.quiet_window) *reinterpret_cast<volatile int*>(&sh.quiet) = 1;
     StagePre<VE> pre;
     const bool gemv = P.kind == CB_PHASE_GEMV;
     if (gemv) {
@@ -804,7 +805,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
           attention_stage_cache<HD>(P.at, grp, split, attn_smem, tid);
           attn_sync();
         }
-        attention_finish<HD>(P.at, grp, split, P.splits, attn_smem, &sh.last, tid, P.merge_in_kernel != 0);
+        unsigned long long* item_stamps =
+            S.timeline != nullptr && it == blockIdx.x
+                ? S.timeline + (static_cast<long long>(blockIdx.x) * S.n_phases + p) * kStamps + kStampLoaded
+                : nullptr;
+        attention_finish<HD>(P.at, grp, split, P.splits, attn_smem, &sh.last, tid, P.merge_in_kernel != 0,
+                             item_stamps);
       }
       if (tid == 0) *reinterpret_cast<volatile int*>(&sh.quiet) = 0;
     }
@@ -1075,6 +1081,7 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
   config->smem = kStepSlots * slot_bytes + x_bytes + 2 * norm_bytes + bar_bytes;
   config->prefetch_bytes = kPrefetchDefault;
   config->lane_inflight = 2;
+  config->quiet_window = 1;
   config->timeline = nullptr;
   return CB_OK;
 }
@@ -1098,6 +1105,7 @@ int cb_decode_step(const void* table, const cb_decode_step_config* config, unsig
   S.prefetch_bytes = config->prefetch_bytes < 0 ? 0 : config->prefetch_bytes;
   CB_REQUIRE(config->lane_inflight == 1 || config->lane_inflight == 2, "decode step: lane_inflight must be 1 or 2");
   S.lane_inflight = config->lane_inflight;
+  S.quiet_window = config->quiet_window != 0;
   return launch_step(S, *config, static_cast<cudaStream_t>(stream));
 }
 

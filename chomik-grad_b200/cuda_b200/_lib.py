@@ -160,7 +160,8 @@ class DecodeStepConfig(ctypes.Structure):
     _fields_ = [("grid", c_int), ("n_phases", c_int), ("w_dtype", c_int), ("head_size", c_int),
                 ("slot_bytes", c_longlong), ("x_bytes", c_longlong), ("norm_bytes", c_longlong),
                 ("smem", c_longlong),
-                ("prefetch_bytes", c_longlong), ("lane_inflight", c_int), ("timeline", c_void_p)]
+                ("prefetch_bytes", c_longlong), ("lane_inflight", c_int), ("quiet_window", c_int),
+                ("timeline", c_void_p)]
 
 
 class KernelError(RuntimeError):

@@ -381,6 +381,10 @@ typedef struct {
   /* ring copies each producer lane keeps in flight (1 or 2; prepare sets 2):
    * fewer queue less data ahead of the consumers' latency-critical loads */
   int lane_inflight;
+  /* 1 (prepare's default): from the start of a phase's wait until its x is
+   * staged, issue no new ring copies, so the latency-critical loads of that
+   * window do not queue behind bulk data; 0: keep streaming */
+  int quiet_window;
   /* optional (NULL = off): grid * n_phases * 12 nanosecond stamps
    * (%globaltimer) per block and phase, for tuning the schedule: wait begins,
    * wait ends, x staged, phase done, producer issued the phase's last stage,
