@@ -30,23 +30,20 @@ __device__ __forceinline__ void attn_sync() {
 
 // Shared floats an item needs.
 __host__ __device__ inline long long attn_smem_floats(long long group, long long hd) {
-  return (group + 2) * hd + kAttnSplit * (hd + 4) + kAttnSplit * hd + group * kAttnSplit + 2 * group +
-         2 * kAttnSplit + hd;
+  return (group + 2) * hd + kAttnSplit * (hd + 4) + kAttnSplit * hd + 2 * kAttnSplit + hd;
 }
 
 template <int HD>
 struct AttnSmem {
   static constexpr int KS = HD + 4;  // padded K rows: conflict-free float4 score loads
-  float *q_rot, *k_new, *v_new, *ks, *vs, *probs, *stats, *wm, *maskv, *cs, *sn;
+  float *q_rot, *k_new, *v_new, *ks, *vs, *wm, *maskv, *cs, *sn;
   __device__ AttnSmem(float* smem, int group) {
     q_rot = smem;                        // [group][HD]
     k_new = q_rot + group * HD;          // [HD]
     v_new = k_new + HD;                  // [HD]
     ks = v_new + HD;                     // [kAttnSplit][KS]
     vs = ks + kAttnSplit * KS;           // [kAttnSplit][HD]
-    probs = vs + kAttnSplit * HD;        // [group][kAttnSplit]
-    stats = probs + group * kAttnSplit;  // [group][2]: max, sum
-    wm = stats + 2 * group;              // [kAttnSplit]
+    wm = vs + kAttnSplit * HD;           // [kAttnSplit]
     maskv = wm + kAttnSplit;             // [kAttnSplit]
     cs = maskv + kAttnSplit;             // [HD / 2]: the position's RoPE cosines
     sn = cs + HD / 2;                    // [HD / 2]: sines
@@ -89,6 +86,86 @@ __device__ void attention_stage_cache(const cb_decode_attention_args& a, int g, 
     s.cs[j] = a.cos_table[pos * half + j];
     s.sn[j] = a.sin_table[pos * half + j];
   }
+}
+
+// Merged attention output for elements [e0, e0 + n) of one head (n <= 8,
+// inside one head) from the split partials (scratch layout above).  Online
+// over splits: the same value as the in-kernel merge up to the last bits.
+// Loads go through L1 (the partials are written once per launch, before the
+// caller's phase): a lane's eight values share sectors the L1 fetches once.
+__device__ __forceinline__ void attention_merge_chunk(const float* parts, long long heads, int hd, int splits,
+                                                      long long e0, int n, float* out) {
+  const long long head = e0 / hd;
+  const int d0 = static_cast<int>(e0 % hd);
+  const long long stride = heads * (hd + 2);
+  const float* base = parts + head * (hd + 2);
+  float m = -INFINITY, lsum = 0.0f, acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll 4
+  for (int sp = 0; sp < splits; ++sp) {
+    const float* part = base + sp * stride;
+    const float ms = __ldca(part), ls = __ldca(part + 1);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = i < n ? __ldca(part + 2 + d0 + i) : 0.0f;
+    if (ms > m) {
+      const float rescale = expf(m - ms);  // 0 on the first split (m = -inf)
+      lsum *= rescale;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] *= rescale;
+      m = ms;
+    }
+    const float scale = expf(ms - m);
+    lsum = fmaf(ls, scale, lsum);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = fmaf(v[i], scale, acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < n) out[i] = __fdiv_rn(acc[i], lsum);
+}
+
+// Merged output for the two elements [e0, e0 + 2) of one head, for up to
+// kMergeRegSplits splits: every split's max, sum and two values are loaded
+// first (one round trip), then merged in split order -- max over the splits,
+// then the rescaled sums -- as two passes over registers.
+constexpr int kMergeRegSplits = 16;
+
+__device__ __forceinline__ void attention_merge_pair_regs(const float* parts, long long heads, int hd, int splits,
+                                                          long long e0, float* out) {
+  const long long head = e0 / hd;
+  const int d0 = static_cast<int>(e0 % hd);
+  const long long stride = heads * (hd + 2);
+  const float* base = parts + head * (hd + 2);
+  float m[kMergeRegSplits], l[kMergeRegSplits], v0[kMergeRegSplits], v1[kMergeRegSplits];
+#pragma unroll
+  for (int sp = 0; sp < kMergeRegSplits; ++sp) {
+    if (sp < splits) {
+      const float* part = base + sp * stride;
+      m[sp] = __ldcg(part);
+      l[sp] = __ldcg(part + 1);
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(part + 2 + d0));
+      v0[sp] = v.x;
+      v1[sp] = v.y;
+    }
+  }
+  float mmax = -INFINITY;
+#pragma unroll
+  for (int sp = 0; sp < kMergeRegSplits; ++sp)
+    if (sp < splits) mmax = fmaxf(mmax, m[sp]);
+  float lsum = 0.0f, a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+  for (int sp = 0; sp < kMergeRegSplits; ++sp) {
+    if (sp < splits) {
+      const float scale = expf(m[sp] - mmax);
+      lsum = fmaf(l[sp], scale, lsum);
+      a0 = fmaf(v0[sp], scale, a0);
+      a1 = fmaf(v1[sp], scale, a1);
+    }
+  }
+  out[0] = __fdiv_rn(a0, lsum);
+  out[1] = __fdiv_rn(a1, lsum);
 }
 
 // Needs attention_stage_cache's shared memory (and an attn_sync after it).
@@ -148,7 +225,9 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
   attn_sync();
   if (stamps != nullptr && tid == 0) stamps[1] = global_ns();
 
-  // scores: warp = query head (looping), lane = position
+  // One warp per query head (looping): scores with lane = position, then
+  // p @ v with lane = two dims, the probabilities moving between them by
+  // shuffle.  Partials (max, sum, unnormalised output) to scratch.
   for (int h = warp; h < group; h += warps) {
     float x = -INFINITY;
     if (lane < n) {
@@ -168,43 +247,34 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
     const float m = warp_max(x);
     const float p = lane < n ? expf(x - m) : 0.0f;
     const float l = warp_sum(p);
-    s.probs[h * kAttnSplit + lane] = p;
-    if (lane == 0) {
-      s.stats[2 * h] = m;
-      s.stats[2 * h + 1] = l;
-    }
-  }
-  attn_sync();
-  if (stamps != nullptr && tid == 0) stamps[2] = global_ns();
-
-  // p @ v: two dims of one head per thread; partials to scratch
-  for (int i = tid; i < group * half; i += kAttnThreads) {
-    const int h = i / half, d = (i % half) * 2;
-    const float* p = s.probs + h * kAttnSplit;
-    float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-    int j = 0;
-    for (; j + 1 < n; j += 2) {
-      const float p0 = p[j], p1 = p[j + 1];
-      const float2 v0 = *reinterpret_cast<const float2*>(s.vs + j * HD + d);
-      const float2 v1 = *reinterpret_cast<const float2*>(s.vs + (j + 1) * HD + d);
-      acc0.x = fmaf(p0, v0.x, acc0.x);
-      acc0.y = fmaf(p0, v0.y, acc0.y);
-      acc1.x = fmaf(p1, v1.x, acc1.x);
-      acc1.y = fmaf(p1, v1.y, acc1.y);
-    }
-    if (j < n) {
-      const float2 v0 = *reinterpret_cast<const float2*>(s.vs + j * HD + d);
-      acc0.x = fmaf(p[j], v0.x, acc0.x);
-      acc0.y = fmaf(p[j], v0.y, acc0.y);
-    }
     float* part = a.scratch + (static_cast<long long>(split) * a.heads + g * group + h) * (HD + 2);
-    *reinterpret_cast<float2*>(part + 2 + d) = make_float2(acc0.x + acc1.x, acc0.y + acc1.y);
-    if (d == 0) {
-      part[0] = s.stats[2 * h];
-      part[1] = s.stats[2 * h + 1];
+#pragma unroll
+    for (int d0 = 0; d0 < HD; d0 += 64) {
+      const int d = d0 + 2 * lane;
+      const bool mine = d < HD;
+      float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
+      for (int j = 0; j < n; j += 2) {  // every lane shuffles; rows j < n only are read
+        const float p0 = __shfl_sync(0xffffffffu, p, j);
+        const float p1 = __shfl_sync(0xffffffffu, p, j + 1);
+        if (mine) {
+          const float2 v0 = *reinterpret_cast<const float2*>(s.vs + j * HD + d);
+          acc0.x = fmaf(p0, v0.x, acc0.x);
+          acc0.y = fmaf(p0, v0.y, acc0.y);
+          if (j + 1 < n) {
+            const float2 v1 = *reinterpret_cast<const float2*>(s.vs + (j + 1) * HD + d);
+            acc1.x = fmaf(p1, v1.x, acc1.x);
+            acc1.y = fmaf(p1, v1.y, acc1.y);
+          }
+        }
+      }
+      if (mine) *reinterpret_cast<float2*>(part + 2 + d) = make_float2(acc0.x + acc1.x, acc0.y + acc1.y);
+    }
+    if (lane == 0) {
+      part[0] = m;
+      part[1] = l;
     }
   }
-  if (stamps != nullptr && tid == 0) stamps[3] = global_ns();
+  if (stamps != nullptr && tid == 0) stamps[2] = stamps[3] = global_ns();
   if (!merge) return;
 
   // merge the splits of this KV group in split order
@@ -217,21 +287,15 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
   attn_sync();
   if (!*s_last) return;
   __threadfence();
-  for (int i = tid; i < group * HD; i += kAttnThreads) {
-    const int h = i / HD, d = i % HD;
-    const long long head = static_cast<long long>(g) * group + h;
-    const float* base = a.scratch + head * (HD + 2);
-    const long long stride = a.heads * (HD + 2);
-    float mmax = -INFINITY;
-    for (int sp = 0; sp < splits; ++sp) mmax = fmaxf(mmax, __ldcg(base + sp * stride));
-    float lsum = 0.0f, acc = 0.0f;
-    for (int sp = 0; sp < splits; ++sp) {
-      const float* part = base + sp * stride;
-      const float scale = expf(__ldcg(part) - mmax);
-      lsum = fmaf(__ldcg(part + 1), scale, lsum);
-      acc = fmaf(__ldcg(part + 2 + d), scale, acc);
-    }
-    a.out[head * HD + d] = __fdiv_rn(acc, lsum);
+  for (int i = tid; i < group * half; i += kAttnThreads) {  // two dims of one head per thread
+    const long long e0 = (static_cast<long long>(g) * group + i / half) * HD + (i % half) * 2;
+    float merged[8];
+    if (splits <= kMergeRegSplits)
+      attention_merge_pair_regs(a.scratch, a.heads, HD, splits, e0, merged);
+    else
+      attention_merge_chunk(a.scratch, a.heads, HD, splits, e0, 2, merged);
+    a.out[e0] = merged[0];
+    a.out[e0 + 1] = merged[1];
   }
   if (tid == 0) a.counters[g] = 0u;
 }
@@ -243,44 +307,6 @@ __device__ void attention_item(const cb_decode_attention_args& a, int g, int spl
   attention_stage_cache<HD>(a, g, split, smem, tid);
   attn_sync();
   attention_finish<HD>(a, g, split, splits, smem, s_last, tid, true);
-}
-
-// Merged attention output for elements [e0, e0 + n) of one head (n <= 8,
-// inside one head) from the split partials (scratch layout above).  Online
-// over splits: the same value as the in-kernel merge up to the last bits.
-// Loads go through L1 (the partials are written once per launch, before the
-// caller's phase): a lane's eight values share sectors the L1 fetches once.
-__device__ __forceinline__ void attention_merge_chunk(const float* parts, long long heads, int hd, int splits,
-                                                      long long e0, int n, float* out) {
-  const long long head = e0 / hd;
-  const int d0 = static_cast<int>(e0 % hd);
-  const long long stride = heads * (hd + 2);
-  const float* base = parts + head * (hd + 2);
-  float m = -INFINITY, lsum = 0.0f, acc[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-#pragma unroll 4
-  for (int sp = 0; sp < splits; ++sp) {
-    const float* part = base + sp * stride;
-    const float ms = __ldca(part), ls = __ldca(part + 1);
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = i < n ? __ldca(part + 2 + d0 + i) : 0.0f;
-    if (ms > m) {
-      const float rescale = expf(m - ms);  // 0 on the first split (m = -inf)
-      lsum *= rescale;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] *= rescale;
-      m = ms;
-    }
-    const float scale = expf(ms - m);
-    lsum = fmaf(ls, scale, lsum);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = fmaf(v[i], scale, acc[i]);
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    if (i < n) out[i] = __fdiv_rn(acc[i], lsum);
 }
 
 }  // namespace cb

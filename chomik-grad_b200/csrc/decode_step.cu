@@ -416,16 +416,16 @@ __device__ void stage_x(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>& p
         }
         part = warp_sum(part);
         if (lane == 0) sh.norm_red[warp] = part;
-        consumers_sync(N);
-        if (tid == 0) {
-          float acc = 0.0f;
-          for (int w = 0; w < kStepConsumers; ++w) acc += sh.norm_red[w];
-          sh.total_sq = acc;
-        }
       }
       consumers_sync(N);
       if (tid == 0) stamp(S, p, kStampFirst);
-      d = norm_finish_d(n, sh.total_sq);
+      if (n.dt_sum != CB_F32) {
+        d = norm_finish_d(n, sh.total_sq);
+      } else {  // every thread adds the warp partials in the same order: no second barrier
+        float acc = 0.0f;
+        for (int w = 0; w < kStepConsumers; ++w) acc += sh.norm_red[w];
+        d = norm_finish_d(n, acc);
+      }
     }
     const void* wbase = a.norm_w;
     bool wvec = P.nw_vec != 0;

@@ -44,11 +44,10 @@ class CudaB200Compiler(Compiler):
         if decode_step is None:  # fused decode steps as one persistent launch (cb_decode_step)
             decode_step = os.environ.get("CUDA_B200_DECODE_STEP", "1") != "0"
         self.decode_step = decode_step
-        # cb_decode_step_prepare flags: attention splits are merged in the O
-        # projection's x staging (measured faster on TinyLlama); set
-        # CUDA_B200_STEP_MERGE=attention to merge them in the attention phase
-        self.step_flags = (0 if os.environ.get("CUDA_B200_STEP_MERGE") == "attention"
-                           else _lib.STEP_MERGE_IN_STAGE)
+        # cb_decode_step_prepare flags: attention splits are merged in the
+        # attention phase (measured faster on TinyLlama); set
+        # CUDA_B200_STEP_MERGE=stage to merge them in the O projection's x staging
+        self.step_flags = _lib.STEP_MERGE_IN_STAGE if os.environ.get("CUDA_B200_STEP_MERGE") == "stage" else 0
         self.use_graphs = use_graphs
         self.pdl = pdl
         self.fuse_decode = fuse_decode
