@@ -48,7 +48,7 @@ METRIC = "decode tokens/sec (bs=1) and % of HBM roofline"
 # DRAM bytes of one gate/up GEMV launch from an ncu capture, per workload
 GATEUP_TRAFFIC = {"tinyllama-bf16-bs1": 56_449_792 + 45_312}
 # DRAM bytes of one cb_decode_step launch from an ncu capture, per workload
-STEP_TRAFFIC: dict = {}
+STEP_TRAFFIC = {"tinyllama-bf16-bs1": 2_091_113_000 + 7_491_584}
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
@@ -347,7 +347,7 @@ def main() -> None:
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": achieved / peak, "traffic": GATEUP_TRAFFIC.get(wl.name),
                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate/up "
-                                      "launch (profiles/gemv_tinyllama_bf16_bs1.txt; cold cache, "
+                                      "launch (profiles/gemv_per_kernel_tinyllama_bf16_bs1.txt; cold cache, "
                                       "includes its L2 prefetch of the next launch's weights)",
                     "kernel": f"cb_gemv silu_mul (gate/up {gemv_bytes / 1e6:.1f} MB per launch, "
                               f"{gemv_layers} layers cycled)", "peak_source": peak_kind}
