@@ -152,6 +152,16 @@ class DecodeAttentionArgs(ctypes.Structure):
     ]
 
 
+class GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("a", c_void_p), ("a_dtype", c_int), ("lda", c_longlong),
+        ("b", c_void_p), ("ldb", c_longlong),
+        ("c", c_void_p), ("ldc", c_longlong),
+        ("m", c_longlong), ("n", c_longlong), ("k", c_longlong),
+        ("a_split", c_void_p), ("error_flag", c_void_p),
+    ]
+
+
 class StepPhase(ctypes.Structure):
     _fields_ = [("kind", c_int), ("x_mode", c_int), ("gemv", GemvArgs), ("attention", DecodeAttentionArgs)]
 
@@ -196,6 +206,8 @@ _SIGNATURES = {
     "cb_decode_attention": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
     "cb_decode_attention_scratch": ([POINTER(DecodeAttentionArgs)], c_longlong),
     "cb_decode_attention_noalloc": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
+    "cb_gemm_tc_scratch": ([POINTER(GemmArgs)], c_longlong),
+    "cb_gemm_tc": ([POINTER(GemmArgs), c_void_p], c_int),
     "cb_decode_step_table_bytes": ([c_int], c_longlong),
     "cb_decode_step_prepare": ([POINTER(StepPhase), c_int, c_void_p, c_longlong, c_int,
                                 POINTER(DecodeStepConfig)], c_int),

@@ -347,6 +347,32 @@ CB_API long long cb_decode_attention_scratch(const cb_decode_attention_args* arg
  * device share the arrays: calls that overlap on the GPU race. */
 CB_API int cb_decode_attention_noalloc(const cb_decode_attention_args* args, cb_stream_t stream);
 
+/* ---- tensor-core GEMM (tcgen05 + TMEM + TMA) -------------------------------
+ * C = A x B^T for the prefill and batched-decode Linear layers: the MATMUL of
+ * `inputs @ weight.T` (chomikgrad/llama.py:275-277, lazy.py:629-630) with the
+ * weight in its (out, in) = (N, K) row-major layout.  B is bf16; A is bf16 or
+ * float32.  The reference multiplies float32 activations by bf16 weights in
+ * float32; here a float32 A is split into two bf16 planes hi = bf16(a),
+ * lo = bf16(a - hi), whose products with bf16 weights are exact in float32,
+ * and both are accumulated in float32 in TMEM (residual about 2^-16 of |a|).
+ * Requirements: k % 64 == 0, n % 128 == 0, b 16-byte aligned with ldb % 8 ==
+ * 0, c 16-byte aligned with ldc % 4 == 0.  `a_split` is scratch of
+ * cb_gemm_tc_scratch bytes (the bf16 planes A is converted into). */
+typedef struct {
+  const void* a; /* m x k, row stride lda (elements) */
+  int a_dtype;   /* CB_BF16 or CB_F32 */
+  long long lda;
+  const void* b; /* n x k bf16, row stride ldb */
+  long long ldb;
+  float* c;      /* m x n float32, row stride ldc */
+  long long ldc;
+  long long m, n, k;
+  void* a_split; /* scratch: the bf16 plane(s) of A */
+  int* error_flag;
+} cb_gemm_args;
+CB_API long long cb_gemm_tc_scratch(const cb_gemm_args* args);
+CB_API int cb_gemm_tc(const cb_gemm_args* args, cb_stream_t stream);
+
 /* ---- whole decode step in one launch --------------------------------------
  * The fused decode step of LlamaDecoderStep (chomikgrad/llama.py:469-543)
  * -- per layer the norm->QKV GEMV, RoPE + cache blend + attention, O GEMV +

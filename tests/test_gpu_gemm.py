@@ -1,0 +1,90 @@
+"""cb_gemm_tc (tcgen05 / TMEM / TMA) against a float64 torch reference.
+
+C = A @ B^T with B a bf16 (n, k) weight.  bf16 A: products are exact and the
+float32 accumulation is the only rounding.  float32 A: split into bf16 hi +
+lo planes, leaving a residual of about 2^-16 of each |a|.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [  # m, n, k: tile tails in m, both tile widths in n, deep and shallow k
+    (128, 256, 64),
+    (100, 128, 128),
+    (300, 512, 2048),
+    (257, 384, 5632),
+    (2048, 2560, 2048),
+]
+
+
+def _run(torch, a, b, out=None):
+    from cuda_b200 import _lib
+
+    m, k = a.shape
+    n = b.shape[0]
+    c = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda") if out is None else out
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    g = _lib.GemmArgs()
+    g.a, g.lda = a.data_ptr(), a.stride(0)
+    g.a_dtype = _lib.F32 if a.dtype == torch.float32 else _lib.BF16
+    g.b, g.ldb = b.data_ptr(), b.stride(0)
+    g.c, g.ldc = c.data_ptr(), c.stride(0)
+    g.m, g.n, g.k = m, n, k
+    scratch = _lib.load().cb_gemm_tc_scratch(ctypes.byref(g))
+    buf = torch.empty(max(scratch, 16), dtype=torch.uint8, device="cuda")
+    g.a_split = buf.data_ptr()
+    g.error_flag = flag.data_ptr()
+    _lib.call("cb_gemm_tc", ctypes.byref(g), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    return c
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("a_dtype", ["bf16", "f32"])
+def test_gemm_tc_matches_float64(m, n, k, a_dtype):
+    torch = pytest.importorskip("torch")
+    gen = torch.Generator().manual_seed(m * 7 + n * 3 + k)
+    a = torch.randn(m, k, generator=gen)
+    b = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16)
+    if a_dtype == "bf16":
+        a = a.to(torch.bfloat16)
+    got = _run(torch, a.cuda(), b.cuda()).cpu().double()
+    ref = a.double() @ b.double().T
+    scale = (a.double().abs() @ b.double().abs().T)  # bound of each dot product's terms
+    err = (got - ref).abs()
+    # float32 accumulation over k terms; plus the hi/lo residual for float32 A
+    bound = scale * (k * 2.0 ** -23 + (2.0 ** -15 if a_dtype == "f32" else 0.0)) + 1e-6
+    assert torch.isfinite(got).all()
+    assert bool((err <= bound).all()), float((err / bound).max())
+
+
+def test_gemm_tc_strided_a_and_c():
+    torch = pytest.importorskip("torch")
+    gen = torch.Generator().manual_seed(5)
+    m, n, k = 200, 256, 256
+    a_full = torch.randn(m, k + 64, generator=gen).cuda()
+    a = a_full[:, 32:32 + k]  # row stride k + 64, not 16-byte aligned start for bf16 TMA
+    b = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+    c_full = torch.zeros(m, n + 128, device="cuda")
+    c = c_full[:, :n]
+    _run(torch, a, b, out=c)
+    ref = a.double().cpu() @ b.double().cpu().T
+    np.testing.assert_allclose(c.cpu().double().numpy(), ref.numpy(), rtol=1e-4, atol=1e-4)
+    assert not c_full[:, n:].any()  # nothing written beyond n
+
+
+def test_gemm_tc_rejects_unsupported_shapes():
+    torch = pytest.importorskip("torch")
+    from cuda_b200 import _lib
+
+    a = torch.zeros(64, 96, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(128, 96, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.KernelError, match="multiple of 64"):
+        _run(torch, a, b)
