@@ -136,6 +136,25 @@ __global__ void copy_strided_kernel(const T* in, T* out, int ndim, CopyShape s, 
   }
 }
 
+__global__ void place_columns_kernel(const void* in, int in_dtype, int ndim, CopyShape s, const int* cols,
+                                     long long n, long long total, void* out, int out_dtype) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / n, j = i - r * n;
+    const int c = cols[j];
+    float v = 0.0f;
+    if (c >= 0) {
+      long long rest = r, off = c * s.strides[ndim - 1];
+      for (int d = ndim - 2; d >= 0; --d) {
+        off += (rest % s.shape[d]) * s.strides[d];
+        rest /= s.shape[d];
+      }
+      v = load_as_f32(in, off, in_dtype);
+    }
+    store_from_f32(out, i, out_dtype, v);
+  }
+}
+
 template <typename T>
 __global__ void gather_kernel(const T* table, long long rows, long long row_units, const void* idx,
                               int idx_dtype, long long n, T* out, int* error_flag) {
@@ -256,6 +275,24 @@ int cb_copy_strided(const void* in, long long in_offset, void* out, int elem_byt
     default: CB_REQUIRE(false, "copy: unsupported element size %d", elem_bytes);
   }
   return check_launch("cb_copy_strided");
+}
+
+int cb_place_columns(const void* in, int in_dtype, int ndim, const long long* shape, const long long* in_strides,
+                     const int* cols, long long n, void* out, int out_dtype, cb_stream_t stream) {
+  CB_REQUIRE(ndim >= 1 && ndim <= CB_MAX_DIMS, "place: bad ndim %d", ndim);
+  CB_REQUIRE(n >= 0, "place: negative width");
+  CopyShape s{};
+  long long rows = 1;
+  for (int d = 0; d < ndim; ++d) {
+    s.shape[d] = shape[d];
+    s.strides[d] = in_strides[d];
+    if (d < ndim - 1) rows *= shape[d];
+  }
+  const long long total = rows * n;
+  if (total == 0) return CB_OK;
+  place_columns_kernel<<<grid_for(total), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      in, in_dtype, ndim, s, cols, n, total, out, out_dtype);
+  return check_launch("cb_place_columns");
 }
 
 int cb_gather(const void* table, long long rows, long long row_bytes, const void* idx, int idx_dtype,

@@ -206,6 +206,10 @@ _SIGNATURES = {
     "cb_decode_attention": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
     "cb_decode_attention_scratch": ([POINTER(DecodeAttentionArgs)], c_longlong),
     "cb_decode_attention_noalloc": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
+    "cb_place_columns": ([c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p, c_int,
+                          c_void_p], c_int),
+    "cb_sdpa_tc_scratch": ([POINTER(SdpaArgs)], c_longlong),
+    "cb_sdpa_tc": ([POINTER(SdpaArgs), c_int, c_void_p, c_void_p, c_void_p], c_int),
     "cb_gemm_tc_scratch": ([POINTER(GemmArgs)], c_longlong),
     "cb_gemm_tc": ([POINTER(GemmArgs), c_void_p], c_int),
     "cb_decode_step_table_bytes": ([c_int], c_longlong),

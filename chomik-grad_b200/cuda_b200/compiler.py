@@ -33,7 +33,8 @@ class CudaB200Compiler(Compiler):
     def __init__(self, device_index: Optional[int] = None, *, use_graphs: Optional[bool] = None,
                  pdl: bool = True, fuse_decode: bool = True, alias_caches: bool = True,
                  max_positions: int = 8192, gemv_grid: Optional[int] = None,
-                 decode_step: Optional[bool] = None) -> None:
+                 decode_step: Optional[bool] = None, gemm_min_rows: Optional[int] = None,
+                 attn_min_rows: Optional[int] = None) -> None:
         import os
 
         self.device = CudaB200Device(device_index)
@@ -44,6 +45,12 @@ class CudaB200Compiler(Compiler):
         if decode_step is None:  # fused decode steps as one persistent launch (cb_decode_step)
             decode_step = os.environ.get("CUDA_B200_DECODE_STEP", "1") != "0"
         self.decode_step = decode_step
+        if gemm_min_rows is None:  # rows from which x @ W.T runs on the tcgen05 GEMM (cb_gemm_tc)
+            gemm_min_rows = int(os.environ.get("CUDA_B200_GEMM_MIN_ROWS", "64"))
+        self.gemm_min_rows = gemm_min_rows
+        if attn_min_rows is None:  # query rows from which attention runs on cb_sdpa_tc
+            attn_min_rows = int(os.environ.get("CUDA_B200_ATTN_MIN_ROWS", "64"))
+        self.attn_min_rows = attn_min_rows
         # cb_decode_step_prepare flags: attention splits are merged in the
         # attention phase (measured faster on TinyLlama); set
         # CUDA_B200_STEP_MERGE=stage to merge them in the O projection's x staging

@@ -723,7 +723,45 @@ class Planner:
                       src=src, how=how, keep=keep, red=list(axes), sequential=sequential)
         self.set_value(node, out)
 
+    def _placement_columns(self, node) -> Optional[np.ndarray]:
+        """Source row of each column when the right operand is a placement matrix.
+
+        The prefill's KV-cache placement (llama.py:243-247, used at 411-418)
+        is a constant 0/1 matrix with one 1 per row and at most one per
+        column; ``x @ P`` then copies columns of x (products by 1, sums with
+        zeros: exact).  Returns int32 sources (-1 = zero column) or None.
+        """
+        p = node.inputs[1]
+        if p.op is not None or p in self.dynamic or len(p.shape) != 2 or len(node.inputs[0].shape) < 1:
+            return None
+        if p.shape[0] * p.shape[1] > (1 << 26) or p.shape[0] >= (1 << 31):
+            return None
+        try:
+            value = np.asarray(p.numpy_value())
+        except Exception:
+            return None
+        ones = value == 1
+        if not np.all(ones | (value == 0)):
+            return None
+        if np.any(ones.sum(axis=1) != 1) or np.any(ones.sum(axis=0) > 1):
+            return None
+        cols = np.full(p.shape[1], -1, dtype=np.int32)
+        rows, where = np.nonzero(ones)
+        cols[where] = rows
+        if not p.cache_native:
+            self.plan.guards.append((p, value.copy()))
+        return cols
+
     def _emit_matmul(self, node) -> None:
+        cols = self._placement_columns(node)
+        if cols is not None:
+            a = self.value(node.inputs[0])
+            out = self.tmp(node.shape, self.rdt(node))
+            self.plan.lowered["place"] = self.plan.lowered.get("place", 0) + 1
+            table = self.aux(cols)
+            self.add_step("place", out, f"place({self._name(a)}, cols={table.name})", src=a, cols=table)
+            self.set_value(node, out)
+            return
         a, b = (self.value(p) for p in node.inputs)
         out = self.tmp(node.shape, self.rdt(node))
         self.add_step("matmul", out, f"matmul({self._name(a)}, {self._name(b)})", a=a, b=b)
@@ -779,13 +817,38 @@ class Planner:
                       sin=sin, n_offsets=n_off, offset=offset, flag=self.error_flag())
         self.set_value(node, out)
 
+    def _causal_mask(self, mask) -> bool:
+        """Whether a constant mask is <= -5000 at every key past the causal diagonal.
+
+        The prefill's causal mask (llama.py:250-258: -1e4 above the diagonal)
+        qualifies; keys j > i + (tk - tq) of query i then add exp(...) == 0
+        exactly, and cb_sdpa_tc skips the key tiles made only of them.
+        """
+        if mask.op is not None or mask in self.dynamic or len(mask.shape) < 2:
+            return False
+        tq, tk = mask.shape[-2:]
+        if int(np.prod(mask.shape)) > (1 << 26) or tk < tq:
+            return False
+        try:
+            value = np.asarray(mask.numpy_value()).astype(np.float32).reshape(-1, tq, tk)
+        except Exception:
+            return False
+        above = np.arange(tk)[None, :] > np.arange(tq)[:, None] + (tk - tq)
+        if not np.all(value[:, above] <= -5000.0):
+            return False
+        if not mask.cache_native:
+            self.plan.guards.append((mask, np.asarray(mask.numpy_value()).copy()))
+        return True
+
     def _emit_sdpa(self, node, low) -> None:
         q, k, v, mask = (self.value(p) for p in low[1])
         out = self.tmp(node.shape, F32)
+        causal = self._causal_mask(low[1][3])
         self.plan.lowered["sdpa"] = self.plan.lowered.get("sdpa", 0) + 1
         self.add_step("sdpa", out, f"sdpa({self._name(q)}, {self._name(k)}, {self._name(v)}, "
-                      f"mask={self._name(mask)}, divisor={self._sdpa[node]!r})",
-                      q=q, k=k, v=v, mask=mask, divisor=self._sdpa[node])
+                      f"mask={self._name(mask)}, divisor={self._sdpa[node]!r}"
+                      f"{', causal' if causal else ''})",
+                      q=q, k=k, v=v, mask=mask, divisor=self._sdpa[node], causal=causal)
         self.set_value(node, out)
 
     # ------------------------------------------------------------ source

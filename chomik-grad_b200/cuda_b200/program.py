@@ -35,13 +35,50 @@ import numpy as np
 from . import _lib
 from .device import DeviceArray, torch_dtype
 from .frontend.lazy import CompiledProgram
-from .planner import Buffer, Plan, Step, View, contiguous_strides
+from .planner import Buffer, Plan, Step, View, bf16, contiguous_strides
+
+_BF16 = bf16()
 
 
 def _torch():
     import torch
 
     return torch
+
+
+def gemm_shape(step: Step, min_rows: int) -> Optional[Tuple[int, int, int, int, int]]:
+    """(m, n, k, lda, ldb) when a MATMUL step is ``x @ W.T`` the tensor-core GEMM takes.
+
+    That is llama.py:275-277 (``inputs @ weight.T``): a bf16 weight seen
+    through its transpose (K contiguous), activations whose leading
+    dimensions fold into rows, a fresh float32 output, and at least
+    ``min_rows`` rows (128-row tiles waste the tensor cores on fewer).
+    """
+    av: View = step.args["a"]
+    bv: View = step.args["b"]
+    out = step.out
+    if len(av.shape) < 2 or len(bv.shape) < 2 or bv.dtype != _BF16 or out.dtype != np.float32:
+        return None
+    if av.dtype not in (np.float32, _BF16) or not out.is_contiguous():
+        return None
+    if any(n != 1 for n in bv.shape[:-2]):
+        return None
+    k, n = bv.shape[-2], bv.shape[-1]
+    ldb = bv.strides[-1]
+    if bv.strides[-2] != 1 and k > 1:
+        return None
+    lda = av.strides[-2]
+    if av.strides[-1] != 1 and k > 1:
+        return None
+    rows = av.shape[-2]
+    for d in range(len(av.shape) - 3, -1, -1):  # leading dims must step by whole row blocks
+        if av.shape[d] != 1 and av.strides[d] != rows * lda:
+            return None
+        rows *= av.shape[d]
+    if (rows < min_rows or k % 8 or n % 4 or ldb % 8
+            or tuple(out.shape[-2:]) != (av.shape[-2], n)):
+        return None
+    return rows, n, k, lda, ldb
 
 
 class CudaB200Program(CompiledProgram):
@@ -96,6 +133,11 @@ class CudaB200Program(CompiledProgram):
             self._step_counters = torch.zeros(n, dtype=torch.int32, device=dev)
             self._step_flag = (self._tensors[self.plan.error_flag] if self.plan.error_flag is not None
                                else torch.zeros(1, dtype=torch.int32, device=dev))
+        scratch = max([self._gemm_scratch_bytes(s) for s in self.plan.steps if s.name == "matmul"] +
+                      [self._sdpa_scratch_bytes(s) for s in self.plan.steps if s.name == "sdpa"] + [0])
+        self._gemm_scratch = torch.empty(max(scratch, 16), dtype=torch.uint8, device=dev)
+        self._gemm_flag = (self._tensors[self.plan.error_flag] if self.plan.error_flag is not None
+                           else torch.zeros(1, dtype=torch.int32, device=dev))
         self._built = True
 
     def _rms_table(self, init, stream: int) -> None:
@@ -288,6 +330,8 @@ class CudaB200Program(CompiledProgram):
             flag = self._step_flag
         elif self.plan.error_flag is not None:
             flag = self._tensors[self.plan.error_flag]
+        elif self._built:
+            flag = self._gemm_flag
         else:
             return
         value = int(flag[0].item())
@@ -308,9 +352,10 @@ class CudaB200Program(CompiledProgram):
         if self.step_mode:
             self._launch_step(stream)
             return
+        self._extra_launches = 0  # kernels beyond one per step (the GEMM's plane split)
         for step in self.plan.steps:
             getattr(self, f"_step_{step.name}")(step, stream)
-        self.launches = len(self.plan.steps)
+        self.launches = len(self.plan.steps) + self._extra_launches
 
     def _step_copy(self, step: Step, stream: int) -> None:
         src: View = step.args["src"]
@@ -367,10 +412,33 @@ class CudaB200Program(CompiledProgram):
             a.red_strides[i] = src.strides[d]
         _lib.call("cb_reduce", ctypes.byref(a), stream)
 
+    def _gemm_scratch_bytes(self, step: Step) -> int:
+        shape = gemm_shape(step, self._compiler.gemm_min_rows)
+        if shape is None:
+            return 0
+        m, _, k, _, _ = shape
+        # float32 A: hi and lo planes; bf16 A: one plane, used when its rows are
+        # not 16-byte aligned (known only once the pointer is bound)
+        return (4 if step.args["a"].dtype == np.float32 else 2) * m * k
+
     def _step_matmul(self, step: Step, stream: int) -> None:
         av: View = step.args["a"]
         bv: View = step.args["b"]
         out = step.out
+        shape = gemm_shape(step, self._compiler.gemm_min_rows)
+        if shape is not None:
+            m, n, k, lda, ldb = shape
+            g = _lib.GemmArgs()
+            g.a, g.a_dtype, g.lda = self.ptr(av), _lib.dtype_code(av.dtype), lda
+            g.b, g.ldb = self.ptr(bv), ldb
+            g.c, g.ldc = self.ptr(out), n
+            g.m, g.n, g.k = m, n, k
+            g.a_split = self._gemm_scratch.data_ptr()
+            g.error_flag = self._gemm_flag.data_ptr()
+            if g.b % 16 == 0 and g.c % 16 == 0:
+                _lib.call("cb_gemm_tc", ctypes.byref(g), stream)
+                self._extra_launches += int(av.dtype == np.float32 or g.a % 16 != 0 or lda % 8 != 0)
+                return
         batch = tuple(out.shape[:-2])
         if len(batch) > _lib.MM_MAX_BATCH:
             raise _lib.KernelError("matmul: too many batch dimensions")
@@ -389,6 +457,13 @@ class CudaB200Program(CompiledProgram):
                 j = d - (len(batch) - (len(view.shape) - 2))
                 target[d] = 0 if j < 0 or view.shape[j] == 1 else view.strides[j]
         _lib.call("cb_matmul", ctypes.byref(a), stream)
+
+    def _step_place(self, step: Step, stream: int) -> None:
+        src: View = step.args["src"]
+        cols: Buffer = step.args["cols"]
+        _lib.call("cb_place_columns", self.ptr(src), _lib.dtype_code(src.dtype), len(src.shape),
+                  _lib.ll_array(src.shape), _lib.ll_array(src.strides), self._ptr[cols], cols.size,
+                  self.ptr(step.out), _lib.dtype_code(step.out.dtype), stream)
 
     def _step_gather(self, step: Step, stream: int) -> None:
         table: View = step.args["table"]
@@ -434,6 +509,20 @@ class CudaB200Program(CompiledProgram):
         a.error_flag = self._ptr[step.args["flag"]]
         _lib.call("cb_rope", ctypes.byref(a), stream)
 
+    def _sdpa_tc(self, step: Step) -> bool:
+        """Whether the attention runs on cb_sdpa_tc (tensor cores) rather than cb_sdpa."""
+        q, k = step.args["q"], step.args["k"]
+        return q.shape[-1] in (64, 128) and q.shape[2] >= self._compiler.attn_min_rows and k.shape[2] >= 1
+
+    def _sdpa_scratch_bytes(self, step: Step) -> int:
+        if not self._sdpa_tc(step):
+            return 0
+        q, k = step.args["q"], step.args["k"]
+        batch, heads, tq, hd = q.shape
+        kv, tk = k.shape[1], k.shape[2]
+        pad = lambda t: (t + 127) // 128 * 128  # noqa: E731
+        return 2 * (2 * batch * heads * pad(tq) * hd + 4 * batch * kv * pad(tk) * hd)
+
     def _step_sdpa(self, step: Step, stream: int) -> None:
         q, k, v, mask = (step.args[n] for n in ("q", "k", "v", "mask"))
         a = _lib.SdpaArgs()
@@ -450,6 +539,11 @@ class CudaB200Program(CompiledProgram):
         a.batch, a.heads, a.tq, a.head_size = q.shape
         a.kv_heads, a.tk = k.shape[1], k.shape[2]
         a.divisor = step.args["divisor"]
+        if self._sdpa_tc(step):
+            _lib.call("cb_sdpa_tc", ctypes.byref(a), int(step.args.get("causal", False)),
+                      self._gemm_scratch.data_ptr(), self._gemm_flag.data_ptr(), stream)
+            self._extra_launches += 1  # the plane pre-pass
+            return
         _lib.call("cb_sdpa", ctypes.byref(a), stream)
 
     def _prefetch(self, args, target: Tuple[int, int]) -> None:

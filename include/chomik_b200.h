@@ -134,6 +134,19 @@ CB_API int cb_reduce(const cb_reduce_args* args, cb_stream_t stream);
 CB_API int cb_copy_strided(const void* in, long long in_offset, void* out, int elem_bytes, int ndim,
                     const long long* shape, const long long* in_strides, cb_stream_t stream);
 
+/* ---- MATMUL by a placement matrix ------------------------------------------
+ * out (rows x n, contiguous) where out[r, j] = in[r, cols[j]], or 0 where
+ * cols[j] < 0; `in` is a strided view whose last dimension (the contracted
+ * one) has length shape[ndim-1] and whose leading dimensions give the rows.
+ * This is `x @ P` for a constant 0/1 matrix P with one 1 per row and at most
+ * one per column: the KV-cache placement of the prefill
+ * (chomikgrad/llama.py:243-247, 411-418).  Each output is one input times 1
+ * plus zeros, so the copy is the product exactly; values convert from
+ * in_dtype to out_dtype. */
+CB_API int cb_place_columns(const void* in, int in_dtype, int ndim, const long long* shape,
+                            const long long* in_strides, const int* cols, long long n, void* out, int out_dtype,
+                            cb_stream_t stream);
+
 /* ---- GATHER --------------------------------------------------------------
  * out[i, :] = table[idx[i], :] (rows of row_bytes bytes); negative indices
  * wrap once, out-of-range indices set *error_flag = 1 and write zeros.
@@ -240,6 +253,18 @@ typedef struct {
   float divisor;
 } cb_sdpa_args;
 CB_API int cb_sdpa(const cb_sdpa_args* args, cb_stream_t stream);
+
+/* Tensor-core (tcgen05) form of cb_sdpa for prefill and verify blocks: the
+ * same softmax(q k^T / divisor + mask) v (chomikgrad/llama.py:332-369,
+ * tensor.py:325-334) with q, k, v split into bf16 hi/lo planes (three MMA
+ * products per product of the reference, float32 accumulation and softmax).
+ * head_size 64 or 128; out (batch, heads, tq, head_size) contiguous and
+ * 16-byte aligned.  causal != 0 asserts mask <= -5000 at every key
+ * j > i + (tk - tq), whose key tiles are then skipped (their terms are exact
+ * zeros of the float32 softmax).  `scratch`: cb_sdpa_tc_scratch bytes, 16-byte
+ * aligned.  A bounded wait that gives up sets *error_flag (CB_FLAG_WAIT_*). */
+CB_API long long cb_sdpa_tc_scratch(const cb_sdpa_args* args);
+CB_API int cb_sdpa_tc(const cb_sdpa_args* args, int causal, void* scratch, int* error_flag, cb_stream_t stream);
 
 /* ---- decode hot path -----------------------------------------------------*/
 
@@ -355,9 +380,10 @@ CB_API int cb_decode_attention_noalloc(const cb_decode_attention_args* args, cb_
  * float32; here a float32 A is split into two bf16 planes hi = bf16(a),
  * lo = bf16(a - hi), whose products with bf16 weights are exact in float32,
  * and both are accumulated in float32 in TMEM (residual about 2^-16 of |a|).
- * Requirements: k % 64 == 0, n % 128 == 0, b 16-byte aligned with ldb % 8 ==
+ * Requirements: k % 8 == 0, n % 4 == 0, b 16-byte aligned with ldb % 8 ==
  * 0, c 16-byte aligned with ldc % 4 == 0.  `a_split` is scratch of
- * cb_gemm_tc_scratch bytes (the bf16 planes A is converted into). */
+ * cb_gemm_tc_scratch bytes (the bf16 planes A is converted into; none for a
+ * bf16 A with 16-byte aligned rows). */
 typedef struct {
   const void* a; /* m x k, row stride lda (elements) */
   int a_dtype;   /* CB_BF16 or CB_F32 */

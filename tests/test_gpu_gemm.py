@@ -20,6 +20,9 @@ SHAPES = [  # m, n, k: tile tails in m, both tile widths in n, deep and shallow 
     (300, 512, 2048),
     (257, 384, 5632),
     (2048, 2560, 2048),
+    (16, 64, 256),      # tiny: one partial tile in every dimension
+    (77, 688, 688),     # k and n tails (688 = 10.75 x 64)
+    (130, 260, 200),    # k % 64 = 8, n % 128 = 4
 ]
 
 
@@ -84,7 +87,10 @@ def test_gemm_tc_rejects_unsupported_shapes():
     torch = pytest.importorskip("torch")
     from cuda_b200 import _lib
 
-    a = torch.zeros(64, 96, dtype=torch.bfloat16, device="cuda")
-    b = torch.zeros(128, 96, dtype=torch.bfloat16, device="cuda")
-    with pytest.raises(_lib.KernelError, match="multiple of 64"):
+    a = torch.zeros(64, 90, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(128, 90, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.KernelError, match="multiple of 8"):
         _run(torch, a, b)
+    b = torch.zeros(126, 96, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.KernelError, match="multiple of 4"):
+        _run(torch, a[:, :80].contiguous(), b[:, :80].contiguous())

@@ -168,3 +168,20 @@ def test_decode_step_kernel_matches_per_kernel_launches(gpu, name):
     program, _ = next(iter(fused._decoders.values()))
     assert program.step_mode and program.launches == 1
     assert not next(iter(split._decoders.values()))[0].step_mode
+
+
+def test_tiny_bf16_with_every_linear_on_the_tensor_core_gemm(gpu):
+    """The prefill Linears on cb_gemm_tc (no row minimum) keep the golden bars."""
+    from cuda_b200.compiler import CudaB200Compiler
+    from cuda_b200.frontend.lazy import register_compiler
+
+    register_compiler("cuda-b200-gemm", lambda: CudaB200Compiler(gemm_min_rows=1), replace=True)
+    g = golden("tiny_bf16")
+    wl = WORKLOADS["tiny-bf16"]
+    rt = LlamaRuntime(wl.config, synthetic_weights(wl.config, dtype=wl.np_dtype), compiler="cuda-b200-gemm")
+    logits, _ = rt.prefill(list(g["prompt"]), int(g["context"]))
+    program = next(iter(rt._prefill.values()))[0]
+    assert program.launches > len(program.plan.steps)  # the float32 activations were split
+    assert np.max(np.abs(rt.device.to_numpy(logits) - g["prefill_logits"])) <= 2e-2
+    result = rt.generate(list(g["prompt"]), len(g["tokens"]))
+    assert result.tokens == [int(t) for t in g["tokens"]]

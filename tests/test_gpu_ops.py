@@ -133,3 +133,23 @@ def test_llama_lowerings_match_portable_cpu_graph(gpu, oracle, dtype):
     for name in ("rms_norm", "rope", "sdpa", "gather"):
         assert name in program.source
     np.testing.assert_allclose(program()[0], output.numpy(compiler="cpu"), rtol=2e-4, atol=2e-5)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_placement_matmul_is_a_bit_exact_column_copy(gpu, oracle, dtype):
+    """x @ P for a placement P (llama.py:411-418) runs cb_place_columns and equals the cpu matmul."""
+    dt = bf16() if dtype == "bfloat16" else np.dtype(np.float32)
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((1, 3, 6, 5)).astype(dt)
+    cache = np.zeros((6, 9), dt)
+    cache[np.arange(6), np.arange(6)] = 1  # the prefill's cache_placement
+    perm = np.zeros((6, 9), dt)
+    perm[np.arange(6), [4, 0, 8, 2, 1, 6]] = 1
+    for p in (cache, perm):
+        expr = (Tensor(x).permute(0, 1, 3, 2) @ Tensor(p)).permute(0, 1, 3, 2)
+        program = compile_graph(expr, compiler="cuda-b200")
+        assert "place(" in program.source and "matmul(" not in program.source
+        got = np.asarray(program()[0])
+        want = expr.numpy(compiler="cpu")
+        assert got.dtype == want.dtype
+        assert np.array_equal(got.astype(np.float32), want.astype(np.float32))

@@ -107,7 +107,7 @@ def test_prefill_uses_lowerings(tiny_bf16):
     outs = m.prefill(ids, Tensor(L.position_selector(15, 16, dtype=dt), copy=False))
     p = plan(outs, [ids])
     layers = cfg.num_hidden_layers
-    assert p.lowered == {"rms_norm": 2 * layers + 1, "rope": 2 * layers, "sdpa": layers}
+    assert p.lowered == {"rms_norm": 2 * layers + 1, "rope": 2 * layers, "sdpa": layers, "place": 2 * layers}
 
 
 def test_lowering_is_skipped_when_the_portable_graph_differs():
@@ -131,3 +131,60 @@ def test_dynamic_input_must_be_a_leaf_of_the_graph():
     b = Tensor(np.ones(2, np.float32))
     with pytest.raises(ValueError):
         plan([a * 2.0], [b])
+
+
+def test_prefill_linears_take_the_tensor_core_gemm(tiny_bf16):
+    """Every ``x @ W.T`` of a bf16 prefill goes to cb_gemm_tc; nothing else does."""
+    from cuda_b200.program import gemm_shape
+
+    wl, weights = tiny_bf16
+    cfg, dt = wl.config, wl.np_dtype
+    m = L.LlamaForCausalLM(cfg, weights, sequence_length=16, dtype=dt, cache_length=48)
+    ids = Tensor(synthetic_prompt(cfg, 16), copy=False)
+    outs = m.prefill(ids, Tensor(L.position_selector(15, 16, dtype=dt), copy=False))
+    p = plan(outs, [ids])
+    matmuls = [s for s in p.steps if s.name == "matmul"]
+    picked = [gemm_shape(s, 1) for s in matmuls]
+    h, kv, inter = cfg.hidden_size, cfg.num_key_value_heads * cfg.head_size, cfg.intermediate_size
+    per_layer = [(16, h, h, h, h), (16, kv, h, h, h), (16, kv, h, h, h), (16, h, h, h, h),
+                 (16, inter, h, h, h), (16, inter, h, h, h), (16, h, inter, inter, inter)]
+    assert [x for x in picked if x is not None] == per_layer * cfg.num_hidden_layers
+    assert picked.count(None) == 1  # the row selector (float32 right operand)
+    assert all(gemm_shape(s, 64) is None for s in matmuls)  # 16 rows: below the default
+
+
+def test_cache_placement_is_lowered_to_a_column_copy(tiny_bf16):
+    """x @ cache_placement (llama.py:411-418) becomes cb_place_columns with the right sources."""
+    wl, weights = tiny_bf16
+    cfg, dt = wl.config, wl.np_dtype
+    m = L.LlamaForCausalLM(cfg, weights, sequence_length=16, dtype=dt, cache_length=48)
+    ids = Tensor(synthetic_prompt(cfg, 16), copy=False)
+    outs = m.prefill(ids, Tensor(L.position_selector(15, 16, dtype=dt), copy=False))
+    p = plan(outs, [ids])
+    places = [s for s in p.steps if s.name == "place"]
+    assert len(places) == 2 * cfg.num_hidden_layers
+    cols = places[0].args["cols"].host
+    assert cols.dtype == np.int32 and list(cols) == list(range(16)) + [-1] * 32
+    src = places[0].args["src"]
+    assert src.shape == (1, cfg.num_key_value_heads, cfg.head_size, 16)
+    assert places[0].out.shape == (1, cfg.num_key_value_heads, cfg.head_size, 48)
+
+
+def test_placement_match_rejects_other_matrices():
+    """Only 0/1 matrices with one 1 per row and at most one per column are copies."""
+    from cuda_b200.planner import Planner
+
+    x = Tensor(np.ones((2, 3), np.float32))
+    cases = {
+        "two ones in a row": np.array([[1, 1], [0, 0], [0, 0]], np.float32),
+        "shared column": np.array([[1, 0], [1, 0], [0, 1]], np.float32),
+        "not 0/1": np.array([[2, 0], [0, 1], [0, 0]], np.float32),
+        "empty row": np.array([[1, 0], [0, 1], [0, 0]], np.float32),
+    }
+    for name, value in cases.items():
+        p = plan([x @ Tensor(value)])
+        assert [s.name for s in p.steps] == ["matmul"], name
+    perm = np.array([[0, 1, 0, 0], [0, 0, 0, 1], [1, 0, 0, 0]], np.float32)
+    p = plan([x @ Tensor(perm)])
+    assert [s.name for s in p.steps] == ["place"]
+    assert list(p.steps[0].args["cols"].host) == [2, 0, -1, 1]
