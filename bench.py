@@ -17,9 +17,13 @@ Reported:
   e2e        the reference's own loop through the public API: per step build
              the host inputs, device.array(...) them, program.run(bindings),
              device.argmax(logits) -- host<->device copies inside the timing.
-  roofline   the fused gate/up GEMV (largest weight stream) timed alone over
-             all layers' weights (> L2), vs the measured HBM copy bandwidth;
-             step_roofline: weight+KV bytes per token x tokens/s vs the same.
+  roofline   the whole decode step is one persistent kernel (cb_decode_step):
+             weight + KV + embedding bytes per launch over its CUDA-event
+             time, vs the measured HBM copy bandwidth; step_roofline: the
+             same bytes per token x tokens/s.
+  prefill    the prefill-heavy config on the same weights: 8 prompts of 2048
+             tokens per step (tcgen05 GEMMs and flash attention), tokens/s
+             and FLOP/s against the measured bf16 tensor peak.
   cpu_baseline  the parity oracle (restated reference cpu compiler, NumPy +
              ml_dtypes) timing real decode steps of the same model on the host.
 Inputs are larger than L2 (2.07 GB of weights per step), so no flush is needed.
@@ -44,7 +48,7 @@ for _p in (ROOT / "chomik-grad_b200", ROOT):
 
 import numpy as np  # noqa: E402
 
-METRIC = "decode tokens/sec (bs=1) and % of HBM roofline"
+METRIC = "decode tokens/sec (bs=1; bs=32 in the bs32 object) and % of HBM roofline"
 # DRAM bytes of one gate/up GEMV launch from an ncu capture, per workload
 GATEUP_TRAFFIC = {"tinyllama-bf16-bs1": 56_449_792 + 45_312}
 # DRAM bytes of one cb_decode_step launch from an ncu capture, per workload
@@ -244,6 +248,177 @@ def gemv_roofline(program, rounds: int = 20):
     return nbytes, per_launch_ms, len(steps)
 
 
+def prefill_flops(cfg, tokens: int) -> float:
+    """FLOPs of one prompt: 2 x non-embedding, non-lm_head parameters x tokens,
+    causal attention L x 2 x T^2 x H, and the lm_head row (2 x V x H)."""
+    h, kv = cfg.hidden_size, cfg.num_key_value_heads * cfg.head_size
+    body = cfg.num_hidden_layers * (h * (h + 2 * kv) + h * h + 3 * h * cfg.intermediate_size)
+    return (2.0 * body * tokens + cfg.num_hidden_layers * 2.0 * tokens * tokens * h
+            + 2.0 * cfg.vocab_size * h)
+
+
+def prefill_measurement(rt, cfg, rank: int, world: int, steps: int, warmup: int) -> dict:
+    """Prefill-heavy config: 8 prompts of 2048 tokens per step, one greedy token each.
+
+    Each prompt is one run of the compiled prefill program (the reference's
+    LlamaForCausalLM.prefill is batch 1); the output token is the argmax of its
+    logits.  Timed with CUDA events on the launching stream, max over ranks.
+    """
+    import torch
+
+    from cuda_b200.models import WORKLOADS, synthetic_prompt
+
+    wl = WORKLOADS["tinyllama-bf16-prefill-bs8"]
+    prompts = [list(p) for p in synthetic_prompt(cfg, wl.prompt_tokens, seed=100 + rank, batch=wl.batch)]
+    context = wl.prompt_tokens
+
+    def one_step():
+        return [rt.prefill(p, context)[0] for p in prompts]
+
+    for _ in range(max(warmup, 1)):
+        one_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        logits = one_step()
+    t1.record()
+    t1.synchronize()
+    ms = reduce_max(t0.elapsed_time(t1), world)
+    tokens = wl.batch * wl.prompt_tokens * steps * world
+    first_tokens = [rt.device.argmax(x) for x in logits]
+    flops = prefill_flops(cfg, wl.prompt_tokens) * wl.batch * steps * world
+    peak = json.loads(PEAKS.read_text())["bf16_tflops"] if PEAKS.exists() else 1590.0
+    achieved = flops / (ms / 1000.0) / 1e12
+    program = rt._prefill[(wl.prompt_tokens, context)][0]
+    return {"workload": wl.name, "value": tokens / (ms / 1000.0), "unit": "tokens/s",
+            "ms_per_step": ms / steps, "steps": steps, "sequences_per_step": wl.batch * world,
+            "first_tokens": first_tokens,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "flops_per_sequence": prefill_flops(cfg, wl.prompt_tokens),
+                         "peak_source": "measured" if PEAKS.exists() else "fallback"},
+            "gpu_launches": program.launches * wl.batch * steps}
+
+
+def rows_roofline(rt, rows: int, rounds: int = 3):
+    """The gate/up cb_gemm_rows launch (largest weight stream of a batched step) timed
+    alone with CUDA events, cycling every layer's weights (> L2): algorithmic bytes
+    (both weights + x + out) per launch over the mean launch time."""
+    import ctypes
+
+    import torch
+
+    from cuda_b200 import _lib
+
+    cfg = rt.config
+    dev = rt.device.torch_device
+    x = torch.randn(rows, cfg.hidden_size, device=dev)
+    outs = [torch.empty(rows, cfg.intermediate_size, device=dev) for _ in range(2)]
+    lib = _lib.load()
+    args = []
+    for layer in range(cfg.num_hidden_layers):
+        g = _lib.GemmRowsArgs()
+        g.x, g.x_dtype, g.ldx, g.rows, g.k, g.n_w = x.data_ptr(), _lib.F32, cfg.hidden_size, rows, cfg.hidden_size, 2
+        for i, name in enumerate(("gate_proj", "up_proj")):
+            w = rt.weights[f"model.layers.{layer}.mlp.{name}.weight"]
+            g.w[i] = rt.device.array(w._node.native_values[rt.device.name]).data_ptr()
+            g.w_rows[i], g.out[i], g.ldo[i] = cfg.intermediate_size, outs[i].data_ptr(), cfg.intermediate_size
+        args.append(g)
+    scratch = torch.empty(lib.cb_gemm_rows_scratch(ctypes.byref(args[0])), dtype=torch.uint8, device=dev)
+    counters = torch.zeros(lib.cb_gemm_rows_counters(ctypes.byref(args[0])), dtype=torch.int32, device=dev)
+    for g in args:
+        g.scratch, g.counters = scratch.data_ptr(), counters.data_ptr()
+    stream = rt.device.stream()
+    for g in args:
+        _lib.call("cb_gemm_rows", ctypes.byref(g), stream)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(rounds):
+        for g in args:
+            _lib.call("cb_gemm_rows", ctypes.byref(g), stream)
+    t1.record()
+    t1.synchronize()
+    ms = t0.elapsed_time(t1) / (rounds * len(args))
+    nbytes = 2 * cfg.intermediate_size * cfg.hidden_size * 2 + rows * cfg.hidden_size * 4 \
+        + 2 * rows * cfg.intermediate_size * 4
+    return nbytes, ms
+
+
+def batched_measurement(cfg, weights, rank: int, world: int, steps: int, warmup: int) -> dict:
+    """Batched decode: 32 sequences of 512-token prompts stepped together (one
+    BatchedDecoderStep program), each step one token of every sequence."""
+    import torch
+
+    from cuda_b200.batched import BatchedRuntime
+    from cuda_b200.models import WORKLOADS, synthetic_prompt
+
+    wl = WORKLOADS["tinyllama-bf16-bs32"]
+    rt = BatchedRuntime(cfg, weights, batch=wl.batch, compiler="cuda-b200")
+    prompts = [list(p) for p in synthetic_prompt(cfg, wl.prompt_tokens, seed=200 + rank, batch=wl.batch)]
+    context = wl.context
+    start = wl.prompt_tokens
+    tokens, caches = rt.prefill_batch(prompts, context)
+    per_chunk = context - start - 2
+    rt.decode_batch_on_device(tokens, start, context, caches, min(max(warmup, 3), per_chunk))
+    barrier(world)
+    replay_ms: list = []
+    elapsed, done = 0.0, 0
+    while done < steps:
+        n = min(per_chunk, steps - done)
+        _, ms = rt.decode_batch_on_device(tokens, start, context, caches, n + 1, replay_times=replay_ms)
+        elapsed += ms
+        done += n
+    slowest = reduce_max(elapsed, world)
+    value = steps * wl.batch * world / (slowest / 1000.0)
+
+    # e2e: host loop through the public API (inputs uploaded, argmax read back every step)
+    def host_steps(n: int):
+        nonlocal caches
+        toks, position = list(tokens), start
+        for _ in range(n):
+            logits, caches = rt.decode_batch(toks, position, context, caches)
+            toks = [int(t) for t in rt.device.argmax_last_axis(logits)]
+            position += 1
+    e2e_steps = min(steps, per_chunk)
+    host_steps(2)
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    host_steps(e2e_steps)
+    t1.record()
+    t1.synchronize()
+    e2e_ms = reduce_max(t0.elapsed_time(t1), world)
+    host = rt.batched_step_inputs(tokens, start, context)
+    program = next(iter(rt._batched.values()))[0]
+
+    peak, peak_kind = measured_peaks()
+    kv_read = wl.batch * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * 4 * context
+    step_bytes = weight_bytes(cfg, 2) + wl.batch * cfg.hidden_size * 2 + kv_read
+    step_ms = statistics.fmean(replay_ms)
+    rbytes, rms = rows_roofline(rt, wl.batch)
+    return {
+        "workload": wl.name, "value": value, "unit": "tokens/s", "sequences": wl.batch * world,
+        "steps": steps, "ms_per_step": slowest / steps,
+        "e2e": {"value": e2e_steps * wl.batch * world / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(sum(a.nbytes for a in host)), "d2h_bytes_per_step": 8 * wl.batch},
+        "roofline": {"bound": "hbm", "achieved": rbytes / (rms / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": rbytes / (rms / 1000.0) / 1e9 / peak, "traffic": None,
+                     "kernel": f"cb_gemm_rows gate/up ({rbytes / 1e6:.1f} MB per launch, "
+                               f"{cfg.num_hidden_layers} layers cycled)", "kernel_ms": rms,
+                     "peak_source": peak_kind},
+        "step_roofline": {"bytes_per_step": step_bytes, "achieved": step_bytes / (step_ms / 1000.0) / 1e9,
+                          "peak": peak, "unit": "GB/s",
+                          "frac": step_bytes / (step_ms / 1000.0) / 1e9 / peak,
+                          "basis": "bf16 weights + float32 K/V over the whole context (the attention reads "
+                                   "every cache row) per step of 32 tokens"},
+        "gpu_launches": (program.launches + 2) * steps,
+    }
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -252,6 +427,10 @@ def main() -> None:
     parser.add_argument("--impl", default="b200", choices=("b200", "reference"))
     parser.add_argument("--workload", default="tinyllama-bf16-bs1")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--bs32-steps", type=int, default=100,
+                        help="batched decode steps (32 sequences each) of the bs32 measurement; 0 skips it")
+    parser.add_argument("--prefill-steps", type=int, default=2,
+                        help="steps (8 prompts of 2048 tokens each) of the prefill measurement; 0 skips it")
     args = parser.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -370,6 +549,10 @@ def main() -> None:
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
+    if args.bs32_steps > 0 and WORKLOADS["tinyllama-bf16-bs32"].config == cfg:
+        line["bs32"] = batched_measurement(cfg, weights, rank, world, args.bs32_steps, args.warmup)
+    if args.prefill_steps > 0 and WORKLOADS["tinyllama-bf16-prefill-bs8"].config == cfg:
+        line["prefill"] = prefill_measurement(rt, cfg, rank, world, args.prefill_steps, 1)
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, weights).items()
                                 if k in ("value", "unit", "cores", "kind", "sample")}

@@ -14,11 +14,15 @@
 //    online softmax in float32, write p as bf16 hi/lo planes into shared
 //    memory (swizzled like a TMA tile) and fold each O_tile into a float32
 //    accumulator in registers;
-//  * with `causal`, key tiles that lie entirely above the diagonal are
+//  * with CB_CAUSAL_SKIP, key tiles that lie entirely above the diagonal are
 //    skipped; the caller asserts the mask there is <= -5000, where
-//    exp(score - row max) is exactly 0 in float32 for any row whose scores
-//    span less than ~4900, so the skipped terms are the zeros the full
-//    softmax would add.
+//    exp(score - row max) underflows to 0 in float32 for any row whose
+//    scores span less than ~4900, so the skipped terms are the zeros the
+//    full softmax would add; with CB_CAUSAL_ZERO_BELOW as well, the mask is
+//    exactly 0 at and below the diagonal and is read only on the diagonal
+//    tiles (adding 0 changes nothing).
+// Exponentials use the __expf intrinsic (a few ulp): p only enters the MMAs
+// through its bf16 hi/lo planes.
 // The three-product split keeps every product to about 2^-16 of |q||k| (and
 // |p||v|); accumulation is float32.
 //
@@ -63,6 +67,7 @@ struct AttnTcParams {
   float divisor, inv_divisor;
   int div_pow2;       // divisor is a power of two: x * inv_divisor == x / divisor exactly
   int causal_offset;  // key tiles past query + causal_offset are skipped
+  int zero_below;     // the mask is exactly 0 at keys <= query + causal_offset: not read there
   int* error_flag;
 };
 
@@ -155,9 +160,9 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         }
       }
       // drain: every copy issued lands before the block can exit
-      bool drained = mbar_wait(&q_full, 0u);
+      bool drained = wait_short(&q_full, 0u);
       for (int t = j - 1; drained && t >= 0 && t >= j - 2; --t)
-        drained = mbar_wait(kv_full + (t & 1), static_cast<uint32_t>((t >> 1) & 1));
+        drained = wait_short(kv_full + (t & 1), static_cast<uint32_t>((t >> 1) & 1));
       if (!drained) flag_error(p.error_flag, CB_FLAG_WAIT_DRAIN);
     }
   } else if (warp == 1) {
@@ -234,10 +239,11 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
     const uint32_t lanes = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const long long mrow = p.mask_offset + b * p.mask_strides[0] + h * p.mask_strides[1] +
                            static_cast<long long>(min(qi, p.tq - 1)) * p.mask_strides[2];
+    bool use_mask = true;  // per key tile: false where the mask is known to be 0
     auto score = [&](float raw, int key) -> float {
       if (key >= p.tk) return -INFINITY;
       float x = p.div_pow2 ? raw * p.inv_divisor : __fdiv_rn(raw, p.divisor);
-      if (p.mask != nullptr) x = __fadd_rn(x, load_as_f32(p.mask, mrow + key * p.mask_strides[3], p.mask_dtype));
+      if (use_mask) x = __fadd_rn(x, load_as_f32(p.mask, mrow + key * p.mask_strides[3], p.mask_dtype));
       return x;
     };
     float o[HD];
@@ -254,6 +260,8 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
       fence_after();
       const uint32_t sb = lanes + static_cast<uint32_t>((j & 1) * kBK);
       const int key0 = j * kBK;
+      use_mask = p.mask != nullptr &&
+                 !(p.zero_below && static_cast<long long>(key0) + kBK - 1 <= static_cast<long long>(q0) + p.causal_offset);
       float tmax = -INFINITY;
 #pragma unroll 1
       for (int c0 = 0; c0 < kBK; c0 += 16) {
@@ -263,7 +271,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         for (int e = 0; e < 16; ++e) tmax = fmaxf(tmax, score(v[e], key0 + c0 + e));
       }
       const float m_new = fmaxf(m, tmax);
-      const float alpha = expf(m - m_new);
+      const float alpha = __expf(m - m_new);
       if (j > 0) {  // fold O_tile of the previous key tile (p of that tile, max m)
         if (!__all_sync(0xffffffffu, wait_or_abort(&o_full, static_cast<uint32_t>((j - 1) & 1), abort))) {
           ok = false;
@@ -287,7 +295,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         tmem_load16(sb + c0, v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          v[e] = expf(score(v[e], key0 + c0 + e) - m_new);
+          v[e] = __expf(score(v[e], key0 + c0 + e) - m_new);
           lsum += v[e];
         }
 #pragma unroll
@@ -341,7 +349,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
   __syncthreads();
   if (warp == 0) {
     // TMEM is freed only after the MMAs that write it have completed
-    if (!mbar_wait(&mma_done, 0u) && lane == 0) flag_error(p.error_flag, CB_FLAG_WAIT_DRAIN);
+    if (!wait_short(&mma_done, 0u) && lane == 0) flag_error(p.error_flag, CB_FLAG_WAIT_DRAIN);
     fence_after();
     tmem_dealloc(tmem, S::kTmemCols);
   }
@@ -447,7 +455,8 @@ int launch_sdpa_tc(const cb_sdpa_args& a, int causal, void* scratch, int* error_
   int exponent = 0;
   p.div_pow2 = std::frexp(a.divisor, &exponent) == 0.5f;
   p.inv_divisor = 1.0f / a.divisor;
-  p.causal_offset = causal ? static_cast<int>(a.tk - a.tq) : static_cast<int>(a.tk);
+  p.causal_offset = (causal & CB_CAUSAL_SKIP) ? static_cast<int>(a.tk - a.tq) : static_cast<int>(a.tk);
+  p.zero_below = (causal & CB_CAUSAL_SKIP) && (causal & CB_CAUSAL_ZERO_BELOW);
   p.error_flag = error_flag;
 
   auto kernel = attn_tc_kernel<HD>;

@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     // drain: the copies of the last round of every stage land before we go on
     for (int t = kb - 1; t >= 0 && t >= kb - G::kStages; --t) {
-      if (!mbar_wait(full + t % G::kStages, static_cast<uint32_t>((t / G::kStages) & 1))) {
+      if (!wait_short(full + t % G::kStages, static_cast<uint32_t>((t / G::kStages) & 1))) {
         if (error_flag != nullptr) atomicCAS(error_flag, 0, CB_FLAG_WAIT_DRAIN);
         break;
       }
@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncwarp();
 
   // ---- epilogue: TMEM -> registers -> global ----
-  bool ok = wait_or_abort(&acc_full, 0u, &abort_flag) || mbar_wait(&acc_full, 0u);
+  bool ok = wait_or_abort(&acc_full, 0u, &abort_flag) || wait_short(&acc_full, 0u);
   ok = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int*>(&abort_flag) == 0);
   fence_after();
   if (ok) {

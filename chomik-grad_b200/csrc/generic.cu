@@ -155,6 +155,25 @@ __global__ void place_columns_kernel(const void* in, int in_dtype, int ndim, Cop
   }
 }
 
+// One block per (batch, head) of the cache; threads scan the write mask and
+// rewrite the rows it selects.
+__global__ void kv_write_kernel(float* cache, long long heads, long long ctx, long long hd, const void* row,
+                                int row_dtype, long long rs_b, long long rs_h, long long rs_d, const void* wm,
+                                int wm_dtype, int one_minus_dtype) {
+  const long long b = blockIdx.x / heads, h = blockIdx.x % heads;
+  float* base = cache + blockIdx.x * ctx * hd;
+  const long long rbase = b * rs_b + h * rs_h;
+  for (long long r = threadIdx.x; r < ctx; r += blockDim.x) {
+    const float w = load_as_f32(wm, r, wm_dtype);
+    if (w == 0.0f) continue;
+    const float keep = round_to(__fsub_rn(1.0f, w), one_minus_dtype);
+    for (long long d = 0; d < hd; ++d) {
+      const float x = load_as_f32(row, rbase + d * rs_d, row_dtype);
+      base[r * hd + d] = __fadd_rn(__fmul_rn(base[r * hd + d], keep), __fmul_rn(x, w));
+    }
+  }
+}
+
 template <typename T>
 __global__ void gather_kernel(const T* table, long long rows, long long row_units, const void* idx,
                               int idx_dtype, long long n, T* out, int* error_flag) {
@@ -293,6 +312,19 @@ int cb_place_columns(const void* in, int in_dtype, int ndim, const long long* sh
   place_columns_kernel<<<grid_for(total), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       in, in_dtype, ndim, s, cols, n, total, out, out_dtype);
   return check_launch("cb_place_columns");
+}
+
+int cb_kv_write(float* cache, long long batch, long long heads, long long ctx, long long head_size,
+                const void* row, int row_dtype, const long long* row_strides, const void* write_mask,
+                int write_mask_dtype, int one_minus_dtype, cb_stream_t stream) {
+  CB_REQUIRE(cache != nullptr && row != nullptr && write_mask != nullptr, "kv_write: null pointer");
+  CB_REQUIRE(batch >= 0 && heads >= 0 && ctx >= 0 && head_size >= 0, "kv_write: negative size");
+  if (batch * heads == 0 || ctx == 0) return CB_OK;
+  CB_REQUIRE(batch * heads < (1LL << 31), "kv_write: too many heads");
+  kv_write_kernel<<<static_cast<unsigned>(batch * heads), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      cache, heads, ctx, head_size, row, row_dtype, row_strides[0], row_strides[1], row_strides[3], write_mask,
+      write_mask_dtype, one_minus_dtype);
+  return check_launch("cb_kv_write");
 }
 
 int cb_gather(const void* table, long long rows, long long row_bytes, const void* idx, int idx_dtype,

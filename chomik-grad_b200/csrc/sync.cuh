@@ -59,6 +59,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait without a suspend-time hint: the thread wakes as soon as the phase
+// completes.  For the short producer/consumer hand-offs of the tcgen05
+// kernels, where a waiter suspended for a long hint would stall the chain.
+__device__ __forceinline__ bool mbar_try_wait_short(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Wait for the phase with the given parity to complete; false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;

@@ -99,12 +99,23 @@ __device__ __forceinline__ void tmem_load16(uint32_t taddr, float* out) {
   for (int i = 0; i < 16; ++i) out[i] = __uint_as_float(v[i]);
 }
 
-// mbarrier wait that also gives up once *abort != 0 (bounded like mbar_wait).
+// mbarrier wait that also gives up once *abort != 0 (bounded like mbar_wait;
+// no suspend hint, so a waiter resumes as soon as the phase completes).
 __device__ inline bool wait_or_abort(uint64_t* bar, uint32_t parity, const volatile int* abort) {
   const uint64_t start = global_ns();
   for (uint32_t i = 0; i < kWaitPolls; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_short(bar, parity)) return true;
     if ((i & 63u) == 63u && (*abort != 0 || global_ns() - start > kWaitNs)) return false;
+  }
+  return false;
+}
+
+// Bounded wait without an abort flag (drains, teardown).
+__device__ inline bool wait_short(uint64_t* bar, uint32_t parity) {
+  const uint64_t start = global_ns();
+  for (uint32_t i = 0; i < kWaitPolls; ++i) {
+    if (mbar_try_wait_short(bar, parity)) return true;
+    if ((i & 255u) == 255u && global_ns() - start > kWaitNs) return false;
   }
   return false;
 }

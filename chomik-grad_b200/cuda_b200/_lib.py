@@ -16,6 +16,7 @@ import numpy as np
 LIBRARY_PATH = Path(__file__).resolve().parent / "libchomik_b200.so"
 
 F32, BF16, F16, I32, I64 = 0, 1, 2, 3, 4
+CAUSAL_SKIP, CAUSAL_ZERO_BELOW = 1, 2  # cb_sdpa_tc causal flags
 MAX_DIMS = 8
 EW_MAX_INPUTS = 8
 EW_MAX_INSTR = 40
@@ -162,6 +163,15 @@ class GemmArgs(ctypes.Structure):
     ]
 
 
+class GemmRowsArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p), ("x_dtype", c_int), ("ldx", c_longlong), ("rows", c_longlong), ("k", c_longlong),
+        ("n_w", c_int), ("w", c_void_p * 3), ("w_rows", c_longlong * 3),
+        ("out", c_void_p * 3), ("ldo", c_longlong * 3), ("splits", c_int),
+        ("scratch", c_void_p), ("counters", c_void_p), ("error_flag", c_void_p),
+    ]
+
+
 class StepPhase(ctypes.Structure):
     _fields_ = [("kind", c_int), ("x_mode", c_int), ("gemv", GemvArgs), ("attention", DecodeAttentionArgs)]
 
@@ -210,6 +220,11 @@ _SIGNATURES = {
                           c_void_p], c_int),
     "cb_sdpa_tc_scratch": ([POINTER(SdpaArgs)], c_longlong),
     "cb_sdpa_tc": ([POINTER(SdpaArgs), c_int, c_void_p, c_void_p, c_void_p], c_int),
+    "cb_kv_write": ([c_void_p, c_longlong, c_longlong, c_longlong, c_longlong, c_void_p, c_int,
+                     POINTER(c_longlong), c_void_p, c_int, c_int, c_void_p], c_int),
+    "cb_gemm_rows_scratch": ([POINTER(GemmRowsArgs)], c_longlong),
+    "cb_gemm_rows_counters": ([POINTER(GemmRowsArgs)], c_longlong),
+    "cb_gemm_rows": ([POINTER(GemmRowsArgs), c_void_p], c_int),
     "cb_gemm_tc_scratch": ([POINTER(GemmArgs)], c_longlong),
     "cb_gemm_tc": ([POINTER(GemmArgs), c_void_p], c_int),
     "cb_decode_step_table_bytes": ([c_int], c_longlong),
@@ -219,6 +234,8 @@ _SIGNATURES = {
     "cb_argmax_rows": ([c_void_p, c_int, c_longlong, c_longlong, c_void_p, c_void_p], c_int),
     "cb_decode_advance": ([c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
                            c_int, c_longlong, c_void_p, c_longlong, c_void_p, c_void_p], c_int),
+    "cb_decode_advance_rows": ([c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
+                                c_void_p, c_int, c_longlong, c_void_p, c_longlong, c_void_p, c_void_p], c_int),
 }
 
 EXPORTED = tuple(_SIGNATURES)

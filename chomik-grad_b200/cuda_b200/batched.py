@@ -1,0 +1,215 @@
+"""Batched greedy decode of independent sequences (an extension of the plugin).
+
+The reference's ``LlamaDecoderStep`` (chomikgrad/llama.py:436-543) takes one
+token of one sequence.  ``BatchedDecoderStep`` builds the same six-op graph
+for B sequences at once: every tensor gains a leading batch dimension, the
+per-step RoPE rotation and masks are shared (the sequences advance in lock
+step at the same position, as in the batched workloads: equal prompt
+lengths), and each sequence reads and writes its own slice of the
+(B, kv_heads, context, head_size) caches.  Per sequence the graph computes
+exactly what ``LlamaDecoderStep`` computes; only the weight reads are shared,
+which turns each Linear into a B-row matmul (the tcgen05 GEMM).
+
+``BatchedRuntime`` prefills each sequence with the ordinary batch-1 prefill
+program (llama.py:432-433 is batch 1), stacks the caches, and then steps all
+sequences together, picking each next token by ``argmax_last_axis``
+(chomikgrad/lazy.py:132-134; the reference's greedy sampler takes the first
+maximum, generate_tinyllama.py:146-157).
+"""
+
+from __future__ import annotations
+
+from typing import Any, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from .device import DeviceArray
+from .frontend.llama import LlamaConfig, LlamaDecoderStep, decode_masks, rope_rotations
+from .frontend.tensor import Tensor, compile_graph, no_grad
+from .runtime import LlamaRuntime
+
+
+class BatchedDecoderStep(LlamaDecoderStep):
+    """One decode step of B independent sequences sharing the position."""
+
+    def __init__(self, config: LlamaConfig, weights, *, batch: int, cache_length: int,
+                 dtype: np.dtype) -> None:
+        super().__init__(config, weights, cache_length=cache_length, dtype=dtype)
+        if batch <= 0:
+            raise ValueError("batch must be positive")
+        self.batch = batch
+
+    def __call__(self, token_matrix: Tensor, rotation: Tensor, attention_mask: Tensor,
+                 write_mask: Tensor, caches: Sequence[Tuple[Tensor, Tensor]], *,
+                 position: Optional[Tensor] = None) -> Tuple[Tensor, ...]:
+        c, ctx, b = self.config, self.cache_length, self.batch
+        if token_matrix.shape != (b, 1):
+            raise ValueError(f"batched decode takes ({b}, 1) token ids")
+        if rotation.shape != (1, 1, 1, c.head_size, c.head_size):
+            raise ValueError("decode RoPE rotation has the wrong shape")
+        if attention_mask.shape != (1, 1, 1, ctx) or write_mask.shape != (1, 1, ctx, 1):
+            raise ValueError("decode masks have the wrong shape")
+        if len(caches) != c.num_hidden_layers:
+            raise ValueError("decode requires one KV cache pair per layer")
+        if position is not None and position.shape != ():
+            raise ValueError("decode position must be a scalar")
+
+        hidden = self._embed(token_matrix)  # (B, 1, H)
+        updated = []
+        cache_shape = (b, c.num_key_value_heads, ctx, c.head_size)
+        for layer, (old_key, old_value) in enumerate(caches):
+            if old_key.shape != cache_shape or old_value.shape != cache_shape:
+                raise ValueError("KV cache has the wrong shape")
+            p = f"model.layers.{layer}"
+            a = f"{p}.self_attn"
+            normed = self._rms_norm(hidden, self._w(f"{p}.input_layernorm.weight"))
+            query = self._linear(normed, self._w(f"{a}.q_proj.weight")).reshape(
+                b, c.num_attention_heads, 1, c.head_size)
+            key = self._linear(normed, self._w(f"{a}.k_proj.weight")).reshape(
+                b, c.num_key_value_heads, 1, c.head_size)
+            value = self._linear(normed, self._w(f"{a}.v_proj.weight")).reshape(
+                b, c.num_key_value_heads, 1, c.head_size)
+            query = self._apply_rotation(query, rotation, position)
+            key = self._apply_rotation(key, rotation, position)
+            new_key = old_key * (1 - write_mask) + key * write_mask
+            new_value = old_value * (1 - write_mask) + value * write_mask
+            updated.extend((new_key, new_value))
+            attended = self._attend(query, new_key, new_value, attention_mask)
+            merged = attended.permute(0, 2, 1, 3).reshape(b, 1, c.hidden_size)
+            hidden = hidden + self._linear(merged, self._w(f"{a}.o_proj.weight"))
+            normed = self._rms_norm(hidden, self._w(f"{p}.post_attention_layernorm.weight"))
+            hidden = hidden + self._mlp(normed, layer)
+
+        hidden = self._rms_norm(hidden, self._w("model.norm.weight"))
+        logits = self._linear(hidden.reshape(b, c.hidden_size), self._w("lm_head.weight"))
+        return (logits, *updated)
+
+
+class BatchedRuntime(LlamaRuntime):
+    """Prefill B prompts one by one, then decode them together."""
+
+    def __init__(self, config: LlamaConfig, weights, *, batch: int, compiler: str = "cuda-b200",
+                 dtype=None) -> None:
+        super().__init__(config, weights, compiler=compiler, dtype=dtype)
+        self.batch = batch
+        self._batched: dict = {}
+
+    def prefill_batch(self, prompts: Sequence[Sequence[int]], context: int) -> Tuple[List[int], List[Any]]:
+        """First greedy token of each prompt and the stacked (B, ...) caches."""
+        if len(prompts) != self.batch or len({len(p) for p in prompts}) != 1:
+            raise ValueError(f"{self.batch} prompts of equal length are required")
+        import torch
+
+        firsts, per_seq = [], []
+        for prompt in prompts:
+            logits, caches = self.prefill(prompt, context)
+            firsts.append(self.device.argmax(logits))
+            per_seq.append(caches)
+        stacked = []
+        for i in range(len(per_seq[0])):
+            first = per_seq[0][i]
+            flat = torch.cat([seq[i].tensor.reshape(-1) for seq in per_seq])
+            stacked.append(DeviceArray(flat, (self.batch,) + tuple(first.shape[1:]), first.dtype))
+        return firsts, stacked
+
+    def batched_step_inputs(self, tokens: Sequence[int], position: int, context: int) -> List[np.ndarray]:
+        c = self.config
+        ids = np.asarray(tokens, dtype=np.int32).reshape(-1, 1)
+        rotation = rope_rotations(1, c.head_size, c.rope_theta, self.dtype, offset=position)
+        attention, write = decode_masks(position, context, self.dtype)
+        return [ids, rotation, attention, write, np.asarray(position, dtype=np.int32)]
+
+    def batched_program(self, context: int, caches: List[Any], tokens: Sequence[int], position: int):
+        cached = self._batched.get(context)
+        if cached is not None:
+            return cached
+        host = self.batched_step_inputs(tokens, position, context)
+        with no_grad():
+            step = BatchedDecoderStep(self.config, self.weights, batch=self.batch, cache_length=context,
+                                      dtype=self.dtype)
+            tensors = [Tensor(v, copy=False) for v in host]
+            cache_tensors = [Tensor.from_native(v, backend=self.device.name, shape=tuple(v.shape),
+                                                dtype=self.dtype) for v in caches]
+            outputs = step(tensors[0], tensors[1], tensors[2], tensors[3],
+                           list(zip(cache_tensors[::2], cache_tensors[1::2])), position=tensors[4])
+            dynamic = [*tensors, *cache_tensors]
+            program = compile_graph(*outputs, compiler=self.compiler_name, dynamic_inputs=dynamic)
+        entry = (program, [t._node for t in dynamic])
+        self._batched[context] = entry
+        return entry
+
+    def decode_batch(self, tokens: Sequence[int], position: int, context: int,
+                     caches: List[Any]) -> Tuple[Any, List[Any]]:
+        """One step of all sequences: native (B, vocab) logits and the caches."""
+        program, nodes = self.batched_program(context, caches, tokens, position)
+        values = [self.device.array(v) for v in self.batched_step_inputs(tokens, position, context)]
+        produced = program.run(dict(zip(nodes, values + list(caches))), synchronize=False)
+        return produced[0], list(produced[1:])
+
+    def generate_batch(self, prompts: Sequence[Sequence[int]], max_new_tokens: int) -> List[List[int]]:
+        """Greedy tokens of every sequence (first one from its prefill)."""
+        length = len(prompts[0])
+        context = length + max_new_tokens
+        tokens, caches = self.prefill_batch(prompts, context)
+        out = [[t] for t in tokens]
+        for i in range(1, max_new_tokens):
+            logits, caches = self.decode_batch(tokens, length + i - 1, context, caches)
+            tokens = [int(t) for t in self.device.argmax_last_axis(logits)]
+            for seq, t in zip(out, tokens):
+                seq.append(t)
+        return out
+
+    def decode_batch_on_device(self, tokens: Sequence[int], position: int, context: int, caches: List[Any],
+                               steps: int, *, replay_times: Optional[List[float]] = None):
+        """Greedy-decode ``steps`` tokens of every sequence with no host round trip per step.
+
+        Two bound runs (the second captures the graph), then ``steps - 1``
+        graph replays, each preceded by cb_argmax_rows over the previous
+        logits and cb_decode_advance_rows writing the next ids, position and
+        masks on the device.  Returns (tokens per sequence, device ms of the
+        whole loop); ``replay_times`` receives each replay's device ms.
+        """
+        import torch
+
+        from . import _lib
+
+        program, nodes = self.batched_program(context, caches, tokens, position)
+        self.decode_batch(tokens, position, context, caches)
+        self.decode_batch(tokens, position, context, caches)
+        ids, _, mask, write, pos = nodes[:5]
+        dev = self.device.torch_device
+        rows = self.batch
+        log = torch.zeros(max(steps, 1) * rows, dtype=torch.int64, device=dev)
+        argmax = torch.zeros(rows, dtype=torch.int64, device=dev)
+        logits_view = program.plan.outputs[0][1]
+        width = logits_view.shape[-1]
+        stream = self.device.stream()
+        lib = _lib.load()
+        slot, code = program.slot_pointer, _lib.dtype_code
+        advance = (argmax.data_ptr(), rows, slot(ids), code(ids.dtype), slot(pos), code(pos.dtype), slot(mask),
+                   code(program.plan.input_buffers[mask].dtype), slot(write),
+                   code(program.plan.input_buffers[write].dtype), context, log.data_ptr())
+        marks = ([(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(1, steps)] if replay_times is not None else None)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(1, steps):
+            _lib.check(lib.cb_argmax_rows(program.ptr(logits_view), code(logits_view.dtype), rows, width,
+                                          argmax.data_ptr(), stream), "cb_argmax_rows")
+            _lib.check(lib.cb_decode_advance_rows(*advance, i - 1, program.error_pointer(), stream),
+                       "cb_decode_advance_rows")
+            if marks is not None:
+                marks[i - 1][0].record()
+            program.replay(stream)
+            if marks is not None:
+                marks[i - 1][1].record()
+        _lib.check(lib.cb_argmax_rows(program.ptr(logits_view), code(logits_view.dtype), rows, width,
+                                      log[(steps - 1) * rows:].data_ptr(), stream), "cb_argmax_rows")
+        end.record()
+        end.synchronize()
+        program.check_errors()
+        if marks is not None:
+            replay_times.extend(a.elapsed_time(b) for a, b in marks)
+        table = log[:steps * rows].view(steps, rows).t().tolist()
+        return [[int(t) for t in seq] for seq in table], start.elapsed_time(end)

@@ -221,6 +221,20 @@ class Plan:
         return buf
 
 
+def _collect_buffers(value, acc: Set[int]) -> None:
+    """ids of every Buffer a step argument refers to (Views, lists, dicts)."""
+    if isinstance(value, View):
+        acc.add(id(value.buf))
+    elif isinstance(value, Buffer):
+        acc.add(id(value))
+    elif isinstance(value, (list, tuple)):
+        for v in value:
+            _collect_buffers(v, acc)
+    elif isinstance(value, dict):
+        for v in value.values():
+            _collect_buffers(v, acc)
+
+
 class Planner:
     """Builds a :class:`Plan` from output nodes (see module docstring)."""
 
@@ -508,6 +522,8 @@ class Planner:
             from .fusion import DecodeFusion
 
             DecodeFusion(self).apply()
+        if self.alias_caches:
+            self._match_kv_writes()
         self._fuse_elementwise_groups()
         for node in order:
             if node.op is None or node in self._val:
@@ -519,11 +535,86 @@ class Planner:
                 self._emit_generic(node)
         for index, node in enumerate(self.outputs):
             plan.outputs.append((node, self.value(node)))
+        self._drop_dead_steps()
         from .fusion import assign_prefetch
 
         assign_prefetch(plan.steps)
         plan.source = self._source()
         return plan
+
+    def _match_kv_writes(self) -> None:
+        """``cache*(1-wm) + row*wm`` on a dynamic cache (llama.py:511-512) => in-place cb_kv_write.
+
+        For caches of any batch (the batch-1 decode fusion claims its own
+        first): the cache leaf is bound by pointer, updated in place and
+        returned as the same object, like the reference runtime rebinding
+        the returned caches as the next step's inputs.
+        """
+        for node in self.order:
+            if not is_ew(node, "add") or node not in self.output_set or node in self.claimed or node in self.units:
+                continue
+            left, right = node.inputs
+            if not (is_ew(left, "mul") and is_ew(right, "mul")):
+                continue
+            cache, keep = left.inputs
+            row, wm = right.inputs
+            if not is_ew(keep, "sub") or keep.inputs[1] is not wm or self._const(keep.inputs[0]) != 1.0:
+                continue
+            if (cache.op is not None or cache not in self.dynamic or cache in self.output_set
+                    or len(cache.shape) != 4 or self.rdt(cache) != F32):
+                continue
+            b, h, ctx, hd = cache.shape
+            if tuple(row.shape) != (b, h, 1, hd) or tuple(wm.shape) != (1, 1, ctx, 1):
+                continue
+            if self.rdt(wm).name not in FLOATS or any(self.rdt(n) != F32 for n in (left, right, node, row)):
+                continue
+            uses = self.consumers
+            if not (len(uses.get(cache, ())) == 1 and uses.get(left) == [node] and uses.get(right) == [node]
+                    and uses.get(keep) == [left]):
+                continue
+            self.claimed.update((left, right, keep))
+            self.units[node] = self._kv_write_unit(node, cache, row, wm, keep)
+
+    def _kv_write_unit(self, node, cache, row, wm, keep):
+        def emit() -> None:
+            view = self.value(cache)
+            view.buf.bind = "pointer"
+            rv, wv = self.value(row), self.contiguous(self.value(wm))
+            self.add_step("kv_write", view, f"kv_write({self._name(view)}, {self._name(rv)}, "
+                          f"write_mask={self._name(wv)}) (in place)",
+                          cache=view, row=rv, write_mask=wv, one_minus=self.rdt(keep))
+            self.set_value(node, view)
+            for i, o in enumerate(self.outputs):
+                if o is node:
+                    self.plan.aliases[i] = cache
+        return emit
+
+    # steps whose only effect is their output buffer
+    PURE_STEPS = frozenset(("elementwise", "matmul", "reduce", "copy", "rms_norm", "rope", "sdpa", "place"))
+
+    def _drop_dead_steps(self) -> None:
+        """Remove pure steps whose output no later step or program output reads.
+
+        Sub-expressions absorbed into a fused elementwise group can also be
+        emitted on their own (a lowering or a second path referenced them);
+        when nothing reads that copy it is dead work.  Temporary buffers left
+        without a writer are dropped too.
+        """
+        plan = self.plan
+        live = {id(v.buf) for _, v in plan.outputs}
+        live.update(id(b) for b in plan.argmax_of.values())
+        kept: List[Step] = []
+        for step in reversed(plan.steps):
+            if step.name in self.PURE_STEPS and step.out is not None and id(step.out.buf) not in live:
+                continue
+            kept.append(step)
+            _collect_buffers(step.args, live)
+            if step.out is not None:
+                live.add(id(step.out.buf))
+        plan.steps = kept[::-1]
+        for init in plan.init_steps:
+            _collect_buffers(init, live)
+        plan.buffers = [b for b in plan.buffers if b.kind != "tmp" or id(b) in live]
 
     def _pruned_leaves(self) -> Set[object]:
         """Leaves only reachable through portable sub-graphs of used lowerings."""
@@ -817,28 +908,34 @@ class Planner:
                       sin=sin, n_offsets=n_off, offset=offset, flag=self.error_flag())
         self.set_value(node, out)
 
-    def _causal_mask(self, mask) -> bool:
-        """Whether a constant mask is <= -5000 at every key past the causal diagonal.
+    def _causal_mask(self, mask) -> int:
+        """cb_sdpa_tc causal flags a constant mask allows (0 = none).
 
-        The prefill's causal mask (llama.py:250-258: -1e4 above the diagonal)
-        qualifies; keys j > i + (tk - tq) of query i then add exp(...) == 0
-        exactly, and cb_sdpa_tc skips the key tiles made only of them.
+        CB_CAUSAL_SKIP when the mask is <= -5000 at every key past the causal
+        diagonal j > i + (tk - tq): those keys add exp(...) == 0 exactly and
+        key tiles made only of them are skipped.  CB_CAUSAL_ZERO_BELOW as well
+        when it is exactly 0 at every other key (then it is read only on the
+        diagonal tiles).  The prefill's mask (llama.py:250-258: -1e4 above
+        the diagonal, 0 elsewhere) has both.
         """
         if mask.op is not None or mask in self.dynamic or len(mask.shape) < 2:
-            return False
+            return 0
         tq, tk = mask.shape[-2:]
         if int(np.prod(mask.shape)) > (1 << 26) or tk < tq:
-            return False
+            return 0
         try:
             value = np.asarray(mask.numpy_value()).astype(np.float32).reshape(-1, tq, tk)
         except Exception:
-            return False
+            return 0
         above = np.arange(tk)[None, :] > np.arange(tq)[:, None] + (tk - tq)
         if not np.all(value[:, above] <= -5000.0):
-            return False
+            return 0
         if not mask.cache_native:
             self.plan.guards.append((mask, np.asarray(mask.numpy_value()).copy()))
-        return True
+        flags = _lib.CAUSAL_SKIP
+        if np.all(value[:, ~above] == 0.0):
+            flags |= _lib.CAUSAL_ZERO_BELOW
+        return flags
 
     def _emit_sdpa(self, node, low) -> None:
         q, k, v, mask = (self.value(p) for p in low[1])
@@ -847,7 +944,7 @@ class Planner:
         self.plan.lowered["sdpa"] = self.plan.lowered.get("sdpa", 0) + 1
         self.add_step("sdpa", out, f"sdpa({self._name(q)}, {self._name(k)}, {self._name(v)}, "
                       f"mask={self._name(mask)}, divisor={self._sdpa[node]!r}"
-                      f"{', causal' if causal else ''})",
+                      f"{', causal=%d' % causal if causal else ''})",
                       q=q, k=k, v=v, mask=mask, divisor=self._sdpa[node], causal=causal)
         self.set_value(node, out)
 

@@ -133,8 +133,16 @@ class CudaB200Program(CompiledProgram):
             self._step_counters = torch.zeros(n, dtype=torch.int32, device=dev)
             self._step_flag = (self._tensors[self.plan.error_flag] if self.plan.error_flag is not None
                                else torch.zeros(1, dtype=torch.int32, device=dev))
+        self._group_row_matmuls()
+        rows_scratch, n_counters = [0], 0
+        for leader, group in self._rows.items():
+            args = self._rows_args(group, counters=0)
+            rows_scratch.append(int(_lib.load().cb_gemm_rows_scratch(ctypes.byref(args))))
+            self._rows_counter_off[leader] = n_counters
+            n_counters += int(_lib.load().cb_gemm_rows_counters(ctypes.byref(args)))
+        self._rows_counters = torch.zeros(max(n_counters, 1), dtype=torch.int32, device=dev)
         scratch = max([self._gemm_scratch_bytes(s) for s in self.plan.steps if s.name == "matmul"] +
-                      [self._sdpa_scratch_bytes(s) for s in self.plan.steps if s.name == "sdpa"] + [0])
+                      [self._sdpa_scratch_bytes(s) for s in self.plan.steps if s.name == "sdpa"] + rows_scratch)
         self._gemm_scratch = torch.empty(max(scratch, 16), dtype=torch.uint8, device=dev)
         self._gemm_flag = (self._tensors[self.plan.error_flag] if self.plan.error_flag is not None
                            else torch.zeros(1, dtype=torch.int32, device=dev))
@@ -412,6 +420,65 @@ class CudaB200Program(CompiledProgram):
             a.red_strides[i] = src.strides[d]
         _lib.call("cb_reduce", ctypes.byref(a), stream)
 
+    # ---------------------------------------------------- few-row matmuls
+    def _rows_shape(self, step: Step):
+        """(m, n, k, lda) when a MATMUL has too few rows for cb_gemm_tc: cb_gemm_rows takes it."""
+        shape = gemm_shape(step, 1)
+        if shape is None:
+            return None
+        m, n, k, lda, ldb = shape
+        if m >= self._compiler.gemm_min_rows or m > 256 or ldb != k:
+            return None
+        return m, n, k, lda
+
+    def _group_row_matmuls(self) -> None:
+        """Group few-row matmuls that share their x into one cb_gemm_rows launch (up to 3).
+
+        The later members run early, at the first one: their x is the same
+        buffer and their weights are program inputs, and a matmul's output
+        is a fresh buffer nothing reads before the matmul itself.
+        """
+        self._rows: Dict[int, List[Step]] = {}
+        self._rows_skip: set = set()
+        self._rows_counter_off: Dict[int, int] = {}
+        steps = self.plan.steps
+        for i, step in enumerate(steps):
+            if step.name != "matmul" or id(step) in self._rows_skip:
+                continue
+            shape = self._rows_shape(step)
+            if shape is None:
+                continue
+            a: View = step.args["a"]
+            group = [step]
+            for later in steps[i + 1:]:
+                if len(group) == 3:
+                    break
+                if later.name != "matmul" or id(later) in self._rows_skip:
+                    continue
+                other = self._rows_shape(later)
+                la: View = later.args["a"]
+                if (other is not None and other[0] == shape[0] and other[2] == shape[2] and other[3] == shape[3]
+                        and la.buf is a.buf and la.offset == a.offset and la.dtype == a.dtype
+                        and later.args["b"].buf.kind == "input"):
+                    group.append(later)
+            self._rows[id(step)] = group
+            self._rows_skip.update(id(g) for g in group[1:])
+
+    def _rows_args(self, group: List[Step], counters: int) -> _lib.GemmRowsArgs:
+        m, _, k, lda = self._rows_shape(group[0])
+        a: View = group[0].args["a"]
+        g = _lib.GemmRowsArgs()
+        g.x = self.ptr(a) if self._built else 0
+        g.x_dtype, g.ldx, g.rows, g.k, g.n_w = _lib.dtype_code(a.dtype), lda, m, k, len(group)
+        for i, st in enumerate(group):
+            n = st.args["b"].shape[-1]
+            g.w[i] = self.ptr(st.args["b"]) if self._built else 0
+            g.w_rows[i], g.ldo[i] = n, n
+            g.out[i] = self.ptr(st.out) if self._built else 0
+        g.splits = 0
+        g.counters = counters
+        return g
+
     def _gemm_scratch_bytes(self, step: Step) -> int:
         shape = gemm_shape(step, self._compiler.gemm_min_rows)
         if shape is None:
@@ -422,6 +489,17 @@ class CudaB200Program(CompiledProgram):
         return (4 if step.args["a"].dtype == np.float32 else 2) * m * k
 
     def _step_matmul(self, step: Step, stream: int) -> None:
+        if id(step) in self._rows_skip:
+            return  # launched with the first matmul of its cb_gemm_rows group
+        group = self._rows.get(id(step))
+        if group is not None:
+            off = self._rows_counter_off[id(step)]
+            g = self._rows_args(group, self._rows_counters.data_ptr() + 4 * off)
+            g.scratch = self._gemm_scratch.data_ptr()
+            g.error_flag = self._gemm_flag.data_ptr()
+            _lib.call("cb_gemm_rows", ctypes.byref(g), stream)
+            self._extra_launches += 2 - len(group)  # plane pass + GEMM for len(group) steps
+            return
         av: View = step.args["a"]
         bv: View = step.args["b"]
         out = step.out
@@ -457,6 +535,15 @@ class CudaB200Program(CompiledProgram):
                 j = d - (len(batch) - (len(view.shape) - 2))
                 target[d] = 0 if j < 0 or view.shape[j] == 1 else view.strides[j]
         _lib.call("cb_matmul", ctypes.byref(a), stream)
+
+    def _step_kv_write(self, step: Step, stream: int) -> None:
+        cache: View = step.args["cache"]
+        row: View = step.args["row"]
+        wm: View = step.args["write_mask"]
+        b, h, ctx, hd = cache.shape
+        _lib.call("cb_kv_write", self.ptr(cache), b, h, ctx, hd, self.ptr(row), _lib.dtype_code(row.dtype),
+                  _lib.ll_array(row.strides), self.ptr(wm), _lib.dtype_code(wm.dtype),
+                  _lib.dtype_code(step.args["one_minus"]), stream)
 
     def _step_place(self, step: Step, stream: int) -> None:
         src: View = step.args["src"]

@@ -147,6 +147,18 @@ CB_API int cb_place_columns(const void* in, int in_dtype, int ndim, const long l
                             const long long* in_strides, const int* cols, long long n, void* out, int out_dtype,
                             cb_stream_t stream);
 
+/* ---- KV-cache write mask, in place -----------------------------------------
+ * cache (batch, heads, ctx, head_size) float32 contiguous becomes
+ * cache * (1 - wm) + row * wm for the decode write mask wm (ctx values) and
+ * the new rows `row` (batch, heads, 1, head_size; element strides
+ * row_strides[4]): the blend of chomikgrad/llama.py:511-512.  1 - wm is
+ * rounded to one_minus_dtype (the dtype the graph computes it in); products
+ * and sum are float32.  Only rows with wm != 0 are rewritten: at wm == 0 the
+ * blend is cache * 1 + row * 0, the cache itself for finite rows. */
+CB_API int cb_kv_write(float* cache, long long batch, long long heads, long long ctx, long long head_size,
+                       const void* row, int row_dtype, const long long* row_strides, const void* write_mask,
+                       int write_mask_dtype, int one_minus_dtype, cb_stream_t stream);
+
 /* ---- GATHER --------------------------------------------------------------
  * out[i, :] = table[idx[i], :] (rows of row_bytes bytes); negative indices
  * wrap once, out-of-range indices set *error_flag = 1 and write zeros.
@@ -259,10 +271,13 @@ CB_API int cb_sdpa(const cb_sdpa_args* args, cb_stream_t stream);
  * tensor.py:325-334) with q, k, v split into bf16 hi/lo planes (three MMA
  * products per product of the reference, float32 accumulation and softmax).
  * head_size 64 or 128; out (batch, heads, tq, head_size) contiguous and
- * 16-byte aligned.  causal != 0 asserts mask <= -5000 at every key
- * j > i + (tk - tq), whose key tiles are then skipped (their terms are exact
- * zeros of the float32 softmax).  `scratch`: cb_sdpa_tc_scratch bytes, 16-byte
- * aligned.  A bounded wait that gives up sets *error_flag (CB_FLAG_WAIT_*). */
+ * 16-byte aligned.  `causal` flags: CB_CAUSAL_SKIP asserts mask <= -5000 at
+ * every key j > i + (tk - tq), whose key tiles are then skipped (their terms
+ * are exact zeros of the float32 softmax); CB_CAUSAL_ZERO_BELOW (with SKIP)
+ * asserts the mask is exactly 0 at every other key, so it is read only on
+ * diagonal tiles.  `scratch`: cb_sdpa_tc_scratch bytes, 16-byte aligned.  A
+ * bounded wait that gives up sets *error_flag (CB_FLAG_WAIT_*). */
+enum { CB_CAUSAL_SKIP = 1, CB_CAUSAL_ZERO_BELOW = 2 };
 CB_API long long cb_sdpa_tc_scratch(const cb_sdpa_args* args);
 CB_API int cb_sdpa_tc(const cb_sdpa_args* args, int causal, void* scratch, int* error_flag, cb_stream_t stream);
 
@@ -399,6 +414,38 @@ typedef struct {
 CB_API long long cb_gemm_tc_scratch(const cb_gemm_args* args);
 CB_API int cb_gemm_tc(const cb_gemm_args* args, cb_stream_t stream);
 
+/* ---- few-row tensor-core GEMM (batched decode) -----------------------------
+ * out_i (rows x w_rows[i], float32, row stride ldo[i]) = x . W_i^T for up to
+ * three bf16 weights W_i (w_rows[i] x k, row-major, 16-byte aligned) sharing
+ * x (rows x k, float32 or bf16, row stride ldx): the q/k/v or gate/up
+ * Linears of a decode step over a batch of 1..256 sequences
+ * (chomikgrad/llama.py:275-277, 387-392, 371-380).  float32 x is split into
+ * bf16 hi/lo planes (products exact, residual about 2^-16 of |x|); the
+ * weight rows are the MMA's 128-row side and K is split across CTAs (splits
+ * = 0 chooses), reduced in split order by the last CTA of each weight tile.
+ * `scratch`: cb_gemm_rows_scratch bytes, 16-byte aligned; `counters`:
+ * cb_gemm_rows_counters unsigned ints, zero before the first call (calls
+ * leave them zero).  k % 8 == 0. */
+typedef struct {
+  const void* x;
+  int x_dtype;
+  long long ldx;
+  long long rows;
+  long long k;
+  int n_w;
+  const void* w[3];
+  long long w_rows[3];
+  float* out[3];
+  long long ldo[3];
+  int splits;
+  void* scratch;
+  unsigned* counters;
+  int* error_flag;
+} cb_gemm_rows_args;
+CB_API long long cb_gemm_rows_scratch(const cb_gemm_rows_args* args);
+CB_API long long cb_gemm_rows_counters(const cb_gemm_rows_args* args);
+CB_API int cb_gemm_rows(const cb_gemm_rows_args* args, cb_stream_t stream);
+
 /* ---- whole decode step in one launch --------------------------------------
  * The fused decode step of LlamaDecoderStep (chomikgrad/llama.py:469-543)
  * -- per layer the norm->QKV GEMV, RoPE + cache blend + attention, O GEMV +
@@ -477,6 +524,14 @@ CB_API int cb_decode_advance(const long long* argmax, void* ids, int ids_dtype, 
                       int position_dtype, void* mask, int mask_dtype, void* write_mask,
                       int write_mask_dtype, long long context, long long* token_log, long long step,
                       int* error_flag, cb_stream_t stream);
+
+/* The same for `rows` sequences decoded together (one batched program):
+ * ids[b] = argmax[b], token_log[step * rows + b]; position and masks are
+ * shared. */
+CB_API int cb_decode_advance_rows(const long long* argmax, long long rows, void* ids, int ids_dtype,
+                                  void* position, int position_dtype, void* mask, int mask_dtype,
+                                  void* write_mask, int write_mask_dtype, long long context,
+                                  long long* token_log, long long step, int* error_flag, cb_stream_t stream);
 
 /* Row-wise argmax with np.argmax semantics (first max, NaN wins).
  * Replaces DeviceAdapter.argmax / argmax_last_axis (chomikgrad/lazy.py:128-134,

@@ -47,13 +47,15 @@ def _causal(torch, tq, tk):
     return torch.where(j > i + (tk - tq), -1e4, 0.0).to(torch.bfloat16).reshape(1, 1, tq, tk)
 
 
-CASES = [  # batch, heads, kv_heads, tq, tk, head_size, causal
-    (1, 8, 2, 300, 300, 64, True),
-    (1, 8, 2, 300, 300, 64, False),
-    (2, 4, 4, 200, 200, 128, True),
-    (1, 4, 1, 64, 192, 64, True),    # verify-block shape: queries at the end of the keys
-    (1, 32, 4, 1024, 1024, 64, True),
-    (1, 2, 2, 129, 129, 128, False),
+SKIP, ZERO = 1, 2  # CB_CAUSAL_SKIP, CB_CAUSAL_ZERO_BELOW
+CASES = [  # batch, heads, kv_heads, tq, tk, head_size, causal flags
+    (1, 8, 2, 300, 300, 64, SKIP | ZERO),
+    (1, 8, 2, 300, 300, 64, 0),
+    (1, 8, 2, 300, 300, 64, SKIP),
+    (2, 4, 4, 200, 200, 128, SKIP | ZERO),
+    (1, 4, 1, 64, 192, 64, SKIP | ZERO),  # verify-block shape: queries at the end of the keys
+    (1, 32, 4, 1024, 1024, 64, SKIP | ZERO),
+    (1, 2, 2, 129, 129, 128, 0),
 ]
 
 
@@ -122,7 +124,7 @@ def test_prefill_with_tensor_core_attention_matches_cpu_graph(gpu, oracle):
     ids = Tensor(rng.integers(0, config.vocab_size, (1, seq)).astype(np.int32), copy=False)
     outputs = model.prefill(ids, Tensor(position_selector(seq - 1, seq, dtype=dt), copy=False))
     program = compile_graph(*outputs, compiler="cuda-b200")
-    assert "causal" in program.source and "place(" in program.source
+    assert "causal=3" in program.source and "place(" in program.source
     got = program()
     want = [o.numpy(compiler="cpu") for o in outputs]
     np.testing.assert_allclose(got[0], want[0], rtol=0, atol=2e-3)  # logits

@@ -94,3 +94,56 @@ def test_gemm_tc_rejects_unsupported_shapes():
     b = torch.zeros(126, 96, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.KernelError, match="multiple of 4"):
         _run(torch, a[:, :80].contiguous(), b[:, :80].contiguous())
+
+
+ROWS_CASES = [  # rows, weight row counts, k, splits (0 = chosen)
+    (1, (2048,), 2048, 0),
+    (5, (2048, 256, 256), 2048, 0),
+    (32, (5632, 5632), 2048, 0),
+    (32, (2048,), 5632, 0),
+    (32, (300,), 200, 1),
+    (100, (640, 64), 1024, 3),
+    (256, (384,), 512, 0),
+]
+
+
+@pytest.mark.parametrize("rows,ns,k,splits", ROWS_CASES)
+@pytest.mark.parametrize("x_dtype", ["f32", "bf16"])
+def test_gemm_rows_matches_float64(rows, ns, k, splits, x_dtype):
+    """cb_gemm_rows (swap-AB, split K, last-CTA reduction) against float64, twice in a row."""
+    torch = pytest.importorskip("torch")
+    from cuda_b200 import _lib
+
+    gen = torch.Generator().manual_seed(rows * 13 + k + len(ns))
+    x = torch.randn(rows, k, generator=gen)
+    if x_dtype == "bf16":
+        x = x.to(torch.bfloat16)
+    ws = [(torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16) for n in ns]
+    xd, wd = x.cuda(), [w.cuda() for w in ws]
+    outs = [torch.full((rows, n + 8), float("nan"), device="cuda") for n in ns]  # row stride n + 8
+    a = _lib.GemmRowsArgs()
+    a.x, a.x_dtype, a.ldx = xd.data_ptr(), _lib.F32 if x_dtype == "f32" else _lib.BF16, k
+    a.rows, a.k, a.n_w, a.splits = rows, k, len(ns), splits
+    for i, (w, o) in enumerate(zip(wd, outs)):
+        a.w[i], a.w_rows[i], a.out[i], a.ldo[i] = w.data_ptr(), w.shape[0], o.data_ptr(), o.stride(0)
+    lib = _lib.load()
+    scratch = torch.empty(lib.cb_gemm_rows_scratch(ctypes.byref(a)), dtype=torch.uint8, device="cuda")
+    counters = torch.zeros(lib.cb_gemm_rows_counters(ctypes.byref(a)), dtype=torch.int32, device="cuda")
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a.scratch, a.counters, a.error_flag = scratch.data_ptr(), counters.data_ptr(), flag.data_ptr()
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):  # the counters must be re-armed by the first call
+        for o in outs:
+            o[:, : o.shape[1] - 8].fill_(float("nan"))
+        _lib.call("cb_gemm_rows", ctypes.byref(a), stream)
+        torch.cuda.synchronize()
+        assert int(flag.item()) == 0 and not counters.any()
+        for w, o in zip(ws, outs):
+            n = w.shape[0]
+            got = o[:, :n].cpu().double()
+            ref = x.double() @ w.double().T
+            scale = x.double().abs() @ w.double().abs().T
+            bound = scale * (k * 2.0 ** -23 + (2.0 ** -15 if x_dtype == "f32" else 0.0)) + 1e-6
+            assert torch.isfinite(got).all()
+            assert bool(((got - ref).abs() <= bound).all()), float(((got - ref).abs() / bound).max())
+            assert torch.isnan(o[:, n:]).all()  # nothing written past n

@@ -108,6 +108,8 @@ def test_prefill_uses_lowerings(tiny_bf16):
     p = plan(outs, [ids])
     layers = cfg.num_hidden_layers
     assert p.lowered == {"rms_norm": 2 * layers + 1, "rope": 2 * layers, "sdpa": layers, "place": 2 * layers}
+    # the causal mask (-1e4 above the diagonal, 0 elsewhere) allows tile skipping and mask-free tiles
+    assert all(s.args["causal"] == 3 for s in p.steps if s.name == "sdpa")
 
 
 def test_lowering_is_skipped_when_the_portable_graph_differs():
@@ -188,3 +190,32 @@ def test_placement_match_rejects_other_matrices():
     p = plan([x @ Tensor(perm)])
     assert [s.name for s in p.steps] == ["place"]
     assert list(p.steps[0].args["cols"].host) == [2, 0, -1, 1]
+
+
+def test_batched_decode_plan_updates_caches_in_place(tiny_bf16):
+    """B sequences in one step: caches bound by pointer, blended in place (cb_kv_write), returned aliased."""
+    from cuda_b200.batched import BatchedDecoderStep
+
+    wl, weights = tiny_bf16
+    cfg, dt = wl.config, wl.np_dtype
+    b, ctx = 4, 48
+    shape = (b, cfg.num_key_value_heads, ctx, cfg.head_size)
+    caches = [Tensor.from_native(np.zeros(shape, np.float32), backend="cpu", shape=shape, dtype=dt)
+              for _ in range(2 * cfg.num_hidden_layers)]
+    am, wm = L.decode_masks(5, ctx, dt)
+    inputs = [Tensor(np.full((b, 1), 3, np.int32), copy=False),
+              Tensor(L.rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=5), copy=False),
+              Tensor(am, copy=False), Tensor(wm, copy=False), Tensor(np.asarray(5, np.int32), copy=False)]
+    outs = BatchedDecoderStep(cfg, weights, batch=b, cache_length=ctx, dtype=dt)(
+        *inputs[:4], list(zip(caches[::2], caches[1::2])), position=inputs[4])
+    p = plan(outs, inputs + caches)
+    kinds = Counter(s.name for s in p.steps)
+    layers = cfg.num_hidden_layers
+    assert kinds["kv_write"] == 2 * layers and kinds["sdpa"] == layers
+    assert kinds["matmul"] == 7 * layers + 1
+    assert sorted(p.aliases) == list(range(1, 2 * layers + 1))
+    for c in caches:
+        assert p.input_buffers[c._node].bind == "pointer"
+    with pytest.raises(ValueError):
+        BatchedDecoderStep(cfg, weights, batch=b, cache_length=ctx, dtype=dt)(
+            Tensor(np.zeros((b + 1, 1), np.int32)), *inputs[1:4], list(zip(caches[::2], caches[1::2])))
