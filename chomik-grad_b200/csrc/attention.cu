@@ -84,6 +84,115 @@ __global__ void __launch_bounds__(kThreads) sdpa_kernel(const cb_sdpa_args a) {
 }
 
 // ---------------------------------------------------------------------------
+// Single-query attention (tq == 1) over float32 K/V rows, split over keys:
+// the batched decode step's attention (every sequence's one new query
+// against its own cache).  Pass 1, grid (splits, kv_heads, batch): a block
+// stages the split's K/V rows with 16-byte loads (coalesced: rows are
+// contiguous), loads the group's q rows and mask values, and one warp per
+// query head computes the split's scores (lane = key), its max, sum and
+// unnormalised p @ v.  Pass 2 merges the splits of each (batch, head) in
+// split order, so results are deterministic.
+constexpr int kQSplit = 32;  // keys per split = lanes
+
+__host__ __device__ inline long long qsplit_smem_floats(long long group, long long hd) {
+  return kQSplit * (hd + 4) + kQSplit * hd + group * hd + group * kQSplit;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads) sdpa_query_kernel(const cb_sdpa_args a, float* parts, int splits) {
+  extern __shared__ float sm[];
+  constexpr int KS = HD + 4;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int group = static_cast<int>(a.heads / a.kv_heads);
+  float* ks = sm;                          // [kQSplit][KS]
+  float* vs = ks + kQSplit * KS;           // [kQSplit][HD]
+  float* qs = vs + kQSplit * HD;           // [group][HD]
+  float* ms = qs + group * HD;             // [group][kQSplit]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long lo = static_cast<long long>(split) * kQSplit;
+  const int n = static_cast<int>(a.tk - lo < kQSplit ? a.tk - lo : kQSplit);
+  const float* kb = static_cast<const float*>(a.k) + a.k_offset + b * a.k_strides[0] + kvh * a.k_strides[1];
+  const float* vb = static_cast<const float*>(a.v) + a.v_offset + b * a.v_strides[0] + kvh * a.v_strides[1];
+  for (int e = tid; e < n * (HD / 4); e += kThreads) {
+    const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
+    const float4 kv = __ldg(reinterpret_cast<const float4*>(kb + (lo + r) * a.k_strides[2] + d4));
+    const float4 vv = __ldg(reinterpret_cast<const float4*>(vb + (lo + r) * a.v_strides[2] + d4));
+    *reinterpret_cast<float4*>(ks + r * KS + d4) = kv;
+    *reinterpret_cast<float4*>(vs + r * HD + d4) = vv;
+  }
+  for (int e = tid; e < group * HD; e += kThreads) {
+    const int h = kvh * group + e / HD, d = e % HD;
+    qs[e] = load_as_f32(a.q, a.q_offset + idx4(a.q_strides, b, h, 0, d), a.q_dtype);
+  }
+  for (int e = tid; e < group * kQSplit; e += kThreads) {
+    const int h = kvh * group + e / kQSplit, j = e % kQSplit;
+    ms[e] = (a.mask != nullptr && j < n)
+                ? load_as_f32(a.mask, a.mask_offset + idx4(a.mask_strides, b, h, 0, lo + j), a.mask_dtype)
+                : 0.0f;
+  }
+  __syncthreads();
+  for (int hl = warp; hl < group; hl += kThreads / 32) {
+    const int h = kvh * group + hl;
+    float x = -INFINITY;
+    if (lane < n) {
+      const float4* q = reinterpret_cast<const float4*>(qs + hl * HD);
+      const float4* k = reinterpret_cast<const float4*>(ks + lane * KS);
+      float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+#pragma unroll
+      for (int d = 0; d < HD / 4; ++d) {
+        const float4 qa = q[d], ka = k[d];
+        s0 = fmaf(qa.x, ka.x, s0);
+        s1 = fmaf(qa.y, ka.y, s1);
+        s2 = fmaf(qa.z, ka.z, s2);
+        s3 = fmaf(qa.w, ka.w, s3);
+      }
+      x = __fadd_rn(__fdiv_rn((s0 + s1) + (s2 + s3), a.divisor), ms[hl * kQSplit + lane]);
+    }
+    const float m = warp_max(x);
+    const float p = lane < n ? expf(x - m) : 0.0f;
+    const float l = warp_sum(p);
+    float* part = parts + ((static_cast<long long>(b) * a.heads + h) * splits + split) * (HD + 2);
+#pragma unroll
+    for (int d0 = 0; d0 < HD; d0 += 64) {
+      const int d = d0 + 2 * lane;
+      const bool mine = d < HD;
+      float2 acc = make_float2(0.0f, 0.0f);
+      for (int j = 0; j < n; ++j) {  // every lane shuffles; rows j < n only are read
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        if (mine) {
+          const float2 v = *reinterpret_cast<const float2*>(vs + j * HD + d);
+          acc.x = fmaf(pj, v.x, acc.x);
+          acc.y = fmaf(pj, v.y, acc.y);
+        }
+      }
+      if (mine) *reinterpret_cast<float2*>(part + 2 + d) = acc;
+    }
+    if (lane == 0) {
+      part[0] = m;
+      part[1] = l;
+    }
+  }
+}
+
+// Pass 2: one block per (batch, head), one thread per output element.
+__global__ void sdpa_query_merge_kernel(const float* parts, int splits, int hd, float* out) {
+  const long long row = blockIdx.x;
+  const float* base = parts + row * splits * (hd + 2);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float m = -INFINITY;
+    for (int s = 0; s < splits; ++s) m = fmaxf(m, base[s * (hd + 2)]);
+    float l = 0.0f, acc = 0.0f;
+    for (int s = 0; s < splits; ++s) {
+      const float* part = base + s * (hd + 2);
+      const float scale = expf(part[0] - m);
+      l = fmaf(part[1], scale, l);
+      acc = fmaf(part[2 + d], scale, acc);
+    }
+    out[row * hd + d] = __fdiv_rn(acc, l);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Decode: grid (splits, kv_heads), 256 threads; the work of one block is
 // attention_item (attn_core.cuh).
 template <int HD>
@@ -117,6 +226,60 @@ int cb_sdpa(const cb_sdpa_args* a, cb_stream_t stream) {
   const size_t smem = static_cast<size_t>(warps) * a->head_size * sizeof(float);
   sdpa_kernel<<<static_cast<unsigned>(blocks), kThreads, smem, static_cast<cudaStream_t>(stream)>>>(*a);
   return check_launch("cb_sdpa");
+}
+
+long long cb_sdpa_query_scratch(const cb_sdpa_args* a) {
+  if (a == nullptr || a->batch <= 0 || a->heads <= 0 || a->tk <= 0 || a->head_size <= 0) return 0;
+  const long long splits = (a->tk + kQSplit - 1) / kQSplit;
+  return a->batch * a->heads * splits * (a->head_size + 2) * static_cast<long long>(sizeof(float));
+}
+
+int cb_sdpa_query(const cb_sdpa_args* a, void* scratch, cb_stream_t stream) {
+  CB_REQUIRE(a != nullptr && a->q != nullptr && a->k != nullptr && a->v != nullptr && a->out != nullptr,
+             "sdpa_query: q, k, v and out are required");
+  CB_REQUIRE(a->tq == 1, "sdpa_query: one query row per head (tq = %lld)", a->tq);
+  CB_REQUIRE(a->head_size == 32 || a->head_size == 64 || a->head_size == 128 || a->head_size == 256,
+             "sdpa_query: head size %lld unsupported (32/64/128/256)", a->head_size);
+  CB_REQUIRE(a->kv_heads > 0 && a->heads % a->kv_heads == 0, "sdpa_query: heads must be a multiple of KV heads");
+  CB_REQUIRE(a->k_dtype == CB_F32 && a->v_dtype == CB_F32, "sdpa_query: K/V must be float32");
+  CB_REQUIRE(a->k_strides[3] == 1 && a->v_strides[3] == 1 && a->k_strides[2] % 4 == 0 && a->v_strides[2] % 4 == 0 &&
+                 a->k_strides[1] % 4 == 0 && a->v_strides[1] % 4 == 0 && a->k_strides[0] % 4 == 0 &&
+                 a->v_strides[0] % 4 == 0 && a->k_offset % 4 == 0 && a->v_offset % 4 == 0 &&
+                 (reinterpret_cast<uintptr_t>(a->k) & 15) == 0 && (reinterpret_cast<uintptr_t>(a->v) & 15) == 0,
+             "sdpa_query: K/V rows must be contiguous and 16-byte aligned");
+  CB_REQUIRE(scratch != nullptr && (reinterpret_cast<uintptr_t>(scratch) & 15) == 0,
+             "sdpa_query: scratch (cb_sdpa_query_scratch bytes, 16-byte aligned) is required");
+  if (a->batch == 0 || a->heads == 0) return CB_OK;
+  const long long splits = (a->tk + kQSplit - 1) / kQSplit;
+  CB_REQUIRE(splits < (1LL << 31) && a->kv_heads < 65536 && a->batch < 65536, "sdpa_query: grid too large");
+  const long long group = a->heads / a->kv_heads;
+  const size_t smem = static_cast<size_t>(qsplit_smem_floats(group, a->head_size)) * sizeof(float);
+  CB_REQUIRE(smem <= 200 * 1024, "sdpa_query: too many query heads per KV head");
+  float* parts = static_cast<float*>(scratch);
+  const dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(a->kv_heads), static_cast<unsigned>(a->batch));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+#define CB_QUERY_CASE(HD)                                                                                   \
+  case HD:                                                                                                  \
+    e = cudaFuncSetAttribute(sdpa_query_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,            \
+                             static_cast<int>(smem));                                                       \
+    if (e == cudaSuccess) sdpa_query_kernel<HD><<<grid, kThreads, smem, s>>>(*a, parts, static_cast<int>(splits)); \
+    break;
+  switch (a->head_size) {
+    CB_QUERY_CASE(32)
+    CB_QUERY_CASE(64)
+    CB_QUERY_CASE(128)
+    CB_QUERY_CASE(256)
+  }
+#undef CB_QUERY_CASE
+  if (e != cudaSuccess) {
+    set_error("cb_sdpa_query: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  const int threads = a->head_size < 128 ? static_cast<int>(a->head_size) : 128;
+  sdpa_query_merge_kernel<<<static_cast<unsigned>(a->batch * a->heads), threads, 0, s>>>(
+      parts, static_cast<int>(splits), static_cast<int>(a->head_size), a->out);
+  return check_launch("cb_sdpa_query");
 }
 
 long long cb_decode_attention_scratch(const cb_decode_attention_args* a) {

@@ -55,6 +55,42 @@ __global__ void elementwise_kernel(const cb_elementwise_args a, long long total)
   }
 }
 
+// Every input is either laid out like the output (offset + i) or a scalar
+// broadcast (bit j of `scalar` set): no per-element index arithmetic.  Each
+// thread handles kFlatIlp elements a grid stride apart, loading all of them
+// before computing, so their loads are in flight together.
+constexpr int kFlatIlp = 4;
+
+__global__ void elementwise_flat_kernel(const cb_elementwise_args a, long long total, unsigned scalar) {
+  float reg[CB_EW_MAX_INPUTS + CB_EW_MAX_INSTR];
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < total; base += stride * kFlatIlp) {
+    float in[kFlatIlp][CB_EW_MAX_INPUTS];
+#pragma unroll
+    for (int e = 0; e < kFlatIlp; ++e) {
+      const long long i = base + e * stride;
+#pragma unroll
+      for (int j = 0; j < CB_EW_MAX_INPUTS; ++j)
+        if (j < a.n_inputs && i < total)
+          in[e][j] = load_as_f32(a.inputs[j], a.in_offset[j] + (((scalar >> j) & 1u) ? 0 : i), a.in_dtype[j]);
+    }
+#pragma unroll
+    for (int e = 0; e < kFlatIlp; ++e) {
+      const long long i = base + e * stride;
+      if (i >= total) break;
+#pragma unroll
+      for (int j = 0; j < CB_EW_MAX_INPUTS; ++j)
+        if (j < a.n_inputs) reg[j] = in[e][j];
+      float result = reg[0];
+      for (int t = 0; t < a.n_instr; ++t) {
+        result = round_to(apply_op(a.op[t], reg[a.lhs[t]], a.rhs[t] >= 0 ? reg[a.rhs[t]] : 0.0f), a.round[t]);
+        reg[a.n_inputs + t] = result;
+      }
+      store_from_f32(a.out, i, a.out_dtype, result);
+    }
+  }
+}
+
 __device__ __forceinline__ float nan_max(float a, float b) {
   if (a != a) return a;
   if (b != b) return b;
@@ -243,6 +279,26 @@ int cb_elementwise(const cb_elementwise_args* a, cb_stream_t stream) {
   long long total = 1;
   for (int d = 0; d < a->ndim; ++d) total *= a->shape[d];
   if (total == 0) return CB_OK;
+  // flat path: every input contiguous like the output, or a scalar
+  unsigned scalar = 0;
+  bool flat = true;
+  for (int j = 0; j < a->n_inputs && flat; ++j) {
+    bool zero = true, contig = true;
+    long long expect = 1;
+    for (int d = a->ndim - 1; d >= 0; --d) {
+      if (a->shape[d] == 1) continue;
+      zero = zero && a->in_strides[j][d] == 0;
+      contig = contig && a->in_strides[j][d] == expect;
+      expect *= a->shape[d];
+    }
+    if (zero) scalar |= 1u << j;
+    flat = zero || contig;
+  }
+  if (flat) {
+    elementwise_flat_kernel<<<grid_for((total + kFlatIlp - 1) / kFlatIlp), kThreads, 0,
+                              static_cast<cudaStream_t>(stream)>>>(*a, total, scalar);
+    return check_launch("cb_elementwise");
+  }
   elementwise_kernel<<<grid_for(total), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(*a, total);
   return check_launch("cb_elementwise");
 }

@@ -211,6 +211,8 @@ _SIGNATURES = {
     "cb_rmsnorm_row_table": ([POINTER(RmsNormArgs), c_void_p, c_void_p], c_int),
     "cb_rope": ([POINTER(RopeArgs), c_void_p], c_int),
     "cb_sdpa": ([POINTER(SdpaArgs), c_void_p], c_int),
+    "cb_sdpa_query_scratch": ([POINTER(SdpaArgs)], c_longlong),
+    "cb_sdpa_query": ([POINTER(SdpaArgs), c_void_p, c_void_p], c_int),
     "cb_gemv": ([POINTER(GemvArgs), c_void_p], c_int),
     "cb_gemv_grid": ([POINTER(GemvArgs), POINTER(c_int)], c_int),
     "cb_decode_attention": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),

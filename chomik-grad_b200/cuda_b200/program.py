@@ -67,14 +67,20 @@ def gemm_shape(step: Step, min_rows: int) -> Optional[Tuple[int, int, int, int, 
     ldb = bv.strides[-1]
     if bv.strides[-2] != 1 and k > 1:
         return None
-    lda = av.strides[-2]
     if av.strides[-1] != 1 and k > 1:
         return None
-    rows = av.shape[-2]
-    for d in range(len(av.shape) - 3, -1, -1):  # leading dims must step by whole row blocks
-        if av.shape[d] != 1 and av.strides[d] != rows * lda:
+    # every dimension before K folds into rows: the non-unit ones must step by
+    # whole rows (a size-1 dimension's stride is meaningless, e.g. the token
+    # axis of a permuted single-token attention output)
+    dims = [(s, st) for s, st in zip(av.shape[:-1], av.strides[:-1]) if s != 1]
+    lda = dims[-1][1] if dims else k
+    rows = 1
+    for size, stride in reversed(dims):
+        if stride != rows * lda:
             return None
-        rows *= av.shape[d]
+        rows *= size
+    if rows > 1 and lda < k:  # overlapping or broadcast rows
+        return None
     if (rows < min_rows or k % 8 or n % 4 or ldb % 8
             or tuple(out.shape[-2:]) != (av.shape[-2], n)):
         return None
@@ -601,7 +607,22 @@ class CudaB200Program(CompiledProgram):
         q, k = step.args["q"], step.args["k"]
         return q.shape[-1] in (64, 128) and q.shape[2] >= self._compiler.attn_min_rows and k.shape[2] >= 1
 
+    def _sdpa_query(self, step: Step) -> bool:
+        """Whether a single-query attention (batched decode) runs on cb_sdpa_query."""
+        q, k, v = step.args["q"], step.args["k"], step.args["v"]
+        if q.shape[2] != 1 or q.shape[-1] not in (32, 64, 128, 256):
+            return False
+        for view in (k, v):
+            st = [0 if n == 1 else s for n, s in zip(view.shape, view.strides)]
+            if view.dtype != np.float32 or st[3] not in (0, 1) or any(x % 4 for x in st[:3]) or view.offset % 4:
+                return False
+        return True
+
     def _sdpa_scratch_bytes(self, step: Step) -> int:
+        if self._sdpa_query(step):
+            q, k = step.args["q"], step.args["k"]
+            splits = (k.shape[2] + 31) // 32
+            return q.shape[0] * q.shape[1] * splits * (q.shape[-1] + 2) * 4
         if not self._sdpa_tc(step):
             return 0
         q, k = step.args["q"], step.args["k"]
@@ -626,6 +647,10 @@ class CudaB200Program(CompiledProgram):
         a.batch, a.heads, a.tq, a.head_size = q.shape
         a.kv_heads, a.tk = k.shape[1], k.shape[2]
         a.divisor = step.args["divisor"]
+        if self._sdpa_query(step):
+            _lib.call("cb_sdpa_query", ctypes.byref(a), self._gemm_scratch.data_ptr(), stream)
+            self._extra_launches += 1  # the merge pass
+            return
         if self._sdpa_tc(step):
             _lib.call("cb_sdpa_tc", ctypes.byref(a), int(step.args.get("causal", False)),
                       self._gemm_scratch.data_ptr(), self._gemm_flag.data_ptr(), stream)

@@ -266,6 +266,16 @@ typedef struct {
 } cb_sdpa_args;
 CB_API int cb_sdpa(const cb_sdpa_args* args, cb_stream_t stream);
 
+/* Single-query form of cb_sdpa (tq == 1): the attention of a batched decode
+ * step, where each sequence's new query attends over its own cache
+ * (chomikgrad/llama.py:514-525 -- scores, softmax, p @ v -- once per
+ * sequence).  K/V float32 with contiguous, 16-byte aligned rows; q and mask
+ * any dtype and strides.  Split over keys (32 per block) with a second pass
+ * that merges the splits of each (batch, head) in split order
+ * (deterministic).  `scratch`: cb_sdpa_query_scratch bytes, 16-byte aligned. */
+CB_API long long cb_sdpa_query_scratch(const cb_sdpa_args* args);
+CB_API int cb_sdpa_query(const cb_sdpa_args* args, void* scratch, cb_stream_t stream);
+
 /* Tensor-core (tcgen05) form of cb_sdpa for prefill and verify blocks: the
  * same softmax(q k^T / divisor + mask) v (chomikgrad/llama.py:332-369,
  * tensor.py:325-334) with q, k, v split into bf16 hi/lo planes (three MMA

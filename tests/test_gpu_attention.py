@@ -130,3 +130,59 @@ def test_prefill_with_tensor_core_attention_matches_cpu_graph(gpu, oracle):
     np.testing.assert_allclose(got[0], want[0], rtol=0, atol=2e-3)  # logits
     for g, w in zip(got[1:], want[1:]):  # the KV caches
         np.testing.assert_allclose(np.asarray(g, np.float32), np.asarray(w, np.float32), rtol=0, atol=1e-3)
+
+
+QUERY_CASES = [  # batch, heads, kv_heads, tk, head_size
+    (3, 8, 2, 100, 64),   # ragged last split
+    (32, 32, 4, 768, 64),  # the batched TinyLlama step
+    (2, 4, 4, 33, 128),
+    (1, 2, 1, 5, 32),
+    (2, 8, 8, 64, 256),
+    (4, 32, 8, 1024, 128),  # Llama-3-8B shape
+]
+
+
+@pytest.mark.parametrize("batch,heads,kv,tk,hd", QUERY_CASES)
+def test_sdpa_query_matches_float64(batch, heads, kv, tk, hd):
+    """cb_sdpa_query (one query row, split over keys) vs float64 and the generic cb_sdpa."""
+    torch = pytest.importorskip("torch")
+    from cuda_b200 import _lib
+
+    gen = torch.Generator().manual_seed(tk * 7 + hd + batch)
+    q = torch.randn(batch, 1, heads, hd, generator=gen).permute(0, 2, 1, 3)  # strided q, like a view
+    k = torch.randn(batch, kv, tk, hd, generator=gen)
+    v = torch.randn(batch, kv, tk, hd, generator=gen)
+    # decode mask: -1e4 past the current position, shared by every head
+    mask = torch.where(torch.arange(tk) > tk - 3, -1e4, 0.0).to(torch.bfloat16).reshape(1, 1, 1, tk)
+    divisor = float(np.sqrt(hd))
+    qd, kd, vd, md = q.cuda(), k.cuda(), v.cuda(), mask.cuda()
+    out = torch.full((batch, heads, 1, hd), float("nan"), device="cuda")
+    a = _args(torch, qd, kd, vd, md, out, divisor)
+    lib = _lib.load()
+    scratch = torch.empty(lib.cb_sdpa_query_scratch(ctypes.byref(a)), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):  # the scratch is reused: a second call gives the same result
+        _lib.call("cb_sdpa_query", ctypes.byref(a), scratch.data_ptr(), stream)
+    torch.cuda.synchronize()
+    ref = _reference(q, k, v, mask.float(), divisor)
+    got = out.cpu().double()
+    assert torch.isfinite(got).all()
+    assert float((got - ref).abs().max()) <= 2e-5 * float(v.abs().max())
+    generic = torch.zeros_like(out)
+    a.out = generic.data_ptr()
+    _lib.call("cb_sdpa", ctypes.byref(a), stream)
+    torch.cuda.synchronize()
+    assert float((generic.cpu().double() - got).abs().max()) <= 2e-5 * float(v.abs().max())
+
+
+def test_sdpa_query_rejects_unaligned_cache_rows():
+    torch = pytest.importorskip("torch")
+    from cuda_b200 import _lib
+
+    q = torch.zeros(1, 2, 1, 64, device="cuda")
+    kv = torch.zeros(1, 2, 8, 66, device="cuda")[..., :64]  # row stride 66 floats
+    mask = torch.zeros(1, 1, 1, 8, device="cuda")
+    out = torch.zeros_like(q)
+    a = _args(torch, q, kv, kv, mask, out, 8.0)
+    with pytest.raises(_lib.KernelError, match="16-byte aligned"):
+        _lib.call("cb_sdpa_query", ctypes.byref(a), out.data_ptr(), None)
