@@ -9,11 +9,14 @@
 //  * one CTA per (128-query tile, head, batch): warp 0 streams K/V tiles with
 //    TMA into two stages, warp 1 issues the MMAs -- S = q k^T as
 //    qh.kh + qh.kl + ql.kh into a double-buffered TMEM S, and O_tile = p v as
-//    ph.vh + ph.vl + pl.vh into TMEM -- and warps 2-5 own one query row per
-//    thread: they read S from TMEM, apply the divisor and the mask, run the
-//    online softmax in float32, write p as bf16 hi/lo planes into shared
-//    memory (swizzled like a TMA tile) and fold each O_tile into a float32
-//    accumulator in registers;
+//    ph.vh + ph.vl + pl.vh into TMEM -- and warps 2-9 run the softmax, two
+//    threads per query row (each half of the row's keys and of its output
+//    dims; two warps per scheduler, so one warp's latency hides behind the
+//    other's work): they read S from TMEM into registers, apply the divisor
+//    and the mask, run the online softmax in float32 (the halves swap tile
+//    maxima through shared memory), write p as bf16 hi/lo planes into
+//    shared memory (swizzled like a TMA tile) and fold each O_tile into a
+//    float32 accumulator in registers;
 //  * with CB_CAUSAL_SKIP, key tiles that lie entirely above the diagonal are
 //    skipped; the caller asserts the mask there is <= -5000, where
 //    exp(score - row max) underflows to 0 in float32 for any row whose
@@ -36,7 +39,7 @@ namespace {
 using namespace tc;
 
 constexpr int kBQ = 128;                 // query rows per CTA = TMEM lanes
-constexpr int kAttnTcThreads = 192;      // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr int kAttnTcThreads = 320;      // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
 constexpr int kPlanesRows = 64;          // rows per pre-pass block
 
 template <int HD>
@@ -53,7 +56,8 @@ struct AttnShape {
   static constexpr int kPOff = kStageOff + 2 * kStage;
   static constexpr int kSmem = kPOff + 2 * kPPlane + 1024;  // + alignment of the swizzled tiles
   static constexpr int kOCol = 2 * kBK;                     // TMEM: S buffers at 0 and kBK, O_tile after
-  static constexpr int kTmemCols = 2 * kBK + HD <= 256 ? 256 : 512;
+  static constexpr int kXCol = kOCol + HD;                  // 4 columns: [tile parity][half] exchange slots
+  static constexpr int kTmemCols = kXCol + 4 <= 256 ? 256 : 512;
   static_assert(kSmem <= 227 * 1024 - 256, "shared memory");
 };
 
@@ -93,6 +97,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
   __shared__ __align__(8) uint64_t p_full;
   __shared__ __align__(8) uint64_t o_full;
   __shared__ __align__(8) uint64_t mma_done;
+  __shared__ __align__(8) uint64_t pair_bar[4];  // the two softmax warps of a TMEM lane quarter
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -115,7 +120,8 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
       mbar_init(kv_empty + s, 1);
       mbar_init(s_full + s, 1);
     }
-    mbar_init(&p_full, kBQ);
+    mbar_init(&p_full, 2 * kBQ);
+    for (int q = 0; q < 4; ++q) mbar_init(pair_bar + q, 64);
     mbar_init(&o_full, 1);
     mbar_init(&mma_done, 1);
     mbar_fence_init();
@@ -232,25 +238,42 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
       umma_commit(&mma_done);  // arrives once every MMA issued above has completed
     }
   } else {
-    // ---- softmax: one query row per thread ----
-    const int quarter = warp & 3;  // the TMEM lane quarter this warp may access
+    // ---- softmax: two threads per query row ----
+    // Warp w (2..9) reads TMEM lane quarter w % 4; the two warps of a
+    // quarter split each row: half h owns S columns [h kBK/2, (h+1) kBK/2)
+    // of every tile and O dims [h HD/2, (h+1) HD/2).  The halves swap their
+    // tile maxima (and at the end their sums) through shared memory, paced
+    // by the quarter's mbarrier (64 arrivals per phase, bounded waits).
+    constexpr int kCols = kBK / 2;  // S columns of this thread
+    constexpr int kDims = HD / 2;   // O dims of this thread
+    static_assert(kCols % 32 == 0 && kDims % 32 == 0, "32-column TMEM loads");
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const int qi = q0 + r;
+    const int col0 = half * kCols;
+    const int dim0 = half * kDims;
     const uint32_t lanes = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    uint64_t* pair = pair_bar + quarter;
     const long long mrow = p.mask_offset + b * p.mask_strides[0] + h * p.mask_strides[1] +
                            static_cast<long long>(min(qi, p.tq - 1)) * p.mask_strides[2];
-    bool use_mask = true;  // per key tile: false where the mask is known to be 0
-    auto score = [&](float raw, int key) -> float {
-      if (key >= p.tk) return -INFINITY;
-      float x = p.div_pow2 ? raw * p.inv_divisor : __fdiv_rn(raw, p.divisor);
-      if (use_mask) x = __fadd_rn(x, load_as_f32(p.mask, mrow + key * p.mask_strides[3], p.mask_dtype));
-      return x;
-    };
-    float o[HD];
+    float o[kDims];
 #pragma unroll
-    for (int d = 0; d < HD; ++d) o[d] = 0.0f;
+    for (int d = 0; d < kDims; ++d) o[d] = 0.0f;
     float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
     bool ok = true;
+    auto fold = [&](int jj) -> bool {  // o = o * alpha_prev + O_tile(jj)
+      if (!__all_sync(0xffffffffu, wait_or_abort(&o_full, static_cast<uint32_t>(jj & 1), abort))) return false;
+      fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < kDims; c0 += 16) {  // 16 columns at a time: x[] is live meanwhile
+        float v[16];
+        tmem_load16(lanes + static_cast<uint32_t>(S::kOCol + dim0 + c0), v);
+#pragma unroll
+        for (int d = 0; d < 16; ++d) o[c0 + d] = fmaf(o[c0 + d], alpha_prev, v[d]);
+      }
+      return true;
+    };
     for (int j = 0; j < n_tiles; ++j) {
       // warp-uniform outcome: the TMEM loads below are warp-wide (.sync.aligned)
       if (!__all_sync(0xffffffffu, wait_or_abort(s_full + (j & 1), static_cast<uint32_t>((j >> 1) & 1), abort))) {
@@ -258,88 +281,100 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         break;
       }
       fence_after();
-      const uint32_t sb = lanes + static_cast<uint32_t>((j & 1) * kBK);
-      const int key0 = j * kBK;
-      use_mask = p.mask != nullptr &&
-                 !(p.zero_below && static_cast<long long>(key0) + kBK - 1 <= static_cast<long long>(q0) + p.causal_offset);
-      float tmax = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kBK; c0 += 16) {
-        float v[16];
-        tmem_load16(sb + c0, v);
+      float x[kCols];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) tmax = fmaxf(tmax, score(v[e], key0 + c0 + e));
+      for (int c0 = 0; c0 < kCols; c0 += 32)
+        tmem_load32_nowait(lanes + static_cast<uint32_t>((j & 1) * kBK + col0 + c0), x + c0);
+      tmem_wait_ld();
+      reg_fence<kCols>(x);
+      const int key0 = j * kBK + col0;
+      const bool use_mask = p.mask != nullptr && !(p.zero_below && static_cast<long long>(j) * kBK + kBK - 1 <=
+                                                                        static_cast<long long>(q0) + p.causal_offset);
+      if (!use_mask && p.div_pow2 && key0 + kCols <= p.tk) {  // the common tile: a scale only
+#pragma unroll
+        for (int e = 0; e < kCols; ++e) x[e] *= p.inv_divisor;
+      } else {
+#pragma unroll
+        for (int e = 0; e < kCols; ++e) {
+          const int key = key0 + e;
+          float v = p.div_pow2 ? x[e] * p.inv_divisor : __fdiv_rn(x[e], p.divisor);
+          if (use_mask && key < p.tk) v = __fadd_rn(v, load_as_f32(p.mask, mrow + key * p.mask_strides[3], p.mask_dtype));
+          x[e] = key < p.tk ? v : -INFINITY;
+        }
       }
+      float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int e = 0; e < kCols; ++e) t4[e & 3] = fmaxf(t4[e & 3], x[e]);
+      const float tmax_mine = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
+      // swap tile maxima with the other half of the row through this lane's
+      // TMEM exchange columns (slot by tile parity)
+      tmem_store1(lanes + static_cast<uint32_t>(S::kXCol + (j & 1) * 2 + half), tmax_mine);
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(pair);
+      if (!__all_sync(0xffffffffu, wait_or_abort(pair, static_cast<uint32_t>(j & 1), abort))) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const float tmax =
+          fmaxf(tmax_mine, tmem_load1(lanes + static_cast<uint32_t>(S::kXCol + (j & 1) * 2 + (half ^ 1))));
       const float m_new = fmaxf(m, tmax);
       const float alpha = __expf(m - m_new);
-      if (j > 0) {  // fold O_tile of the previous key tile (p of that tile, max m)
-        if (!__all_sync(0xffffffffu, wait_or_abort(&o_full, static_cast<uint32_t>((j - 1) & 1), abort))) {
-          ok = false;
-          break;
-        }
-        fence_after();
-#pragma unroll
-        for (int c0 = 0; c0 < HD; c0 += 16) {
-          float v[16];
-          tmem_load16(lanes + static_cast<uint32_t>(S::kOCol + c0), v);
-#pragma unroll
-          for (int e = 0; e < 16; ++e) o[c0 + e] = fmaf(o[c0 + e], alpha_prev, v[e]);
-        }
+      if (j > 0 && !fold(j - 1)) {  // O_tile of the previous key tile (p of that tile, max m)
+        ok = false;
+        break;
       }
       // p = exp(x - m_new) as bf16 hi/lo into the swizzled P planes (free: the
       // previous tile's p.v has completed)
-      float lsum = 0.0f;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kBK; c0 += 16) {
-        float v[16];
-        tmem_load16(sb + c0, v);
+      float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          v[e] = __expf(score(v[e], key0 + c0 + e) - m_new);
-          lsum += v[e];
+      for (int c0 = 0; c0 < kCols; c0 += 8) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float x0 = __expf(x[c0 + 2 * i] - m_new), x1 = __expf(x[c0 + 2 * i + 1] - m_new);
+          s4[i] += x0 + x1;
+          const __nv_bfloat162 hi = __floats2bfloat162_rn(x0, x1);
+          const float2 hf = __bfloat1622float2(hi);
+          const __nv_bfloat162 lo = __floats2bfloat162_rn(__fsub_rn(x0, hf.x), __fsub_rn(x1, hf.y));
+          hw[i] = *reinterpret_cast<const uint32_t*>(&hi);
+          lw[i] = *reinterpret_cast<const uint32_t*>(&lo);
         }
-#pragma unroll
-        for (int grp = 0; grp < 2; ++grp) {
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float x0 = v[grp * 8 + 2 * i], x1 = v[grp * 8 + 2 * i + 1];
-            const __nv_bfloat162 hi = __floats2bfloat162_rn(x0, x1);
-            const float2 hf = __bfloat1622float2(hi);
-            const __nv_bfloat162 lo = __floats2bfloat162_rn(__fsub_rn(x0, hf.x), __fsub_rn(x1, hf.y));
-            hw[i] = *reinterpret_cast<const uint32_t*>(&hi);
-            lw[i] = *reinterpret_cast<const uint32_t*>(&lo);
-          }
-          const int kin = c0 + grp * 8;
-          unsigned char* dst = smem + S::kPOff + (kin / kChunk) * kBQ * kChunkRowBytes + swizzle_offset(r, (kin % kChunk) / 8);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4*>(dst + S::kPPlane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
+        const int kin = col0 + c0;
+        unsigned char* dst = smem + S::kPOff + (kin / kChunk) * kBQ * kChunkRowBytes + swizzle_offset(r, (kin % kChunk) / 8);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(dst + S::kPPlane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
-      l = l * alpha + lsum;
+      l = l * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
       m = m_new;
       alpha_prev = alpha;
       fence_async_shared();
       fence_before();
       mbar_arrive(&p_full);
     }
-    if (__all_sync(0xffffffffu, ok && wait_or_abort(&o_full, static_cast<uint32_t>((n_tiles - 1) & 1), abort))) {
-      fence_after();
+    if (ok && fold(n_tiles - 1)) {
+      // the row's sum is the two halves' sums (both scaled to the same max)
+      tmem_store1(lanes + static_cast<uint32_t>(S::kXCol + (n_tiles & 1) * 2 + half), l);
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(pair);
+      ok = __all_sync(0xffffffffu, wait_or_abort(pair, static_cast<uint32_t>(n_tiles & 1), abort));
+      if (ok) {
+        fence_after();
+        const float lt = l + tmem_load1(lanes + static_cast<uint32_t>(S::kXCol + (n_tiles & 1) * 2 + (half ^ 1)));
+        if (qi < p.tq) {
+          float* dst = p.out + ((static_cast<long long>(b) * p.heads + h) * p.tq + qi) * HD + dim0;
 #pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 16) {
-        float v[16];
-        tmem_load16(lanes + static_cast<uint32_t>(S::kOCol + c0), v);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) o[c0 + e] = fmaf(o[c0 + e], alpha_prev, v[e]);
-      }
-      if (qi < p.tq) {
-        float* dst = p.out + ((static_cast<long long>(b) * p.heads + h) * p.tq + qi) * HD;
-#pragma unroll
-        for (int d = 0; d < HD; d += 4)
-          *reinterpret_cast<float4*>(dst + d) = make_float4(__fdiv_rn(o[d], l), __fdiv_rn(o[d + 1], l),
-                                                           __fdiv_rn(o[d + 2], l), __fdiv_rn(o[d + 3], l));
+          for (int d = 0; d < kDims; d += 4)
+            *reinterpret_cast<float4*>(dst + d) = make_float4(__fdiv_rn(o[d], lt), __fdiv_rn(o[d + 1], lt),
+                                                             __fdiv_rn(o[d + 2], lt), __fdiv_rn(o[d + 3], lt));
+        }
       }
     } else {
+      ok = false;
+    }
+    if (!ok) {
       flag_error(p.error_flag, CB_FLAG_WAIT_DATA);
       *abort = 1;
     }
