@@ -174,21 +174,44 @@ __global__ void __launch_bounds__(kThreads) sdpa_query_kernel(const cb_sdpa_args
   }
 }
 
-// Pass 2: one block per (batch, head), one thread per output element.
-__global__ void sdpa_query_merge_kernel(const float* parts, int splits, int hd, float* out) {
-  const long long row = blockIdx.x;
+// Pass 2: one warp per (batch, head).  Lanes take the splits' maxima and
+// sums (32 splits at a time), the scales move to the dimension lanes by
+// shuffle; every sum runs in a fixed order (deterministic).
+constexpr int kMergeWarps = 4;
+
+__global__ void __launch_bounds__(kMergeWarps * 32) sdpa_query_merge_kernel(const float* parts, long long rows,
+                                                                             int splits, int hd, float* out) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * kMergeWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
   const float* base = parts + row * splits * (hd + 2);
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float m = -INFINITY;
-    for (int s = 0; s < splits; ++s) m = fmaxf(m, base[s * (hd + 2)]);
-    float l = 0.0f, acc = 0.0f;
-    for (int s = 0; s < splits; ++s) {
-      const float* part = base + s * (hd + 2);
-      const float scale = expf(part[0] - m);
-      l = fmaf(part[1], scale, l);
-      acc = fmaf(part[2 + d], scale, acc);
+  float m = -INFINITY;
+  for (int s = lane; s < splits; s += 32) m = fmaxf(m, base[s * (hd + 2)]);
+  m = warp_max(m);
+  float l = 0.0f;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  for (int s0 = 0; s0 < splits; s0 += 32) {
+    const int s = s0 + lane;
+    const float scale = s < splits ? expf(base[s * (hd + 2)] - m) : 0.0f;
+    const float ls = s < splits ? base[s * (hd + 2) + 1] * scale : 0.0f;
+    l += warp_sum(ls);
+    const int n = splits - s0 < 32 ? splits - s0 : 32;
+    for (int j = 0; j < n; ++j) {
+      const float sc = __shfl_sync(0xffffffffu, scale, j);
+      const float* part = base + (s0 + j) * (hd + 2) + 2;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int d = lane + 32 * i;
+        if (d < hd) acc[i] = fmaf(part[d], sc, acc[i]);
+      }
     }
-    out[row * hd + d] = __fdiv_rn(acc, l);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = lane + 32 * i;
+    if (d < hd) out[row * hd + d] = __fdiv_rn(acc[i], l);
   }
 }
 
@@ -276,9 +299,9 @@ int cb_sdpa_query(const cb_sdpa_args* a, void* scratch, cb_stream_t stream) {
     set_error("cb_sdpa_query: %s", cudaGetErrorString(e));
     return CB_ERR_CUDA;
   }
-  const int threads = a->head_size < 128 ? static_cast<int>(a->head_size) : 128;
-  sdpa_query_merge_kernel<<<static_cast<unsigned>(a->batch * a->heads), threads, 0, s>>>(
-      parts, static_cast<int>(splits), static_cast<int>(a->head_size), a->out);
+  const long long rows = a->batch * a->heads;
+  sdpa_query_merge_kernel<<<static_cast<unsigned>((rows + kMergeWarps - 1) / kMergeWarps), kMergeWarps * 32, 0, s>>>(
+      parts, rows, static_cast<int>(splits), static_cast<int>(a->head_size), a->out);
   return check_launch("cb_sdpa_query");
 }
 

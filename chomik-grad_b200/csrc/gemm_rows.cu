@@ -4,20 +4,27 @@
 // weights W_i (n_i x k, HF (out, in) layout) sharing one x -- the q/k/v or
 // gate/up Linears of a decode step over a batch of sequences
 // (chomikgrad/llama.py:275-277).  With few rows (a batch of 1..256
-// sequences) a weight-streaming GEMM is bound by the weight bytes, so the
-// operands are swapped: the weight rows are the MMA's M = 128 side, the
-// batch rows its N side (rows padded to a multiple of 16 by the tensor map's
-// zero fill), and K is split across CTAs so that the weight stream is spread
-// over every SM:
-//  * thread 0 streams 64-wide K chunks of the weight tile and of x's bf16
-//    hi/lo planes (split once by a pre-pass) with TMA into a ring of stages;
-//  * thread 32 issues tcgen05.mma (kind::f16, M=128, N=rows padded, K=16)
-//    W.x_hi + W.x_lo into a TMEM accumulator;
-//  * all four warps read the accumulator (warp w owns weight rows 32w..);
-//    with one split they store out directly, otherwise they store a partial
-//    and the last CTA of the weight tile (a ticket counter) sums the splits
-//    in split order -- deterministic -- stores out and re-arms the counter.
-// Every wait is bounded (sync.cuh).
+// sequences) the GEMM is bound by the weight bytes, so the operands are
+// swapped: the weight rows are the MMA's M = 128 side, the batch rows its N
+// side (rows padded to a multiple of 16 by the tensor map's zero fill).
+//
+// The weight stream is cut into 64-wide K chunks of 128-row tiles and the
+// flattened (tile, chunk) sequence is split into one contiguous, equal range
+// per CTA (one persistent CTA per SM), so every SM streams the same number
+// of bytes without a break:
+//  * warp 4 streams its range with TMA (the weight chunk and x's bf16 hi/lo
+//    planes, split once by a pre-pass) into a ring of stages;
+//  * warp 5 issues tcgen05.mma (kind::f16, M=128, N=rows padded, K=16)
+//    W.x_hi + W.x_lo into one of two TMEM accumulators, switching at each
+//    tile boundary of the range (a "segment"), so the epilogue of one tile
+//    overlaps the MMAs of the next;
+//  * warps 0-3 read each finished accumulator (warp w owns weight rows
+//    32w..): a segment that covers the whole tile stores out directly;
+//    otherwise it stores a partial, and the last of the tile's parts (a
+//    ticket counter) sums them in part order -- deterministic -- stores out
+//    and re-arms the counter.
+// Every wait is bounded (sync.cuh); on a timeout the kernel records an
+// error, lets its copies land and its MMAs finish, frees TMEM and returns.
 #include "tc_core.cuh"
 
 namespace cb {
@@ -25,17 +32,18 @@ namespace {
 
 using namespace tc;
 
-constexpr int kRowsThreads = 128;
-constexpr int kWTile = 128;  // weight rows per tile = TMEM lanes
+constexpr int kRowsThreads = 192;  // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
+constexpr int kWTile = 128;        // weight rows per tile = TMEM lanes
 
 template <int NB>
 struct RowsShape {
   static constexpr int kW = kWTile * kChunk * 2;  // weight chunk bytes
   static constexpr int kX = NB * kChunk * 2;      // one x plane chunk
   static constexpr int kStage = kW + 2 * kX;
-  static constexpr int kStages = (NB <= 64 ? 96 * 1024 : 192 * 1024) / kStage;
+  static constexpr int kStages = 200 * 1024 / kStage;
   static constexpr int kSmem = kStages * kStage + 1024;
-  static constexpr int kTmemCols = NB < 32 ? 32 : NB;
+  static constexpr int kAcc = NB < 32 ? 32 : NB;  // columns of one accumulator
+  static constexpr int kTmemCols = 2 * kAcc;
   static_assert(kStages >= 2, "at least double buffering");
 };
 
@@ -46,15 +54,25 @@ struct RowsParams {
   int n[3];
   int n_w;
   int rows;
-  int kchunks;         // 64-wide K chunks
-  int splits;
-  float* partial;      // (tiles, splits, NB, 128) float32, splits > 1
+  int kchunks;         // 64-wide K chunks per tile
+  long long total;     // tiles * kchunks
+  int max_parts;       // partial slots per tile
+  float* partial;      // (tiles, max_parts, NB, 128) float32
   unsigned* counters;  // one per tile, 0 between launches
   int* error_flag;
 };
 
+// The CTA whose range holds flattened chunk f: ranges are [c T / G, (c+1) T / G).
+__device__ __forceinline__ int cta_of(long long f, long long total, int grid) {
+  return static_cast<int>(((f + 1) * grid + total - 1) / total - 1);
+}
+
+__device__ __forceinline__ void set_flag(int* flag, int code) {
+  if (flag != nullptr) atomicCAS(flag, 0, code);
+}
+
 template <int NB>
-__global__ void __launch_bounds__(kRowsThreads)
+__global__ void __launch_bounds__(kRowsThreads, 1)
     gemm_rows_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
                      const __grid_constant__ CUtensorMap map_w2, const __grid_constant__ CUtensorMap map_xh,
                      const __grid_constant__ CUtensorMap map_xl, const __grid_constant__ RowsParams p) {
@@ -64,18 +82,17 @@ __global__ void __launch_bounds__(kRowsThreads)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   __shared__ __align__(8) uint64_t full[G::kStages];
   __shared__ __align__(8) uint64_t empty[G::kStages];
-  __shared__ __align__(8) uint64_t acc_full;
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
-  __shared__ int last_split;
+  __shared__ __align__(8) uint64_t parts_in;    // the epilogue's partials of a segment are written (128)
+  __shared__ __align__(8) uint64_t ticket_out;  // thread 0 has taken the tile's ticket (1)
+  __shared__ int last_part[2];                  // by split-segment parity
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
-  int seg = 0, seg_tile = tile;
-  while (seg + 1 < p.n_w && seg_tile >= p.tiles[seg]) seg_tile -= p.tiles[seg++];
-  const int row0 = seg_tile * kWTile;
-  const int per = (p.kchunks + p.splits - 1) / p.splits;
-  const int c_begin = split * per, c_end = min(p.kchunks, c_begin + per);
-  const int nchunks = max(c_end - c_begin, 0);
+  const long long f0 = static_cast<long long>(blockIdx.x) * p.total / gridDim.x;
+  const long long f1 = static_cast<long long>(blockIdx.x + 1) * p.total / gridDim.x;
 
   if (warp == 0) tmem_alloc(&tmem_base, G::kTmemCols);
   if (threadIdx.x == 32) {
@@ -83,7 +100,13 @@ __global__ void __launch_bounds__(kRowsThreads)
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    mbar_init(&acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 128);
+    }
+    mbar_init(&mma_done, 1);
+    mbar_init(&parts_in, 128);
+    mbar_init(&ticket_out, 1);
     mbar_fence_init();
     abort_flag = 0;
   }
@@ -93,117 +116,202 @@ __global__ void __launch_bounds__(kRowsThreads)
   const uint32_t tmem = tmem_base;
   volatile int* abort = &abort_flag;
 
-  if (warp == 0 && lane == 0) {
-    int i = 0;
-    for (; i < nchunks; ++i) {
-      const int s = i % G::kStages, round = i / G::kStages;
-      if (round > 0 && !wait_or_abort(empty + s, static_cast<uint32_t>((round - 1) & 1), abort)) {
-        if (p.error_flag != nullptr) atomicCAS(p.error_flag, 0, CB_FLAG_WAIT_SLOT);
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---- TMA producer: the range's chunks in order ----
+      long long i = 0;
+      for (long long f = f0; f < f1; ++f, ++i) {
+        const int s = static_cast<int>(i % G::kStages);
+        const long long round = i / G::kStages;
+        if (round > 0 && !wait_or_abort(empty + s, static_cast<uint32_t>((round - 1) & 1), abort)) {
+          set_flag(p.error_flag, CB_FLAG_WAIT_SLOT);
+          *abort = 1;
+          break;
+        }
+        int tile = static_cast<int>(f / p.kchunks);
+        const int kx = static_cast<int>(f % p.kchunks) * kChunk;
+        int seg = 0;
+        while (seg + 1 < p.n_w && tile >= p.tiles[seg]) tile -= p.tiles[seg++];
+        unsigned char* st = smem + s * G::kStage;
+        mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(G::kStage));
+        const CUtensorMap* mw = seg == 0 ? &map_w0 : seg == 1 ? &map_w1 : &map_w2;
+        tma_load_2d(st, mw, kx, tile * kWTile, full + s);
+        tma_load_2d(st + G::kW, &map_xh, kx, 0, full + s);
+        tma_load_2d(st + G::kW + G::kX, &map_xl, kx, 0, full + s);
+      }
+      // drain: every copy issued lands before the block can exit
+      for (long long t = i - 1; t >= 0 && t >= i - G::kStages; --t) {
+        if (!wait_short(full + t % G::kStages, static_cast<uint32_t>((t / G::kStages) & 1))) {
+          set_flag(p.error_flag, CB_FLAG_WAIT_DRAIN);
+          break;
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---- MMA issuer: one accumulator per segment, alternating ----
+      constexpr uint32_t idesc = idesc_bf16(kWTile, NB < 16 ? 16 : NB);
+      long long i = 0;
+      int seg_no = 0;
+      bool ok = true;
+      for (long long a = f0; ok && a < f1; ++seg_no) {
+        const long long b = min(f1, (a / p.kchunks + 1) * p.kchunks);  // segment [a, b): one tile
+        const int buf = seg_no & 1;
+        if (seg_no >= 2 && !wait_or_abort(acc_empty + buf, static_cast<uint32_t>(((seg_no >> 1) - 1) & 1), abort)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * G::kAcc);
+        for (long long f = a; f < b; ++f, ++i) {
+          const int s = static_cast<int>(i % G::kStages);
+          if (!wait_or_abort(full + s, static_cast<uint32_t>((i / G::kStages) & 1), abort)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const unsigned char* st = smem + s * G::kStage;
+#pragma unroll
+          for (int kk = 0; kk < kChunk / kUmmaK; ++kk) {
+            const uint64_t dw = sw128_desc(st + kk * kUmmaK * 2);
+            umma_bf16(d, dw, sw128_desc(st + G::kW + kk * kUmmaK * 2), idesc, (f != a || kk != 0) ? 1u : 0u);
+            umma_bf16(d, dw, sw128_desc(st + G::kW + G::kX + kk * kUmmaK * 2), idesc, 1u);
+          }
+          umma_commit(empty + s);
+        }
+        if (ok) umma_commit(acc_full + buf);
+        a = b;
+      }
+      if (!ok) {
+        set_flag(p.error_flag, CB_FLAG_WAIT_DATA);
         *abort = 1;
-        break;
       }
-      unsigned char* st = smem + s * G::kStage;
-      const int kx = (c_begin + i) * kChunk;
-      mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(G::kStage));
-      if (seg == 0)
-        tma_load_2d(st, &map_w0, kx, row0, full + s);
-      else if (seg == 1)
-        tma_load_2d(st, &map_w1, kx, row0, full + s);
-      else
-        tma_load_2d(st, &map_w2, kx, row0, full + s);
-      tma_load_2d(st + G::kW, &map_xh, kx, 0, full + s);
-      tma_load_2d(st + G::kW + G::kX, &map_xl, kx, 0, full + s);
+      umma_commit(&mma_done);  // arrives once every MMA issued above has completed
     }
-    for (int t = i - 1; t >= 0 && t >= i - G::kStages; --t) {
-      if (!wait_short(full + t % G::kStages, static_cast<uint32_t>((t / G::kStages) & 1))) {
-        if (p.error_flag != nullptr) atomicCAS(p.error_flag, 0, CB_FLAG_WAIT_DRAIN);
-        break;
-      }
-    }
-  } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = idesc_bf16(kWTile, NB < 16 ? 16 : NB);
-    for (int i = 0; i < nchunks; ++i) {
-      const int s = i % G::kStages, round = i / G::kStages;
-      if (!wait_or_abort(full + s, static_cast<uint32_t>(round & 1), abort)) {
-        if (p.error_flag != nullptr) atomicCAS(p.error_flag, 0, CB_FLAG_WAIT_DATA);
+  } else {
+    // ---- epilogue: warps 0-3, thread = weight row of the tile ----
+    const int r = warp * 32 + lane;
+    const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    int seg_no = 0, splits_done = 0;
+    for (long long a = f0; a < f1; ++seg_no) {
+      const long long tile_flat = a / p.kchunks;
+      const long long b = min(f1, (tile_flat + 1) * p.kchunks);
+      const int buf = seg_no & 1;
+      if (!__all_sync(0xffffffffu, wait_or_abort(acc_full + buf, static_cast<uint32_t>((seg_no >> 1) & 1), abort))) {
+        set_flag(p.error_flag, CB_FLAG_WAIT_DATA);
         *abort = 1;
         break;
       }
       fence_after();
-      const unsigned char* st = smem + s * G::kStage;
-#pragma unroll
-      for (int kk = 0; kk < kChunk / kUmmaK; ++kk) {
-        const uint64_t dw = sw128_desc(st + kk * kUmmaK * 2);
-        umma_bf16(tmem, dw, sw128_desc(st + G::kW + kk * kUmmaK * 2), idesc, (i | kk) != 0 ? 1u : 0u);
-        umma_bf16(tmem, dw, sw128_desc(st + G::kW + G::kX + kk * kUmmaK * 2), idesc, 1u);
-      }
-      umma_commit(empty + s);
-    }
-    umma_commit(&acc_full);
-  }
-  __syncwarp();
-
-  bool ok = wait_or_abort(&acc_full, 0u, abort) || wait_short(&acc_full, 0u);
-  ok = __all_sync(0xffffffffu, ok && *abort == 0 && nchunks > 0);
-  fence_after();
-  const int r = warp * 32 + lane;  // weight row within the tile
-  const int row = row0 + r;
-  const int n = p.n[seg];
-  float* out = p.out[seg];
-  const long long ldo = p.ldo[seg];
-  if (p.splits == 1) {
-    if (ok) {
+      int tile = static_cast<int>(tile_flat), seg = 0;
+      while (seg + 1 < p.n_w && tile >= p.tiles[seg]) tile -= p.tiles[seg++];
+      const int row = tile * kWTile + r;
+      const int n = p.n[seg];
+      float* out = p.out[seg];
+      const long long ldo = p.ldo[seg];
+      const bool whole = a == tile_flat * p.kchunks && b == (tile_flat + 1) * p.kchunks;
+      const long long c_first = cta_of(tile_flat * p.kchunks, p.total, gridDim.x);
+      float* mine = p.partial + ((tile_flat * p.max_parts + (blockIdx.x - c_first)) * NB) * kWTile;
 #pragma unroll 1
       for (int c0 = 0; c0 < NB; c0 += 16) {
         float v[16];
-        tmem_load16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(c0), v);
-        if (row < n) {
+        tmem_load16(lanes + static_cast<uint32_t>(buf * G::kAcc + c0), v);
+        if (whole) {
+          if (row < n) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (c0 + e < p.rows) out[static_cast<long long>(c0 + e) * ldo + row] = v[e];
+            for (int e = 0; e < 16; ++e)
+              if (c0 + e < p.rows) out[static_cast<long long>(c0 + e) * ldo + row] = v[e];
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) mine[(c0 + e) * kWTile + r] = v[e];
         }
       }
-    }
-  } else {
-    float* mine = p.partial + (static_cast<long long>(tile) * p.splits + split) * NB * kWTile;
-#pragma unroll 1
-    for (int c0 = 0; c0 < NB; c0 += 16) {
-      float v[16];
-      if (ok) {
-        tmem_load16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(c0), v);
-      } else {
+      fence_before();
+      mbar_arrive(acc_empty + buf);  // the accumulator is free for segment seg_no + 2
+      if (!whole) {
+        // every thread's partial is visible GPU-wide before thread 0 takes
+        // the tile's ticket; the last part sums all parts in part order
+        const int parts = cta_of((tile_flat + 1) * p.kchunks - 1, p.total, gridDim.x) - static_cast<int>(c_first) + 1;
+        const uint32_t phase = static_cast<uint32_t>(splits_done & 1);
+        __threadfence();
+        mbar_arrive(&parts_in);
+        if (r == 0) {
+          const bool in = wait_or_abort(&parts_in, phase, abort);
+          if (!in) set_flag(p.error_flag, CB_FLAG_WAIT_DATA);
+          last_part[splits_done & 1] =
+              in && atomicAdd(p.counters + tile_flat, 1u) == static_cast<unsigned>(parts - 1);
+          mbar_arrive(&ticket_out);
+        }
+        if (!__all_sync(0xffffffffu, wait_or_abort(&ticket_out, phase, abort))) {
+          set_flag(p.error_flag, CB_FLAG_WAIT_DATA);
+          *abort = 1;
+          break;
+        }
+        if (last_part[splits_done & 1]) {
+          // thread t sums 4 weight rows (float4 group t % 32) for batch rows
+          // t / 32 + 4 j, every part in order; 8 batch rows per batch of
+          // loads, all in flight together
+          __threadfence();
+          const float4* base = reinterpret_cast<const float4*>(p.partial + tile_flat * p.max_parts * NB * kWTile);
+          const int g = r & 31, b0 = r >> 5;
+          const int row4 = tile * kWTile + 4 * g;
+          for (int bs = b0; bs < p.rows; bs += 32) {
+            float4 acc[8];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = 0.0f;
-      }
+            for (int j = 0; j < 8; ++j) acc[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int q = 0; q < parts; ++q) {
+              float4 v[8];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) mine[(c0 + e) * kWTile + r] = v[e];
-    }
-    if (!ok && threadIdx.x == 0 && nchunks > 0 && p.error_flag != nullptr) atomicCAS(p.error_flag, 0, CB_FLAG_WAIT_DATA);
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) last_split = atomicAdd(p.counters + tile, 1u) == static_cast<unsigned>(p.splits - 1);
-    __syncthreads();
-    if (last_split) {
-      __threadfence();
-      const float* base = p.partial + static_cast<long long>(tile) * p.splits * NB * kWTile;
-      for (int b = 0; b < p.rows; ++b) {
-        float acc = 0.0f;
-        for (int s = 0; s < p.splits; ++s) acc += __ldcg(base + (static_cast<long long>(s) * NB + b) * kWTile + r);
-        if (row < n) out[static_cast<long long>(b) * ldo + row] = acc;
+              for (int j = 0; j < 8; ++j) {
+                const int bb = bs + 4 * j;
+                v[j] = bb < p.rows ? __ldcg(base + ((static_cast<long long>(q) * NB + bb) * kWTile) / 4 + g)
+                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                acc[j].x += v[j].x;
+                acc[j].y += v[j].y;
+                acc[j].z += v[j].z;
+                acc[j].w += v[j].w;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int bb = bs + 4 * j;
+              if (bb >= p.rows) continue;
+              float* o = out + static_cast<long long>(bb) * ldo;
+              const float a4[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                if (row4 + e < n) o[row4 + e] = a4[e];
+            }
+          }
+          if (r == 0) p.counters[tile_flat] = 0u;
+        }
+        ++splits_done;
       }
-      if (threadIdx.x == 0) p.counters[tile] = 0u;
+      a = b;
     }
   }
+  __syncwarp();
   fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, G::kTmemCols);
+  if (warp == 0) {
+    // TMEM is freed only after every MMA that writes it has completed
+    if (!wait_short(&mma_done, 0u) && lane == 0) set_flag(p.error_flag, CB_FLAG_WAIT_DRAIN);
+    fence_after();
+    tmem_dealloc(tmem, G::kTmemCols);
+  }
 }
 
-// x rows (float32 or bf16, row stride ldx) -> bf16 planes hi, lo (rows x k).
+// x rows (float32 or bf16, row stride ldx) -> bf16 planes hi, lo (rows x k);
+// grid (rows, k chunks of 1024).
 __global__ void rows_planes_kernel(const void* x, int x_dtype, long long ldx, long long k, __nv_bfloat16* hi,
                                    __nv_bfloat16* lo) {
   const long long r = blockIdx.x;
-  for (long long c = threadIdx.x; c < k; c += blockDim.x) {
+  const long long c1 = min(k, (blockIdx.y + 1) * 1024LL);
+  for (long long c = blockIdx.y * 1024LL + threadIdx.x; c < c1; c += blockDim.x) {
     const float v = load_as_f32(x, r * ldx + c, x_dtype);
     const __nv_bfloat16 h = __float2bfloat16_rn(v);
     hi[r * k + c] = h;
@@ -214,24 +322,31 @@ __global__ void rows_planes_kernel(const void* x, int x_dtype, long long ldx, lo
 int padded_rows(long long rows) { return rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256; }
 
 struct RowsPlan {
-  int nb, tiles, splits, kchunks;
-  long long plane_elems, partial_floats;
+  int nb, tiles, kchunks, grid, max_parts;
+  long long total, plane_elems, partial_floats;
 };
+
+// The CTA range holding flattened chunk f (host copy of cta_of).
+long long host_cta_of(long long f, long long total, long long grid) { return ((f + 1) * grid + total - 1) / total - 1; }
 
 RowsPlan plan_rows(const cb_gemm_rows_args& a, int sms) {
   RowsPlan r{};
   r.nb = padded_rows(a.rows);
   r.kchunks = static_cast<int>((a.k + kChunk - 1) / kChunk);
   for (int i = 0; i < a.n_w; ++i) r.tiles += static_cast<int>((a.w_rows[i] + kWTile - 1) / kWTile);
-  // spread the weight stream over about two CTAs per SM, at least 4 K chunks per split
-  int splits = a.splits > 0 ? a.splits : (2 * sms + r.tiles - 1) / r.tiles;
-  const int most = r.kchunks / 4 > 0 ? r.kchunks / 4 : 1;
-  splits = splits < 1 ? 1 : splits;
-  splits = splits > most ? most : splits;
-  splits = splits > 16 ? 16 : splits;
-  r.splits = splits;
+  r.total = static_cast<long long>(r.tiles) * r.kchunks;
+  // one persistent CTA per SM (a.splits > 0: that many CTAs), each streaming an equal range
+  long long grid = a.splits > 0 ? a.splits : sms;
+  if (grid > r.total) grid = r.total;
+  if (grid < 1) grid = 1;
+  r.grid = static_cast<int>(grid);
+  r.max_parts = 1;
+  for (long long t = 0; t < r.tiles; ++t) {
+    const long long parts = host_cta_of((t + 1) * r.kchunks - 1, r.total, grid) - host_cta_of(t * r.kchunks, r.total, grid) + 1;
+    if (parts > r.max_parts) r.max_parts = static_cast<int>(parts);
+  }
   r.plane_elems = a.rows * a.k;
-  r.partial_floats = splits > 1 ? static_cast<long long>(r.tiles) * splits * r.nb * kWTile : 0;
+  r.partial_floats = r.max_parts > 1 ? static_cast<long long>(r.tiles) * r.max_parts * r.nb * kWTile : 0;
   return r;
 }
 
@@ -240,7 +355,8 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
   using G = RowsShape<NB>;
   __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(a.scratch);
   __nv_bfloat16* lo = hi + pl.plane_elems;
-  rows_planes_kernel<<<static_cast<unsigned>(a.rows), 256, 0, s>>>(a.x, a.x_dtype, a.ldx, a.k, hi, lo);
+  const dim3 pgrid(static_cast<unsigned>(a.rows), static_cast<unsigned>((a.k + 1023) / 1024));
+  rows_planes_kernel<<<pgrid, 256, 0, s>>>(a.x, a.x_dtype, a.ldx, a.k, hi, lo);
   CB_REQUIRE(cudaGetLastError() == cudaSuccess, "cb_gemm_rows: plane pass launch failed");
   CUtensorMap mw[3], mxh, mxl;
   for (int i = 0; i < 3; ++i) {
@@ -259,15 +375,17 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
   p.n_w = a.n_w;
   p.rows = static_cast<int>(a.rows);
   p.kchunks = pl.kchunks;
-  p.splits = pl.splits;
-  p.partial = reinterpret_cast<float*>(lo + pl.plane_elems + (pl.plane_elems & 1 ? 1 : 0));
+  p.total = pl.total;
+  p.max_parts = pl.max_parts;
+  // partials after the planes, 16-byte aligned
+  const uintptr_t after = reinterpret_cast<uintptr_t>(lo + pl.plane_elems);
+  p.partial = reinterpret_cast<float*>((after + 15) & ~static_cast<uintptr_t>(15));
   p.counters = a.counters;
   p.error_flag = a.error_flag;
   auto kernel = gemm_rows_kernel<NB>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
   if (e == cudaSuccess) {
-    kernel<<<static_cast<unsigned>(pl.tiles * pl.splits), kRowsThreads, G::kSmem, s>>>(mw[0], mw[1], mw[2], mxh,
-                                                                                        mxl, p);
+    kernel<<<static_cast<unsigned>(pl.grid), kRowsThreads, G::kSmem, s>>>(mw[0], mw[1], mw[2], mxh, mxl, p);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
@@ -298,7 +416,7 @@ long long cb_gemm_rows_scratch(const cb_gemm_rows_args* a) {
   if (a == nullptr || a->rows <= 0 || a->k <= 0 || a->n_w < 1 || a->n_w > 3) return 0;
   const RowsPlan pl = plan_rows(*a, sm_count_cached());
   const long long planes = 2 * pl.plane_elems * 2 + 16;  // hi, lo (+ alignment of the partials)
-  return (planes + 15) / 16 * 16 + pl.partial_floats * 4;
+  return (planes + 15) / 16 * 16 + pl.partial_floats * 4 + 16;
 }
 
 long long cb_gemm_rows_counters(const cb_gemm_rows_args* a) {
@@ -321,8 +439,8 @@ int cb_gemm_rows(const cb_gemm_rows_args* a, cb_stream_t stream) {
                "gemm_rows: weight %d shape", i);
   }
   const RowsPlan pl = plan_rows(*a, sm_count_cached());
-  CB_REQUIRE(pl.splits == 1 || a->counters != nullptr, "gemm_rows: split K needs counters");
-  CB_REQUIRE(static_cast<long long>(pl.tiles) * pl.splits < (1LL << 31), "gemm_rows: too many tiles");
+  CB_REQUIRE(pl.max_parts == 1 || a->counters != nullptr, "gemm_rows: split tiles need counters");
+  CB_REQUIRE(pl.total < (1LL << 40) && pl.tiles < (1 << 30), "gemm_rows: too many tiles");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (pl.nb) {
     case 16: return launch_rows<16>(*a, pl, s);

@@ -191,22 +191,26 @@ __global__ void place_columns_kernel(const void* in, int in_dtype, int ndim, Cop
   }
 }
 
-// One block per (batch, head) of the cache; threads scan the write mask and
-// rewrite the rows it selects.
+// Grid (units / 256, batch * heads): one thread per (row, 4 dims) of a
+// head's cache; rows whose write mask is 0 are left alone (the blend is the
+// cache itself there), so only the written row costs more than a mask read.
 __global__ void kv_write_kernel(float* cache, long long heads, long long ctx, long long hd, const void* row,
                                 int row_dtype, long long rs_b, long long rs_h, long long rs_d, const void* wm,
                                 int wm_dtype, int one_minus_dtype) {
-  const long long b = blockIdx.x / heads, h = blockIdx.x % heads;
-  float* base = cache + blockIdx.x * ctx * hd;
+  const long long bh = blockIdx.y;
+  const long long b = bh / heads, h = bh % heads;
+  const long long groups = (hd + 3) / 4;
+  const long long u = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (u >= ctx * groups) return;
+  const long long r = u / groups, d0 = (u % groups) * 4;
+  const float w = load_as_f32(wm, r, wm_dtype);
+  if (w == 0.0f) return;
+  const float keep = round_to(__fsub_rn(1.0f, w), one_minus_dtype);
+  float* base = cache + (bh * ctx + r) * hd;
   const long long rbase = b * rs_b + h * rs_h;
-  for (long long r = threadIdx.x; r < ctx; r += blockDim.x) {
-    const float w = load_as_f32(wm, r, wm_dtype);
-    if (w == 0.0f) continue;
-    const float keep = round_to(__fsub_rn(1.0f, w), one_minus_dtype);
-    for (long long d = 0; d < hd; ++d) {
-      const float x = load_as_f32(row, rbase + d * rs_d, row_dtype);
-      base[r * hd + d] = __fadd_rn(__fmul_rn(base[r * hd + d], keep), __fmul_rn(x, w));
-    }
+  for (long long d = d0; d < d0 + 4 && d < hd; ++d) {
+    const float x = load_as_f32(row, rbase + d * rs_d, row_dtype);
+    base[d] = __fadd_rn(__fmul_rn(base[d], keep), __fmul_rn(x, w));
   }
 }
 
@@ -376,8 +380,10 @@ int cb_kv_write(float* cache, long long batch, long long heads, long long ctx, l
   CB_REQUIRE(cache != nullptr && row != nullptr && write_mask != nullptr, "kv_write: null pointer");
   CB_REQUIRE(batch >= 0 && heads >= 0 && ctx >= 0 && head_size >= 0, "kv_write: negative size");
   if (batch * heads == 0 || ctx == 0) return CB_OK;
-  CB_REQUIRE(batch * heads < (1LL << 31), "kv_write: too many heads");
-  kv_write_kernel<<<static_cast<unsigned>(batch * heads), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+  CB_REQUIRE(batch * heads < 65536 && ctx * ((head_size + 3) / 4) < (1LL << 40), "kv_write: too many heads");
+  const long long units = ctx * ((head_size + 3) / 4);
+  const dim3 grid(static_cast<unsigned>((units + 255) / 256), static_cast<unsigned>(batch * heads));
+  kv_write_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       cache, heads, ctx, head_size, row, row_dtype, row_strides[0], row_strides[1], row_strides[3], write_mask,
       write_mask_dtype, one_minus_dtype);
   return check_launch("cb_kv_write");

@@ -787,6 +787,8 @@ class CudaB200Program(CompiledProgram):
         """Zero every arrival/ticket counter after a kernel wait gave up."""
         if self.step_mode:
             self._step_counters.zero_()
+        if getattr(self, "_rows_counters", None) is not None:
+            self._rows_counters.zero_()
         for step in self.plan.steps:
             for name in ("counters", "counter"):
                 buf = step.args.get(name)

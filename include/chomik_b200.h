@@ -431,8 +431,10 @@ CB_API int cb_gemm_tc(const cb_gemm_args* args, cb_stream_t stream);
  * Linears of a decode step over a batch of 1..256 sequences
  * (chomikgrad/llama.py:275-277, 387-392, 371-380).  float32 x is split into
  * bf16 hi/lo planes (products exact, residual about 2^-16 of |x|); the
- * weight rows are the MMA's 128-row side and K is split across CTAs (splits
- * = 0 chooses), reduced in split order by the last CTA of each weight tile.
+ * weight rows are the MMA's 128-row side.  The (128-row tile, 64-wide K
+ * chunk) sequence is cut into `splits` equal contiguous ranges, one per
+ * persistent CTA (splits = 0: one per SM); a tile cut between CTAs is
+ * reduced in part order by its last part (deterministic).
  * `scratch`: cb_gemm_rows_scratch bytes, 16-byte aligned; `counters`:
  * cb_gemm_rows_counters unsigned ints, zero before the first call (calls
  * leave them zero).  k % 8 == 0. */
