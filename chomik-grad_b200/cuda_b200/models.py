@@ -98,3 +98,29 @@ def synthetic_prompt(config: LlamaConfig, length: int, *, seed: int = 0,
     """(batch, length) uniform token ids in [0, vocab)."""
     rng = np.random.default_rng(seed + 1)
     return rng.integers(0, config.vocab_size, size=(batch, length)).astype(np.int32)
+
+
+def device_weights(config: LlamaConfig, *, device, seed: int = 0, std: float = 0.02, layout=None):
+    """Seeded random-init bf16 weights drawn on the GPU (torch), optionally one rank's shards.
+
+    For the large benchmark shapes (Llama-3-8B: 8 billion values), where the
+    host-side ``synthetic_weights`` takes minutes.  Tensor k (in
+    ``required_weight_shapes`` order) comes from a CUDA generator seeded with
+    ``seed * 1000003 + k``; norm weights are 1.  With ``layout`` (a
+    ``tensor_parallel.ShardLayout``) each full tensor is drawn, then only this
+    rank's shard is kept, so every rank's shards come from the same tensors.
+    """
+    import torch
+
+    from .tensor_parallel import shard_weights
+
+    out = {}
+    gen = torch.Generator(device=device)
+    for index, (name, shape) in enumerate(required_weight_shapes(config).items()):
+        if name.endswith("norm.weight"):
+            out[name] = torch.ones(shape, dtype=torch.bfloat16, device=device)
+            continue
+        gen.manual_seed(seed * 1000003 + index)
+        full = (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
+        out[name] = shard_weights(config, {name: full}, layout)[name] if layout is not None else full
+    return out

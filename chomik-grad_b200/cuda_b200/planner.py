@@ -238,7 +238,7 @@ def _collect_buffers(value, acc: Set[int]) -> None:
 class Planner:
     """Builds a :class:`Plan` from output nodes (see module docstring)."""
 
-    SUPPORTED_LOWERINGS = frozenset({"rms_norm", "rope", "sdpa"})
+    SUPPORTED_LOWERINGS = frozenset({"rms_norm", "rope", "sdpa", "all_reduce"})
 
     def __init__(self, outputs: Sequence[object], dynamic_inputs: Sequence[object], *,
                  backend: str, leaf_dtype, max_positions: int = 8192,
@@ -314,6 +314,8 @@ class Planner:
             return low
         if kind_ == "sdpa" and self._match_sdpa(node, low):
             return low
+        if kind_ == "all_reduce" and self._match_all_reduce(node, low):
+            return low
         return None
 
     def _parents(self, node):
@@ -359,6 +361,15 @@ class Planner:
         except Exception:
             return None
         return float(value.reshape(-1)[0].astype(np.float32))
+
+    def _match_all_reduce(self, node, low) -> bool:
+        """out = x * 1: the portable form of a tensor-parallel sum (cuda_b200.tensor_parallel)."""
+        if not is_ew(node, "mul") or len(low[1]) != 1 or not isinstance(low[2], str):
+            return False
+        x = low[1][0]
+        if len(node.inputs) != 2 or node.inputs[0] is not x or self._const(node.inputs[1]) != 1.0:
+            return False
+        return self.rdt(x).name in ("float32", "bfloat16")
 
     def _match_rms(self, node, low) -> bool:
         """out = x / sqrt(sum(x*x, -1, keepdims)/c + eps) * w (llama.py:279-287)."""
@@ -936,6 +947,14 @@ class Planner:
         if np.all(value[:, ~above] == 0.0):
             flags |= _lib.CAUSAL_ZERO_BELOW
         return flags
+
+    def _emit_all_reduce(self, node, low) -> None:
+        src = self.contiguous(self.value(low[1][0]))
+        out = self.tmp(node.shape, src.dtype)
+        self.plan.lowered["all_reduce"] = self.plan.lowered.get("all_reduce", 0) + 1
+        self.add_step("all_reduce", out, f"all_reduce({self._name(src)}, group={low[2]!r})", src=src,
+                      group=low[2])
+        self.set_value(node, out)
 
     def _emit_sdpa(self, node, low) -> None:
         q, k, v, mask = (self.value(p) for p in low[1])

@@ -542,6 +542,13 @@ class CudaB200Program(CompiledProgram):
                 target[d] = 0 if j < 0 or view.shape[j] == 1 else view.strides[j]
         _lib.call("cb_matmul", ctypes.byref(a), stream)
 
+    def _step_all_reduce(self, step: Step, stream: int) -> None:
+        from . import parallel
+
+        src: View = step.args["src"]
+        parallel.get_group(step.args["group"]).all_reduce(self.ptr(src), self.ptr(step.out), src.size,
+                                                          _lib.dtype_code(src.dtype), stream)
+
     def _step_kv_write(self, step: Step, stream: int) -> None:
         cache: View = step.args["cache"]
         row: View = step.args["row"]

@@ -458,6 +458,20 @@ CB_API long long cb_gemm_rows_scratch(const cb_gemm_rows_args* args);
 CB_API long long cb_gemm_rows_counters(const cb_gemm_rows_args* args);
 CB_API int cb_gemm_rows(const cb_gemm_rows_args* args, cb_stream_t stream);
 
+/* ---- tensor-parallel collectives ------------------------------------------
+ * The reference is single-GPU; these serve the tensor-parallel lowering of
+ * its graphs (all_reduce after the row-sharded O and down projections).  A
+ * sum all-reduce over NCCL, loaded at run time (cb_comm_load: a libnccl.so.2
+ * path, or NULL for the one the process already has).  cb_comm_unique_id
+ * writes NCCL's 128-byte id on one rank; every rank passes it to
+ * cb_comm_init.  cb_all_reduce(src -> dst, count elements, CB_F32 or CB_BF16)
+ * is issued on `stream`, so a CUDA graph captured on that stream holds it. */
+CB_API int cb_comm_load(const char* path);
+CB_API int cb_comm_unique_id(void* out, int bytes);
+CB_API int cb_comm_init(const void* id, int bytes, int nranks, int rank, void** comm);
+CB_API int cb_comm_destroy(void* comm);
+CB_API int cb_all_reduce(void* comm, const void* src, void* dst, long long count, int dtype, cb_stream_t stream);
+
 /* ---- whole decode step in one launch --------------------------------------
  * The fused decode step of LlamaDecoderStep (chomikgrad/llama.py:469-543)
  * -- per layer the norm->QKV GEMV, RoPE + cache blend + attention, O GEMV +
