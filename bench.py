@@ -24,6 +24,12 @@ Reported:
   prefill    the prefill-heavy config on the same weights: 8 prompts of 2048
              tokens per step (tcgen05 GEMMs and flash attention), tokens/s
              and FLOP/s against the measured bf16 tensor peak.
+  bs32       batched decode of 32 sequences (one BatchedDecoderStep program,
+             tcgen05 row GEMMs, split-key attention), graph replays; per rank.
+  llama3_8b_tp  Llama-3-8B shape, 16 sequences of 1024-token prompts, prefill
+             then batched decode, tensor-parallel over all N ranks (TP = N,
+             NCCL all-reduce inside each rank's decode graph); tokens/s of the
+             group and the fraction of the group's aggregate HBM bandwidth.
   cpu_baseline  the parity oracle (restated reference cpu compiler, NumPy +
              ml_dtypes) timing real decode steps of the same model on the host.
 Inputs are larger than L2 (2.07 GB of weights per step), so no flush is needed.
@@ -48,7 +54,8 @@ for _p in (ROOT / "chomik-grad_b200", ROOT):
 
 import numpy as np  # noqa: E402
 
-METRIC = "decode tokens/sec (bs=1; bs=32 in the bs32 object) and % of HBM roofline"
+METRIC = ("decode tokens/sec (bs=1; bs=32 in the bs32 object; Llama-3-8B bs16 tensor-parallel in "
+          "llama3_8b_tp) and % of HBM roofline")
 # DRAM bytes of one gate/up GEMV launch from an ncu capture, per workload
 GATEUP_TRAFFIC = {"tinyllama-bf16-bs1": 56_449_792 + 45_312}
 # DRAM bytes of one cb_decode_step launch from an ncu capture, per workload
@@ -419,6 +426,78 @@ def batched_measurement(cfg, weights, rank: int, world: int, steps: int, warmup:
     }
 
 
+def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: int, prompt_len: int) -> dict:
+    """Llama-3-8B shape, batch 16, tensor-parallel over all ranks (TP = world size).
+
+    Weights are random-init bf16 drawn on each GPU (cuda_b200.models.device_weights)
+    and sharded by cuda_b200.tensor_parallel; the all-reduce after the O and
+    down projections is an NCCL step inside each rank's captured decode graph.
+    Tokens per step are the 16 sequences (shared by every rank).
+    """
+    import torch
+
+    from cuda_b200 import parallel, tensor_parallel as tp
+    from cuda_b200.models import WORKLOADS, bfloat16, device_weights, synthetic_prompt
+    from cuda_b200.frontend.llama import required_weight_shapes
+
+    wl = WORKLOADS["llama3-8b-bf16-bs16"]
+    cfg = wl.config
+    if world > 1:
+        parallel.init_group("tp")
+    layout = tp.shard_layout(cfg, world, rank)
+    weights = device_weights(cfg, device=torch.device("cuda", local), layout=layout)
+    rt = tp.TensorParallelRuntime(cfg, weights, layout, batch=wl.batch, dtype=bfloat16())
+    context = prompt_len + wl.decode_steps
+    prompts = [list(p) for p in synthetic_prompt(cfg, prompt_len, seed=300, batch=wl.batch)]
+    rt.prefill(prompts[0], context)  # compile + capture
+    rt.prefill(prompts[0], context)
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    tokens, caches = rt.prefill_batch(prompts, context)
+    t1.record()
+    t1.synchronize()
+    prefill_ms = reduce_max(t0.elapsed_time(t1), world)
+    rt.decode_batch_on_device(tokens, prompt_len, context, caches, max(warmup, 3))
+    barrier(world)
+    replay_ms: list = []
+    per_chunk = context - prompt_len - 2
+    elapsed, done = 0.0, 0
+    while done < steps:
+        n = min(per_chunk, steps - done)
+        _, ms = rt.decode_batch_on_device(tokens, prompt_len, context, caches, n + 1, replay_times=replay_ms)
+        elapsed += ms
+        done += n
+    slowest = reduce_max(elapsed, world)
+    step_ms = reduce_max(statistics.fmean(replay_ms), world)
+    rt.close()  # release the graphs that hold NCCL work before the communicator
+    if world > 1:
+        barrier(world)
+        parallel.destroy_group("tp")
+    peak, peak_kind = measured_peaks()
+    flops = json.loads(PEAKS.read_text())["bf16_tflops"] if PEAKS.exists() else 1590.0
+    weight_bytes_model = sum(int(np.prod(s)) for n, s in required_weight_shapes(cfg).items()
+                             if n != "model.embed_tokens.weight") * 2
+    kv_bytes = wl.batch * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * 4 * context
+    step_bytes = weight_bytes_model + kv_bytes
+    achieved = step_bytes / (step_ms / 1000.0) / 1e9
+    pflops = prefill_flops(cfg, prompt_len) * wl.batch / (prefill_ms / 1000.0) / 1e12
+    return {
+        "workload": wl.name, "tensor_parallel": world, "sequences": wl.batch, "prompt_tokens": prompt_len,
+        "context": context, "value": steps * wl.batch / (slowest / 1000.0), "unit": "tokens/s",
+        "ms_per_step": step_ms,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
+                     "frac": achieved / (peak * world), "bytes_per_step": step_bytes,
+                     "basis": "bf16 weights (embedding excluded, lm_head once) + float32 K/V over the context, "
+                              "per step of 16 tokens, against the aggregate HBM bandwidth of the group",
+                     "peak_source": peak_kind},
+        "prefill": {"value": wl.batch * prompt_len / (prefill_ms / 1000.0), "unit": "tokens/s",
+                    "ms": prefill_ms, "tflops": pflops, "frac_of_bf16_peak": pflops / (flops * world)},
+        "data": "random-init bf16 weights drawn on the GPU (seeded), uniform random prompt ids",
+    }
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -431,6 +510,9 @@ def main() -> None:
                         help="batched decode steps (32 sequences each) of the bs32 measurement; 0 skips it")
     parser.add_argument("--prefill-steps", type=int, default=2,
                         help="steps (8 prompts of 2048 tokens each) of the prefill measurement; 0 skips it")
+    parser.add_argument("--llama3-steps", type=int, default=30,
+                        help="tensor-parallel Llama-3-8B bs16 decode steps (TP = GPUs); 0 skips it")
+    parser.add_argument("--llama3-prompt", type=int, default=1024, help="Llama-3-8B prompt tokens")
     args = parser.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -553,6 +635,9 @@ def main() -> None:
         line["bs32"] = batched_measurement(cfg, weights, rank, world, args.bs32_steps, args.warmup)
     if args.prefill_steps > 0 and WORKLOADS["tinyllama-bf16-prefill-bs8"].config == cfg:
         line["prefill"] = prefill_measurement(rt, cfg, rank, world, args.prefill_steps, 1)
+    if args.llama3_steps > 0 and args.workload == "tinyllama-bf16-bs1":
+        line["llama3_8b_tp"] = llama3_measurement(rank, world, local, args.llama3_steps, args.warmup,
+                                                  args.llama3_prompt)
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, weights).items()
                                 if k in ("value", "unit", "cores", "kind", "sample")}
