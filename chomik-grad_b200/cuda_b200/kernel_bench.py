@@ -1,0 +1,170 @@
+"""Microbenchmarks of single kernels and of the batched decode step (needs a B200).
+
+    python -m cuda_b200.kernel_bench sdpa_tc   [--tokens 2048 --heads 32 --kv 4 --hd 64 --causal 3]
+    python -m cuda_b200.kernel_bench gemm_tc   [--m 2048 --n 5632 --k 2048]
+    python -m cuda_b200.kernel_bench sdpa_query [--batch 32 --heads 32 --kv 4 --tokens 768 --hd 64]
+    python -m cuda_b200.kernel_bench batched   [--workload tinyllama-bf16-bs32 --steps 20 --prompt 64]
+
+Each prints CUDA-event times (warm, averaged over --reps launches on the
+current stream).  ``batched`` wraps the timed graph replays in
+cudaProfilerStart/Stop, so ``ncu --profile-from-start off`` sees only them.
+Inputs are random; these time kernels, they do not check results (the
+``-m gpu`` tests do).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import statistics
+
+import numpy as np
+
+
+def _timed(fn, reps: int) -> float:
+    import torch
+
+    fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        fn()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / reps
+
+
+def _sdpa_args(q, k, v, mask, out, divisor: float):
+    import torch
+
+    from . import _lib
+
+    a = _lib.SdpaArgs()
+    for name, t in (("q", q), ("k", k), ("v", v), ("mask", mask)):
+        setattr(a, name, t.data_ptr())
+        setattr(a, f"{name}_dtype", _lib.F32 if t.dtype == torch.float32 else _lib.BF16)
+        strides = getattr(a, f"{name}_strides")
+        for d in range(4):
+            strides[d] = 0 if t.shape[d] == 1 else t.stride(d)
+    a.out = out.data_ptr()
+    a.batch, a.heads, a.tq, a.head_size = q.shape
+    a.kv_heads, a.tk = k.shape[1], k.shape[2]
+    a.divisor = divisor
+    return a
+
+
+def sdpa_tc(args) -> None:
+    import torch
+
+    from . import _lib
+
+    b, h, kv, t, hd = 1, args.heads, args.kv, args.tokens, args.hd
+    q = torch.randn(b, h, t, hd, device="cuda")
+    k = torch.randn(b, kv, t, hd, device="cuda")
+    v = torch.randn(b, t, kv, hd, device="cuda").permute(0, 2, 1, 3)  # strided, like the model's v
+    i, j = torch.arange(t)[:, None], torch.arange(t)[None, :]
+    mask = torch.where(j > i, -1e4, 0.0).to(torch.bfloat16).reshape(1, 1, t, t).cuda()
+    out = torch.empty(b, h, t, hd, device="cuda")
+    a = _sdpa_args(q, k, v, mask, out, float(np.sqrt(hd)))
+    lib = _lib.load()
+    scratch = torch.empty(lib.cb_sdpa_tc_scratch(ctypes.byref(a)), dtype=torch.uint8, device="cuda")
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    ms = _timed(lambda: _lib.call("cb_sdpa_tc", ctypes.byref(a), args.causal, scratch.data_ptr(),
+                                  flag.data_ptr(), stream), args.reps)
+    flops = 4.0 * b * h * t * t * hd * (0.5 if args.causal else 1.0)
+    print(f"cb_sdpa_tc heads {h}/{kv} tokens {t} hd {hd} causal {args.causal}: {ms * 1000:.1f} us, "
+          f"{flops / ms / 1e9:.1f} TFLOP/s of the reference's products, error flag {int(flag.item())}")
+
+
+def gemm_tc(args) -> None:
+    import torch
+
+    from . import _lib
+
+    m, n, k = args.m, args.n, args.k
+    a_t = torch.randn(m, k, device="cuda")
+    b_t = (torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16)
+    c_t = torch.empty(m, n, device="cuda")
+    g = _lib.GemmArgs()
+    g.a, g.a_dtype, g.lda = a_t.data_ptr(), _lib.F32, k
+    g.b, g.ldb, g.c, g.ldc = b_t.data_ptr(), k, c_t.data_ptr(), n
+    g.m, g.n, g.k = m, n, k
+    lib = _lib.load()
+    scratch = torch.empty(lib.cb_gemm_tc_scratch(ctypes.byref(g)), dtype=torch.uint8, device="cuda")
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    g.a_split, g.error_flag = scratch.data_ptr(), flag.data_ptr()
+    stream = torch.cuda.current_stream().cuda_stream
+    ms = _timed(lambda: _lib.call("cb_gemm_tc", ctypes.byref(g), stream), args.reps)
+    print(f"cb_gemm_tc float32 A {m}x{k}, W {n}x{k}: {ms * 1000:.1f} us, {2 * m * n * k / ms / 1e9:.0f} TFLOP/s "
+          f"of the reference's product, error flag {int(flag.item())}")
+
+
+def sdpa_query(args) -> None:
+    import torch
+
+    from . import _lib
+
+    b, h, kv, t, hd = args.batch, args.heads, args.kv, args.tokens, args.hd
+    q = torch.randn(b, h, 1, hd, device="cuda")
+    k = torch.randn(b, kv, t, hd, device="cuda")
+    v = torch.randn(b, kv, t, hd, device="cuda")
+    mask = torch.zeros(1, 1, 1, t, device="cuda")
+    out = torch.empty(b, h, 1, hd, device="cuda")
+    a = _sdpa_args(q, k, v, mask, out, float(np.sqrt(hd)))
+    lib = _lib.load()
+    scratch = torch.empty(lib.cb_sdpa_query_scratch(ctypes.byref(a)), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    ms = _timed(lambda: _lib.call("cb_sdpa_query", ctypes.byref(a), scratch.data_ptr(), stream), args.reps)
+    print(f"cb_sdpa_query batch {b} heads {h}/{kv} keys {t} hd {hd}: {ms * 1000:.1f} us, "
+          f"{2 * b * kv * t * hd * 4 / ms / 1e6:.0f} GB/s of K/V")
+
+
+def batched(args) -> None:
+    import torch
+
+    from .batched import BatchedRuntime
+    from .models import WORKLOADS, synthetic_prompt, synthetic_weights
+
+    wl = WORKLOADS[args.workload]
+    cfg = wl.config
+    rt = BatchedRuntime(cfg, synthetic_weights(cfg, dtype=wl.np_dtype), batch=wl.batch)
+    prompts = [list(p) for p in synthetic_prompt(cfg, args.prompt, batch=wl.batch)]
+    tokens, caches = rt.prefill_batch(prompts, wl.context)
+    rt.decode_batch_on_device(tokens, args.prompt, wl.context, caches, 4)
+    torch.cuda.synchronize()
+    times: list = []
+    torch.cuda.profiler.start()
+    rt.decode_batch_on_device(tokens, args.prompt, wl.context, caches, args.steps, replay_times=times)
+    torch.cuda.profiler.stop()
+    step = statistics.fmean(times)
+    print(f"{wl.name}: graph replay {step:.3f} ms per step, {wl.batch / step * 1000:.0f} tokens/s")
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("kernel", choices=("sdpa_tc", "gemm_tc", "sdpa_query", "batched"))
+    parser.add_argument("--reps", type=int, default=20)
+    parser.add_argument("--tokens", type=int, default=None)
+    parser.add_argument("--heads", type=int, default=32)
+    parser.add_argument("--kv", type=int, default=None)
+    parser.add_argument("--hd", type=int, default=64)
+    parser.add_argument("--causal", type=int, default=3)
+    parser.add_argument("--batch", type=int, default=32)
+    parser.add_argument("--m", type=int, default=2048)
+    parser.add_argument("--n", type=int, default=5632)
+    parser.add_argument("--k", type=int, default=2048)
+    parser.add_argument("--workload", default="tinyllama-bf16-bs32")
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--prompt", type=int, default=64)
+    args = parser.parse_args()
+    if args.kv is None:
+        args.kv = 4
+    if args.tokens is None:
+        args.tokens = 2048 if args.kernel == "sdpa_tc" else 768
+    {"sdpa_tc": sdpa_tc, "gemm_tc": gemm_tc, "sdpa_query": sdpa_query, "batched": batched}[args.kernel](args)
+
+
+if __name__ == "__main__":
+    main()
