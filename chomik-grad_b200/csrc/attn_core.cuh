@@ -277,16 +277,16 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
   if (stamps != nullptr && tid == 0) stamps[2] = stamps[3] = global_ns();
   if (!merge) return;
 
-  // merge the splits of this KV group in split order
-  __threadfence();
+  // merge the splits of this KV group in split order; the barrier orders every
+  // thread's partial before thread 0's release, whose acquire side (the last
+  // item's thread 0, then its barrier) makes all partials visible there
   attn_sync();
   if (tid == 0) {
-    const unsigned ticket = atomicAdd(a.counters + g, 1u);
+    const unsigned ticket = ticket_acq_rel(a.counters + g);
     *s_last = ticket == static_cast<unsigned>(splits - 1);
   }
   attn_sync();
   if (!*s_last) return;
-  __threadfence();
   for (int i = tid; i < group * half; i += kAttnThreads) {  // two dims of one head per thread
     const long long e0 = (static_cast<long long>(g) * group + i / half) * HD + (i % half) * 2;
     float merged[8];

@@ -594,13 +594,11 @@ __device__ void gemv_phase(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>
     }
     a.scratch_val[blockIdx.x] = bv;
     a.scratch_idx[blockIdx.x] = bi;
-    __threadfence();
-    const unsigned ticket = atomicAdd(a.counter, 1u);
+    const unsigned ticket = ticket_acq_rel(a.counter);  // releases this block's partial
     sh.last = ticket == gridDim.x - 1;
   }
   consumers_sync(N);
   if (!sh.last) return;  // block-uniform: the last block merges with all its consumer threads
-  __threadfence();
   const long long bi = argmax_merge(a.scratch_val, a.scratch_idx, static_cast<int>(gridDim.x), tid, N,
                                     sh.warp_best_v, sh.warp_best_i);
   if (tid == 0) {
@@ -818,9 +816,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     consumers_sync(kAttnThreads);  // ... and this block's phase-p writes are issued
     if (tid == 0) stamp(S, p, kStampDone);
     if (tid == 0 && *reinterpret_cast<volatile int*>(&sh.stop) == 0) {
-      __threadfence();
-      const unsigned arrived = atomicAdd(S.counters + p, 1u);
-      if (p == S.n_phases - 1 && arrived == static_cast<unsigned>(S.grid) - 1) {
+      if (p < S.n_phases - 1) {
+        arrive_release(S.counters + p);  // the barrier above ordered the block's writes
+      } else if (ticket_acq_rel(S.counters + p) == static_cast<unsigned>(S.grid) - 1) {
         // every block has finished every phase: zero the counters for the next step
         for (int q = 0; q < S.n_phases; ++q) S.counters[q] = 0u;
         __threadfence();

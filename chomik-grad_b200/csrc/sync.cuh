@@ -85,6 +85,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   return false;
 }
 
+// Grid-wide arrivals and tickets with release/acquire ordering instead of a
+// full fence: the caller's block barrier orders its threads' earlier writes
+// before the arriving thread, and a release at gpu scope is cumulative over
+// them, so they are visible to whoever acquires the counter value.
+__device__ __forceinline__ void arrive_release(unsigned* counter) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+}
+__device__ __forceinline__ unsigned ticket_acq_rel(unsigned* counter) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  return old;
+}
+
 // Bulk copy global -> this CTA's shared memory, completing `bytes` of the
 // barrier's transaction count.  dst/src 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
