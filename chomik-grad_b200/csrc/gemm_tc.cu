@@ -1,17 +1,27 @@
-// Tensor-core GEMM for sm_100a: cb_gemm_tc, C (m x n, float32) = A (m x k) x B^T,
-// B the (n x k) bf16 weight of a Linear layer.
+// Tensor-core GEMM for sm_100a: cb_gemm_tc / cb_gemm_tc_multi,
+// C (m x n, float32) = A (m x k) x B^T, B the (n x k) bf16 weight of a Linear
+// layer (chomikgrad/llama.py:275-277), with three epilogues:
+//  * store, for up to three weights that share A (q/k/v of a prefill layer):
+//    one launch, its tiles the concatenation of every weight's tiles;
+//  * residual: C = R + A B^T (the residual add after the O and down
+//    projections, llama.py:529-535), added in float32 before the store;
+//  * SwiGLU: two weights (gate, up) computed on the same output tile into two
+//    TMEM accumulators, stored as silu(g) * u = g / (1 + exp(-g)) * u
+//    (llama.py:289-291, 371-380) -- the gate and up matrices are never
+//    written.
 //
 // One block of 128 threads per 128 x BN output tile (BN = 256 or 128):
 //  * thread 0 streams K in 64-element steps -- one 128-byte swizzle atom of
 //    bf16 -- with TMA (cp.async.bulk.tensor, SWIZZLE_128B) into a ring of
-//    shared-memory stages: A's plane(s) and B per stage, completion counted
-//    on an mbarrier per stage;
+//    shared-memory stages: A's plane(s) and B's (two for SwiGLU) per stage,
+//    completion counted on an mbarrier per stage;
 //  * thread 32 issues tcgen05.mma (kind::f16, bf16 x bf16 -> float32, M=128,
-//    N=BN, K=16 per instruction) from those stages into a float32
-//    accumulator in TMEM, and tcgen05.commit frees each stage when its MMAs
+//    N=BN, K=16 per instruction) from those stages into float32
+//    accumulators in TMEM, and tcgen05.commit frees each stage when its MMAs
 //    have read it;
-//  * after the last commit all four warps read the accumulator back with
-//    tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = tile rows) and store it.
+//  * after the last commit all four warps read the accumulators back with
+//    tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = tile rows), apply the
+//    epilogue and store.
 // A float32 A enters as two bf16 planes (hi = bf16(a), lo = bf16(a - hi)),
 // split by a pre-pass; each K step then issues the MMAs of both planes into
 // the same accumulator.
@@ -31,14 +41,30 @@ constexpr int kBK = kChunk;           // K per stage: one 128-byte swizzle atom 
 constexpr int kGemmThreads = 128;
 constexpr int kStageBudget = 192 * 1024;
 
-template <int BN, int NA>
+enum { kStore = 0, kResidual = 1, kSwiglu = 2 };
+
+template <int BN, int NA, int MODE>
 struct GemmShape {
-  static constexpr int kA = kBM * kBK * 2;  // one A plane of a stage
+  static constexpr int kW = MODE == kSwiglu ? 2 : 1;  // weight chunks per stage
+  static constexpr int kA = kBM * kBK * 2;            // one A plane of a stage
   static constexpr int kB = BN * kBK * 2;
-  static constexpr int kStage = NA * kA + kB;
+  static constexpr int kStage = NA * kA + kW * kB;
   static constexpr int kStages = kStageBudget / kStage;
   static constexpr int kSmem = kStages * kStage + 1024;  // + 1024-byte alignment of the swizzled tiles
+  static constexpr int kTmemCols = kW * BN;
   static_assert(kStages >= 2, "at least double buffering");
+};
+
+struct GemmParams {
+  float* c[3];
+  long long ldc[3];
+  int n[3];        // output columns of each weight
+  int tiles_n[3];  // BN-wide column tiles of each weight (store: 1..3 weights; else 1)
+  int n_seg;
+  int m, k;
+  const float* residual;
+  long long ldr;
+  int* error_flag;
 };
 
 // Tile order: groups of kGroupM row tiles; inside a group the row tile varies
@@ -55,12 +81,16 @@ __device__ __forceinline__ void tile_of(int t, int tiles_m, int tiles_n, int* tm
   *tn = r / rows;
 }
 
-template <int BN, int NA>
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(expf(-g), 1.0f)), u);
+}
+
+template <int BN, int NA, int MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
-                   const __grid_constant__ CUtensorMap map_b, float* __restrict__ c, long long ldc, int m, int n,
-                   int k, int* error_flag) {
-  using G = GemmShape<BN, NA>;
+                   const __grid_constant__ CUtensorMap map_b0, const __grid_constant__ CUtensorMap map_b1,
+                   const __grid_constant__ CUtensorMap map_b2, const __grid_constant__ GemmParams p) {
+  using G = GemmShape<BN, NA, MODE>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -70,12 +100,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_m = (p.m + kBM - 1) / kBM;
+  int t = blockIdx.x, seg = 0;
+  while (seg + 1 < p.n_seg && t >= tiles_m * p.tiles_n[seg]) t -= tiles_m * p.tiles_n[seg++];
   int tm, tn;
-  tile_of(blockIdx.x, (m + kBM - 1) / kBM, (n + BN - 1) / BN, &tm, &tn);
+  tile_of(t, tiles_m, p.tiles_n[seg], &tm, &tn);
   const int m0 = tm * kBM, n0 = tn * BN;
-  const int kblocks = (k + kBK - 1) / kBK;  // the tensor maps zero-fill K past k
+  const int kblocks = (p.k + kBK - 1) / kBK;  // the tensor maps zero-fill K past k
+  const CUtensorMap* mb = seg == 0 ? &map_b0 : seg == 1 ? &map_b1 : &map_b2;
 
-  if (warp == 0) tmem_alloc(&tmem_base, BN);  // the accumulator: BN float32 columns x 128 lanes
+  if (warp == 0) tmem_alloc(&tmem_base, G::kTmemCols);  // the accumulator(s): BN float32 columns x 128 lanes
   if (threadIdx.x == 32) {
     for (int s = 0; s < G::kStages; ++s) {
       mbar_init(full + s, 1);
@@ -96,7 +130,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (; kb < kblocks; ++kb) {
       const int s = kb % G::kStages, round = kb / G::kStages;
       if (round > 0 && !wait_or_abort(empty + s, static_cast<uint32_t>((round - 1) & 1), &abort_flag)) {
-        if (error_flag != nullptr) atomicCAS(error_flag, 0, CB_FLAG_WAIT_SLOT);
+        if (p.error_flag != nullptr) atomicCAS(p.error_flag, 0, CB_FLAG_WAIT_SLOT);
         abort_flag = 1;
         break;
       }
@@ -104,12 +138,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(G::kStage));
       tma_load_2d(st, &map_a, kb * kBK, m0, full + s);
       if (NA == 2) tma_load_2d(st + G::kA, &map_a2, kb * kBK, m0, full + s);
-      tma_load_2d(st + NA * G::kA, &map_b, kb * kBK, n0, full + s);
+      tma_load_2d(st + NA * G::kA, MODE == kSwiglu ? &map_b0 : mb, kb * kBK, n0, full + s);
+      if (MODE == kSwiglu) tma_load_2d(st + NA * G::kA + G::kB, &map_b1, kb * kBK, n0, full + s);
     }
     // drain: the copies of the last round of every stage land before we go on
-    for (int t = kb - 1; t >= 0 && t >= kb - G::kStages; --t) {
-      if (!wait_short(full + t % G::kStages, static_cast<uint32_t>((t / G::kStages) & 1))) {
-        if (error_flag != nullptr) atomicCAS(error_flag, 0, CB_FLAG_WAIT_DRAIN);
+    for (int q = kb - 1; q >= 0 && q >= kb - G::kStages; --q) {
+      if (!wait_short(full + q % G::kStages, static_cast<uint32_t>((q / G::kStages) & 1))) {
+        if (p.error_flag != nullptr) atomicCAS(p.error_flag, 0, CB_FLAG_WAIT_DRAIN);
         break;
       }
     }
@@ -119,7 +154,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int kb = 0; kb < kblocks; ++kb) {
       const int s = kb % G::kStages, round = kb / G::kStages;
       if (!wait_or_abort(full + s, static_cast<uint32_t>(round & 1), &abort_flag)) {
-        if (error_flag != nullptr) atomicCAS(error_flag, 0, CB_FLAG_WAIT_DATA);
+        if (p.error_flag != nullptr) atomicCAS(p.error_flag, 0, CB_FLAG_WAIT_DATA);
         abort_flag = 1;
         break;
       }
@@ -127,11 +162,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const unsigned char* st = smem + s * G::kStage;
 #pragma unroll
       for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-        const uint64_t db = sw128_desc(st + NA * G::kA + kk * kUmmaK * 2);
 #pragma unroll
-        for (int pl = 0; pl < NA; ++pl)
-          umma_bf16(tmem, sw128_desc(st + pl * G::kA + kk * kUmmaK * 2), db, idesc,
-                    (kb | kk | pl) != 0 ? 1u : 0u);
+        for (int w = 0; w < G::kW; ++w) {
+          const uint64_t db = sw128_desc(st + NA * G::kA + w * G::kB + kk * kUmmaK * 2);
+#pragma unroll
+          for (int pl = 0; pl < NA; ++pl)
+            umma_bf16(tmem + static_cast<uint32_t>(w * BN), sw128_desc(st + pl * G::kA + kk * kUmmaK * 2), db, idesc,
+                      (kb | kk | pl) != 0 ? 1u : 0u);
+        }
       }
       umma_commit(empty + s);  // the stage is free once these MMAs have read it
     }
@@ -145,25 +183,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   fence_after();
   if (ok) {
     const int row = m0 + warp * 32 + lane;
-    float* crow = c + static_cast<long long>(row) * ldc + n0;
-    const int cols = min(BN, n - n0);  // a multiple of 4
+    float* crow = p.c[seg] + static_cast<long long>(row) * p.ldc[seg] + n0;
+    const float* rrow = MODE == kResidual ? p.residual + static_cast<long long>(row) * p.ldr + n0 : nullptr;
+    const int cols = min(BN, p.n[seg] - n0);  // a multiple of 4
+    const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 #pragma unroll 1
     for (int c0 = 0; c0 < cols; c0 += 16) {
       float v[16];
-      tmem_load16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(c0), v);
-      if (row < m) {
+      tmem_load16(lanes + static_cast<uint32_t>(c0), v);
+      if (MODE == kSwiglu) {
+        float u[16];
+        tmem_load16(lanes + static_cast<uint32_t>(BN + c0), u);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (c0 + 4 * q < cols)
-            reinterpret_cast<float4*>(crow + c0)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        for (int e = 0; e < 16; ++e) v[e] = silu_mul(v[e], u[e]);
+      }
+      if (row < p.m) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (c0 + 4 * q >= cols) continue;
+          float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          if (MODE == kResidual) {
+            const float* r4 = rrow + c0 + 4 * q;
+            o = make_float4(__fadd_rn(r4[0], o.x), __fadd_rn(r4[1], o.y), __fadd_rn(r4[2], o.z), __fadd_rn(r4[3], o.w));
+          }
+          reinterpret_cast<float4*>(crow + c0)[q] = o;
+        }
       }
     }
-  } else if (threadIdx.x == 0 && error_flag != nullptr) {
-    atomicCAS(error_flag, 0, CB_FLAG_WAIT_DATA);
+  } else if (threadIdx.x == 0 && p.error_flag != nullptr) {
+    atomicCAS(p.error_flag, 0, CB_FLAG_WAIT_DATA);
   }
   fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, BN);
+  if (warp == 0) tmem_dealloc(tmem, G::kTmemCols);
 }
 
 // float32 (or strided bf16) A -> bf16 planes hi = bf16(a), lo = bf16(a - hi),
@@ -200,51 +252,58 @@ __global__ void split_planes_kernel(const void* a, int a_dtype, long long lda, l
 }
 
 // bf16 A usable by TMA as it is (no plane copy).
-bool a_direct(const cb_gemm_args& g) {
+bool a_direct(const cb_gemm_multi_args& g) {
   return g.a_dtype == CB_BF16 && aligned16(g.a) && g.lda % 8 == 0 && g.lda >= g.k;
 }
 
-template <int BN, int NA>
-cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& mb, const cb_gemm_args& g,
-                        cudaStream_t s) {
-  using G = GemmShape<BN, NA>;
-  auto kernel = gemm_tc_kernel<BN, NA>;
+template <int BN, int NA, int MODE>
+cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap* mb, const GemmParams& p,
+                        long long tiles, cudaStream_t s) {
+  using G = GemmShape<BN, NA, MODE>;
+  auto kernel = gemm_tc_kernel<BN, NA, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
   if (e != cudaSuccess) return e;
-  const long long tiles = ((g.n + BN - 1) / BN) * ((g.m + kBM - 1) / kBM);
-  kernel<<<static_cast<unsigned>(tiles), kGemmThreads, G::kSmem, s>>>(
-      ma, ma2, mb, g.c, g.ldc, static_cast<int>(g.m), static_cast<int>(g.n), static_cast<int>(g.k), g.error_flag);
+  kernel<<<static_cast<unsigned>(tiles), kGemmThreads, G::kSmem, s>>>(ma, ma2, mb[0], mb[1], mb[2], p);
   return cudaGetLastError();
 }
 
-}  // namespace
-}  // namespace cb
-
-using namespace cb;
-
-extern "C" {
-
-long long cb_gemm_tc_scratch(const cb_gemm_args* g) {
-  if (g == nullptr || g->m <= 0 || g->k <= 0) return 0;
-  if (g->a_dtype == CB_F32) return 2 * g->m * g->k * 2;
-  return a_direct(*g) ? 0 : g->m * g->k * 2;
+template <int BN, int MODE>
+cudaError_t launch_mode(bool split, const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap* mb,
+                        const GemmParams& p, long long tiles, cudaStream_t s) {
+  return split ? launch_gemm<BN, 2, MODE>(ma, ma2, mb, p, tiles, s) : launch_gemm<BN, 1, MODE>(ma, ma2, mb, p, tiles, s);
 }
 
-int cb_gemm_tc(const cb_gemm_args* g, cb_stream_t stream) {
-  CB_REQUIRE(g != nullptr && g->a != nullptr && g->b != nullptr && g->c != nullptr, "gemm: a, b and c are required");
-  CB_REQUIRE(g->m > 0 && g->n > 0 && g->k > 0, "gemm: empty problem");
+long long round_up_to(long long v, long long m) { return (v + m - 1) / m * m; }
+
+int run_multi(const cb_gemm_multi_args* g, cb_stream_t stream) {
+  CB_REQUIRE(g != nullptr && g->a != nullptr, "gemm: a is required");
+  CB_REQUIRE(g->m > 0 && g->k > 0, "gemm: empty problem");
   CB_REQUIRE(g->k % 8 == 0, "gemm: k=%lld must be a multiple of 8", g->k);
-  CB_REQUIRE(g->n % 4 == 0, "gemm: n=%lld must be a multiple of 4", g->n);
-  CB_REQUIRE(g->m < (1LL << 31) && g->n < (1LL << 31) && g->k < (1LL << 31) &&
-                 ((g->m + kBM - 1) / kBM) * ((g->n + 127) / 128) < (1LL << 31),
-             "gemm: problem too large");
+  CB_REQUIRE(g->epilogue == CB_GEMM_STORE || g->epilogue == CB_GEMM_RESIDUAL || g->epilogue == CB_GEMM_SWIGLU,
+             "gemm: unknown epilogue %d", g->epilogue);
+  const int expect_w = g->epilogue == CB_GEMM_SWIGLU ? 2 : g->epilogue == CB_GEMM_RESIDUAL ? 1 : 0;
+  CB_REQUIRE(g->n_w >= 1 && g->n_w <= 3 && (expect_w == 0 || g->n_w == expect_w),
+             "gemm: %d weights for epilogue %d", g->n_w, g->epilogue);
+  CB_REQUIRE(g->m < (1LL << 31) && g->k < (1LL << 31), "gemm: problem too large");
   CB_REQUIRE(g->a_dtype == CB_BF16 || g->a_dtype == CB_F32, "gemm: a must be bf16 or float32");
-  CB_REQUIRE(aligned16(g->b) && g->ldb % 8 == 0 && g->ldb >= g->k, "gemm: b must be 16-byte aligned rows");
-  CB_REQUIRE(aligned16(g->c) && g->ldc % 4 == 0 && g->ldc >= g->n, "gemm: c must be 16-byte aligned rows");
+  const int n_out = g->epilogue == CB_GEMM_SWIGLU ? 1 : g->n_w;
+  for (int i = 0; i < g->n_w; ++i) {
+    CB_REQUIRE(g->b[i] != nullptr && aligned16(g->b[i]) && g->ldb[i] % 8 == 0 && g->ldb[i] >= g->k,
+               "gemm: weight %d must be 16-byte aligned rows", i);
+    CB_REQUIRE(g->n[i] > 0 && g->n[i] % 4 == 0 && g->n[i] < (1LL << 31), "gemm: n=%lld must be a multiple of 4",
+               g->n[i]);
+  }
+  if (g->epilogue == CB_GEMM_SWIGLU) CB_REQUIRE(g->n[0] == g->n[1], "gemm: SwiGLU needs gate and up of equal rows");
+  for (int i = 0; i < n_out; ++i)
+    CB_REQUIRE(g->c[i] != nullptr && aligned16(g->c[i]) && g->ldc[i] % 4 == 0 && g->ldc[i] >= g->n[i],
+               "gemm: c must be 16-byte aligned rows");
+  if (g->epilogue == CB_GEMM_RESIDUAL)
+    CB_REQUIRE(g->residual != nullptr && aligned16(g->residual) && g->ldr % 4 == 0 && g->ldr >= g->n[0],
+               "gemm: residual must be 16-byte aligned rows");
   const bool split = g->a_dtype == CB_F32;
   const bool direct = a_direct(*g);
   CB_REQUIRE(direct || (g->a_split != nullptr && aligned16(g->a_split)), "gemm: a needs %lld bytes of a_split",
-             cb_gemm_tc_scratch(g));
+             cb_gemm_tc_multi_scratch(g));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const void* a_hi = g->a;
   const void* a_lo = nullptr;
@@ -257,23 +316,104 @@ int cb_gemm_tc(const cb_gemm_args* g, cb_stream_t stream) {
     a_lo = lo;
     lda = g->k;
   }
-  // 256-wide tiles unless 128 wastes less of the last column tile
-  const int bn = (g->n + 255) / 256 * 256 - g->n <= (g->n + 127) / 128 * 128 - g->n ? 256 : 128;
-  CUtensorMap ma, ma2, mb;
-  CB_REQUIRE(make_map(&ma, a_hi, g->m, g->k, lda, kBM) && make_map(&mb, g->b, g->n, g->k, g->ldb, bn) &&
-                 (a_lo == nullptr || make_map(&ma2, a_lo, g->m, g->k, lda, kBM)),
+  // 256-wide tiles unless 128 wastes less of the last column tiles
+  long long waste256 = 0, waste128 = 0;
+  for (int i = 0; i < (g->epilogue == CB_GEMM_SWIGLU ? 1 : g->n_w); ++i) {
+    waste256 += round_up_to(g->n[i], 256) - g->n[i];
+    waste128 += round_up_to(g->n[i], 128) - g->n[i];
+  }
+  const int bn = waste256 <= waste128 ? 256 : 128;
+  GemmParams p{};
+  const long long tiles_m = (g->m + kBM - 1) / kBM;
+  long long tiles = 0;
+  p.n_seg = g->epilogue == CB_GEMM_STORE ? g->n_w : 1;
+  for (int i = 0; i < n_out; ++i) {
+    p.c[i] = g->c[i];
+    p.ldc[i] = g->ldc[i];
+  }
+  for (int i = 0; i < p.n_seg; ++i) {
+    p.n[i] = static_cast<int>(g->n[i]);
+    p.tiles_n[i] = static_cast<int>((g->n[i] + bn - 1) / bn);
+    tiles += tiles_m * p.tiles_n[i];
+  }
+  CB_REQUIRE(tiles < (1LL << 31), "gemm: problem too large");
+  p.m = static_cast<int>(g->m);
+  p.k = static_cast<int>(g->k);
+  p.residual = g->residual;
+  p.ldr = g->ldr;
+  p.error_flag = g->error_flag;
+  CUtensorMap ma, ma2, mb[3];
+  CB_REQUIRE(make_map(&ma, a_hi, g->m, g->k, lda, kBM) && (a_lo == nullptr || make_map(&ma2, a_lo, g->m, g->k, lda, kBM)),
              "gemm: tensor map encoding failed");
   if (a_lo == nullptr) ma2 = ma;
+  for (int i = 0; i < 3; ++i) {
+    const int j = i < g->n_w ? i : 0;
+    CB_REQUIRE(make_map(mb + i, g->b[j], g->n[j], g->k, g->ldb[j], bn), "gemm: tensor map encoding failed");
+  }
   cudaError_t e;
-  if (bn == 256)
-    e = split ? launch_gemm<256, 2>(ma, ma2, mb, *g, s) : launch_gemm<256, 1>(ma, ma2, mb, *g, s);
-  else
-    e = split ? launch_gemm<128, 2>(ma, ma2, mb, *g, s) : launch_gemm<128, 1>(ma, ma2, mb, *g, s);
+  if (bn == 256) {
+    e = g->epilogue == CB_GEMM_SWIGLU     ? launch_mode<256, kSwiglu>(split, ma, ma2, mb, p, tiles, s)
+        : g->epilogue == CB_GEMM_RESIDUAL ? launch_mode<256, kResidual>(split, ma, ma2, mb, p, tiles, s)
+                                          : launch_mode<256, kStore>(split, ma, ma2, mb, p, tiles, s);
+  } else {
+    e = g->epilogue == CB_GEMM_SWIGLU     ? launch_mode<128, kSwiglu>(split, ma, ma2, mb, p, tiles, s)
+        : g->epilogue == CB_GEMM_RESIDUAL ? launch_mode<128, kResidual>(split, ma, ma2, mb, p, tiles, s)
+                                          : launch_mode<128, kStore>(split, ma, ma2, mb, p, tiles, s);
+  }
   if (e != cudaSuccess) {
     set_error("cb_gemm_tc: %s", cudaGetErrorString(e));
     return CB_ERR_CUDA;
   }
   return check_launch("cb_gemm_tc");
+}
+
+cb_gemm_multi_args single(const cb_gemm_args* g) {
+  cb_gemm_multi_args m{};
+  m.a = g->a;
+  m.a_dtype = g->a_dtype;
+  m.lda = g->lda;
+  m.m = g->m;
+  m.k = g->k;
+  m.n_w = 1;
+  m.b[0] = g->b;
+  m.ldb[0] = g->ldb;
+  m.n[0] = g->n;
+  m.c[0] = g->c;
+  m.ldc[0] = g->ldc;
+  m.epilogue = CB_GEMM_STORE;
+  m.a_split = g->a_split;
+  m.error_flag = g->error_flag;
+  return m;
+}
+
+}  // namespace
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" {
+
+long long cb_gemm_tc_multi_scratch(const cb_gemm_multi_args* g) {
+  if (g == nullptr || g->m <= 0 || g->k <= 0) return 0;
+  if (g->a_dtype == CB_F32) return 2 * g->m * g->k * 2;
+  return a_direct(*g) ? 0 : g->m * g->k * 2;
+}
+
+int cb_gemm_tc_multi(const cb_gemm_multi_args* g, cb_stream_t stream) { return run_multi(g, stream); }
+
+long long cb_gemm_tc_scratch(const cb_gemm_args* g) {
+  if (g == nullptr) return 0;
+  const cb_gemm_multi_args m = single(g);
+  return cb_gemm_tc_multi_scratch(&m);
+}
+
+int cb_gemm_tc(const cb_gemm_args* g, cb_stream_t stream) {
+  CB_REQUIRE(g != nullptr && g->a != nullptr && g->b != nullptr && g->c != nullptr, "gemm: a, b and c are required");
+  CB_REQUIRE(g->m > 0 && g->n > 0 && g->k > 0, "gemm: empty problem");
+  CB_REQUIRE(g->k % 8 == 0, "gemm: k=%lld must be a multiple of 8", g->k);
+  CB_REQUIRE(g->n % 4 == 0, "gemm: n=%lld must be a multiple of 4", g->n);
+  const cb_gemm_multi_args m = single(g);
+  return run_multi(&m, stream);
 }
 
 }  // extern "C"

@@ -163,6 +163,20 @@ class GemmArgs(ctypes.Structure):
     ]
 
 
+GEMM_STORE, GEMM_RESIDUAL, GEMM_SWIGLU = 0, 1, 2  # cb_gemm_tc_multi epilogues
+
+
+class GemmMultiArgs(ctypes.Structure):
+    _fields_ = [
+        ("a", c_void_p), ("a_dtype", c_int), ("lda", c_longlong),
+        ("m", c_longlong), ("k", c_longlong), ("n_w", c_int),
+        ("b", c_void_p * 3), ("ldb", c_longlong * 3), ("n", c_longlong * 3),
+        ("c", c_void_p * 3), ("ldc", c_longlong * 3),
+        ("epilogue", c_int), ("residual", c_void_p), ("ldr", c_longlong),
+        ("a_split", c_void_p), ("error_flag", c_void_p),
+    ]
+
+
 class GemmRowsArgs(ctypes.Structure):
     _fields_ = [
         ("x", c_void_p), ("x_dtype", c_int), ("ldx", c_longlong), ("rows", c_longlong), ("k", c_longlong),
@@ -234,6 +248,8 @@ _SIGNATURES = {
     "cb_gemm_rows": ([POINTER(GemmRowsArgs), c_void_p], c_int),
     "cb_gemm_tc_scratch": ([POINTER(GemmArgs)], c_longlong),
     "cb_gemm_tc": ([POINTER(GemmArgs), c_void_p], c_int),
+    "cb_gemm_tc_multi_scratch": ([POINTER(GemmMultiArgs)], c_longlong),
+    "cb_gemm_tc_multi": ([POINTER(GemmMultiArgs), c_void_p], c_int),
     "cb_decode_step_table_bytes": ([c_int], c_longlong),
     "cb_decode_step_prepare": ([POINTER(StepPhase), c_int, c_void_p, c_longlong, c_int,
                                 POINTER(DecodeStepConfig)], c_int),

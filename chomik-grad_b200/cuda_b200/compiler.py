@@ -92,7 +92,7 @@ class CudaB200Compiler(Compiler):
         return Planner(outputs, dynamic_inputs, backend=self.device.name,
                        leaf_dtype=self._leaf_dtype, max_positions=self.max_positions,
                        fuse_decode=self.fuse_decode, alias_caches=self.alias_caches,
-                       table_cache=self._tables).build()
+                       table_cache=self._tables, gemm_min_rows=self.gemm_min_rows).build()
 
     def compile(self, outputs: Sequence[object],
                 dynamic_inputs: Sequence[object] = ()) -> CudaB200Program:

@@ -61,6 +61,48 @@ def dt_code(dtype: np.dtype) -> int:
     return _lib.dtype_code(dtype)
 
 
+def gemm_shape(step, min_rows: int) -> Optional[Tuple[int, int, int, int, int]]:
+    """(m, n, k, lda, ldb) when a MATMUL step is ``x @ W.T`` the tensor-core GEMM takes.
+
+    That is llama.py:275-277 (``inputs @ weight.T``): a bf16 weight seen
+    through its transpose (K contiguous), activations whose leading
+    dimensions fold into rows, a fresh float32 output, and at least
+    ``min_rows`` rows (128-row tiles waste the tensor cores on fewer).
+    """
+    av = step.args["a"]
+    bv = step.args["b"]
+    out = step.out
+    b16 = bf16()
+    if len(av.shape) < 2 or len(bv.shape) < 2 or bv.dtype != b16 or out.dtype != np.float32:
+        return None
+    if av.dtype not in (np.float32, b16) or not out.is_contiguous():
+        return None
+    if any(n != 1 for n in bv.shape[:-2]):
+        return None
+    k, n = bv.shape[-2], bv.shape[-1]
+    ldb = bv.strides[-1]
+    if bv.strides[-2] != 1 and k > 1:
+        return None
+    if av.strides[-1] != 1 and k > 1:
+        return None
+    # every dimension before K folds into rows: the non-unit ones must step by
+    # whole rows (a size-1 dimension's stride is meaningless, e.g. the token
+    # axis of a permuted single-token attention output)
+    dims = [(s, st) for s, st in zip(av.shape[:-1], av.strides[:-1]) if s != 1]
+    lda = dims[-1][1] if dims else k
+    rows = 1
+    for size, stride in reversed(dims):
+        if stride != rows * lda:
+            return None
+        rows *= size
+    if rows > 1 and lda < k:  # overlapping or broadcast rows
+        return None
+    if (rows < min_rows or k % 8 or n % 4 or ldb % 8
+            or tuple(out.shape[-2:]) != (av.shape[-2], n)):
+        return None
+    return rows, n, k, lda, ldb
+
+
 def contiguous_strides(shape: Sequence[int]) -> Tuple[int, ...]:
     strides, step = [], 1
     for n in reversed(shape):
@@ -243,7 +285,7 @@ class Planner:
     def __init__(self, outputs: Sequence[object], dynamic_inputs: Sequence[object], *,
                  backend: str, leaf_dtype, max_positions: int = 8192,
                  fuse_decode: bool = True, alias_caches: bool = True,
-                 table_cache: Optional[dict] = None) -> None:
+                 table_cache: Optional[dict] = None, gemm_min_rows: Optional[int] = None) -> None:
         self.outputs = tuple(outputs)
         self.dynamic = set(dynamic_inputs)
         self.backend = backend
@@ -252,6 +294,7 @@ class Planner:
         self.fuse_decode = fuse_decode
         self.alias_caches = alias_caches
         self.table_cache = table_cache if table_cache is not None else {}
+        self.gemm_min_rows = gemm_min_rows  # None: no tensor-core GEMM epilogue fusion
         self.plan = Plan()
         self._rdt: Dict[object, np.dtype] = {}
         self._val: Dict[object, View] = {}
@@ -546,6 +589,8 @@ class Planner:
                 self._emit_generic(node)
         for index, node in enumerate(self.outputs):
             plan.outputs.append((node, self.value(node)))
+        self._drop_dead_steps()  # before the fusion: dead copies must not count as readers
+        self._fuse_gemms()
         self._drop_dead_steps()
         from .fusion import assign_prefetch
 
@@ -601,6 +646,125 @@ class Planner:
         return emit
 
     # steps whose only effect is their output buffer
+    # ------------------------------------------------ GEMM epilogue fusion
+    _SWIGLU = [("neg", 0, -1), ("exp", 3, -1), ("add", 4, 1), ("div", 0, 5), ("mul", 6, 2)]
+
+    def _fuse_gemms(self) -> None:
+        """Fold the prefill's tensor-core GEMMs and their elementwise neighbours.
+
+        On steps whose matmuls run on cb_gemm_tc (``gemm_shape`` with the
+        compiler's row threshold), three rewrites into ``matmul_multi`` steps
+        (cb_gemm_tc_multi):
+        * SwiGLU: ``silu(x @ Wg.T) * (x @ Wu.T)`` -- the reference's
+          elementwise chain g / (1 + exp(-g)) * u (llama.py:289-291) over two
+          matmuls of the same x read by nothing else -- becomes one launch
+          whose epilogue computes the chain (same float32 steps);
+        * residual: ``r + x @ W.T`` (llama.py:529-535) with a float32 r
+          computed before the matmul becomes the GEMM's epilogue add;
+        * grouping: up to three remaining matmuls of the same x (q/k/v)
+          become one launch.
+        Each removed matmul output was read by the fused elementwise step
+        only, so no other step sees a difference.
+        """
+        if self.gemm_min_rows is None:
+            return
+        plan = self.plan
+        steps = plan.steps
+        readers: Dict[int, int] = {}
+        for st in steps:
+            acc: Set[int] = set()
+            _collect_buffers(st.args, acc)
+            for b in acc:
+                readers[b] = readers.get(b, 0) + 1
+        external = {id(v.buf) for _, v in plan.outputs} | {id(b) for b in plan.argmax_of.values()}
+        producer = {id(st.out.buf): st for st in steps if st.out is not None}
+        index = {id(st): i for i, st in enumerate(steps)}
+        removed: Set[int] = set()
+        replace: Dict[int, Step] = {}
+
+        def gemmable(st) -> Optional[tuple]:
+            if st is None or st.name != "matmul" or id(st) in removed or id(st) in replace:
+                return None
+            return gemm_shape(st, self.gemm_min_rows)
+
+        def only_for(view: View, consumer) -> Optional[Step]:
+            """The matmul producing all of ``view``'s buffer, read by ``consumer`` alone."""
+            st = producer.get(id(view.buf))
+            if st is None or readers.get(id(view.buf), 0) != 1 or id(view.buf) in external:
+                return None
+            if view.offset != 0 or not view.is_contiguous() or view.size != view.buf.size:
+                return None
+            return st
+
+        def same_a(x: Step, y: Step) -> bool:
+            a, b = x.args["a"], y.args["a"]
+            return a.buf is b.buf and a.offset == b.offset and a.shape == b.shape and a.strides == b.strides
+
+        def fused(first: Step, mats: List[Step], epilogue: int, outs: List[View], residual=None) -> Step:
+            m, _, k, lda, _ = gemm_shape(first, self.gemm_min_rows)
+            args = dict(a=first.args["a"], weights=[st.args["b"] for st in mats],
+                        shapes=[gemm_shape(st, self.gemm_min_rows) for st in mats], outs=outs,
+                        epilogue=epilogue, residual=residual, m=m, k=k, lda=lda)
+            names = ", ".join(self._name(st.args["b"]) for st in mats)
+            kind_ = {_lib.GEMM_STORE: "store", _lib.GEMM_RESIDUAL: "residual", _lib.GEMM_SWIGLU: "swiglu"}[epilogue]
+            text = f"matmul_multi({self._name(first.args['a'])}, [{names}], epilogue={kind_})"
+            return Step("matmul_multi", outs[0], args, text)
+
+        for st in steps:  # SwiGLU and residual epilogues
+            if st.name != "elementwise" or id(st) in removed:
+                continue
+            ins, ops = st.args["inputs"], st.args["instrs"]
+            if any(np.dtype(o[3]) != np.float32 for o in ops) or st.out.dtype != np.float32:
+                continue
+            shape = tuple(st.out.shape)
+            if len(ins) == 3 and [tuple(o[:3]) for o in ops] == self._SWIGLU:
+                one = ins[1]
+                if one.buf.kind != "input" or one.buf.node is None or self._const(one.buf.node) != 1.0:
+                    continue
+                g, u = only_for(ins[0], st), only_for(ins[2], st)
+                if (g is None or u is None or g is u or tuple(ins[0].shape) != shape or tuple(ins[2].shape) != shape
+                        or not same_a(g, u)):
+                    continue
+                sg, su = gemmable(g), gemmable(u)
+                if sg is None or su is None or sg[0] != su[0] or sg[1] != su[1] or sg[2:4] != su[2:4]:
+                    continue
+                first, second = (g, u) if index[id(g)] < index[id(u)] else (u, g)
+                replace[id(first)] = fused(g, [g, u], _lib.GEMM_SWIGLU, [st.out])
+                removed.update((id(second), id(st)))
+            elif len(ins) == 2 and [tuple(o[:3]) for o in ops] == [("add", 0, 1)]:
+                for mi, ri in ((1, 0), (0, 1)):
+                    mat = only_for(ins[mi], st)
+                    r = ins[ri]
+                    if mat is None or gemmable(mat) is None or tuple(ins[mi].shape) != shape:
+                        continue
+                    if r.dtype != np.float32 or tuple(r.shape) != shape or not r.is_contiguous():
+                        continue
+                    made = producer.get(id(r.buf))
+                    if made is not None and index[id(made)] > index[id(mat)]:
+                        continue  # the residual is computed after the matmul
+                    replace[id(mat)] = fused(mat, [mat], _lib.GEMM_RESIDUAL, [st.out], residual=r)
+                    removed.add(id(st))
+                    break
+        for i, st in enumerate(steps):  # group plain matmuls that share x
+            if gemmable(st) is None:
+                continue
+            group = [st]
+            written = set()
+            for later in steps[i + 1:]:
+                if len(group) == 3:
+                    break
+                if later.out is not None:
+                    written.add(id(later.out.buf))
+                if id(st.args["a"].buf) in written:
+                    break
+                if (gemmable(later) is not None and same_a(st, later)
+                        and gemm_shape(later, self.gemm_min_rows)[2:4] == gemm_shape(st, self.gemm_min_rows)[2:4]):
+                    group.append(later)
+            if len(group) > 1:
+                replace[id(st)] = fused(st, group, _lib.GEMM_STORE, [g.out for g in group])
+                removed.update(id(g) for g in group[1:])
+        plan.steps = [replace.get(id(st), st) for st in steps if id(st) not in removed]
+
     PURE_STEPS = frozenset(("elementwise", "matmul", "reduce", "copy", "rms_norm", "rope", "sdpa", "place"))
 
     def _drop_dead_steps(self) -> None:

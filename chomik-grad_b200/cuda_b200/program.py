@@ -35,7 +35,7 @@ import numpy as np
 from . import _lib
 from .device import DeviceArray, torch_dtype
 from .frontend.lazy import CompiledProgram
-from .planner import Buffer, Plan, Step, View, bf16, contiguous_strides
+from .planner import Buffer, Plan, Step, View, bf16, contiguous_strides, gemm_shape  # noqa: F401
 
 _BF16 = bf16()
 
@@ -44,47 +44,6 @@ def _torch():
     import torch
 
     return torch
-
-
-def gemm_shape(step: Step, min_rows: int) -> Optional[Tuple[int, int, int, int, int]]:
-    """(m, n, k, lda, ldb) when a MATMUL step is ``x @ W.T`` the tensor-core GEMM takes.
-
-    That is llama.py:275-277 (``inputs @ weight.T``): a bf16 weight seen
-    through its transpose (K contiguous), activations whose leading
-    dimensions fold into rows, a fresh float32 output, and at least
-    ``min_rows`` rows (128-row tiles waste the tensor cores on fewer).
-    """
-    av: View = step.args["a"]
-    bv: View = step.args["b"]
-    out = step.out
-    if len(av.shape) < 2 or len(bv.shape) < 2 or bv.dtype != _BF16 or out.dtype != np.float32:
-        return None
-    if av.dtype not in (np.float32, _BF16) or not out.is_contiguous():
-        return None
-    if any(n != 1 for n in bv.shape[:-2]):
-        return None
-    k, n = bv.shape[-2], bv.shape[-1]
-    ldb = bv.strides[-1]
-    if bv.strides[-2] != 1 and k > 1:
-        return None
-    if av.strides[-1] != 1 and k > 1:
-        return None
-    # every dimension before K folds into rows: the non-unit ones must step by
-    # whole rows (a size-1 dimension's stride is meaningless, e.g. the token
-    # axis of a permuted single-token attention output)
-    dims = [(s, st) for s, st in zip(av.shape[:-1], av.strides[:-1]) if s != 1]
-    lda = dims[-1][1] if dims else k
-    rows = 1
-    for size, stride in reversed(dims):
-        if stride != rows * lda:
-            return None
-        rows *= size
-    if rows > 1 and lda < k:  # overlapping or broadcast rows
-        return None
-    if (rows < min_rows or k % 8 or n % 4 or ldb % 8
-            or tuple(out.shape[-2:]) != (av.shape[-2], n)):
-        return None
-    return rows, n, k, lda, ldb
 
 
 class CudaB200Program(CompiledProgram):
@@ -148,6 +107,7 @@ class CudaB200Program(CompiledProgram):
             n_counters += int(_lib.load().cb_gemm_rows_counters(ctypes.byref(args)))
         self._rows_counters = torch.zeros(max(n_counters, 1), dtype=torch.int32, device=dev)
         scratch = max([self._gemm_scratch_bytes(s) for s in self.plan.steps if s.name == "matmul"] +
+                      [self._multi_scratch_bytes(s) for s in self.plan.steps if s.name == "matmul_multi"] +
                       [self._sdpa_scratch_bytes(s) for s in self.plan.steps if s.name == "sdpa"] + rows_scratch)
         self._gemm_scratch = torch.empty(max(scratch, 16), dtype=torch.uint8, device=dev)
         self._gemm_flag = (self._tensors[self.plan.error_flag] if self.plan.error_flag is not None
@@ -548,6 +508,33 @@ class CudaB200Program(CompiledProgram):
         src: View = step.args["src"]
         parallel.get_group(step.args["group"]).all_reduce(self.ptr(src), self.ptr(step.out), src.size,
                                                           _lib.dtype_code(src.dtype), stream)
+
+    @staticmethod
+    def _multi_scratch_bytes(step: Step) -> int:
+        g = step.args
+        return (4 if g["a"].dtype == np.float32 else 2) * g["m"] * g["k"]
+
+    def _step_matmul_multi(self, step: Step, stream: int) -> None:
+        """cb_gemm_tc_multi: grouped x @ W.T (q/k/v), or with a residual / SwiGLU epilogue."""
+        g = step.args
+        a = _lib.GemmMultiArgs()
+        av: View = g["a"]
+        a.a, a.a_dtype, a.lda = self.ptr(av), _lib.dtype_code(av.dtype), g["lda"]
+        a.m, a.k = g["m"], g["k"]
+        a.n_w = len(g["weights"])
+        for i, (w, shape) in enumerate(zip(g["weights"], g["shapes"])):
+            a.b[i], a.ldb[i], a.n[i] = self.ptr(w), shape[4], shape[1]
+        for i, out in enumerate(g["outs"]):
+            a.c[i], a.ldc[i] = self.ptr(out), out.shape[-1]
+        a.epilogue = g["epilogue"]
+        if g["residual"] is not None:
+            r: View = g["residual"]
+            a.residual, a.ldr = self.ptr(r), r.shape[-1]
+        a.a_split = self._gemm_scratch.data_ptr()
+        a.error_flag = self._gemm_flag.data_ptr()
+        _lib.call("cb_gemm_tc_multi", ctypes.byref(a), stream)
+        direct = av.dtype == _BF16 and a.a % 16 == 0 and g["lda"] % 8 == 0
+        self._extra_launches += int(not direct)  # the plane pass
 
     def _step_kv_write(self, step: Step, stream: int) -> None:
         cache: View = step.args["cache"]

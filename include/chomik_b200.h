@@ -424,6 +424,39 @@ typedef struct {
 CB_API long long cb_gemm_tc_scratch(const cb_gemm_args* args);
 CB_API int cb_gemm_tc(const cb_gemm_args* args, cb_stream_t stream);
 
+/* cb_gemm_tc with up to three weights sharing A and a fused epilogue -- the
+ * prefill Linears of one layer (chomikgrad/llama.py:275-277) and the
+ * elementwise work that follows them:
+ *  CB_GEMM_STORE     c[i] = A B[i]^T for i < n_w (q/k/v: one launch, one
+ *                    plane split of A);
+ *  CB_GEMM_RESIDUAL  c[0] = residual + A B[0]^T, the add in float32 (the
+ *                    residual adds after the O and down projections,
+ *                    llama.py:529-535);
+ *  CB_GEMM_SWIGLU    c[0] = silu(A B[0]^T) * (A B[1]^T), silu(g) =
+ *                    g / (1 + exp(-g)), every step float32 (llama.py:289-291,
+ *                    371-380); gate and up are never stored.
+ * Operands as cb_gemm_tc; n[i] % 4 == 0, rows 16-byte aligned. */
+enum { CB_GEMM_STORE = 0, CB_GEMM_RESIDUAL = 1, CB_GEMM_SWIGLU = 2 };
+typedef struct {
+  const void* a; /* m x k, row stride lda (elements), shared by every weight */
+  int a_dtype;   /* CB_BF16 or CB_F32 */
+  long long lda;
+  long long m, k;
+  int n_w;
+  const void* b[3]; /* n[i] x k bf16, row stride ldb[i] */
+  long long ldb[3];
+  long long n[3];
+  float* c[3];      /* m x n[i] float32, row stride ldc[i] (SwiGLU, residual: c[0]) */
+  long long ldc[3];
+  int epilogue;     /* CB_GEMM_* */
+  const float* residual; /* m x n[0], row stride ldr (CB_GEMM_RESIDUAL) */
+  long long ldr;
+  void* a_split; /* scratch: the bf16 plane(s) of A */
+  int* error_flag;
+} cb_gemm_multi_args;
+CB_API long long cb_gemm_tc_multi_scratch(const cb_gemm_multi_args* args);
+CB_API int cb_gemm_tc_multi(const cb_gemm_multi_args* args, cb_stream_t stream);
+
 /* ---- few-row tensor-core GEMM (batched decode) -----------------------------
  * out_i (rows x w_rows[i], float32, row stride ldo[i]) = x . W_i^T for up to
  * three bf16 weights W_i (w_rows[i] x k, row-major, 16-byte aligned) sharing

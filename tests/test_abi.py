@@ -46,6 +46,7 @@ STRUCTS = {
     "cb_gemv_args": _lib.GemvArgs,
     "cb_decode_attention_args": _lib.DecodeAttentionArgs,
     "cb_gemm_args": _lib.GemmArgs,
+    "cb_gemm_multi_args": _lib.GemmMultiArgs,
     "cb_gemm_rows_args": _lib.GemmRowsArgs,
     "cb_step_phase": _lib.StepPhase,
     "cb_decode_step_config": _lib.DecodeStepConfig,

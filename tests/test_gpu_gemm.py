@@ -147,3 +147,96 @@ def test_gemm_rows_matches_float64(rows, ns, k, splits, x_dtype):
             assert torch.isfinite(got).all()
             assert bool(((got - ref).abs() <= bound).all()), float(((got - ref).abs() / bound).max())
             assert torch.isnan(o[:, n:]).all()  # nothing written past n
+
+
+def _multi(torch, a, ws, epilogue, residual=None):
+    """cb_gemm_tc_multi: returns the output tensors (row stride n + 8: nothing may land past n)."""
+    from cuda_b200 import _lib
+
+    m, k = a.shape
+    g = _lib.GemmMultiArgs()
+    g.a, g.lda, g.m, g.k = a.data_ptr(), a.stride(0), m, k
+    g.a_dtype = _lib.F32 if a.dtype == torch.float32 else _lib.BF16
+    g.n_w, g.epilogue = len(ws), epilogue
+    outs = []
+    for i, w in enumerate(ws):
+        g.b[i], g.ldb[i], g.n[i] = w.data_ptr(), w.stride(0), w.shape[0]
+    for i in range(1 if epilogue != _lib.GEMM_STORE else len(ws)):
+        c = torch.full((m, ws[i].shape[0] + 8), float("nan"), device="cuda")
+        g.c[i], g.ldc[i] = c.data_ptr(), c.stride(0)
+        outs.append(c)
+    if residual is not None:
+        g.residual, g.ldr = residual.data_ptr(), residual.stride(0)
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scratch = torch.empty(max(_lib.load().cb_gemm_tc_multi_scratch(ctypes.byref(g)), 16), dtype=torch.uint8,
+                          device="cuda")
+    g.a_split, g.error_flag = scratch.data_ptr(), flag.data_ptr()
+    for _ in range(2):  # twice: a second launch over the same buffers gives the same result
+        _lib.call("cb_gemm_tc_multi", ctypes.byref(g), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    for o, w in zip(outs, ws):
+        assert torch.isnan(o[:, w.shape[0]:]).all()
+    return [o[:, : w.shape[0]].cpu().double() for o, w in zip(outs, ws)]
+
+
+def _bound(a, w, k, a_dtype):
+    scale = a.double().abs() @ w.double().abs().T
+    return scale * (k * 2.0 ** -23 + (2.0 ** -15 if a_dtype == "f32" else 0.0)) + 1e-6
+
+
+@pytest.mark.parametrize("m,ns,k", [(300, (2048, 256, 256), 2048), (130, (260, 128), 200), (64, (688,), 688)])
+@pytest.mark.parametrize("a_dtype", ["bf16", "f32"])
+def test_gemm_multi_grouped_matches_float64(m, ns, k, a_dtype):
+    """q/k/v-style: several weights share A, one launch."""
+    torch = pytest.importorskip("torch")
+    from cuda_b200 import _lib
+
+    gen = torch.Generator().manual_seed(m + k + len(ns))
+    a = torch.randn(m, k, generator=gen)
+    if a_dtype == "bf16":
+        a = a.to(torch.bfloat16)
+    ws = [(torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16) for n in ns]
+    got = _multi(torch, a.cuda(), [w.cuda() for w in ws], _lib.GEMM_STORE)
+    for g, w in zip(got, ws):
+        ref = a.double() @ w.double().T
+        assert bool(((g - ref).abs() <= _bound(a, w, k, a_dtype)).all())
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 512, 2048), (2048, 2048, 5632), (77, 260, 200)])
+def test_gemm_multi_residual_matches_float64(m, n, k):
+    torch = pytest.importorskip("torch")
+    from cuda_b200 import _lib
+
+    gen = torch.Generator().manual_seed(m * 3 + n)
+    a = torch.randn(m, k, generator=gen)
+    w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16)
+    r = torch.randn(m, n, generator=gen)
+    (got,) = _multi(torch, a.cuda(), [w.cuda()], _lib.GEMM_RESIDUAL, residual=r.cuda())
+    ref = r.double() + a.double() @ w.double().T
+    bound = _bound(a, w, k, "f32") + r.double().abs() * 2.0 ** -23
+    assert bool(((got - ref).abs() <= bound).all())
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 5632, 2048), (2048, 5632, 2048), (100, 688, 256)])
+@pytest.mark.parametrize("a_dtype", ["bf16", "f32"])
+def test_gemm_multi_swiglu_matches_float64(m, n, k, a_dtype):
+    """silu(A Wg^T) * (A Wu^T) in one launch, against float64."""
+    torch = pytest.importorskip("torch")
+    from cuda_b200 import _lib
+
+    gen = torch.Generator().manual_seed(n + k + m)
+    a = torch.randn(m, k, generator=gen)
+    if a_dtype == "bf16":
+        a = a.to(torch.bfloat16)
+    wg = (torch.randn(n, k, generator=gen) * 0.05).to(torch.bfloat16)
+    wu = (torch.randn(n, k, generator=gen) * 0.05).to(torch.bfloat16)
+    (got,) = _multi(torch, a.cuda(), [wg.cuda(), wu.cuda()], _lib.GEMM_SWIGLU)
+    g = a.double() @ wg.double().T
+    u = a.double() @ wu.double().T
+    ref = g / (1 + torch.exp(-g)) * u
+    bg, bu = _bound(a, wg, k, a_dtype), _bound(a, wu, k, a_dtype)
+    silu = (g / (1 + torch.exp(-g))).abs()
+    bound = 1.2 * bg * (u.abs() + bu) + (silu + 1.2 * bg) * bu + 4 * 2.0 ** -23 * ref.abs() + 1e-6
+    assert torch.isfinite(got).all()
+    assert bool(((got - ref).abs() <= bound).all()), float(((got - ref).abs() / bound).max())

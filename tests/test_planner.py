@@ -155,6 +155,30 @@ def test_prefill_linears_take_the_tensor_core_gemm(tiny_bf16):
     assert all(gemm_shape(s, 64) is None for s in matmuls)  # 16 rows: below the default
 
 
+def test_prefill_gemm_epilogues_are_fused(tiny_bf16):
+    """With the tensor-core GEMM in play, q/k/v group, SwiGLU and residual adds fold into GEMMs."""
+    from cuda_b200 import _lib
+
+    wl, weights = tiny_bf16
+    cfg, dt = wl.config, wl.np_dtype
+    m = L.LlamaForCausalLM(cfg, weights, sequence_length=16, dtype=dt, cache_length=48)
+    ids = Tensor(synthetic_prompt(cfg, 16), copy=False)
+    outs = m.prefill(ids, Tensor(L.position_selector(15, 16, dtype=dt), copy=False))
+    p = Planner([o._node for o in outs], [ids._node], backend="cuda-b200", leaf_dtype=_leaf_dtype,
+                gemm_min_rows=16).build()
+    multi = [s for s in p.steps if s.name == "matmul_multi"]
+    kinds = Counter((s.args["epilogue"], len(s.args["weights"])) for s in multi)
+    layers = cfg.num_hidden_layers
+    assert kinds[(_lib.GEMM_STORE, 3)] == layers  # q, k, v
+    assert kinds[(_lib.GEMM_SWIGLU, 2)] == layers  # gate, up
+    # residual adds after O and down; layer 0's first add reads the bf16 embedding, kept apart
+    assert kinds[(_lib.GEMM_RESIDUAL, 1)] == 2 * layers - 1
+    assert sum(1 for s in p.steps if s.name == "elementwise") == 1
+    for s in multi:
+        if s.args["epilogue"] == _lib.GEMM_RESIDUAL:
+            assert s.args["residual"].dtype == np.float32
+
+
 def test_cache_placement_is_lowered_to_a_column_copy(tiny_bf16):
     """x @ cache_placement (llama.py:411-418) becomes cb_place_columns with the right sources."""
     wl, weights = tiny_bf16
