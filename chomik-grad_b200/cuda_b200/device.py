@@ -57,18 +57,36 @@ def numpy_dtype(tdtype) -> np.dtype:
 
 
 class DeviceArray:
-    """A dense device buffer with NumPy shape/dtype metadata."""
+    """A dense device buffer with NumPy shape/dtype metadata.
 
-    __slots__ = ("tensor", "shape", "dtype", "argmax_value", "__weakref__")
+    A small host array handed to ``CudaB200Device.array`` is kept as a
+    pending upload (``host``) until its device tensor is first needed: a
+    program that binds it as a per-step input copies it straight into its
+    own input slots (one pinned staging copy for all of a step's inputs)
+    instead of through a separate device buffer.  Reading ``tensor``
+    uploads it.
+    """
+
+    __slots__ = ("_tensor", "host", "device", "shape", "dtype", "argmax_value", "__weakref__")
 
     def __init__(self, tensor: Any, shape: Optional[Sequence[int]] = None,
-                 dtype: Optional[np.dtype] = None) -> None:
-        self.tensor = tensor
+                 dtype: Optional[np.dtype] = None, *, host: Optional[np.ndarray] = None,
+                 device: Any = None) -> None:
+        self._tensor = tensor
+        self.host = host
+        self.device = device
         self.shape = tuple(int(n) for n in (shape if shape is not None else tensor.shape))
         self.dtype = np.dtype(dtype) if dtype is not None else numpy_dtype(tensor.dtype)
         # Optional device int64 holding argmax(self) computed by the program
         # that produced this array (saves a reduction in DeviceAdapter.argmax).
         self.argmax_value = None
+
+    @property
+    def tensor(self) -> Any:
+        if self._tensor is None:
+            self._tensor = upload(self.host, self.device).tensor
+            self.host = None
+        return self._tensor
 
     @property
     def size(self) -> int:
@@ -86,7 +104,8 @@ class DeviceArray:
         return int(self.tensor.data_ptr())
 
     def __repr__(self) -> str:
-        return f"DeviceArray(shape={self.shape}, dtype={self.dtype}, device={self.tensor.device})"
+        where = self.tensor.device if self._tensor is not None else f"{self.device} (upload pending)"
+        return f"DeviceArray(shape={self.shape}, dtype={self.dtype}, device={where})"
 
 
 def empty(shape: Sequence[int], dtype: np.dtype, device: Any) -> DeviceArray:
@@ -112,6 +131,8 @@ def upload(value: np.ndarray, device: Any) -> DeviceArray:
 
 
 def download(array: DeviceArray) -> np.ndarray:
+    if array.host is not None:  # never uploaded: the host copy is the value
+        return np.array(array.host, copy=True).reshape(array.shape)
     torch = _torch()
     flat = array.tensor[: array.size] if array.size else array.tensor[:0]
     if array.dtype.name == "bfloat16":
@@ -121,10 +142,14 @@ def download(array: DeviceArray) -> np.ndarray:
     return host.reshape(array.shape).copy()
 
 
+_UPLOADABLE = frozenset(("float32", "bfloat16", "float16", "int32", "int64"))
+
+
 class CudaB200Device(DeviceAdapter):
     """``DeviceAdapter`` over one B200 (the current CUDA device by default)."""
 
     name = "cuda-b200"
+    PENDING_BYTES = 64 * 1024  # host arrays up to this size are uploaded lazily
 
     def __init__(self, index: Optional[int] = None) -> None:
         torch = _torch()
@@ -152,8 +177,14 @@ class CudaB200Device(DeviceAdapter):
         if isinstance(value, torch.Tensor):
             tensor = value.detach().to(self.torch_device).contiguous().reshape(-1)
             return DeviceArray(tensor, tuple(value.shape), numpy_dtype(value.dtype))
+        host = np.asarray(value)
+        if host.nbytes <= self.PENDING_BYTES and host.dtype.name in _UPLOADABLE:
+            # a small per-step input: upload when first needed (a program
+            # binding it copies it into its input slots directly)
+            return DeviceArray(None, host.shape, host.dtype, host=np.array(host, copy=True),
+                               device=self.torch_device)
         with torch.cuda.device(self.torch_device):
-            return upload(np.asarray(value), self.torch_device)
+            return upload(host, self.torch_device)
 
     def evaluate(self, values: Sequence[object]) -> None:
         self.synchronize()

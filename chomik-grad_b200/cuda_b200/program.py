@@ -64,6 +64,12 @@ class CudaB200Program(CompiledProgram):
         self.use_graphs = compiler.use_graphs
         self.launches = 0  # kernels launched by the last eager run (graph replays re-run them)
         self.step_mode = bool(getattr(compiler, "decode_step", False)) and self._fusable(plan)
+        # constants the plan was specialised on, once per leaf (a shared leaf,
+        # e.g. the GQA broadcast's ones, is guarded by every layer that uses it)
+        guards: Dict[int, tuple] = {}
+        for leaf, expected in plan.guards:
+            guards.setdefault(id(leaf), (leaf, np.ascontiguousarray(expected)))
+        self._guards = list(guards.values())
         self._step_tables: Dict[tuple, Tuple[object, _lib.DecodeStepConfig]] = {}
 
     @staticmethod
@@ -76,9 +82,32 @@ class CudaB200Program(CompiledProgram):
     def _build(self) -> None:
         torch = _torch()
         dev = self.device.torch_device
+        # Copy-bound inputs (the small per-step ones) live in one device arena
+        # mirrored by a pinned host block: a step's host inputs are written
+        # into the mirror and reach their slots in one asynchronous copy.
+        arena_off: Dict[Buffer, int] = {}
+        top = 0
+        for buf in self.plan.buffers:
+            if buf.kind == "input" and buf.bind == "copy":
+                arena_off[buf] = top
+                top += (max(buf.size, 1) * buf.dtype.itemsize + 15) // 16 * 16
+        self._arena = torch.empty(max(top, 16), dtype=torch.uint8, device=dev)
+        self._staging = torch.empty(max(top, 16), dtype=torch.uint8, pin_memory=True)
+        self._staging_np = self._staging.numpy()
+        self._staging_done = None  # event after the last staged copy (the mirror is reused)
+        self._arena_off = arena_off
+        for buf, off in arena_off.items():
+            count = max(buf.size, 1)
+            view = self._arena[off: off + count * buf.dtype.itemsize]
+            tensor = view.view(torch_dtype(buf.dtype)) if buf.dtype.name != "bfloat16" else \
+                view.view(torch.int16).view(torch.bfloat16)
+            self._tensors[buf] = tensor
+            self._ptr[buf] = int(tensor.data_ptr())
         for buf in self.plan.buffers:
             if buf.kind == "input" and buf.bind == "pointer":
                 continue  # bound per run
+            if buf in arena_off:
+                continue
             if buf.kind == "aux" and buf.host is not None:
                 arr = self.device.array(buf.host)
                 self._tensors[buf] = arr.tensor
@@ -153,15 +182,17 @@ class CudaB200Program(CompiledProgram):
 
     @staticmethod
     def _check(arr: DeviceArray, buf: Buffer) -> None:
-        if tuple(arr.shape) != tuple(buf.shape):
+        if arr.shape != tuple(buf.shape):
             raise ValueError(f"input bound with shape {arr.shape}, program expects {buf.shape}")
-        if np.dtype(arr.dtype) != np.dtype(buf.dtype):
+        if arr.dtype != buf.dtype:
             raise TypeError(f"input bound with dtype {arr.dtype}, program was compiled for "
                             f"{buf.dtype}; compile a new program for this dtype")
 
     def _bind(self, bindings: Mapping) -> Tuple[Dict[object, DeviceArray], tuple]:
         bound: Dict[object, DeviceArray] = dict(self._constants)
         key = []
+        device_copies = []
+        staged = False
         for leaf, buf in self._per_run:
             if leaf in bindings:
                 arr = self.device.array(bindings[leaf])
@@ -172,11 +203,26 @@ class CudaB200Program(CompiledProgram):
             if buf.bind == "pointer":
                 self._ptr[buf] = arr.data_ptr()
                 key.append(self._ptr[buf])
+            elif arr.size == 0:
+                continue
+            elif arr.host is not None:  # pending host input: through the pinned mirror
+                if not staged and self._staging_done is not None:
+                    self._staging_done.synchronize()  # the previous step's copy has read the mirror
+                staged = True
+                host = np.ascontiguousarray(arr.host).reshape(-1)
+                off = self._arena_off[buf]
+                self._staging_np[off: off + host.nbytes] = host.view(np.uint8)
             else:
-                slot = self._tensors[buf]
-                n = max(buf.size, 1)
-                if arr.size:
-                    slot[:n].copy_(arr.tensor[:n], non_blocking=True)
+                device_copies.append((buf, arr))
+        if staged:
+            torch = _torch()
+            self._arena.copy_(self._staging, non_blocking=True)
+            if self._staging_done is None:
+                self._staging_done = torch.cuda.Event()
+            self._staging_done.record()
+        for buf, arr in device_copies:  # after the mirror copy, which covers every slot
+            n = max(buf.size, 1)
+            self._tensors[buf][:n].copy_(arr.tensor[:n], non_blocking=True)
         return bound, tuple(key)
 
     # ------------------------------------------------------------ run
@@ -185,8 +231,10 @@ class CudaB200Program(CompiledProgram):
         with torch.cuda.device(self.device.torch_device):
             if not self._built:
                 self._build()
-            for leaf, expected in self.plan.guards:
-                if not np.array_equal(np.asarray(leaf.numpy_value()), expected):
+            for leaf, expected in self._guards:
+                value = np.asarray(leaf.numpy_value())
+                if (value.shape != expected.shape or value.dtype != expected.dtype
+                        or value.tobytes() != expected.tobytes()):
                     raise RuntimeError("a constant the program was specialised on has changed; "
                                        "compile the graph again")
             bound, key = self._bind(bindings or {})
@@ -269,10 +317,12 @@ class CudaB200Program(CompiledProgram):
             outs.append(self._copy_out(view, node.shape))
             argmax = self.plan.argmax_of.get(index)
             if argmax is not None:
-                status = torch.zeros(2, dtype=torch.int64, device=self.device.torch_device)
+                status = torch.empty(2, dtype=torch.int64, device=self.device.torch_device)
                 status[:1].copy_(self._tensors[argmax][:1])
                 if self.plan.error_flag is not None:
                     status[1:].copy_(self._tensors[self.plan.error_flag][:1])
+                else:
+                    status[1:].zero_()
                 outs[-1].argmax_value = status
         return tuple(outs)
 
