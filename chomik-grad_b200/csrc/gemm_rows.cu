@@ -25,6 +25,7 @@
 //    and re-arms the counter.
 // Every wait is bounded (sync.cuh); on a timeout the kernel records an
 // error, lets its copies land and its MMAs finish, frees TMEM and returns.
+#include "norm.cuh"
 #include "tc_core.cuh"
 
 namespace cb {
@@ -60,6 +61,8 @@ struct RowsParams {
   float* partial;      // (tiles, max_parts, NB, 128) float32
   unsigned* counters;  // one per tile, 0 between launches
   int* error_flag;
+  const float* residual;  // n_w == 1: out = residual + x W^T
+  long long ldr;
 };
 
 // The CTA whose range holds flattened chunk f: ranges are [c T / G, (c+1) T / G).
@@ -219,8 +222,11 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         if (whole) {
           if (row < n) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (c0 + e < p.rows) out[static_cast<long long>(c0 + e) * ldo + row] = v[e];
+            for (int e = 0; e < 16; ++e) {
+              if (c0 + e >= p.rows) continue;
+              const float r = p.residual != nullptr ? p.residual[static_cast<long long>(c0 + e) * p.ldr + row] : 0.0f;
+              out[static_cast<long long>(c0 + e) * ldo + row] = p.residual != nullptr ? __fadd_rn(r, v[e]) : v[e];
+            }
           }
         } else {
 #pragma unroll
@@ -282,9 +288,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
               if (bb >= p.rows) continue;
               float* o = out + static_cast<long long>(bb) * ldo;
               const float a4[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
+              const float* rr = p.residual != nullptr ? p.residual + static_cast<long long>(bb) * p.ldr : nullptr;
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                if (row4 + e < n) o[row4 + e] = a4[e];
+                if (row4 + e < n) o[row4 + e] = rr != nullptr ? __fadd_rn(rr[row4 + e], a4[e]) : a4[e];
             }
           }
           if (r == 0) p.counters[tile_flat] = 0u;
@@ -305,18 +312,43 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   }
 }
 
-// x rows (float32 or bf16, row stride ldx) -> bf16 planes hi, lo (rows x k);
-// grid (rows, k chunks of 1024).
-__global__ void rows_planes_kernel(const void* x, int x_dtype, long long ldx, long long k, __nv_bfloat16* hi,
-                                   __nv_bfloat16* lo) {
+__device__ __forceinline__ void split_store(float v, __nv_bfloat16* hi, __nv_bfloat16* lo, long long i) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  hi[i] = h;
+  lo[i] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h)));
+}
+
+// x rows (float32 or bf16, row stride ldx) -> bf16 planes hi, lo (rows x k),
+// through the PLAIN or SWIGLU prologue; grid (rows, k chunks of 1024).
+__global__ void rows_planes_kernel(const void* x, int x_dtype, long long ldx, long long k, const void* x2,
+                                   int x2_dtype, long long ldx2, int swiglu, __nv_bfloat16* hi, __nv_bfloat16* lo) {
   const long long r = blockIdx.x;
   const long long c1 = min(k, (blockIdx.y + 1) * 1024LL);
   for (long long c = blockIdx.y * 1024LL + threadIdx.x; c < c1; c += blockDim.x) {
-    const float v = load_as_f32(x, r * ldx + c, x_dtype);
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    hi[r * k + c] = h;
-    lo[r * k + c] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h)));
+    float v = load_as_f32(x, r * ldx + c, x_dtype);
+    if (swiglu) {  // the reference's float32 chain: x / (1 + exp(-x)) * x2
+      const float u = load_as_f32(x2, r * ldx2 + c, x2_dtype);
+      v = __fmul_rn(__fdiv_rn(v, __fadd_rn(expf(-v), 1.0f)), u);
+    }
+    split_store(v, hi, lo, r * k + c);
   }
+}
+
+// RMS prologue: one block per row; the row is staged in shared memory, its
+// sum of squares reduced as cb_rmsnorm reduces it, then normalised, rounded
+// to dt_out and split into the planes.
+__global__ void __launch_bounds__(256) rows_rms_planes_kernel(const void* x, int x_dtype, long long ldx, long long k,
+                                                               const void* w, int w_dtype, NormSpec n, int dt_out,
+                                                               __nv_bfloat16* hi, __nv_bfloat16* lo) {
+  extern __shared__ float row[];
+  __shared__ float red[8];
+  const long long r = blockIdx.x;
+  const int width = static_cast<int>(k);
+  for (int i = threadIdx.x; i < width; i += blockDim.x) row[i] = load_as_f32(x, r * ldx + i, x_dtype);
+  __syncthreads();
+  const float d = norm_finish_d(n, norm_block_sum(n, row, width, red));
+  for (int i = threadIdx.x; i < width; i += blockDim.x)
+    split_store(norm_apply(n, row[i], d, load_as_f32(w, i, w_dtype), dt_out), hi, lo, r * k + i);
 }
 
 int padded_rows(long long rows) { return rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256; }
@@ -355,8 +387,18 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
   using G = RowsShape<NB>;
   __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(a.scratch);
   __nv_bfloat16* lo = hi + pl.plane_elems;
-  const dim3 pgrid(static_cast<unsigned>(a.rows), static_cast<unsigned>((a.k + 1023) / 1024));
-  rows_planes_kernel<<<pgrid, 256, 0, s>>>(a.x, a.x_dtype, a.ldx, a.k, hi, lo);
+  if (a.x_mode == CB_ROWS_X_RMS) {
+    const NormSpec n{a.divisor, a.eps, a.dt_sq, a.dt_sum, a.dt_mean, a.dt_t, a.dt_d, a.dt_y};
+    const size_t smem = static_cast<size_t>(a.k) * sizeof(float);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(rows_rms_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    rows_rms_planes_kernel<<<static_cast<unsigned>(a.rows), 256, smem, s>>>(a.x, a.x_dtype, a.ldx, a.k, a.norm_w,
+                                                                            a.norm_w_dtype, n, a.dt_out, hi, lo);
+  } else {
+    const dim3 pgrid(static_cast<unsigned>(a.rows), static_cast<unsigned>((a.k + 1023) / 1024));
+    rows_planes_kernel<<<pgrid, 256, 0, s>>>(a.x, a.x_dtype, a.ldx, a.k, a.x2, a.x2_dtype, a.ldx2,
+                                             a.x_mode == CB_ROWS_X_SWIGLU, hi, lo);
+  }
   CB_REQUIRE(cudaGetLastError() == cudaSuccess, "cb_gemm_rows: plane pass launch failed");
   CUtensorMap mw[3], mxh, mxl;
   for (int i = 0; i < 3; ++i) {
@@ -382,6 +424,8 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
   p.partial = reinterpret_cast<float*>((after + 15) & ~static_cast<uintptr_t>(15));
   p.counters = a.counters;
   p.error_flag = a.error_flag;
+  p.residual = a.residual;
+  p.ldr = a.ldr;
   auto kernel = gemm_rows_kernel<NB>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
   if (e == cudaSuccess) {
@@ -433,6 +477,15 @@ int cb_gemm_rows(const cb_gemm_rows_args* a, cb_stream_t stream) {
   CB_REQUIRE(a->k > 0 && a->k % 8 == 0 && a->k < (1LL << 31), "gemm_rows: k=%lld must be a multiple of 8", a->k);
   CB_REQUIRE(a->x_dtype == CB_F32 || a->x_dtype == CB_BF16, "gemm_rows: x must be float32 or bf16");
   CB_REQUIRE(aligned16(a->scratch), "gemm_rows: scratch must be 16-byte aligned");
+  CB_REQUIRE(a->x_mode == CB_ROWS_X_PLAIN || a->x_mode == CB_ROWS_X_RMS || a->x_mode == CB_ROWS_X_SWIGLU,
+             "gemm_rows: unknown x mode %d", a->x_mode);
+  if (a->x_mode == CB_ROWS_X_RMS)
+    CB_REQUIRE(a->norm_w != nullptr && a->k <= 49152 && a->divisor != 0.0f, "gemm_rows: RMS prologue needs norm_w");
+  if (a->x_mode == CB_ROWS_X_SWIGLU)
+    CB_REQUIRE(a->x2 != nullptr && (a->x2_dtype == CB_F32 || a->x2_dtype == CB_BF16),
+               "gemm_rows: SwiGLU prologue needs x2");
+  if (a->residual != nullptr)
+    CB_REQUIRE(a->n_w == 1 && a->ldr >= a->w_rows[0], "gemm_rows: a residual epilogue takes one weight");
   for (int i = 0; i < a->n_w; ++i) {
     CB_REQUIRE(a->w[i] != nullptr && aligned16(a->w[i]) && a->out[i] != nullptr, "gemm_rows: weight %d", i);
     CB_REQUIRE(a->w_rows[i] > 0 && a->w_rows[i] < (1LL << 31) && a->ldo[i] >= a->w_rows[i],

@@ -183,7 +183,16 @@ class GemmRowsArgs(ctypes.Structure):
         ("n_w", c_int), ("w", c_void_p * 3), ("w_rows", c_longlong * 3),
         ("out", c_void_p * 3), ("ldo", c_longlong * 3), ("splits", c_int),
         ("scratch", c_void_p), ("counters", c_void_p), ("error_flag", c_void_p),
+        ("x_mode", c_int), ("norm_w", c_void_p), ("norm_w_dtype", c_int),
+        ("divisor", c_float), ("eps", c_float),
+        ("dt_sq", c_int), ("dt_sum", c_int), ("dt_mean", c_int), ("dt_t", c_int), ("dt_d", c_int),
+        ("dt_y", c_int), ("dt_out", c_int),
+        ("x2", c_void_p), ("x2_dtype", c_int), ("ldx2", c_longlong),
+        ("residual", c_void_p), ("ldr", c_longlong),
     ]
+
+
+ROWS_X_PLAIN, ROWS_X_RMS, ROWS_X_SWIGLU = 0, 1, 2  # cb_gemm_rows x prologues
 
 
 class StepPhase(ctypes.Structure):

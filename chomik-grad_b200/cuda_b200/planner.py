@@ -764,6 +764,135 @@ class Planner:
                 replace[id(st)] = fused(st, group, _lib.GEMM_STORE, [g.out for g in group])
                 removed.update(id(g) for g in group[1:])
         plan.steps = [replace.get(id(st), st) for st in steps if id(st) not in removed]
+        self._fuse_rows()
+
+    def _rows_route(self, st) -> Optional[tuple]:
+        """gemm_shape of a matmul that runs on cb_gemm_rows (few rows, dense weight rows)."""
+        if st.name != "matmul":
+            return None
+        shape = gemm_shape(st, 1)
+        if shape is None or shape[0] >= self.gemm_min_rows or shape[0] > 256 or shape[4] != shape[2]:
+            return None
+        return shape
+
+    def _fuse_rows(self) -> None:
+        """Fold batched decode's elementwise neighbours into cb_gemm_rows (``matmul_rows`` steps).
+
+        * RMSNorm read only by up to three row-GEMM matmuls of its output
+          (q/k/v, gate/up) becomes their x prologue (the norm is computed
+          while x is split into bf16 planes);
+        * SwiGLU read only by one row-GEMM matmul (down) becomes its prologue;
+        * ``r + x @ W.T`` with a float32 r computed before becomes the
+          residual epilogue of a one-weight row GEMM.
+        """
+        plan = self.plan
+        steps = plan.steps
+        readers: Dict[int, List[Step]] = {}
+        for st in steps:
+            acc: Set[int] = set()
+            _collect_buffers(st.args, acc)
+            for b in acc:
+                readers.setdefault(b, []).append(st)
+        external = {id(v.buf) for _, v in plan.outputs} | {id(b) for b in plan.argmax_of.values()}
+        producer = {id(st.out.buf): st for st in steps if st.out is not None}
+        index = {id(st): i for i, st in enumerate(steps)}
+        removed: Set[int] = set()
+        replace: Dict[int, Step] = {}
+
+        def sole_readers(st) -> Optional[List[Step]]:
+            buf = st.out.buf
+            if id(buf) in external or st.out.offset != 0 or not st.out.is_contiguous():
+                return None
+            return readers.get(id(buf), [])
+
+        def rows_step(x: View, mats: List[Step], shapes, outs, **extra) -> Step:
+            m, _, k, ldx, _ = shapes[0]
+            args = dict(x=x, weights=[st.args["b"] for st in mats], shapes=shapes, outs=outs, m=m, k=k,
+                        ldx=ldx, x_mode=extra.get("x_mode", _lib.ROWS_X_PLAIN), norm_w=extra.get("norm_w"),
+                        spec=extra.get("spec"), x2=extra.get("x2"), residual=extra.get("residual"))
+            names = ", ".join(self._name(st.args["b"]) for st in mats)
+            mode = {_lib.ROWS_X_PLAIN: "", _lib.ROWS_X_RMS: ", prologue=rms_norm",
+                    _lib.ROWS_X_SWIGLU: ", prologue=swiglu"}[args["x_mode"]]
+            res = ", epilogue=residual" if args["residual"] is not None else ""
+            return Step("matmul_rows", outs[0], args, f"matmul_rows({self._name(x)}, [{names}]{mode}{res})")
+
+        for st in steps:  # RMSNorm prologues
+            if st.name != "rms_norm" or st.args.get("table") is not None:
+                continue
+            users = sole_readers(st)
+            if not users or len(users) > 3 or any(self._rows_route(u) is None for u in users):
+                continue
+            shapes = [self._rows_route(u) for u in users]
+            if (any(u.args["a"].buf is not st.out.buf or u.args["a"].offset != 0 for u in users)
+                    or len({sh[2:4] for sh in shapes}) != 1 or shapes[0][3] != shapes[0][2]):
+                continue
+            x = st.args["x"]
+            if not x.is_contiguous() or x.dtype not in (np.float32, bf16()):
+                continue
+            first = min(users, key=lambda u: index[id(u)])
+            shapes_x = [(sh[0], sh[1], sh[2], x.shape[-1], sh[4]) for sh in shapes]
+            replace[id(first)] = rows_step(x, users, shapes_x, [u.out for u in users], x_mode=_lib.ROWS_X_RMS,
+                                           norm_w=st.args["w"], spec=st.args["spec"])
+            removed.update(id(u) for u in users if u is not first)
+            removed.add(id(st))
+        for st in steps:  # SwiGLU prologues
+            if st.name != "elementwise" or id(st) in removed:
+                continue
+            ins, ops = st.args["inputs"], st.args["instrs"]
+            if ([tuple(o[:3]) for o in ops] != self._SWIGLU or any(np.dtype(o[3]) != np.float32 for o in ops)
+                    or ins[1].buf.kind != "input" or ins[1].buf.node is None
+                    or self._const(ins[1].buf.node) != 1.0):
+                continue
+            users = sole_readers(st)
+            if not users or len(users) != 1 or self._rows_route(users[0]) is None or id(users[0]) in replace:
+                continue
+            g, u = ins[0], ins[2]
+            shape = tuple(st.out.shape)
+            if (tuple(g.shape) != shape or tuple(u.shape) != shape or not g.is_contiguous()
+                    or not u.is_contiguous() or g.dtype != np.float32 or u.dtype != np.float32):
+                continue
+            mat = users[0]
+            sh = self._rows_route(mat)
+            replace[id(mat)] = rows_step(g, [mat], [(sh[0], sh[1], sh[2], g.shape[-1], sh[4])], [mat.out],
+                                         x_mode=_lib.ROWS_X_SWIGLU, x2=u)
+            removed.add(id(st))
+        for st in steps:  # residual epilogues
+            if st.name != "elementwise" or id(st) in removed:
+                continue
+            ins, ops = st.args["inputs"], st.args["instrs"]
+            if len(ins) != 2 or [tuple(o[:3]) for o in ops] != [("add", 0, 1)] or np.dtype(ops[0][3]) != np.float32:
+                continue
+            shape = tuple(st.out.shape)
+            for mi, ri in ((1, 0), (0, 1)):
+                mv, r = ins[mi], ins[ri]
+                mat = producer.get(id(mv.buf))
+                if mat is None or id(mat) in removed:
+                    continue
+                cur = replace.get(id(mat), mat)
+                users = readers.get(id(mv.buf), [])
+                if (len(users) != 1 or id(mv.buf) in external or mv.offset != 0 or not mv.is_contiguous()
+                        or tuple(mv.shape) != shape):
+                    continue
+                if cur.name == "matmul":
+                    sh = self._rows_route(cur)
+                    if sh is None:
+                        continue
+                    cur = rows_step(cur.args["a"], [cur], [sh], [cur.out])
+                elif cur.name != "matmul_rows" or len(cur.args["weights"]) != 1 or cur.args["residual"] is not None:
+                    continue
+                if r.dtype != np.float32 or tuple(r.shape) != shape or not r.is_contiguous():
+                    continue
+                made = producer.get(id(r.buf))
+                if made is not None and index[id(made)] > index[id(mat)]:
+                    continue
+                cur.args["residual"] = r
+                cur.args["outs"] = [st.out]
+                cur.out = st.out
+                cur.text = cur.text[:-1] + ", epilogue=residual)"
+                replace[id(mat)] = cur
+                removed.add(id(st))
+                break
+        plan.steps = [replace.get(id(st), st) for st in steps if id(st) not in removed]
 
     PURE_STEPS = frozenset(("elementwise", "matmul", "reduce", "copy", "rms_norm", "rope", "sdpa", "place"))
 

@@ -134,6 +134,13 @@ class CudaB200Program(CompiledProgram):
             rows_scratch.append(int(_lib.load().cb_gemm_rows_scratch(ctypes.byref(args))))
             self._rows_counter_off[leader] = n_counters
             n_counters += int(_lib.load().cb_gemm_rows_counters(ctypes.byref(args)))
+        for step in self.plan.steps:  # fused row GEMMs (planner's matmul_rows)
+            if step.name != "matmul_rows":
+                continue
+            args = self._matmul_rows_args(step, counters=0)
+            rows_scratch.append(int(_lib.load().cb_gemm_rows_scratch(ctypes.byref(args))))
+            self._rows_counter_off[id(step)] = n_counters
+            n_counters += int(_lib.load().cb_gemm_rows_counters(ctypes.byref(args)))
         self._rows_counters = torch.zeros(max(n_counters, 1), dtype=torch.int32, device=dev)
         scratch = max([self._gemm_scratch_bytes(s) for s in self.plan.steps if s.name == "matmul"] +
                       [self._multi_scratch_bytes(s) for s in self.plan.steps if s.name == "matmul_multi"] +
@@ -558,6 +565,45 @@ class CudaB200Program(CompiledProgram):
         src: View = step.args["src"]
         parallel.get_group(step.args["group"]).all_reduce(self.ptr(src), self.ptr(step.out), src.size,
                                                           _lib.dtype_code(src.dtype), stream)
+
+    def _matmul_rows_args(self, step: Step, counters: int) -> _lib.GemmRowsArgs:
+        """cb_gemm_rows arguments of a planner-fused row GEMM (prologue / residual epilogue)."""
+        g = step.args
+        x: View = g["x"]
+        a = _lib.GemmRowsArgs()
+        a.x = self.ptr(x) if self._built else 0
+        a.x_dtype, a.ldx, a.rows, a.k = _lib.dtype_code(x.dtype), g["ldx"], g["m"], g["k"]
+        a.n_w = len(g["weights"])
+        for i, (w, shape, out) in enumerate(zip(g["weights"], g["shapes"], g["outs"])):
+            a.w[i] = self.ptr(w) if self._built else 0
+            a.w_rows[i], a.ldo[i] = shape[1], out.shape[-1]
+            a.out[i] = self.ptr(out) if self._built else 0
+        a.splits, a.counters = 0, counters
+        a.x_mode = g["x_mode"]
+        if g["x_mode"] == _lib.ROWS_X_RMS:
+            spec = g["spec"]
+            w: View = g["norm_w"]
+            a.norm_w = self.ptr(w) if self._built else 0
+            a.norm_w_dtype = _lib.dtype_code(w.dtype)
+            a.divisor, a.eps = spec.divisor, spec.eps
+            (a.dt_sq, a.dt_sum, a.dt_mean, a.dt_t, a.dt_d, a.dt_y) = (_lib.dtype_code(d) for d in spec.dts)
+            a.dt_out = _lib.dtype_code(spec.out_dtype)
+        elif g["x_mode"] == _lib.ROWS_X_SWIGLU:
+            x2: View = g["x2"]
+            a.x2 = self.ptr(x2) if self._built else 0
+            a.x2_dtype, a.ldx2 = _lib.dtype_code(x2.dtype), x2.shape[-1]
+        if g["residual"] is not None:
+            r: View = g["residual"]
+            a.residual = self.ptr(r) if self._built else 0
+            a.ldr = r.shape[-1]
+        return a
+
+    def _step_matmul_rows(self, step: Step, stream: int) -> None:
+        a = self._matmul_rows_args(step, self._rows_counters.data_ptr() + 4 * self._rows_counter_off[id(step)])
+        a.scratch = self._gemm_scratch.data_ptr()
+        a.error_flag = self._gemm_flag.data_ptr()
+        _lib.call("cb_gemm_rows", ctypes.byref(a), stream)
+        self._extra_launches += 1  # the plane pass
 
     @staticmethod
     def _multi_scratch_bytes(step: Step) -> int:

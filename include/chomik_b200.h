@@ -486,7 +486,26 @@ typedef struct {
   void* scratch;
   unsigned* counters;
   int* error_flag;
+  /* x prologue, applied while x is split into planes (CB_ROWS_X_*):
+   *  PLAIN   x as given;
+   *  RMS     rms_norm(x) * norm_w with the rounding dtypes of
+   *          cb_rmsnorm_args (llama.py:279-287), rounded to dt_out;
+   *  SWIGLU  silu(x) * x2 = x / (1 + exp(-x)) * x2 in float32
+   *          (llama.py:289-291, 371-380), x2 rows of stride ldx2. */
+  int x_mode;
+  const void* norm_w;
+  int norm_w_dtype;
+  float divisor, eps;
+  int dt_sq, dt_sum, dt_mean, dt_t, dt_d, dt_y, dt_out;
+  const void* x2;
+  int x2_dtype;
+  long long ldx2;
+  /* epilogue (n_w == 1): out[0] = residual + x . W^T, the add in float32
+   * (llama.py:529-535); NULL: store */
+  const float* residual;
+  long long ldr;
 } cb_gemm_rows_args;
+enum { CB_ROWS_X_PLAIN = 0, CB_ROWS_X_RMS = 1, CB_ROWS_X_SWIGLU = 2 };
 CB_API long long cb_gemm_rows_scratch(const cb_gemm_rows_args* args);
 CB_API long long cb_gemm_rows_counters(const cb_gemm_rows_args* args);
 CB_API int cb_gemm_rows(const cb_gemm_rows_args* args, cb_stream_t stream);
