@@ -23,6 +23,13 @@ __device__ __forceinline__ long long idx4(const long long* st, long long a, long
   return a * st[0] + b * st[1] + c * st[2] + d * st[3];
 }
 
+// Offset of out[b, h, t, 0]: contiguous (B, H, T, D) unless out_strides are given.
+__device__ __forceinline__ long long out_index(const cb_sdpa_args& a, long long b, long long h, long long t) {
+  if (a.out_strides[0] == 0 && a.out_strides[1] == 0 && a.out_strides[2] == 0)
+    return ((b * a.heads + h) * a.tq + t) * a.head_size;
+  return b * a.out_strides[0] + h * a.out_strides[1] + t * a.out_strides[2];
+}
+
 __global__ void __launch_bounds__(kThreads) sdpa_kernel(const cb_sdpa_args a) {
   extern __shared__ float qs[];  // (warps, head_size)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -73,7 +80,7 @@ __global__ void __launch_bounds__(kThreads) sdpa_kernel(const cb_sdpa_args a) {
       }
       m = m_new;
     }
-    const long long ob = row * D;
+    const long long ob = out_index(a, b, h, t);
 #pragma unroll
     for (int i = 0; i < kMaxLaneDims; ++i) {
       const long long d = lane + 32 * i;
@@ -180,7 +187,8 @@ __global__ void __launch_bounds__(kThreads) sdpa_query_kernel(const cb_sdpa_args
 constexpr int kMergeWarps = 4;
 
 __global__ void __launch_bounds__(kMergeWarps * 32) sdpa_query_merge_kernel(const float* parts, long long rows,
-                                                                             int splits, int hd, float* out) {
+                                                                             int splits, int hd,
+                                                                             const cb_sdpa_args a) {
   const int lane = threadIdx.x & 31;
   const long long row = static_cast<long long>(blockIdx.x) * kMergeWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -208,10 +216,11 @@ __global__ void __launch_bounds__(kMergeWarps * 32) sdpa_query_merge_kernel(cons
       }
     }
   }
+  float* out = a.out + out_index(a, row / a.heads, row % a.heads, 0);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int d = lane + 32 * i;
-    if (d < hd) out[row * hd + d] = __fdiv_rn(acc[i], l);
+    if (d < hd) out[d] = __fdiv_rn(acc[i], l);
   }
 }
 
@@ -301,7 +310,7 @@ int cb_sdpa_query(const cb_sdpa_args* a, void* scratch, cb_stream_t stream) {
   }
   const long long rows = a->batch * a->heads;
   sdpa_query_merge_kernel<<<static_cast<unsigned>((rows + kMergeWarps - 1) / kMergeWarps), kMergeWarps * 32, 0, s>>>(
-      parts, rows, static_cast<int>(splits), static_cast<int>(a->head_size), a->out);
+      parts, rows, static_cast<int>(splits), static_cast<int>(a->head_size), *a);
   return check_launch("cb_sdpa_query");
 }
 

@@ -66,7 +66,8 @@ struct AttnTcParams {
   int mask_dtype;
   long long mask_offset;
   long long mask_strides[4];
-  float* out;  // (batch, heads, tq, head_size) contiguous
+  float* out;  // (batch, heads, tq, head_size), element strides out_s* (d contiguous)
+  long long out_sb, out_sh, out_st;
   int heads, kv_heads, tq, tk, tq_pad, tk_pad;
   float divisor, inv_divisor;
   int div_pow2;       // divisor is a power of two: x * inv_divisor == x / divisor exactly
@@ -364,7 +365,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 1)
         fence_after();
         const float lt = l + tmem_load1(lanes + static_cast<uint32_t>(S::kXCol + (n_tiles & 1) * 2 + (half ^ 1)));
         if (qi < p.tq) {
-          float* dst = p.out + ((static_cast<long long>(b) * p.heads + h) * p.tq + qi) * HD + dim0;
+          float* dst = p.out + b * p.out_sb + h * p.out_sh + static_cast<long long>(qi) * p.out_st + dim0;
 #pragma unroll
           for (int d = 0; d < kDims; d += 4)
             *reinterpret_cast<float4*>(dst + d) = make_float4(__fdiv_rn(o[d], lt), __fdiv_rn(o[d + 1], lt),
@@ -480,6 +481,10 @@ int launch_sdpa_tc(const cb_sdpa_args& a, int causal, void* scratch, int* error_
   p.mask_offset = a.mask_offset;
   for (int d = 0; d < 4; ++d) p.mask_strides[d] = a.mask_strides[d];
   p.out = a.out;
+  const bool packed = a.out_strides[0] == 0 && a.out_strides[1] == 0 && a.out_strides[2] == 0;
+  p.out_sb = packed ? a.heads * a.tq * HD : a.out_strides[0];
+  p.out_sh = packed ? a.tq * HD : a.out_strides[1];
+  p.out_st = packed ? HD : a.out_strides[2];
   p.heads = static_cast<int>(a.heads);
   p.kv_heads = static_cast<int>(a.kv_heads);
   p.tq = static_cast<int>(a.tq);
@@ -535,6 +540,9 @@ int cb_sdpa_tc(const cb_sdpa_args* a, int causal, void* scratch, int* error_flag
              "sdpa_tc: problem too large");
   CB_REQUIRE(a->divisor != 0.0f && std::isfinite(a->divisor), "sdpa_tc: bad divisor");
   CB_REQUIRE(scratch != nullptr && aligned16(scratch) && aligned16(a->out), "sdpa_tc: scratch and out must be 16-byte aligned");
+  CB_REQUIRE((a->out_strides[3] == 0 || a->out_strides[3] == 1) && a->out_strides[0] % 4 == 0 &&
+                 a->out_strides[1] % 4 == 0 && a->out_strides[2] % 4 == 0,
+             "sdpa_tc: out rows must be contiguous and 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return a->head_size == 64 ? launch_sdpa_tc<64>(*a, causal, scratch, error_flag, s)
                             : launch_sdpa_tc<128>(*a, causal, scratch, error_flag, s);

@@ -29,6 +29,7 @@
 // Every wait is bounded (sync.cuh): on a timeout the kernel records an error,
 // lets its issued copies land, lets issued MMAs finish, frees its TMEM and
 // returns.
+#include "norm.cuh"
 #include "tc_core.cuh"
 
 namespace cb {
@@ -251,10 +252,34 @@ __global__ void split_planes_kernel(const void* a, int a_dtype, long long lda, l
   }
 }
 
+// RMS prologue: rows of rms_norm(a) * w (cb_rmsnorm's roundings, rounded to
+// dt_out) split into bf16 planes (lo omitted when dt_out is bf16: hi is
+// exact).  One block per row; the row is staged in shared memory.
+__global__ void __launch_bounds__(256) rms_planes_kernel(const void* a, int a_dtype, long long lda, long long k,
+                                                         const void* w, int w_dtype, NormSpec n, int dt_out,
+                                                         __nv_bfloat16* hi, __nv_bfloat16* lo) {
+  extern __shared__ float row[];
+  __shared__ float red[8];
+  const long long r = blockIdx.x;
+  const int width = static_cast<int>(k);
+  for (int i = threadIdx.x; i < width; i += blockDim.x) row[i] = load_as_f32(a, r * lda + i, a_dtype);
+  __syncthreads();
+  const float d = norm_finish_d(n, norm_block_sum(n, row, width, red));
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    const float v = norm_apply(n, row[i], d, load_as_f32(w, i, w_dtype), dt_out);
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[r * k + i] = h;
+    if (lo != nullptr) lo[r * k + i] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h)));
+  }
+}
+
 // bf16 A usable by TMA as it is (no plane copy).
 bool a_direct(const cb_gemm_multi_args& g) {
-  return g.a_dtype == CB_BF16 && aligned16(g.a) && g.lda % 8 == 0 && g.lda >= g.k;
+  return g.x_mode == CB_ROWS_X_PLAIN && g.a_dtype == CB_BF16 && aligned16(g.a) && g.lda % 8 == 0 && g.lda >= g.k;
 }
+
+// dtype of the A the MMAs see (the prologue's output)
+int a_effective_dtype(const cb_gemm_multi_args& g) { return g.x_mode == CB_ROWS_X_RMS ? g.dt_out : g.a_dtype; }
 
 template <int BN, int NA, int MODE>
 cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap* mb, const GemmParams& p,
@@ -300,7 +325,12 @@ int run_multi(const cb_gemm_multi_args* g, cb_stream_t stream) {
   if (g->epilogue == CB_GEMM_RESIDUAL)
     CB_REQUIRE(g->residual != nullptr && aligned16(g->residual) && g->ldr % 4 == 0 && g->ldr >= g->n[0],
                "gemm: residual must be 16-byte aligned rows");
-  const bool split = g->a_dtype == CB_F32;
+  CB_REQUIRE(g->x_mode == CB_ROWS_X_PLAIN || g->x_mode == CB_ROWS_X_RMS, "gemm: unknown A prologue %d", g->x_mode);
+  if (g->x_mode == CB_ROWS_X_RMS)
+    CB_REQUIRE(g->norm_w != nullptr && g->k <= 49152 && g->divisor != 0.0f &&
+                   (g->dt_out == CB_F32 || g->dt_out == CB_BF16),
+               "gemm: RMS prologue needs norm_w, k <= 49152 and a float32 or bf16 output");
+  const bool split = a_effective_dtype(*g) == CB_F32;
   const bool direct = a_direct(*g);
   CB_REQUIRE(direct || (g->a_split != nullptr && aligned16(g->a_split)), "gemm: a needs %lld bytes of a_split",
              cb_gemm_tc_multi_scratch(g));
@@ -308,7 +338,19 @@ int run_multi(const cb_gemm_multi_args* g, cb_stream_t stream) {
   const void* a_hi = g->a;
   const void* a_lo = nullptr;
   long long lda = g->lda;
-  if (!direct) {
+  if (g->x_mode == CB_ROWS_X_RMS) {
+    __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(g->a_split);
+    __nv_bfloat16* lo = split ? hi + g->m * g->k : nullptr;
+    const NormSpec n{g->divisor, g->eps, g->dt_sq, g->dt_sum, g->dt_mean, g->dt_t, g->dt_d, g->dt_y};
+    const size_t smem = static_cast<size_t>(g->k) * sizeof(float);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(rms_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    rms_planes_kernel<<<static_cast<unsigned>(g->m), 256, smem, s>>>(g->a, g->a_dtype, g->lda, g->k, g->norm_w,
+                                                                     g->norm_w_dtype, n, g->dt_out, hi, lo);
+    a_hi = hi;
+    a_lo = lo;
+    lda = g->k;
+  } else if (!direct) {
     __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(g->a_split);
     __nv_bfloat16* lo = split ? hi + g->m * g->k : nullptr;
     split_planes_kernel<<<static_cast<unsigned>(g->m), 256, 0, s>>>(g->a, g->a_dtype, g->lda, g->k, hi, lo);
@@ -395,7 +437,7 @@ extern "C" {
 
 long long cb_gemm_tc_multi_scratch(const cb_gemm_multi_args* g) {
   if (g == nullptr || g->m <= 0 || g->k <= 0) return 0;
-  if (g->a_dtype == CB_F32) return 2 * g->m * g->k * 2;
+  if (a_effective_dtype(*g) == CB_F32) return 2 * g->m * g->k * 2;
   return a_direct(*g) ? 0 : g->m * g->k * 2;
 }
 

@@ -110,7 +110,7 @@ class SdpaArgs(ctypes.Structure):
         ("out", c_void_p),
         ("batch", c_longlong), ("heads", c_longlong), ("kv_heads", c_longlong),
         ("tq", c_longlong), ("tk", c_longlong), ("head_size", c_longlong),
-        ("divisor", c_float),
+        ("divisor", c_float), ("out_strides", c_longlong * 4),
     ]
 
 
@@ -174,6 +174,10 @@ class GemmMultiArgs(ctypes.Structure):
         ("c", c_void_p * 3), ("ldc", c_longlong * 3),
         ("epilogue", c_int), ("residual", c_void_p), ("ldr", c_longlong),
         ("a_split", c_void_p), ("error_flag", c_void_p),
+        ("x_mode", c_int), ("norm_w", c_void_p), ("norm_w_dtype", c_int),
+        ("divisor", c_float), ("eps", c_float),
+        ("dt_sq", c_int), ("dt_sum", c_int), ("dt_mean", c_int), ("dt_t", c_int), ("dt_d", c_int),
+        ("dt_y", c_int), ("dt_out", c_int),
     ]
 
 

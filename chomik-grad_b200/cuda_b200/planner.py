@@ -704,7 +704,8 @@ class Planner:
             m, _, k, lda, _ = gemm_shape(first, self.gemm_min_rows)
             args = dict(a=first.args["a"], weights=[st.args["b"] for st in mats],
                         shapes=[gemm_shape(st, self.gemm_min_rows) for st in mats], outs=outs,
-                        epilogue=epilogue, residual=residual, m=m, k=k, lda=lda)
+                        epilogue=epilogue, residual=residual, m=m, k=k, lda=lda, x_mode=_lib.ROWS_X_PLAIN,
+                        norm_w=None, spec=None)
             names = ", ".join(self._name(st.args["b"]) for st in mats)
             kind_ = {_lib.GEMM_STORE: "store", _lib.GEMM_RESIDUAL: "residual", _lib.GEMM_SWIGLU: "swiglu"}[epilogue]
             text = f"matmul_multi({self._name(first.args['a'])}, [{names}], epilogue={kind_})"
@@ -764,7 +765,41 @@ class Planner:
                 replace[id(st)] = fused(st, group, _lib.GEMM_STORE, [g.out for g in group])
                 removed.update(id(g) for g in group[1:])
         plan.steps = [replace.get(id(st), st) for st in steps if id(st) not in removed]
+        self._fuse_norm_into_gemm()
         self._fuse_rows()
+
+    def _fuse_norm_into_gemm(self) -> None:
+        """An RMSNorm read by one tensor-core GEMM step only becomes its A prologue.
+
+        cb_gemm_tc_multi computes rms_norm(x) * w (the same rounding stages)
+        while it splits A into bf16 planes, so the normalised activations are
+        never stored.
+        """
+        plan = self.plan
+        readers: Dict[int, List[Step]] = {}
+        for st in plan.steps:
+            acc: Set[int] = set()
+            _collect_buffers(st.args, acc)
+            for b in acc:
+                readers.setdefault(b, []).append(st)
+        external = {id(v.buf) for _, v in plan.outputs} | {id(b) for b in plan.argmax_of.values()}
+        removed: Set[int] = set()
+        for st in plan.steps:
+            if st.name != "rms_norm" or st.args.get("table") is not None or id(st.out.buf) in external:
+                continue
+            users = readers.get(id(st.out.buf), [])
+            if len(users) != 1 or users[0].name != "matmul_multi" or users[0].args["x_mode"] != _lib.ROWS_X_PLAIN:
+                continue
+            mm, x = users[0], st.args["x"]
+            a = mm.args["a"]
+            if (a.buf is not st.out.buf or a.offset != 0 or not a.is_contiguous() or not x.is_contiguous()
+                    or x.dtype not in (np.float32, bf16()) or st.out.dtype not in (np.float32, bf16())
+                    or tuple(x.shape) != tuple(st.out.shape)):
+                continue
+            mm.args.update(a=x, lda=x.shape[-1], x_mode=_lib.ROWS_X_RMS, norm_w=st.args["w"], spec=st.args["spec"])
+            mm.text = mm.text[:-1] + ", prologue=rms_norm)"
+            removed.add(id(st))
+        plan.steps = [st for st in plan.steps if id(st) not in removed]
 
     def _rows_route(self, st) -> Optional[tuple]:
         """gemm_shape of a matmul that runs on cb_gemm_rows (few rows, dense weight rows)."""
@@ -1251,7 +1286,16 @@ class Planner:
 
     def _emit_sdpa(self, node, low) -> None:
         q, k, v, mask = (self.value(p) for p in low[1])
-        out = self.tmp(node.shape, F32)
+        b, h, t, d = node.shape
+        users = self.consumers.get(node, [])
+        if (t > 1 and len(users) == 1 and kind(users[0]) == "permute" and tuple(users[0].arg) == (0, 2, 1, 3)
+                and node not in self.output_set):
+            # the graph merges the heads next (llama.py:362-363): write token-major
+            # rows, so the permute is a view and the merge needs no copy
+            buf = self.plan.buffer("tmp", (b, t, h, d), F32)
+            out = View(buf, (b, h, t, d), (t * h * d, d, h * d, 1), 0)
+        else:
+            out = self.tmp(node.shape, F32)
         causal = self._causal_mask(low[1][3])
         self.plan.lowered["sdpa"] = self.plan.lowered.get("sdpa", 0) + 1
         self.add_step("sdpa", out, f"sdpa({self._name(q)}, {self._name(k)}, {self._name(v)}, "

@@ -608,7 +608,8 @@ class CudaB200Program(CompiledProgram):
     @staticmethod
     def _multi_scratch_bytes(step: Step) -> int:
         g = step.args
-        return (4 if g["a"].dtype == np.float32 else 2) * g["m"] * g["k"]
+        dt = g["spec"].out_dtype if g["x_mode"] == _lib.ROWS_X_RMS else g["a"].dtype
+        return (4 if dt == np.float32 else 2) * g["m"] * g["k"]
 
     def _step_matmul_multi(self, step: Step, stream: int) -> None:
         """cb_gemm_tc_multi: grouped x @ W.T (q/k/v), or with a residual / SwiGLU epilogue."""
@@ -628,8 +629,15 @@ class CudaB200Program(CompiledProgram):
             a.residual, a.ldr = self.ptr(r), r.shape[-1]
         a.a_split = self._gemm_scratch.data_ptr()
         a.error_flag = self._gemm_flag.data_ptr()
+        if g["x_mode"] == _lib.ROWS_X_RMS:
+            spec = g["spec"]
+            w: View = g["norm_w"]
+            a.x_mode, a.norm_w, a.norm_w_dtype = _lib.ROWS_X_RMS, self.ptr(w), _lib.dtype_code(w.dtype)
+            a.divisor, a.eps = spec.divisor, spec.eps
+            (a.dt_sq, a.dt_sum, a.dt_mean, a.dt_t, a.dt_d, a.dt_y) = (_lib.dtype_code(d) for d in spec.dts)
+            a.dt_out = _lib.dtype_code(spec.out_dtype)
         _lib.call("cb_gemm_tc_multi", ctypes.byref(a), stream)
-        direct = av.dtype == _BF16 and a.a % 16 == 0 and g["lda"] % 8 == 0
+        direct = g["x_mode"] == _lib.ROWS_X_PLAIN and av.dtype == _BF16 and a.a % 16 == 0 and g["lda"] % 8 == 0
         self._extra_launches += int(not direct)  # the plane pass
 
     def _step_kv_write(self, step: Step, stream: int) -> None:
@@ -734,6 +742,9 @@ class CudaB200Program(CompiledProgram):
         for d in range(4):
             a.mask_strides[d] = 0 if mask.shape[d] == 1 else mask.strides[d]
         a.out = self.ptr(step.out)
+        if not step.out.is_contiguous():  # token-major rows (the planner's head merge without a copy)
+            for d in range(4):
+                a.out_strides[d] = step.out.strides[d]
         a.batch, a.heads, a.tq, a.head_size = q.shape
         a.kv_heads, a.tk = k.shape[1], k.shape[2]
         a.divisor = step.args["divisor"]

@@ -263,6 +263,9 @@ typedef struct {
   float* out;
   long long batch, heads, kv_heads, tq, tk, head_size;
   float divisor;
+  /* element strides of out over (B, H, Tq, D); all 0 = contiguous.  D's
+   * stride must be 1 (e.g. token-major (B, Tq, H, D) rows: {Tq*H*D, D, H*D, 1}) */
+  long long out_strides[4];
 } cb_sdpa_args;
 CB_API int cb_sdpa(const cb_sdpa_args* args, cb_stream_t stream);
 
@@ -453,6 +456,14 @@ typedef struct {
   long long ldr;
   void* a_split; /* scratch: the bf16 plane(s) of A */
   int* error_flag;
+  /* A prologue (CB_ROWS_X_PLAIN or CB_ROWS_X_RMS): with RMS, A is
+   * rms_norm(a) * norm_w, computed while A is split into planes, with the
+   * rounding dtypes of cb_rmsnorm_args, rounded to dt_out (llama.py:279-287) */
+  int x_mode;
+  const void* norm_w;
+  int norm_w_dtype;
+  float divisor, eps;
+  int dt_sq, dt_sum, dt_mean, dt_t, dt_d, dt_y, dt_out;
 } cb_gemm_multi_args;
 CB_API long long cb_gemm_tc_multi_scratch(const cb_gemm_multi_args* args);
 CB_API int cb_gemm_tc_multi(const cb_gemm_multi_args* args, cb_stream_t stream);

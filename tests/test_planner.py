@@ -174,6 +174,12 @@ def test_prefill_gemm_epilogues_are_fused(tiny_bf16):
     # residual adds after O and down; layer 0's first add reads the bf16 embedding, kept apart
     assert kinds[(_lib.GEMM_RESIDUAL, 1)] == 2 * layers - 1
     assert sum(1 for s in p.steps if s.name == "elementwise") == 1
+    # the input and post-attention norms are the A prologues of q/k/v and gate/up
+    assert sum(1 for s in multi if s.args["x_mode"] == _lib.ROWS_X_RMS) == 2 * layers
+    assert sum(1 for s in p.steps if s.name == "rms_norm") == 1  # the final norm (read by the row selector)
+    # attention writes token-major rows: the head merge before the O projection is a view
+    assert not any(s.name == "copy" for s in p.steps)
+    assert all(not s.out.is_contiguous() for s in p.steps if s.name == "sdpa")
     for s in multi:
         if s.args["epilogue"] == _lib.GEMM_RESIDUAL:
             assert s.args["residual"].dtype == np.float32
