@@ -238,12 +238,78 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const cb
   attention_item<HD>(a, blockIdx.y, blockIdx.x, gridDim.x, smem, &s_last, threadIdx.x);
 }
 
+// Batched decode: grid (splits, kv_heads, batch).  Sequence b's q | k | v
+// row starts at qkv + b * qkv_stride; its caches, output, partials and
+// counters are the b-th of `batch` equal slices; position, masks and RoPE
+// row are shared (the sequences step together).
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kernel(const cb_decode_attention_args args,
+                                                                                   long long qkv_stride) {
+  extern __shared__ float smem[];
+  __shared__ int s_last;
+  cb_decode_attention_args a = args;
+  const long long b = blockIdx.z;
+  const long long kv_rows = a.kv_heads * a.context * a.head_size;
+  a.qkv += b * qkv_stride;
+  a.k_cache += b * kv_rows;
+  a.v_cache += b * kv_rows;
+  a.out += b * a.heads * a.head_size;
+  a.scratch += b * static_cast<long long>(gridDim.x) * a.heads * (a.head_size + 2);
+  a.counters += b * a.kv_heads;
+  attention_item<HD, false>(a, blockIdx.y, blockIdx.x, gridDim.x, smem, &s_last, threadIdx.x);
+}
+
 }  // namespace
 }  // namespace cb
 
 using namespace cb;
 
 extern "C" {
+
+long long cb_decode_attention_batched_scratch(const cb_decode_attention_args* a, long long batch) {
+  if (a == nullptr || batch <= 0) return 0;
+  return batch * cb_decode_attention_scratch(a);
+}
+
+int cb_decode_attention_batched(const cb_decode_attention_args* a, long long batch, long long qkv_stride,
+                                cb_stream_t stream) {
+  CB_REQUIRE(a != nullptr && batch >= 1 && batch < 65536, "decode attention: batch %lld (1..65535)", batch);
+  CB_REQUIRE(a->head_size == 32 || a->head_size == 64 || a->head_size == 128 || a->head_size == 256,
+             "decode attention: head size %lld unsupported (32/64/128/256)", a->head_size);
+  CB_REQUIRE(a->kv_heads > 0 && a->heads % a->kv_heads == 0, "decode attention: bad head grouping");
+  CB_REQUIRE(a->context > 0, "decode attention: empty context");
+  CB_REQUIRE(a->qkv != nullptr && a->mask != nullptr && a->write_mask != nullptr && a->position != nullptr &&
+                 a->scratch != nullptr && a->counters != nullptr && a->out != nullptr,
+             "decode attention: qkv, masks, position, scratch, counters and out are required");
+  CB_REQUIRE(qkv_stride >= a->v_off + a->kv_heads * a->head_size, "decode attention: qkv rows overlap");
+  CB_REQUIRE(a->split == 0 || a->split == kAttnSplit, "decode attention: split must be %d", kAttnSplit);
+  const long long splits = (a->context + kAttnSplit - 1) / kAttnSplit;
+  CB_REQUIRE(splits < (1LL << 31) && a->kv_heads < 65536, "decode attention: grid too large");
+  const long long group = a->heads / a->kv_heads;
+  const size_t smem = static_cast<size_t>(attn_smem_floats(group, a->head_size)) * sizeof(float);
+  CB_REQUIRE(smem <= 200 * 1024, "decode attention: too many query heads per KV head");
+  const dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(a->kv_heads), static_cast<unsigned>(batch));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+#define CB_BATCHED_CASE(HD)                                                                               \
+  case HD:                                                                                                \
+    e = cudaFuncSetAttribute(decode_attention_batched_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             static_cast<int>(smem));                                                     \
+    if (e == cudaSuccess) decode_attention_batched_kernel<HD><<<grid, kAttnThreads, smem, s>>>(*a, qkv_stride); \
+    break;
+  switch (a->head_size) {
+    CB_BATCHED_CASE(32)
+    CB_BATCHED_CASE(64)
+    CB_BATCHED_CASE(128)
+    CB_BATCHED_CASE(256)
+  }
+#undef CB_BATCHED_CASE
+  if (e != cudaSuccess) {
+    set_error("cb_decode_attention_batched: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return check_launch("cb_decode_attention_batched");
+}
 
 int cb_sdpa(const cb_sdpa_args* a, cb_stream_t stream) {
   CB_REQUIRE(a->head_size > 0 && a->head_size <= 32 * kMaxLaneDims, "sdpa: head size %lld unsupported",

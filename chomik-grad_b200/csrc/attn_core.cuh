@@ -169,7 +169,9 @@ __device__ __forceinline__ void attention_merge_pair_regs(const float* parts, lo
 }
 
 // Needs attention_stage_cache's shared memory (and an attn_sync after it).
-template <int HD>
+// kRegMerge = false compiles only the warp-per-head merge (fewer registers:
+// more blocks per SM for launches of many small items).
+template <int HD, bool kRegMerge = true>
 __device__ void attention_finish(const cb_decode_attention_args& a, int g, int split, int splits, float* smem,
                                  int* s_last, int tid, bool merge, unsigned long long* stamps = nullptr) {
   const int group = static_cast<int>(a.heads / a.kv_heads);
@@ -287,26 +289,55 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
   }
   attn_sync();
   if (!*s_last) return;
-  for (int i = tid; i < group * half; i += kAttnThreads) {  // two dims of one head per thread
-    const long long e0 = (static_cast<long long>(g) * group + i / half) * HD + (i % half) * 2;
-    float merged[8];
-    if (splits <= kMergeRegSplits)
+  if (kRegMerge && splits <= kMergeRegSplits) {
+    for (int i = tid; i < group * half; i += kAttnThreads) {  // two dims of one head per thread
+      const long long e0 = (static_cast<long long>(g) * group + i / half) * HD + (i % half) * 2;
+      float merged[8];
       attention_merge_pair_regs(a.scratch, a.heads, HD, splits, e0, merged);
-    else
-      attention_merge_chunk(a.scratch, a.heads, HD, splits, e0, 2, merged);
-    a.out[e0] = merged[0];
-    a.out[e0 + 1] = merged[1];
+      a.out[e0] = merged[0];
+      a.out[e0 + 1] = merged[1];
+    }
+  } else {
+    // many splits: one warp per head; lanes take the splits' maxima and sums,
+    // the scales move to the dimension lanes by shuffle, so every split's
+    // values are loaded independently (sums in a fixed order: deterministic)
+    const long long stride = a.heads * (HD + 2);
+    for (int h = warp; h < group; h += warps) {
+      const long long head = static_cast<long long>(g) * group + h;
+      const float* base = a.scratch + head * (HD + 2);
+      float m = -INFINITY;
+      for (int sp = lane; sp < splits; sp += 32) m = fmaxf(m, __ldcg(base + sp * stride));
+      m = warp_max(m);
+      float l = 0.0f, acc[HD / 32];
+#pragma unroll
+      for (int i = 0; i < HD / 32; ++i) acc[i] = 0.0f;
+      for (int s0 = 0; s0 < splits; s0 += 32) {
+        const int sp = s0 + lane;
+        const float scale = sp < splits ? expf(__ldcg(base + sp * stride) - m) : 0.0f;
+        l += warp_sum(sp < splits ? __ldcg(base + sp * stride + 1) * scale : 0.0f);
+        const int n = splits - s0 < 32 ? splits - s0 : 32;
+#pragma unroll 4
+        for (int j = 0; j < n; ++j) {
+          const float sc = __shfl_sync(0xffffffffu, scale, j);
+          const float* part = base + (s0 + j) * stride + 2;
+#pragma unroll
+          for (int i = 0; i < HD / 32; ++i) acc[i] = fmaf(__ldcg(part + lane + 32 * i), sc, acc[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < HD / 32; ++i) a.out[head * HD + lane + 32 * i] = __fdiv_rn(acc[i], l);
+    }
   }
   if (tid == 0) a.counters[g] = 0u;
 }
 
 // The whole item: stage, then finish with the in-kernel merge.
-template <int HD>
+template <int HD, bool kRegMerge = true>
 __device__ void attention_item(const cb_decode_attention_args& a, int g, int split, int splits, float* smem,
                                int* s_last, int tid) {
   attention_stage_cache<HD>(a, g, split, smem, tid);
   attn_sync();
-  attention_finish<HD>(a, g, split, splits, smem, s_last, tid, true);
+  attention_finish<HD, kRegMerge>(a, g, split, splits, smem, s_last, tid, true);
 }
 
 }  // namespace cb

@@ -249,6 +249,8 @@ _SIGNATURES = {
     "cb_gemv_grid": ([POINTER(GemvArgs), POINTER(c_int)], c_int),
     "cb_decode_attention": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
     "cb_decode_attention_scratch": ([POINTER(DecodeAttentionArgs)], c_longlong),
+    "cb_decode_attention_batched_scratch": ([POINTER(DecodeAttentionArgs), c_longlong], c_longlong),
+    "cb_decode_attention_batched": ([POINTER(DecodeAttentionArgs), c_longlong, c_longlong, c_void_p], c_int),
     "cb_decode_attention_noalloc": ([POINTER(DecodeAttentionArgs), c_void_p], c_int),
     "cb_place_columns": ([c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p, c_int,
                           c_void_p], c_int),

@@ -263,6 +263,21 @@ class Plan:
         return buf
 
 
+def _same_table(a, b) -> bool:
+    """Whether two constant table buffers hold the same values."""
+    if a is b:
+        return True
+    ha, hb = getattr(a, "host", None), getattr(b, "host", None)
+    return ha is not None and hb is not None and ha.shape == hb.shape and bool(np.array_equal(ha, hb))
+
+
+def _step_reads(step) -> Set[int]:
+    """ids of the buffers a step reads (its arguments without its own output list)."""
+    acc: Set[int] = set()
+    _collect_buffers({k: v for k, v in step.args.items() if k != "outs"}, acc)
+    return acc
+
+
 def _collect_buffers(value, acc: Set[int]) -> None:
     """ids of every Buffer a step argument refers to (Views, lists, dicts)."""
     if isinstance(value, View):
@@ -927,6 +942,98 @@ class Planner:
                 replace[id(mat)] = cur
                 removed.add(id(st))
                 break
+        plan.steps = [replace.get(id(st), st) for st in steps if id(st) not in removed]
+        self._fuse_batched_attention()
+
+    def _fuse_batched_attention(self) -> None:
+        """RoPE(q), RoPE(k), the two cache blends and the attention of a batched decode step => one kernel.
+
+        The chain of LlamaDecoderStep (llama.py:509-525) over B sequences at
+        one position: q and k roped at ``position``, the write-mask blend
+        ``cache*(1-wm) + row*wm`` of k and v into the caches (in place), then
+        single-query attention.  When q, k and v are the three outputs of one
+        row GEMM read by nothing else, that GEMM writes them as one
+        (B, q | k | v) buffer and cb_decode_attention_batched runs the chain
+        per (context split, KV head, sequence) -- the single-sequence decode
+        attention's arithmetic, rebased per sequence.
+        """
+        plan = self.plan
+        steps = plan.steps
+        readers: Dict[int, List[Step]] = {}
+        for st in steps:
+            for b in _step_reads(st):
+                readers.setdefault(b, []).append(st)
+        external = {id(v.buf) for _, v in plan.outputs} | {id(b) for b in plan.argmax_of.values()}
+        writer: Dict[int, Step] = {}
+        for st in steps:
+            if st.out is not None:
+                writer[id(st.out.buf)] = st  # the last writer (kv_write updates caches in place)
+        removed: Set[int] = set()
+        replace: Dict[int, Step] = {}
+
+        def only(view: View, reader: Step) -> bool:
+            return (id(view.buf) not in external and readers.get(id(view.buf), []) == [reader])
+
+        for st in steps:
+            if st.name != "sdpa" or id(st) in removed:
+                continue
+            q, k, v, mask = (st.args[n] for n in ("q", "k", "v", "mask"))
+            if len(q.shape) != 4 or q.shape[2] != 1 or len(k.shape) != 4:
+                continue
+            b, heads, _, hd = q.shape
+            _, kvh, ctx, _ = k.shape
+            if hd not in (32, 64, 128, 256) or heads % kvh or tuple(v.shape) != tuple(k.shape):
+                continue
+            if tuple(mask.shape) != (1, 1, 1, ctx) or not mask.is_contiguous() or not st.out.is_contiguous():
+                continue
+            rq = writer.get(id(q.buf))
+            kwk, kwv = writer.get(id(k.buf)), writer.get(id(v.buf))
+            if (rq is None or kwk is None or kwv is None or rq.name != "rope" or kwk.name != "kv_write"
+                    or kwv.name != "kv_write" or rq.out is not q and rq.out.buf is not q.buf):
+                continue
+            rk = writer.get(id(kwk.args["row"].buf))
+            if rk is None or rk.name != "rope" or not only(q, st) or not only(rk.out, kwk):
+                continue
+            if (kwk.args["write_mask"].buf is not kwv.args["write_mask"].buf
+                    or np.dtype(kwk.args["one_minus"]) != np.dtype(kwv.args["one_minus"])
+                    or rq.args["offset"] is None or rk.args["offset"] is None
+                    or rq.args["offset"].buf is not rk.args["offset"].buf
+                    or not _same_table(rq.args["cos"], rk.args["cos"])
+                    or not _same_table(rq.args["sin"], rk.args["sin"])):
+                continue
+            xq, xk, xv = rq.args["x"], rk.args["x"], kwv.args["row"]
+            m = writer.get(id(xq.buf))
+            if m is None or m.name != "matmul_rows" or len(m.args["outs"]) != 3 or id(m) in replace:
+                continue
+            outs = m.args["outs"]
+            if not (xq.buf is outs[0].buf and xk.buf is outs[1].buf and xv.buf is outs[2].buf):
+                continue
+            if not (only(xq, rq) and only(xk, rk) and only(xv, kwv)):
+                continue
+            nq, nk = heads * hd, kvh * hd
+            if tuple(outs[0].shape[-1:]) != (nq,) or outs[1].shape[-1] != nk or outs[2].shape[-1] != nk:
+                continue
+            if any(o.size != b * o.shape[-1] for o in outs) or m.args["m"] != b:
+                continue
+            row = nq + 2 * nk
+            qkv = self.plan.buffer("tmp", (b, row), F32)
+            cols = (0, nq, nq + nk)
+            m.args["outs"] = [View(qkv, (b, 1, n), (row, n, 1), c) for n, c in zip((nq, nk, nk), cols)]
+            m.args["ldo"] = [row, row, row]
+            m.out = m.args["outs"][0]
+            splits = -(-ctx // 32)
+            scratch = self.aux(shape=(b * splits * heads * (hd + 2),), dtype=np.float32)
+            counters = self.aux(shape=(b * kvh,), dtype=np.int32, zero=True)  # used as unsigned
+            kc, vc = kwk.args["cache"], kwv.args["cache"]
+            fused = Step("decode_attention_batched", st.out, dict(
+                qkv=View.whole(qkv), q_off=0, k_off=nq, v_off=nq + nk, batch=b, qkv_stride=row,
+                heads=heads, kv_heads=kvh, head_size=hd, context=ctx, position=rq.args["offset"],
+                cos=rq.args["cos"], sin=rq.args["sin"], n_positions=rq.args["n_offsets"],
+                k_cache=kc, v_cache=vc, write_mask=kwk.args["write_mask"], one_minus=kwk.args["one_minus"],
+                mask=mask, divisor=st.args["divisor"], scratch=scratch, counters=counters, flag=self.error_flag()),
+                f"decode_attention_batched(qkv={qkv.name}, kv=({self._name(kc)}, {self._name(vc)}), batch={b})")
+            replace[id(st)] = fused
+            removed.update(id(x) for x in (rq, rk, kwk, kwv))
         plan.steps = [replace.get(id(st), st) for st in steps if id(st) not in removed]
 
     PURE_STEPS = frozenset(("elementwise", "matmul", "reduce", "copy", "rms_norm", "rope", "sdpa", "place"))

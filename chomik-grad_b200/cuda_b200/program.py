@@ -253,6 +253,8 @@ class CudaB200Program(CompiledProgram):
             else:
                 self._seen[key] = self._seen.get(key, 0) + 1
                 if self.use_graphs and self._seen[key] >= 2 and len(self._graphs) < 8:
+                    if self.step_mode:
+                        self._step_table()  # prepared outside the capture (it copies and synchronises)
                     exec_ = self._capture()
                     self._graphs[key] = exec_
                     _lib.call("cb_graph_launch", exec_, stream)
@@ -574,9 +576,10 @@ class CudaB200Program(CompiledProgram):
         a.x = self.ptr(x) if self._built else 0
         a.x_dtype, a.ldx, a.rows, a.k = _lib.dtype_code(x.dtype), g["ldx"], g["m"], g["k"]
         a.n_w = len(g["weights"])
+        ldo = g.get("ldo") or [out.shape[-1] for out in g["outs"]]
         for i, (w, shape, out) in enumerate(zip(g["weights"], g["shapes"], g["outs"])):
             a.w[i] = self.ptr(w) if self._built else 0
-            a.w_rows[i], a.ldo[i] = shape[1], out.shape[-1]
+            a.w_rows[i], a.ldo[i] = shape[1], ldo[i]
             a.out[i] = self.ptr(out) if self._built else 0
         a.splits, a.counters = 0, counters
         a.x_mode = g["x_mode"]
@@ -848,6 +851,11 @@ class CudaB200Program(CompiledProgram):
         a.pdl = int(self._compiler.pdl)
         return a
 
+    def _step_decode_attention_batched(self, step: Step, stream: int) -> None:
+        a = self._attention_args(step)
+        _lib.call("cb_decode_attention_batched", ctypes.byref(a), step.args["batch"], step.args["qkv_stride"],
+                  stream)
+
     # ------------------------------------------------------------ whole decode step
     def _step_table(self, flags: Optional[int] = None) -> Tuple[object, _lib.DecodeStepConfig]:
         """The prepared cb_decode_step table of the current bindings (one per key)."""
@@ -874,7 +882,17 @@ class CudaB200Program(CompiledProgram):
         _lib.check(lib.cb_decode_step_prepare(phases, len(steps), table.data_ptr(), table.numel(), flags,
                                               ctypes.byref(config)), "cb_decode_step_prepare")
         if len(self._step_tables) >= 8:
-            self._step_tables.pop(next(iter(self._step_tables)))
+            # A captured graph launches cb_decode_step with its key's table: a
+            # table is freed only together with that graph (after the device
+            # has finished with both), or a later run whose caches land at the
+            # same addresses would replay a graph reading freed descriptors.
+            old_key = next(iter(self._step_tables))
+            self.device.synchronize()
+            exec_ = self._graphs.pop(old_key[0], None)
+            if exec_ is not None:
+                lib.cb_graph_destroy(exec_)
+            self._seen.pop(old_key[0], None)
+            self._step_tables.pop(old_key)
         self._step_tables[key] = (table, config)
         return table, config
 

@@ -386,6 +386,16 @@ typedef struct {
 CB_API int cb_decode_attention(const cb_decode_attention_args* args, cb_stream_t stream);
 /* Scratch floats cb_decode_attention needs for these args. */
 CB_API long long cb_decode_attention_scratch(const cb_decode_attention_args* args);
+/* cb_decode_attention over `batch` sequences stepping together (the same
+ * position, masks and RoPE row): sequence b's q | k | v projections start at
+ * qkv + b * qkv_stride, its caches are the b-th (kv_heads, context, hd)
+ * slice of k_cache / v_cache, its output the b-th heads * hd slice of out;
+ * scratch holds cb_decode_attention_batched_scratch floats and counters
+ * batch * kv_heads zeros.  Replaces, for a batched decode step, the same
+ * chain as cb_decode_attention for every sequence. */
+CB_API long long cb_decode_attention_batched_scratch(const cb_decode_attention_args* args, long long batch);
+CB_API int cb_decode_attention_batched(const cb_decode_attention_args* args, long long batch, long long qkv_stride,
+                                       cb_stream_t stream);
 
 /* cb_decode_attention for callers that cannot allocate device memory (an FFI
  * binding that owns only the graph's bound arrays, a process whose arena

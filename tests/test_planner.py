@@ -249,3 +249,40 @@ def test_batched_decode_plan_updates_caches_in_place(tiny_bf16):
     with pytest.raises(ValueError):
         BatchedDecoderStep(cfg, weights, batch=b, cache_length=ctx, dtype=dt)(
             Tensor(np.zeros((b + 1, 1), np.int32)), *inputs[1:4], list(zip(caches[::2], caches[1::2])))
+
+
+def test_batched_decode_plan_fuses_into_row_gemms_and_one_attention(tiny_bf16):
+    """With the row GEMM in play: per layer q/k/v (+ input norm), one attention kernel for
+    RoPE + cache blend + attention, O (+ residual), gate/up (+ norm), down (+ SwiGLU, residual)."""
+    from cuda_b200 import _lib
+    from cuda_b200.batched import BatchedDecoderStep
+
+    wl, weights = tiny_bf16
+    cfg, dt = wl.config, wl.np_dtype
+    b, ctx = 4, 48
+    shape = (b, cfg.num_key_value_heads, ctx, cfg.head_size)
+    caches = [Tensor.from_native(np.zeros(shape, np.float32), backend="cpu", shape=shape, dtype=dt)
+              for _ in range(2 * cfg.num_hidden_layers)]
+    am, wm = L.decode_masks(5, ctx, dt)
+    inputs = [Tensor(np.full((b, 1), 3, np.int32), copy=False),
+              Tensor(L.rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=5), copy=False),
+              Tensor(am, copy=False), Tensor(wm, copy=False), Tensor(np.asarray(5, np.int32), copy=False)]
+    outs = BatchedDecoderStep(cfg, weights, batch=b, cache_length=ctx, dtype=dt)(
+        *inputs[:4], list(zip(caches[::2], caches[1::2])), position=inputs[4])
+    p = Planner([o._node for o in outs], [t._node for t in inputs + caches], backend="cuda-b200",
+                leaf_dtype=_leaf_dtype, gemm_min_rows=64).build()
+    kinds = Counter(s.name for s in p.steps)
+    layers = cfg.num_hidden_layers
+    assert kinds["decode_attention_batched"] == layers
+    assert kinds["kv_write"] == kinds["rope"] == kinds["sdpa"] == 0
+    # 4 row GEMMs per layer (layer 0's O projection reads the bf16 embedding residual: kept apart) + lm_head
+    assert kinds["matmul_rows"] == 4 * layers
+    assert kinds["matmul"] == 1 and kinds["elementwise"] == 1
+    rows = [s for s in p.steps if s.name == "matmul_rows"]
+    assert sum(s.args["x_mode"] == _lib.ROWS_X_RMS for s in rows) == 2 * layers + 1
+    assert sum(s.args["x_mode"] == _lib.ROWS_X_SWIGLU for s in rows) == layers
+    assert sum(s.args["residual"] is not None for s in rows) == 2 * layers - 1
+    for s in p.steps:
+        if s.name == "decode_attention_batched":
+            assert s.args["k_cache"].buf.bind == "pointer" and s.args["batch"] == b
+    assert sorted(p.aliases) == list(range(1, 2 * layers + 1))
