@@ -114,6 +114,15 @@ class SdpaArgs(ctypes.Structure):
     ]
 
 
+class SampleArgs(ctypes.Structure):
+    _fields_ = [
+        ("logits", c_void_p), ("logits_dtype", c_int),
+        ("rows", c_longlong), ("width", c_longlong), ("ld", c_longlong),
+        ("temperature", ctypes.c_double), ("top_k", c_longlong),
+        ("uniforms", c_void_p), ("out", c_void_p), ("error_flag", c_void_p),
+    ]
+
+
 class GemvArgs(ctypes.Structure):
     _fields_ = [
         ("w", c_void_p * 3), ("w_rows", c_longlong * 3), ("n_w", c_int), ("w_dtype", c_int),
@@ -270,6 +279,7 @@ _SIGNATURES = {
                                 POINTER(DecodeStepConfig)], c_int),
     "cb_decode_step": ([c_void_p, POINTER(DecodeStepConfig), c_void_p, c_void_p, c_void_p], c_int),
     "cb_argmax_rows": ([c_void_p, c_int, c_longlong, c_longlong, c_void_p, c_void_p], c_int),
+    "cb_sample_rows": ([c_void_p, c_void_p], c_int),
     "cb_decode_advance": ([c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
                            c_int, c_longlong, c_void_p, c_longlong, c_void_p, c_void_p], c_int),
     "cb_decode_advance_rows": ([c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
@@ -299,6 +309,7 @@ def load() -> ctypes.CDLL:
 
 FLAG_INDEX, FLAG_POSITION, FLAG_CONTEXT = 1, 2, 3
 FLAG_WAIT_DATA, FLAG_WAIT_SLOT, FLAG_WAIT_DRAIN, FLAG_WAIT_PHASE = 4, 5, 6, 7
+FLAG_NAN = 8
 
 
 def flag_error(value: int) -> Exception:
@@ -309,6 +320,8 @@ def flag_error(value: int) -> Exception:
         return IndexError("RoPE position is outside the precomputed table")
     if value == FLAG_CONTEXT:
         return IndexError("decode step would write past the KV-cache context")
+    if value == FLAG_NAN:  # what NumPy's Generator.choice raises for the reference's sampler
+        return ValueError("probabilities contain NaN")
     waits = {FLAG_WAIT_DATA: "a consumer waiting for weight data",
              FLAG_WAIT_SLOT: "a producer waiting for a free ring slot",
              FLAG_WAIT_DRAIN: "the end-of-kernel drain of bulk copies",

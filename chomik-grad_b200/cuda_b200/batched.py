@@ -94,8 +94,9 @@ class BatchedRuntime(LlamaRuntime):
         self.batch = batch
         self._batched: dict = {}
 
-    def prefill_batch(self, prompts: Sequence[Sequence[int]], context: int) -> Tuple[List[int], List[Any]]:
-        """First greedy token of each prompt and the stacked (B, ...) caches."""
+    def prefill_batch(self, prompts: Sequence[Sequence[int]], context: int, *, temperature: float = 0.0,
+                      top_k: int = 50, rng: Optional[np.random.Generator] = None) -> Tuple[List[int], List[Any]]:
+        """First token of each prompt (greedy, or sampled with ``rng``) and the stacked (B, ...) caches."""
         if len(prompts) != self.batch or len({len(p) for p in prompts}) != 1:
             raise ValueError(f"{self.batch} prompts of equal length are required")
         import torch
@@ -103,7 +104,7 @@ class BatchedRuntime(LlamaRuntime):
         firsts, per_seq = [], []
         for prompt in prompts:
             logits, caches = self.prefill(prompt, context)
-            firsts.append(self.device.argmax(logits))
+            firsts.append(self.sample(logits, temperature, top_k, rng))
             per_seq.append(caches)
         stacked = []
         for i in range(len(per_seq[0])):
@@ -146,15 +147,24 @@ class BatchedRuntime(LlamaRuntime):
         produced = program.run(dict(zip(nodes, values + list(caches))), synchronize=False)
         return produced[0], list(produced[1:])
 
-    def generate_batch(self, prompts: Sequence[Sequence[int]], max_new_tokens: int) -> List[List[int]]:
-        """Greedy tokens of every sequence (first one from its prefill)."""
+    def generate_batch(self, prompts: Sequence[Sequence[int]], max_new_tokens: int, *,
+                       temperature: float = 0.0, top_k: int = 50, seed: int = 0) -> List[List[int]]:
+        """Tokens of every sequence (first one from its prefill): greedy at temperature 0, else
+        sampled per row on the device, one ``default_rng(seed)`` draw per token in row order."""
+        if temperature < 0 or top_k < 0:
+            raise ValueError("temperature and top-k cannot be negative")
+        rng = np.random.default_rng(seed)
         length = len(prompts[0])
         context = length + max_new_tokens
-        tokens, caches = self.prefill_batch(prompts, context)
+        tokens, caches = self.prefill_batch(prompts, context, temperature=temperature, top_k=top_k, rng=rng)
         out = [[t] for t in tokens]
         for i in range(1, max_new_tokens):
             logits, caches = self.decode_batch(tokens, length + i - 1, context, caches)
-            tokens = [int(t) for t in self.device.argmax_last_axis(logits)]
+            if temperature == 0:
+                tokens = [int(t) for t in self.device.argmax_last_axis(logits)]
+            else:
+                tokens = [int(t) for t in self.device.sample_rows(logits, temperature=temperature, top_k=top_k,
+                                                                  rng=rng)]
             for seq, t in zip(out, tokens):
                 seq.append(t)
         return out

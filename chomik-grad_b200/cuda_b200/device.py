@@ -14,6 +14,7 @@ a Python int after a 8-byte read-back; there is no host fallback.
 
 from __future__ import annotations
 
+import ctypes
 from pathlib import Path
 from typing import Any, Dict, Mapping, Optional, Sequence
 
@@ -223,6 +224,56 @@ class CudaB200Device(DeviceAdapter):
             _lib.call("cb_argmax_rows", array.data_ptr(), _lib.dtype_code(array.dtype), rows, width,
                       result.data_ptr(), self.stream())
         return result[:rows].cpu().numpy().reshape(array.shape[:-1])
+
+    def sample(self, value: object, *, temperature: float, top_k: int, rng: np.random.Generator) -> int:
+        """The reference's sampler on the device (generate_tinyllama.py:124-157).
+
+        Samples row 0 of the logits (the reference reads ``logits[0]``):
+        temperature 0 is ``argmax``; otherwise one ``rng.random()`` draw --
+        the one NumPy's ``Generator.choice`` would take -- selects the token
+        in cb_sample_rows, so only 8 bytes cross each way instead of the
+        logit row.  Raises ValueError where NumPy's choice does (NaN
+        probabilities).
+        """
+        if temperature == 0:
+            return self.argmax(value)
+        array = self.array(value)
+        width = array.shape[-1] if array.shape else 1
+        return int(self._sample(array, 1, width, temperature, top_k, rng)[0])
+
+    def sample_rows(self, value: object, *, temperature: float, top_k: int,
+                    rng: np.random.Generator) -> np.ndarray:
+        """``sample`` for every row of the last axis, drawing in row order (batched decode)."""
+        if temperature == 0:
+            return self.argmax_last_axis(value)
+        array = self.array(value)
+        width = array.shape[-1] if array.shape else 1
+        rows = array.size // width if width else 0
+        return self._sample(array, rows, width, temperature, top_k, rng).reshape(array.shape[:-1])
+
+    def _sample(self, array: DeviceArray, rows: int, width: int, temperature: float, top_k: int,
+                rng: np.random.Generator) -> np.ndarray:
+        if width == 0:
+            raise ValueError("cannot sample from an empty sequence")
+        if not np.isfinite(temperature) or temperature < 0:
+            raise ValueError(f"temperature must be finite and >= 0 on cuda-b200, got {temperature}")
+        torch = _torch()
+        uniforms = rng.random(rows)  # the draws rng.choice would take, in row order
+        dev = self.torch_device
+        u = torch.from_numpy(uniforms).to(dev, non_blocking=False)
+        result = torch.empty(rows + 1, dtype=torch.int64, device=dev)  # tokens, then the error flag
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        a = _lib.SampleArgs()
+        a.logits, a.logits_dtype = array.data_ptr(), _lib.dtype_code(array.dtype)
+        a.rows, a.width, a.ld = rows, width, width
+        a.temperature, a.top_k = float(temperature), int(top_k)
+        a.uniforms, a.out, a.error_flag = u.data_ptr(), result.data_ptr(), flag.data_ptr()
+        _lib.call("cb_sample_rows", ctypes.byref(a), self.stream())
+        result[rows:].copy_(flag)
+        host = result.cpu().numpy()
+        if host[rows]:
+            raise _lib.flag_error(int(host[rows]))
+        return host[:rows].copy()
 
     def dtype(self, value: object) -> np.dtype:
         if isinstance(value, DeviceArray):

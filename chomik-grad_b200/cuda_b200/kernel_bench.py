@@ -4,6 +4,7 @@
     python -m cuda_b200.kernel_bench gemm_tc   [--m 2048 --n 5632 --k 2048]
     python -m cuda_b200.kernel_bench sdpa_query [--batch 32 --heads 32 --kv 4 --tokens 768 --hd 64]
     python -m cuda_b200.kernel_bench batched   [--workload tinyllama-bf16-bs32 --steps 20 --prompt 64]
+    python -m cuda_b200.kernel_bench sample    [--rows 1 --width 32000 --top-k 50]
 
 Each prints CUDA-event times (warm, averaged over --reps launches on the
 current stream).  ``batched`` wraps the timed graph replays in
@@ -121,6 +122,29 @@ def sdpa_query(args) -> None:
           f"{2 * b * kv * t * hd * 4 / ms / 1e6:.0f} GB/s of K/V")
 
 
+def sample(args) -> None:
+    import torch
+
+    from . import _lib
+
+    rows, width = args.rows, args.width
+    logits = torch.randn(rows, width, device="cuda") * 2.0
+    uniforms = torch.rand(rows, dtype=torch.float64, device="cuda")
+    out = torch.empty(rows, dtype=torch.int64, device="cuda")
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = _lib.SampleArgs()
+    a.logits, a.logits_dtype, a.rows, a.width, a.ld = logits.data_ptr(), _lib.F32, rows, width, width
+    a.temperature, a.top_k = 0.8, args.top_k
+    a.uniforms, a.out, a.error_flag = uniforms.data_ptr(), out.data_ptr(), flag.data_ptr()
+    stream = torch.cuda.current_stream().cuda_stream
+    ms = _timed(lambda: _lib.call("cb_sample_rows", ctypes.byref(a), stream), args.reps)
+    # what the host sampler needs first: the rows in host memory
+    host = torch.empty(rows, width, pin_memory=True)
+    copy_ms = _timed(lambda: host.copy_(logits, non_blocking=True), args.reps)
+    print(f"cb_sample_rows rows {rows} width {width} top_k {args.top_k}: {ms * 1000:.1f} us "
+          f"(device-to-host copy of the rows alone: {copy_ms * 1000:.1f} us), error flag {int(flag.item())}")
+
+
 def batched(args) -> None:
     import torch
 
@@ -144,7 +168,7 @@ def batched(args) -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("kernel", choices=("sdpa_tc", "gemm_tc", "sdpa_query", "batched"))
+    parser.add_argument("kernel", choices=("sdpa_tc", "gemm_tc", "sdpa_query", "batched", "sample"))
     parser.add_argument("--reps", type=int, default=20)
     parser.add_argument("--tokens", type=int, default=None)
     parser.add_argument("--heads", type=int, default=32)
@@ -158,12 +182,16 @@ def main() -> None:
     parser.add_argument("--workload", default="tinyllama-bf16-bs32")
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--prompt", type=int, default=64)
+    parser.add_argument("--rows", type=int, default=1)
+    parser.add_argument("--width", type=int, default=32000)
+    parser.add_argument("--top-k", type=int, default=50)
     args = parser.parse_args()
     if args.kv is None:
         args.kv = 4
     if args.tokens is None:
         args.tokens = 2048 if args.kernel == "sdpa_tc" else 768
-    {"sdpa_tc": sdpa_tc, "gemm_tc": gemm_tc, "sdpa_query": sdpa_query, "batched": batched}[args.kernel](args)
+    {"sdpa_tc": sdpa_tc, "gemm_tc": gemm_tc, "sdpa_query": sdpa_query, "batched": batched,
+     "sample": sample}[args.kernel](args)
 
 
 if __name__ == "__main__":

@@ -9,7 +9,9 @@
 * the decode step graph is compiled once per context with tokens, rotation,
   attention mask, write mask, position and the 2L caches as dynamic inputs
   (:788-842) and replayed with fresh host inputs every step;
-* the greedy token is ``device.argmax`` of the step's logits (:146-157);
+* the token is ``device.argmax`` of the step's logits at temperature 0, else
+  the device's temperature / top-k sampler with the reference's seeded
+  generator (:124-157, :712);
 * the caches returned by step n are bound as inputs of step n+1 (:857).
 
 It works with any registered compiler: ``cuda-b200`` for the product path,
@@ -191,9 +193,27 @@ class LlamaRuntime:
         return (tokens, start.elapsed_time(end)) if timed else tokens
 
     # -- the loop ---------------------------------------------------------
+    def sample(self, logits: Any, temperature: float, top_k: int, rng: np.random.Generator) -> int:
+        """sample_native_token (generate_tinyllama.py:146-157): argmax at temperature 0, else the
+        device's sampler (cb_sample_rows on cuda-b200: one draw up, one token down)."""
+        if temperature == 0:
+            return self.device.argmax(logits)
+        return int(self.device.sample(logits, temperature=temperature, top_k=top_k, rng=rng))
+
     def generate(self, prompt_ids: Sequence[int], max_new_tokens: int, *,
-                 stop_at_eos: bool = False) -> GenerationResult:
-        """Greedy decode (temperature 0) like generate_tinyllama.py:719-857."""
+                 stop_at_eos: bool = False, temperature: float = 0.0, top_k: int = 50,
+                 seed: int = 0) -> GenerationResult:
+        """Decode like generate_tinyllama.py:678-857 (greedy at temperature 0, the default).
+
+        The sampler's generator is ``np.random.default_rng(seed)`` (:712),
+        drawn once per sampled token, so a run consumes the same random
+        stream as the reference's with the same seed.
+        """
+        if temperature < 0:
+            raise ValueError("temperature cannot be negative")
+        if top_k < 0:
+            raise ValueError("top-k cannot be negative")
+        rng = np.random.default_rng(seed)
         prompt = [int(t) for t in prompt_ids]
         if not prompt:
             raise ValueError("the prompt produced no tokens")
@@ -203,7 +223,7 @@ class LlamaRuntime:
                              f"{self.config.max_position_embeddings}")
         started = time.perf_counter()
         logits, caches = self.prefill(prompt, context)
-        token = self.device.argmax(logits)
+        token = self.sample(logits, temperature, top_k, rng)
         result = GenerationResult([token], time.perf_counter() - started)
         tokens = prompt + [token]
         for _ in range(1, max_new_tokens):
@@ -211,7 +231,7 @@ class LlamaRuntime:
                 break
             begun = time.perf_counter()
             logits, caches = self.decode(token, len(tokens) - 1, context, caches)
-            token = self.device.argmax(logits)
+            token = self.sample(logits, temperature, top_k, rng)
             result.step_seconds.append(time.perf_counter() - begun)
             tokens.append(token)
             result.tokens.append(token)

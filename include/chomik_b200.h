@@ -30,8 +30,9 @@ enum { CB_OK = 0, CB_ERR_INVALID = 1, CB_ERR_CUDA = 2 };
 
 /* values kernels store in an `error_flag` (0 = no error): an index outside
  * its table, a RoPE position outside the table, a decode step past the
- * context, and bounded waits that gave up (a consumer waiting for data, a
- * producer waiting for a free slot, the end-of-kernel drain of copies) */
+ * context, bounded waits that gave up (a consumer waiting for data, a
+ * producer waiting for a free slot, the end-of-kernel drain of copies), and a
+ * sampled row whose probabilities are NaN */
 enum {
   CB_FLAG_INDEX = 1,
   CB_FLAG_POSITION = 2,
@@ -39,7 +40,8 @@ enum {
   CB_FLAG_WAIT_DATA = 4,
   CB_FLAG_WAIT_SLOT = 5,
   CB_FLAG_WAIT_DRAIN = 6,
-  CB_FLAG_WAIT_PHASE = 7 /* cb_decode_step: a block waiting for the previous phase */
+  CB_FLAG_WAIT_PHASE = 7, /* cb_decode_step: a block waiting for the previous phase */
+  CB_FLAG_NAN = 8         /* cb_sample_rows: NaN probabilities */
 };
 
 #define CB_MAX_DIMS 8
@@ -637,6 +639,28 @@ CB_API int cb_decode_advance_rows(const long long* argmax, long long rows, void*
  * cuda_backend.py:37-41). */
 CB_API int cb_argmax_rows(const void* x, int dtype, long long rows, long long width,
                    long long* out_index, cb_stream_t stream);
+
+/* Temperature / top-k sampling of each row of a logit matrix, on the device.
+ * Replaces the host sampler sample_token (examples/generate_tinyllama.py
+ * :124-143) that sample_native_token (:146-157) calls for temperature != 0:
+ * v = logits / temperature in float64, top-k filter, p = softmax(v),
+ * token = the first index whose cumulative p exceeds u * sum(p), where u is
+ * the caller's draw -- NumPy's Generator.choice(V, p=p) takes exactly one
+ * u = rng.random() and returns that index.  Ties at the k-th largest value
+ * keep the lowest indices.  A row with a NaN logit, or whose largest
+ * logit / temperature is not finite, gets token -1 and CB_FLAG_NAN (NumPy's
+ * choice raises ValueError on NaN probabilities). */
+typedef struct {
+  const void* logits;
+  int logits_dtype;            /* CB_F32 / CB_BF16 / CB_F16 */
+  long long rows, width, ld;   /* ld: elements between consecutive rows (>= width) */
+  double temperature;          /* > 0 (temperature 0 is cb_argmax_rows) */
+  long long top_k;             /* <= 0 or >= width: no top-k filter */
+  const double* uniforms;      /* device: one draw in [0, 1) per row */
+  long long* out;              /* device: one token id per row */
+  int* error_flag;             /* optional: CB_FLAG_NAN */
+} cb_sample_args;
+CB_API int cb_sample_rows(const cb_sample_args* a, cb_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -114,6 +114,22 @@ class NumpyDeviceAdapter(DeviceAdapter):
     def argmax(self, value: object) -> int:
         return int(np.asarray(value).argmax())
 
+    def sample(self, value: object, *, temperature: float, top_k: int, rng: np.random.Generator) -> int:
+        """The reference's host sampler (generate_tinyllama.py:124-157) on the oracle's arrays."""
+        from .sampling import sample_token
+
+        return sample_token(np.asarray(value), temperature=temperature, top_k=top_k, rng=rng)
+
+    def sample_rows(self, value: object, *, temperature: float, top_k: int,
+                    rng: np.random.Generator) -> np.ndarray:
+        from .sampling import sample_token
+
+        rows = np.asarray(value)
+        flat = rows.reshape(-1, rows.shape[-1])
+        out = [sample_token(flat[i:i + 1], temperature=temperature, top_k=top_k, rng=rng)
+               for i in range(flat.shape[0])]
+        return np.asarray(out, dtype=np.int64).reshape(rows.shape[:-1])
+
     def dtype(self, value: object) -> np.dtype:
         return np.asarray(value).dtype
 

@@ -31,6 +31,7 @@ sys.dont_write_bytecode = True
 
 def _reference(path: str):
     sys.path.insert(0, path)
+    sys.path.insert(0, str(Path(path) / "examples"))
     import chomikgrad  # noqa: F401
     from chomikgrad import Tensor, compile_graph, get_compiler, no_grad
     from chomikgrad import llama as L
@@ -72,9 +73,25 @@ def six_ops(ref) -> dict:
     return out
 
 
-def generation(ref, workload_name: str, steps: int, keep_logits: tuple) -> dict:
-    """Prefill + greedy decode with the reference classes and its cpu compiler."""
+def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling=None) -> dict:
+    """Prefill + decode with the reference classes and its cpu compiler.
+
+    Greedy, or with ``sampling = (temperature, top_k, seed)`` each token from
+    the reference's own ``sample_native_token`` (generate_tinyllama.py:146-157)
+    with ``np.random.default_rng(seed)`` (:712).
+    """
     Tensor, compile_graph, get_compiler, no_grad, L = ref
+    if sampling is not None:
+        from generate_tinyllama import sample_native_token
+
+        temperature, top_k, seed = sampling
+        rng = np.random.default_rng(seed)
+
+        def pick(native):
+            return sample_native_token(native, temperature=temperature, top_k=top_k, rng=rng, device=device)
+    else:
+        def pick(native):
+            return device.argmax(native)
     from cuda_b200.models import WORKLOADS, synthetic_prompt, synthetic_weights
     from cuda_b200.frontend.llama import decode_masks
 
@@ -98,7 +115,7 @@ def generation(ref, workload_name: str, steps: int, keep_logits: tuple) -> dict:
         sel = Tensor(L.position_selector(len(prompt) - 1, len(prompt), dtype=dtype), copy=False)
         program = compile_graph(*model.prefill(ids, sel), compiler="cpu", dynamic_inputs=(ids,))
         native = program.run(None, synchronize=False)
-        token = device.argmax(native[0])
+        token = pick(native[0])
         out["prefill_logits"] = np.asarray(native[0], dtype=np.float32)
         caches = list(native[1:])
         out["prefill_cache_dtype"] = np.array(str(np.asarray(caches[0]).dtype))
@@ -132,7 +149,7 @@ def generation(ref, workload_name: str, steps: int, keep_logits: tuple) -> dict:
                 bindings = dict(zip(nodes, [device.array(v) for v in host] + caches))
             native = decoder.run(bindings, synchronize=False)
             logits = np.asarray(native[0], dtype=np.float32)
-            token = device.argmax(native[0])
+            token = pick(native[0])
             order = np.argsort(-logits[0], kind="stable")[:8]
             top.append(np.stack([order.astype(np.float32), logits[0, order]]))
             if i in keep_logits:
@@ -148,6 +165,32 @@ def generation(ref, workload_name: str, steps: int, keep_logits: tuple) -> dict:
                                        float(np.sum(np.abs(np.asarray(c, np.float64))))]
                                       for c in caches])
     return out
+
+
+def sampling_rows(ref) -> dict:
+    """The reference's host sampler (generate_tinyllama.py:124-143) on seeded logit rows.
+
+    Rows: N(0, 3) logits, one with a third of its entries -inf (masked), one
+    float32 row rounded from bfloat16; per (temperature, top_k) setting the
+    token each of a list of seeds gives (a fresh default_rng(seed) per draw).
+    """
+    from generate_tinyllama import sample_token
+    import ml_dtypes
+
+    rng = np.random.default_rng(11)
+    width = 2048
+    rows = rng.normal(0.0, 3.0, (4, width)).astype(np.float32)
+    rows[1, rng.permutation(width)[: width // 3]] = -np.inf
+    rows[2] = rows[2].astype(ml_dtypes.bfloat16).astype(np.float32)
+    settings = np.array([[0.7, 0], [1.0, 40], [1.5, 1], [0.25, 5], [1.0, width - 1], [2.0, width]], np.float64)
+    seeds = np.arange(24, dtype=np.int64) * 7919 + 5
+    tokens = np.zeros((rows.shape[0], len(settings), len(seeds)), np.int64)
+    for r in range(rows.shape[0]):
+        for s, (temperature, top_k) in enumerate(settings):
+            for j, seed in enumerate(seeds):
+                tokens[r, s, j] = sample_token(rows[r:r + 1], temperature=float(temperature), top_k=int(top_k),
+                                               rng=np.random.default_rng(int(seed)))
+    return {"rows": rows, "settings": settings, "seeds": seeds, "tokens": tokens}
 
 
 def block_decode(ref) -> dict:
@@ -194,6 +237,8 @@ CASES = {
     "tiny_bf16": lambda ref: generation(ref, "tiny-bf16", 32, (1, 31)),
     "tiny_block": lambda ref: block_decode(ref),
     "tinyllama_bf16": lambda ref: generation(ref, "tinyllama-bf16-bs1", 128, (1, 2, 64, 127)),
+    "sampling": lambda ref: sampling_rows(ref),
+    "tiny_fp32_sampled": lambda ref: generation(ref, "tiny-fp32", 32, (), sampling=(0.8, 40, 3)),
 }
 
 

@@ -50,6 +50,7 @@ STRUCTS = {
     "cb_gemm_rows_args": _lib.GemmRowsArgs,
     "cb_step_phase": _lib.StepPhase,
     "cb_decode_step_config": _lib.DecodeStepConfig,
+    "cb_sample_args": _lib.SampleArgs,
 }
 
 
