@@ -38,6 +38,7 @@ from .frontend.lazy import CompiledProgram
 from .planner import Buffer, Plan, Step, View, bf16, contiguous_strides, gemm_shape  # noqa: F401
 
 _BF16 = bf16()
+_UNBOUND = object()  # a leaf without a binding in this run
 
 
 def _torch():
@@ -186,6 +187,7 @@ class CudaB200Program(CompiledProgram):
                 self._ptr[buf] = arr.data_ptr()
             else:
                 self._per_run.append((leaf, buf))
+        self._last_bound: List[Optional[Tuple[DeviceArray, int]]] = [None] * len(self._per_run)
 
     @staticmethod
     def _check(arr: DeviceArray, buf: Buffer) -> None:
@@ -196,21 +198,36 @@ class CudaB200Program(CompiledProgram):
                             f"{buf.dtype}; compile a new program for this dtype")
 
     def _bind(self, bindings: Mapping) -> Tuple[Dict[object, DeviceArray], tuple]:
-        bound: Dict[object, DeviceArray] = dict(self._constants)
+        """Per-run inputs: pointers of pointer-bound leaves, host values into the input slots.
+
+        A pointer-bound leaf rebound with the very DeviceArray it had last
+        run (the caches a decode step returned, bound to the next step) keeps
+        its checked pointer without re-checking.
+        """
+        bound: Dict[object, DeviceArray] = {}
         key = []
         device_copies = []
         staged = False
-        for leaf, buf in self._per_run:
-            if leaf in bindings:
-                arr = self.device.array(bindings[leaf])
-            else:
-                arr = self._load(leaf)
+        last = self._last_bound
+        for i, (leaf, buf) in enumerate(self._per_run):
+            value = bindings.get(leaf, _UNBOUND)
+            if buf.bind == "pointer":
+                prev = last[i]
+                if prev is not None and value is prev[0]:
+                    arr, ptr = prev
+                else:
+                    arr = self.device.array(value) if value is not _UNBOUND else self._load(leaf)
+                    self._check(arr, buf)
+                    ptr = arr.data_ptr()
+                    last[i] = (arr, ptr) if value is arr else None
+                bound[leaf] = arr
+                self._ptr[buf] = ptr
+                key.append(ptr)
+                continue
+            arr = self.device.array(value) if value is not _UNBOUND else self._load(leaf)
             self._check(arr, buf)
             bound[leaf] = arr
-            if buf.bind == "pointer":
-                self._ptr[buf] = arr.data_ptr()
-                key.append(self._ptr[buf])
-            elif arr.size == 0:
+            if arr.size == 0:
                 continue
             elif arr.host is not None:  # pending host input: through the pinned mirror
                 if not staged and self._staging_done is not None:
@@ -320,8 +337,8 @@ class CudaB200Program(CompiledProgram):
             if alias is not None:
                 outs.append(bound[alias])
                 continue
-            if node.op is None and node in bound:
-                outs.append(bound[node])
+            if node.op is None and (node in bound or node in self._constants):
+                outs.append(bound[node] if node in bound else self._constants[node])
                 continue
             outs.append(self._copy_out(view, node.shape))
             argmax = self.plan.argmax_of.get(index)

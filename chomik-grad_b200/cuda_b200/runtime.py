@@ -72,6 +72,7 @@ class LlamaRuntime:
                     dtype=self.device.dtype(native))
         self._prefill: Dict[Tuple[int, int], Tuple[Any, Any]] = {}
         self._decoders: Dict[int, Tuple[Any, List[Any]]] = {}
+        self._ahead: Optional[Tuple[Tuple[int, int], List[Any]]] = None
 
     # -- one program each -------------------------------------------------
     def prefill(self, prompt_ids: Sequence[int], context: int) -> Tuple[Any, List[Any]]:
@@ -99,11 +100,22 @@ class LlamaRuntime:
 
     def step_inputs(self, token: int, position: int, context: int) -> List[np.ndarray]:
         """Host inputs of one decode step, built as generate_tinyllama.py:773-786 builds them."""
+        return [np.asarray([[token]], dtype=np.int32), *self._position_host(position, context)]
+
+    def _position_host(self, position: int, context: int) -> List[np.ndarray]:
+        """The inputs of a step that depend on its position only: rotation, masks, position."""
         c = self.config
-        ids = np.asarray([[token]], dtype=np.int32)
         rotation = rope_rotations(1, c.head_size, c.rope_theta, self.dtype, offset=position)
         attention, write = decode_masks(position, context, self.dtype)
-        return [ids, rotation, attention, write, np.asarray(position, dtype=np.int32)]
+        return [rotation, attention, write, np.asarray(position, dtype=np.int32)]
+
+    def _position_values(self, position: int, context: int) -> List[Any]:
+        """Native position inputs of a step: prepared by the previous decode() while the device ran it."""
+        ahead = self._ahead
+        self._ahead = None
+        if ahead is not None and ahead[0] == (position, context):
+            return ahead[1]
+        return [self.device.array(v) for v in self._position_host(position, context)]
 
     def decode_program(self, context: int, caches: List[Any], token: int, position: int):
         """The cached decode program for ``context`` (compiled on first use)."""
@@ -130,10 +142,20 @@ class LlamaRuntime:
 
     def decode(self, token: int, position: int, context: int,
                caches: List[Any]) -> Tuple[Any, List[Any]]:
-        """One cached step: bind fresh host inputs and the previous caches."""
+        """One cached step: bind fresh host inputs and the previous caches.
+
+        The next position's rotation and masks (they do not depend on the
+        token) are built after the launch, while the device runs this step,
+        so the host's share of the step is shorter; the token id is bound
+        when it is known.
+        """
         program, nodes = self.decode_program(context, caches, token, position)
-        values = [self.device.array(v) for v in self.step_inputs(token, position, context)]
+        values = [self.device.array(np.asarray([[token]], dtype=np.int32)),
+                  *self._position_values(position, context)]
         produced = program.run(dict(zip(nodes, values + list(caches))), synchronize=False)
+        if position + 1 < context:
+            nxt = position + 1
+            self._ahead = ((nxt, context), [self.device.array(v) for v in self._position_host(nxt, context)])
         return produced[0], list(produced[1:])
 
     def decode_on_device(self, token: int, position: int, context: int, caches: List[Any],
