@@ -238,17 +238,93 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const cb
   attention_item<HD>(a, blockIdx.y, blockIdx.x, gridDim.x, smem, &s_last, threadIdx.x);
 }
 
-// Batched decode: grid (splits, kv_heads, batch).  Sequence b's q | k | v
-// row starts at qkv + b * qkv_stride; its caches, output, partials and
-// counters are the b-th of `batch` equal slices; position, masks and RoPE
-// row are shared (the sequences step together).
+// ---- batched decode attention -------------------------------------------
+// Sequence b's q | k | v row starts at qkv + b * qkv_stride; its caches,
+// output, partials and counters are the b-th of `batch` equal slices;
+// position, masks and RoPE row are shared (the sequences step together).
+// One CTA per (range of 32-key chunks, KV head, sequence).  The chunks of a
+// range are staged with cp.async into two alternating shared-memory buffers
+// (the next chunk's copies are in flight while the current one is scored),
+// each query head keeps an online softmax state (max, sum, p.v) across the
+// chunks, and one partial per head is written per CTA; the last CTA of a
+// (sequence, KV head) group merges the partials in range order.  Per chunk
+// the arithmetic is the single-sequence decode attention's (RoPE of q and
+// k at the bound position, write-mask blend of the cache rows, scores
+// s / divisor + mask, exp against the running max).
 template <int HD>
+struct ChunkSmem {
+  static constexpr int KS = HD + 4;  // padded K rows: conflict-free float4 score loads
+  // one staging buffer: K rows [32][KS], V rows [32][HD], write mask [32], mask [32]
+  static constexpr int kBuf = kAttnSplit * KS + kAttnSplit * HD + 2 * kAttnSplit;
+  float *q_rot, *k_new, *v_new, *cs, *sn, *bufs;
+  __device__ ChunkSmem(float* smem, int group) {
+    q_rot = smem;                // [group][HD]
+    k_new = q_rot + group * HD;  // [HD]
+    v_new = k_new + HD;          // [HD]
+    cs = v_new + HD;             // [HD / 2]
+    sn = cs + HD / 2;            // [HD / 2]
+    bufs = sn + HD / 2;          // [2][kBuf]; a multiple of 4 floats from the base: 16-byte aligned rows
+  }
+  __device__ float* ks(int b) const { return bufs + b * kBuf; }
+  __device__ float* vs(int b) const { return ks(b) + kAttnSplit * KS; }
+  __device__ float* wm(int b) const { return vs(b) + kAttnSplit * HD; }
+  __device__ float* maskv(int b) const { return wm(b) + kAttnSplit; }
+};
+
+inline long long chunk_smem_floats(long long group, long long hd) {
+  return (group + 2) * hd + hd + 2 * (kAttnSplit * (hd + 4) + kAttnSplit * hd + 2 * kAttnSplit);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Issue the copies of chunk `chunk`'s K/V rows into buffer `buf` (one commit
+// group per thread, possibly empty).
+template <int HD>
+__device__ __forceinline__ void stage_chunk(const cb_decode_attention_args& a, const ChunkSmem<HD>& s, int buf, int g,
+                                            long long chunk, int tid) {
+  const long long lo = chunk * kAttnSplit;
+  const int n = attn_rows(a, static_cast<int>(chunk));
+  const float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo) * HD;
+  const float* vc = a.v_cache + (static_cast<long long>(g) * a.context + lo) * HD;
+  for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
+    const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
+    cp_async16(s.ks(buf) + r * ChunkSmem<HD>::KS + d4, kc + 4 * e);
+    cp_async16(s.vs(buf) + r * HD + d4, vc + 4 * e);
+  }
+  cp_async_commit();
+}
+
+// Write-mask and mask value of row `tid` of chunk `chunk` (threads tid < 32;
+// the loads are consumed later, so they stay in flight meanwhile).
+__device__ __forceinline__ void chunk_masks(const cb_decode_attention_args& a, long long chunk, int tid, float* wm,
+                                            float* mk) {
+  const long long r = chunk * kAttnSplit + tid;
+  const bool in = tid < kAttnSplit && r < a.context;
+  *wm = in ? load_as_f32(a.write_mask, r, a.write_mask_dtype) : 0.0f;
+  *mk = in ? load_as_f32(a.mask, r, a.mask_dtype) : 0.0f;
+}
+
+template <int HD, int HPW>  // HPW: query heads per warp (group <= 8 * HPW)
 __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kernel(const cb_decode_attention_args args,
-                                                                                   long long qkv_stride) {
+                                                                                   long long qkv_stride,
+                                                                                   int chunks_per_cta) {
   extern __shared__ float smem[];
   __shared__ int s_last;
   cb_decode_attention_args a = args;
   const long long b = blockIdx.z;
+  const int g = static_cast<int>(blockIdx.y);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int warps = kAttnThreads / 32;
+  constexpr int half = HD / 2;
+  constexpr int KS = ChunkSmem<HD>::KS;
+  constexpr int kPairs = (HD + 63) / 64;  // float2 output dims per lane
   const long long kv_rows = a.kv_heads * a.context * a.head_size;
   a.qkv += b * qkv_stride;
   a.k_cache += b * kv_rows;
@@ -256,7 +332,203 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
   a.out += b * a.heads * a.head_size;
   a.scratch += b * static_cast<long long>(gridDim.x) * a.heads * (a.head_size + 2);
   a.counters += b * a.kv_heads;
-  attention_item<HD, false>(a, blockIdx.y, blockIdx.x, gridDim.x, smem, &s_last, threadIdx.x);
+  const int group = static_cast<int>(a.heads / a.kv_heads);
+  ChunkSmem<HD> s(smem, group);
+  const long long splits = (a.context + kAttnSplit - 1) / kAttnSplit;
+  const long long c0 = static_cast<long long>(blockIdx.x) * chunks_per_cta;
+  const long long c1 = c0 + chunks_per_cta < splits ? c0 + chunks_per_cta : splits;
+
+  // the first chunk's copies and mask values overlap the RoPE row and q/k/v loads
+  stage_chunk<HD>(a, s, 0, g, c0, tid);
+  float wm_next, mk_next;
+  chunk_masks(a, c0, tid, &wm_next, &mk_next);
+  long long pos = load_index(a.position, 0, a.position_dtype);
+  if (pos < 0 || pos >= a.n_positions) {
+    if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_POSITION);
+    pos = pos < 0 ? 0 : a.n_positions - 1;
+  }
+  for (int j = tid; j < half; j += kAttnThreads) {
+    s.cs[j] = a.cos_table[pos * half + j];
+    s.sn[j] = a.sin_table[pos * half + j];
+  }
+  attn_sync();
+  for (int i = tid; i < group * half; i += kAttnThreads) {
+    const int h = i / half, j = i % half;
+    const float* src = a.qkv + a.q_off + (static_cast<long long>(g) * group + h) * HD;
+    const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = s.cs[j], sv = s.sn[j];
+    s.q_rot[h * HD + j] = fmaf(-hi, sv, __fmul_rn(lo, c));
+    s.q_rot[h * HD + j + half] = fmaf(hi, c, __fmul_rn(lo, sv));
+  }
+  for (int j = tid; j < half; j += kAttnThreads) {
+    const float* src = a.qkv + a.k_off + static_cast<long long>(g) * HD;
+    const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = s.cs[j], sv = s.sn[j];
+    s.k_new[j] = fmaf(-hi, sv, __fmul_rn(lo, c));
+    s.k_new[j + half] = fmaf(hi, c, __fmul_rn(lo, sv));
+  }
+  for (int d = tid; d < HD; d += kAttnThreads) s.v_new[d] = __ldcg(a.qkv + a.v_off + static_cast<long long>(g) * HD + d);
+  if (tid < kAttnSplit) {
+    s.wm(0)[tid] = wm_next;
+    s.maskv(0)[tid] = mk_next;
+  }
+
+  float m_run[HPW], l_run[HPW];
+  float2 acc[HPW][kPairs];
+#pragma unroll
+  for (int k = 0; k < HPW; ++k) {
+    m_run[k] = -INFINITY;
+    l_run[k] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPairs; ++i) acc[k][i] = make_float2(0.0f, 0.0f);
+  }
+
+  for (long long c = c0; c < c1; ++c) {
+    const int buf = static_cast<int>((c - c0) & 1);
+    const bool more = c + 1 < c1;
+    if (more) {
+      stage_chunk<HD>(a, s, buf ^ 1, g, c + 1, tid);
+      chunk_masks(a, c + 1, tid, &wm_next, &mk_next);  // stored after this chunk's scores
+      cp_async_wait<1>();  // this thread's copies of chunk c have landed
+    } else {
+      cp_async_wait<0>();
+    }
+    attn_sync();  // every thread's copies of chunk c (and, first time round, q/k/v) are visible
+
+    // rows with wm != 0 get the blend, in shared memory and in the cache
+    const long long lo_pos = c * kAttnSplit;
+    const int n = attn_rows(a, static_cast<int>(c));
+    float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
+    float* vc = a.v_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
+    float* ks = s.ks(buf);
+    float* vs = s.vs(buf);
+    for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
+      const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
+      const float wm = s.wm(buf)[r];
+      if (wm == 0.0f) continue;
+      const float keep = round_to(__fsub_rn(1.0f, wm), a.one_minus_dtype);
+      float4 kv = *reinterpret_cast<float4*>(ks + r * KS + d4);
+      float4 vv = *reinterpret_cast<float4*>(vs + r * HD + d4);
+      float* kf = &kv.x;
+      float* vf = &vv.x;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        kf[i] = __fadd_rn(__fmul_rn(kf[i], keep), __fmul_rn(s.k_new[d4 + i], wm));
+        vf[i] = __fadd_rn(__fmul_rn(vf[i], keep), __fmul_rn(s.v_new[d4 + i], wm));
+      }
+      reinterpret_cast<float4*>(kc)[e] = kv;
+      reinterpret_cast<float4*>(vc)[e] = vv;
+      *reinterpret_cast<float4*>(ks + r * KS + d4) = kv;
+      *reinterpret_cast<float4*>(vs + r * HD + d4) = vv;
+    }
+    attn_sync();
+
+    // one warp per query head: scores with lane = position, then p @ v with
+    // lane = two dims, folded into the head's running state
+#pragma unroll
+    for (int k = 0; k < HPW; ++k) {
+      const int h = warp + k * warps;
+      if (h >= group) break;
+      float x = -INFINITY;
+      if (lane < n) {
+        const float4* q = reinterpret_cast<const float4*>(s.q_rot + h * HD);
+        const float4* kr = reinterpret_cast<const float4*>(ks + lane * KS);
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+#pragma unroll
+        for (int d = 0; d < HD / 4; ++d) {
+          const float4 qa = q[d], ka = kr[d];
+          s0 = fmaf(qa.x, ka.x, s0);
+          s1 = fmaf(qa.y, ka.y, s1);
+          s2 = fmaf(qa.z, ka.z, s2);
+          s3 = fmaf(qa.w, ka.w, s3);
+        }
+        x = __fadd_rn(__fdiv_rn((s0 + s1) + (s2 + s3), a.divisor), s.maskv(buf)[lane]);
+      }
+      const float mn = fmaxf(m_run[k], warp_max(x));
+      const float scale = expf(m_run[k] - mn);  // 0 on the first chunk (running max -inf)
+      const float p = lane < n ? expf(x - mn) : 0.0f;
+      l_run[k] = fmaf(l_run[k], scale, warp_sum(p));
+      m_run[k] = mn;
+#pragma unroll
+      for (int i = 0; i < kPairs; ++i) {
+        const int d = i * 64 + 2 * lane;
+        const bool mine = d < HD;
+        float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
+        for (int j = 0; j < n; j += 2) {  // every lane shuffles; rows j < n only are read
+          const float p0 = __shfl_sync(0xffffffffu, p, j);
+          const float p1 = __shfl_sync(0xffffffffu, p, j + 1);
+          if (mine) {
+            const float2 v0 = *reinterpret_cast<const float2*>(vs + j * HD + d);
+            a0.x = fmaf(p0, v0.x, a0.x);
+            a0.y = fmaf(p0, v0.y, a0.y);
+            if (j + 1 < n) {
+              const float2 v1 = *reinterpret_cast<const float2*>(vs + (j + 1) * HD + d);
+              a1.x = fmaf(p1, v1.x, a1.x);
+              a1.y = fmaf(p1, v1.y, a1.y);
+            }
+          }
+        }
+        acc[k][i].x = fmaf(acc[k][i].x, scale, a0.x + a1.x);
+        acc[k][i].y = fmaf(acc[k][i].y, scale, a0.y + a1.y);
+      }
+    }
+    if (more && tid < kAttnSplit) {
+      s.wm(buf ^ 1)[tid] = wm_next;
+      s.maskv(buf ^ 1)[tid] = mk_next;
+    }
+    attn_sync();  // buffer `buf` is refilled by the copies issued for chunk c + 2
+  }
+
+  // this CTA's partial per head: (max, sum, unnormalised output)
+#pragma unroll
+  for (int k = 0; k < HPW; ++k) {
+    const int h = warp + k * warps;
+    if (h >= group) break;
+    float* part = a.scratch + (static_cast<long long>(blockIdx.x) * a.heads + g * group + h) * (HD + 2);
+#pragma unroll
+    for (int i = 0; i < kPairs; ++i) {
+      const int d = i * 64 + 2 * lane;
+      if (d < HD) *reinterpret_cast<float2*>(part + 2 + d) = acc[k][i];
+    }
+    if (lane == 0) {
+      part[0] = m_run[k];
+      part[1] = l_run[k];
+    }
+  }
+
+  // the last CTA of the group merges the partials in range order; the
+  // barrier orders every thread's partial before thread 0's release, whose
+  // acquire side (the last CTA's thread 0, then its barrier) makes them
+  // visible there
+  attn_sync();
+  const int parts = static_cast<int>(gridDim.x);
+  if (tid == 0) s_last = ticket_acq_rel(a.counters + g) == static_cast<unsigned>(parts - 1);
+  attn_sync();
+  if (!s_last) return;
+  const long long stride = a.heads * (HD + 2);
+  for (int h = warp; h < group; h += warps) {
+    const long long head = static_cast<long long>(g) * group + h;
+    const float* base = a.scratch + head * (HD + 2);
+    float m = -INFINITY;
+    for (int sp = lane; sp < parts; sp += 32) m = fmaxf(m, __ldcg(base + sp * stride));
+    m = warp_max(m);
+    float l = 0.0f, out[HD / 32 > 0 ? HD / 32 : 1];
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) out[i] = 0.0f;
+    for (int s0 = 0; s0 < parts; s0 += 32) {
+      const int sp = s0 + lane;
+      const float sc_mine = sp < parts ? expf(__ldcg(base + sp * stride) - m) : 0.0f;
+      l += warp_sum(sp < parts ? __ldcg(base + sp * stride + 1) * sc_mine : 0.0f);
+      const int n = parts - s0 < 32 ? parts - s0 : 32;
+      for (int j = 0; j < n; ++j) {
+        const float sc = __shfl_sync(0xffffffffu, sc_mine, j);
+        const float* part = base + (s0 + j) * stride + 2;
+#pragma unroll
+        for (int i = 0; i < HD / 32; ++i) out[i] = fmaf(__ldcg(part + lane + 32 * i), sc, out[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) a.out[head * HD + lane + 32 * i] = __fdiv_rn(out[i], l);
+  }
+  if (tid == 0) a.counters[g] = 0u;
 }
 
 }  // namespace
@@ -286,23 +558,43 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   const long long splits = (a->context + kAttnSplit - 1) / kAttnSplit;
   CB_REQUIRE(splits < (1LL << 31) && a->kv_heads < 65536, "decode attention: grid too large");
   const long long group = a->heads / a->kv_heads;
-  const size_t smem = static_cast<size_t>(attn_smem_floats(group, a->head_size)) * sizeof(float);
+  CB_REQUIRE(group <= 32, "decode attention: at most 32 query heads per KV head (got %lld)", group);
+  const size_t smem = static_cast<size_t>(chunk_smem_floats(group, a->head_size)) * sizeof(float);
   CB_REQUIRE(smem <= 200 * 1024, "decode attention: too many query heads per KV head");
-  const dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(a->kv_heads), static_cast<unsigned>(batch));
+  // about one wave of resident CTAs (4 per SM): each CTA takes a range of
+  // consecutive chunks of its (sequence, KV head)
+  const long long groups = batch * a->kv_heads;
+  long long per_group = 4LL * sm_count() / groups;
+  if (per_group < 1) per_group = 1;
+  if (per_group > splits) per_group = splits;
+  const long long chunks = (splits + per_group - 1) / per_group;
+  const long long ctas = (splits + chunks - 1) / chunks;
+  const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(a->kv_heads), static_cast<unsigned>(batch));
+  const int per_cta = static_cast<int>(chunks);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
-#define CB_BATCHED_CASE(HD)                                                                               \
-  case HD:                                                                                                \
-    e = cudaFuncSetAttribute(decode_attention_batched_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             static_cast<int>(smem));                                                     \
-    if (e == cudaSuccess) decode_attention_batched_kernel<HD><<<grid, kAttnThreads, smem, s>>>(*a, qkv_stride); \
+#define CB_BATCHED_CASE(HD, HPW)                                                                          \
+  {                                                                                                       \
+    auto kernel = decode_attention_batched_kernel<HD, HPW>;                                               \
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
+    if (e == cudaSuccess) kernel<<<grid, kAttnThreads, smem, s>>>(*a, qkv_stride, per_cta);               \
+  }
+#define CB_BATCHED_HD(HD)            \
+  case HD:                           \
+    if (group <= 8)                  \
+      CB_BATCHED_CASE(HD, 1)         \
+    else if (group <= 16)            \
+      CB_BATCHED_CASE(HD, 2)         \
+    else                             \
+      CB_BATCHED_CASE(HD, 4)         \
     break;
   switch (a->head_size) {
-    CB_BATCHED_CASE(32)
-    CB_BATCHED_CASE(64)
-    CB_BATCHED_CASE(128)
-    CB_BATCHED_CASE(256)
+    CB_BATCHED_HD(32)
+    CB_BATCHED_HD(64)
+    CB_BATCHED_HD(128)
+    CB_BATCHED_HD(256)
   }
+#undef CB_BATCHED_HD
 #undef CB_BATCHED_CASE
   if (e != cudaSuccess) {
     set_error("cb_decode_attention_batched: %s", cudaGetErrorString(e));
