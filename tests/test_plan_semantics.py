@@ -234,6 +234,41 @@ def test_tensor_parallel_plans_match_the_one_rank_oracle(size):
             np.testing.assert_allclose(a, b[:, kv:kv + lay.kv_heads], rtol=0, atol=1e-4, err_msg=f"cache {i}")
 
 
+def test_tensor_parallel_prefill_plans_match_the_one_rank_oracle():
+    """Each rank's planned prefill (grouped q/k/v, RMSNorm prologues, SwiGLU epilogue on the
+    tensor-core GEMM, token-major attention, all_reduce steps after O and down) gives the
+    unsharded prefill's logits on every rank and the rank's KV heads of its caches."""
+    config, size, seq, ctx = TINY, 2, 16, 24
+    full_w = {k: v.astype(BF16) for k, v in synthetic_weights(config, dtype=np.float32).items()}
+    ids = np.random.default_rng(3).integers(0, config.vocab_size, (1, seq)).astype(np.int32)
+    selector = L.position_selector(seq - 1, seq, dtype=BF16)
+    with no_grad():
+        model = L.LlamaForCausalLM(config, {k: Tensor(v) for k, v in full_w.items()}, sequence_length=seq,
+                                   dtype=BF16, cache_length=ctx)
+        want = _oracle(list(model.prefill(Tensor(ids), Tensor(selector))))
+    interpreters, layouts = [], []
+    for rank in range(size):
+        lay = tp.shard_layout(config, size, rank)
+        with no_grad():
+            m = tp.TensorParallelPrefill(config, {k: Tensor(v) for k, v in tp.shard_weights(config, full_w, lay).items()},
+                                         lay, sequence_length=seq, dtype=BF16, cache_length=ctx)
+            source = Tensor(ids)
+            outs = list(m.prefill(source, Tensor(selector)))
+        plan = _plan(outs, [source], gemm_min_rows=16)
+        kinds = Counter(s.name for s in plan.steps)
+        assert kinds["all_reduce"] == 2 * config.num_hidden_layers and kinds["matmul_multi"] > 0
+        interpreters.append(PlanInterpreter(plan))
+        layouts.append((lay, lay.kv_rows.start // config.head_size))
+    run_ranks(interpreters)
+    for it, (lay, kv) in zip(interpreters, layouts):
+        got = it.outputs()
+        _close(got[0], want[0], BF16, "logits")
+        assert int(np.argmax(got[0])) == int(np.argmax(want[0]))
+        for i, (a, b) in enumerate(zip(got[1:], want[1:])):
+            b = np.asarray(b, np.float32)[:, kv:kv + lay.kv_heads]
+            np.testing.assert_allclose(a, b, rtol=0, atol=1e-4 * max(1.0, float(np.abs(b).max())), err_msg=f"cache {i}")
+
+
 # ------------------------------------------------------------------ the interpreter itself
 def test_interpreter_catches_a_wrong_operand():
     """A plan whose fused step reads the wrong buffer is caught (the check has teeth)."""
