@@ -1,12 +1,12 @@
-// Tensor-parallel collectives: a sum all-reduce over NCCL, issued on the
-// caller's stream so that it is recorded into the same CUDA graph as the
-// kernels of a decode step.
+// Tensor-parallel collectives: a sum all-reduce and an all-gather over NCCL,
+// issued on the caller's stream so that they are recorded into the same CUDA
+// graph as the kernels of a decode step.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2, or a path the caller
 // gives), so the library has no link-time NCCL dependency and shares the NCCL
 // that torch.distributed already loaded in the process.  Only NCCL's public
 // C API is used: ncclGetUniqueId, ncclCommInitRank, ncclAllReduce,
-// ncclCommDestroy, ncclGetErrorString, with the documented enum values
+// ncclAllGather, ncclCommDestroy, ncclGetErrorString, with the documented enum values
 // ncclSum = 0, ncclFloat32 = 7, ncclBfloat16 = 9 and 128-byte unique ids.
 #include <dlfcn.h>
 
@@ -26,6 +26,7 @@ struct UniqueId {
 using GetUniqueIdFn = int (*)(UniqueId*);
 using CommInitRankFn = int (*)(void**, int, UniqueId, int);
 using AllReduceFn = int (*)(const void*, void*, size_t, int, int, void*, cudaStream_t);
+using AllGatherFn = int (*)(const void*, void*, size_t, int, void*, cudaStream_t);
 using CommDestroyFn = int (*)(void*);
 using ErrorStringFn = const char* (*)(int);
 
@@ -34,6 +35,7 @@ struct Nccl {
   GetUniqueIdFn get_unique_id = nullptr;
   CommInitRankFn comm_init_rank = nullptr;
   AllReduceFn all_reduce = nullptr;
+  AllGatherFn all_gather = nullptr;
   CommDestroyFn comm_destroy = nullptr;
   ErrorStringFn error_string = nullptr;
 };
@@ -54,9 +56,11 @@ int load_nccl(const char* path) {
   n.get_unique_id = reinterpret_cast<GetUniqueIdFn>(dlsym(h, "ncclGetUniqueId"));
   n.comm_init_rank = reinterpret_cast<CommInitRankFn>(dlsym(h, "ncclCommInitRank"));
   n.all_reduce = reinterpret_cast<AllReduceFn>(dlsym(h, "ncclAllReduce"));
+  n.all_gather = reinterpret_cast<AllGatherFn>(dlsym(h, "ncclAllGather"));
   n.comm_destroy = reinterpret_cast<CommDestroyFn>(dlsym(h, "ncclCommDestroy"));
   n.error_string = reinterpret_cast<ErrorStringFn>(dlsym(h, "ncclGetErrorString"));
-  if (!n.get_unique_id || !n.comm_init_rank || !n.all_reduce || !n.comm_destroy || !n.error_string) {
+  if (!n.get_unique_id || !n.comm_init_rank || !n.all_reduce || !n.all_gather || !n.comm_destroy ||
+      !n.error_string) {
     set_error("cb_comm: the loaded NCCL lacks a required symbol");
     dlclose(h);
     return CB_ERR_INVALID;
@@ -115,6 +119,17 @@ int cb_all_reduce(void* comm, const void* src, void* dst, long long count, int d
   return nccl_status(g_nccl.all_reduce(src, dst, static_cast<size_t>(count), nccl_dtype, /*ncclSum*/ 0, comm,
                                        static_cast<cudaStream_t>(stream)),
                      "ncclAllReduce");
+}
+
+int cb_all_gather(void* comm, const void* src, void* dst, long long count, int dtype, cb_stream_t stream) {
+  CB_REQUIRE(comm != nullptr && g_nccl.handle != nullptr, "cb_all_gather: no communicator");
+  CB_REQUIRE(count >= 0 && (count == 0 || (src != nullptr && dst != nullptr)), "cb_all_gather: bad buffers");
+  CB_REQUIRE(dtype == CB_F32 || dtype == CB_BF16, "cb_all_gather: float32 or bfloat16 only");
+  if (count == 0) return CB_OK;
+  const int nccl_dtype = dtype == CB_F32 ? 7 : 9;  // ncclFloat32, ncclBfloat16
+  return nccl_status(g_nccl.all_gather(src, dst, static_cast<size_t>(count), nccl_dtype, comm,
+                                       static_cast<cudaStream_t>(stream)),
+                     "ncclAllGather");
 }
 
 }  // extern "C"

@@ -252,6 +252,7 @@ _SIGNATURES = {
     "cb_comm_init": ([c_void_p, c_int, c_int, c_int, POINTER(c_void_p)], c_int),
     "cb_comm_destroy": ([c_void_p], c_int),
     "cb_all_reduce": ([c_void_p, c_void_p, c_void_p, c_longlong, c_int, c_void_p], c_int),
+    "cb_all_gather": ([c_void_p, c_void_p, c_void_p, c_longlong, c_int, c_void_p], c_int),
     "cb_sdpa_query_scratch": ([POINTER(SdpaArgs)], c_longlong),
     "cb_sdpa_query": ([POINTER(SdpaArgs), c_void_p, c_void_p], c_int),
     "cb_gemv": ([POINTER(GemvArgs), c_void_p], c_int),

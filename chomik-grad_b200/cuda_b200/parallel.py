@@ -57,6 +57,10 @@ class Communicator:
         """dst = sum over ranks of src (device pointers), issued on ``stream``."""
         _lib.call("cb_all_reduce", self.handle, src, dst, count, dtype_code, stream)
 
+    def all_gather(self, src: int, dst: int, count: int, dtype_code: int, stream: int) -> None:
+        """dst = every rank's ``count``-element src, rank after rank (device pointers), on ``stream``."""
+        _lib.call("cb_all_gather", self.handle, src, dst, count, dtype_code, stream)
+
     def close(self) -> None:
         if self._handle:
             _lib.call("cb_comm_destroy", self._handle)

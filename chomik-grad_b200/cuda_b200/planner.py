@@ -295,7 +295,7 @@ def _collect_buffers(value, acc: Set[int]) -> None:
 class Planner:
     """Builds a :class:`Plan` from output nodes (see module docstring)."""
 
-    SUPPORTED_LOWERINGS = frozenset({"rms_norm", "rope", "sdpa", "all_reduce"})
+    SUPPORTED_LOWERINGS = frozenset({"rms_norm", "rope", "sdpa", "all_reduce", "all_gather"})
 
     def __init__(self, outputs: Sequence[object], dynamic_inputs: Sequence[object], *,
                  backend: str, leaf_dtype, max_positions: int = 8192,
@@ -374,6 +374,8 @@ class Planner:
             return low
         if kind_ == "all_reduce" and self._match_all_reduce(node, low):
             return low
+        if kind_ == "all_gather" and self._match_all_gather(node, low):
+            return low
         return None
 
     def _parents(self, node):
@@ -428,6 +430,29 @@ class Planner:
         if len(node.inputs) != 2 or node.inputs[0] is not x or self._const(node.inputs[1]) != 1.0:
             return False
         return self.rdt(x).name in ("float32", "bfloat16")
+
+    def _match_all_gather(self, node, low) -> bool:
+        """out = x.reshape(1, *x.shape) * ones(G, 1, ..., 1): the portable form of a
+        tensor-parallel gather of G shards (cuda_b200.tensor_parallel); exact on one rank."""
+        if not is_ew(node, "mul") or len(low[1]) != 1 or not isinstance(low[2], str) or len(node.inputs) != 2:
+            return False
+        x = low[1][0]
+        spread, ones = node.inputs
+        if kind(spread) != "reshape" or spread.inputs[0] is not x or tuple(spread.shape) != (1,) + tuple(x.shape):
+            return False
+        if ones.op is not None or ones in self.dynamic:
+            return False
+        if tuple(ones.shape) != (node.shape[0],) + (1,) * len(x.shape):
+            return False
+        try:
+            value = np.asarray(ones.numpy_value())
+        except Exception:
+            return False
+        if not np.all(value == 1) or self.rdt(x).name not in ("float32", "bfloat16") or self.rdt(node) != self.rdt(x):
+            return False
+        if not ones.cache_native:  # specialised on: checked again before every run
+            self.plan.guards.append((ones, value.copy()))
+        return True
 
     def _match_rms(self, node, low) -> bool:
         """out = x / sqrt(sum(x*x, -1, keepdims)/c + eps) * w (llama.py:279-287)."""
@@ -1388,6 +1413,14 @@ class Planner:
         out = self.tmp(node.shape, src.dtype)
         self.plan.lowered["all_reduce"] = self.plan.lowered.get("all_reduce", 0) + 1
         self.add_step("all_reduce", out, f"all_reduce({self._name(src)}, group={low[2]!r})", src=src,
+                      group=low[2])
+        self.set_value(node, out)
+
+    def _emit_all_gather(self, node, low) -> None:
+        src = self.contiguous(self.value(low[1][0]))
+        out = self.tmp(node.shape, src.dtype)
+        self.plan.lowered["all_gather"] = self.plan.lowered.get("all_gather", 0) + 1
+        self.add_step("all_gather", out, f"all_gather({self._name(src)}, group={low[2]!r})", src=src,
                       group=low[2])
         self.set_value(node, out)
 

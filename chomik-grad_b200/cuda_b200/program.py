@@ -585,6 +585,15 @@ class CudaB200Program(CompiledProgram):
         parallel.get_group(step.args["group"]).all_reduce(self.ptr(src), self.ptr(step.out), src.size,
                                                           _lib.dtype_code(src.dtype), stream)
 
+    def _step_all_gather(self, step: Step, stream: int) -> None:
+        from . import parallel
+
+        src: View = step.args["src"]
+        comm = parallel.get_group(step.args["group"])
+        if step.out.size != src.size * comm.world_size:
+            raise ValueError(f"all_gather of {step.out.shape[0]} shards over a group of {comm.world_size} ranks")
+        comm.all_gather(self.ptr(src), self.ptr(step.out), src.size, _lib.dtype_code(src.dtype), stream)
+
     def _matmul_rows_args(self, step: Step, counters: int) -> _lib.GemmRowsArgs:
         """cb_gemm_rows arguments of a planner-fused row GEMM (prologue / residual epilogue)."""
         g = step.args

@@ -10,7 +10,8 @@ The reference (chomikgrad/llama.py) is single-device.  Here each of
   (replicated on ``size / num_key_value_heads`` ranks);
 * ``intermediate_size / size`` rows of gate_proj and up_proj and the matching
   columns of down_proj;
-* everything else (embedding, norms, lm_head) whole.
+* everything else (embedding, norms) whole, and the lm_head whole or, with
+  ``vocab_shard``, ``vocab_size / size`` of its rows.
 
 The rank's graph is the reference's graph over those shards, with one
 change: the O and down projections produce partial sums, which
@@ -19,7 +20,12 @@ all-reduce is an identity node (``x * 1``) carrying an ``all_reduce``
 lowering hint, the same mechanism as the reference's preferred lowerings
 (llama.py:13-25): on one rank the portable graph is exact, and the
 ``cuda-b200`` planner lowers the hint to an NCCL all-reduce step of the
-compiled program (``cuda_b200.parallel``).
+compiled program (``cuda_b200.parallel``).  A vocabulary-sharded lm_head
+produces this rank's columns of the logits; ``all_gather`` (the portable
+form ``x.reshape(1, ...) * ones(G, 1, ...)``, exact on one rank, with an
+``all_gather`` hint lowered to NCCL's all-gather) collects every rank's
+columns, so each rank still returns the whole logits and picks the same
+greedy token, while it reads 1/size of the lm_head.
 
 Per rank and step the decode reads 1/size of the sharded weights (plus the
 replicated ones) and exchanges 2 x layers x batch x hidden float32 values.
@@ -50,6 +56,16 @@ class ShardLayout:
     q_start: int        # first q_proj row (= first o_proj column)
     kv_start: int       # first k_proj / v_proj row
     i_start: int        # first gate/up row (= first down_proj column)
+    vocab: int = 0      # lm_head rows on this rank (vocab_shard); 0: the whole lm_head
+    vocab_start: int = 0
+
+    @property
+    def vocab_shard(self) -> bool:
+        return self.vocab > 0
+
+    @property
+    def vocab_rows(self) -> slice:
+        return slice(self.vocab_start, self.vocab_start + self.vocab)
 
     @property
     def group(self) -> int:
@@ -68,9 +84,12 @@ class ShardLayout:
         return slice(self.i_start, self.i_start + self.intermediate)
 
 
-def shard_layout(config: LlamaConfig, size: int, rank: int) -> ShardLayout:
+def shard_layout(config: LlamaConfig, size: int, rank: int, *, vocab_shard: bool = False) -> ShardLayout:
     if size < 1 or not 0 <= rank < size:
         raise ValueError(f"rank {rank} of {size}")
+    if vocab_shard and config.vocab_size % size:
+        raise ValueError(f"{size} ranks must divide the vocabulary of {config.vocab_size} to shard the lm_head")
+    vocab = config.vocab_size // size if vocab_shard else 0
     nh, nkv, hd = config.num_attention_heads, config.num_key_value_heads, config.head_size
     if nh % size or config.intermediate_size % size:
         raise ValueError(f"{size} ranks must divide the {nh} heads and the intermediate size "
@@ -89,7 +108,7 @@ def shard_layout(config: LlamaConfig, size: int, rank: int) -> ShardLayout:
     inter = config.intermediate_size // size
     return ShardLayout(size=size, rank=rank, heads=heads, kv_heads=kv_heads, head_size=hd,
                        intermediate=inter, q_start=rank * heads * hd, kv_start=kv_first * hd,
-                       i_start=rank * inter)
+                       i_start=rank * inter, vocab=vocab, vocab_start=rank * vocab)
 
 
 def _contiguous(value):
@@ -112,6 +131,8 @@ def shard_weights(config: LlamaConfig, weights: Mapping[str, Any], layout: Shard
             out[name] = _contiguous(w[layout.i_rows])
         elif name.endswith("down_proj.weight"):
             out[name] = _contiguous(w[:, layout.i_rows])
+        elif name == "lm_head.weight" and layout.vocab_shard:
+            out[name] = _contiguous(w[layout.vocab_rows])
         else:
             out[name] = w
     return out
@@ -120,6 +141,12 @@ def shard_weights(config: LlamaConfig, weights: Mapping[str, Any], layout: Shard
 def all_reduce(partial: Tensor, group: str) -> Tensor:
     """Sum of ``partial`` over the ranks of ``group``; on one rank the graph is ``partial`` itself."""
     return _prefer(partial * 1, "all_reduce", (partial,), group)
+
+
+def all_gather(part: Tensor, group: str, size: int, dtype) -> Tensor:
+    """(size, *part.shape): every rank's ``part`` in rank order; on one rank the graph is exact."""
+    spread = part.reshape(1, *part.shape) * Tensor.ones((size,) + (1,) * len(part.shape), dtype=dtype)
+    return _prefer(spread, "all_gather", (part,), group)
 
 
 class _ShardMixin:
@@ -144,6 +171,15 @@ class _ShardMixin:
 
     def _mlp(self, inputs: Tensor, layer: int) -> Tensor:
         return self._reduce(LlamaForCausalLM._mlp(self, inputs, layer))
+
+    def _linear(self, inputs: Tensor, weight: Tensor) -> Tensor:
+        """``x @ W.T``; through a vocabulary-sharded lm_head, the whole logits gathered from the group."""
+        out = inputs @ weight.T
+        if self.layout.vocab_shard and weight is self.weights.get("lm_head.weight"):
+            rows, cols = out.shape
+            gathered = all_gather(out, self.group_name, self.layout.size, self.dtype)  # (G, rows, V / G)
+            return gathered.permute(1, 0, 2).reshape(rows, self.layout.size * cols)
+        return out
 
 
 def _init_model(model, config: LlamaConfig, weights: Mapping[str, Tensor], *, sequence_length: int,
@@ -247,8 +283,9 @@ class TensorParallelRuntime(BatchedRuntime):
     """Prefill and batched greedy decode of one rank of a tensor-parallel group.
 
     ``weights`` are this rank's shards (``shard_weights``).  Every rank runs
-    the same calls with the same token ids; the logits (replicated lm_head)
-    and so the greedy tokens are the same on every rank.
+    the same calls with the same token ids; the logits (replicated lm_head,
+    or the gathered columns of a vocabulary-sharded one) and so the greedy
+    tokens are the same on every rank.
     """
 
     def __init__(self, config: LlamaConfig, weights, layout: ShardLayout, *, batch: int,

@@ -540,12 +540,16 @@ CB_API int cb_gemm_rows(const cb_gemm_rows_args* args, cb_stream_t stream);
  * path, or NULL for the one the process already has).  cb_comm_unique_id
  * writes NCCL's 128-byte id on one rank; every rank passes it to
  * cb_comm_init.  cb_all_reduce(src -> dst, count elements, CB_F32 or CB_BF16)
- * is issued on `stream`, so a CUDA graph captured on that stream holds it. */
+ * is issued on `stream`, so a CUDA graph captured on that stream holds it.
+ * cb_all_gather writes the ranks' `count`-element src buffers into dst one
+ * after the other in rank order (dst holds nranks * count elements): the
+ * vocabulary-sharded lm_head's logits, gathered before the argmax. */
 CB_API int cb_comm_load(const char* path);
 CB_API int cb_comm_unique_id(void* out, int bytes);
 CB_API int cb_comm_init(const void* id, int bytes, int nranks, int rank, void** comm);
 CB_API int cb_comm_destroy(void* comm);
 CB_API int cb_all_reduce(void* comm, const void* src, void* dst, long long count, int dtype, cb_stream_t stream);
+CB_API int cb_all_gather(void* comm, const void* src, void* dst, long long count, int dtype, cb_stream_t stream);
 
 /* ---- whole decode step in one launch --------------------------------------
  * The fused decode step of LlamaDecoderStep (chomikgrad/llama.py:469-543)

@@ -17,8 +17,9 @@ it launches documents in ``include/chomik_b200.h``:
 * ``decode_attention`` and ``decode_attention_batched`` rope q and k at the
   bound position from the plan's cos/sin tables, blend k and v into the
   caches where the write mask is non-zero, then attend over the context;
-* ``all_reduce`` hands its operand to the caller (:func:`run_ranks` sums the
-  ranks' operands in rank order).
+* ``all_reduce`` and ``all_gather`` hand their operand to the caller
+  (:func:`run_ranks` sums the ranks' operands, or stacks them, in rank
+  order).
 
 The CPU suite runs planned programs through this and compares them with the
 parity oracle, so the planner's rewrites (decode fusion, GEMM prologues and
@@ -171,16 +172,16 @@ class PlanInterpreter:
             self._flat(init["out"])[: d.size] = d
 
     def steps(self) -> Iterator[Step]:
-        """Run the plan; yields each ``all_reduce`` step for the caller to complete."""
+        """Run the plan; yields each collective step (all_reduce, all_gather) for the caller to complete."""
         self.init()
         for step in self.plan.steps:
-            if step.name == "all_reduce":
+            if step.name in COLLECTIVES:
                 yield step
                 continue
             getattr(self, f"_step_{step.name}")(step)
 
     def run(self) -> None:
-        """Run a plan whose all-reduces span one rank (the sum of one partial)."""
+        """Run a plan whose collectives span one rank (the sum or the stack of one operand)."""
         for step in self.steps():
             self.write(step.out, self.read(step.args["src"]))
 
@@ -445,18 +446,25 @@ def _blend(cache: np.ndarray, row: np.ndarray, wm: np.ndarray, one_minus) -> np.
     return cache
 
 
+COLLECTIVES = ("all_reduce", "all_gather")
+
+
 def run_ranks(interpreters: Sequence[PlanInterpreter]) -> None:
-    """Run one plan per rank in lock step; each all_reduce sums the ranks' operands in rank order."""
+    """Run one plan per rank in lock step: each all_reduce sums the ranks' operands in rank order,
+    each all_gather stacks them in rank order."""
     runs = [it.steps() for it in interpreters]
     while True:
         pending = [next(r, None) for r in runs]
         if all(p is None for p in pending):
             return
-        if any(p is None for p in pending):
-            raise RuntimeError("ranks disagree on the number of all_reduce steps")
+        if any(p is None for p in pending) or len({p.name for p in pending}) != 1:
+            raise RuntimeError("ranks disagree on their collective steps")
         parts = [it.read_f32(p.args["src"]) for it, p in zip(interpreters, pending)]
-        total = parts[0]
-        for part in parts[1:]:
-            total = total + part
+        if pending[0].name == "all_gather":
+            result = np.stack(parts)
+        else:
+            result = parts[0]
+            for part in parts[1:]:
+                result = result + part
         for it, p in zip(interpreters, pending):
-            it.write(p.out, total)
+            it.write(p.out, result)

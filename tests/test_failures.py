@@ -50,6 +50,8 @@ def test_missing_nccl_is_reported():
 def test_collective_arguments_are_checked_before_any_launch():
     with pytest.raises(_lib.KernelError, match="no communicator"):
         _lib.call("cb_all_reduce", None, 0, 0, 16, _lib.F32, None)
+    with pytest.raises(_lib.KernelError, match="no communicator"):
+        _lib.call("cb_all_gather", None, 0, 0, 16, _lib.F32, None)
     uid = (ctypes.c_char * 128)()
     handle = ctypes.c_void_p()
     with pytest.raises(_lib.KernelError, match="rank 3 of 2"):

@@ -6,7 +6,9 @@ projections is an NCCL step of each compiled program (cuda_b200.parallel),
 replayed inside the decode step's CUDA graph.  Every rank must produce the
 one-GPU program's greedy tokens, and logits equal up to the float32
 reassociation of the sharded sums.  Skipped on a machine with fewer than two
-GPUs.
+GPUs.  On one GPU, a one-rank group with a vocabulary-sharded lm_head runs
+the same checks: its logits pass through an NCCL all-gather step (inside the
+captured graph) before the argmax.
 """
 
 from __future__ import annotations
@@ -16,7 +18,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def _rank(rank: int, size: int, port: int, queue) -> None:
+def _rank(rank: int, size: int, port: int, queue, vocab_shard: bool = False) -> None:
     import os
     import sys
 
@@ -38,7 +40,7 @@ def _rank(rank: int, size: int, port: int, queue) -> None:
         wl = WORKLOADS["tiny-bf16"]
         cfg, batch, prompt_len, steps = wl.config, 4, 16, 10
         weights = synthetic_weights(cfg, dtype=wl.np_dtype)
-        layout = tp.shard_layout(cfg, size, rank)
+        layout = tp.shard_layout(cfg, size, rank, vocab_shard=vocab_shard)
         rt = tp.TensorParallelRuntime(cfg, tp.shard_weights(cfg, weights, layout), layout, batch=batch)
         prompts = [list(p) for p in synthetic_prompt(cfg, prompt_len, batch=batch)]
         context = prompt_len + steps + 2
@@ -75,10 +77,7 @@ def _rank(rank: int, size: int, port: int, queue) -> None:
         dist.destroy_process_group()
 
 
-def test_tensor_parallel_decode_on_two_gpus_matches_one_gpu():
-    torch = pytest.importorskip("torch")
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _run_group(size: int, vocab_shard: bool) -> None:
     import multiprocessing as mp
     import socket
 
@@ -89,7 +88,7 @@ def test_tensor_parallel_decode_on_two_gpus_matches_one_gpu():
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, size, port, queue, vocab_shard)) for r in range(size)]
     for p in procs:
         p.start()
     got = {}
@@ -108,13 +107,26 @@ def test_tensor_parallel_decode_on_two_gpus_matches_one_gpu():
         p.join(timeout=120)
         if p.is_alive():
             p.kill()
-    for rank in range(2):
+    for rank in range(size):
         assert isinstance(got[rank], dict), got[rank]
     ref = got[0]["one_gpu"]
     scale = float(np.abs(got[0]["one_gpu_logits"]).max())
-    for rank in range(2):
+    for rank in range(size):
         r = got[rank]
         assert r["host"] == ref, (rank, r["host"], ref)
         np.testing.assert_allclose(r["logits"], got[0]["one_gpu_logits"], rtol=0, atol=1e-3 * scale)
         # graph replays: entry i of sequence b is the token decoded at step i (after the prefill's)
         assert [list(col) for col in zip(*r["replayed"])][: len(ref) - 1] == ref[1:], rank
+
+
+@pytest.mark.parametrize("vocab_shard", [False, True])
+def test_tensor_parallel_decode_on_two_gpus_matches_one_gpu(vocab_shard):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _run_group(2, vocab_shard)
+
+
+def test_one_rank_group_with_a_sharded_lm_head_matches_one_gpu():
+    pytest.importorskip("torch")
+    _run_group(1, True)

@@ -193,10 +193,11 @@ def test_batched_decode_plan_matches_the_oracle(name):
 
 
 # ------------------------------------------------------------------ tensor parallel
-@pytest.mark.parametrize("size", [2, 4])
-def test_tensor_parallel_plans_match_the_one_rank_oracle(size):
+@pytest.mark.parametrize("size,vocab_shard", [(2, False), (4, False), (2, True), (4, True)])
+def test_tensor_parallel_plans_match_the_one_rank_oracle(size, vocab_shard):
     """Each rank's planned batched step (row GEMMs, fused attention, all_reduce steps after O and
-    down), run in lock step with the all-reduces summing the ranks' partials, gives the
+    down, and with a vocabulary-sharded lm_head one all_gather of the logits' columns), run in
+    lock step with the collectives summing or stacking the ranks' operands, gives the
     unsharded graph's logits on every rank and the rank's KV heads of its caches."""
     config, batch, ctx, position = TINY, 3, 24, 9
     full_w = {k: v.astype(BF16) for k, v in synthetic_weights(config, dtype=np.float32).items()}
@@ -209,7 +210,7 @@ def test_tensor_parallel_plans_match_the_one_rank_oracle(size):
     am, wm = L.decode_masks(position, ctx, BF16)
     interpreters, layouts = [], []
     for rank in range(size):
-        lay = tp.shard_layout(config, size, rank)
+        lay = tp.shard_layout(config, size, rank, vocab_shard=vocab_shard)
         kv = lay.kv_rows.start // config.head_size
         with no_grad():
             step = tp.TensorParallelDecoderStep(
@@ -223,6 +224,7 @@ def test_tensor_parallel_plans_match_the_one_rank_oracle(size):
         kinds = Counter(s.name for s in plan.steps)
         assert kinds["all_reduce"] == 2 * config.num_hidden_layers
         assert kinds["decode_attention_batched"] == config.num_hidden_layers
+        assert kinds["all_gather"] == int(vocab_shard)
         interpreters.append(PlanInterpreter(plan))
         layouts.append((lay, kv))
     run_ranks(interpreters)

@@ -69,6 +69,7 @@ def _decode_inputs(config, batch, context, position, seed):
 
 
 def _tp_decode_graph(config, weights, layout, batch, context, inputs):
+    """One rank's decode step over its shards and its KV heads of the caches."""
     ids, rotation, attention, write, position, caches = inputs
     kv = layout.kv_rows.start // config.head_size
     local = [c[:, kv:kv + layout.kv_heads] for c in caches]
@@ -80,8 +81,9 @@ def _tp_decode_graph(config, weights, layout, batch, context, inputs):
         return step(t[0], t[1], t[2], t[3], list(zip(ct[::2], ct[1::2])), position=t[4])
 
 
-def _run(outputs, reduce_fn: Callable[[np.ndarray], np.ndarray]) -> List[np.ndarray]:
-    """The oracle's evaluation, with all_reduce nodes computed by ``reduce_fn``."""
+def _run(outputs, reduce_fn: Callable[[np.ndarray], np.ndarray],
+         gather_fn: Callable[[np.ndarray], np.ndarray] = None) -> List[np.ndarray]:
+    """The oracle's evaluation, with all_reduce / all_gather nodes computed by ``reduce_fn`` / ``gather_fn``."""
     nodes = [o._node for o in outputs]
     values: Dict[object, np.ndarray] = {}
     for node in topological_sort(nodes):
@@ -89,6 +91,8 @@ def _run(outputs, reduce_fn: Callable[[np.ndarray], np.ndarray]) -> List[np.ndar
             values[node] = node.numpy_value()
         elif node.lowering is not None and node.lowering[0] == "all_reduce":
             values[node] = reduce_fn(values[node.lowering[1][0]])
+        elif node.lowering is not None and node.lowering[0] == "all_gather" and gather_fn is not None:
+            values[node] = gather_fn(values[node.lowering[1][0]])
         else:
             values[node] = evaluate_node(node, [values[p] for p in node.inputs])
     return [np.asarray(values[n]) for n in nodes]
@@ -114,7 +118,14 @@ def _threaded_ranks(size: int, build: Callable[[int], list]) -> List[List[np.nda
                 barrier.wait(timeout=60)
                 return total.astype(x.dtype)
 
-            results[rank] = _run(outputs, reduce_fn)
+            def gather_fn(x):
+                slots[rank] = x
+                barrier.wait(timeout=60)
+                stacked = np.stack([np.asarray(v) for v in slots])
+                barrier.wait(timeout=60)
+                return stacked.astype(x.dtype)
+
+            results[rank] = _run(outputs, reduce_fn, gather_fn)
         except Exception as exc:  # noqa: BLE001
             errors.append(exc)
             barrier.abort()
@@ -150,6 +161,33 @@ def test_tensor_parallel_decode_equals_one_rank(size):
         kv = lay.kv_rows.start // config.head_size
         for g, f in zip(got[1:], full[1:]):  # the rank's KV heads of the updated caches
             np.testing.assert_allclose(g, f[:, kv:kv + lay.kv_heads], rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("size", [2, 4])
+def test_vocabulary_sharded_lm_head_gathers_the_whole_logits(size):
+    """With the lm_head's rows split over the ranks, every rank still returns the unsharded logits."""
+    config, batch, context, position = TINY, 3, 24, 9
+    weights = synthetic_weights(config, dtype=np.float32)
+    inputs = _decode_inputs(config, batch, context, position, seed=11)
+    ids, rotation, attention, write, pos, caches = inputs
+    with no_grad():
+        step = BatchedDecoderStep(config, _tensors(weights), batch=batch, cache_length=context, dtype=np.float32)
+        t = [Tensor(v) for v in (ids, rotation, attention, write, pos)]
+        ct = [Tensor(c) for c in caches]
+        full = _run(step(t[0], t[1], t[2], t[3], list(zip(ct[::2], ct[1::2])), position=t[4]), lambda x: x)
+    layouts = [tp.shard_layout(config, size, r, vocab_shard=True) for r in range(size)]
+    assert sum(lay.vocab for lay in layouts) == config.vocab_size
+    assert tp.shard_weights(config, weights, layouts[1])["lm_head.weight"].shape[0] == config.vocab_size // size
+    ranks = _threaded_ranks(size, lambda r: _tp_decode_graph(config, weights, layouts[r], batch, context, inputs))
+    scale = float(np.abs(full[0]).max())
+    for got in ranks:
+        assert got[0].shape == full[0].shape
+        np.testing.assert_allclose(got[0], full[0], rtol=0, atol=1e-4 * scale)
+        assert (got[0].argmax(-1) == full[0].argmax(-1)).all()
+    import dataclasses
+
+    with pytest.raises(ValueError, match="vocabulary"):
+        tp.shard_layout(dataclasses.replace(config, vocab_size=4095), 2, 0, vocab_shard=True)
 
 
 def test_tensor_parallel_prefill_equals_one_rank():
