@@ -428,7 +428,8 @@ def batched_measurement(cfg, weights, rank: int, world: int, steps: int, warmup:
     }
 
 
-def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: int, prompt_len: int) -> dict:
+def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: int, prompt_len: int,
+                       vocab_shard: bool = False) -> dict:
     """Llama-3-8B shape, batch 16, tensor-parallel over all ranks (TP = world size).
 
     Weights are random-init bf16 drawn on each GPU (cuda_b200.models.device_weights)
@@ -446,7 +447,7 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
     cfg = wl.config
     if world > 1:
         parallel.init_group("tp")
-    layout = tp.shard_layout(cfg, world, rank)
+    layout = tp.shard_layout(cfg, world, rank, vocab_shard=vocab_shard)
     weights = device_weights(cfg, device=torch.device("cuda", local), layout=layout)
     rt = tp.TensorParallelRuntime(cfg, weights, layout, batch=wl.batch, dtype=bfloat16())
     context = prompt_len + wl.decode_steps
@@ -487,6 +488,7 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
     pflops = prefill_flops(cfg, prompt_len) * wl.batch / (prefill_ms / 1000.0) / 1e12
     return {
         "workload": wl.name, "tensor_parallel": world, "sequences": wl.batch, "prompt_tokens": prompt_len,
+        "lm_head": "vocab-sharded, logits all-gathered" if vocab_shard else "replicated",
         "context": context, "value": steps * wl.batch / (slowest / 1000.0), "unit": "tokens/s",
         "ms_per_step": step_ms,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
@@ -515,6 +517,8 @@ def main() -> None:
     parser.add_argument("--llama3-steps", type=int, default=30,
                         help="tensor-parallel Llama-3-8B bs16 decode steps (TP = GPUs); 0 skips it")
     parser.add_argument("--llama3-prompt", type=int, default=1024, help="Llama-3-8B prompt tokens")
+    parser.add_argument("--vocab-shard", action="store_true",
+                        help="Llama-3-8B: shard the lm_head's rows over the ranks (logits gathered by NCCL)")
     args = parser.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -639,7 +643,7 @@ def main() -> None:
         line["prefill"] = prefill_measurement(rt, cfg, rank, world, args.prefill_steps, 1)
     if args.llama3_steps > 0 and args.workload == "tinyllama-bf16-bs1":
         line["llama3_8b_tp"] = llama3_measurement(rank, world, local, args.llama3_steps, args.warmup,
-                                                  args.llama3_prompt)
+                                                  args.llama3_prompt, args.vocab_shard)
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, weights).items()
                                 if k in ("value", "unit", "cores", "kind", "sample")}
