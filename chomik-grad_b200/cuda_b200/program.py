@@ -949,6 +949,8 @@ class CudaB200Program(CompiledProgram):
         if self._capture_stream is not None:
             lib.cb_stream_destroy(self._capture_stream)
             self._capture_stream = None
+        if getattr(self, "_last_bound", None):  # the arrays the last run bound by pointer
+            self._last_bound = [None] * len(self._last_bound)
 
     def __del__(self) -> None:
         try:
