@@ -236,7 +236,8 @@ def test_tensor_parallel_plans_match_the_one_rank_oracle(size, vocab_shard):
             np.testing.assert_allclose(a, b[:, kv:kv + lay.kv_heads], rtol=0, atol=1e-4, err_msg=f"cache {i}")
 
 
-def test_tensor_parallel_prefill_plans_match_the_one_rank_oracle():
+@pytest.mark.parametrize("vocab_shard", [False, True])
+def test_tensor_parallel_prefill_plans_match_the_one_rank_oracle(vocab_shard):
     """Each rank's planned prefill (grouped q/k/v, RMSNorm prologues, SwiGLU epilogue on the
     tensor-core GEMM, token-major attention, all_reduce steps after O and down) gives the
     unsharded prefill's logits on every rank and the rank's KV heads of its caches."""
@@ -250,7 +251,7 @@ def test_tensor_parallel_prefill_plans_match_the_one_rank_oracle():
         want = _oracle(list(model.prefill(Tensor(ids), Tensor(selector))))
     interpreters, layouts = [], []
     for rank in range(size):
-        lay = tp.shard_layout(config, size, rank)
+        lay = tp.shard_layout(config, size, rank, vocab_shard=vocab_shard)
         with no_grad():
             m = tp.TensorParallelPrefill(config, {k: Tensor(v) for k, v in tp.shard_weights(config, full_w, lay).items()},
                                          lay, sequence_length=seq, dtype=BF16, cache_length=ctx)
@@ -259,6 +260,7 @@ def test_tensor_parallel_prefill_plans_match_the_one_rank_oracle():
         plan = _plan(outs, [source], gemm_min_rows=16)
         kinds = Counter(s.name for s in plan.steps)
         assert kinds["all_reduce"] == 2 * config.num_hidden_layers and kinds["matmul_multi"] > 0
+        assert kinds["all_gather"] == int(vocab_shard)
         interpreters.append(PlanInterpreter(plan))
         layouts.append((lay, lay.kv_rows.start // config.head_size))
     run_ranks(interpreters)
