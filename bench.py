@@ -48,7 +48,7 @@ import threading
 import time
 
 ROOT = Path(__file__).resolve().parent
-for _p in (ROOT / "chomik-grad_b200", ROOT):
+for _p in (ROOT / "baseline" / "_ref", ROOT / "chomik-grad_b200", ROOT):
     if str(_p) not in sys.path:
         sys.path.insert(0, str(_p))
 
@@ -168,7 +168,7 @@ def barrier(world: int) -> None:
 
 
 def weight_bytes(config, itemsize: int) -> int:
-    from cuda_b200.frontend.llama import required_weight_shapes
+    from chomikgrad.llama import required_weight_shapes
 
     total = sum(int(np.prod(s)) for n, s in required_weight_shapes(config).items()
                 if n != "model.embed_tokens.weight")
@@ -441,7 +441,7 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
 
     from cuda_b200 import parallel, tensor_parallel as tp
     from cuda_b200.models import WORKLOADS, bfloat16, device_weights, synthetic_prompt
-    from cuda_b200.frontend.llama import required_weight_shapes
+    from chomikgrad.llama import required_weight_shapes
 
     wl = WORKLOADS["llama3-8b-bf16-bs16"]
     cfg = wl.config

@@ -1,33 +1,21 @@
 """``cuda-b200``: a B200-native compiler/device plugin for chomik-grad.
 
-Importing the package registers the ``cuda-b200`` compiler (a lazy factory:
-no GPU is touched until it is first used) in the package's mirror of
-chomik-grad's plugin registry, whose front-end (``Tensor``, ``compile_graph``,
-Llama builders) lives in :mod:`cuda_b200.frontend`.
+The plugin runs under the unmodified reference package: importing
+``cuda_b200`` registers the ``cuda-b200`` compiler in ``chomikgrad``'s own
+registry (``register_compiler``, chomikgrad/lazy.py:646-656) as a lazy
+factory, so no GPU is touched until ``get_compiler("cuda-b200")`` first
+instantiates it.  After that, the reference's graphs select it by name::
 
-To use the plugin from the original ``chomikgrad`` package instead::
+    import chomikgrad, cuda_b200  # noqa: F401
+    program = chomikgrad.compile_graph(*outputs, compiler="cuda-b200",
+                                       dynamic_inputs=...)
 
-    import chomikgrad, cuda_b200
-    cuda_b200.install(chomikgrad)        # register_compiler("cuda-b200", ...)
-    program = chomikgrad.compile_graph(*outputs, compiler="cuda-b200", ...)
+``chomikgrad`` must be importable; the plugin has no front-end of its own.
 """
 
 from __future__ import annotations
 
-from .frontend.lazy import (
-    CompiledProgram,
-    Compiler,
-    DeviceAdapter,
-    GraphPlan,
-    LazyNode,
-    Op,
-    get_compiler,
-    register_compiler,
-    set_default_compiler,
-)
-from .frontend.tensor import Tensor, compile_graph, no_grad, realize
-from .frontend import llama
-from .generation import GreedyVerification, verify_greedy_candidates
+import chomikgrad
 
 BACKEND = "cuda-b200"
 
@@ -38,31 +26,12 @@ def _factory():
     return CudaB200Compiler()
 
 
-register_compiler(BACKEND, _factory, replace=True)
-
-
 def install(chomikgrad_module=None, *, replace: bool = True) -> None:
-    """Register ``cuda-b200`` with the original chomikgrad package.
-
-    The plugin classes are registered as virtual subclasses of chomikgrad's
-    ``Compiler`` / ``DeviceAdapter`` / ``CompiledProgram`` ABCs so that
-    ``get_compiler``'s ``isinstance`` check (lazy.py:674-676) accepts them.
-    """
-    if chomikgrad_module is None:
-        import chomikgrad as chomikgrad_module  # type: ignore[no-redef]
-    from .compiler import CudaB200Compiler
-    from .device import CudaB200Device
-    from .program import CudaB200Program
-
-    lazy = chomikgrad_module.lazy
-    lazy.Compiler.register(CudaB200Compiler)
-    lazy.DeviceAdapter.register(CudaB200Device)
-    lazy.CompiledProgram.register(CudaB200Program)
-    chomikgrad_module.register_compiler(BACKEND, CudaB200Compiler, replace=replace)
+    """(Re-)register ``cuda-b200`` in a chomikgrad module's registry (the imported one by default)."""
+    module = chomikgrad if chomikgrad_module is None else chomikgrad_module
+    module.register_compiler(BACKEND, _factory, replace=replace)
 
 
-__all__ = [
-    "BACKEND", "CompiledProgram", "Compiler", "DeviceAdapter", "GraphPlan", "GreedyVerification",
-    "LazyNode", "Op", "Tensor", "compile_graph", "get_compiler", "install", "llama", "no_grad",
-    "realize", "register_compiler", "set_default_compiler", "verify_greedy_candidates",
-]
+install()
+
+__all__ = ["BACKEND", "install"]

@@ -23,14 +23,22 @@ from typing import Any, List, Optional, Sequence, Tuple
 
 import numpy as np
 
+from chomikgrad.llama import LlamaConfig, LlamaDecoderStep, _rope_rotations
+from chomikgrad.tensor import Tensor, compile_graph, no_grad
+
 from .device import DeviceArray
-from .frontend.llama import LlamaConfig, LlamaDecoderStep, decode_masks, rope_rotations
-from .frontend.tensor import Tensor, compile_graph, no_grad
+from .graphs import GraphHelpers, decode_masks
 from .runtime import LlamaRuntime
 
 
-class BatchedDecoderStep(LlamaDecoderStep):
-    """One decode step of B independent sequences sharing the position."""
+class BatchedDecoderStep(GraphHelpers, LlamaDecoderStep):
+    """One decode step of B independent sequences sharing the position.
+
+    A subclass of the reference's ``LlamaDecoderStep``: the same validation
+    of rotation, masks and caches, the same per-layer chain of the reference's
+    own building blocks (``_rms_norm``, ``_linear``, ``_apply_rotation``,
+    ``_repeat_kv``, ``_mlp``), with B in the leading dimension.
+    """
 
     def __init__(self, config: LlamaConfig, weights, *, batch: int, cache_length: int,
                  dtype: np.dtype) -> None:
@@ -39,9 +47,8 @@ class BatchedDecoderStep(LlamaDecoderStep):
             raise ValueError("batch must be positive")
         self.batch = batch
 
-    def __call__(self, token_matrix: Tensor, rotation: Tensor, attention_mask: Tensor,
-                 write_mask: Tensor, caches: Sequence[Tuple[Tensor, Tensor]], *,
-                 position: Optional[Tensor] = None) -> Tuple[Tensor, ...]:
+    def _check_step(self, token_matrix: Tensor, rotation: Tensor, attention_mask: Tensor,
+                    write_mask: Tensor, caches, position: Optional[Tensor]) -> None:
         c, ctx, b = self.config, self.cache_length, self.batch
         if token_matrix.shape != (b, 1):
             raise ValueError(f"batched decode takes ({b}, 1) token ids")
@@ -54,34 +61,34 @@ class BatchedDecoderStep(LlamaDecoderStep):
         if position is not None and position.shape != ():
             raise ValueError("decode position must be a scalar")
 
+    def __call__(self, token_matrix: Tensor, rotation: Tensor, attention_mask: Tensor,
+                 write_mask: Tensor, caches: Sequence[Tuple[Tensor, Tensor]], *,
+                 position: Optional[Tensor] = None) -> Tuple[Tensor, ...]:
+        self._check_step(token_matrix, rotation, attention_mask, write_mask, caches, position)
+        c, ctx, b = self.config, self.cache_length, self.batch
+        hd, nh, nkv = c.head_size, c.num_attention_heads, c.num_key_value_heads
         hidden = self._embed(token_matrix)  # (B, 1, H)
         updated = []
-        cache_shape = (b, c.num_key_value_heads, ctx, c.head_size)
         for layer, (old_key, old_value) in enumerate(caches):
-            if old_key.shape != cache_shape or old_value.shape != cache_shape:
+            if old_key.shape != (b, nkv, ctx, hd) or old_value.shape != (b, nkv, ctx, hd):
                 raise ValueError("KV cache has the wrong shape")
-            p = f"model.layers.{layer}"
-            a = f"{p}.self_attn"
-            normed = self._rms_norm(hidden, self._w(f"{p}.input_layernorm.weight"))
-            query = self._linear(normed, self._w(f"{a}.q_proj.weight")).reshape(
-                b, c.num_attention_heads, 1, c.head_size)
-            key = self._linear(normed, self._w(f"{a}.k_proj.weight")).reshape(
-                b, c.num_key_value_heads, 1, c.head_size)
-            value = self._linear(normed, self._w(f"{a}.v_proj.weight")).reshape(
-                b, c.num_key_value_heads, 1, c.head_size)
-            query = self._apply_rotation(query, rotation, position)
-            key = self._apply_rotation(key, rotation, position)
-            new_key = old_key * (1 - write_mask) + key * write_mask
-            new_value = old_value * (1 - write_mask) + value * write_mask
-            updated.extend((new_key, new_value))
-            attended = self._attend(query, new_key, new_value, attention_mask)
-            merged = attended.permute(0, 2, 1, 3).reshape(b, 1, c.hidden_size)
-            hidden = hidden + self._linear(merged, self._w(f"{a}.o_proj.weight"))
-            normed = self._rms_norm(hidden, self._w(f"{p}.post_attention_layernorm.weight"))
+            w = f"model.layers.{layer}"
+            normed = self._rms_norm(hidden, self.weights[f"{w}.input_layernorm.weight"])
+            q = self._linear(normed, self.weights[f"{w}.self_attn.q_proj.weight"]).reshape(b, nh, 1, hd)
+            k = self._linear(normed, self.weights[f"{w}.self_attn.k_proj.weight"]).reshape(b, nkv, 1, hd)
+            v = self._linear(normed, self.weights[f"{w}.self_attn.v_proj.weight"]).reshape(b, nkv, 1, hd)
+            q = self._apply_rotation(q, rotation, position)
+            k = self._apply_rotation(k, rotation, position)
+            keys = old_key * (1 - write_mask) + k * write_mask
+            values = old_value * (1 - write_mask) + v * write_mask
+            updated.extend((keys, values))
+            heads = self._attend(q, keys, values, attention_mask)
+            hidden = hidden + self._linear(heads.permute(0, 2, 1, 3).reshape(b, 1, c.hidden_size),
+                                           self.weights[f"{w}.self_attn.o_proj.weight"])
+            normed = self._rms_norm(hidden, self.weights[f"{w}.post_attention_layernorm.weight"])
             hidden = hidden + self._mlp(normed, layer)
-
-        hidden = self._rms_norm(hidden, self._w("model.norm.weight"))
-        logits = self._linear(hidden.reshape(b, c.hidden_size), self._w("lm_head.weight"))
+        hidden = self._rms_norm(hidden, self.weights["model.norm.weight"])
+        logits = self._linear(hidden.reshape(b, c.hidden_size), self.weights["lm_head.weight"])
         return (logits, *updated)
 
 
@@ -116,7 +123,7 @@ class BatchedRuntime(LlamaRuntime):
     def batched_step_inputs(self, tokens: Sequence[int], position: int, context: int) -> List[np.ndarray]:
         c = self.config
         ids = np.asarray(tokens, dtype=np.int32).reshape(-1, 1)
-        rotation = rope_rotations(1, c.head_size, c.rope_theta, self.dtype, offset=position)
+        rotation = _rope_rotations(1, c.head_size, c.rope_theta, self.dtype, offset=position)
         attention, write = decode_masks(position, context, self.dtype)
         return [ids, rotation, attention, write, np.asarray(position, dtype=np.int32)]
 

@@ -20,7 +20,7 @@ import numpy as np
 
 from . import _lib
 from .device import CudaB200Device, DeviceArray
-from .frontend.lazy import Compiler
+from chomikgrad.lazy import Compiler
 from .planner import Planner
 from .program import CudaB200Program
 

@@ -21,7 +21,7 @@ from typing import Any, Dict, Mapping, Optional, Sequence
 import numpy as np
 
 from . import _lib
-from .frontend.lazy import DeviceAdapter
+from chomikgrad.lazy import DeviceAdapter
 
 
 def _torch():

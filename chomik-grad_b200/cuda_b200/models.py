@@ -18,7 +18,7 @@ from typing import Dict, Optional
 
 import numpy as np
 
-from .frontend.llama import LlamaConfig, required_weight_shapes
+from chomikgrad.llama import LlamaConfig, required_weight_shapes
 
 
 def bfloat16() -> np.dtype:
@@ -59,6 +59,13 @@ LLAMA3_8B = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=1
                         num_hidden_layers=32, num_attention_heads=32,
                         num_key_value_heads=8, max_position_embeddings=8192,
                         rope_theta=500_000.0)
+# The Llama-3-8B shape cut to two layers: every per-layer shape, the head size
+# 128, theta 5e5 and the 128256-row vocabulary of LLAMA3_8B, at a size the
+# reference's cpu compiler runs in minutes (parity fixtures only).
+LLAMA3_8B_2L = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336,
+                           num_hidden_layers=2, num_attention_heads=32,
+                           num_key_value_heads=8, max_position_embeddings=8192,
+                           rope_theta=500_000.0)
 
 WORKLOADS: Dict[str, Workload] = {
     w.name: w
@@ -69,6 +76,7 @@ WORKLOADS: Dict[str, Workload] = {
         Workload("tinyllama-bf16-bs32", TINYLLAMA, "bfloat16", 32, 512, 256),
         Workload("tinyllama-bf16-prefill-bs8", TINYLLAMA, "bfloat16", 8, 2048, 0),
         Workload("llama3-8b-bf16-bs16", LLAMA3_8B, "bfloat16", 16, 1024, 256),
+        Workload("llama3-8b-2layer-bf16", LLAMA3_8B_2L, "bfloat16", 1, 32, 8),
     )
 }
 

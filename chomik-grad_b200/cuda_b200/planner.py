@@ -1358,7 +1358,7 @@ class Planner:
         key = ("rope", theta, np.dtype(dtype).str, tokens, hd, self.max_positions)
         cached = self.table_cache.get(key)
         if cached is None:
-            from .frontend.llama import rope_angles
+            from .graphs import rope_angles
 
             angles = rope_angles(self.max_positions + tokens - 1, hd, theta)
             cos = np.cos(angles).astype(dtype).astype(np.float32)

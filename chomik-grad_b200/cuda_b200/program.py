@@ -34,7 +34,7 @@ import numpy as np
 
 from . import _lib
 from .device import DeviceArray, torch_dtype
-from .frontend.lazy import CompiledProgram
+from chomikgrad.lazy import CompiledProgram
 from .planner import Buffer, Plan, Step, View, bf16, contiguous_strides, gemm_shape  # noqa: F401
 
 _BF16 = bf16()

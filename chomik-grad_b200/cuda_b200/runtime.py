@@ -14,8 +14,11 @@
   generator (:124-157, :712);
 * the caches returned by step n are bound as inputs of step n+1 (:857).
 
-It works with any registered compiler: ``cuda-b200`` for the product path,
-and the parity oracle's ``cpu`` compiler in tests.
+The graphs are the reference package's own (``chomikgrad.llama``
+``LlamaForCausalLM.prefill`` and ``LlamaDecoderStep``), compiled through
+``chomikgrad.compile_graph``.  It works with any compiler registered in
+``chomikgrad``'s registry: ``cuda-b200`` for the product path, the parity
+oracle or the reference's own ``cpu`` compiler in tests.
 """
 
 from __future__ import annotations
@@ -26,16 +29,11 @@ from typing import Any, Dict, List, Mapping, Optional, Sequence, Tuple
 
 import numpy as np
 
-from .frontend.lazy import get_compiler
-from .frontend.llama import (
-    LlamaConfig,
-    LlamaDecoderStep,
-    LlamaForCausalLM,
-    decode_masks,
-    position_selector,
-    rope_rotations,
-)
-from .frontend.tensor import Tensor, compile_graph, no_grad
+from chomikgrad.lazy import get_compiler
+from chomikgrad.llama import LlamaConfig, LlamaDecoderStep, LlamaForCausalLM, _rope_rotations, position_selector
+from chomikgrad.tensor import Tensor, compile_graph, no_grad
+
+from .graphs import decode_masks
 
 
 @dataclass
@@ -105,7 +103,7 @@ class LlamaRuntime:
     def _position_host(self, position: int, context: int) -> List[np.ndarray]:
         """The inputs of a step that depend on its position only: rotation, masks, position."""
         c = self.config
-        rotation = rope_rotations(1, c.head_size, c.rope_theta, self.dtype, offset=position)
+        rotation = _rope_rotations(1, c.head_size, c.rope_theta, self.dtype, offset=position)
         attention, write = decode_masks(position, context, self.dtype)
         return [rotation, attention, write, np.asarray(position, dtype=np.int32)]
 

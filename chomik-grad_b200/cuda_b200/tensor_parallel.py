@@ -38,9 +38,11 @@ from typing import Any, Dict, List, Mapping, Optional, Sequence, Tuple
 
 import numpy as np
 
+from chomikgrad.llama import LlamaConfig, LlamaForCausalLM, _prefer_lowering, _rope_rotations, position_selector
+from chomikgrad.tensor import Tensor, compile_graph, no_grad
+
 from .batched import BatchedDecoderStep, BatchedRuntime
-from .frontend.llama import MASKED, LlamaConfig, LlamaForCausalLM, _prefer, position_selector, rope_rotations
-from .frontend.tensor import Tensor, compile_graph, no_grad
+from .graphs import MASKED, GraphHelpers
 
 
 @dataclass(frozen=True)
@@ -140,17 +142,18 @@ def shard_weights(config: LlamaConfig, weights: Mapping[str, Any], layout: Shard
 
 def all_reduce(partial: Tensor, group: str) -> Tensor:
     """Sum of ``partial`` over the ranks of ``group``; on one rank the graph is ``partial`` itself."""
-    return _prefer(partial * 1, "all_reduce", (partial,), group)
+    return _prefer_lowering(partial * 1, "all_reduce", (partial,), group)
 
 
 def all_gather(part: Tensor, group: str, size: int, dtype) -> Tensor:
     """(size, *part.shape): every rank's ``part`` in rank order; on one rank the graph is exact."""
     spread = part.reshape(1, *part.shape) * Tensor.ones((size,) + (1,) * len(part.shape), dtype=dtype)
-    return _prefer(spread, "all_gather", (part,), group)
+    return _prefer_lowering(spread, "all_gather", (part,), group)
 
 
-class _ShardMixin:
-    """Shared overrides: local head counts in the GQA broadcast and the MLP all-reduce."""
+class _ShardMixin(GraphHelpers):
+    """Shared overrides of the reference's building blocks: local head counts in the GQA
+    broadcast, the MLP all-reduce, the vocabulary-sharded lm_head."""
 
     layout: ShardLayout
     group_name: str
@@ -198,11 +201,16 @@ def _init_model(model, config: LlamaConfig, weights: Mapping[str, Tensor], *, se
         model.cache_placement = Tensor(place)
     mask = np.triu(np.full((sequence_length, sequence_length), MASKED, dtype=model.dtype), k=1)
     model.causal_mask = Tensor(mask.reshape(1, 1, sequence_length, sequence_length))
-    model.rotations = Tensor(rope_rotations(sequence_length, config.head_size, config.rope_theta, model.dtype))
+    model.rotations = Tensor(_rope_rotations(sequence_length, config.head_size, config.rope_theta, model.dtype))
 
 
 class TensorParallelPrefill(_ShardMixin, LlamaForCausalLM):
-    """One rank's prefill (llama.py:382-433) over its shards, all-reducing O and down."""
+    """One rank's prefill (llama.py:382-433) over its shards, all-reducing O and down.
+
+    The reference's ``_forward`` runs unchanged; this class replaces its
+    ``_attention`` (local head counts, all-reduced O projection), ``_mlp``
+    and ``_linear`` (see ``_ShardMixin``).
+    """
 
     def __init__(self, config: LlamaConfig, weights: Mapping[str, Tensor], layout: ShardLayout, *,
                  sequence_length: int, dtype, cache_length: int, group: str = "tp") -> None:
@@ -214,9 +222,9 @@ class TensorParallelPrefill(_ShardMixin, LlamaForCausalLM):
         lay = self.layout
         p = f"model.layers.{layer}.self_attn"
         batch, tokens, _ = inputs.shape
-        query = self._linear(inputs, self._w(f"{p}.q_proj.weight"))
-        key = self._linear(inputs, self._w(f"{p}.k_proj.weight"))
-        value = self._linear(inputs, self._w(f"{p}.v_proj.weight"))
+        query = self._linear(inputs, self.weights[f"{p}.q_proj.weight"])
+        key = self._linear(inputs, self.weights[f"{p}.k_proj.weight"])
+        value = self._linear(inputs, self.weights[f"{p}.v_proj.weight"])
         query = query.reshape(batch, tokens, lay.heads, lay.head_size).permute(0, 2, 1, 3)
         key = key.reshape(batch, tokens, lay.kv_heads, lay.head_size).permute(0, 2, 1, 3)
         value = value.reshape(batch, tokens, lay.kv_heads, lay.head_size).permute(0, 2, 1, 3)
@@ -224,7 +232,7 @@ class TensorParallelPrefill(_ShardMixin, LlamaForCausalLM):
         key = self._apply_rope(key)
         attended = self._attend(query, key, value, self.causal_mask)
         merged = attended.permute(0, 2, 1, 3).reshape(batch, tokens, lay.heads * lay.head_size)
-        partial = self._linear(merged, self._w(f"{p}.o_proj.weight"))
+        partial = self._linear(merged, self.weights[f"{p}.o_proj.weight"])
         return self._reduce(partial), key, value
 
 
@@ -259,10 +267,10 @@ class TensorParallelDecoderStep(_ShardMixin, BatchedDecoderStep):
                 raise ValueError("KV cache shard has the wrong shape")
             p = f"model.layers.{layer}"
             a = f"{p}.self_attn"
-            normed = self._rms_norm(hidden, self._w(f"{p}.input_layernorm.weight"))
-            query = self._linear(normed, self._w(f"{a}.q_proj.weight")).reshape(b, lay.heads, 1, hd)
-            key = self._linear(normed, self._w(f"{a}.k_proj.weight")).reshape(b, lay.kv_heads, 1, hd)
-            value = self._linear(normed, self._w(f"{a}.v_proj.weight")).reshape(b, lay.kv_heads, 1, hd)
+            normed = self._rms_norm(hidden, self.weights[f"{p}.input_layernorm.weight"])
+            query = self._linear(normed, self.weights[f"{a}.q_proj.weight"]).reshape(b, lay.heads, 1, hd)
+            key = self._linear(normed, self.weights[f"{a}.k_proj.weight"]).reshape(b, lay.kv_heads, 1, hd)
+            value = self._linear(normed, self.weights[f"{a}.v_proj.weight"]).reshape(b, lay.kv_heads, 1, hd)
             query = self._apply_rotation(query, rotation, position)
             key = self._apply_rotation(key, rotation, position)
             new_key = old_key * (1 - write_mask) + key * write_mask
@@ -270,12 +278,12 @@ class TensorParallelDecoderStep(_ShardMixin, BatchedDecoderStep):
             updated.extend((new_key, new_value))
             attended = self._attend(query, new_key, new_value, attention_mask)
             merged = attended.permute(0, 2, 1, 3).reshape(b, 1, lay.heads * hd)
-            partial = self._linear(merged, self._w(f"{a}.o_proj.weight"))
+            partial = self._linear(merged, self.weights[f"{a}.o_proj.weight"])
             hidden = hidden + self._reduce(partial)
-            normed = self._rms_norm(hidden, self._w(f"{p}.post_attention_layernorm.weight"))
+            normed = self._rms_norm(hidden, self.weights[f"{p}.post_attention_layernorm.weight"])
             hidden = hidden + self._mlp(normed, layer)
-        hidden = self._rms_norm(hidden, self._w("model.norm.weight"))
-        logits = self._linear(hidden.reshape(b, c.hidden_size), self._w("lm_head.weight"))
+        hidden = self._rms_norm(hidden, self.weights["model.norm.weight"])
+        logits = self._linear(hidden.reshape(b, c.hidden_size), self.weights["lm_head.weight"])
         return (logits, *updated)
 
 

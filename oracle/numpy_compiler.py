@@ -23,7 +23,7 @@ from typing import Callable, Dict, List, Mapping, Optional, Sequence, Tuple
 
 import numpy as np
 
-from cuda_b200.frontend.lazy import (
+from chomikgrad.lazy import (
     CompiledProgram,
     Compiler,
     DeviceAdapter,
@@ -176,7 +176,13 @@ class NumpyCompiler(Compiler):
 
 
 def install() -> None:
-    """Register the oracle as the ``cpu`` compiler of the mirror registry."""
+    """Register the oracle as the ``cpu`` compiler of chomikgrad's registry (tests only).
+
+    It replaces the reference's own ``NumpyCompiler`` under that name in the
+    test process, so every ``compiler="cpu"`` graph runs on the restatement;
+    ``tests/test_oracle.py`` checks the restatement against the reference's
+    compiler on the same graphs and against the golden fixtures.
+    """
     register_compiler("cpu", NumpyCompiler, replace=True)
 
 

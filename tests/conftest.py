@@ -17,13 +17,16 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = ROOT / "tests" / "golden"
-for path in (ROOT / "chomik-grad_b200", ROOT):
+# The plugin runs under the unmodified reference package; machines without a
+# reference checkout import it from baseline/_ref (baseline/install_reference.py).
+for path in (ROOT / "baseline" / "_ref", ROOT / "chomik-grad_b200", ROOT):
     if str(path) not in sys.path:
         sys.path.insert(0, str(path))
 
-# The reference checkout, when this machine has one (fixture generation and
-# graph-equality tests only; never needed by GPU tests).
-REFERENCE = Path(os.environ.get("CHOMIK_REFERENCE", "/root/reference"))
+# A reference checkout (its examples/ and tests/ are not in the installed
+# package), only when CHOMIK_REFERENCE names one; tests that need it skip
+# otherwise.  GPU tests never need it.
+REFERENCE = Path(os.environ["CHOMIK_REFERENCE"]) if os.environ.get("CHOMIK_REFERENCE") else None
 
 
 def pytest_configure(config) -> None:
@@ -40,7 +43,7 @@ def golden(name: str) -> dict:
 
 @pytest.fixture(scope="session")
 def oracle():
-    """The restated reference ``cpu`` compiler, registered in the mirror registry."""
+    """The restated reference ``cpu`` compiler, registered as ``cpu`` in chomikgrad's registry."""
     from oracle import numpy_compiler
 
     numpy_compiler.install()
@@ -50,7 +53,7 @@ def oracle():
 @pytest.fixture(scope="session")
 def gpu():
     """The ``cuda-b200`` compiler on cuda:0 (GPU tests only)."""
+    import chomikgrad
     import cuda_b200
-    from cuda_b200.frontend.lazy import get_compiler
 
-    return get_compiler(cuda_b200.BACKEND)
+    return chomikgrad.get_compiler(cuda_b200.BACKEND)

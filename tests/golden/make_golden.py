@@ -73,7 +73,8 @@ def six_ops(ref) -> dict:
     return out
 
 
-def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling=None) -> dict:
+def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling=None,
+               prompt_tokens=None) -> dict:
     """Prefill + decode with the reference classes and its cpu compiler.
 
     Greedy, or with ``sampling = (temperature, top_k, seed)`` each token from
@@ -93,7 +94,7 @@ def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling
         def pick(native):
             return device.argmax(native)
     from cuda_b200.models import WORKLOADS, synthetic_prompt, synthetic_weights
-    from cuda_b200.frontend.llama import decode_masks
+    from cuda_b200.graphs import decode_masks
 
     wl = WORKLOADS[workload_name]
     cfg = L.LlamaConfig(**{k: getattr(wl.config, k) for k in (
@@ -104,7 +105,7 @@ def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling
     device = get_compiler("cpu").device
     weights = {n: Tensor.from_native(v, backend="cpu", shape=v.shape, dtype=v.dtype)
                for n, v in synthetic_weights(wl.config, dtype=dtype).items()}
-    prompt = synthetic_prompt(wl.config, wl.prompt_tokens)[0]
+    prompt = synthetic_prompt(wl.config, prompt_tokens or wl.prompt_tokens)[0]
     context = len(prompt) + steps
     out = {"prompt": prompt, "context": np.int64(context)}
     t0 = time.perf_counter()
@@ -237,6 +238,10 @@ CASES = {
     "tiny_bf16": lambda ref: generation(ref, "tiny-bf16", 32, (1, 31)),
     "tiny_block": lambda ref: block_decode(ref),
     "tinyllama_bf16": lambda ref: generation(ref, "tinyllama-bf16-bs1", 128, (1, 2, 64, 127)),
+    # the Llama-3-8B shape (head size 128, theta 5e5, vocabulary 128256) on two layers
+    "llama3_2layer_bf16": lambda ref: generation(ref, "llama3-8b-2layer-bf16", 8, (1, 7)),
+    # one 2048-token TinyLlama-shape prompt of the prefill workload: logits and first token
+    "tinyllama_prefill2048": lambda ref: generation(ref, "tinyllama-bf16-prefill-bs8", 1, (), prompt_tokens=2048),
     "sampling": lambda ref: sampling_rows(ref),
     "tiny_fp32_sampled": lambda ref: generation(ref, "tiny-fp32", 32, (), sampling=(0.8, 40, 3)),
 }

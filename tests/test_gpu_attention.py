@@ -109,8 +109,8 @@ def test_prefill_with_tensor_core_attention_matches_cpu_graph(gpu, oracle):
     """A 1-layer, head_size-64 bf16 model over 130 tokens: GEMMs + cb_sdpa_tc vs the cpu compiler."""
     import ml_dtypes
 
-    from cuda_b200.frontend.llama import LlamaConfig, LlamaForCausalLM, position_selector, required_weight_shapes
-    from cuda_b200.frontend.tensor import Tensor, compile_graph
+    from chomikgrad.llama import LlamaConfig, LlamaForCausalLM, position_selector, required_weight_shapes
+    from chomikgrad.tensor import Tensor, compile_graph
 
     dt = np.dtype(ml_dtypes.bfloat16)
     config = LlamaConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=1,

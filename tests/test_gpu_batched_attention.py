@@ -44,7 +44,7 @@ def test_batched_decode_attention_matches_float64(batch, heads, kv, hd, ctx, pos
     import torch
 
     from cuda_b200 import _lib
-    from cuda_b200.frontend.llama import decode_masks
+    from cuda_b200.graphs import decode_masks
 
     rng = np.random.default_rng(batch * 1000 + ctx)
     row = (heads + 2 * kv) * hd

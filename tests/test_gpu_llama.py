@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 
 from conftest import golden
-from cuda_b200.frontend.tensor import Tensor, compile_graph
+from chomikgrad.tensor import Tensor, compile_graph
 from cuda_b200.models import WORKLOADS, synthetic_weights
 from cuda_b200.runtime import LlamaRuntime
 
@@ -92,7 +92,7 @@ def test_returned_caches_are_the_bound_buffers(tiny_fp32):
 
 
 def test_block_decode_matches_reference(gpu, oracle):
-    from cuda_b200.frontend import llama as L
+    from chomikgrad import llama as L
 
     g = golden("tiny_block")
     wl = WORKLOADS["tiny-fp32"]
@@ -115,7 +115,7 @@ def test_block_decode_matches_reference(gpu, oracle):
         mask[0, 0, i, : start + i + 1] = 0
     block = L.LlamaDecoderBlock(cfg, weights, block_length=t, cache_length=ctx, dtype=np.float32)
     got = compile_graph(*block(Tensor(np.asarray([proposed], dtype=np.int32), copy=False),
-                               Tensor(L.rope_rotations(t, cfg.head_size, cfg.rope_theta,
+                               Tensor(L._rope_rotations(t, cfg.head_size, cfg.rope_theta,
                                                        np.dtype(np.float32), offset=start)),
                                Tensor(mask), Tensor(placement), Tensor(write), caches),
                         compiler="cuda-b200")()
@@ -143,7 +143,7 @@ def test_tinyllama_bf16_prefill_and_128_greedy_tokens(gpu):
 def test_decode_step_kernel_matches_per_kernel_launches(gpu, name):
     """One cb_decode_step launch per token == the same steps launched one by one."""
     from cuda_b200.compiler import CudaB200Compiler
-    from cuda_b200.frontend.lazy import register_compiler
+    from chomikgrad.lazy import register_compiler
 
     register_compiler("cuda-b200-kernels", lambda: CudaB200Compiler(decode_step=False), replace=True)
     wl = WORKLOADS[name]
@@ -173,7 +173,7 @@ def test_decode_step_kernel_matches_per_kernel_launches(gpu, name):
 def test_tiny_bf16_with_every_linear_on_the_tensor_core_gemm(gpu):
     """The prefill Linears on cb_gemm_tc (no row minimum) keep the golden bars."""
     from cuda_b200.compiler import CudaB200Compiler
-    from cuda_b200.frontend.lazy import register_compiler
+    from chomikgrad.lazy import register_compiler
 
     register_compiler("cuda-b200-gemm", lambda: CudaB200Compiler(gemm_min_rows=1), replace=True)
     g = golden("tiny_bf16")
@@ -185,3 +185,55 @@ def test_tiny_bf16_with_every_linear_on_the_tensor_core_gemm(gpu):
     assert np.max(np.abs(rt.device.to_numpy(logits) - g["prefill_logits"])) <= 2e-2
     result = rt.generate(list(g["prompt"]), len(g["tokens"]))
     assert result.tokens == [int(t) for t in g["tokens"]]
+
+
+def test_reference_graphs_through_chomikgrad_compile_graph(gpu):
+    """The reference's own entry points with no plugin runtime in between, driven the way
+    examples/generate_tinyllama.py:727-857 drives them: chomikgrad.compile_graph(...,
+    compiler="cuda-b200", dynamic_inputs=...) of LlamaForCausalLM.prefill and LlamaDecoderStep,
+    CompiledProgram.run(bindings), DeviceAdapter.array / argmax; the caches returned by one step
+    are bound as the next step's inputs."""
+    import chomikgrad
+    from chomikgrad import llama as L
+    from cuda_b200.graphs import decode_masks
+
+    g = golden("tiny_bf16")
+    wl = WORKLOADS["tiny-bf16"]
+    cfg, dt = wl.config, wl.np_dtype
+    device = chomikgrad.get_compiler("cuda-b200").device
+    weights = {}
+    for name, value in synthetic_weights(cfg, dtype=dt).items():
+        native = device.array(value)
+        weights[name] = chomikgrad.Tensor.from_native(native, backend="cuda-b200", shape=tuple(native.shape),
+                                                      dtype=device.dtype(native))
+    prompt, context = [int(t) for t in g["prompt"]], int(g["context"])
+    with chomikgrad.no_grad():
+        model = L.LlamaForCausalLM(cfg, weights, sequence_length=len(prompt), dtype=dt, cache_length=context)
+        ids = chomikgrad.Tensor(np.asarray([prompt], np.int32), copy=False)
+        selector = chomikgrad.Tensor(L.position_selector(len(prompt) - 1, len(prompt), dtype=dt), copy=False)
+        prefill = chomikgrad.compile_graph(*model.prefill(ids, selector), compiler="cuda-b200",
+                                           dynamic_inputs=(ids,))
+    native = prefill.run(None, synchronize=False)
+    assert np.max(np.abs(device.to_numpy(native[0]) - g["prefill_logits"])) <= 2e-2
+    tokens, caches = [device.argmax(native[0])], list(native[1:])
+    step = L.LlamaDecoderStep(cfg, weights, cache_length=context, dtype=dt)
+    decoder = nodes = None
+    for i in range(1, len(g["tokens"])):
+        position = len(prompt) + i - 1
+        host = [np.asarray([[tokens[-1]]], np.int32),
+                L._rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=position),
+                *decode_masks(position, context, dt), np.asarray(position, np.int32)]
+        if decoder is None:
+            inputs = [chomikgrad.Tensor(v, copy=False) for v in host]
+            cache_inputs = [chomikgrad.Tensor.from_native(c, backend="cuda-b200", shape=tuple(c.shape), dtype=dt)
+                            for c in caches]
+            with chomikgrad.no_grad():
+                outs = step(*inputs[:4], list(zip(cache_inputs[::2], cache_inputs[1::2])), position=inputs[4])
+            decoder = chomikgrad.compile_graph(*outs, compiler="cuda-b200", dynamic_inputs=inputs + cache_inputs)
+            nodes = [t._node for t in inputs + cache_inputs]
+            native = decoder.run(None, synchronize=False)
+        else:
+            native = decoder.run(dict(zip(nodes, [device.array(v) for v in host] + caches)), synchronize=False)
+        tokens.append(device.argmax(native[0]))
+        caches = list(native[1:])
+    assert tokens == [int(t) for t in g["tokens"]]

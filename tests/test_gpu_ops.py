@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from conftest import golden
-from cuda_b200.frontend.tensor import Tensor, compile_graph
+from chomikgrad.tensor import Tensor, compile_graph
 
 pytestmark = pytest.mark.gpu
 
@@ -117,7 +117,7 @@ def test_float64_is_rejected_without_fallback(gpu):
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
 def test_llama_lowerings_match_portable_cpu_graph(gpu, oracle, dtype):
     """rms_norm/rope/sdpa lowerings on a 1-layer model (pattern of test_mlx.py:120-158)."""
-    from cuda_b200.frontend.llama import LlamaConfig, LlamaForCausalLM, position_selector, required_weight_shapes
+    from chomikgrad.llama import LlamaConfig, LlamaForCausalLM, position_selector, required_weight_shapes
 
     dt = np.dtype(np.float32) if dtype == "float32" else bf16()
     config = LlamaConfig(vocab_size=64, hidden_size=64, intermediate_size=96, num_hidden_layers=1,

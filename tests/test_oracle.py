@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 from conftest import golden
-from cuda_b200.frontend.tensor import Tensor
+from chomikgrad.tensor import Tensor
 from cuda_b200.models import WORKLOADS, synthetic_weights
 from cuda_b200.runtime import LlamaRuntime
 

@@ -24,10 +24,11 @@ import pytest
 from cuda_b200 import _lib
 from cuda_b200 import tensor_parallel as tp
 from cuda_b200.batched import BatchedDecoderStep
-from cuda_b200.frontend import llama as L
-from cuda_b200.frontend.tensor import Tensor, no_grad
+from chomikgrad import llama as L
+from chomikgrad.tensor import Tensor, no_grad
 from cuda_b200.models import TINY, WORKLOADS, synthetic_prompt, synthetic_weights
 from cuda_b200.planner import Planner
+from cuda_b200.graphs import decode_masks
 from plan_interpreter import PlanInterpreter, run_ranks
 
 BF16 = np.dtype(ml_dtypes.bfloat16)
@@ -104,9 +105,9 @@ def _decode_graph(wl, weights, ctx, position, seed):
     shape = (1, cfg.num_key_value_heads, ctx, cfg.head_size)
     caches = [Tensor.from_native(c, backend="cpu", shape=shape, dtype=dt)
               for c in _caches(shape, 2 * cfg.num_hidden_layers, seed)]
-    am, wm = L.decode_masks(position, ctx, dt)
+    am, wm = decode_masks(position, ctx, dt)
     inputs = [Tensor(np.array([[11]], np.int32), copy=False),
-              Tensor(L.rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=position), copy=False),
+              Tensor(L._rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=position), copy=False),
               Tensor(am, copy=False), Tensor(wm, copy=False), Tensor(np.asarray(position, np.int32), copy=False)]
     with no_grad():
         outs = L.LlamaDecoderStep(cfg, weights, cache_length=ctx, dtype=dt)(
@@ -161,10 +162,10 @@ def _batched_graph(config, weights, dt, batch, ctx, position, seed):
     shape = (batch, config.num_key_value_heads, ctx, config.head_size)
     caches = [Tensor.from_native(c, backend="cpu", shape=shape, dtype=dt)
               for c in _caches(shape, 2 * config.num_hidden_layers, seed)]
-    am, wm = L.decode_masks(position, ctx, dt)
+    am, wm = decode_masks(position, ctx, dt)
     rng = np.random.default_rng(seed)
     inputs = [Tensor(rng.integers(0, config.vocab_size, (batch, 1)).astype(np.int32), copy=False),
-              Tensor(L.rope_rotations(1, config.head_size, config.rope_theta, dt, offset=position), copy=False),
+              Tensor(L._rope_rotations(1, config.head_size, config.rope_theta, dt, offset=position), copy=False),
               Tensor(am, copy=False), Tensor(wm, copy=False), Tensor(np.asarray(position, np.int32), copy=False)]
     with no_grad():
         outs = BatchedDecoderStep(config, weights, batch=batch, cache_length=ctx, dtype=dt)(
@@ -207,7 +208,7 @@ def test_tensor_parallel_plans_match_the_one_rank_oracle(size, vocab_shard):
                                                   2 * config.num_hidden_layers, 5)]
     rng = np.random.default_rng(5)
     ids = rng.integers(0, config.vocab_size, (batch, 1)).astype(np.int32)
-    am, wm = L.decode_masks(position, ctx, BF16)
+    am, wm = decode_masks(position, ctx, BF16)
     interpreters, layouts = [], []
     for rank in range(size):
         lay = tp.shard_layout(config, size, rank, vocab_shard=vocab_shard)
@@ -216,7 +217,7 @@ def test_tensor_parallel_plans_match_the_one_rank_oracle(size, vocab_shard):
             step = tp.TensorParallelDecoderStep(
                 config, {k: Tensor(v) for k, v in tp.shard_weights(config, full_w, lay).items()}, lay,
                 batch=batch, cache_length=ctx, dtype=BF16)
-            t = [Tensor(ids), Tensor(L.rope_rotations(1, config.head_size, config.rope_theta, BF16, offset=position)),
+            t = [Tensor(ids), Tensor(L._rope_rotations(1, config.head_size, config.rope_theta, BF16, offset=position)),
                  Tensor(am), Tensor(wm), Tensor(np.asarray(position, np.int32))]
             ct = [Tensor(c[:, kv:kv + lay.kv_heads].copy()) for c in full_caches]
             rank_outs = step(t[0], t[1], t[2], t[3], list(zip(ct[::2], ct[1::2])), position=t[4])

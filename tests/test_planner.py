@@ -8,9 +8,10 @@ import itertools
 import numpy as np
 import pytest
 
-from cuda_b200.frontend import llama as L
-from cuda_b200.frontend.tensor import Tensor
+from chomikgrad import llama as L
+from chomikgrad.tensor import Tensor
 from cuda_b200.models import WORKLOADS, synthetic_prompt, synthetic_weights
+from cuda_b200.graphs import decode_masks
 from cuda_b200.planner import Planner, PlanError, reshape_strides
 
 
@@ -64,9 +65,9 @@ def _decode_graph(wl, weights, ctx=48, cache_dtype=np.float32):
     shape = (1, cfg.num_key_value_heads, ctx, cfg.head_size)
     caches = [Tensor.from_native(np.zeros(shape, cache_dtype), backend="cpu", shape=shape, dtype=dt)
               for _ in range(2 * cfg.num_hidden_layers)]
-    am, wm = L.decode_masks(5, ctx, dt)
+    am, wm = decode_masks(5, ctx, dt)
     inputs = [Tensor(np.array([[3]], np.int32), copy=False),
-              Tensor(L.rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=5), copy=False),
+              Tensor(L._rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=5), copy=False),
               Tensor(am, copy=False), Tensor(wm, copy=False), Tensor(np.asarray(5, np.int32), copy=False)]
     outs = L.LlamaDecoderStep(cfg, weights, cache_length=ctx, dtype=dt)(
         *inputs[:4], list(zip(caches[::2], caches[1::2])), position=inputs[4])
@@ -232,9 +233,9 @@ def test_batched_decode_plan_updates_caches_in_place(tiny_bf16):
     shape = (b, cfg.num_key_value_heads, ctx, cfg.head_size)
     caches = [Tensor.from_native(np.zeros(shape, np.float32), backend="cpu", shape=shape, dtype=dt)
               for _ in range(2 * cfg.num_hidden_layers)]
-    am, wm = L.decode_masks(5, ctx, dt)
+    am, wm = decode_masks(5, ctx, dt)
     inputs = [Tensor(np.full((b, 1), 3, np.int32), copy=False),
-              Tensor(L.rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=5), copy=False),
+              Tensor(L._rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=5), copy=False),
               Tensor(am, copy=False), Tensor(wm, copy=False), Tensor(np.asarray(5, np.int32), copy=False)]
     outs = BatchedDecoderStep(cfg, weights, batch=b, cache_length=ctx, dtype=dt)(
         *inputs[:4], list(zip(caches[::2], caches[1::2])), position=inputs[4])
@@ -263,9 +264,9 @@ def test_batched_decode_plan_fuses_into_row_gemms_and_one_attention(tiny_bf16):
     shape = (b, cfg.num_key_value_heads, ctx, cfg.head_size)
     caches = [Tensor.from_native(np.zeros(shape, np.float32), backend="cpu", shape=shape, dtype=dt)
               for _ in range(2 * cfg.num_hidden_layers)]
-    am, wm = L.decode_masks(5, ctx, dt)
+    am, wm = decode_masks(5, ctx, dt)
     inputs = [Tensor(np.full((b, 1), 3, np.int32), copy=False),
-              Tensor(L.rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=5), copy=False),
+              Tensor(L._rope_rotations(1, cfg.head_size, cfg.rope_theta, dt, offset=5), copy=False),
               Tensor(am, copy=False), Tensor(wm, copy=False), Tensor(np.asarray(5, np.int32), copy=False)]
     outs = BatchedDecoderStep(cfg, weights, batch=b, cache_length=ctx, dtype=dt)(
         *inputs[:4], list(zip(caches[::2], caches[1::2])), position=inputs[4])

@@ -18,9 +18,10 @@ import pytest
 
 from cuda_b200 import tensor_parallel as tp
 from cuda_b200.batched import BatchedDecoderStep
-from cuda_b200.frontend.llama import LlamaForCausalLM, decode_masks, position_selector, rope_rotations
-from cuda_b200.frontend.lazy import topological_sort
-from cuda_b200.frontend.tensor import Tensor, no_grad
+from chomikgrad.llama import LlamaForCausalLM, _rope_rotations as rope_rotations, position_selector
+from cuda_b200.graphs import decode_masks
+from chomikgrad.lazy import topological_sort
+from chomikgrad.tensor import Tensor, no_grad
 from cuda_b200.models import LLAMA3_8B, TINY, TINYLLAMA, synthetic_weights
 from cuda_b200.planner import Planner
 from oracle.numpy_compiler import evaluate_node

@@ -39,7 +39,7 @@ class _Case:
 
     def __init__(self, torch, tables, qkv, k_cache, v_cache, position, share_caches=None):
         from cuda_b200 import _lib
-        from cuda_b200.frontend.llama import decode_masks
+        from cuda_b200.graphs import decode_masks
 
         mask, write = decode_masks(position, CONTEXT, np.float32)
         self.qkv = qkv.cuda()
