@@ -20,7 +20,7 @@
 // call before any stream capture on the device.  Later calls only launch.
 //
 // Limits.  splits * heads * (head_size + 2) floats of partials (splits =
-// ceil(context / 32)) must fit kScratchFloats (4 MiB), and kv_heads must not
+// ceil(context / 32)) must fit kScratchFloats (1 Mi floats, 4 MiB), and kv_heads must not
 // exceed kMaxKvHeads; larger requests are rejected before any launch.
 //
 // Sharing.  One scratch area per device serves every call: calls that
@@ -34,7 +34,7 @@
 namespace cb {
 namespace {
 
-constexpr long long kScratchFloats = 1LL << 20;  // 4 MiB of split partials
+constexpr long long kScratchFloats = 1LL << 20;  // 1 Mi floats (4 MiB) of split partials
 constexpr int kMaxKvHeads = 256;
 constexpr int kMaxDevices = 64;
 

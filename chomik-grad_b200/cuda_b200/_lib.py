@@ -206,6 +206,7 @@ class GemmRowsArgs(ctypes.Structure):
 
 
 ROWS_X_PLAIN, ROWS_X_RMS, ROWS_X_SWIGLU = 0, 1, 2  # cb_gemm_rows x prologues
+STEP_X_VECTORS = 3 * 256  # x vectors (8 bf16-weight or 4 float32-weight columns) a cb_decode_step phase stages
 
 
 class StepPhase(ctypes.Structure):

@@ -75,9 +75,21 @@ class CudaB200Program(CompiledProgram):
 
     @staticmethod
     def _fusable(plan: Plan) -> bool:
-        """Whether the plan is a fused decode step cb_decode_step can run whole."""
+        """Whether the plan is a fused decode step cb_decode_step can run whole.
+
+        Its consumer threads stage at most 3 x 256 vectors of x per phase
+        (6144 bf16-weight or 3072 float32-weight columns); a plan with a wider
+        GEMV (the Llama-3-8B down projection, 14336) runs kernel by kernel.
+        """
         names = {s.name for s in plan.steps}
-        return bool(plan.steps) and names <= {"gemv", "decode_attention"} and "gemv" in names
+        if not (plan.steps and names <= {"gemv", "decode_attention"} and "gemv" in names):
+            return False
+        for s in plan.steps:
+            if s.name == "gemv":
+                elems = 8 if s.args["weights"][0].dtype.itemsize == 2 else 4
+                if s.args["k"] > _lib.STEP_X_VECTORS * elems:
+                    return False
+        return True
 
     # ------------------------------------------------------------ build
     def _build(self) -> None:

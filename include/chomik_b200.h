@@ -404,10 +404,11 @@ CB_API int cb_decode_attention_batched(const cb_decode_attention_args* args, lon
  * already holds all of HBM, a decode loop that cannot afford the device
  * synchronisation cudaFree brings).  This entry point has no counterpart in
  * the reference.  `scratch` and `counters` in args are ignored: the library
- * uses its own fixed device arrays (4 Mi floats of partials, 256 counters).
+ * uses its own fixed device arrays (1 Mi floats = 4 MiB of partials, 256
+ * counters).
  * The first call on a device, with that device current, sets them up (symbol
  * lookup, counters cleared, device synchronised); make it before any stream
- * capture.  Larger requests (splits * heads * (head_size + 2) > 4 Mi floats,
+ * capture.  Larger requests (splits * heads * (head_size + 2) > 1 Mi floats,
  * kv_heads > 256) return CB_ERR_INVALID before any launch.  All calls on a
  * device share the arrays: calls that overlap on the GPU race. */
 CB_API int cb_decode_attention_noalloc(const cb_decode_attention_args* args, cb_stream_t stream);

@@ -1,10 +1,15 @@
 """cb_decode_attention_noalloc against cb_decode_attention, through the C ABI.
 
-The no-alloc entry point keeps its split partials and counters in fixed
-device arrays inside the library.  Two calls in a row (different positions,
-the second on the caches the first updated) must match the allocating entry
-point, and the counters must be back at zero after each call.  This file is
-named to run last, so it is exercised both alone and after every other test.
+The no-alloc entry point serves callers that cannot allocate device memory:
+it keeps its split partials and per-KV-head counters in fixed device arrays
+inside the library.  Two calls in a row (different positions, the second on
+the caches the first updated) must match the allocating entry point.  The
+counters are not readable from outside the library; that each call leaves
+them at zero is shown by its effect: two more calls with four KV heads (the
+first uses counters 0-3, the second reuses them, including the two that no
+earlier call touched) also match the allocating entry point, which only holds
+if every counter was back at zero.  This file is named to run last, so it is
+exercised both alone and after every other test.
 """
 
 from __future__ import annotations
@@ -19,11 +24,11 @@ pytestmark = pytest.mark.gpu
 HEADS, KV_HEADS, HEAD_SIZE, CONTEXT, N_POSITIONS = 8, 2, 64, 80, 128
 
 
-def _inputs(torch, seed):
+def _inputs(torch, seed, heads=HEADS, kv_heads=KV_HEADS):
     gen = torch.Generator().manual_seed(seed)
-    qkv = torch.randn((HEADS + 2 * KV_HEADS) * HEAD_SIZE, generator=gen)
-    k_cache = torch.randn(KV_HEADS, CONTEXT, HEAD_SIZE, generator=gen)
-    v_cache = torch.randn(KV_HEADS, CONTEXT, HEAD_SIZE, generator=gen)
+    qkv = torch.randn((heads + 2 * kv_heads) * HEAD_SIZE, generator=gen)
+    k_cache = torch.randn(kv_heads, CONTEXT, HEAD_SIZE, generator=gen)
+    v_cache = torch.randn(kv_heads, CONTEXT, HEAD_SIZE, generator=gen)
     return qkv, k_cache, v_cache
 
 
@@ -37,7 +42,8 @@ def _tables(torch):
 class _Case:
     """Device buffers of one decode-attention call at `position`."""
 
-    def __init__(self, torch, tables, qkv, k_cache, v_cache, position, share_caches=None):
+    def __init__(self, torch, tables, qkv, k_cache, v_cache, position, share_caches=None,
+                 heads=HEADS, kv_heads=KV_HEADS):
         from cuda_b200 import _lib
         from cuda_b200.graphs import decode_masks
 
@@ -51,12 +57,12 @@ class _Case:
         self.position = torch.tensor([position], dtype=torch.int64).cuda()
         self.mask = torch.from_numpy(mask.reshape(-1).copy()).cuda()
         self.write = torch.from_numpy(write.reshape(-1).copy()).cuda()
-        self.out = torch.full((HEADS * HEAD_SIZE,), float("nan")).cuda()
+        self.out = torch.full((heads * HEAD_SIZE,), float("nan")).cuda()
         self.flag = torch.zeros(1, dtype=torch.int32).cuda()
         a = _lib.DecodeAttentionArgs()
         a.qkv = self.qkv.data_ptr()
-        a.q_off, a.k_off, a.v_off = 0, HEADS * HEAD_SIZE, (HEADS + KV_HEADS) * HEAD_SIZE
-        a.heads, a.kv_heads, a.head_size, a.context = HEADS, KV_HEADS, HEAD_SIZE, CONTEXT
+        a.q_off, a.k_off, a.v_off = 0, heads * HEAD_SIZE, (heads + kv_heads) * HEAD_SIZE
+        a.heads, a.kv_heads, a.head_size, a.context = heads, kv_heads, HEAD_SIZE, CONTEXT
         a.position, a.position_dtype = self.position.data_ptr(), _lib.I64
         a.cos_table, a.sin_table = tables[0].data_ptr(), tables[1].data_ptr()
         a.n_positions = N_POSITIONS
@@ -80,7 +86,7 @@ def _allocating(torch, case):
 
     floats = _lib.load().cb_decode_attention_scratch(ctypes.byref(case.args))
     scratch = torch.empty(floats, dtype=torch.float32, device="cuda")
-    counters = torch.zeros(KV_HEADS, dtype=torch.int32, device="cuda")
+    counters = torch.zeros(case.args.kv_heads, dtype=torch.int32, device="cuda")
     case.args.scratch, case.args.counters = scratch.data_ptr(), counters.data_ptr()
     _lib.call("cb_decode_attention", ctypes.byref(case.args), torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
@@ -123,12 +129,30 @@ def test_no_alloc_decode_attention_matches_two_calls_in_a_row():
     assert not np.array_equal(got1[1][:, 37], k_cache.numpy()[:, 37])
     np.testing.assert_array_equal(np.delete(got1[1], 37, axis=1), np.delete(k_cache.numpy(), 37, axis=1))
 
+    # two more calls in order with four KV heads: counters 2 and 3 are used for the first time by
+    # the third call and again by the fourth, so the fourth matches only if the third reset them
+    wide = dict(heads=16, kv_heads=4)
+    qkv3, k3, v3 = _inputs(torch, 3, **wide)
+    qkv4, _, _ = _inputs(torch, 4, **wide)
+    expect3 = _allocating(torch, _Case(torch, tables, qkv3, k3, v3, 50, **wide))
+    expect4 = _allocating(torch, _Case(torch, tables, qkv4, torch.from_numpy(expect3[1]),
+                                       torch.from_numpy(expect3[2]), 51, **wide))
+    third = _Case(torch, tables, qkv3, k3, v3, 50, **wide)
+    fourth = _Case(torch, tables, qkv4, None, None, 51, share_caches=third, **wide)
+    got3 = _no_alloc(torch, third)
+    got4 = _no_alloc(torch, fourth)
+    for got, expect in ((got3, expect3), (got4, expect4)):
+        assert np.isfinite(got[0]).all()
+        for g, e in zip(got[:3], expect[:3]):
+            np.testing.assert_allclose(g, e, rtol=1e-4, atol=1e-6)
+        assert got[3][0] == 0
+
 
 def test_no_alloc_decode_attention_rejects_requests_beyond_its_scratch():
     torch = pytest.importorskip("torch")
     from cuda_b200 import _lib
 
-    heads, kv_heads, hd, context = 32, 8, 128, 8192  # 256 splits * 32 * 130 > 4 Mi floats
+    heads, kv_heads, hd, context = 32, 8, 128, 8192  # 256 splits * 32 * 130 = 1,064,960 > 1 Mi floats
     qkv = torch.zeros((heads + 2 * kv_heads) * hd, device="cuda")
     k_cache = torch.zeros(kv_heads, context, hd, device="cuda")
     v_cache = torch.zeros_like(k_cache)
