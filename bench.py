@@ -30,8 +30,11 @@ Reported:
              then batched decode, tensor-parallel over all N ranks (TP = N,
              NCCL all-reduce inside each rank's decode graph); tokens/s of the
              group and the fraction of the group's aggregate HBM bandwidth.
-  cpu_baseline  the parity oracle (restated reference cpu compiler, NumPy +
-             ml_dtypes) timing real decode steps of the same model on the host.
+  cpu_baseline  the unmodified reference's own cpu compiler (from baseline/_ref)
+             timing real decode steps of the same model on the host cores:
+             the float32 model on the bf16-rounded weights (BLAS threads
+             measured), and beside it the bf16 model as the reference's loop
+             runs it (cpu_baseline_bf16_literal).
 Inputs are larger than L2 (2.07 GB of weights per step), so no flush is needed.
 """
 
@@ -175,15 +178,33 @@ def weight_bytes(config, itemsize: int) -> int:
     return total * itemsize
 
 
-def cpu_baseline(wl, weights, budget_s: float = 25.0):
-    """Oracle decode steps of the same model on host cores (bounded sample)."""
-    from oracle import numpy_compiler
+def blas_threads() -> int:
+    """Threads NumPy's BLAS uses (threadpoolctl), after a first matmul loaded it."""
+    import threadpoolctl
 
-    numpy_compiler.install()
+    np.ones((64, 64), np.float32) @ np.ones((64, 64), np.float32)
+    counts = [info.get("num_threads", 1) for info in threadpoolctl.threadpool_info() if info.get("user_api") == "blas"]
+    return max(counts) if counts else 1
+
+
+def cpu_baseline(wl, weights, budget_s: float = 25.0, mode: str = "fp32"):
+    """Decode steps of the same model on the host cores through the UNMODIFIED reference's own
+    ``cpu`` compiler (chomikgrad.lazy.NumpyCompiler, imported from baseline/_ref), in a bounded sample.
+
+    mode "fp32": the model in float32 on the bf16-rounded weights -- every matmul a float32 BLAS
+    call on all the BLAS threads (the fastest the reference runs this model on a CPU);
+    mode "bf16": the bf16 model as the reference's loop runs it, whose first matmul per layer
+    runs in ml_dtypes bfloat16 loops (single-threaded) and the rest in float32.
+    """
+    import chomikgrad
+
     from cuda_b200.runtime import LlamaRuntime
 
+    assert type(chomikgrad.get_compiler("cpu")).__module__ == "chomikgrad.lazy", "cpu must be the reference's"
     cfg = wl.config
-    rt = LlamaRuntime(cfg, weights, compiler="cpu")
+    dtype = np.dtype(np.float32) if mode == "fp32" else wl.np_dtype
+    host = {k: np.asarray(v).astype(dtype) for k, v in weights.items()} if mode == "fp32" else weights
+    rt = LlamaRuntime(cfg, host, compiler="cpu", dtype=dtype)
     context = wl.context
     shape = (1, cfg.num_key_value_heads, context, cfg.head_size)
     caches = [np.zeros(shape, np.float32) for _ in range(2 * cfg.num_hidden_layers)]
@@ -203,11 +224,15 @@ def cpu_baseline(wl, weights, budget_s: float = 25.0):
             break
     warm = times[1:] if len(times) > 1 else times
     per_token = statistics.median(warm)
-    return {"value": 1.0 / per_token, "unit": "tokens/s", "cores": 1, "kind": "port",
-            "sample": f"{len(times)} decode steps (first excluded if >1) of {wl.name} at context "
-                      f"{context} through the restated reference cpu compiler (NumPy {np.__version__}, "
-                      f"ml_dtypes bf16 matmuls run single-threaded); {os.cpu_count()} host cores present",
-            "seconds_per_token": per_token}
+    threads = blas_threads() if mode == "fp32" else 1
+    what = ("float32 model on the bf16-rounded weights, every matmul a float32 BLAS call" if mode == "fp32" else
+            "bf16 model as the reference's loop runs it (first matmul per layer in single-threaded ml_dtypes "
+            "bfloat16 loops, the rest float32)")
+    return {"value": 1.0 / per_token, "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"{len(times)} decode steps (first excluded if >1) of {wl.name} at context {context} through "
+                      f"the unmodified reference's cpu compiler (chomikgrad.lazy.NumpyCompiler): {what}; "
+                      f"NumPy {np.__version__}, {threads} BLAS thread(s) used, {os.cpu_count()} host cores",
+            "seconds_per_token": per_token, "mode": mode}
 
 
 def run_reference(args) -> None:
@@ -219,14 +244,16 @@ def run_reference(args) -> None:
     wl = WORKLOADS[args.workload]
     weights = synthetic_weights(wl.config, dtype=wl.np_dtype)
     budget = float(os.environ.get("CB_REFERENCE_BUDGET_S", "150"))
-    base = cpu_baseline(wl, weights, budget_s=budget)
+    base = cpu_baseline(wl, weights, budget_s=budget, mode=args.reference_mode)
     line = {
         "metric": METRIC, "value": base["value"], "unit": "tokens/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * base["seconds_per_token"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.reference_mode == "fp32" else "bf16",
+        "data": "synthetic",
         "config": {"workload": wl.name, "model": "TinyLlama-1.1B-shape (random init)", "global_batch": 1,
-                   "prompt_tokens": wl.prompt_tokens, "context": wl.context},
+                   "prompt_tokens": wl.prompt_tokens, "context": wl.context,
+                   "reference_mode": args.reference_mode},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -510,6 +537,9 @@ def main() -> None:
     parser.add_argument("--impl", default="b200", choices=("b200", "reference"))
     parser.add_argument("--workload", default="tinyllama-bf16-bs1")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--reference-mode", default="fp32", choices=("fp32", "bf16"),
+                        help="--impl reference: the reference cpu compiler on the float32 model (bf16-rounded "
+                             "weights, BLAS on every core; the default) or on the bf16 model as its loop runs it")
     parser.add_argument("--bs32-steps", type=int, default=100,
                         help="batched decode steps (32 sequences each) of the bs32 measurement; 0 skips it")
     parser.add_argument("--prefill-steps", type=int, default=2,
@@ -645,8 +675,10 @@ def main() -> None:
         line["llama3_8b_tp"] = llama3_measurement(rank, world, local, args.llama3_steps, args.warmup,
                                                   args.llama3_prompt, args.vocab_shard)
     if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, weights).items()
-                                if k in ("value", "unit", "cores", "kind", "sample")}
+        keys = ("value", "unit", "cores", "kind", "sample")
+        line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, weights, mode="fp32").items() if k in keys}
+        line["cpu_baseline_bf16_literal"] = {k: v for k, v in cpu_baseline(wl, weights, budget_s=15.0,
+                                                                           mode="bf16").items() if k in keys}
     if world > 1:
         import torch.distributed as dist
 

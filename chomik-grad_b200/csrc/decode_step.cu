@@ -98,6 +98,7 @@ struct StepParams {
   long long prefetch_bytes;      // L2 lookahead per block and phase
   int lane_inflight;             // ring copies in flight per producer lane (1 or 2)
   int quiet_window;              // pause ring copies from a phase's wait until its x is staged
+  int test_withhold;             // see cb_decode_step_config
 };
 
 enum {
@@ -138,22 +139,37 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 
 // Until *c >= target: bounded by time and polls, and abandoned once the
 // step has failed elsewhere.
+// The waits below read the clock (%globaltimer) only every few polls and
+// start it at the first such read, so a wait that finds its condition met
+// costs one poll.  `limit_ns` bounds a wait in time: the producer's waits on
+// the consumers get twice the consumers' limit, so when a consumer wait runs
+// out, it is the one that reports.
+__device__ __forceinline__ bool waited_too_long(uint64_t* start, uint64_t limit_ns) {
+  const uint64_t now = global_ns();
+  if (*start == 0) {
+    *start = now;
+    return false;
+  }
+  return now - *start > limit_ns;
+}
+
 __device__ bool wait_counter(const unsigned* c, unsigned target, const int* flag) {
-  const uint64_t start = global_ns();
+  uint64_t start = 0;
   for (uint32_t i = 0; i < kWaitPolls; ++i) {
     if (ld_acquire(c) >= target) return true;
-    if ((i & 15u) == 15u && (step_failed(flag) || global_ns() - start > kWaitNs)) return false;
+    if ((i & 15u) == 15u && (step_failed(flag) || waited_too_long(&start, kWaitNs))) return false;
     __nanosleep(32);
   }
   return false;
 }
 
 // mbarrier wait that also gives up when this block has stopped (*stop != 0).
-__device__ bool wait_or_stop(uint64_t* bar, uint32_t parity, const volatile int* stop) {
-  const uint64_t start = global_ns();
+__device__ bool wait_or_stop(uint64_t* bar, uint32_t parity, const volatile int* stop,
+                             uint64_t limit_ns = kWaitNs) {
+  uint64_t start = 0;
   for (uint32_t i = 0; i < kWaitPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 63u && (*stop != 0 || global_ns() - start > kWaitNs)) return false;
+    if ((i & 63u) == 63u && (*stop != 0 || waited_too_long(&start, limit_ns))) return false;
   }
   return false;
 }
@@ -164,10 +180,10 @@ __device__ bool wait_loud(const int* quiet, const int* stop) {
   const volatile int* q = quiet;
   const volatile int* s = stop;
   if (*q == 0) return true;
-  const uint64_t start = global_ns();
+  uint64_t start = 0;
   for (uint32_t i = 0; i < kWaitPolls; ++i) {
     if (*q == 0) return true;
-    if (*s != 0 || ((i & 15u) == 15u && global_ns() - start > kWaitNs)) return false;
+    if (*s != 0 || ((i & 15u) == 15u && waited_too_long(&start, 2 * kWaitNs))) return false;
     __nanosleep(64);
   }
   return false;
@@ -673,7 +689,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
           const long long gs = g + s;
           const int slot = static_cast<int>(gs % kStepSlots);
           const long long round = gs / kStepSlots;
-          if (round > 0 && !wait_or_stop(empty + slot, static_cast<uint32_t>((round - 1) & 1), &sh.stop)) {
+          if (round > 0 &&
+              !wait_or_stop(empty + slot, static_cast<uint32_t>((round - 1) & 1), &sh.stop, 2 * kWaitNs)) {
             if (!sh.stop) raise_flag(S.error_flag, CB_FLAG_WAIT_SLOT);
             stop = true;
             break;
@@ -681,7 +698,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
           // with one copy in flight per lane, the lane's previous copy lands first
           // (its slot is not reused before it is consumed, so the parity is exact)
           if (S.lane_inflight == 1 && last >= 0 &&
-              !wait_or_stop(full + last % kStepSlots, static_cast<uint32_t>((last / kStepSlots) & 1), &sh.stop)) {
+              !wait_or_stop(full + last % kStepSlots, static_cast<uint32_t>((last / kStepSlots) & 1), &sh.stop,
+                            2 * kWaitNs)) {
             if (!sh.stop) raise_flag(S.error_flag, CB_FLAG_WAIT_SLOT);
             stop = true;
             break;
@@ -817,7 +835,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     if (tid == 0) stamp(S, p, kStampDone);
     if (tid == 0 && *reinterpret_cast<volatile int*>(&sh.stop) == 0) {
       if (p < S.n_phases - 1) {
-        arrive_release(S.counters + p);  // the barrier above ordered the block's writes
+        if (!(p == 0 && S.test_withhold == static_cast<int>(blockIdx.x) + 1))
+          arrive_release(S.counters + p);  // the barrier above ordered the block's writes
       } else if (ticket_acq_rel(S.counters + p) == static_cast<unsigned>(S.grid) - 1) {
         // every block has finished every phase: zero the counters for the next step
         for (int q = 0; q < S.n_phases; ++q) S.counters[q] = 0u;
@@ -1080,6 +1099,7 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
   config->prefetch_bytes = kPrefetchDefault;
   config->lane_inflight = 2;
   config->quiet_window = 1;
+  config->test_withhold = 0;
   config->timeline = nullptr;
   return CB_OK;
 }
@@ -1104,6 +1124,10 @@ int cb_decode_step(const void* table, const cb_decode_step_config* config, unsig
   CB_REQUIRE(config->lane_inflight == 1 || config->lane_inflight == 2, "decode step: lane_inflight must be 1 or 2");
   S.lane_inflight = config->lane_inflight;
   S.quiet_window = config->quiet_window != 0;
+  CB_REQUIRE(config->test_withhold >= 0 && config->test_withhold <= config->grid,
+             "decode step: test_withhold must be 0 or 1 + a block index");
+  CB_REQUIRE(config->test_withhold == 0 || config->n_phases > 1, "decode step: test_withhold needs two phases");
+  S.test_withhold = config->test_withhold;
   return launch_step(S, *config, static_cast<cudaStream_t>(stream));
 }
 

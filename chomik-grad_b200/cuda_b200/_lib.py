@@ -207,6 +207,7 @@ class GemmRowsArgs(ctypes.Structure):
 
 ROWS_X_PLAIN, ROWS_X_RMS, ROWS_X_SWIGLU = 0, 1, 2  # cb_gemm_rows x prologues
 STEP_X_VECTORS = 3 * 256  # x vectors (8 bf16-weight or 4 float32-weight columns) a cb_decode_step phase stages
+STEP_ROWS_PER_BLOCK = 128  # SwiGLU gate/up pairs one cb_decode_step block owns in a phase
 
 
 class StepPhase(ctypes.Structure):
@@ -218,6 +219,7 @@ class DecodeStepConfig(ctypes.Structure):
                 ("slot_bytes", c_longlong), ("x_bytes", c_longlong), ("norm_bytes", c_longlong),
                 ("smem", c_longlong),
                 ("prefetch_bytes", c_longlong), ("lane_inflight", c_int), ("quiet_window", c_int),
+                ("test_withhold", c_int),
                 ("timeline", c_void_p)]
 
 

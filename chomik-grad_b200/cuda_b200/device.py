@@ -163,6 +163,7 @@ class CudaB200Device(DeviceAdapter):
             raise RuntimeError(f"cuda-b200 kernels are built for sm_100a; device {self.index} "
                                f"is sm_{major}{minor}")
         _lib.load()
+        self.sm_count = int(torch.cuda.get_device_properties(self.index).multi_processor_count)
         self.inference_dtype = _bf16()
 
     # -- stream ------------------------------------------------------------

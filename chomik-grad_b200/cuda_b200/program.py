@@ -64,7 +64,7 @@ class CudaB200Program(CompiledProgram):
         self._capture_stream: Optional[int] = None
         self.use_graphs = compiler.use_graphs
         self.launches = 0  # kernels launched by the last eager run (graph replays re-run them)
-        self.step_mode = bool(getattr(compiler, "decode_step", False)) and self._fusable(plan)
+        self.step_mode = bool(getattr(compiler, "decode_step", False)) and self._fusable(plan, self.device.sm_count)
         # constants the plan was specialised on, once per leaf (a shared leaf,
         # e.g. the GQA broadcast's ones, is guarded by every layer that uses it)
         guards: Dict[int, tuple] = {}
@@ -74,21 +74,26 @@ class CudaB200Program(CompiledProgram):
         self._step_tables: Dict[tuple, Tuple[object, _lib.DecodeStepConfig]] = {}
 
     @staticmethod
-    def _fusable(plan: Plan) -> bool:
+    def _fusable(plan: Plan, sms: int) -> bool:
         """Whether the plan is a fused decode step cb_decode_step can run whole.
 
         Its consumer threads stage at most 3 x 256 vectors of x per phase
-        (6144 bf16-weight or 3072 float32-weight columns); a plan with a wider
-        GEMV (the Llama-3-8B down projection, 14336) runs kernel by kernel.
+        (6144 bf16-weight or 3072 float32-weight columns), and a block (one
+        per SM) owns at most 128 SwiGLU gate/up pairs; a plan with a wider
+        GEMV (the Llama-3-8B down projection, 14336 columns) runs kernel by
+        kernel.
         """
         names = {s.name for s in plan.steps}
         if not (plan.steps and names <= {"gemv", "decode_attention"} and "gemv" in names):
             return False
         for s in plan.steps:
-            if s.name == "gemv":
-                elems = 8 if s.args["weights"][0].dtype.itemsize == 2 else 4
-                if s.args["k"] > _lib.STEP_X_VECTORS * elems:
-                    return False
+            if s.name != "gemv":
+                continue
+            elems = 8 if s.args["weights"][0].dtype.itemsize == 2 else 4
+            if s.args["k"] > _lib.STEP_X_VECTORS * elems:
+                return False
+            if s.args["epilogue"] == _lib.EPI_SILU_MUL and -(-s.args["rows"][0] // sms) > _lib.STEP_ROWS_PER_BLOCK:
+                return False
         return True
 
     # ------------------------------------------------------------ build

@@ -590,6 +590,11 @@ typedef struct {
    * staged, issue no new ring copies, so the latency-critical loads of that
    * window do not queue behind bulk data; 0: keep streaming */
   int quiet_window;
+  /* tests only (0 = off): 1 + the index of a block that withholds its
+   * arrival after the first phase, so every block's wait for that phase
+   * runs out (after about 1 s) and the step stops with CB_FLAG_WAIT_PHASE;
+   * the caller then zeroes the counters, as after any wait that gave up */
+  int test_withhold;
   /* optional (NULL = off): grid * n_phases * 12 nanosecond stamps
    * (%globaltimer) per block and phase, for tuning the schedule: wait begins,
    * wait ends, x staged, phase done, producer issued the phase's last stage,

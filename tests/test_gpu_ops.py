@@ -153,3 +153,29 @@ def test_placement_matmul_is_a_bit_exact_column_copy(gpu, oracle, dtype):
         want = expr.numpy(compiler="cpu")
         assert got.dtype == want.dtype
         assert np.array_equal(got.astype(np.float32), want.astype(np.float32))
+
+
+def test_load_safetensors_round_trip(gpu, tmp_path):
+    """DeviceAdapter.load_safetensors (chomikgrad/lazy.py:140-145) through the reference's own
+    wrapper chomikgrad.llama.load_safetensors (:186-203): bf16 and float32 tensors come back
+    bit-exact as device arrays, with an optional cast."""
+    import ml_dtypes
+    import torch
+    from safetensors.torch import save_file
+    from chomikgrad.llama import load_safetensors
+
+    rng = np.random.default_rng(8)
+    bf16 = np.dtype(ml_dtypes.bfloat16)
+    tensors = {"a.weight": rng.normal(0, 0.02, (64, 32)).astype(np.float32).astype(bf16),
+               "b.bias": rng.normal(0, 1, (17,)).astype(np.float32)}
+    path = tmp_path / "tiny.safetensors"
+    save_file({"a.weight": torch.from_numpy(tensors["a.weight"].view(np.int16)).view(torch.bfloat16),
+               "b.bias": torch.from_numpy(tensors["b.bias"])}, str(path))
+    loaded = load_safetensors(path, gpu.device)
+    assert set(loaded) == set(tensors)
+    for name, want in tensors.items():
+        got = gpu.device.to_numpy(loaded[name]._node.native_values[gpu.device.name])
+        assert got.dtype == want.dtype and got.shape == want.shape
+        np.testing.assert_array_equal(got.view(np.uint8), np.ascontiguousarray(want).view(np.uint8))
+    cast = gpu.device.load_safetensors(path, dtype=np.float32)
+    np.testing.assert_array_equal(gpu.device.to_numpy(cast["a.weight"]), tensors["a.weight"].astype(np.float32))
