@@ -67,6 +67,14 @@ LLAMA3_8B_2L = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_siz
                            num_key_value_heads=8, max_position_embeddings=8192,
                            rope_theta=500_000.0)
 
+# The TinyLlama shape cut to four layers: every per-layer shape of TINYLLAMA,
+# for the 2048-token prefill fixture (the reference's cpu compiler keeps every
+# intermediate of a program alive, about 2.5 GB per layer at 2048 tokens).
+TINYLLAMA_4L = LlamaConfig(vocab_size=32000, hidden_size=2048, intermediate_size=5632,
+                           num_hidden_layers=4, num_attention_heads=32,
+                           num_key_value_heads=4, max_position_embeddings=4096,
+                           rope_theta=10_000.0)
+
 WORKLOADS: Dict[str, Workload] = {
     w.name: w
     for w in (
@@ -77,6 +85,7 @@ WORKLOADS: Dict[str, Workload] = {
         Workload("tinyllama-bf16-prefill-bs8", TINYLLAMA, "bfloat16", 8, 2048, 0),
         Workload("llama3-8b-bf16-bs16", LLAMA3_8B, "bfloat16", 16, 1024, 256),
         Workload("llama3-8b-2layer-bf16", LLAMA3_8B_2L, "bfloat16", 1, 32, 8),
+        Workload("tinyllama-4layer-prefill2048-bf16", TINYLLAMA_4L, "bfloat16", 1, 2048, 1),
     )
 }
 

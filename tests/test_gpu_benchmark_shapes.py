@@ -5,9 +5,11 @@
   steps of the reference's ``cpu`` compiler (``llama3_2layer_bf16``), through
   the batch-1 runtime and through the tensor-parallel runtime of the C5
   benchmark at TP = 1 (batched decode, the golden prompt in row 0);
-* C4 -- one 2048-token TinyLlama-shape prompt of the prefill workload
-  (``tinyllama_prefill2048``): logits and first token of the reference's
-  prefill, through the prefill program (tcgen05 GEMMs, flash attention);
+* C4 -- one 2048-token prompt, the prefill workload's length, with
+  TinyLlama's per-layer shapes on four layers (``tinyllama_prefill2048``;
+  the reference's cpu compiler keeps every intermediate, so all 22 layers do
+  not fit a 62 GB host): logits and first token of the reference's prefill,
+  through the prefill program (tcgen05 GEMMs, flash attention);
 * C3 -- the TinyLlama-shape batch of 32 sequences: the ``tinyllama_bf16``
   golden prompt in row 0 (128 greedy tokens against the reference), every
   other row against its own batch-1 run, logits of one step row by row.
@@ -78,7 +80,7 @@ def test_llama3_shape_through_the_tensor_parallel_runtime(llama3_weights):
 
 def test_tinyllama_prefill_of_2048_tokens(gpu):
     g = golden("tinyllama_prefill2048")
-    wl = WORKLOADS["tinyllama-bf16-prefill-bs8"]
+    wl = WORKLOADS["tinyllama-4layer-prefill2048-bf16"]
     rt = LlamaRuntime(wl.config, synthetic_weights(wl.config, dtype=wl.np_dtype), compiler="cuda-b200")
     prompt = [int(t) for t in g["prompt"]]
     assert len(prompt) == 2048
