@@ -251,28 +251,68 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const cb
 // the arithmetic is the single-sequence decode attention's (RoPE of q and
 // k at the bound position, write-mask blend of the cache rows, scores
 // s / divisor + mask, exp against the running max).
-template <int HD>
+// K/V element types of the batched kernel's shared-memory chunks: float32,
+// or bfloat16 (a bfloat16 cache stays bfloat16 in shared memory: half the
+// bytes; values convert to float32 where they are used).
+template <typename KT>
+struct KvTraits;
+template <>
+struct KvTraits<float> {
+  static constexpr int kPad = 4;  // K row padding (elements): conflict-free 16-byte score loads
+  static constexpr int kDtype = CB_F32;
+};
+template <>
+struct KvTraits<uint16_t> {
+  static constexpr int kPad = 8;  // keeps K rows 16-byte aligned for cp.async, loads conflict-free
+  static constexpr int kDtype = CB_BF16;
+};
+
+// Four / two consecutive K/V values of a shared-memory row as float32.
+__device__ __forceinline__ float4 smem_load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 smem_load4(const uint16_t* p) {
+  const uint2 w = *reinterpret_cast<const uint2*>(p);
+  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
+                     __uint_as_float(w.y & 0xffff0000u));
+}
+__device__ __forceinline__ float2 smem_load2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 smem_load2(const uint16_t* p) {
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+// Stores four values already representable in the row's type.
+__device__ __forceinline__ void smem_store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void smem_store4(uint16_t* p, float4 v) {
+  *reinterpret_cast<uint2*>(p) = make_uint2((__float_as_uint(v.x) >> 16) | (__float_as_uint(v.y) & 0xffff0000u),
+                                            (__float_as_uint(v.z) >> 16) | (__float_as_uint(v.w) & 0xffff0000u));
+}
+
+template <int HD, typename KT>
 struct ChunkSmem {
-  static constexpr int KS = HD + 4;  // padded K rows: conflict-free float4 score loads
+  static constexpr int KS = HD + KvTraits<KT>::kPad;  // padded K rows (elements)
+  static constexpr int kKBytes = kAttnSplit * KS * static_cast<int>(sizeof(KT));
+  static constexpr int kVBytes = kAttnSplit * HD * static_cast<int>(sizeof(KT));
   // one staging buffer: K rows [32][KS], V rows [32][HD], write mask [32], mask [32]
-  static constexpr int kBuf = kAttnSplit * KS + kAttnSplit * HD + 2 * kAttnSplit;
-  float *q_rot, *k_new, *v_new, *cs, *sn, *bufs;
+  static constexpr int kBufBytes = kKBytes + kVBytes + 2 * kAttnSplit * 4;
+  static_assert(kKBytes % 16 == 0 && kVBytes % 16 == 0, "16-byte aligned staging rows");
+  float *q_rot, *k_new, *v_new, *cs, *sn;
+  unsigned char* bufs;
   __device__ ChunkSmem(float* smem, int group) {
     q_rot = smem;                // [group][HD]
     k_new = q_rot + group * HD;  // [HD]
     v_new = k_new + HD;          // [HD]
     cs = v_new + HD;             // [HD / 2]
     sn = cs + HD / 2;            // [HD / 2]
-    bufs = sn + HD / 2;          // [2][kBuf]; a multiple of 4 floats from the base: 16-byte aligned rows
+    bufs = reinterpret_cast<unsigned char*>(sn + HD / 2);  // [2][kBufBytes]; 16-byte aligned (HD % 32 == 0)
   }
-  __device__ float* ks(int b) const { return bufs + b * kBuf; }
-  __device__ float* vs(int b) const { return ks(b) + kAttnSplit * KS; }
-  __device__ float* wm(int b) const { return vs(b) + kAttnSplit * HD; }
+  __device__ KT* ks(int b) const { return reinterpret_cast<KT*>(bufs + b * kBufBytes); }
+  __device__ KT* vs(int b) const { return reinterpret_cast<KT*>(bufs + b * kBufBytes + kKBytes); }
+  __device__ float* wm(int b) const { return reinterpret_cast<float*>(bufs + b * kBufBytes + kKBytes + kVBytes); }
   __device__ float* maskv(int b) const { return wm(b) + kAttnSplit; }
 };
 
-inline long long chunk_smem_floats(long long group, long long hd) {
-  return (group + 2) * hd + hd + 2 * (kAttnSplit * (hd + 4) + kAttnSplit * hd + 2 * kAttnSplit);
+inline long long chunk_smem_bytes(long long group, long long hd, int kv_dtype) {
+  const long long es = kv_dtype == CB_BF16 ? 2 : 4, pad = kv_dtype == CB_BF16 ? 8 : 4;
+  return ((group + 2) * hd + hd) * 4 + 2 * (kAttnSplit * (hd + pad) * es + kAttnSplit * hd * es + 2 * kAttnSplit * 4);
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -286,17 +326,22 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // Issue the copies of chunk `chunk`'s K/V rows into buffer `buf` (one commit
 // group per thread, possibly empty).
-template <int HD>
-__device__ __forceinline__ void stage_chunk(const cb_decode_attention_args& a, const ChunkSmem<HD>& s, int buf, int g,
-                                            long long chunk, int tid) {
+template <int HD, typename KT>
+__device__ __forceinline__ void stage_chunk(const cb_decode_attention_args& a, const ChunkSmem<HD, KT>& s, int buf,
+                                            int g, long long chunk, int tid) {
+  constexpr int kUnits = HD * static_cast<int>(sizeof(KT)) / 16;  // 16-byte pieces per row
+  constexpr int kEs = static_cast<int>(sizeof(KT));
   const long long lo = chunk * kAttnSplit;
   const int n = attn_rows(a, static_cast<int>(chunk));
-  const float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo) * HD;
-  const float* vc = a.v_cache + (static_cast<long long>(g) * a.context + lo) * HD;
-  for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
-    const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
-    cp_async16(s.ks(buf) + r * ChunkSmem<HD>::KS + d4, kc + 4 * e);
-    cp_async16(s.vs(buf) + r * HD + d4, vc + 4 * e);
+  const long long first = (static_cast<long long>(g) * a.context + lo) * HD;
+  const char* kc = static_cast<const char*>(kv_at(static_cast<const void*>(a.k_cache), first, KvTraits<KT>::kDtype));
+  const char* vc = static_cast<const char*>(kv_at(static_cast<const void*>(a.v_cache), first, KvTraits<KT>::kDtype));
+  char* kd = reinterpret_cast<char*>(s.ks(buf));
+  char* vd = reinterpret_cast<char*>(s.vs(buf));
+  for (int e = tid; e < n * kUnits; e += kAttnThreads) {
+    const int r = e / kUnits, u = e % kUnits;
+    cp_async16(kd + r * ChunkSmem<HD, KT>::KS * kEs + u * 16, kc + r * HD * kEs + u * 16);
+    cp_async16(vd + r * HD * kEs + u * 16, vc + r * HD * kEs + u * 16);
   }
   cp_async_commit();
 }
@@ -311,7 +356,7 @@ __device__ __forceinline__ void chunk_masks(const cb_decode_attention_args& a, l
   *mk = in ? load_as_f32(a.mask, r, a.mask_dtype) : 0.0f;
 }
 
-template <int HD, int HPW>  // HPW: query heads per warp (group <= 8 * HPW)
+template <int HD, int HPW, typename KT>  // HPW: query heads per warp (group <= 8 * HPW); KT: K/V element type
 __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kernel(const cb_decode_attention_args args,
                                                                                    long long qkv_stride,
                                                                                    int chunks_per_cta) {
@@ -323,23 +368,24 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int warps = kAttnThreads / 32;
   constexpr int half = HD / 2;
-  constexpr int KS = ChunkSmem<HD>::KS;
+  constexpr int KS = ChunkSmem<HD, KT>::KS;
+  constexpr int kDt = KvTraits<KT>::kDtype;
   constexpr int kPairs = (HD + 63) / 64;  // float2 output dims per lane
   const long long kv_rows = a.kv_heads * a.context * a.head_size;
   a.qkv += b * qkv_stride;
-  a.k_cache += b * kv_rows;
-  a.v_cache += b * kv_rows;
+  a.k_cache = kv_at(a.k_cache, b * kv_rows, kDt);
+  a.v_cache = kv_at(a.v_cache, b * kv_rows, kDt);
   a.out += b * a.heads * a.head_size;
   a.scratch += b * static_cast<long long>(gridDim.x) * a.heads * (a.head_size + 2);
   a.counters += b * a.kv_heads;
   const int group = static_cast<int>(a.heads / a.kv_heads);
-  ChunkSmem<HD> s(smem, group);
+  ChunkSmem<HD, KT> s(smem, group);
   const long long splits = (a.context + kAttnSplit - 1) / kAttnSplit;
   const long long c0 = static_cast<long long>(blockIdx.x) * chunks_per_cta;
   const long long c1 = c0 + chunks_per_cta < splits ? c0 + chunks_per_cta : splits;
 
   // the first chunk's copies and mask values overlap the RoPE row and q/k/v loads
-  stage_chunk<HD>(a, s, 0, g, c0, tid);
+  stage_chunk<HD, KT>(a, s, 0, g, c0, tid);
   float wm_next, mk_next;
   chunk_masks(a, c0, tid, &wm_next, &mk_next);
   long long pos = load_index(a.position, 0, a.position_dtype);
@@ -385,7 +431,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
     const int buf = static_cast<int>((c - c0) & 1);
     const bool more = c + 1 < c1;
     if (more) {
-      stage_chunk<HD>(a, s, buf ^ 1, g, c + 1, tid);
+      stage_chunk<HD, KT>(a, s, buf ^ 1, g, c + 1, tid);
       chunk_masks(a, c + 1, tid, &wm_next, &mk_next);  // stored after this chunk's scores
       cp_async_wait<1>();  // this thread's copies of chunk c have landed
     } else {
@@ -396,17 +442,18 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
     // rows with wm != 0 get the blend, in shared memory and in the cache
     const long long lo_pos = c * kAttnSplit;
     const int n = attn_rows(a, static_cast<int>(c));
-    float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
-    float* vc = a.v_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
-    float* ks = s.ks(buf);
-    float* vs = s.vs(buf);
+    const long long first = (static_cast<long long>(g) * a.context + lo_pos) * HD;
+    void* kc = kv_at(a.k_cache, first, kDt);
+    void* vc = kv_at(a.v_cache, first, kDt);
+    KT* ks = s.ks(buf);
+    KT* vs = s.vs(buf);
     for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
       const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
       const float wm = s.wm(buf)[r];
       if (wm == 0.0f) continue;
       const float keep = round_to(__fsub_rn(1.0f, wm), a.one_minus_dtype);
-      float4 kv = *reinterpret_cast<float4*>(ks + r * KS + d4);
-      float4 vv = *reinterpret_cast<float4*>(vs + r * HD + d4);
+      float4 kv = smem_load4(ks + r * KS + d4);
+      float4 vv = smem_load4(vs + r * HD + d4);
       float* kf = &kv.x;
       float* vf = &vv.x;
 #pragma unroll
@@ -414,10 +461,10 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
         kf[i] = __fadd_rn(__fmul_rn(kf[i], keep), __fmul_rn(s.k_new[d4 + i], wm));
         vf[i] = __fadd_rn(__fmul_rn(vf[i], keep), __fmul_rn(s.v_new[d4 + i], wm));
       }
-      reinterpret_cast<float4*>(kc)[e] = kv;
-      reinterpret_cast<float4*>(vc)[e] = vv;
-      *reinterpret_cast<float4*>(ks + r * KS + d4) = kv;
-      *reinterpret_cast<float4*>(vs + r * HD + d4) = vv;
+      kv = kv_store4(kc, e, kDt, kv);  // rounded for a bfloat16 cache, and attended as stored
+      vv = kv_store4(vc, e, kDt, vv);
+      smem_store4(ks + r * KS + d4, kv);
+      smem_store4(vs + r * HD + d4, vv);
     }
     attn_sync();
 
@@ -430,15 +477,32 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
       float x = -INFINITY;
       if (lane < n) {
         const float4* q = reinterpret_cast<const float4*>(s.q_rot + h * HD);
-        const float4* kr = reinterpret_cast<const float4*>(ks + lane * KS);
         float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+        if constexpr (sizeof(KT) == 4) {
+          const float4* kr = reinterpret_cast<const float4*>(ks + lane * KS);
 #pragma unroll
-        for (int d = 0; d < HD / 4; ++d) {
-          const float4 qa = q[d], ka = kr[d];
-          s0 = fmaf(qa.x, ka.x, s0);
-          s1 = fmaf(qa.y, ka.y, s1);
-          s2 = fmaf(qa.z, ka.z, s2);
-          s3 = fmaf(qa.w, ka.w, s3);
+          for (int d = 0; d < HD / 4; ++d) {
+            const float4 qa = q[d], ka = kr[d];
+            s0 = fmaf(qa.x, ka.x, s0);
+            s1 = fmaf(qa.y, ka.y, s1);
+            s2 = fmaf(qa.z, ka.z, s2);
+            s3 = fmaf(qa.w, ka.w, s3);
+          }
+        } else {  // eight bfloat16 K values per 16-byte load, in the same accumulation order
+          const uint4* kr = reinterpret_cast<const uint4*>(ks + lane * KS);
+#pragma unroll
+          for (int d = 0; d < HD / 8; ++d) {
+            const uint4 w = kr[d];
+            const float4 qa = q[2 * d], qb = q[2 * d + 1];
+            s0 = fmaf(qa.x, __uint_as_float(w.x << 16), s0);
+            s1 = fmaf(qa.y, __uint_as_float(w.x & 0xffff0000u), s1);
+            s2 = fmaf(qa.z, __uint_as_float(w.y << 16), s2);
+            s3 = fmaf(qa.w, __uint_as_float(w.y & 0xffff0000u), s3);
+            s0 = fmaf(qb.x, __uint_as_float(w.z << 16), s0);
+            s1 = fmaf(qb.y, __uint_as_float(w.z & 0xffff0000u), s1);
+            s2 = fmaf(qb.z, __uint_as_float(w.w << 16), s2);
+            s3 = fmaf(qb.w, __uint_as_float(w.w & 0xffff0000u), s3);
+          }
         }
         x = __fadd_rn(__fdiv_rn((s0 + s1) + (s2 + s3), a.divisor), s.maskv(buf)[lane]);
       }
@@ -456,11 +520,11 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
           const float p0 = __shfl_sync(0xffffffffu, p, j);
           const float p1 = __shfl_sync(0xffffffffu, p, j + 1);
           if (mine) {
-            const float2 v0 = *reinterpret_cast<const float2*>(vs + j * HD + d);
+            const float2 v0 = smem_load2(vs + j * HD + d);
             a0.x = fmaf(p0, v0.x, a0.x);
             a0.y = fmaf(p0, v0.y, a0.y);
             if (j + 1 < n) {
-              const float2 v1 = *reinterpret_cast<const float2*>(vs + (j + 1) * HD + d);
+              const float2 v1 = smem_load2(vs + (j + 1) * HD + d);
               a1.x = fmaf(p1, v1.x, a1.x);
               a1.y = fmaf(p1, v1.y, a1.y);
             }
@@ -559,7 +623,8 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   CB_REQUIRE(splits < (1LL << 31) && a->kv_heads < 65536, "decode attention: grid too large");
   const long long group = a->heads / a->kv_heads;
   CB_REQUIRE(group <= 32, "decode attention: at most 32 query heads per KV head (got %lld)", group);
-  const size_t smem = static_cast<size_t>(chunk_smem_floats(group, a->head_size)) * sizeof(float);
+  CB_REQUIRE(a->kv_dtype == CB_F32 || a->kv_dtype == CB_BF16, "decode attention: caches must be float32 or bfloat16");
+  const size_t smem = static_cast<size_t>(chunk_smem_bytes(group, a->head_size, a->kv_dtype));
   CB_REQUIRE(smem <= 200 * 1024, "decode attention: too many query heads per KV head");
   // about one wave of resident CTAs (4 per SM): each CTA takes a range of
   // consecutive chunks of its (sequence, KV head)
@@ -575,7 +640,8 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   cudaError_t e = cudaSuccess;
 #define CB_BATCHED_CASE(HD, HPW)                                                                          \
   {                                                                                                       \
-    auto kernel = decode_attention_batched_kernel<HD, HPW>;                                               \
+    auto kernel = a->kv_dtype == CB_BF16 ? decode_attention_batched_kernel<HD, HPW, uint16_t>            \
+                                         : decode_attention_batched_kernel<HD, HPW, float>;               \
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
     if (e == cudaSuccess) kernel<<<grid, kAttnThreads, smem, s>>>(*a, qkv_stride, per_cta);               \
   }
@@ -684,6 +750,7 @@ int cb_decode_attention(const cb_decode_attention_args* a, cb_stream_t stream) {
   CB_REQUIRE(a->context > 0, "decode attention: empty context");
   CB_REQUIRE(a->mask != nullptr && a->write_mask != nullptr && a->position != nullptr,
              "decode attention: mask, write mask and position are required");
+  CB_REQUIRE(a->kv_dtype == CB_F32 || a->kv_dtype == CB_BF16, "decode attention: caches must be float32 or bfloat16");
   CB_REQUIRE(a->split == 0 || a->split == kAttnSplit, "decode attention: split must be %d", kAttnSplit);
   const long long splits = (a->context + kAttnSplit - 1) / kAttnSplit;
   CB_REQUIRE(splits < 65536 && a->kv_heads < 65536, "decode attention: grid too large");

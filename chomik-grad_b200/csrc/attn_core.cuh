@@ -9,7 +9,8 @@
 //    so the megakernel runs it before waiting for the QKV phase;
 //  * attention_finish: rope the new q/k rows, apply the write-mask blend
 //    cache*(1-wm) + new*wm (float32, as llama.py:511-512 computes it) to the
-//    rows with wm != 0 and write them back, compute every (query head,
+//    rows with wm != 0 and write them back (rounded to bfloat16 for a
+//    bfloat16 cache), compute every (query head,
 //    position) score in one pass (x = q.k / divisor + mask), and write the
 //    split's partial softmax state.  With `merge`, the last item of each KV
 //    group then merges the splits in split order (deterministic) and resets
@@ -50,6 +51,36 @@ struct AttnSmem {
   }
 };
 
+// KV cache element access for float32 or bfloat16 caches: `base` offset by
+// `elems` elements, and groups of four consecutive values (16 or 8 bytes).
+__device__ __forceinline__ const void* kv_at(const void* base, long long elems, int dtype) {
+  return static_cast<const char*>(base) + elems * (dtype == CB_BF16 ? 2 : 4);
+}
+__device__ __forceinline__ void* kv_at(void* base, long long elems, int dtype) {
+  return static_cast<char*>(base) + elems * (dtype == CB_BF16 ? 2 : 4);
+}
+__device__ __forceinline__ float4 kv_load4(const void* base, long long i4, int dtype) {
+  if (dtype == CB_BF16) {
+    const uint2 w = __ldcg(reinterpret_cast<const uint2*>(base) + i4);
+    return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
+                       __uint_as_float(w.y & 0xffff0000u));
+  }
+  return __ldcg(reinterpret_cast<const float4*>(base) + i4);
+}
+// Stores four values (rounded to bfloat16 for a bfloat16 cache) and returns
+// them as stored.
+__device__ __forceinline__ float4 kv_store4(void* base, long long i4, int dtype, float4 v) {
+  if (dtype == CB_BF16) {
+    const uint32_t b0 = __bfloat16_as_ushort(__float2bfloat16_rn(v.x)), b1 = __bfloat16_as_ushort(__float2bfloat16_rn(v.y));
+    const uint32_t b2 = __bfloat16_as_ushort(__float2bfloat16_rn(v.z)), b3 = __bfloat16_as_ushort(__float2bfloat16_rn(v.w));
+    reinterpret_cast<uint2*>(base)[i4] = make_uint2(b0 | (b1 << 16), b2 | (b3 << 16));
+    return make_float4(__uint_as_float(b0 << 16), __uint_as_float(b1 << 16), __uint_as_float(b2 << 16),
+                       __uint_as_float(b3 << 16));
+  }
+  reinterpret_cast<float4*>(base)[i4] = v;
+  return v;
+}
+
 __device__ __forceinline__ int attn_rows(const cb_decode_attention_args& a, int split) {
   const long long lo = static_cast<long long>(split) * kAttnSplit;
   return static_cast<int>(a.context - lo < kAttnSplit ? a.context - lo : kAttnSplit);
@@ -63,12 +94,13 @@ __device__ void attention_stage_cache(const cb_decode_attention_args& a, int g, 
   constexpr int half = HD / 2;
   const long long lo_pos = static_cast<long long>(split) * kAttnSplit;
   const int n = attn_rows(a, split);
-  const float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
-  const float* vc = a.v_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
+  const long long first = (static_cast<long long>(g) * a.context + lo_pos) * HD;
+  const void* kc = kv_at(static_cast<const void*>(a.k_cache), first, a.kv_dtype);
+  const void* vc = kv_at(static_cast<const void*>(a.v_cache), first, a.kv_dtype);
   for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
     const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
-    const float4 kv = __ldcg(reinterpret_cast<const float4*>(kc) + e);
-    const float4 vv = __ldcg(reinterpret_cast<const float4*>(vc) + e);
+    const float4 kv = kv_load4(kc, e, a.kv_dtype);
+    const float4 vv = kv_load4(vc, e, a.kv_dtype);
     *reinterpret_cast<float4*>(s.ks + r * AttnSmem<HD>::KS + d4) = kv;
     *reinterpret_cast<float4*>(s.vs + r * HD + d4) = vv;
   }
@@ -203,8 +235,9 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
   // rows with wm != 0 get the blend, in shared memory and in the cache
   const long long lo_pos = static_cast<long long>(split) * kAttnSplit;
   const int n = attn_rows(a, split);
-  float* kc = a.k_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
-  float* vc = a.v_cache + (static_cast<long long>(g) * a.context + lo_pos) * HD;
+  const long long first = (static_cast<long long>(g) * a.context + lo_pos) * HD;
+  void* kc = kv_at(a.k_cache, first, a.kv_dtype);
+  void* vc = kv_at(a.v_cache, first, a.kv_dtype);
   for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
     const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
     const float wm = s.wm[r];
@@ -219,8 +252,8 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
       kf[i] = __fadd_rn(__fmul_rn(kf[i], keep), __fmul_rn(s.k_new[d4 + i], wm));
       vf[i] = __fadd_rn(__fmul_rn(vf[i], keep), __fmul_rn(s.v_new[d4 + i], wm));
     }
-    reinterpret_cast<float4*>(kc)[e] = kv;
-    reinterpret_cast<float4*>(vc)[e] = vv;
+    kv = kv_store4(kc, e, a.kv_dtype, kv);  // attended as stored
+    vv = kv_store4(vc, e, a.kv_dtype, vv);
     *reinterpret_cast<float4*>(s.ks + r * KS + d4) = kv;
     *reinterpret_cast<float4*>(s.vs + r * HD + d4) = vv;
   }

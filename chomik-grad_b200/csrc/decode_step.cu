@@ -1004,6 +1004,8 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
       CB_REQUIRE(t.context > 0, "decode step phase %d: empty context", i);
       CB_REQUIRE(t.mask && t.write_mask && t.position && t.scratch && t.counters && t.out,
                  "decode step phase %d: attention buffers missing", i);
+      CB_REQUIRE(t.kv_dtype == CB_F32 || t.kv_dtype == CB_BF16,
+                 "decode step phase %d: caches must be float32 or bfloat16", i);
       CB_REQUIRE(t.split == 0 || t.split == kAttnSplit, "decode step phase %d: split must be %d", i, kAttnSplit);
       const long long splits = (t.context + kAttnSplit - 1) / kAttnSplit;
       const long long bytes = attn_smem_floats(t.heads / t.kv_heads, t.head_size) * 4;

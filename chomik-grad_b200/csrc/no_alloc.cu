@@ -107,6 +107,8 @@ int cb_decode_attention_noalloc(const cb_decode_attention_args* args, cb_stream_
   CB_REQUIRE(a.heads > 0 && a.kv_heads > 0 && a.heads % a.kv_heads == 0,
              "decode attention (no-alloc): bad head grouping");
   CB_REQUIRE(a.context > 0, "decode attention (no-alloc): empty context");
+  CB_REQUIRE(a.kv_dtype == CB_F32 || a.kv_dtype == CB_BF16,
+             "decode attention (no-alloc): caches must be float32 or bfloat16");
   CB_REQUIRE(a.mask != nullptr && a.write_mask != nullptr && a.position != nullptr,
              "decode attention (no-alloc): mask, write mask and position are required");
   CB_REQUIRE(a.split == 0 || a.split == kAttnSplit, "decode attention (no-alloc): split must be %d", kAttnSplit);

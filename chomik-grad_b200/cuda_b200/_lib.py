@@ -158,7 +158,7 @@ class DecodeAttentionArgs(ctypes.Structure):
         ("divisor", c_float),
         ("out", c_void_p), ("scratch", c_void_p), ("counters", c_void_p), ("error_flag", c_void_p),
         ("prefetch_ptr", c_void_p * 3), ("prefetch_bytes", c_longlong * 3),
-        ("split", c_int), ("pdl", c_int),
+        ("split", c_int), ("pdl", c_int), ("kv_dtype", c_int),
     ]
 
 

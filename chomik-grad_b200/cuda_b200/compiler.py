@@ -34,7 +34,7 @@ class CudaB200Compiler(Compiler):
                  pdl: bool = True, fuse_decode: bool = True, alias_caches: bool = True,
                  max_positions: int = 8192, gemv_grid: Optional[int] = None,
                  decode_step: Optional[bool] = None, gemm_min_rows: Optional[int] = None,
-                 attn_min_rows: Optional[int] = None) -> None:
+                 attn_min_rows: Optional[int] = None, kv_cache_dtype: Optional[str] = None) -> None:
         import os
 
         self.device = CudaB200Device(device_index)
@@ -51,6 +51,15 @@ class CudaB200Compiler(Compiler):
         if attn_min_rows is None:  # query rows from which attention runs on cb_sdpa_tc
             attn_min_rows = int(os.environ.get("CUDA_B200_ATTN_MIN_ROWS", "64"))
         self.attn_min_rows = attn_min_rows
+        # KV caches produced by prefill and updated by decode: float32 (the
+        # runtime dtype of the reference's caches, the default) or bfloat16
+        # (CUDA_B200_KV_DTYPE=bfloat16): half the attention's bytes; the rows
+        # a step writes are rounded to bfloat16.
+        if kv_cache_dtype is None:
+            kv_cache_dtype = os.environ.get("CUDA_B200_KV_DTYPE", "float32")
+        if kv_cache_dtype not in ("float32", "bfloat16"):
+            raise ValueError(f"kv_cache_dtype must be float32 or bfloat16, not {kv_cache_dtype!r}")
+        self.kv_cache_dtype = kv_cache_dtype
         # cb_decode_step_prepare flags: attention splits are merged in the
         # attention phase (measured faster on TinyLlama); set
         # CUDA_B200_STEP_MERGE=stage to merge them in the O projection's x staging
@@ -92,7 +101,8 @@ class CudaB200Compiler(Compiler):
         return Planner(outputs, dynamic_inputs, backend=self.device.name,
                        leaf_dtype=self._leaf_dtype, max_positions=self.max_positions,
                        fuse_decode=self.fuse_decode, alias_caches=self.alias_caches,
-                       table_cache=self._tables, gemm_min_rows=self.gemm_min_rows).build()
+                       table_cache=self._tables, gemm_min_rows=self.gemm_min_rows,
+                       kv_bf16=self.kv_cache_dtype == "bfloat16").build()
 
     def compile(self, outputs: Sequence[object],
                 dynamic_inputs: Sequence[object] = ()) -> CudaB200Program:

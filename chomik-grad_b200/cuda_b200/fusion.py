@@ -182,7 +182,9 @@ class DecodeFusion:
             return None
         if cache.op is not None or tuple(cache.shape) != cache_shape:
             return None
-        if self.p.rdt(cache) != F32 or any(self.p.rdt(n) != F32 for n in (left, right, node)):
+        kv = self.p.kv_dtypes()
+        if self.p.rdt(cache) not in kv or self.p.rdt(left) not in kv or any(
+                self.p.rdt(n) != F32 for n in (right, node)):
             return None
         ctx = cache_shape[2]
         if tuple(wm.shape) != (1, 1, ctx, 1) or self.p.rdt(wm).name not in ("float32", "bfloat16", "float16"):
@@ -292,7 +294,7 @@ class DecodeFusion:
         if aliasable:
             view.buf.bind = "pointer"
             return view
-        out = p.tmp(cache.shape, F32)
+        out = p.tmp(cache.shape, view.dtype)
         p.add_step("copy", out, f"copy({p._name(view)})", src=view)
         return out
 

@@ -300,7 +300,8 @@ class Planner:
     def __init__(self, outputs: Sequence[object], dynamic_inputs: Sequence[object], *,
                  backend: str, leaf_dtype, max_positions: int = 8192,
                  fuse_decode: bool = True, alias_caches: bool = True,
-                 table_cache: Optional[dict] = None, gemm_min_rows: Optional[int] = None) -> None:
+                 table_cache: Optional[dict] = None, gemm_min_rows: Optional[int] = None,
+                 kv_bf16: bool = False) -> None:
         self.outputs = tuple(outputs)
         self.dynamic = set(dynamic_inputs)
         self.backend = backend
@@ -310,6 +311,9 @@ class Planner:
         self.alias_caches = alias_caches
         self.table_cache = table_cache if table_cache is not None else {}
         self.gemm_min_rows = gemm_min_rows  # None: no tensor-core GEMM epilogue fusion
+        # bfloat16 KV caches: the prefill's cache placement stores bfloat16, and the
+        # fused decode attentions accept bfloat16 caches (rows they write are rounded)
+        self.kv_bf16 = kv_bf16
         self.plan = Plan()
         self._rdt: Dict[object, np.dtype] = {}
         self._val: Dict[object, View] = {}
@@ -657,12 +661,13 @@ class Planner:
             if not is_ew(keep, "sub") or keep.inputs[1] is not wm or self._const(keep.inputs[0]) != 1.0:
                 continue
             if (cache.op is not None or cache not in self.dynamic or cache in self.output_set
-                    or len(cache.shape) != 4 or self.rdt(cache) != F32):
+                    or len(cache.shape) != 4 or self.rdt(cache) not in self.kv_dtypes()):
                 continue
             b, h, ctx, hd = cache.shape
             if tuple(row.shape) != (b, h, 1, hd) or tuple(wm.shape) != (1, 1, ctx, 1):
                 continue
-            if self.rdt(wm).name not in FLOATS or any(self.rdt(n) != F32 for n in (left, right, node, row)):
+            if (self.rdt(wm).name not in FLOATS or self.rdt(left) not in self.kv_dtypes()
+                    or any(self.rdt(n) != F32 for n in (right, node, row))):
                 continue
             uses = self.consumers
             if not (len(uses.get(cache, ())) == 1 and uses.get(left) == [node] and uses.get(right) == [node]
@@ -670,6 +675,10 @@ class Planner:
                 continue
             self.claimed.update((left, right, keep))
             self.units[node] = self._kv_write_unit(node, cache, row, wm, keep)
+
+    def kv_dtypes(self) -> Tuple[np.dtype, ...]:
+        """Cache dtypes the decode blends accept: float32, and bfloat16 in bfloat16-KV mode."""
+        return (F32, bf16()) if self.kv_bf16 else (F32,)
 
     def _kv_write_unit(self, node, cache, row, wm, keep):
         def emit() -> None:
@@ -1060,6 +1069,10 @@ class Planner:
             replace[id(st)] = fused
             removed.update(id(x) for x in (rq, rk, kwk, kwv))
         plan.steps = [replace.get(id(st), st) for st in steps if id(st) not in removed]
+        for st in plan.steps:
+            if st.name == "kv_write" and st.args["cache"].dtype != F32:
+                raise PlanError("a bfloat16 KV cache is updated only by the fused decode attention kernels "
+                                "(bfloat16 weights on the tensor-core row GEMM); this graph needs float32 caches")
 
     PURE_STEPS = frozenset(("elementwise", "matmul", "reduce", "copy", "rms_norm", "rope", "sdpa", "place"))
 
@@ -1318,7 +1331,8 @@ class Planner:
         cols = self._placement_columns(node)
         if cols is not None:
             a = self.value(node.inputs[0])
-            out = self.tmp(node.shape, self.rdt(node))
+            dt = self.rdt(node)
+            out = self.tmp(node.shape, bf16() if self.kv_bf16 and dt == F32 else dt)
             self.plan.lowered["place"] = self.plan.lowered.get("place", 0) + 1
             table = self.aux(cols)
             self.add_step("place", out, f"place({self._name(a)}, cols={table.name})", src=a, cols=table)

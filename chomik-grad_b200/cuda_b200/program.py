@@ -879,6 +879,9 @@ class CudaB200Program(CompiledProgram):
         a.cos_table, a.sin_table = self._ptr[g["cos"]], self._ptr[g["sin"]]
         a.n_positions = g["n_positions"]
         a.k_cache, a.v_cache = self.ptr(g["k_cache"]), self.ptr(g["v_cache"])
+        a.kv_dtype = _lib.dtype_code(g["k_cache"].dtype)
+        if g["v_cache"].dtype != g["k_cache"].dtype:
+            raise TypeError("K and V caches of one attention step must have one dtype")
         a.write_mask = self.ptr(g["write_mask"])
         a.write_mask_dtype = _lib.dtype_code(g["write_mask"].dtype)
         a.one_minus_dtype = _lib.dtype_code(g["one_minus"])

@@ -368,8 +368,8 @@ typedef struct {
   const float* cos_table; /* [n_positions][hd/2] */
   const float* sin_table;
   long long n_positions;
-  float* k_cache; /* (kv_heads, context, hd) float32, updated in place */
-  float* v_cache;
+  void* k_cache; /* (kv_heads, context, hd) of kv_dtype, updated in place */
+  void* v_cache;
   const void* write_mask; /* context values */
   int write_mask_dtype;
   int one_minus_dtype; /* dtype of (1 - write_mask) in the graph */
@@ -384,6 +384,10 @@ typedef struct {
   long long prefetch_bytes[3];
   int split; /* positions per CTA (0 = default) */
   int pdl;
+  /* CB_F32 (0) or CB_BF16: the caches' element type.  A bfloat16 cache is
+   * read as float32 values; the rows the write mask rewrites are blended in
+   * float32 and stored rounded to bfloat16 (and attended as stored). */
+  int kv_dtype;
 } cb_decode_attention_args;
 CB_API int cb_decode_attention(const cb_decode_attention_args* args, cb_stream_t stream);
 /* Scratch floats cb_decode_attention needs for these args. */

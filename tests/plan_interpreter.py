@@ -393,6 +393,9 @@ class PlanInterpreter:
         q, k = _rotate(q, cos[None], sin[None]), _rotate(k, cos[None], sin[None])
         k_cache = _blend(k_cache, k, wm, g["one_minus"])
         v_cache = _blend(v_cache, v, wm, g["one_minus"])
+        if g["k_cache"].dtype != F32:  # a bfloat16 cache: the written rows are stored, and attended, rounded
+            k_cache = k_cache.astype(g["k_cache"].dtype).astype(F32)
+            v_cache = v_cache.astype(g["v_cache"].dtype).astype(F32)
         out = _softmax_attention(q, k_cache, v_cache, mask.reshape(1, 1, 1, -1).astype(np.float64), g["divisor"])
         return out, k_cache, v_cache
 

@@ -100,10 +100,10 @@ def test_generic_steps_match_the_oracle(dtype):
 
 
 # ------------------------------------------------------------------ bs-1 decode
-def _decode_graph(wl, weights, ctx, position, seed):
+def _decode_graph(wl, weights, ctx, position, seed, cache_dtype=np.float32):
     cfg, dt = wl.config, wl.np_dtype
     shape = (1, cfg.num_key_value_heads, ctx, cfg.head_size)
-    caches = [Tensor.from_native(c, backend="cpu", shape=shape, dtype=dt)
+    caches = [Tensor.from_native(c.astype(cache_dtype), backend="cpu", shape=shape, dtype=dt)
               for c in _caches(shape, 2 * cfg.num_hidden_layers, seed)]
     am, wm = decode_masks(position, ctx, dt)
     inputs = [Tensor(np.array([[11]], np.int32), copy=False),
@@ -129,6 +129,38 @@ def test_fused_decode_step_plan_matches_the_oracle(name):
     assert it.argmax(0) == int(np.argmax(want[0]))
     for i, (a, b) in enumerate(zip(got[1:], want[1:])):
         np.testing.assert_allclose(a, b, rtol=0, atol=1e-4, err_msg=f"cache {i}")
+
+
+def test_bf16_kv_decode_step_plan_matches_the_oracle():
+    """bfloat16-KV mode: the fused decode step reads bfloat16 caches and stores the row it writes
+    rounded; against the oracle's graph on the same bfloat16 caches (whose blend keeps the new
+    row in float32): logits within the bf16 bar, same argmax, caches within one bf16 rounding."""
+    wl, weights = _weights("tiny-bf16")
+    outs, dynamic = _decode_graph(wl, weights, ctx=40, position=17, seed=1, cache_dtype=BF16)
+    want = _oracle(outs)
+    plan, it, got = _interpret(outs, dynamic, kv_bf16=True)
+    kinds = Counter(s.name for s in plan.steps)
+    assert kinds == {"gemv": 4 * wl.config.num_hidden_layers + 1, "decode_attention": wl.config.num_hidden_layers}
+    _close(got[0], want[0], BF16, "logits")
+    assert it.argmax(0) == int(np.argmax(want[0]))
+    for i, (a, b) in enumerate(zip(got[1:], want[1:])):
+        assert a.dtype == BF16, f"cache {i} stays bfloat16"
+        b = np.asarray(b, np.float32)
+        # one bfloat16 rounding of values whose float32 sums differ in the last bits: within one bf16 ulp
+        np.testing.assert_allclose(np.asarray(a, np.float32), b, rtol=2 ** -7, atol=1e-4, err_msg=f"cache {i}")
+
+
+def test_bf16_kv_prefill_places_bfloat16_caches():
+    wl, weights = _weights("tiny-bf16")
+    outs, dynamic = _prefill(wl, weights, seq=16, ctx=24)
+    want = _oracle(outs)
+    plan, _, got = _interpret(outs, dynamic, kv_bf16=True)
+    assert any(st.name == "place" and st.out.dtype == BF16 for st in plan.steps)
+    _close(got[0], want[0], BF16, "logits")
+    for i, (a, b) in enumerate(zip(got[1:], want[1:])):
+        assert a.dtype == BF16
+        np.testing.assert_allclose(np.asarray(a, np.float32), np.asarray(b, np.float32), rtol=2 ** -7, atol=1e-4,
+                                   err_msg=f"cache {i}")
 
 
 # ------------------------------------------------------------------ prefill
@@ -158,9 +190,9 @@ def test_prefill_plan_matches_the_oracle(name, gemm_min_rows):
 
 
 # ------------------------------------------------------------------ batched decode
-def _batched_graph(config, weights, dt, batch, ctx, position, seed):
+def _batched_graph(config, weights, dt, batch, ctx, position, seed, cache_dtype=np.float32):
     shape = (batch, config.num_key_value_heads, ctx, config.head_size)
-    caches = [Tensor.from_native(c, backend="cpu", shape=shape, dtype=dt)
+    caches = [Tensor.from_native(c.astype(cache_dtype), backend="cpu", shape=shape, dtype=dt)
               for c in _caches(shape, 2 * config.num_hidden_layers, seed)]
     am, wm = decode_masks(position, ctx, dt)
     rng = np.random.default_rng(seed)
@@ -191,6 +223,21 @@ def test_batched_decode_plan_matches_the_oracle(name):
     assert (np.argmax(got[0], -1) == np.argmax(want[0], -1)).all()
     for i, (a, b) in enumerate(zip(got[1:], want[1:])):
         np.testing.assert_allclose(a, b, rtol=0, atol=1e-4, err_msg=f"cache {i}")
+
+
+def test_bf16_kv_batched_decode_plan_matches_the_oracle():
+    wl, weights = _weights("tiny-bf16")
+    outs, dynamic = _batched_graph(wl.config, weights, wl.np_dtype, batch=3, ctx=40, position=21, seed=2,
+                                   cache_dtype=BF16)
+    want = _oracle(outs)
+    plan, _, got = _interpret(outs, dynamic, gemm_min_rows=64, kv_bf16=True)
+    assert Counter(s.name for s in plan.steps)["decode_attention_batched"] == wl.config.num_hidden_layers
+    _close(got[0], want[0], BF16, "logits")
+    assert (np.argmax(got[0], -1) == np.argmax(want[0], -1)).all()
+    for i, (a, b) in enumerate(zip(got[1:], want[1:])):
+        assert a.dtype == BF16
+        np.testing.assert_allclose(np.asarray(a, np.float32), np.asarray(b, np.float32), rtol=2 ** -7, atol=1e-4,
+                                   err_msg=f"cache {i}")
 
 
 # ------------------------------------------------------------------ tensor parallel
