@@ -5,7 +5,8 @@
 
 Workload (default): TinyLlama-1.1B shape, bf16 weights, random init, batch 1,
 128-token prompt then greedy decode with a 384-row KV cache (the reference's
-``context = prompt + 256`` rule).  A *step* is one decode step (one token).
+``context = prompt + 256`` rule), the cache held in bfloat16 (``--kv-cache
+float32`` keeps the reference's float32 cache layout).  A *step* is one decode step (one token).
 With N GPUs (torchrun, one process per GPU) every rank decodes its own
 sequence: independent replicas, weak scaling, no collective on the data path.
 
@@ -61,8 +62,8 @@ METRIC = ("decode tokens/sec (bs=1; bs=32 in the bs32 object; Llama-3-8B bs16 te
           "llama3_8b_tp) and % of HBM roofline")
 # DRAM bytes of one gate/up GEMV launch from an ncu capture, per workload
 GATEUP_TRAFFIC = {"tinyllama-bf16-bs1": 56_449_792 + 45_312}
-# DRAM bytes of one cb_decode_step launch from an ncu capture, per workload
-STEP_TRAFFIC = {"tinyllama-bf16-bs1": 2_091_113_000 + 7_491_584}
+# DRAM bytes of one cb_decode_step launch from an ncu capture, per (workload, KV-cache dtype)
+STEP_TRAFFIC = {("tinyllama-bf16-bs1", "float32"): 2_091_113_000 + 7_491_584}
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
@@ -176,6 +177,15 @@ def weight_bytes(config, itemsize: int) -> int:
     total = sum(int(np.prod(s)) for n, s in required_weight_shapes(config).items()
                 if n != "model.embed_tokens.weight")
     return total * itemsize
+
+
+def kv_name() -> str:
+    """The KV-cache storage the b200 compiler was created with (the CUDA_B200_KV_DTYPE it read)."""
+    return os.environ.get("CUDA_B200_KV_DTYPE", "float32")
+
+
+def kv_itemsize() -> int:
+    return 2 if kv_name() == "bfloat16" else 4
 
 
 def blas_threads() -> int:
@@ -432,12 +442,13 @@ def batched_measurement(cfg, weights, rank: int, world: int, steps: int, warmup:
     program = next(iter(rt._batched.values()))[0]
 
     peak, peak_kind = measured_peaks()
-    kv_read = wl.batch * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * 4 * context
+    kv_read = wl.batch * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * kv_itemsize() * context
     step_bytes = weight_bytes(cfg, 2) + wl.batch * cfg.hidden_size * 2 + kv_read
     step_ms = statistics.fmean(replay_ms)
     rbytes, rms = rows_roofline(rt, wl.batch)
     return {
         "workload": wl.name, "value": value, "unit": "tokens/s", "sequences": wl.batch * world,
+        "kv_cache": kv_name(),
         "steps": steps, "ms_per_step": slowest / steps,
         "e2e": {"value": e2e_steps * wl.batch * world / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(sum(a.nbytes for a in host)), "d2h_bytes_per_step": 8 * wl.batch},
@@ -449,8 +460,8 @@ def batched_measurement(cfg, weights, rank: int, world: int, steps: int, warmup:
         "step_roofline": {"bytes_per_step": step_bytes, "achieved": step_bytes / (step_ms / 1000.0) / 1e9,
                           "peak": peak, "unit": "GB/s",
                           "frac": step_bytes / (step_ms / 1000.0) / 1e9 / peak,
-                          "basis": "bf16 weights + float32 K/V over the whole context (the attention reads "
-                                   "every cache row) per step of 32 tokens"},
+                          "basis": f"bf16 weights + {kv_name()} K/V over the whole context (the attention "
+                                   "reads every cache row) per step of 32 tokens"},
         "gpu_launches": (program.launches + 2) * steps,
     }
 
@@ -509,18 +520,19 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
     flops = json.loads(PEAKS.read_text())["bf16_tflops"] if PEAKS.exists() else 1590.0
     weight_bytes_model = sum(int(np.prod(s)) for n, s in required_weight_shapes(cfg).items()
                              if n != "model.embed_tokens.weight") * 2
-    kv_bytes = wl.batch * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * 4 * context
+    kv_bytes = wl.batch * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * kv_itemsize() * context
     step_bytes = weight_bytes_model + kv_bytes
     achieved = step_bytes / (step_ms / 1000.0) / 1e9
     pflops = prefill_flops(cfg, prompt_len) * wl.batch / (prefill_ms / 1000.0) / 1e12
     return {
         "workload": wl.name, "tensor_parallel": world, "sequences": wl.batch, "prompt_tokens": prompt_len,
+        "kv_cache": kv_name(),
         "lm_head": "vocab-sharded, logits all-gathered" if vocab_shard else "replicated",
         "context": context, "value": steps * wl.batch / (slowest / 1000.0), "unit": "tokens/s",
         "ms_per_step": step_ms,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
                      "frac": achieved / (peak * world), "bytes_per_step": step_bytes,
-                     "basis": "bf16 weights (embedding excluded, lm_head once) + float32 K/V over the context, "
+                     "basis": f"bf16 weights (embedding excluded, lm_head once) + {kv_name()} K/V over the context, "
                               "per step of 16 tokens, against the aggregate HBM bandwidth of the group",
                      "peak_source": peak_kind},
         "prefill": {"value": wl.batch * prompt_len / (prefill_ms / 1000.0), "unit": "tokens/s",
@@ -547,6 +559,8 @@ def main() -> None:
     parser.add_argument("--llama3-steps", type=int, default=30,
                         help="tensor-parallel Llama-3-8B bs16 decode steps (TP = GPUs); 0 skips it")
     parser.add_argument("--llama3-prompt", type=int, default=1024, help="Llama-3-8B prompt tokens")
+    parser.add_argument("--kv-cache", default="bfloat16", choices=("bfloat16", "float32"),
+                        help="KV-cache storage of every b200 measurement (the compiler's kv_cache_dtype)")
     parser.add_argument("--vocab-shard", action="store_true",
                         help="Llama-3-8B: shard the lm_head's rows over the ranks (logits gathered by NCCL)")
     args = parser.parse_args()
@@ -556,6 +570,7 @@ def main() -> None:
 
     import torch
 
+    os.environ["CUDA_B200_KV_DTYPE"] = args.kv_cache  # read when the compiler is first created
     rank, world, local = dist_setup(args.gpus)
     import cuda_b200  # noqa: F401
     from cuda_b200.models import WORKLOADS, synthetic_prompt, synthetic_weights
@@ -624,7 +639,8 @@ def main() -> None:
     peak, peak_kind = measured_peaks()
     itemsize = wl.np_dtype.itemsize
     avg_ctx = start_pos + min(args.steps, per_chunk) / 2
-    kv_bytes = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * 4 * context
+    kv_item = kv_itemsize()
+    kv_bytes = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_size * kv_item * context
     step_bytes = weight_bytes(cfg, itemsize) + cfg.hidden_size * itemsize + kv_bytes
     step_gbs = step_bytes * (value / world) / 1e9
     if program.step_mode:
@@ -632,11 +648,12 @@ def main() -> None:
         kernel_ms = statistics.fmean(replay_ms)
         achieved = step_bytes / (kernel_ms / 1000.0) / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                    "frac": achieved / peak, "traffic": STEP_TRAFFIC.get(wl.name),
+                    "frac": achieved / peak, "traffic": STEP_TRAFFIC.get((wl.name, args.kv_cache)),
                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
                                       "decode-step launch (profiles/decode_step_tinyllama_bf16_bs1.txt)",
                     "kernel": f"cb_decode_step (whole decode step, {step_bytes / 1e9:.3f} GB per launch: "
-                              f"weights + K/V over the {context}-row cache + embedding row)",
+                              f"weights + {args.kv_cache} K/V over the {context}-row cache (the attention "
+                              f"reads every row, masked ones included) + embedding row)",
                     "kernel_ms": kernel_ms, "peak_source": peak_kind}
     else:
         gemv_bytes, gemv_ms, gemv_layers = gemv_roofline(program)
@@ -656,7 +673,7 @@ def main() -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights N(0,0.02), uniform random prompt ids)",
         "config": {"workload": wl.name, "model": "TinyLlama-1.1B-shape", "global_batch": world,
-                   "seq_len": context, "prompt_tokens": wl.prompt_tokens, "kv_cache": "float32",
+                   "seq_len": context, "prompt_tokens": wl.prompt_tokens, "kv_cache": args.kv_cache,
                    "parallelism": f"replicas x{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (2.07 GB weights per step)"},
         "roofline": roofline,

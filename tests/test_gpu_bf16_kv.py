@@ -1,0 +1,123 @@
+"""The bfloat16 KV-cache mode against the reference's golden outputs.
+
+With ``kv_cache_dtype="bfloat16"`` the prefill places bfloat16 caches, and the
+fused decode attentions (batch 1 and batched) read bfloat16 K/V and store the
+row they write rounded to bfloat16.  The reference keeps float32 caches after
+the prefill (its bf16 matmuls return float32, llama.py:509-525 blends into
+them), so the bars are the bf16-model bars of the plugin's specification:
+greedy token ids bit-exact, logits within 2e-2 absolute of the reference's.
+
+* TinyLlama shape (C1/C2): 128 greedy tokens, prefill and first-step logits;
+* the batched decode (C3 shape, batch of 32): row 0 is the golden prompt,
+  every row equals its own batch-1 run in the same mode;
+* Llama-3-8B shape on two layers (C5): the batch-1 runtime and the
+  tensor-parallel runtime at TP = 1.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import golden
+from cuda_b200.models import WORKLOADS, synthetic_prompt, synthetic_weights
+from cuda_b200.runtime import LlamaRuntime
+
+pytestmark = pytest.mark.gpu
+
+BF16_LOGITS = 2e-2
+NAME = "cuda-b200-bf16kv"
+
+
+def _close(got, want):
+    err = float(np.max(np.abs(np.asarray(got, np.float32) - np.asarray(want, np.float32))))
+    assert err <= BF16_LOGITS, f"max abs logit error {err:.3g}"
+
+
+@pytest.fixture(scope="module")
+def bf16kv(gpu):
+    from chomikgrad.lazy import register_compiler
+    from cuda_b200.compiler import CudaB200Compiler
+
+    register_compiler(NAME, lambda: CudaB200Compiler(kv_cache_dtype="bfloat16"), replace=True)
+    return NAME
+
+
+def _bf16_caches(rt, caches):
+    return all(np.dtype(rt.device.dtype(c)).name == "bfloat16" for c in caches)
+
+
+def test_tinyllama_bf16_kv_prefill_and_128_greedy_tokens(bf16kv):
+    g = golden("tinyllama_bf16")
+    wl = WORKLOADS["tinyllama-bf16-bs1"]
+    rt = LlamaRuntime(wl.config, synthetic_weights(wl.config, dtype=wl.np_dtype), compiler=bf16kv)
+    prompt, context = [int(t) for t in g["prompt"]], int(g["context"])
+    logits, caches = rt.prefill(prompt, context)
+    assert _bf16_caches(rt, caches)
+    _close(rt.device.to_numpy(logits), g["prefill_logits"])
+    first = rt.device.argmax(logits)
+    logits, caches = rt.decode(first, len(prompt), context, caches)
+    _close(rt.device.to_numpy(logits), g["step1_logits"])
+    program, _ = next(iter(rt._decoders.values()))
+    assert program.step_mode and program.launches == 1  # still the one-launch decode step
+    result = rt.generate(prompt, len(g["tokens"]))
+    assert result.tokens == [int(t) for t in g["tokens"]]
+    logits, caches = rt.prefill(prompt, context)
+    first = rt.device.argmax(logits)
+    tokens = rt.decode_on_device(first, len(prompt), context, caches, len(g["tokens"]) - 1)
+    assert [first] + list(tokens) == [int(t) for t in g["tokens"]]
+
+
+def test_tinyllama_bf16_kv_batch_of_32(bf16kv):
+    from cuda_b200.batched import BatchedRuntime
+
+    g = golden("tinyllama_bf16")
+    wl = WORKLOADS["tinyllama-bf16-bs32"]
+    weights = synthetic_weights(wl.config, dtype=wl.np_dtype)
+    prompt0 = [int(t) for t in g["prompt"]]
+    prompts = [prompt0] + [list(synthetic_prompt(wl.config, len(prompt0), seed=s)[0]) for s in range(1, wl.batch)]
+    steps = 32
+    batched = BatchedRuntime(wl.config, weights, batch=wl.batch, compiler=bf16kv)
+    got = batched.generate_batch(prompts, steps)
+    assert got[0] == [int(t) for t in g["tokens"][:steps]]
+    single = LlamaRuntime(wl.config, weights, compiler=bf16kv)
+    for i in range(1, wl.batch, 3):
+        assert got[i] == single.generate(prompts[i], steps).tokens, i
+    context = len(prompt0) + steps
+    tokens, caches = batched.prefill_batch(prompts, context)
+    logits, _ = batched.decode_batch(tokens, len(prompt0), context, caches)
+    rows = batched.device.to_numpy(logits)
+    _close(rows[0], g["step1_logits"][0])
+
+
+@pytest.fixture(scope="module")
+def llama3_weights(gpu):
+    wl = WORKLOADS["llama3-8b-2layer-bf16"]
+    return wl, synthetic_weights(wl.config, dtype=wl.np_dtype)
+
+
+def test_llama3_shape_bf16_kv(bf16kv, llama3_weights):
+    from cuda_b200 import tensor_parallel as tp
+
+    g = golden("llama3_2layer_bf16")
+    wl, weights = llama3_weights
+    prompt, context = [int(t) for t in g["prompt"]], int(g["context"])
+    want = [int(t) for t in g["tokens"]]
+    rt = LlamaRuntime(wl.config, weights, compiler=bf16kv)
+    logits, caches = rt.prefill(prompt, context)
+    assert _bf16_caches(rt, caches)
+    _close(rt.device.to_numpy(logits), g["prefill_logits"])
+    tokens = [rt.device.argmax(logits)]
+    for i in range(1, len(want)):
+        logits, caches = rt.decode(tokens[-1], len(prompt) + i - 1, context, caches)
+        if f"step{i}_logits" in g:
+            _close(rt.device.to_numpy(logits), g[f"step{i}_logits"])
+        tokens.append(rt.device.argmax(logits))
+    assert tokens == want
+
+    layout = tp.shard_layout(wl.config, 1, 0)
+    trt = tp.TensorParallelRuntime(wl.config, tp.shard_weights(wl.config, weights, layout), layout, batch=2,
+                                   compiler=bf16kv)
+    other = [int(t) for t in synthetic_prompt(wl.config, len(prompt), seed=7)[0]]
+    assert trt.generate_batch([prompt, other], len(want))[0] == want
+    trt.close()
