@@ -527,7 +527,7 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
     return {
         "workload": wl.name, "tensor_parallel": world, "sequences": wl.batch, "prompt_tokens": prompt_len,
         "kv_cache": kv_name(),
-        "lm_head": "vocab-sharded, logits all-gathered" if vocab_shard else "replicated",
+        "lm_head": "vocab-sharded, distributed argmax" if vocab_shard else "replicated",
         "context": context, "value": steps * wl.batch / (slowest / 1000.0), "unit": "tokens/s",
         "ms_per_step": step_ms,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
@@ -561,8 +561,9 @@ def main() -> None:
     parser.add_argument("--llama3-prompt", type=int, default=1024, help="Llama-3-8B prompt tokens")
     parser.add_argument("--kv-cache", default="bfloat16", choices=("bfloat16", "float32"),
                         help="KV-cache storage of every b200 measurement (the compiler's kv_cache_dtype)")
-    parser.add_argument("--vocab-shard", action="store_true",
-                        help="Llama-3-8B: shard the lm_head's rows over the ranks (logits gathered by NCCL)")
+    parser.add_argument("--lm-head", default="auto", choices=("auto", "replicated", "vocab-shard"),
+                        help="Llama-3-8B: the lm_head's rows replicated, or sharded over the ranks with a distributed "
+                             "argmax (auto: sharded when TP > 1)")
     args = parser.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -690,7 +691,8 @@ def main() -> None:
         line["prefill"] = prefill_measurement(rt, cfg, rank, world, args.prefill_steps, 1)
     if args.llama3_steps > 0 and args.workload == "tinyllama-bf16-bs1":
         line["llama3_8b_tp"] = llama3_measurement(rank, world, local, args.llama3_steps, args.warmup,
-                                                  args.llama3_prompt, args.vocab_shard)
+                                                  args.llama3_prompt,
+                                                  args.lm_head == "vocab-shard" or (args.lm_head == "auto" and world > 1))
     if rank == 0 and not args.no_cpu_baseline:
         keys = ("value", "unit", "cores", "kind", "sample")
         line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, weights, mode="fp32").items() if k in keys}

@@ -283,6 +283,17 @@ _SIGNATURES = {
                                 POINTER(DecodeStepConfig)], c_int),
     "cb_decode_step": ([c_void_p, POINTER(DecodeStepConfig), c_void_p, c_void_p, c_void_p], c_int),
     "cb_argmax_rows": ([c_void_p, c_int, c_longlong, c_longlong, c_void_p, c_void_p], c_int),
+    "cb_argmax_rows_sharded": ([c_void_p, c_int, c_void_p, c_int, c_longlong, c_longlong, c_longlong, c_void_p,
+                                c_void_p, c_void_p], c_int),
+    "cb_argmax_rows_partial": ([c_void_p, c_int, c_longlong, c_longlong, c_longlong, c_void_p, c_void_p], c_int),
+    "cb_argmax_pick": ([c_void_p, c_int, c_longlong, c_void_p, c_void_p], c_int),
+    "cb_peer_create": ([c_int, c_int, c_longlong, c_void_p, c_void_p, c_int], c_int),
+    "cb_peer_connect": ([c_void_p, c_void_p, c_int], c_int),
+    "cb_peer_set_wait": ([c_void_p, c_longlong], c_int),
+    "cb_peer_max_count": ([c_void_p, c_void_p], c_int),
+    "cb_peer_all_reduce": ([c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_longlong, c_void_p, c_void_p],
+                           c_int),
+    "cb_peer_destroy": ([c_void_p], c_int),
     "cb_sample_rows": ([c_void_p, c_void_p], c_int),
     "cb_decode_advance": ([c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
                            c_int, c_longlong, c_void_p, c_longlong, c_void_p, c_void_p], c_int),
@@ -314,6 +325,7 @@ def load() -> ctypes.CDLL:
 FLAG_INDEX, FLAG_POSITION, FLAG_CONTEXT = 1, 2, 3
 FLAG_WAIT_DATA, FLAG_WAIT_SLOT, FLAG_WAIT_DRAIN, FLAG_WAIT_PHASE = 4, 5, 6, 7
 FLAG_NAN = 8
+FLAG_WAIT_PEER = 9
 
 
 def flag_error(value: int) -> Exception:
@@ -329,7 +341,8 @@ def flag_error(value: int) -> Exception:
     waits = {FLAG_WAIT_DATA: "a consumer waiting for weight data",
              FLAG_WAIT_SLOT: "a producer waiting for a free ring slot",
              FLAG_WAIT_DRAIN: "the end-of-kernel drain of bulk copies",
-             FLAG_WAIT_PHASE: "a block waiting for the previous phase of the decode step"}
+             FLAG_WAIT_PHASE: "a block waiting for the previous phase of the decode step",
+             FLAG_WAIT_PEER: "the peer all-reduce waiting for another rank of the group"}
     if value in waits:
         return KernelError(f"kernel timed out in {waits[value]} (results are invalid)")
     return KernelError(f"kernel error flag {value}")

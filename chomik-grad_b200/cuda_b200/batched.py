@@ -168,13 +168,28 @@ class BatchedRuntime(LlamaRuntime):
         for i in range(1, max_new_tokens):
             logits, caches = self.decode_batch(tokens, length + i - 1, context, caches)
             if temperature == 0:
-                tokens = [int(t) for t in self.device.argmax_last_axis(logits)]
+                tokens = self.greedy_rows(logits)
             else:
-                tokens = [int(t) for t in self.device.sample_rows(logits, temperature=temperature, top_k=top_k,
-                                                                  rng=rng)]
+                tokens = [int(t) for t in self.device.sample_rows(self.full_logits(logits), temperature=temperature,
+                                                                  top_k=top_k, rng=rng)]
             for seq, t in zip(out, tokens):
                 seq.append(t)
         return out
+
+    def greedy_rows(self, logits) -> List[int]:
+        """The greedy token of every row of ``decode_batch``'s logits (argmax_last_axis)."""
+        return [int(t) for t in self.device.argmax_last_axis(logits)]
+
+    def full_logits(self, logits):
+        """``decode_batch``'s logits as whole (B, vocab) rows (they already are, here)."""
+        return logits
+
+    def _argmax_rows(self, program, logits_view, out_ptr: int, stream: int) -> None:
+        """Device argmax of the decode program's logits into ``out_ptr`` (int64 per row), on ``stream``."""
+        from . import _lib
+
+        _lib.call("cb_argmax_rows", program.ptr(logits_view), _lib.dtype_code(logits_view.dtype), self.batch,
+                  logits_view.shape[-1], out_ptr, stream)
 
     def decode_batch_on_device(self, tokens: Sequence[int], position: int, context: int, caches: List[Any],
                                steps: int, *, replay_times: Optional[List[float]] = None):
@@ -199,7 +214,6 @@ class BatchedRuntime(LlamaRuntime):
         log = torch.zeros(max(steps, 1) * rows, dtype=torch.int64, device=dev)
         argmax = torch.zeros(rows, dtype=torch.int64, device=dev)
         logits_view = program.plan.outputs[0][1]
-        width = logits_view.shape[-1]
         stream = self.device.stream()
         lib = _lib.load()
         slot, code = program.slot_pointer, _lib.dtype_code
@@ -212,8 +226,7 @@ class BatchedRuntime(LlamaRuntime):
         end = torch.cuda.Event(enable_timing=True)
         start.record()
         for i in range(1, steps):
-            _lib.check(lib.cb_argmax_rows(program.ptr(logits_view), code(logits_view.dtype), rows, width,
-                                          argmax.data_ptr(), stream), "cb_argmax_rows")
+            self._argmax_rows(program, logits_view, argmax.data_ptr(), stream)
             _lib.check(lib.cb_decode_advance_rows(*advance, i - 1, program.error_pointer(), stream),
                        "cb_decode_advance_rows")
             if marks is not None:
@@ -221,8 +234,7 @@ class BatchedRuntime(LlamaRuntime):
             program.replay(stream)
             if marks is not None:
                 marks[i - 1][1].record()
-        _lib.check(lib.cb_argmax_rows(program.ptr(logits_view), code(logits_view.dtype), rows, width,
-                                      log[(steps - 1) * rows:].data_ptr(), stream), "cb_argmax_rows")
+        self._argmax_rows(program, logits_view, log[(steps - 1) * rows:].data_ptr(), stream)
         end.record()
         end.synchronize()
         program.check_errors()

@@ -1427,7 +1427,7 @@ class Planner:
         out = self.tmp(node.shape, src.dtype)
         self.plan.lowered["all_reduce"] = self.plan.lowered.get("all_reduce", 0) + 1
         self.add_step("all_reduce", out, f"all_reduce({self._name(src)}, group={low[2]!r})", src=src,
-                      group=low[2])
+                      group=low[2], flag=self.error_flag())  # the peer kernel reports a rank that did not arrive
         self.set_value(node, out)
 
     def _emit_all_gather(self, node, low) -> None:

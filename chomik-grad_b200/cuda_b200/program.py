@@ -600,7 +600,8 @@ class CudaB200Program(CompiledProgram):
 
         src: View = step.args["src"]
         parallel.get_group(step.args["group"]).all_reduce(self.ptr(src), self.ptr(step.out), src.size,
-                                                          _lib.dtype_code(src.dtype), stream)
+                                                          _lib.dtype_code(src.dtype), stream,
+                                                          error_flag=self.error_pointer())
 
     def _step_all_gather(self, step: Step, stream: int) -> None:
         from . import parallel

@@ -21,11 +21,16 @@ lowering hint, the same mechanism as the reference's preferred lowerings
 (llama.py:13-25): on one rank the portable graph is exact, and the
 ``cuda-b200`` planner lowers the hint to an NCCL all-reduce step of the
 compiled program (``cuda_b200.parallel``).  A vocabulary-sharded lm_head
-produces this rank's columns of the logits; ``all_gather`` (the portable
-form ``x.reshape(1, ...) * ones(G, 1, ...)``, exact on one rank, with an
-``all_gather`` hint lowered to NCCL's all-gather) collects every rank's
-columns, so each rank still returns the whole logits and picks the same
-greedy token, while it reads 1/size of the lm_head.
+produces this rank's columns of the logits.  The prefill gathers them
+(``all_gather``: the portable form ``x.reshape(1, ...) * ones(G, 1, ...)``,
+exact on one rank, with an ``all_gather`` hint lowered to NCCL's
+all-gather), so its program returns the whole logits.  The batched decode
+step returns this rank's columns only, and the greedy token of every row
+comes from a distributed argmax (``cb_argmax_rows_sharded``: each rank's
+(value, global index) winner per row, all-gathered, the same pick on every
+rank -- np.argmax's order over the whole row), so a step exchanges 16 bytes
+per row and rank instead of the logits, while each rank reads 1/size of the
+lm_head.
 
 Per rank and step the decode reads 1/size of the sharded weights (plus the
 replicated ones) and exchanges 2 x layers x batch x hidden float32 values.
@@ -157,6 +162,7 @@ class _ShardMixin(GraphHelpers):
 
     layout: ShardLayout
     group_name: str
+    gather_logits = True  # a vocabulary-sharded lm_head returns the whole logits (else this rank's columns)
 
     def _init_shard(self, layout: ShardLayout, group: str) -> None:
         self.layout = layout
@@ -176,9 +182,10 @@ class _ShardMixin(GraphHelpers):
         return self._reduce(LlamaForCausalLM._mlp(self, inputs, layer))
 
     def _linear(self, inputs: Tensor, weight: Tensor) -> Tensor:
-        """``x @ W.T``; through a vocabulary-sharded lm_head, the whole logits gathered from the group."""
+        """``x @ W.T``; through a vocabulary-sharded lm_head, the whole logits gathered from the group
+        (or, with ``gather_logits`` off, this rank's columns)."""
         out = inputs @ weight.T
-        if self.layout.vocab_shard and weight is self.weights.get("lm_head.weight"):
+        if self.layout.vocab_shard and self.gather_logits and weight is self.weights.get("lm_head.weight"):
             rows, cols = out.shape
             gathered = all_gather(out, self.group_name, self.layout.size, self.dtype)  # (G, rows, V / G)
             return gathered.permute(1, 0, 2).reshape(rows, self.layout.size * cols)
@@ -237,7 +244,11 @@ class TensorParallelPrefill(_ShardMixin, LlamaForCausalLM):
 
 
 class TensorParallelDecoderStep(_ShardMixin, BatchedDecoderStep):
-    """One rank's batched decode step over its shards; caches are (B, kv_heads, ctx, hd) per rank."""
+    """One rank's batched decode step over its shards; caches are (B, kv_heads, ctx, hd) per rank.
+
+    With a vocabulary-sharded lm_head the logits are this rank's (B, vocab / size) columns."""
+
+    gather_logits = False
 
     def __init__(self, config: LlamaConfig, weights: Mapping[str, Tensor], layout: ShardLayout, *,
                  batch: int, cache_length: int, dtype, group: str = "tp") -> None:
@@ -291,9 +302,11 @@ class TensorParallelRuntime(BatchedRuntime):
     """Prefill and batched greedy decode of one rank of a tensor-parallel group.
 
     ``weights`` are this rank's shards (``shard_weights``).  Every rank runs
-    the same calls with the same token ids; the logits (replicated lm_head,
-    or the gathered columns of a vocabulary-sharded one) and so the greedy
-    tokens are the same on every rank.
+    the same calls with the same token ids; the greedy tokens are the same on
+    every rank.  With a replicated lm_head ``decode_batch`` returns the whole
+    logits; with a vocabulary-sharded one it returns this rank's columns,
+    ``greedy_rows`` picks the tokens by the distributed argmax and
+    ``full_logits`` gathers whole rows (collective: every rank calls it).
     """
 
     def __init__(self, config: LlamaConfig, weights, layout: ShardLayout, *, batch: int,
@@ -301,6 +314,67 @@ class TensorParallelRuntime(BatchedRuntime):
         super().__init__(config, weights, batch=batch, compiler=compiler, dtype=dtype)
         self.layout = layout
         self.group = group
+        self._argmax_scratch = None
+        self._argmax_out = None
+
+    def _comm_handle(self) -> Optional[int]:
+        from . import parallel
+
+        return parallel.get_group(self.group).handle if self.layout.size > 1 else None
+
+    def _argmax_rows(self, program, logits_view, out_ptr: int, stream: int) -> None:
+        if not self.layout.vocab_shard:
+            super()._argmax_rows(program, logits_view, out_ptr, stream)
+            return
+        self._sharded_argmax(program.ptr(logits_view), logits_view.dtype, logits_view.shape[-1], out_ptr, stream)
+
+    def _sharded_argmax(self, ptr: int, dtype, width: int, out_ptr: int, stream: int) -> None:
+        import torch
+
+        from . import _lib
+
+        if self._argmax_scratch is None:  # (size + 1) * batch 16-byte records
+            self._argmax_scratch = torch.empty((self.layout.size + 1) * self.batch * 4, dtype=torch.float32,
+                                               device=self.device.torch_device)
+        _lib.call("cb_argmax_rows_sharded", self._comm_handle(), self.layout.size, ptr, _lib.dtype_code(dtype),
+                  self.batch, width, self.layout.vocab_start, self._argmax_scratch.data_ptr(), out_ptr, stream)
+
+    def greedy_rows(self, logits) -> List[int]:
+        if not self.layout.vocab_shard:
+            return super().greedy_rows(logits)
+        tensor = logits.tensor if hasattr(logits, "tensor") else logits
+        self._sharded_argmax(tensor.data_ptr(), self.device.dtype(logits), logits.shape[-1],
+                             self._ensure_out(), self.device.stream())
+        return [int(t) for t in self._argmax_out.tolist()]
+
+    def _ensure_out(self) -> int:
+        import torch
+
+        if self._argmax_out is None:
+            self._argmax_out = torch.empty(self.batch, dtype=torch.int64, device=self.device.torch_device)
+        return self._argmax_out.data_ptr()
+
+    def full_logits(self, logits):
+        """Whole (B, vocab) rows: this rank's columns all-gathered from the group (collective)."""
+        if not self.layout.vocab_shard:
+            return logits
+        import torch
+
+        from . import _lib
+
+        tensor = logits.tensor if hasattr(logits, "tensor") else logits
+        local = tensor.reshape(self.batch, -1).float().contiguous()
+        size, cols = self.layout.size, local.shape[1]
+        gathered = torch.empty((size, self.batch, cols), dtype=torch.float32, device=local.device)
+        if size == 1:
+            gathered[0].copy_(local)
+        else:
+            from . import parallel
+
+            parallel.get_group(self.group).all_gather(local.data_ptr(), gathered.data_ptr(), local.numel(),
+                                                      _lib.F32, self.device.stream())
+        whole = gathered.permute(1, 0, 2).reshape(self.batch, size * cols)
+        return self.device.array(whole)
 
     def prefill(self, prompt_ids: Sequence[int], context: int) -> Tuple[Any, List[Any]]:
         ids = np.asarray(prompt_ids, dtype=np.int32).reshape(1, -1)

@@ -41,7 +41,8 @@ enum {
   CB_FLAG_WAIT_SLOT = 5,
   CB_FLAG_WAIT_DRAIN = 6,
   CB_FLAG_WAIT_PHASE = 7, /* cb_decode_step: a block waiting for the previous phase */
-  CB_FLAG_NAN = 8         /* cb_sample_rows: NaN probabilities */
+  CB_FLAG_NAN = 8,        /* cb_sample_rows: NaN probabilities */
+  CB_FLAG_WAIT_PEER = 9   /* cb_peer_all_reduce: a rank of the group did not arrive in time */
 };
 
 #define CB_MAX_DIMS 8
@@ -555,6 +556,49 @@ CB_API int cb_comm_init(const void* id, int bytes, int nranks, int rank, void** 
 CB_API int cb_comm_destroy(void* comm);
 CB_API int cb_all_reduce(void* comm, const void* src, void* dst, long long count, int dtype, cb_stream_t stream);
 CB_API int cb_all_gather(void* comm, const void* src, void* dst, long long count, int dtype, cb_stream_t stream);
+
+/* One-shot all-reduce over NVLink peer memory, for the small per-layer sums
+ * of the tensor-parallel decode (batch x hidden float32 after the O and
+ * down projections; the graph's all_reduce, then hidden + sum).  Each rank
+ * creates its exchange region (the one allocation of this library:
+ * cudaMalloc of 2 * ranks * max_count floats plus flags) and gets its 64-byte
+ * CUDA IPC handle; the ranks exchange handles (host side) and each maps the
+ * others' regions with cb_peer_connect (handles[ranks][64], rank order).
+ * cb_peer_all_reduce: every rank stores its `count` float32 partials into
+ * every region over NVLink, raises its flags, waits (bounded, 10 s or
+ * cb_peer_set_wait) for every rank's flags, and writes
+ * out[i] = (residual[i] +) sum over ranks in rank order -- the same value on
+ * every rank.  Every rank must make the same calls in the same order.  A rank
+ * that does not arrive makes the others store CB_FLAG_WAIT_PEER in
+ * *error_flag (results invalid).  Plain loads / stores only (no TMA, no
+ * multicast). */
+CB_API int cb_peer_create(int ranks, int rank, long long max_count, void** group, void* handle_out,
+                          int handle_bytes);
+CB_API int cb_peer_connect(void* group, const void* handles, int handle_bytes);
+CB_API int cb_peer_set_wait(void* group, long long wait_ns);
+CB_API int cb_peer_max_count(void* group, long long* count);
+CB_API int cb_peer_all_reduce(void* group, const float* src, void* out, int out_dtype, const void* residual,
+                              int residual_dtype, long long count, int* error_flag, cb_stream_t stream);
+CB_API int cb_peer_destroy(void* group);
+
+/* Greedy argmax of every row over a vocabulary-sharded lm_head, without
+ * gathering the logits.  Replaces DeviceAdapter.argmax_last_axis
+ * (chomikgrad/lazy.py:132-134) for a rank whose logits `x` (rows x width) are
+ * columns [col_offset, col_offset + width) of the whole rows: each rank
+ * reduces its columns to a 16-byte (value, global index) record per row, the
+ * records are all-gathered over `comm` (NCCL, on `stream`; comm may be NULL
+ * when ranks == 1) and every rank writes the same winner to out_index[rows]:
+ * np.argmax of the whole row (a NaN first, then the larger value, then the
+ * lower index).  scratch: (ranks + 1) * rows * 16 bytes, 16-byte aligned. */
+CB_API int cb_argmax_rows_sharded(void* comm, int ranks, const void* x, int dtype, long long rows, long long width,
+                                  long long col_offset, void* scratch, long long* out_index, cb_stream_t stream);
+/* Its two halves: cb_argmax_rows_partial writes each row's record
+ * {float value; int valid; long long global index} to records[rows];
+ * cb_argmax_pick reduces records[ranks][rows] (rank after rank) to
+ * out_index[rows]. */
+CB_API int cb_argmax_rows_partial(const void* x, int dtype, long long rows, long long width, long long col_offset,
+                                  void* records, cb_stream_t stream);
+CB_API int cb_argmax_pick(const void* records, int ranks, long long rows, long long* out_index, cb_stream_t stream);
 
 /* ---- whole decode step in one launch --------------------------------------
  * The fused decode step of LlamaDecoderStep (chomikgrad/llama.py:469-543)

@@ -74,12 +74,21 @@ def six_ops(ref) -> dict:
 
 
 def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling=None,
-               prompt_tokens=None) -> dict:
+               prompt_tokens=None, kv_bf16: bool = False) -> dict:
     """Prefill + decode with the reference classes and its cpu compiler.
 
     Greedy, or with ``sampling = (temperature, top_k, seed)`` each token from
     the reference's own ``sample_native_token`` (generate_tinyllama.py:146-157)
     with ``np.random.default_rng(seed)`` (:712).
+
+    ``kv_bf16``: the plugin's bfloat16 KV-cache mode, through the same graphs
+    and compiler.  The reference keeps float32 caches; here every cache it
+    returns is rounded to bfloat16 (round to nearest even) before it is bound
+    again, and each decode step runs twice: once as usual, which writes the
+    new K/V row, then -- after rounding -- again with an all-zero write mask,
+    so that the step attends the row as stored (the plugin stores the row it
+    writes rounded and attends the stored value).  The second run's logits
+    and caches are kept.
     """
     Tensor, compile_graph, get_compiler, no_grad, L = ref
     if sampling is not None:
@@ -119,6 +128,9 @@ def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling
         token = pick(native[0])
         out["prefill_logits"] = np.asarray(native[0], dtype=np.float32)
         caches = list(native[1:])
+        if kv_bf16:
+            caches = [_round_bf16(c) for c in caches]
+            out["kv_cache"] = np.array("bfloat16")
         out["prefill_cache_dtype"] = np.array(str(np.asarray(caches[0]).dtype))
         out["prefill_cache_fp"] = np.array([[float(np.sum(np.asarray(c, np.float64))),
                                              float(np.sum(np.abs(np.asarray(c, np.float64))))]
@@ -149,6 +161,11 @@ def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling
             else:
                 bindings = dict(zip(nodes, [device.array(v) for v in host] + caches))
             native = decoder.run(bindings, synchronize=False)
+            if kv_bf16:  # the written row rounded, then attended as stored (write mask all zero)
+                caches = [_round_bf16(c) for c in native[1:]]
+                host[3] = np.zeros_like(host[3])
+                native = decoder.run(dict(zip(nodes, [device.array(v) for v in host] + caches)),
+                                     synchronize=False)
             logits = np.asarray(native[0], dtype=np.float32)
             token = pick(native[0])
             order = np.argsort(-logits[0], kind="stable")[:8]
@@ -166,6 +183,14 @@ def generation(ref, workload_name: str, steps: int, keep_logits: tuple, sampling
                                        float(np.sum(np.abs(np.asarray(c, np.float64))))]
                                       for c in caches])
     return out
+
+
+def _round_bf16(cache):
+    """A float32 cache rounded to bfloat16 values (kept as float32, the reference's cache dtype)."""
+    import ml_dtypes
+
+    host = np.asarray(cache)
+    return host.astype(ml_dtypes.bfloat16).astype(host.dtype)
 
 
 def sampling_rows(ref) -> dict:
@@ -240,6 +265,9 @@ CASES = {
     "tinyllama_bf16": lambda ref: generation(ref, "tinyllama-bf16-bs1", 128, (1, 2, 64, 127)),
     # the Llama-3-8B shape (head size 128, theta 5e5, vocabulary 128256) on two layers
     "llama3_2layer_bf16": lambda ref: generation(ref, "llama3-8b-2layer-bf16", 8, (1, 7)),
+    # the bfloat16 KV-cache mode (see generation): TinyLlama shape, 128 steps; Llama-3 shape, 8 steps
+    "tinyllama_bf16_kvbf16": lambda ref: generation(ref, "tinyllama-bf16-bs1", 128, (1, 2, 64, 127), kv_bf16=True),
+    "llama3_2layer_bf16_kvbf16": lambda ref: generation(ref, "llama3-8b-2layer-bf16", 8, (1, 7), kv_bf16=True),
     # one 2048-token prompt of the prefill workload's length, TinyLlama per-layer shapes on four
     # layers (all 22 would need ~55 GB: the cpu compiler keeps every intermediate): logits, first token
     "tinyllama_prefill2048": lambda ref: generation(ref, "tinyllama-4layer-prefill2048-bf16", 1, ()),

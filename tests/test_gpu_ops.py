@@ -102,6 +102,46 @@ def test_argmax_first_occurrence_and_nan(gpu):
     np.testing.assert_array_equal(device.argmax_last_axis(device.array(rows)), rows.argmax(axis=-1))
 
 
+@pytest.mark.parametrize("ranks", [1, 2, 4, 8])
+def test_sharded_argmax_records_and_pick(gpu, ranks):
+    """cb_argmax_rows_partial over column slices (one per emulated rank) + cb_argmax_pick == np.argmax of the
+    whole row: ties across slice boundaries (lower index), NaN (first NaN), inf, all-equal rows; bf16 too."""
+    import ml_dtypes
+    import torch
+
+    from cuda_b200 import _lib
+
+    rng = np.random.default_rng(ranks)
+    vocab = 96 * ranks
+    logits = rng.normal(0, 1, (10, vocab)).astype(np.float32)
+    cols = vocab // ranks
+    logits[1, [5, min(cols, vocab - 1)]] = 9.0
+    logits[2, [vocab - 1, 0]] = 7.0
+    logits[3, vocab // 2 + 1] = np.nan
+    logits[4, [3, vocab - 2]] = np.nan
+    logits[5] = 0.0
+    logits[6, -1] = np.inf
+    logits[7] = -np.inf
+    for dtype, code in ((np.float32, _lib.F32), (ml_dtypes.bfloat16, _lib.BF16)):
+        host = logits.astype(dtype)
+        dev = torch.from_numpy(host.view(np.uint16) if dtype != np.float32 else host).cuda()
+        records = torch.zeros(ranks * host.shape[0] * 4, dtype=torch.float32, device="cuda")
+        out = torch.full((host.shape[0],), -7, dtype=torch.int64, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        for r in range(ranks):
+            piece = dev[:, r * cols:(r + 1) * cols].contiguous()
+            _lib.call("cb_argmax_rows_partial", piece.data_ptr(), code, host.shape[0], cols, r * cols,
+                      records.data_ptr() + r * host.shape[0] * 16, stream)
+        _lib.call("cb_argmax_pick", records.data_ptr(), ranks, host.shape[0], out.data_ptr(), stream)
+        np.testing.assert_array_equal(out.cpu().numpy(), np.argmax(host.astype(np.float32), axis=-1))
+        # the whole path on one rank (no communicator): partial, copy, pick
+        scratch = torch.zeros(2 * host.shape[0] * 4, dtype=torch.float32, device="cuda")
+        out.fill_(-7)
+        _lib.call("cb_argmax_rows_sharded", None, 1, dev.data_ptr(), code, host.shape[0], vocab, 0,
+                  scratch.data_ptr(), out.data_ptr(), stream)
+        np.testing.assert_array_equal(out.cpu().numpy(), np.argmax(host.astype(np.float32), axis=-1))
+
+
 def test_gather_out_of_range_raises(gpu):
     table = Tensor(np.arange(6, dtype=np.float32).reshape(3, 2))
     bad = Tensor(np.array([[0, 3]], dtype=np.int32), copy=False)

@@ -6,9 +6,12 @@ projections is an NCCL step of each compiled program (cuda_b200.parallel),
 replayed inside the decode step's CUDA graph.  Every rank must produce the
 one-GPU program's greedy tokens, and logits equal up to the float32
 reassociation of the sharded sums.  Skipped on a machine with fewer than two
-GPUs.  On one GPU, a one-rank group with a vocabulary-sharded lm_head runs
-the same checks: its logits pass through an NCCL all-gather step (inside the
-captured graph) before the argmax.
+GPUs.  With a vocabulary-sharded lm_head each rank's decode step returns its
+columns of the logits and the greedy tokens come from the distributed argmax
+(cb_argmax_rows_sharded: records all-gathered by NCCL, inside the captured
+graph for the replays); ``full_logits`` gathers whole rows for the logit
+check.  On one GPU, a one-rank group with a vocabulary-sharded lm_head runs
+the same checks.
 """
 
 from __future__ import annotations
@@ -49,9 +52,9 @@ def _rank(rank: int, size: int, port: int, queue, vocab_shard: bool = False) -> 
         tokens, logits = first, None
         for i in range(steps):
             logits, caches = rt.decode_batch(tokens, prompt_len + i, context, caches)
-            tokens = [int(t) for t in rt.device.argmax_last_axis(logits)]
+            tokens = rt.greedy_rows(logits)
             host.append(tokens)
-        result = {"host": host, "logits": rt.device.to_numpy(logits).astype(np.float32)}
+        result = {"host": host, "logits": rt.device.to_numpy(rt.full_logits(logits)).astype(np.float32)}
         # the same steps again as graph replays (NCCL inside the captured graph)
         first2, caches2 = rt.prefill_batch(prompts, context)
         replayed, _ = rt.decode_batch_on_device(first2, prompt_len, context, caches2, steps + 1)

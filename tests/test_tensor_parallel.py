@@ -164,9 +164,55 @@ def test_tensor_parallel_decode_equals_one_rank(size):
             np.testing.assert_allclose(g, f[:, kv:kv + lay.kv_heads], rtol=0, atol=1e-5)
 
 
+def _pick(records):
+    """The distributed argmax's pick (cb_argmax_pick): records (ranks, rows, [value, global index]) in rank
+    order -> per row a NaN first, then the larger value, then the lower index."""
+    out = []
+    for row in range(records.shape[1]):
+        best = None
+        for value, index in records[:, row]:
+            if best is None:
+                best = (value, index)
+                continue
+            bv, bi = best
+            if np.isnan(value) or np.isnan(bv):
+                better = np.isnan(value) and (not np.isnan(bv) or index < bi)
+            else:
+                better = value > bv or (value == bv and index < bi)
+            if better:
+                best = (value, index)
+        out.append(int(best[1]))
+    return np.asarray(out)
+
+
+def _records(local, offset):
+    """One rank's records: np.argmax of its columns, as a global index."""
+    idx = np.argmax(local, axis=-1)
+    return np.stack([local[np.arange(local.shape[0]), idx], idx + offset], axis=-1)
+
+
 @pytest.mark.parametrize("size", [2, 4])
-def test_vocabulary_sharded_lm_head_gathers_the_whole_logits(size):
-    """With the lm_head's rows split over the ranks, every rank still returns the unsharded logits."""
+def test_distributed_argmax_equals_argmax_of_the_whole_row(size):
+    rng = np.random.default_rng(size)
+    vocab = 64 * size
+    logits = rng.normal(0, 1, (9, vocab)).astype(np.float32)
+    logits[1, [5, 64]] = 9.0                       # a tie across a shard boundary: the lower index wins
+    logits[2, [vocab - 1, 0]] = 7.0
+    logits[3, 70] = np.nan                         # NaN wins wherever it is
+    logits[4, [3, vocab - 2]] = np.nan             # the first NaN wins
+    logits[5] = 0.0                                # all equal: index 0
+    logits[6, -1] = np.inf
+    logits[7] = -np.inf
+    logits[8, [10, 10 + vocab // size]] = np.finfo(np.float32).max
+    cols = vocab // size
+    records = np.stack([_records(logits[:, r * cols:(r + 1) * cols], r * cols) for r in range(size)])
+    np.testing.assert_array_equal(_pick(records), np.argmax(logits, axis=-1))
+
+
+@pytest.mark.parametrize("size", [2, 4])
+def test_vocabulary_sharded_lm_head_returns_the_rank_columns(size):
+    """With the lm_head's rows split over the ranks, each rank's decode step returns its columns of the
+    unsharded logits, and the records of the distributed argmax pick the unsharded greedy tokens."""
     config, batch, context, position = TINY, 3, 24, 9
     weights = synthetic_weights(config, dtype=np.float32)
     inputs = _decode_inputs(config, batch, context, position, seed=11)
@@ -181,10 +227,10 @@ def test_vocabulary_sharded_lm_head_gathers_the_whole_logits(size):
     assert tp.shard_weights(config, weights, layouts[1])["lm_head.weight"].shape[0] == config.vocab_size // size
     ranks = _threaded_ranks(size, lambda r: _tp_decode_graph(config, weights, layouts[r], batch, context, inputs))
     scale = float(np.abs(full[0]).max())
-    for got in ranks:
-        assert got[0].shape == full[0].shape
-        np.testing.assert_allclose(got[0], full[0], rtol=0, atol=1e-4 * scale)
-        assert (got[0].argmax(-1) == full[0].argmax(-1)).all()
+    for lay, got in zip(layouts, ranks):
+        np.testing.assert_allclose(got[0], full[0][:, lay.vocab_rows], rtol=0, atol=1e-4 * scale)
+    records = np.stack([_records(got[0], lay.vocab_start) for lay, got in zip(layouts, ranks)])
+    np.testing.assert_array_equal(_pick(records), full[0].argmax(-1))
     import dataclasses
 
     with pytest.raises(ValueError, match="vocabulary"):
