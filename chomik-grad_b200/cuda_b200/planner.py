@@ -622,6 +622,7 @@ class Planner:
             DecodeFusion(self).apply()
         if self.alias_caches:
             self._match_kv_writes()
+        self._match_all_reduce_adds()
         self._fuse_elementwise_groups()
         for node in order:
             if node.op is None or node in self._val:
@@ -675,6 +676,38 @@ class Planner:
                 continue
             self.claimed.update((left, right, keep))
             self.units[node] = self._kv_write_unit(node, cache, row, wm, keep)
+
+    def _match_all_reduce_adds(self) -> None:
+        """``hidden + all_reduce(partial)`` (the residual add after the row-sharded O and down
+        projections, llama.py:526-535 over shards) => one all_reduce step carrying the residual:
+        the peer kernel adds it while it sums the ranks' partials (NCCL's path adds it after)."""
+        for node in self.order:
+            if not is_ew(node, "add") or node in self.claimed or node in self.units or node in self._low:
+                continue
+            for reduced, other in ((node.inputs[1], node.inputs[0]), (node.inputs[0], node.inputs[1])):
+                low = self._low.get(reduced)
+                if low is None or low[0] != "all_reduce" or reduced in self.output_set:
+                    continue
+                if self.consumers.get(reduced) != [node] or tuple(reduced.shape) != tuple(node.shape):
+                    continue
+                if tuple(other.shape) != tuple(node.shape) or self.rdt(node) != F32 or self.rdt(reduced) != F32:
+                    continue
+                if self.rdt(other).name not in ("float32", "bfloat16") or self.rdt(low[1][0]) != F32:
+                    continue
+                self.claimed.add(reduced)
+                self.units[node] = self._all_reduce_add_unit(node, reduced, low, other)
+                break
+
+    def _all_reduce_add_unit(self, node, reduced, low, other):
+        def emit() -> None:
+            src = self.contiguous(self.value(low[1][0]))
+            res = self.contiguous(self.value(other))
+            out = self.tmp(node.shape, F32)
+            self.plan.lowered["all_reduce"] = self.plan.lowered.get("all_reduce", 0) + 1
+            self.add_step("all_reduce", out, f"{self._name(res)} + all_reduce({self._name(src)}, group={low[2]!r})",
+                          src=src, group=low[2], flag=self.error_flag(), residual=res)
+            self.set_value(node, out)
+        return emit
 
     def kv_dtypes(self) -> Tuple[np.dtype, ...]:
         """Cache dtypes the decode blends accept: float32, and bfloat16 in bfloat16-KV mode."""

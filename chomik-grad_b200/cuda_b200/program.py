@@ -459,6 +459,20 @@ class CudaB200Program(CompiledProgram):
         a.out = self.ptr(step.out)
         _lib.call("cb_elementwise", ctypes.byref(a), stream)
 
+    def _add_into(self, out: View, residual: View, stream: int) -> None:
+        """out = residual + out (both contiguous, the same shape), in place."""
+        a = _lib.ElementwiseArgs()
+        a.ndim, a.out_dtype, a.n_inputs, a.n_instr = 1, _lib.dtype_code(out.dtype), 2, 1
+        a.shape[0] = out.size
+        for i, v in enumerate((residual, out)):
+            a.inputs[i] = self.ptr(v)
+            a.in_dtype[i] = _lib.dtype_code(v.dtype)
+            a.in_offset[i] = 0
+            a.in_strides[i][0] = 1
+        a.op[0], a.lhs[0], a.rhs[0], a.round[0] = _lib.OPS["add"], 0, 1, _lib.F32
+        a.out = self.ptr(out)
+        _lib.call("cb_elementwise", ctypes.byref(a), stream)
+
     def _step_reduce(self, step: Step, stream: int) -> None:
         src: View = step.args["src"]
         a = _lib.ReduceArgs()
@@ -599,9 +613,18 @@ class CudaB200Program(CompiledProgram):
         from . import parallel
 
         src: View = step.args["src"]
-        parallel.get_group(step.args["group"]).all_reduce(self.ptr(src), self.ptr(step.out), src.size,
-                                                          _lib.dtype_code(src.dtype), stream,
-                                                          error_flag=self.error_pointer())
+        comm = parallel.get_group(step.args["group"])
+        residual: Optional[View] = step.args.get("residual")
+        code = _lib.dtype_code(src.dtype)
+        if residual is not None and not (comm.peer and code == _lib.F32 and src.size <= comm.peer_max_count):
+            # NCCL sums into the output, then the residual is added to it in place
+            comm.all_reduce(self.ptr(src), self.ptr(step.out), src.size, code, stream)
+            self._add_into(step.out, residual, stream)
+            return
+        comm.all_reduce(self.ptr(src), self.ptr(step.out), src.size, code, stream,
+                        error_flag=self.error_pointer(),
+                        residual=None if residual is None else self.ptr(residual),
+                        residual_dtype=_lib.F32 if residual is None else _lib.dtype_code(residual.dtype))
 
     def _step_all_gather(self, step: Step, stream: int) -> None:
         from . import parallel

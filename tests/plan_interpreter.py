@@ -453,8 +453,8 @@ COLLECTIVES = ("all_reduce", "all_gather")
 
 
 def run_ranks(interpreters: Sequence[PlanInterpreter]) -> None:
-    """Run one plan per rank in lock step: each all_reduce sums the ranks' operands in rank order,
-    each all_gather stacks them in rank order."""
+    """Run one plan per rank in lock step: each all_reduce sums the ranks' operands in rank order
+    (then adds the step's residual, if it carries one), each all_gather stacks them in rank order."""
     runs = [it.steps() for it in interpreters]
     while True:
         pending = [next(r, None) for r in runs]
@@ -470,4 +470,6 @@ def run_ranks(interpreters: Sequence[PlanInterpreter]) -> None:
             for part in parts[1:]:
                 result = result + part
         for it, p in zip(interpreters, pending):
-            it.write(p.out, result)
+            residual = p.args.get("residual")
+            # an all_reduce carrying the residual add that follows it: hidden + sum
+            it.write(p.out, result if residual is None else it.read_f32(residual) + result)

