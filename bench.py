@@ -513,9 +513,30 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
     slowest = reduce_max(elapsed, world)
     step_ms = reduce_max(statistics.fmean(replay_ms), world)
     rt.close()  # release the graphs that hold NCCL work before the communicator
+    nccl = None
     if world > 1:
+        allreduce = "peer one-shot (NVLink stores, CUDA IPC)" if parallel.get_group("tp").peer else "nccl"
         barrier(world)
         parallel.destroy_group("tp")
+        del rt, caches
+        torch.cuda.empty_cache()
+        # the same decode with every all-reduce on NCCL, for comparison (fewer steps)
+        parallel.init_group("tp-nccl", peer=False)
+        rt2 = tp.TensorParallelRuntime(cfg, weights, layout, batch=wl.batch, dtype=bfloat16(), group="tp-nccl")
+        tokens2, caches2 = rt2.prefill_batch(prompts, context)
+        rt2.decode_batch_on_device(tokens2, prompt_len, context, caches2, max(warmup, 3))
+        barrier(world)
+        nccl_times: list = []
+        rt2.decode_batch_on_device(tokens2, prompt_len, context, caches2, min(steps, per_chunk) + 1,
+                                   replay_times=nccl_times)
+        nccl_ms = reduce_max(statistics.fmean(nccl_times), world)
+        rt2.close()
+        barrier(world)
+        parallel.destroy_group("tp-nccl")
+        nccl = {"allreduce": "nccl", "ms_per_step": nccl_ms, "value": wl.batch / (nccl_ms / 1000.0),
+                "unit": "tokens/s", "steps": min(steps, per_chunk)}
+    else:
+        allreduce = "none (one rank)"
     peak, peak_kind = measured_peaks()
     flops = json.loads(PEAKS.read_text())["bf16_tflops"] if PEAKS.exists() else 1590.0
     weight_bytes_model = sum(int(np.prod(s)) for n, s in required_weight_shapes(cfg).items()
@@ -528,6 +549,7 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
         "workload": wl.name, "tensor_parallel": world, "sequences": wl.batch, "prompt_tokens": prompt_len,
         "kv_cache": kv_name(),
         "lm_head": "vocab-sharded, distributed argmax" if vocab_shard else "replicated",
+        "allreduce": allreduce,
         "context": context, "value": steps * wl.batch / (slowest / 1000.0), "unit": "tokens/s",
         "ms_per_step": step_ms,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
@@ -538,6 +560,7 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
         "prefill": {"value": wl.batch * prompt_len / (prefill_ms / 1000.0), "unit": "tokens/s",
                     "ms": prefill_ms, "tflops": pflops, "frac_of_bf16_peak": pflops / (flops * world)},
         "data": "random-init bf16 weights drawn on the GPU (seeded), uniform random prompt ids",
+        "decode_nccl_allreduce": nccl,
     }
 
 
