@@ -214,6 +214,14 @@ class StepPhase(ctypes.Structure):
     _fields_ = [("kind", c_int), ("x_mode", c_int), ("gemv", GemvArgs), ("attention", DecodeAttentionArgs)]
 
 
+SGD_GROUP = 16
+
+
+class SgdGroup(ctypes.Structure):
+    _fields_ = [("n", c_int), ("lr", c_float), ("param", c_void_p * SGD_GROUP), ("grad", c_void_p * SGD_GROUP),
+                ("out", c_void_p * SGD_GROUP), ("count", c_longlong * SGD_GROUP)]
+
+
 class DecodeStepConfig(ctypes.Structure):
     _fields_ = [("grid", c_int), ("n_phases", c_int), ("w_dtype", c_int), ("head_size", c_int),
                 ("slot_bytes", c_longlong), ("x_bytes", c_longlong), ("norm_bytes", c_longlong),
@@ -294,6 +302,13 @@ _SIGNATURES = {
     "cb_peer_all_reduce": ([c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_longlong, c_void_p, c_void_p],
                            c_int),
     "cb_peer_destroy": ([c_void_p], c_int),
+    "cb_softmax_rows": ([c_void_p, c_longlong, c_longlong, c_int, c_void_p, c_void_p], c_int),
+    "cb_softmax_backward_rows": ([c_void_p, c_void_p, c_longlong, c_longlong, c_int, c_void_p, c_void_p], c_int),
+    "cb_layer_norm_rows": ([c_void_p, c_void_p, c_void_p, c_longlong, c_longlong, c_float, c_void_p, c_void_p],
+                           c_int),
+    "cb_layer_norm_backward_rows": ([c_void_p, c_void_p, c_void_p, c_longlong, c_longlong, c_float, c_void_p,
+                                     c_void_p, c_void_p, c_void_p, c_void_p], c_int),
+    "cb_sgd_update": ([c_void_p, c_void_p], c_int),
     "cb_sample_rows": ([c_void_p, c_void_p], c_int),
     "cb_decode_advance": ([c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
                            c_int, c_longlong, c_void_p, c_longlong, c_void_p, c_void_p], c_int),

@@ -108,3 +108,60 @@ class CudaB200Compiler(Compiler):
                 dynamic_inputs: Sequence[object] = ()) -> CudaB200Program:
         program = CudaB200Program(self.plan(outputs, dynamic_inputs), self)
         return program
+
+    # ------------------------------------------------------------ training
+    def update_parameters(self, parameters: Sequence[object], gradients: Sequence[object], learning_rate: float,
+                          *, inplace: bool = False):
+        """SGD step (``SGD.step``, chomikgrad/optim.py:28-64): the gradients' graph compiled and run
+        on the device, then :meth:`update_native_parameters`."""
+        if len(parameters) != len(gradients):
+            raise ValueError("parameter and gradient counts must match")
+        native = self.compile(list(gradients)).run(synchronize=False) if gradients else []
+        return self.update_native_parameters(parameters, native, learning_rate, inplace=inplace)
+
+    def update_native_parameters(self, parameters: Sequence[object], gradients: Sequence[object],
+                                 learning_rate: float, *, inplace: bool = False):
+        """``param - lr * grad`` for float32 parameters, up to ``_lib.SGD_GROUP`` tensors per launch
+        (``cb_sgd_update``).  Returns new leaves holding the updated parameters (in place: the
+        parameters' own storage) and the gradients (Compiler.update_native_parameters,
+        chomikgrad/lazy.py:199-209; compiled training steps, chomikgrad/jit.py:113-160)."""
+        import ctypes
+
+        import torch
+        from chomikgrad.lazy import LazyNode
+
+        if len(parameters) != len(gradients):
+            raise ValueError("parameter and gradient counts must match")
+        natives, grads = [], []
+        for node, grad in zip(parameters, gradients):
+            native = node.native_values.get(self.device.name)
+            if not isinstance(native, DeviceArray):
+                native = self.device.array(node.numpy_value())
+                if node.cache_native:
+                    node.native_values[self.device.name] = native
+            grad = self.device.array(grad)
+            if native.dtype != np.float32 or grad.dtype != np.float32:
+                raise TypeError("cuda-b200 updates float32 parameters with float32 gradients")
+            if native.size != grad.size or tuple(native.shape) != tuple(node.shape):
+                raise ValueError("gradient shape does not match parameter shape")
+            natives.append(native)
+            grads.append(grad)
+        outs = natives if inplace else [DeviceArray(torch.empty_like(p.tensor), p.shape, p.dtype) for p in natives]
+        stream = self.device.stream()
+        for start in range(0, len(natives), _lib.SGD_GROUP):
+            group = _lib.SgdGroup()
+            chunk = range(start, min(start + _lib.SGD_GROUP, len(natives)))
+            group.n = len(chunk)
+            group.lr = float(np.float32(learning_rate))
+            for j, i in enumerate(chunk):
+                group.param[j] = natives[i].data_ptr()
+                group.grad[j] = grads[i].data_ptr()
+                group.out[j] = outs[i].data_ptr()
+                group.count[j] = natives[i].size
+            _lib.call("cb_sgd_update", ctypes.byref(group), stream)
+        name = self.device.name
+        parameter_nodes = tuple(LazyNode.native_leaf(name, out, node.shape, node.dtype)
+                                for node, out in zip(parameters, outs))
+        gradient_nodes = tuple(LazyNode.native_leaf(name, grad, node.shape, node.dtype)
+                               for node, grad in zip(parameters, grads))
+        return parameter_nodes, gradient_nodes

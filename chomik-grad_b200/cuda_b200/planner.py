@@ -295,7 +295,12 @@ def _collect_buffers(value, acc: Set[int]) -> None:
 class Planner:
     """Builds a :class:`Plan` from output nodes (see module docstring)."""
 
-    SUPPORTED_LOWERINGS = frozenset({"rms_norm", "rope", "sdpa", "all_reduce", "all_gather"})
+    SUPPORTED_LOWERINGS = frozenset({"rms_norm", "rope", "sdpa", "all_reduce", "all_gather",
+                                     "softmax", "log_softmax", "softmax_backward", "log_softmax_backward",
+                                     "layer_norm", "layer_norm_backward"})
+    # the training lowerings' hinted subgraphs end in these operations (chomikgrad/tensor.py:316-450)
+    _TRAIN_TOP = {"softmax": "div", "log_softmax": "sub", "softmax_backward": "mul",
+                  "log_softmax_backward": "sub", "layer_norm": "add"}
 
     def __init__(self, outputs: Sequence[object], dynamic_inputs: Sequence[object], *,
                  backend: str, leaf_dtype, max_positions: int = 8192,
@@ -380,7 +385,33 @@ class Planner:
             return low
         if kind_ == "all_gather" and self._match_all_gather(node, low):
             return low
+        if kind_ in self._TRAIN_TOP or kind_ == "layer_norm_backward":
+            return low if self._match_train(node, low) else None
         return None
+
+    def _match_train(self, node, low) -> bool:
+        """The training lowerings (softmax / log_softmax and their backward, layer_norm and its
+        backward), float32 over the last axis.  The reference builds the hinted subgraph and
+        the hint together (chomikgrad/tensor.py:316-450); the checks here are the ones the
+        kernels rely on: dtypes, shapes, the axis, the subgraph's final operation."""
+        name, inputs, arg = low[0], low[1], low[2]
+        if any(self.rdt(n) != F32 for n in (node, *inputs)) or not node.shape:
+            return False
+        width = node.shape[-1] if name != "layer_norm_backward" else inputs[1].shape[-1]
+        if name in self._TRAIN_TOP:
+            if not is_ew(node, self._TRAIN_TOP[name]):
+                return False
+            if name in ("softmax", "log_softmax", "softmax_backward", "log_softmax_backward"):
+                return (arg == len(node.shape) - 1 and all(tuple(n.shape) == tuple(node.shape) for n in inputs))
+            x, w, b = inputs
+            return (tuple(x.shape) == tuple(node.shape) and tuple(w.shape) == (width,)
+                    and tuple(b.shape) == (width,) and float(arg) > 0)
+        grad, x, w = inputs
+        if not (isinstance(arg, tuple) and len(arg) == 2 and arg[1] in (0, 1, 2) and float(arg[0]) > 0):
+            return False
+        if tuple(grad.shape) != tuple(x.shape) or tuple(w.shape) != (width,):
+            return False
+        return tuple(node.shape) == (tuple(x.shape) if arg[1] == 0 else (width,))
 
     def _parents(self, node):
         low = self._low.get(node)
@@ -1454,6 +1485,69 @@ class Planner:
         if np.all(value[:, ~above] == 0.0):
             flags |= _lib.CAUSAL_ZERO_BELOW
         return flags
+
+    # ------------------------------------------------------------ training
+    def _rows_view(self, node):
+        v = self.contiguous(self.value(node))
+        width = v.shape[-1] if v.shape else 1
+        return v, (v.size // width if width else 0), width
+
+    def _emit_softmax(self, node, low, log_form: bool = False, name: str = "softmax") -> None:
+        x, rows, width = self._rows_view(low[1][0])
+        out = self.tmp(node.shape, F32)
+        self.plan.lowered[name] = self.plan.lowered.get(name, 0) + 1
+        self.add_step("softmax", out, f"{name}({self._name(x)}, axis=-1)", x=x, rows=rows, width=width,
+                      log=log_form)
+        self.set_value(node, out)
+
+    def _emit_log_softmax(self, node, low) -> None:
+        self._emit_softmax(node, low, True, "log_softmax")
+
+    def _emit_softmax_backward(self, node, low, log_form: bool = False, name: str = "softmax_backward") -> None:
+        g, rows, width = self._rows_view(low[1][0])
+        y = self.contiguous(self.value(low[1][1]))
+        out = self.tmp(node.shape, F32)
+        self.plan.lowered[name] = self.plan.lowered.get(name, 0) + 1
+        self.add_step("softmax_backward", out, f"{name}({self._name(g)}, {self._name(y)}, axis=-1)", grad=g, y=y,
+                      rows=rows, width=width, log=log_form)
+        self.set_value(node, out)
+
+    def _emit_log_softmax_backward(self, node, low) -> None:
+        self._emit_softmax_backward(node, low, True, "log_softmax_backward")
+
+    def _emit_layer_norm(self, node, low) -> None:
+        x, rows, width = self._rows_view(low[1][0])
+        w, b = (self.contiguous(self.value(n)) for n in low[1][1:])
+        out = self.tmp(node.shape, F32)
+        eps = float(np.float32(low[2]))
+        self.plan.lowered["layer_norm"] = self.plan.lowered.get("layer_norm", 0) + 1
+        self.add_step("layer_norm", out, f"layer_norm({self._name(x)}, {self._name(w)}, {self._name(b)}, "
+                      f"eps={eps!r})", x=x, w=w, b=b, rows=rows, width=width, eps=eps)
+        self.set_value(node, out)
+
+    def _emit_layer_norm_backward(self, node, low) -> None:
+        """One step for every requested contribution (input, weight, bias) of the same backward."""
+        inputs, eps = low[1], float(np.float32(low[2][0]))
+        siblings = {}
+        for other in self.order:
+            olow = self._low.get(other)
+            if (olow is not None and olow[0] == "layer_norm_backward" and tuple(olow[1]) == tuple(inputs)
+                    and float(np.float32(olow[2][0])) == eps and other not in self._val):
+                siblings.setdefault(olow[2][1], other)
+        siblings.setdefault(low[2][1], node)
+        g, rows, width = self._rows_view(inputs[0])
+        x = self.contiguous(self.value(inputs[1]))
+        w = self.contiguous(self.value(inputs[2]))
+        outs = {which: self.tmp(n.shape, F32) for which, n in siblings.items()}
+        stats = self.aux(shape=(max(rows, 1) * 2,), dtype=np.float32) if 1 in outs else None
+        names = ", ".join(self._name(outs[k]) if k in outs else "_" for k in (0, 1, 2))
+        self.plan.lowered["layer_norm_backward"] = self.plan.lowered.get("layer_norm_backward", 0) + 1
+        self.add_step("layer_norm_backward", outs[min(outs)],
+                      f"layer_norm_backward({self._name(g)}, {self._name(x)}, {self._name(w)}, eps={eps!r})"
+                      f" -> ({names})", grad=g, x=x, w=w, rows=rows, width=width, eps=eps,
+                      dx=outs.get(0), dw=outs.get(1), db=outs.get(2), stats=stats)
+        for which, n in siblings.items():
+            self.set_value(n, outs[which])
 
     def _emit_all_reduce(self, node, low) -> None:
         src = self.contiguous(self.value(low[1][0]))

@@ -459,6 +459,29 @@ class CudaB200Program(CompiledProgram):
         a.out = self.ptr(step.out)
         _lib.call("cb_elementwise", ctypes.byref(a), stream)
 
+    # ------------------------------------------------------------ training lowerings
+    def _step_softmax(self, step: Step, stream: int) -> None:
+        a = step.args
+        _lib.call("cb_softmax_rows", self.ptr(a["x"]), a["rows"], a["width"], int(a["log"]), self.ptr(step.out),
+                  stream)
+
+    def _step_softmax_backward(self, step: Step, stream: int) -> None:
+        a = step.args
+        _lib.call("cb_softmax_backward_rows", self.ptr(a["grad"]), self.ptr(a["y"]), a["rows"], a["width"],
+                  int(a["log"]), self.ptr(step.out), stream)
+
+    def _step_layer_norm(self, step: Step, stream: int) -> None:
+        a = step.args
+        _lib.call("cb_layer_norm_rows", self.ptr(a["x"]), self.ptr(a["w"]), self.ptr(a["b"]), a["rows"], a["width"],
+                  a["eps"], self.ptr(step.out), stream)
+
+    def _step_layer_norm_backward(self, step: Step, stream: int) -> None:
+        a = step.args
+        opt = lambda v: None if v is None else self.ptr(v)  # noqa: E731
+        stats = None if a["stats"] is None else self._ptr[a["stats"]]
+        _lib.call("cb_layer_norm_backward_rows", self.ptr(a["grad"]), self.ptr(a["x"]), self.ptr(a["w"]), a["rows"],
+                  a["width"], a["eps"], opt(a["dx"]), opt(a["dw"]), opt(a["db"]), stats, stream)
+
     def _add_into(self, out: View, residual: View, stream: int) -> None:
         """out = residual + out (both contiguous, the same shape), in place."""
         a = _lib.ElementwiseArgs()

@@ -539,6 +539,42 @@ CB_API long long cb_gemm_rows_scratch(const cb_gemm_rows_args* args);
 CB_API long long cb_gemm_rows_counters(const cb_gemm_rows_args* args);
 CB_API int cb_gemm_rows(const cb_gemm_rows_args* args, cb_stream_t stream);
 
+/* ---- training ----------------------------------------------------------------
+ * The reference's fused lowerings of compiled training steps (lowering hints
+ * of chomikgrad/tensor.py:316-450; CuPy kernels cuda_backend.py:85-322) over
+ * the last axis of contiguous (rows, width) float32 matrices, one warp per
+ * row:
+ *   cb_softmax_rows            y = exp(x - max) / sum   (log_form: (x - max) - log(sum))
+ *   cb_softmax_backward_rows   dx = y * (g - sum(g * y)) (log_form: g - exp(y) * sum(g))
+ *   cb_layer_norm_rows         y = (x - mean) / sqrt(mean((x - mean)^2) + eps) * w + b
+ *   cb_layer_norm_backward_rows  any of dx (rows x width), dw, db (width;
+ *                              column sums over the rows, in row order);
+ *                              row_stats: rows * 2 floats of scratch, needed
+ *                              for dw
+ * cb_sgd_update: out[i] = param[i] - lr * grad[i] (the product rounded to
+ * float32 first) for up to CB_SGD_GROUP float32 tensors in one launch; out
+ * may alias param (in place).  Replaces the grouped SGD of
+ * Compiler.update_native_parameters (cuda_backend.py:471-617). */
+#define CB_SGD_GROUP 16
+typedef struct {
+  int n;
+  float lr;
+  const float* param[CB_SGD_GROUP];
+  const float* grad[CB_SGD_GROUP];
+  float* out[CB_SGD_GROUP];
+  long long count[CB_SGD_GROUP];
+} cb_sgd_group;
+CB_API int cb_softmax_rows(const float* x, long long rows, long long width, int log_form, float* out,
+                           cb_stream_t stream);
+CB_API int cb_softmax_backward_rows(const float* grad, const float* y, long long rows, long long width,
+                                    int log_form, float* out, cb_stream_t stream);
+CB_API int cb_layer_norm_rows(const float* x, const float* w, const float* b, long long rows, long long width,
+                              float eps, float* out, cb_stream_t stream);
+CB_API int cb_layer_norm_backward_rows(const float* grad, const float* x, const float* w, long long rows,
+                                       long long width, float eps, float* dx, float* dw, float* db,
+                                       float* row_stats, cb_stream_t stream);
+CB_API int cb_sgd_update(const cb_sgd_group* group, cb_stream_t stream);
+
 /* ---- tensor-parallel collectives ------------------------------------------
  * The reference is single-GPU; these serve the tensor-parallel lowering of
  * its graphs (all_reduce after the row-sharded O and down projections).  A

@@ -280,6 +280,56 @@ class PlanInterpreter:
         wm = self.read_f32(step.args["write_mask"]).reshape(-1)
         self.write(cache_v, _blend(cache, row, wm, step.args["one_minus"]))
 
+    # ------------------------------------------------------------ training lowerings
+    # what cb_softmax_rows / cb_softmax_backward_rows / cb_layer_norm_rows /
+    # cb_layer_norm_backward_rows document, in float32 over rows of `width`
+    def _rows(self, view: View, width: int) -> np.ndarray:
+        return self.read_f32(view).reshape(-1, width)
+
+    def _step_softmax(self, step: Step) -> None:
+        a = step.args
+        x = self._rows(a["x"], a["width"])
+        shifted = x - x.max(axis=-1, keepdims=True)
+        e = np.exp(shifted)
+        total = e.sum(axis=-1, keepdims=True)
+        self.write(step.out, shifted - np.log(total) if a["log"] else e / total)
+
+    def _step_softmax_backward(self, step: Step) -> None:
+        a = step.args
+        g, y = self._rows(a["grad"], a["width"]), self._rows(a["y"], a["width"])
+        if a["log"]:
+            out = g - np.exp(y) * g.sum(axis=-1, keepdims=True)
+        else:
+            out = y * (g - (g * y).sum(axis=-1, keepdims=True))
+        self.write(step.out, out)
+
+    @staticmethod
+    def _moments(x: np.ndarray, eps: float):
+        mean = x.sum(axis=-1, keepdims=True) / np.float32(x.shape[-1])
+        c = x - mean
+        return c, np.sqrt((c * c).sum(axis=-1, keepdims=True) / np.float32(x.shape[-1]) + np.float32(eps))
+
+    def _step_layer_norm(self, step: Step) -> None:
+        a = step.args
+        x = self._rows(a["x"], a["width"])
+        c, sd = self._moments(x, a["eps"])
+        self.write(step.out, c / sd * self.read_f32(a["w"]) + self.read_f32(a["b"]))
+
+    def _step_layer_norm_backward(self, step: Step) -> None:
+        a = step.args
+        width = a["width"]
+        g, x, w = self._rows(a["grad"], width), self._rows(a["x"], width), self.read_f32(a["w"])
+        c, sd = self._moments(x, a["eps"])
+        n = c / sd
+        if a["dx"] is not None:
+            gw = g * w
+            self.write(a["dx"], (gw - gw.mean(axis=-1, keepdims=True) - n * (gw * n).mean(axis=-1, keepdims=True))
+                       / sd)
+        if a["dw"] is not None:
+            self.write(a["dw"], (g * n).sum(axis=0))
+        if a["db"] is not None:
+            self.write(a["db"], g.sum(axis=0))
+
     def _step_rms_norm(self, step: Step) -> None:
         x = self.read_f32(step.args["x"])
         w = self.read_f32(step.args["w"])

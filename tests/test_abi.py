@@ -51,6 +51,7 @@ STRUCTS = {
     "cb_step_phase": _lib.StepPhase,
     "cb_decode_step_config": _lib.DecodeStepConfig,
     "cb_sample_args": _lib.SampleArgs,
+    "cb_sgd_group": _lib.SgdGroup,
 }
 
 

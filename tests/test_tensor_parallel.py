@@ -106,9 +106,13 @@ def _threaded_ranks(size: int, build: Callable[[int], list]) -> List[List[np.nda
     results: List = [None] * size
     errors: List = []
 
+    # graphs are built here, one rank after another: the reference's grad mode
+    # (no_grad) is a process-wide flag that concurrent builders would leave off
+    built = [build(rank) for rank in range(size)]
+
     def worker(rank: int) -> None:
         try:
-            outputs = build(rank)
+            outputs = built[rank]
 
             def reduce_fn(x):
                 slots[rank] = x
