@@ -1,10 +1,10 @@
 """Microbenchmarks of single kernels and of the batched decode step (needs a B200).
 
-    python -m cuda_b200.kernel_bench sdpa_tc   [--tokens 2048 --heads 32 --kv 4 --hd 64 --causal 3]
-    python -m cuda_b200.kernel_bench gemm_tc   [--m 2048 --n 5632 --k 2048]
-    python -m cuda_b200.kernel_bench sdpa_query [--batch 32 --heads 32 --kv 4 --tokens 768 --hd 64]
-    python -m cuda_b200.kernel_bench batched   [--workload tinyllama-bf16-bs32 --steps 20 --prompt 64]
-    python -m cuda_b200.kernel_bench sample    [--rows 1 --width 32000 --top-k 50]
+    python kernel_bench.py sdpa_tc   [--tokens 2048 --heads 32 --kv 4 --hd 64 --causal 3]
+    python kernel_bench.py gemm_tc   [--m 2048 --n 5632 --k 2048]
+    python kernel_bench.py sdpa_query [--batch 32 --heads 32 --kv 4 --tokens 768 --hd 64]
+    python kernel_bench.py batched   [--workload tinyllama-bf16-bs32 --steps 20 --prompt 64]
+    python kernel_bench.py sample    [--rows 1 --width 32000 --top-k 50]
 
 Each prints CUDA-event times (warm, averaged over --reps launches on the
 current stream).  ``batched`` wraps the timed graph replays in
@@ -17,9 +17,16 @@ from __future__ import annotations
 
 import argparse
 import ctypes
+from pathlib import Path
 import statistics
+import sys
 
-import numpy as np
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "baseline" / "_ref", ROOT / "chomik-grad_b200", ROOT):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
 
 
 def _timed(fn, reps: int) -> float:
@@ -39,7 +46,7 @@ def _timed(fn, reps: int) -> float:
 def _sdpa_args(q, k, v, mask, out, divisor: float):
     import torch
 
-    from . import _lib
+    from cuda_b200 import _lib
 
     a = _lib.SdpaArgs()
     for name, t in (("q", q), ("k", k), ("v", v), ("mask", mask)):
@@ -58,7 +65,7 @@ def _sdpa_args(q, k, v, mask, out, divisor: float):
 def sdpa_tc(args) -> None:
     import torch
 
-    from . import _lib
+    from cuda_b200 import _lib
 
     b, h, kv, t, hd = 1, args.heads, args.kv, args.tokens, args.hd
     q = torch.randn(b, h, t, hd, device="cuda")
@@ -82,7 +89,7 @@ def sdpa_tc(args) -> None:
 def gemm_tc(args) -> None:
     import torch
 
-    from . import _lib
+    from cuda_b200 import _lib
 
     m, n, k = args.m, args.n, args.k
     a_t = torch.randn(m, k, device="cuda")
@@ -105,7 +112,7 @@ def gemm_tc(args) -> None:
 def sdpa_query(args) -> None:
     import torch
 
-    from . import _lib
+    from cuda_b200 import _lib
 
     b, h, kv, t, hd = args.batch, args.heads, args.kv, args.tokens, args.hd
     q = torch.randn(b, h, 1, hd, device="cuda")
@@ -125,7 +132,7 @@ def sdpa_query(args) -> None:
 def sample(args) -> None:
     import torch
 
-    from . import _lib
+    from cuda_b200 import _lib
 
     rows, width = args.rows, args.width
     logits = torch.randn(rows, width, device="cuda") * 2.0
@@ -148,8 +155,8 @@ def sample(args) -> None:
 def batched(args) -> None:
     import torch
 
-    from .batched import BatchedRuntime
-    from .models import WORKLOADS, synthetic_prompt, synthetic_weights
+    from cuda_b200.batched import BatchedRuntime
+    from cuda_b200.models import WORKLOADS, synthetic_prompt, synthetic_weights
 
     wl = WORKLOADS[args.workload]
     cfg = wl.config
@@ -185,7 +192,12 @@ def main() -> None:
     parser.add_argument("--rows", type=int, default=1)
     parser.add_argument("--width", type=int, default=32000)
     parser.add_argument("--top-k", type=int, default=50)
+    parser.add_argument("--kv-cache", default="bfloat16", choices=("bfloat16", "float32"),
+                        help="batched: KV-cache storage (the compiler's kv_cache_dtype), as bench.py")
     args = parser.parse_args()
+    import os
+
+    os.environ["CUDA_B200_KV_DTYPE"] = args.kv_cache  # read when the compiler is first created
     if args.kv is None:
         args.kv = 4
     if args.tokens is None:
