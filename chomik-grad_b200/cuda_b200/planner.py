@@ -1040,6 +1040,12 @@ class Planner:
                 replace[id(mat)] = cur
                 removed.add(id(st))
                 break
+        for st in steps:  # the rest: plain row GEMMs (an O projection feeding an all-reduce, or a bf16 residual)
+            if id(st) in removed or id(st) in replace:
+                continue
+            sh = self._rows_route(st)
+            if sh is not None:
+                replace[id(st)] = rows_step(st.args["a"], [st], [sh], [st.out])
         plan.steps = [replace.get(id(st), st) for st in steps if id(st) not in removed]
         self._fuse_batched_attention()
 

@@ -276,9 +276,10 @@ def test_batched_decode_plan_fuses_into_row_gemms_and_one_attention(tiny_bf16):
     layers = cfg.num_hidden_layers
     assert kinds["decode_attention_batched"] == layers
     assert kinds["kv_write"] == kinds["rope"] == kinds["sdpa"] == 0
-    # 4 row GEMMs per layer (layer 0's O projection reads the bf16 embedding residual: kept apart) + lm_head
-    assert kinds["matmul_rows"] == 4 * layers
-    assert kinds["matmul"] == 1 and kinds["elementwise"] == 1
+    # 4 row GEMMs per layer + lm_head; layer 0's O projection reads the bf16 embedding residual, so it
+    # is a plain row GEMM and its residual add stays apart
+    assert kinds["matmul_rows"] == 4 * layers + 1
+    assert kinds["matmul"] == 0 and kinds["elementwise"] == 1
     rows = [s for s in p.steps if s.name == "matmul_rows"]
     assert sum(s.args["x_mode"] == _lib.ROWS_X_RMS for s in rows) == 2 * layers + 1
     assert sum(s.args["x_mode"] == _lib.ROWS_X_SWIGLU for s in rows) == layers
