@@ -122,8 +122,34 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   if (warp == 4) {
     if (lane == 0) {
       // ---- TMA producer: the range's chunks in order ----
-      long long i = 0;
-      for (long long f = f0; f < f1; ++f, ++i) {
+      // The weights do not depend on the previous kernel: the first ring's
+      // worth of weight chunks is issued before waiting for it (programmatic
+      // dependent launch), the x planes (written by the plane pass just
+      // before) only after.
+      auto weight_load = [&](long long f, int s) {
+        int tile = static_cast<int>(f / p.kchunks);
+        const int kx = static_cast<int>(f % p.kchunks) * kChunk;
+        int seg = 0;
+        while (seg + 1 < p.n_w && tile >= p.tiles[seg]) tile -= p.tiles[seg++];
+        const CUtensorMap* mw = seg == 0 ? &map_w0 : seg == 1 ? &map_w1 : &map_w2;
+        tma_load_2d(smem + s * G::kStage, mw, kx, tile * kWTile, full + s);
+      };
+      auto x_load = [&](long long f, int s) {
+        const int kx = static_cast<int>(f % p.kchunks) * kChunk;
+        unsigned char* st = smem + s * G::kStage;
+        tma_load_2d(st + G::kW, &map_xh, kx, 0, full + s);
+        tma_load_2d(st + G::kW + G::kX, &map_xl, kx, 0, full + s);
+      };
+      const long long pre = f1 - f0 < G::kStages ? f1 - f0 : G::kStages;
+      for (long long j = 0; j < pre; ++j) {
+        mbar_arrive_expect_tx(full + j, static_cast<uint32_t>(G::kStage));
+        weight_load(f0 + j, static_cast<int>(j));
+      }
+      pdl_wait();
+      pdl_launch_dependents();
+      for (long long j = 0; j < pre; ++j) x_load(f0 + j, static_cast<int>(j));
+      long long i = pre;
+      for (long long f = f0 + pre; f < f1; ++f, ++i) {
         const int s = static_cast<int>(i % G::kStages);
         const long long round = i / G::kStages;
         if (round > 0 && !wait_or_abort(empty + s, static_cast<uint32_t>((round - 1) & 1), abort)) {
@@ -131,16 +157,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           *abort = 1;
           break;
         }
-        int tile = static_cast<int>(f / p.kchunks);
-        const int kx = static_cast<int>(f % p.kchunks) * kChunk;
-        int seg = 0;
-        while (seg + 1 < p.n_w && tile >= p.tiles[seg]) tile -= p.tiles[seg++];
-        unsigned char* st = smem + s * G::kStage;
         mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(G::kStage));
-        const CUtensorMap* mw = seg == 0 ? &map_w0 : seg == 1 ? &map_w1 : &map_w2;
-        tma_load_2d(st, mw, kx, tile * kWTile, full + s);
-        tma_load_2d(st + G::kW, &map_xh, kx, 0, full + s);
-        tma_load_2d(st + G::kW + G::kX, &map_xl, kx, 0, full + s);
+        weight_load(f, s);
+        x_load(f, s);
       }
       // drain: every copy issued lands before the block can exit
       for (long long t = i - 1; t >= 0 && t >= i - G::kStages; --t) {
@@ -193,6 +212,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     }
   } else {
     // ---- epilogue: warps 0-3, thread = weight row of the tile ----
+    pdl_wait();  // residual, partials, counters and out: after the previous kernel
     const int r = warp * 32 + lane;
     const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     int seg_no = 0, splits_done = 0;
@@ -322,6 +342,8 @@ __device__ __forceinline__ void split_store(float v, __nv_bfloat16* hi, __nv_bfl
 // through the PLAIN or SWIGLU prologue; grid (rows, k chunks of 1024).
 __global__ void rows_planes_kernel(const void* x, int x_dtype, long long ldx, long long k, const void* x2,
                                    int x2_dtype, long long ldx2, int swiglu, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long r = blockIdx.x;
   const long long c1 = min(k, (blockIdx.y + 1) * 1024LL);
   for (long long c = blockIdx.y * 1024LL + threadIdx.x; c < c1; c += blockDim.x) {
@@ -342,6 +364,8 @@ __global__ void __launch_bounds__(256) rows_rms_planes_kernel(const void* x, int
                                                                __nv_bfloat16* hi, __nv_bfloat16* lo) {
   extern __shared__ float row[];
   __shared__ float red[8];
+  pdl_wait();
+  pdl_launch_dependents();
   const long long r = blockIdx.x;
   const int width = static_cast<int>(k);
   for (int i = threadIdx.x; i < width; i += blockDim.x) row[i] = load_as_f32(x, r * ldx + i, x_dtype);
@@ -392,14 +416,16 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
     const size_t smem = static_cast<size_t>(a.k) * sizeof(float);
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(rows_rms_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    rows_rms_planes_kernel<<<static_cast<unsigned>(a.rows), 256, smem, s>>>(a.x, a.x_dtype, a.ldx, a.k, a.norm_w,
-                                                                            a.norm_w_dtype, n, a.dt_out, hi, lo);
+    const cudaError_t e = launch(rows_rms_planes_kernel, dim3(static_cast<unsigned>(a.rows)), dim3(256), smem, s,
+                                 a.pdl != 0, a.x, a.x_dtype, a.ldx, a.k, a.norm_w, a.norm_w_dtype, n, a.dt_out, hi,
+                                 lo);
+    CB_REQUIRE(e == cudaSuccess, "cb_gemm_rows: plane pass launch failed (%s)", cudaGetErrorString(e));
   } else {
     const dim3 pgrid(static_cast<unsigned>(a.rows), static_cast<unsigned>((a.k + 1023) / 1024));
-    rows_planes_kernel<<<pgrid, 256, 0, s>>>(a.x, a.x_dtype, a.ldx, a.k, a.x2, a.x2_dtype, a.ldx2,
-                                             a.x_mode == CB_ROWS_X_SWIGLU, hi, lo);
+    const cudaError_t e = launch(rows_planes_kernel, pgrid, dim3(256), 0, s, a.pdl != 0, a.x, a.x_dtype, a.ldx, a.k,
+                                 a.x2, a.x2_dtype, a.ldx2, static_cast<int>(a.x_mode == CB_ROWS_X_SWIGLU), hi, lo);
+    CB_REQUIRE(e == cudaSuccess, "cb_gemm_rows: plane pass launch failed (%s)", cudaGetErrorString(e));
   }
-  CB_REQUIRE(cudaGetLastError() == cudaSuccess, "cb_gemm_rows: plane pass launch failed");
   CUtensorMap mw[3], mxh, mxl;
   for (int i = 0; i < 3; ++i) {
     const int j = i < a.n_w ? i : 0;
@@ -428,10 +454,9 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
   p.ldr = a.ldr;
   auto kernel = gemm_rows_kernel<NB>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
-  if (e == cudaSuccess) {
-    kernel<<<static_cast<unsigned>(pl.grid), kRowsThreads, G::kSmem, s>>>(mw[0], mw[1], mw[2], mxh, mxl, p);
-    e = cudaGetLastError();
-  }
+  if (e == cudaSuccess)
+    e = launch(kernel, dim3(static_cast<unsigned>(pl.grid)), dim3(kRowsThreads), static_cast<size_t>(G::kSmem), s,
+               a.pdl != 0, mw[0], mw[1], mw[2], mxh, mxl, p);
   if (e != cudaSuccess) {
     set_error("cb_gemm_rows: %s", cudaGetErrorString(e));
     return CB_ERR_CUDA;

@@ -201,7 +201,7 @@ class GemmRowsArgs(ctypes.Structure):
         ("dt_sq", c_int), ("dt_sum", c_int), ("dt_mean", c_int), ("dt_t", c_int), ("dt_d", c_int),
         ("dt_y", c_int), ("dt_out", c_int),
         ("x2", c_void_p), ("x2_dtype", c_int), ("ldx2", c_longlong),
-        ("residual", c_void_p), ("ldr", c_longlong),
+        ("residual", c_void_p), ("ldr", c_longlong), ("pdl", c_int),
     ]
 
 

@@ -695,6 +695,7 @@ class CudaB200Program(CompiledProgram):
         a = self._matmul_rows_args(step, self._rows_counters.data_ptr() + 4 * self._rows_counter_off[id(step)])
         a.scratch = self._gemm_scratch.data_ptr()
         a.error_flag = self._gemm_flag.data_ptr()
+        a.pdl = int(self._compiler.pdl)
         _lib.call("cb_gemm_rows", ctypes.byref(a), stream)
         self._extra_launches += 1  # the plane pass
 

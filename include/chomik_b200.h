@@ -533,6 +533,10 @@ typedef struct {
    * (llama.py:529-535); NULL: store */
   const float* residual;
   long long ldr;
+  /* 1: programmatic dependent launch -- the first stages of weight chunks
+   * stream while the previous kernel finishes (x, residual and outputs wait
+   * for it) */
+  int pdl;
 } cb_gemm_rows_args;
 enum { CB_ROWS_X_PLAIN = 0, CB_ROWS_X_RMS = 1, CB_ROWS_X_SWIGLU = 2 };
 CB_API long long cb_gemm_rows_scratch(const cb_gemm_rows_args* args);
