@@ -315,6 +315,14 @@ inline long long chunk_smem_bytes(long long group, long long hd, int kv_dtype) {
   return ((group + 2) * hd + hd) * 4 + 2 * (kAttnSplit * (hd + pad) * es + kAttnSplit * hd * es + 2 * kAttnSplit * 4);
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // Issue the copies of chunk `chunk`'s K/V rows into buffer `buf` (one commit
 // group per thread, possibly empty).
@@ -602,6 +610,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
 // arithmetic runs on the tensor cores; the chunks stream through two
 // cp.async buffers.  The last CTA of a group merges the ranges' partials in
 // range order, as above.
+constexpr int kMmaHeads = 16;  // query heads per KV head this kernel takes (the MMA's M)
 
 template <int HD>
 struct MmaSmem {
@@ -626,6 +635,34 @@ struct MmaSmem {
 
 inline long long mma_smem_bytes(long long hd) {
   return (kMmaHeads * hd + 3 * hd) * 4 + 2 * (2 * kAttnSplit * (hd + 8) * 2 + 2 * kAttnSplit * 4);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo_elem));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi_elem));
+  return a | (b << 16);
+}
+// x ~ hi + lo: hi = bf16(x), lo = bf16(x - hi), two values per register
+__device__ __forceinline__ void split_pack(float x0, float x1, uint32_t* hi, uint32_t* lo) {
+  const float h0 = __bfloat162float(__float2bfloat16_rn(x0)), h1 = __bfloat162float(__float2bfloat16_rn(x1));
+  *hi = pack_bf16(h0, h1);
+  *lo = pack_bf16(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+}
+
+__device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t* r, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t* r, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_addr(p)));
 }
 
 // The chunk's K/V rows into buffer `buf` by the warp's 32 lanes (one commit group).

@@ -200,9 +200,6 @@ __device__ __forceinline__ void attention_merge_pair_regs(const float* parts, lo
   out[1] = __fdiv_rn(a1, lsum);
 }
 
-template <int HD, bool kRegMerge>
-__device__ void attention_merge_group(const cb_decode_attention_args& a, int g, int splits, int* s_last, int tid);
-
 // Needs attention_stage_cache's shared memory (and an attn_sync after it).
 // kRegMerge = false compiles only the warp-per-head merge (fewer registers:
 // more blocks per SM for launches of many small items).
@@ -314,20 +311,10 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
   }
   if (stamps != nullptr && tid == 0) stamps[2] = stamps[3] = global_ns();
   if (!merge) return;
-  attention_merge_group<HD, kRegMerge>(a, g, splits, s_last, tid);
-}
 
-// The last item of KV group g to finish merges the group's splits in split
-// order (scratch layout: [split][head][max, sum, hd values]) and resets the
-// group's counter.  The barrier orders every thread's partial before thread
-// 0's release, whose acquire side (the last item's thread 0, then its
-// barrier) makes all partials visible there.
-template <int HD, bool kRegMerge>
-__device__ void attention_merge_group(const cb_decode_attention_args& a, int g, int splits, int* s_last, int tid) {
-  const int group = static_cast<int>(a.heads / a.kv_heads);
-  constexpr int half = HD / 2;
-  const int warp = tid >> 5, lane = tid & 31;
-  constexpr int warps = kAttnThreads / 32;
+  // merge the splits of this KV group in split order; the barrier orders every
+  // thread's partial before thread 0's release, whose acquire side (the last
+  // item's thread 0, then its barrier) makes all partials visible there
   attn_sync();
   if (tid == 0) {
     const unsigned ticket = ticket_acq_rel(a.counters + g);
@@ -375,320 +362,6 @@ __device__ void attention_merge_group(const cb_decode_attention_args& a, int g, 
     }
   }
   if (tid == 0) a.counters[g] = 0u;
-}
-
-// ---- bfloat16 MMA helpers (m16n8k16, float32 accumulation) ----------------
-// The decode attentions over bfloat16 caches put a KV group's query heads on
-// the 16 rows of an MMA (rows past the group are zero).
-constexpr int kMmaHeads = 16;
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
-  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo_elem));
-  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi_elem));
-  return a | (b << 16);
-}
-// x ~ hi + lo: hi = bf16(x), lo = bf16(x - hi), two values per register
-__device__ __forceinline__ void split_pack(float x0, float x1, uint32_t* hi, uint32_t* lo) {
-  const float h0 = __bfloat162float(__float2bfloat16_rn(x0)), h1 = __bfloat162float(__float2bfloat16_rn(x1));
-  *hi = pack_bf16(h0, h1);
-  *lo = pack_bf16(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
-}
-
-__device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t* r, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_addr(p)));
-}
-__device__ __forceinline__ void ldsm_x2_trans(uint32_t* r, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-               : "=r"(r[0]), "=r"(r[1])
-               : "r"(smem_addr(p)));
-}
-
-
-// ---- decode-step attention items over bfloat16 caches on mma.sync ---------
-// Item i of KV group g covers kStepMmaChunks consecutive 32-key chunks, one
-// per warp (warps past the context stay idle).  Before the QKV phase
-// completes, the item's chunks are staged as bfloat16 (cp.async: no
-// registers held across the phase wait).  After it: RoPE of q (the group's
-// heads as the MMA's rows) and k, the write-mask blend of each warp's chunk
-// (stored and attended rounded to bfloat16), S = Q K^T, an online softmax
-// and O = P V per warp on m16n8k16 MMAs (q and p as bf16 hi/lo planes, K and
-// V exact), the warps' states combined in shared memory into the item's
-// partial, and the group's items merged by the last one
-// (attention_merge_group).
-constexpr int kStepMmaChunks = 2;
-
-template <int HD>
-struct StepMmaSmem {
-  static constexpr int KS = HD + 8;  // bf16 row stride of K and V
-  static constexpr int kRowsBytes = kAttnSplit * KS * 2;
-  static constexpr int kBufBytes = 2 * kRowsBytes + 2 * kAttnSplit * 4;  // K, V, write mask, mask
-  float *q, *k_new, *v_new, *cs, *sn;
-  unsigned char* bufs;
-  __device__ explicit StepMmaSmem(float* smem) {
-    q = smem;                      // [16][HD]
-    k_new = q + kMmaHeads * HD;    // [HD]
-    v_new = k_new + HD;            // [HD]
-    cs = v_new + HD;               // [HD / 2]
-    sn = cs + HD / 2;              // [HD / 2]
-    bufs = reinterpret_cast<unsigned char*>(sn + HD / 2);  // [kStepMmaChunks][kBufBytes], 16-byte aligned
-  }
-  __device__ uint16_t* ks(int w) const { return reinterpret_cast<uint16_t*>(bufs + w * kBufBytes); }
-  __device__ uint16_t* vs(int w) const { return reinterpret_cast<uint16_t*>(bufs + w * kBufBytes + kRowsBytes); }
-  __device__ float* wm(int w) const { return reinterpret_cast<float*>(bufs + w * kBufBytes + 2 * kRowsBytes); }
-  __device__ float* maskv(int w) const { return wm(w) + kAttnSplit; }
-  // after the products, a warp's buffer holds its softmax state: m[16], l[16], o[16][HD]
-  __device__ float* state(int w) const { return reinterpret_cast<float*>(bufs + w * kBufBytes); }
-};
-static_assert(2 * kMmaHeads + kMmaHeads * 64 <= (2 * kAttnSplit * (64 + 8) * 2 + 2 * kAttnSplit * 4) / 4,
-              "a warp's state fits its chunk buffer");
-
-__host__ __device__ inline long long step_mma_smem_bytes(long long hd) {
-  return (kMmaHeads * hd + 3 * hd) * 4 + kStepMmaChunks * (2 * kAttnSplit * (hd + 8) * 2 + 2 * kAttnSplit * 4);
-}
-
-template <int HD>
-__device__ void attention_mma_stage(const cb_decode_attention_args& a, int g, int item, float* smem, int tid) {
-  StepMmaSmem<HD> s(smem);
-  constexpr int half = HD / 2;
-  constexpr int kUnits = HD * 2 / 16;  // 16-byte pieces per row
-  constexpr int KS = StepMmaSmem<HD>::KS;
-  const long long chunks = (a.context + kAttnSplit - 1) / kAttnSplit;
-  for (int w = 0; w < kStepMmaChunks; ++w) {
-    const long long c = static_cast<long long>(item) * kStepMmaChunks + w;
-    if (c >= chunks) break;
-    const int n = attn_rows(a, static_cast<int>(c));
-    const long long first = (static_cast<long long>(g) * a.context + c * kAttnSplit) * HD;
-    const char* kc = static_cast<const char*>(a.k_cache) + first * 2;
-    const char* vc = static_cast<const char*>(a.v_cache) + first * 2;
-    char* kd = reinterpret_cast<char*>(s.ks(w));
-    char* vd = reinterpret_cast<char*>(s.vs(w));
-    for (int e = tid; e < kAttnSplit * kUnits; e += kAttnThreads) {
-      const int r = e / kUnits, u = e % kUnits;
-      if (r < n) {
-        cp_async16(kd + r * KS * 2 + u * 16, kc + r * HD * 2 + u * 16);
-        cp_async16(vd + r * KS * 2 + u * 16, vc + r * HD * 2 + u * 16);
-      } else {  // rows past a ragged last chunk: zeros (their p is 0; 0 times a stale NaN would not be)
-        *reinterpret_cast<uint4*>(kd + r * KS * 2 + u * 16) = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(vd + r * KS * 2 + u * 16) = make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-    for (int r = tid; r < kAttnSplit; r += kAttnThreads) {
-      const long long row = c * kAttnSplit + r;
-      s.wm(w)[r] = r < n ? load_as_f32(a.write_mask, row, a.write_mask_dtype) : 0.0f;
-      s.maskv(w)[r] = r < n ? load_as_f32(a.mask, row, a.mask_dtype) : 0.0f;
-    }
-  }
-  cp_async_commit();
-  long long pos = load_index(a.position, 0, a.position_dtype);
-  if (pos < 0 || pos >= a.n_positions) {
-    if (tid == 0 && item == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_POSITION);
-    pos = pos < 0 ? 0 : a.n_positions - 1;
-  }
-  for (int j = tid; j < half; j += kAttnThreads) {
-    s.cs[j] = a.cos_table[pos * half + j];
-    s.sn[j] = a.sin_table[pos * half + j];
-  }
-}
-
-// Needs attention_mma_stage's shared memory (its copies are waited for here).
-template <int HD>
-__device__ void attention_mma_finish(const cb_decode_attention_args& a, int g, int item, int items, float* smem,
-                                     int* s_last, int tid, bool merge) {
-  StepMmaSmem<HD> s(smem);
-  constexpr int half = HD / 2;
-  constexpr int KS = StepMmaSmem<HD>::KS;
-  constexpr int kSteps = HD / 16;
-  constexpr int kTiles = HD / 8;
-  const int group = static_cast<int>(a.heads / a.kv_heads);
-  const int warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
-  cp_async_wait<0>();
-  for (int i = tid; i < kMmaHeads * half; i += kAttnThreads) {
-    const int h = i / half, j = i % half;
-    float r0 = 0.0f, r1 = 0.0f;
-    if (h < group) {
-      const float* src = a.qkv + a.q_off + (static_cast<long long>(g) * group + h) * HD;
-      const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = s.cs[j], sv = s.sn[j];
-      r0 = fmaf(-hi, sv, __fmul_rn(lo, c));
-      r1 = fmaf(hi, c, __fmul_rn(lo, sv));
-    }
-    s.q[h * HD + j] = r0;
-    s.q[h * HD + j + half] = r1;
-  }
-  for (int j = tid; j < half; j += kAttnThreads) {
-    const float* src = a.qkv + a.k_off + static_cast<long long>(g) * HD;
-    const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = s.cs[j], sv = s.sn[j];
-    s.k_new[j] = fmaf(-hi, sv, __fmul_rn(lo, c));
-    s.k_new[j + half] = fmaf(hi, c, __fmul_rn(lo, sv));
-  }
-  for (int d = tid; d < HD; d += kAttnThreads) s.v_new[d] = __ldcg(a.qkv + a.v_off + static_cast<long long>(g) * HD + d);
-  attn_sync();  // q, k_new, v_new, and every thread's staged copies
-
-  const long long chunks = (a.context + kAttnSplit - 1) / kAttnSplit;
-  const long long c = static_cast<long long>(item) * kStepMmaChunks + warp;
-  const bool active = warp < kStepMmaChunks && c < chunks;
-  if (active) {
-    const int n = attn_rows(a, static_cast<int>(c));
-    uint16_t* ks = s.ks(warp);
-    uint16_t* vs = s.vs(warp);
-    const float* wmv = s.wm(warp);
-    const float* mkv = s.maskv(warp);
-    // rows with wm != 0: the blend in float32, stored (cache and shared) rounded to bfloat16
-    const long long first = (static_cast<long long>(g) * a.context + c * kAttnSplit) * HD;
-    void* kc = kv_at(a.k_cache, first, CB_BF16);
-    void* vc = kv_at(a.v_cache, first, CB_BF16);
-    for (int e = lane; e < n * (HD / 4); e += 32) {
-      const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
-      const float wm = wmv[r];
-      if (wm == 0.0f) continue;
-      const float keep = round_to(__fsub_rn(1.0f, wm), a.one_minus_dtype);
-      const uint2 kw = *reinterpret_cast<const uint2*>(ks + r * KS + d4);
-      const uint2 vw = *reinterpret_cast<const uint2*>(vs + r * KS + d4);
-      float kf[4] = {__uint_as_float(kw.x << 16), __uint_as_float(kw.x & 0xffff0000u), __uint_as_float(kw.y << 16),
-                     __uint_as_float(kw.y & 0xffff0000u)};
-      float vf[4] = {__uint_as_float(vw.x << 16), __uint_as_float(vw.x & 0xffff0000u), __uint_as_float(vw.y << 16),
-                     __uint_as_float(vw.y & 0xffff0000u)};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        kf[i] = __fadd_rn(__fmul_rn(kf[i], keep), __fmul_rn(s.k_new[d4 + i], wm));
-        vf[i] = __fadd_rn(__fmul_rn(vf[i], keep), __fmul_rn(s.v_new[d4 + i], wm));
-      }
-      const float4 k4 = kv_store4(kc, e, CB_BF16, make_float4(kf[0], kf[1], kf[2], kf[3]));  // rounded
-      const float4 v4 = kv_store4(vc, e, CB_BF16, make_float4(vf[0], vf[1], vf[2], vf[3]));
-      *reinterpret_cast<uint2*>(ks + r * KS + d4) =
-          make_uint2((__float_as_uint(k4.x) >> 16) | (__float_as_uint(k4.y) & 0xffff0000u),
-                     (__float_as_uint(k4.z) >> 16) | (__float_as_uint(k4.w) & 0xffff0000u));
-      *reinterpret_cast<uint2*>(vs + r * KS + d4) =
-          make_uint2((__float_as_uint(v4.x) >> 16) | (__float_as_uint(v4.y) & 0xffff0000u),
-                     (__float_as_uint(v4.z) >> 16) | (__float_as_uint(v4.w) & 0xffff0000u));
-    }
-    __syncwarp();
-    uint32_t qh[kSteps][4], ql[kSteps][4];
-#pragma unroll
-    for (int k = 0; k < kSteps; ++k) {
-      const int col = 16 * k + 2 * tig;
-      split_pack(s.q[gid * HD + col], s.q[gid * HD + col + 1], &qh[k][0], &ql[k][0]);
-      split_pack(s.q[(gid + 8) * HD + col], s.q[(gid + 8) * HD + col + 1], &qh[k][1], &ql[k][1]);
-      split_pack(s.q[gid * HD + col + 8], s.q[gid * HD + col + 9], &qh[k][2], &ql[k][2]);
-      split_pack(s.q[(gid + 8) * HD + col + 8], s.q[(gid + 8) * HD + col + 9], &qh[k][3], &ql[k][3]);
-    }
-    const bool row1 = gid + 8 < group;
-    float sc[4][4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      sc[t][0] = sc[t][1] = sc[t][2] = sc[t][3] = 0.0f;
-#pragma unroll
-      for (int k = 0; k < kSteps; ++k) {
-        uint32_t kb[2];
-        ldsm_x2(kb, ks + (8 * t + (lane & 7)) * KS + 16 * k + ((lane >> 3) & 1) * 8);
-        mma_16816(sc[t], qh[k], kb[0], kb[1]);
-        mma_16816(sc[t], ql[k], kb[0], kb[1]);
-      }
-    }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int key = 8 * t + 2 * tig + j;
-        const bool in = key < n;
-        const float mk = in ? mkv[key] : 0.0f;
-        sc[t][j] = in ? __fadd_rn(__fdiv_rn(sc[t][j], a.divisor), mk) : -INFINITY;
-        sc[t][2 + j] = row1 ? (in ? __fadd_rn(__fdiv_rn(sc[t][2 + j], a.divisor), mk) : -INFINITY) : 0.0f;
-        mx0 = fmaxf(mx0, sc[t][j]);
-        mx1 = fmaxf(mx1, sc[t][2 + j]);
-      }
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    float sum0 = 0.0f, sum1 = 0.0f;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        sc[t][j] = expf(sc[t][j] - mx0);
-        sc[t][2 + j] = expf(sc[t][2 + j] - mx1);
-        sum0 += sc[t][j];
-        sum1 += sc[t][2 + j];
-      }
-    }
-    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
-    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
-    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
-    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
-    float o[kTiles][4];
-#pragma unroll
-    for (int t = 0; t < kTiles; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      uint32_t ph[4], pl[4];
-      split_pack(sc[2 * kk][0], sc[2 * kk][1], &ph[0], &pl[0]);
-      split_pack(sc[2 * kk][2], sc[2 * kk][3], &ph[1], &pl[1]);
-      split_pack(sc[2 * kk + 1][0], sc[2 * kk + 1][1], &ph[2], &pl[2]);
-      split_pack(sc[2 * kk + 1][2], sc[2 * kk + 1][3], &ph[3], &pl[3]);
-#pragma unroll
-      for (int t = 0; t < kTiles; ++t) {
-        uint32_t vb[2];
-        ldsm_x2_trans(vb, vs + (16 * kk + (lane & 15)) * KS + 8 * t);
-        mma_16816(o[t], ph, vb[0], vb[1]);
-        mma_16816(o[t], pl, vb[0], vb[1]);
-      }
-    }
-    __syncwarp();  // every lane's K / V reads are done: the buffer takes the state
-    float* st = s.state(warp);  // m[16], l[16], o[16][HD]
-    if (tig == 0) {
-      st[gid] = mx0;
-      st[kMmaHeads + gid] = sum0;
-      st[gid + 8] = row1 ? mx1 : -INFINITY;
-      st[kMmaHeads + gid + 8] = row1 ? sum1 : 0.0f;
-    }
-#pragma unroll
-    for (int t = 0; t < kTiles; ++t) {
-      *reinterpret_cast<float2*>(st + 2 * kMmaHeads + gid * HD + 8 * t + 2 * tig) = make_float2(o[t][0], o[t][1]);
-      *reinterpret_cast<float2*>(st + 2 * kMmaHeads + (gid + 8) * HD + 8 * t + 2 * tig) =
-          make_float2(o[t][2], o[t][3]);
-    }
-  }
-  attn_sync();
-  // the item's partial per head: the warps' states combined (max first, then the rescaled sums)
-  const int live = static_cast<int>(chunks - static_cast<long long>(item) * kStepMmaChunks < kStepMmaChunks
-                                         ? chunks - static_cast<long long>(item) * kStepMmaChunks
-                                         : kStepMmaChunks);
-  for (int i = tid; i < group * (HD + 2); i += kAttnThreads) {
-    const int h = i / (HD + 2), e = i % (HD + 2);
-    float m = -INFINITY;
-    for (int w = 0; w < live; ++w) m = fmaxf(m, s.state(w)[h]);
-    float v = 0.0f;
-    if (e == 0) {
-      v = m;
-    } else {
-      for (int w = 0; w < live; ++w) {
-        const float* st = s.state(w);
-        const float sc = expf(st[h] - m);
-        v = fmaf(e == 1 ? st[kMmaHeads + h] : st[2 * kMmaHeads + h * HD + e - 2], sc, v);
-      }
-    }
-    a.scratch[(static_cast<long long>(item) * a.heads + static_cast<long long>(g) * group + h) * (HD + 2) + e] = v;
-  }
-  if (!merge) return;
-  attention_merge_group<HD, true>(a, g, items, s_last, tid);
 }
 
 // The whole item: stage, then finish with the in-kernel merge.

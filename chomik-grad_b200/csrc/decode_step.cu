@@ -623,12 +623,8 @@ __device__ void gemv_phase(const PhaseDesc& P, const StagePre<Chunk<WT>::kElems>
   }
 }
 
-// kMma: the attention phases run bfloat16 MMA items (attn_core.cuh); a
-// separate instantiation, so neither attention path adds to the other's
-// register pressure.
-template <typename WT, int HD, bool kMma>
+template <typename WT, int HD>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepParams S) {
-  constexpr bool kMmaItems = kMma && HD <= 64;
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ StepShared sh;
   __shared__ PhaseDesc sh_desc[2];
@@ -800,11 +796,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     if (gemv) {
       if (block_stages(P, blockIdx.x) > 0) stage_pre<WT>(P, pre, S.error_flag, tid);
     } else if (blockIdx.x < P.items) {
-      const int grp = static_cast<int>(blockIdx.x / P.splits), split = static_cast<int>(blockIdx.x % P.splits);
-      if constexpr (kMmaItems)
-        attention_mma_stage<HD>(P.at, grp, split, attn_smem, tid);
-      else
-        attention_stage_cache<HD>(P.at, grp, split, attn_smem, tid);
+      attention_stage_cache<HD>(P.at, static_cast<int>(blockIdx.x / P.splits),
+                                static_cast<int>(blockIdx.x % P.splits), attn_smem, tid);
     }
     if (tid == 0) stamp(S, p, kStampWait);
     if (p > 0) {
@@ -825,15 +818,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         const int grp = static_cast<int>(it / P.splits), split = static_cast<int>(it % P.splits);
         if (it != blockIdx.x) {  // later items of this block: stage after the previous one
           attn_sync();
-          if constexpr (kMmaItems)
-            attention_mma_stage<HD>(P.at, grp, split, attn_smem, tid);
-          else
-            attention_stage_cache<HD>(P.at, grp, split, attn_smem, tid);
+          attention_stage_cache<HD>(P.at, grp, split, attn_smem, tid);
           attn_sync();
-        }
-        if constexpr (kMmaItems) {
-          attention_mma_finish<HD>(P.at, grp, split, P.splits, attn_smem, &sh.last, tid, P.merge_in_kernel != 0);
-          continue;
         }
         unsigned long long* item_stamps =
             S.timeline != nullptr && it == blockIdx.x
@@ -887,7 +873,7 @@ int launch_step(const StepParams& S, const cb_decode_step_config& c, cudaStream_
   cudaError_t e = cudaSuccess;
 #define CB_STEP_CASE(WT, HD)                                                                          \
   {                                                                                                  \
-    auto kernel = c.attn_mma ? decode_step_kernel<WT, HD, true> : decode_step_kernel<WT, HD, false>;  \
+    auto kernel = decode_step_kernel<WT, HD>;                                                         \
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(c.smem)); \
     if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, kernel, S);                                   \
   }
@@ -944,7 +930,7 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
   CB_REQUIRE(aligned16(table), "decode step: table must be 16-byte aligned");
   const int grid = sm_count();
   std::vector<PhaseDesc> desc(static_cast<size_t>(n_phases));
-  int w_dtype = -1, head_size = 0, n_gemv = 0, attn_mma = -1;
+  int w_dtype = -1, head_size = 0, n_gemv = 0;
   long long max_row = 0, x_bytes = 1024;
   for (int i = 0; i < n_phases; ++i) {
     const cb_step_phase& ph = phases[i];
@@ -1021,19 +1007,8 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
       CB_REQUIRE(t.kv_dtype == CB_F32 || t.kv_dtype == CB_BF16,
                  "decode step phase %d: caches must be float32 or bfloat16", i);
       CB_REQUIRE(t.split == 0 || t.split == kAttnSplit, "decode step phase %d: split must be %d", i, kAttnSplit);
-      // bfloat16 caches (head size <= 64, groups up to 16 heads): MMA items of kStepMmaChunks chunks
-      const bool mma = t.kv_dtype == CB_BF16 && t.head_size <= 64 && t.heads / t.kv_heads <= kMmaHeads &&
-                       (flags & CB_STEP_ATTN_SPLIT32) == 0;
-      CB_REQUIRE(attn_mma < 0 || attn_mma == static_cast<int>(mma),
-                 "decode step phase %d: attention phases mix float32 and bfloat16 caches", i);
-      attn_mma = mma ? 1 : 0;
-      const long long chunks = (t.context + kAttnSplit - 1) / kAttnSplit;
-      const long long splits = mma ? (chunks + kStepMmaChunks - 1) / kStepMmaChunks : chunks;
-      const long long bytes = mma ? step_mma_smem_bytes(t.head_size)
-                                  : attn_smem_floats(t.heads / t.kv_heads, t.head_size) * 4;
-      if (mma)
-        CB_REQUIRE(aligned16(t.k_cache) && aligned16(t.v_cache), "decode step phase %d: caches must be 16-byte aligned",
-                   i);
+      const long long splits = (t.context + kAttnSplit - 1) / kAttnSplit;
+      const long long bytes = attn_smem_floats(t.heads / t.kv_heads, t.head_size) * 4;
       if (bytes > x_bytes) x_bytes = bytes;
       d.at = t;
       d.splits = static_cast<int>(splits);
@@ -1127,7 +1102,6 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
   config->lane_inflight = 2;
   config->quiet_window = 1;
   config->test_withhold = 0;
-  config->attn_mma = attn_mma > 0 ? 1 : 0;
   config->timeline = nullptr;
   return CB_OK;
 }

@@ -31,7 +31,6 @@ EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
 PHASE_GEMV, PHASE_ATTENTION = 0, 1
 X_PLAIN, X_SILU_MUL = 0, 1
 STEP_MERGE_IN_STAGE = 1
-STEP_ATTN_SPLIT32 = 2
 
 LL8 = c_longlong * MAX_DIMS
 
@@ -228,7 +227,7 @@ class DecodeStepConfig(ctypes.Structure):
                 ("slot_bytes", c_longlong), ("x_bytes", c_longlong), ("norm_bytes", c_longlong),
                 ("smem", c_longlong),
                 ("prefetch_bytes", c_longlong), ("lane_inflight", c_int), ("quiet_window", c_int),
-                ("test_withhold", c_int), ("attn_mma", c_int),
+                ("test_withhold", c_int),
                 ("timeline", c_void_p)]
 
 

@@ -64,8 +64,6 @@ class CudaB200Compiler(Compiler):
         # attention phase (measured faster on TinyLlama); set
         # CUDA_B200_STEP_MERGE=stage to merge them in the O projection's x staging
         self.step_flags = _lib.STEP_MERGE_IN_STAGE if os.environ.get("CUDA_B200_STEP_MERGE") == "stage" else 0
-        if os.environ.get("CUDA_B200_STEP_ATTN") == "split32":  # the float32 caches' items over bfloat16 too
-            self.step_flags |= _lib.STEP_ATTN_SPLIT32
         self.use_graphs = use_graphs
         self.pdl = pdl
         self.fuse_decode = fuse_decode

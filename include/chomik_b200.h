@@ -683,10 +683,6 @@ typedef struct {
    * runs out (after about 1 s) and the step stops with CB_FLAG_WAIT_PHASE;
    * the caller then zeroes the counters, as after any wait that gave up */
   int test_withhold;
-  /* set by prepare: 1 when the attention phases run bfloat16 MMA items
-   * (bfloat16 caches, head size <= 64, up to 16 query heads per KV head,
-   * CB_STEP_ATTN_SPLIT32 not given), 0 for the 32-key float32 items */
-  int attn_mma;
   /* optional (NULL = off): grid * n_phases * 12 nanosecond stamps
    * (%globaltimer) per block and phase, for tuning the schedule: wait begins,
    * wait ends, x staged, phase done, producer issued the phase's last stage,
@@ -698,9 +694,8 @@ typedef struct {
 CB_API long long cb_decode_step_table_bytes(int n_phases);
 /* prepare flags: merge an attention phase's splits while the next phase (the
  * O projection reading its output) stages x, instead of in the attention
- * phase itself (the output is then never written); over bfloat16 caches,
- * the 32-key items of the float32 caches instead of the MMA items */
-enum { CB_STEP_MERGE_IN_STAGE = 1, CB_STEP_ATTN_SPLIT32 = 2 };
+ * phase itself (the output is then never written) */
+enum { CB_STEP_MERGE_IN_STAGE = 1 };
 /* Check the phases and write their schedule to `table` (device memory of
  * cb_decode_step_table_bytes bytes; synchronous, so not during stream
  * capture).  The table holds the phases' pointers: prepare again when any
