@@ -595,352 +595,6 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
   if (tid == 0) a.counters[g] = 0u;
 }
 
-// ---- batched decode attention over bfloat16 caches on mma.sync -----------
-// One warp per CTA, a range of 32-key chunks of one (sequence, KV head).  The
-// group's query heads are the rows of an m16n8k16 MMA (up to 16 heads; rows
-// past the group are zero): S = Q K^T per chunk takes K straight from the
-// bfloat16 rows in shared memory (ldmatrix) and Q as two bfloat16 planes
-// (hi = bf16(q), lo = bf16(q - hi): q to about 2^-16), accumulating in
-// float32; the online softmax runs on the S fragments (each thread holds
-// eight keys of two heads); O += P V takes P from the same fragments, again
-// as hi / lo planes, and V by transposing ldmatrix.  K and V values are
-// bfloat16 already, so both products see them exactly.  Compared with the
-// CUDA-core kernel above (one warp per head, every warp converting every
-// K and V value of the chunk), the conversions happen once and the
-// arithmetic runs on the tensor cores; the chunks stream through two
-// cp.async buffers.  The last CTA of a group merges the ranges' partials in
-// range order, as above.
-constexpr int kMmaHeads = 16;  // query heads per KV head this kernel takes (the MMA's M)
-
-template <int HD>
-struct MmaSmem {
-  static constexpr int KS = HD + 8;  // bf16 row stride of K and V: 16-byte rows, conflict-free ldmatrix
-  static constexpr int kRowsBytes = kAttnSplit * KS * 2;
-  static constexpr int kBufBytes = 2 * kRowsBytes + 2 * kAttnSplit * 4;  // K, V, write mask, mask
-  float *q, *k_new, *v_new, *cs, *sn;
-  unsigned char* bufs;
-  __device__ explicit MmaSmem(float* smem) {
-    q = smem;                      // [16][HD]
-    k_new = q + kMmaHeads * HD;    // [HD]
-    v_new = k_new + HD;            // [HD]
-    cs = v_new + HD;               // [HD / 2]
-    sn = cs + HD / 2;              // [HD / 2]
-    bufs = reinterpret_cast<unsigned char*>(sn + HD / 2);  // [2][kBufBytes], 16-byte aligned
-  }
-  __device__ uint16_t* ks(int b) const { return reinterpret_cast<uint16_t*>(bufs + b * kBufBytes); }
-  __device__ uint16_t* vs(int b) const { return reinterpret_cast<uint16_t*>(bufs + b * kBufBytes + kRowsBytes); }
-  __device__ float* wm(int b) const { return reinterpret_cast<float*>(bufs + b * kBufBytes + 2 * kRowsBytes); }
-  __device__ float* maskv(int b) const { return wm(b) + kAttnSplit; }
-};
-
-inline long long mma_smem_bytes(long long hd) {
-  return (kMmaHeads * hd + 3 * hd) * 4 + 2 * (2 * kAttnSplit * (hd + 8) * 2 + 2 * kAttnSplit * 4);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
-  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo_elem));
-  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi_elem));
-  return a | (b << 16);
-}
-// x ~ hi + lo: hi = bf16(x), lo = bf16(x - hi), two values per register
-__device__ __forceinline__ void split_pack(float x0, float x1, uint32_t* hi, uint32_t* lo) {
-  const float h0 = __bfloat162float(__float2bfloat16_rn(x0)), h1 = __bfloat162float(__float2bfloat16_rn(x1));
-  *hi = pack_bf16(h0, h1);
-  *lo = pack_bf16(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
-}
-
-__device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t* r, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_addr(p)));
-}
-__device__ __forceinline__ void ldsm_x2_trans(uint32_t* r, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-               : "=r"(r[0]), "=r"(r[1])
-               : "r"(smem_addr(p)));
-}
-
-// The chunk's K/V rows into buffer `buf` by the warp's 32 lanes (one commit group).
-template <int HD>
-__device__ __forceinline__ void mma_stage_chunk(const cb_decode_attention_args& a, const MmaSmem<HD>& s, int buf, int g,
-                                                long long chunk, int lane) {
-  constexpr int kUnits = HD * 2 / 16;  // 16-byte pieces per row
-  const long long lo = chunk * kAttnSplit;
-  const int n = attn_rows(a, static_cast<int>(chunk));
-  const long long first = (static_cast<long long>(g) * a.context + lo) * HD;
-  const char* kc = static_cast<const char*>(kv_at(static_cast<const void*>(a.k_cache), first, CB_BF16));
-  const char* vc = static_cast<const char*>(kv_at(static_cast<const void*>(a.v_cache), first, CB_BF16));
-  char* kd = reinterpret_cast<char*>(s.ks(buf));
-  char* vd = reinterpret_cast<char*>(s.vs(buf));
-  for (int e = lane; e < n * kUnits; e += 32) {
-    const int r = e / kUnits, u = e % kUnits;
-    cp_async16(kd + r * MmaSmem<HD>::KS * 2 + u * 16, kc + r * HD * 2 + u * 16);
-    cp_async16(vd + r * MmaSmem<HD>::KS * 2 + u * 16, vc + r * HD * 2 + u * 16);
-  }
-  // rows past a ragged last chunk: zeros (their p is 0, and 0 times a stale NaN would not be)
-  for (int e = lane; e < (kAttnSplit - n) * kUnits; e += 32) {
-    const int r = n + e / kUnits, u = e % kUnits;
-    *reinterpret_cast<uint4*>(kd + r * MmaSmem<HD>::KS * 2 + u * 16) = make_uint4(0u, 0u, 0u, 0u);
-    *reinterpret_cast<uint4*>(vd + r * MmaSmem<HD>::KS * 2 + u * 16) = make_uint4(0u, 0u, 0u, 0u);
-  }
-  cp_async_commit();
-}
-
-template <int HD>
-__global__ void __launch_bounds__(32) decode_attention_mma_kernel(const cb_decode_attention_args args,
-                                                                  long long qkv_stride, int chunks_per_cta) {
-  extern __shared__ float smem[];
-  cb_decode_attention_args a = args;
-  const long long b = blockIdx.z;
-  const int g = static_cast<int>(blockIdx.y);
-  const int lane = threadIdx.x;
-  const int gid = lane >> 2, tig = lane & 3;
-  constexpr int half = HD / 2;
-  constexpr int KS = MmaSmem<HD>::KS;
-  constexpr int kSteps = HD / 16;  // K steps of S = Q K^T
-  constexpr int kTiles = HD / 8;   // n tiles of O
-  const long long kv_rows = a.kv_heads * a.context * a.head_size;
-  a.qkv += b * qkv_stride;
-  a.k_cache = kv_at(a.k_cache, b * kv_rows, CB_BF16);
-  a.v_cache = kv_at(a.v_cache, b * kv_rows, CB_BF16);
-  a.out += b * a.heads * a.head_size;
-  a.scratch += b * static_cast<long long>(gridDim.x) * a.heads * (a.head_size + 2);
-  a.counters += b * a.kv_heads;
-  const int group = static_cast<int>(a.heads / a.kv_heads);
-  MmaSmem<HD> s(smem);
-  const long long splits = (a.context + kAttnSplit - 1) / kAttnSplit;
-  const long long c0 = static_cast<long long>(blockIdx.x) * chunks_per_cta;
-  const long long c1 = c0 + chunks_per_cta < splits ? c0 + chunks_per_cta : splits;
-
-  mma_stage_chunk<HD>(a, s, 0, g, c0, lane);
-  float wm_next, mk_next;
-  chunk_masks(a, c0, lane, &wm_next, &mk_next);
-  long long pos = load_index(a.position, 0, a.position_dtype);
-  if (pos < 0 || pos >= a.n_positions) {
-    if (lane == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_POSITION);
-    pos = pos < 0 ? 0 : a.n_positions - 1;
-  }
-  for (int j = lane; j < half; j += 32) {
-    s.cs[j] = a.cos_table[pos * half + j];
-    s.sn[j] = a.sin_table[pos * half + j];
-  }
-  __syncwarp();
-  for (int i = lane; i < kMmaHeads * half; i += 32) {
-    const int h = i / half, j = i % half;
-    float r0 = 0.0f, r1 = 0.0f;
-    if (h < group) {
-      const float* src = a.qkv + a.q_off + (static_cast<long long>(g) * group + h) * HD;
-      const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = s.cs[j], sv = s.sn[j];
-      r0 = fmaf(-hi, sv, __fmul_rn(lo, c));
-      r1 = fmaf(hi, c, __fmul_rn(lo, sv));
-    }
-    s.q[h * HD + j] = r0;
-    s.q[h * HD + j + half] = r1;
-  }
-  for (int j = lane; j < half; j += 32) {
-    const float* src = a.qkv + a.k_off + static_cast<long long>(g) * HD;
-    const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = s.cs[j], sv = s.sn[j];
-    s.k_new[j] = fmaf(-hi, sv, __fmul_rn(lo, c));
-    s.k_new[j + half] = fmaf(hi, c, __fmul_rn(lo, sv));
-  }
-  for (int d = lane; d < HD; d += 32) s.v_new[d] = __ldcg(a.qkv + a.v_off + static_cast<long long>(g) * HD + d);
-  s.wm(0)[lane] = wm_next;
-  s.maskv(0)[lane] = mk_next;
-  __syncwarp();
-
-  // Q as A fragments (rows gid and gid + 8, columns 16 ks + 2 tig (+1) and + 8), hi and lo planes
-  uint32_t qh[kSteps][4], ql[kSteps][4];
-#pragma unroll
-  for (int ks = 0; ks < kSteps; ++ks) {
-    const int c = 16 * ks + 2 * tig;
-    split_pack(s.q[gid * HD + c], s.q[gid * HD + c + 1], &qh[ks][0], &ql[ks][0]);
-    split_pack(s.q[(gid + 8) * HD + c], s.q[(gid + 8) * HD + c + 1], &qh[ks][1], &ql[ks][1]);
-    split_pack(s.q[gid * HD + c + 8], s.q[gid * HD + c + 9], &qh[ks][2], &ql[ks][2]);
-    split_pack(s.q[(gid + 8) * HD + c + 8], s.q[(gid + 8) * HD + c + 9], &qh[ks][3], &ql[ks][3]);
-  }
-  const bool row1 = gid + 8 < group;  // the fragment's second head row is a real head
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-  float o[kTiles][4];
-#pragma unroll
-  for (int t = 0; t < kTiles; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
-
-  for (long long c = c0; c < c1; ++c) {
-    const int buf = static_cast<int>((c - c0) & 1);
-    const bool more = c + 1 < c1;
-    if (more) {
-      mma_stage_chunk<HD>(a, s, buf ^ 1, g, c + 1, lane);
-      chunk_masks(a, c + 1, lane, &wm_next, &mk_next);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncwarp();  // every lane's copies of chunk c are visible
-
-    // rows with wm != 0: the blend in float32, stored (cache and shared) rounded to bfloat16
-    const long long lo_pos = c * kAttnSplit;
-    const int n = attn_rows(a, static_cast<int>(c));
-    const long long first = (static_cast<long long>(g) * a.context + lo_pos) * HD;
-    void* kc = kv_at(a.k_cache, first, CB_BF16);
-    void* vc = kv_at(a.v_cache, first, CB_BF16);
-    uint16_t* ks = s.ks(buf);
-    uint16_t* vs = s.vs(buf);
-    const float* wmv = s.wm(buf);
-    const float* mkv = s.maskv(buf);
-    for (int e = lane; e < n * (HD / 4); e += 32) {
-      const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
-      const float wm = wmv[r];
-      if (wm == 0.0f) continue;
-      const float keep = round_to(__fsub_rn(1.0f, wm), a.one_minus_dtype);
-      float4 kv = smem_load4(ks + r * KS + d4);
-      float4 vv = smem_load4(vs + r * KS + d4);
-      float* kf = &kv.x;
-      float* vf = &vv.x;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        kf[i] = __fadd_rn(__fmul_rn(kf[i], keep), __fmul_rn(s.k_new[d4 + i], wm));
-        vf[i] = __fadd_rn(__fmul_rn(vf[i], keep), __fmul_rn(s.v_new[d4 + i], wm));
-      }
-      kv = kv_store4(kc, e, CB_BF16, kv);  // rounded, and attended as stored
-      vv = kv_store4(vc, e, CB_BF16, vv);
-      smem_store4(ks + r * KS + d4, kv);
-      smem_store4(vs + r * KS + d4, vv);
-    }
-    __syncwarp();
-
-    // S = Q K^T: four n tiles of 8 keys; thread holds keys 8 t + 2 tig (+1) of heads gid, gid + 8
-    float sc[4][4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      sc[t][0] = sc[t][1] = sc[t][2] = sc[t][3] = 0.0f;
-#pragma unroll
-      for (int k = 0; k < kSteps; ++k) {
-        uint32_t kb[2];  // lanes 0-7: key rows 8 t + i at column 16 k; lanes 8-15: column 16 k + 8
-        ldsm_x2(kb, ks + (8 * t + (lane & 7)) * KS + 16 * k + ((lane >> 3) & 1) * 8);
-        mma_16816(sc[t], qh[k], kb[0], kb[1]);
-        mma_16816(sc[t], ql[k], kb[0], kb[1]);
-      }
-    }
-    // x = s / divisor + mask (keys past the chunk: -inf); padding head rows stay finite
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int key = 8 * t + 2 * tig + j;
-        const bool in = key < n;
-        const float mk = in ? mkv[key] : 0.0f;
-        sc[t][j] = in ? __fadd_rn(__fdiv_rn(sc[t][j], a.divisor), mk) : -INFINITY;
-        sc[t][2 + j] = row1 ? (in ? __fadd_rn(__fdiv_rn(sc[t][2 + j], a.divisor), mk) : -INFINITY) : 0.0f;
-        mx0 = fmaxf(mx0, sc[t][j]);
-        mx1 = fmaxf(mx1, sc[t][2 + j]);
-      }
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-    const float scale0 = expf(m0 - n0), scale1 = expf(m1 - n1);  // 0 on the first chunk (m = -inf)
-    float sum0 = 0.0f, sum1 = 0.0f;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        sc[t][j] = expf(sc[t][j] - n0);
-        sc[t][2 + j] = expf(sc[t][2 + j] - n1);
-        sum0 += sc[t][j];
-        sum1 += sc[t][2 + j];
-      }
-    }
-    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
-    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
-    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
-    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
-    l0 = fmaf(l0, scale0, sum0);
-    l1 = fmaf(l1, scale1, sum1);
-    m0 = n0;
-    m1 = n1;
-#pragma unroll
-    for (int t = 0; t < kTiles; ++t) {
-      o[t][0] *= scale0;
-      o[t][1] *= scale0;
-      o[t][2] *= scale1;
-      o[t][3] *= scale1;
-    }
-    // O += P V: P's A fragments are the S fragments of n tiles 2 kk and 2 kk + 1
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      uint32_t ph[4], pl[4];
-      split_pack(sc[2 * kk][0], sc[2 * kk][1], &ph[0], &pl[0]);
-      split_pack(sc[2 * kk][2], sc[2 * kk][3], &ph[1], &pl[1]);
-      split_pack(sc[2 * kk + 1][0], sc[2 * kk + 1][1], &ph[2], &pl[2]);
-      split_pack(sc[2 * kk + 1][2], sc[2 * kk + 1][3], &ph[3], &pl[3]);
-#pragma unroll
-      for (int t = 0; t < kTiles; ++t) {
-        uint32_t vb[2];  // lanes 0-7: key rows 16 kk + i; lanes 8-15: rows 16 kk + 8 + i; columns 8 t
-        ldsm_x2_trans(vb, vs + (16 * kk + (lane & 15)) * KS + 8 * t);
-        mma_16816(o[t], ph, vb[0], vb[1]);
-        mma_16816(o[t], pl, vb[0], vb[1]);
-      }
-    }
-    if (more) {  // the next chunk's masks (its buffer's previous chunk was read two iterations ago)
-      s.wm(buf ^ 1)[lane] = wm_next;
-      s.maskv(buf ^ 1)[lane] = mk_next;
-    }
-    __syncwarp();  // buffer `buf` is refilled by the copies issued for chunk c + 2
-  }
-
-  // this CTA's partials: (max, sum, unnormalised output) per head
-  const long long r = blockIdx.x;
-  if (gid < group) {
-    float* part = a.scratch + (r * a.heads + static_cast<long long>(g) * group + gid) * (HD + 2);
-#pragma unroll
-    for (int t = 0; t < kTiles; ++t) *reinterpret_cast<float2*>(part + 2 + 8 * t + 2 * tig) = make_float2(o[t][0], o[t][1]);
-    if (tig == 0) {
-      part[0] = m0;
-      part[1] = l0;
-    }
-  }
-  if (row1) {
-    float* part = a.scratch + (r * a.heads + static_cast<long long>(g) * group + gid + 8) * (HD + 2);
-#pragma unroll
-    for (int t = 0; t < kTiles; ++t) *reinterpret_cast<float2*>(part + 2 + 8 * t + 2 * tig) = make_float2(o[t][2], o[t][3]);
-    if (tig == 0) {
-      part[0] = m1;
-      part[1] = l1;
-    }
-  }
-  // the last CTA of the group merges the ranges in range order
-  __syncwarp();
-  int last = 0;
-  if (lane == 0) last = ticket_acq_rel(a.counters + g) == static_cast<unsigned>(gridDim.x - 1);
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
-  __syncwarp();
-  const int parts = static_cast<int>(gridDim.x);
-  const long long stride = a.heads * (HD + 2);
-  for (int i = lane; i < group * HD; i += 32) {
-    const int h = i / HD, d = i % HD;
-    const long long head = static_cast<long long>(g) * group + h;
-    const float* base = a.scratch + head * (HD + 2);
-    float m = -INFINITY;
-    for (int sp = 0; sp < parts; ++sp) m = fmaxf(m, __ldcg(base + sp * stride));
-    float l = 0.0f, acc = 0.0f;
-    for (int sp = 0; sp < parts; ++sp) {
-      const float sc = expf(__ldcg(base + sp * stride) - m);
-      l = fmaf(__ldcg(base + sp * stride + 1), sc, l);
-      acc = fmaf(__ldcg(base + sp * stride + 2 + d), sc, acc);
-    }
-    a.out[head * HD + d] = __fdiv_rn(acc, l);
-  }
-  if (lane == 0) a.counters[g] = 0u;
-}
-
 }  // namespace
 }  // namespace cb
 
@@ -970,43 +624,11 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   const long long group = a->heads / a->kv_heads;
   CB_REQUIRE(group <= 32, "decode attention: at most 32 query heads per KV head (got %lld)", group);
   CB_REQUIRE(a->kv_dtype == CB_F32 || a->kv_dtype == CB_BF16, "decode attention: caches must be float32 or bfloat16");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const long long groups = batch * a->kv_heads;
-  if (a->kv_dtype == CB_BF16 && group <= kMmaHeads && a->head_size <= 128) {
-    // bfloat16 caches: one warp per CTA, about eight CTAs per SM over the (range, KV head, sequence) grid
-    long long per_group = 8LL * sm_count() / groups;
-    if (per_group < 1) per_group = 1;
-    if (per_group > splits) per_group = splits;
-    const long long chunks = (splits + per_group - 1) / per_group;
-    const long long ctas = (splits + chunks - 1) / chunks;
-    const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(a->kv_heads), static_cast<unsigned>(batch));
-    const size_t msmem = static_cast<size_t>(mma_smem_bytes(a->head_size));
-    cudaError_t e = cudaSuccess;
-#define CB_MMA_CASE(HD)                                                                                  \
-  case HD: {                                                                                             \
-    e = cudaFuncSetAttribute(decode_attention_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             static_cast<int>(msmem));                                                   \
-    if (e == cudaSuccess)                                                                                \
-      decode_attention_mma_kernel<HD><<<grid, 32, msmem, s>>>(*a, qkv_stride, static_cast<int>(chunks));   \
-    break;                                                                                               \
-  }
-    switch (a->head_size) {
-      CB_MMA_CASE(32)
-      CB_MMA_CASE(64)
-      CB_MMA_CASE(128)
-      default: break;
-    }
-#undef CB_MMA_CASE
-    if (e != cudaSuccess) {
-      set_error("cb_decode_attention_batched: %s", cudaGetErrorString(e));
-      return CB_ERR_CUDA;
-    }
-    return check_launch("cb_decode_attention_batched");
-  }
   const size_t smem = static_cast<size_t>(chunk_smem_bytes(group, a->head_size, a->kv_dtype));
   CB_REQUIRE(smem <= 200 * 1024, "decode attention: too many query heads per KV head");
   // about one wave of resident CTAs (4 per SM): each CTA takes a range of
   // consecutive chunks of its (sequence, KV head)
+  const long long groups = batch * a->kv_heads;
   long long per_group = 4LL * sm_count() / groups;
   if (per_group < 1) per_group = 1;
   if (per_group > splits) per_group = splits;
@@ -1014,6 +636,7 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   const long long ctas = (splits + chunks - 1) / chunks;
   const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(a->kv_heads), static_cast<unsigned>(batch));
   const int per_cta = static_cast<int>(chunks);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
 #define CB_BATCHED_CASE(HD, HPW)                                                                          \
   {                                                                                                       \
