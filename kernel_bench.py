@@ -160,7 +160,15 @@ def batched(args) -> None:
 
     wl = WORKLOADS[args.workload]
     cfg = wl.config
-    rt = BatchedRuntime(cfg, synthetic_weights(cfg, dtype=wl.np_dtype), batch=wl.batch)
+    if cfg.hidden_size >= 4096:  # Llama-3-8B shape: weights drawn on the GPU, the TP = 1 runtime (as bench.py)
+        from cuda_b200 import tensor_parallel as tp
+        from cuda_b200.models import bfloat16, device_weights
+
+        layout = tp.shard_layout(cfg, 1, 0)
+        rt = tp.TensorParallelRuntime(cfg, device_weights(cfg, device=torch.device("cuda", 0), layout=layout), layout,
+                                      batch=wl.batch, dtype=bfloat16())
+    else:
+        rt = BatchedRuntime(cfg, synthetic_weights(cfg, dtype=wl.np_dtype), batch=wl.batch)
     prompts = [list(p) for p in synthetic_prompt(cfg, args.prompt, batch=wl.batch)]
     tokens, caches = rt.prefill_batch(prompts, wl.context)
     rt.decode_batch_on_device(tokens, args.prompt, wl.context, caches, 4)
