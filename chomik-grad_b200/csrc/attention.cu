@@ -326,7 +326,7 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // Issue the copies of chunk `chunk`'s K/V rows into buffer `buf` (one commit
 // group per thread, possibly empty).
-template <int HD, typename KT>
+template <int HD, typename KT, int NT>
 __device__ __forceinline__ void stage_chunk(const cb_decode_attention_args& a, const ChunkSmem<HD, KT>& s, int buf,
                                             int g, long long chunk, int tid) {
   constexpr int kUnits = HD * static_cast<int>(sizeof(KT)) / 16;  // 16-byte pieces per row
@@ -338,7 +338,7 @@ __device__ __forceinline__ void stage_chunk(const cb_decode_attention_args& a, c
   const char* vc = static_cast<const char*>(kv_at(static_cast<const void*>(a.v_cache), first, KvTraits<KT>::kDtype));
   char* kd = reinterpret_cast<char*>(s.ks(buf));
   char* vd = reinterpret_cast<char*>(s.vs(buf));
-  for (int e = tid; e < n * kUnits; e += kAttnThreads) {
+  for (int e = tid; e < n * kUnits; e += NT) {
     const int r = e / kUnits, u = e % kUnits;
     cp_async16(kd + r * ChunkSmem<HD, KT>::KS * kEs + u * 16, kc + r * HD * kEs + u * 16);
     cp_async16(vd + r * HD * kEs + u * 16, vc + r * HD * kEs + u * 16);
@@ -356,8 +356,10 @@ __device__ __forceinline__ void chunk_masks(const cb_decode_attention_args& a, l
   *mk = in ? load_as_f32(a.mask, r, a.mask_dtype) : 0.0f;
 }
 
-template <int HD, int HPW, typename KT>  // HPW: query heads per warp (group <= 8 * HPW); KT: K/V element type
-__global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kernel(const cb_decode_attention_args args,
+// NT: threads per CTA (one warp per query head of the group, HPW heads per warp; 128 threads for groups
+// of up to four heads, so more CTAs fit an SM)
+template <int HD, int HPW, typename KT, int NT>  // HPW: query heads per warp (group <= NT / 32 * HPW); KT: K/V element type
+__global__ void __launch_bounds__(NT, 1024 / NT) decode_attention_batched_kernel(const cb_decode_attention_args args,
                                                                                    long long qkv_stride,
                                                                                    int chunks_per_cta) {
   extern __shared__ float smem[];
@@ -366,7 +368,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
   const long long b = blockIdx.z;
   const int g = static_cast<int>(blockIdx.y);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int warps = kAttnThreads / 32;
+  constexpr int warps = NT / 32;
   constexpr int half = HD / 2;
   constexpr int KS = ChunkSmem<HD, KT>::KS;
   constexpr int kDt = KvTraits<KT>::kDtype;
@@ -385,7 +387,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
   const long long c1 = c0 + chunks_per_cta < splits ? c0 + chunks_per_cta : splits;
 
   // the first chunk's copies and mask values overlap the RoPE row and q/k/v loads
-  stage_chunk<HD, KT>(a, s, 0, g, c0, tid);
+  stage_chunk<HD, KT, NT>(a, s, 0, g, c0, tid);
   float wm_next, mk_next;
   chunk_masks(a, c0, tid, &wm_next, &mk_next);
   long long pos = load_index(a.position, 0, a.position_dtype);
@@ -393,25 +395,25 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
     if (tid == 0 && blockIdx.x == 0 && a.error_flag != nullptr) atomicExch(a.error_flag, CB_FLAG_POSITION);
     pos = pos < 0 ? 0 : a.n_positions - 1;
   }
-  for (int j = tid; j < half; j += kAttnThreads) {
+  for (int j = tid; j < half; j += NT) {
     s.cs[j] = a.cos_table[pos * half + j];
     s.sn[j] = a.sin_table[pos * half + j];
   }
-  attn_sync();
-  for (int i = tid; i < group * half; i += kAttnThreads) {
+  __syncthreads();
+  for (int i = tid; i < group * half; i += NT) {
     const int h = i / half, j = i % half;
     const float* src = a.qkv + a.q_off + (static_cast<long long>(g) * group + h) * HD;
     const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = s.cs[j], sv = s.sn[j];
     s.q_rot[h * HD + j] = fmaf(-hi, sv, __fmul_rn(lo, c));
     s.q_rot[h * HD + j + half] = fmaf(hi, c, __fmul_rn(lo, sv));
   }
-  for (int j = tid; j < half; j += kAttnThreads) {
+  for (int j = tid; j < half; j += NT) {
     const float* src = a.qkv + a.k_off + static_cast<long long>(g) * HD;
     const float lo = __ldcg(src + j), hi = __ldcg(src + j + half), c = s.cs[j], sv = s.sn[j];
     s.k_new[j] = fmaf(-hi, sv, __fmul_rn(lo, c));
     s.k_new[j + half] = fmaf(hi, c, __fmul_rn(lo, sv));
   }
-  for (int d = tid; d < HD; d += kAttnThreads) s.v_new[d] = __ldcg(a.qkv + a.v_off + static_cast<long long>(g) * HD + d);
+  for (int d = tid; d < HD; d += NT) s.v_new[d] = __ldcg(a.qkv + a.v_off + static_cast<long long>(g) * HD + d);
   if (tid < kAttnSplit) {
     s.wm(0)[tid] = wm_next;
     s.maskv(0)[tid] = mk_next;
@@ -431,13 +433,13 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
     const int buf = static_cast<int>((c - c0) & 1);
     const bool more = c + 1 < c1;
     if (more) {
-      stage_chunk<HD, KT>(a, s, buf ^ 1, g, c + 1, tid);
+      stage_chunk<HD, KT, NT>(a, s, buf ^ 1, g, c + 1, tid);
       chunk_masks(a, c + 1, tid, &wm_next, &mk_next);  // stored after this chunk's scores
       cp_async_wait<1>();  // this thread's copies of chunk c have landed
     } else {
       cp_async_wait<0>();
     }
-    attn_sync();  // every thread's copies of chunk c (and, first time round, q/k/v) are visible
+    __syncthreads();  // every thread's copies of chunk c (and, first time round, q/k/v) are visible
 
     // rows with wm != 0 get the blend, in shared memory and in the cache
     const long long lo_pos = c * kAttnSplit;
@@ -447,7 +449,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
     void* vc = kv_at(a.v_cache, first, kDt);
     KT* ks = s.ks(buf);
     KT* vs = s.vs(buf);
-    for (int e = tid; e < n * (HD / 4); e += kAttnThreads) {
+    for (int e = tid; e < n * (HD / 4); e += NT) {
       const int r = e / (HD / 4), d4 = (e % (HD / 4)) * 4;
       const float wm = s.wm(buf)[r];
       if (wm == 0.0f) continue;
@@ -466,7 +468,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
       smem_store4(ks + r * KS + d4, kv);
       smem_store4(vs + r * HD + d4, vv);
     }
-    attn_sync();
+    __syncthreads();
 
     // one warp per query head: scores with lane = position, then p @ v with
     // lane = two dims, folded into the head's running state
@@ -538,7 +540,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
       s.wm(buf ^ 1)[tid] = wm_next;
       s.maskv(buf ^ 1)[tid] = mk_next;
     }
-    attn_sync();  // buffer `buf` is refilled by the copies issued for chunk c + 2
+    __syncthreads();  // buffer `buf` is refilled by the copies issued for chunk c + 2
   }
 
   // this CTA's partial per head: (max, sum, unnormalised output)
@@ -562,10 +564,10 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_batched_kern
   // barrier orders every thread's partial before thread 0's release, whose
   // acquire side (the last CTA's thread 0, then its barrier) makes them
   // visible there
-  attn_sync();
+  __syncthreads();
   const int parts = static_cast<int>(gridDim.x);
   if (tid == 0) s_last = ticket_acq_rel(a.counters + g) == static_cast<unsigned>(parts - 1);
-  attn_sync();
+  __syncthreads();
   if (!s_last) return;
   const long long stride = a.heads * (HD + 2);
   for (int h = warp; h < group; h += warps) {
@@ -629,7 +631,8 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   // about one wave of resident CTAs (4 per SM): each CTA takes a range of
   // consecutive chunks of its (sequence, KV head)
   const long long groups = batch * a->kv_heads;
-  long long per_group = 4LL * sm_count() / groups;
+  const bool narrow = group <= 4;  // 128-thread CTAs, twice as many per SM
+  long long per_group = (narrow ? 8LL : 4LL) * sm_count() / groups;
   if (per_group < 1) per_group = 1;
   if (per_group > splits) per_group = splits;
   const long long chunks = (splits + per_group - 1) / per_group;
@@ -640,10 +643,13 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   cudaError_t e = cudaSuccess;
 #define CB_BATCHED_CASE(HD, HPW)                                                                          \
   {                                                                                                       \
-    auto kernel = a->kv_dtype == CB_BF16 ? decode_attention_batched_kernel<HD, HPW, uint16_t>            \
-                                         : decode_attention_batched_kernel<HD, HPW, float>;               \
+    auto kernel = a->kv_dtype == CB_BF16                                                                \
+                      ? (narrow ? decode_attention_batched_kernel<HD, HPW, uint16_t, 128>                \
+                                : decode_attention_batched_kernel<HD, HPW, uint16_t, 256>)               \
+                      : (narrow ? decode_attention_batched_kernel<HD, HPW, float, 128>                   \
+                                : decode_attention_batched_kernel<HD, HPW, float, 256>);                 \
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
-    if (e == cudaSuccess) kernel<<<grid, kAttnThreads, smem, s>>>(*a, qkv_stride, per_cta);               \
+    if (e == cudaSuccess) kernel<<<grid, narrow ? 128 : 256, smem, s>>>(*a, qkv_stride, per_cta);          \
   }
 #define CB_BATCHED_HD(HD)            \
   case HD:                           \

@@ -356,14 +356,14 @@ __global__ void rows_planes_kernel(const void* x, int x_dtype, long long ldx, lo
   }
 }
 
-// RMS prologue: one block per row; the row is staged in shared memory, its
+// RMS prologue: one block per row (256 to 1024 threads); the row is staged in shared memory, its
 // sum of squares reduced as cb_rmsnorm reduces it, then normalised, rounded
 // to dt_out and split into the planes.
-__global__ void __launch_bounds__(256) rows_rms_planes_kernel(const void* x, int x_dtype, long long ldx, long long k,
+__global__ void __launch_bounds__(1024) rows_rms_planes_kernel(const void* x, int x_dtype, long long ldx, long long k,
                                                                const void* w, int w_dtype, NormSpec n, int dt_out,
                                                                __nv_bfloat16* hi, __nv_bfloat16* lo) {
   extern __shared__ float row[];
-  __shared__ float red[8];
+  __shared__ float red[32];
   pdl_wait();
   pdl_launch_dependents();
   const long long r = blockIdx.x;
@@ -416,7 +416,9 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
     const size_t smem = static_cast<size_t>(a.k) * sizeof(float);
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(rows_rms_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    const cudaError_t e = launch(rows_rms_planes_kernel, dim3(static_cast<unsigned>(a.rows)), dim3(256), smem, s,
+    // one block per row, up to 1024 threads: a few elements per thread (the row's chain is the cost)
+    const unsigned threads = static_cast<unsigned>(a.k >= 4096 ? 1024 : a.k >= 2048 ? 512 : 256);
+    const cudaError_t e = launch(rows_rms_planes_kernel, dim3(static_cast<unsigned>(a.rows)), dim3(threads), smem, s,
                                  a.pdl != 0, a.x, a.x_dtype, a.ldx, a.k, a.norm_w, a.norm_w_dtype, n, a.dt_out, hi,
                                  lo);
     CB_REQUIRE(e == cudaSuccess, "cb_gemm_rows: plane pass launch failed (%s)", cudaGetErrorString(e));
