@@ -470,70 +470,105 @@ __global__ void __launch_bounds__(NT, 1024 / NT) decode_attention_batched_kernel
     }
     __syncthreads();
 
-    // one warp per query head: scores with lane = position, then p @ v with
-    // lane = two dims, folded into the head's running state
+    // a warp's HPW query heads: scores with lane = position (each K row
+    // loaded and converted once for all of them), then p @ v with lane = two
+    // dims (each V pair loaded once), folded into every head's running state
+    float x[HPW];
 #pragma unroll
-    for (int k = 0; k < HPW; ++k) {
-      const int h = warp + k * warps;
-      if (h >= group) break;
-      float x = -INFINITY;
-      if (lane < n) {
-        const float4* q = reinterpret_cast<const float4*>(s.q_rot + h * HD);
-        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-        if constexpr (sizeof(KT) == 4) {
-          const float4* kr = reinterpret_cast<const float4*>(ks + lane * KS);
+    for (int k = 0; k < HPW; ++k) x[k] = -INFINITY;
+    if (lane < n) {
+      float sacc[HPW][4];
 #pragma unroll
-          for (int d = 0; d < HD / 4; ++d) {
-            const float4 qa = q[d], ka = kr[d];
-            s0 = fmaf(qa.x, ka.x, s0);
-            s1 = fmaf(qa.y, ka.y, s1);
-            s2 = fmaf(qa.z, ka.z, s2);
-            s3 = fmaf(qa.w, ka.w, s3);
-          }
-        } else {  // eight bfloat16 K values per 16-byte load, in the same accumulation order
-          const uint4* kr = reinterpret_cast<const uint4*>(ks + lane * KS);
+      for (int k = 0; k < HPW; ++k) sacc[k][0] = sacc[k][1] = sacc[k][2] = sacc[k][3] = 0.0f;
+      if constexpr (sizeof(KT) == 4) {
+        const float4* kr = reinterpret_cast<const float4*>(ks + lane * KS);
 #pragma unroll
-          for (int d = 0; d < HD / 8; ++d) {
-            const uint4 w = kr[d];
-            const float4 qa = q[2 * d], qb = q[2 * d + 1];
-            s0 = fmaf(qa.x, __uint_as_float(w.x << 16), s0);
-            s1 = fmaf(qa.y, __uint_as_float(w.x & 0xffff0000u), s1);
-            s2 = fmaf(qa.z, __uint_as_float(w.y << 16), s2);
-            s3 = fmaf(qa.w, __uint_as_float(w.y & 0xffff0000u), s3);
-            s0 = fmaf(qb.x, __uint_as_float(w.z << 16), s0);
-            s1 = fmaf(qb.y, __uint_as_float(w.z & 0xffff0000u), s1);
-            s2 = fmaf(qb.z, __uint_as_float(w.w << 16), s2);
-            s3 = fmaf(qb.w, __uint_as_float(w.w & 0xffff0000u), s3);
+        for (int d = 0; d < HD / 4; ++d) {
+          const float4 ka = kr[d];
+#pragma unroll
+          for (int k = 0; k < HPW; ++k) {
+            if (warp + k * warps >= group) continue;
+            const float4 qa = reinterpret_cast<const float4*>(s.q_rot + (warp + k * warps) * HD)[d];
+            sacc[k][0] = fmaf(qa.x, ka.x, sacc[k][0]);
+            sacc[k][1] = fmaf(qa.y, ka.y, sacc[k][1]);
+            sacc[k][2] = fmaf(qa.z, ka.z, sacc[k][2]);
+            sacc[k][3] = fmaf(qa.w, ka.w, sacc[k][3]);
           }
         }
-        x = __fadd_rn(__fdiv_rn((s0 + s1) + (s2 + s3), a.divisor), s.maskv(buf)[lane]);
-      }
-      const float mn = fmaxf(m_run[k], warp_max(x));
-      const float scale = expf(m_run[k] - mn);  // 0 on the first chunk (running max -inf)
-      const float p = lane < n ? expf(x - mn) : 0.0f;
-      l_run[k] = fmaf(l_run[k], scale, warp_sum(p));
-      m_run[k] = mn;
+      } else {  // eight bfloat16 K values per 16-byte load, in the same accumulation order
+        const uint4* kr = reinterpret_cast<const uint4*>(ks + lane * KS);
 #pragma unroll
-      for (int i = 0; i < kPairs; ++i) {
-        const int d = i * 64 + 2 * lane;
-        const bool mine = d < HD;
-        float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
-        for (int j = 0; j < n; j += 2) {  // every lane shuffles; rows j < n only are read
-          const float p0 = __shfl_sync(0xffffffffu, p, j);
-          const float p1 = __shfl_sync(0xffffffffu, p, j + 1);
-          if (mine) {
-            const float2 v0 = smem_load2(vs + j * HD + d);
-            a0.x = fmaf(p0, v0.x, a0.x);
-            a0.y = fmaf(p0, v0.y, a0.y);
-            if (j + 1 < n) {
-              const float2 v1 = smem_load2(vs + (j + 1) * HD + d);
-              a1.x = fmaf(p1, v1.x, a1.x);
-              a1.y = fmaf(p1, v1.y, a1.y);
+        for (int d = 0; d < HD / 8; ++d) {
+          const uint4 w = kr[d];
+          const float k0 = __uint_as_float(w.x << 16), k1 = __uint_as_float(w.x & 0xffff0000u);
+          const float k2 = __uint_as_float(w.y << 16), k3 = __uint_as_float(w.y & 0xffff0000u);
+          const float k4 = __uint_as_float(w.z << 16), k5 = __uint_as_float(w.z & 0xffff0000u);
+          const float k6 = __uint_as_float(w.w << 16), k7 = __uint_as_float(w.w & 0xffff0000u);
+#pragma unroll
+          for (int k = 0; k < HPW; ++k) {
+            if (warp + k * warps >= group) continue;
+            const float4* q = reinterpret_cast<const float4*>(s.q_rot + (warp + k * warps) * HD);
+            const float4 qa = q[2 * d], qb = q[2 * d + 1];
+            sacc[k][0] = fmaf(qa.x, k0, sacc[k][0]);
+            sacc[k][1] = fmaf(qa.y, k1, sacc[k][1]);
+            sacc[k][2] = fmaf(qa.z, k2, sacc[k][2]);
+            sacc[k][3] = fmaf(qa.w, k3, sacc[k][3]);
+            sacc[k][0] = fmaf(qb.x, k4, sacc[k][0]);
+            sacc[k][1] = fmaf(qb.y, k5, sacc[k][1]);
+            sacc[k][2] = fmaf(qb.z, k6, sacc[k][2]);
+            sacc[k][3] = fmaf(qb.w, k7, sacc[k][3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < HPW; ++k)
+        x[k] = __fadd_rn(__fdiv_rn((sacc[k][0] + sacc[k][1]) + (sacc[k][2] + sacc[k][3]), a.divisor),
+                         s.maskv(buf)[lane]);
+    }
+    float p[HPW], scale[HPW];
+#pragma unroll
+    for (int k = 0; k < HPW; ++k) {
+      const float mn = fmaxf(m_run[k], warp_max(x[k]));
+      scale[k] = expf(m_run[k] - mn);  // 0 on the first chunk (running max -inf)
+      p[k] = lane < n ? expf(x[k] - mn) : 0.0f;
+      l_run[k] = fmaf(l_run[k], scale[k], warp_sum(p[k]));
+      m_run[k] = mn;
+    }
+#pragma unroll
+    for (int i = 0; i < kPairs; ++i) {
+      const int d = i * 64 + 2 * lane;
+      const bool mine = d < HD;
+      float2 a0[HPW], a1[HPW];
+#pragma unroll
+      for (int k = 0; k < HPW; ++k) a0[k] = a1[k] = make_float2(0.0f, 0.0f);
+      for (int j = 0; j < n; j += 2) {  // every lane shuffles; rows j < n only are read
+        float p0[HPW], p1[HPW];
+#pragma unroll
+        for (int k = 0; k < HPW; ++k) {
+          p0[k] = __shfl_sync(0xffffffffu, p[k], j);
+          p1[k] = __shfl_sync(0xffffffffu, p[k], j + 1);
+        }
+        if (mine) {
+          const float2 v0 = smem_load2(vs + j * HD + d);
+#pragma unroll
+          for (int k = 0; k < HPW; ++k) {
+            a0[k].x = fmaf(p0[k], v0.x, a0[k].x);
+            a0[k].y = fmaf(p0[k], v0.y, a0[k].y);
+          }
+          if (j + 1 < n) {
+            const float2 v1 = smem_load2(vs + (j + 1) * HD + d);
+#pragma unroll
+            for (int k = 0; k < HPW; ++k) {
+              a1[k].x = fmaf(p1[k], v1.x, a1[k].x);
+              a1[k].y = fmaf(p1[k], v1.y, a1[k].y);
             }
           }
         }
-        acc[k][i].x = fmaf(acc[k][i].x, scale, a0.x + a1.x);
-        acc[k][i].y = fmaf(acc[k][i].y, scale, a0.y + a1.y);
+      }
+#pragma unroll
+      for (int k = 0; k < HPW; ++k) {
+        acc[k][i].x = fmaf(acc[k][i].x, scale[k], a0[k].x + a1[k].x);
+        acc[k][i].y = fmaf(acc[k][i].y, scale[k], a0[k].y + a1[k].y);
       }
     }
     if (more && tid < kAttnSplit) {
@@ -631,7 +666,7 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   // about one wave of resident CTAs (4 per SM): each CTA takes a range of
   // consecutive chunks of its (sequence, KV head)
   const long long groups = batch * a->kv_heads;
-  const bool narrow = group <= 4;  // 128-thread CTAs, twice as many per SM
+  const bool narrow = group <= 8;  // 128-thread CTAs (two heads per warp past four), twice as many per SM
   long long per_group = (narrow ? 8LL : 4LL) * sm_count() / groups;
   if (per_group < 1) per_group = 1;
   if (per_group > splits) per_group = splits;
@@ -653,7 +688,7 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   }
 #define CB_BATCHED_HD(HD)            \
   case HD:                           \
-    if (group <= 8)                  \
+    if (group <= 4)                  \
       CB_BATCHED_CASE(HD, 1)         \
     else if (group <= 16)            \
       CB_BATCHED_CASE(HD, 2)         \
