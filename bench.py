@@ -337,7 +337,9 @@ def prefill_measurement(rt, cfg, rank: int, world: int, steps: int, warmup: int)
     tokens = wl.batch * wl.prompt_tokens * steps * world
     first_tokens = [rt.device.argmax(x) for x in logits]
     flops = prefill_flops(cfg, wl.prompt_tokens) * wl.batch * steps * world
-    peak = json.loads(PEAKS.read_text())["bf16_tflops"] if PEAKS.exists() else 1590.0
+    # the group's peak: every rank prefills its own prompts (replicas), so the
+    # whole job's FLOP/s is measured against world x one B200's peak
+    peak = (json.loads(PEAKS.read_text())["bf16_tflops"] if PEAKS.exists() else 1590.0) * world
     achieved = flops / (ms / 1000.0) / 1e12
     program = rt._prefill[(wl.prompt_tokens, context)][0]
     return {"workload": wl.name, "value": tokens / (ms / 1000.0), "unit": "tokens/s",
