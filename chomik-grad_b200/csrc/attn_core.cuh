@@ -104,6 +104,9 @@ __device__ void attention_stage_cache(const cb_decode_attention_args& a, int g, 
     *reinterpret_cast<float4*>(s.ks + r * AttnSmem<HD>::KS + d4) = kv;
     *reinterpret_cast<float4*>(s.vs + r * HD + d4) = vv;
   }
+  // V rows past a short last split are zeros: p @ v runs a fixed number of
+  // rows, and 0 * 0 adds nothing
+  for (int e = n * HD + tid; e < kAttnSplit * HD; e += kAttnThreads) s.vs[e] = 0.0f;
   for (int r = tid; r < n; r += kAttnThreads) {
     s.wm[r] = load_as_f32(a.write_mask, lo_pos + r, a.write_mask_dtype);
     s.maskv[r] = load_as_f32(a.mask, lo_pos + r, a.mask_dtype);
@@ -288,18 +291,19 @@ __device__ void attention_finish(const cb_decode_attention_args& a, int g, int s
       const int d = d0 + 2 * lane;
       const bool mine = d < HD;
       float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-      for (int j = 0; j < n; j += 2) {  // every lane shuffles; rows j < n only are read
+      // every row of the split's slot: p is 0 at lanes >= n and those V rows
+      // are zeros, so the sums equal the sums over the n rows
+#pragma unroll
+      for (int j = 0; j < kAttnSplit; j += 2) {
         const float p0 = __shfl_sync(0xffffffffu, p, j);
         const float p1 = __shfl_sync(0xffffffffu, p, j + 1);
         if (mine) {
           const float2 v0 = *reinterpret_cast<const float2*>(s.vs + j * HD + d);
+          const float2 v1 = *reinterpret_cast<const float2*>(s.vs + (j + 1) * HD + d);
           acc0.x = fmaf(p0, v0.x, acc0.x);
           acc0.y = fmaf(p0, v0.y, acc0.y);
-          if (j + 1 < n) {
-            const float2 v1 = *reinterpret_cast<const float2*>(s.vs + (j + 1) * HD + d);
-            acc1.x = fmaf(p1, v1.x, acc1.x);
-            acc1.y = fmaf(p1, v1.y, acc1.y);
-          }
+          acc1.x = fmaf(p1, v1.x, acc1.x);
+          acc1.y = fmaf(p1, v1.y, acc1.y);
         }
       }
       if (mine) *reinterpret_cast<float2*>(part + 2 + d) = make_float2(acc0.x + acc1.x, acc0.y + acc1.y);

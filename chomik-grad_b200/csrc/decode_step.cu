@@ -61,6 +61,7 @@ struct alignas(16) PhaseDesc {
   long long merge_heads;
   const float* merge_parts;  // kXMerge: the attention phase's split partials
   long long units, per_cta, row_bytes, items;
+  long long cta0;  // GEMV: blocks [0, cta0) have no rows of this phase (see the prepare step)
   // Norm weights staged in shared memory (two slots, bulk copies): this
   // phase's ordinal among such phases (-1: read from global memory), and the
   // copy this phase's start issues -- the NEXT staged phase's weights.
@@ -70,6 +71,13 @@ struct alignas(16) PhaseDesc {
   long long next_norm_bytes;
   const void* first_norm_w;  // phase 0 only: the copy issued at kernel start
   long long first_norm_bytes;
+  // L2 prefetch of the NEXT phase's attention cache rows (set on the phase
+  // before an attention phase): item i = blockIdx.x reads rows
+  // [split * kAttnSplit, ...) of KV head i / pf_splits in both caches.
+  const void* pf_k;
+  const void* pf_v;
+  long long pf_context, pf_row_bytes;
+  int pf_items, pf_splits;
   cb_gemv_args g;
   cb_decode_attention_args at;
 };
@@ -190,7 +198,8 @@ __device__ bool wait_loud(const int* quiet, const int* stop) {
 }
 
 __device__ __forceinline__ void unit_range(const PhaseDesc& P, long long cta, long long* u0, long long* u1) {
-  long long a = cta * P.per_cta, b = a + P.per_cta;
+  const long long c = cta - P.cta0;
+  const long long a = c < 0 ? P.units : c * P.per_cta, b = a + P.per_cta;
   *u0 = a < P.units ? a : P.units;
   *u1 = b < P.units ? b : P.units;
 }
@@ -678,7 +687,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
           }
           prefetch_rows(S.phases[q], blockIdx.x, S.prefetch_bytes);
         }
-        const long long lo = static_cast<long long>(blockIdx.x) * per_cta;
+        const long long c = static_cast<long long>(blockIdx.x) - Pp->cta0;
+        const long long lo = c < 0 ? units : c * per_cta;
         const long long u0 = lo < units ? lo : units;
         const long long u1 = lo + per_cta < units ? lo + per_cta : units;
         // block-local rows j: its units in order, or (SwiGLU) its gate rows then its up rows
@@ -788,6 +798,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
       bulk_load(norm_smem + slot * S.norm_bytes, P.next_norm_w, static_cast<uint32_t>(P.next_norm_bytes),
                 norm_bar + slot);
       ++norm_issued;
+    }
+    // the next phase's attention item reads its K/V cache rows right after
+    // this phase: fetch them into L2 now, off every critical path
+    if (tid == 32 && blockIdx.x < P.pf_items) {
+      const long long grp = blockIdx.x / P.pf_splits, lo = (blockIdx.x % P.pf_splits) * kAttnSplit;
+      const long long rows = P.pf_context - lo < kAttnSplit ? P.pf_context - lo : kAttnSplit;
+      const long long off = (grp * P.pf_context + lo) * P.pf_row_bytes;
+      prefetch_l2(static_cast<const char*>(P.pf_k) + off, static_cast<uint32_t>(rows * P.pf_row_bytes));
+      prefetch_l2(static_cast<const char*>(P.pf_v) + off, static_cast<uint32_t>(rows * P.pf_row_bytes));
     }
     // before the wait: everything that does not depend on phase p-1
     if (tid == 0 && S.quiet_window) *reinterpret_cast<volatile int*>(&sh.quiet) = 1;
@@ -1019,6 +1038,28 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
     }
   }
   CB_REQUIRE(n_gemv > 0, "decode step: no GEMV phase");
+  // The phase before an attention phase (its q/k/v projection): the blocks
+  // that run attention items get none of its rows, so they stage their
+  // items' cache rows while the other blocks multiply, and the attention
+  // starts as soon as q/k/v are complete.  Its cache rows are prefetched
+  // into L2 at that phase's start.
+  for (int i = 1; i < n_phases; ++i) {
+    const PhaseDesc& at = desc[static_cast<size_t>(i)];
+    PhaseDesc& before = desc[static_cast<size_t>(i) - 1];
+    if (at.kind != CB_PHASE_ATTENTION) continue;
+    if (before.kind == CB_PHASE_GEMV && before.paired == 0 && at.items <= grid / 2) {
+      before.cta0 = at.items;
+      before.per_cta = (before.units + (grid - at.items) - 1) / (grid - at.items);
+    }
+    const long long row_bytes = at.at.head_size * (at.at.kv_dtype == CB_BF16 ? 2 : 4);
+    if (row_bytes % 16 != 0 || !aligned16(at.at.k_cache) || !aligned16(at.at.v_cache)) continue;
+    before.pf_k = at.at.k_cache;
+    before.pf_v = at.at.v_cache;
+    before.pf_context = at.at.context;
+    before.pf_row_bytes = row_bytes;
+    before.pf_items = at.items < grid ? static_cast<int>(at.items) : grid;
+    before.pf_splits = at.splits;
+  }
   // With CB_STEP_MERGE_IN_STAGE, an attention output read only by the next
   // phase's x (the O projection) is never materialised: that phase merges
   // the split partials while staging.  Otherwise the attention phase merges.
@@ -1100,7 +1141,7 @@ int cb_decode_step_prepare(const cb_step_phase* phases, int n_phases, void* tabl
   config->smem = kStepSlots * slot_bytes + x_bytes + 2 * norm_bytes + bar_bytes;
   config->prefetch_bytes = kPrefetchDefault;
   config->lane_inflight = 2;
-  config->quiet_window = 1;
+  config->quiet_window = 0;  // measured: streaming on through the staging window is faster
   config->test_withhold = 0;
   config->timeline = nullptr;
   return CB_OK;

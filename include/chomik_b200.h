@@ -674,9 +674,9 @@ typedef struct {
   /* ring copies each producer lane keeps in flight (1 or 2; prepare sets 2):
    * fewer queue less data ahead of the consumers' latency-critical loads */
   int lane_inflight;
-  /* 1 (prepare's default): from the start of a phase's wait until its x is
-   * staged, issue no new ring copies, so the latency-critical loads of that
-   * window do not queue behind bulk data; 0: keep streaming */
+  /* 1: from the start of a phase's wait until its x is staged, issue no new
+   * ring copies, so the latency-critical loads of that window do not queue
+   * behind bulk data; 0 (prepare's default): keep streaming */
   int quiet_window;
   /* tests only (0 = off): 1 + the index of a block that withholds its
    * arrival after the first phase, so every block's wait for that phase
