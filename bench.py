@@ -307,9 +307,10 @@ def prefill_flops(cfg, tokens: int) -> float:
 def prefill_measurement(rt, cfg, rank: int, world: int, steps: int, warmup: int) -> dict:
     """Prefill-heavy config: 8 prompts of 2048 tokens per step, one greedy token each.
 
-    Each prompt is one run of the compiled prefill program (the reference's
-    LlamaForCausalLM.prefill is batch 1); the output token is the argmax of its
-    logits.  Timed with CUDA events on the launching stream, max over ranks.
+    The 8 prompts run as one program (``LlamaRuntime.prefill_batched``: the
+    reference's prefill graph with its batch dimension, every Linear one GEMM
+    over all 16384 rows); the output tokens are the argmax of each prompt's
+    logits row.  Timed with CUDA events on the launching stream, max over ranks.
     """
     import torch
 
@@ -320,7 +321,7 @@ def prefill_measurement(rt, cfg, rank: int, world: int, steps: int, warmup: int)
     context = wl.prompt_tokens
 
     def one_step():
-        return [rt.prefill(p, context)[0] for p in prompts]
+        return rt.prefill_batched(prompts, context)[0]
 
     for _ in range(max(warmup, 1)):
         one_step()
@@ -335,20 +336,20 @@ def prefill_measurement(rt, cfg, rank: int, world: int, steps: int, warmup: int)
     t1.synchronize()
     ms = reduce_max(t0.elapsed_time(t1), world)
     tokens = wl.batch * wl.prompt_tokens * steps * world
-    first_tokens = [rt.device.argmax(x) for x in logits]
+    first_tokens = [int(t) for t in rt.device.argmax_last_axis(logits)]
     flops = prefill_flops(cfg, wl.prompt_tokens) * wl.batch * steps * world
     # the group's peak: every rank prefills its own prompts (replicas), so the
     # whole job's FLOP/s is measured against world x one B200's peak
     peak = (json.loads(PEAKS.read_text())["bf16_tflops"] if PEAKS.exists() else 1590.0) * world
     achieved = flops / (ms / 1000.0) / 1e12
-    program = rt._prefill[(wl.prompt_tokens, context)][0]
+    program = rt._prefill[("batched", wl.batch, wl.prompt_tokens, context)][0]
     return {"workload": wl.name, "value": tokens / (ms / 1000.0), "unit": "tokens/s",
             "ms_per_step": ms / steps, "steps": steps, "sequences_per_step": wl.batch * world,
             "first_tokens": first_tokens,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "flops_per_sequence": prefill_flops(cfg, wl.prompt_tokens),
                          "peak_source": "measured" if PEAKS.exists() else "fallback"},
-            "gpu_launches": program.launches * wl.batch * steps}
+            "gpu_launches": program.launches * steps}
 
 
 def rows_roofline(rt, rows: int, rounds: int = 3):
@@ -493,8 +494,7 @@ def llama3_measurement(rank: int, world: int, local: int, steps: int, warmup: in
     rt = tp.TensorParallelRuntime(cfg, weights, layout, batch=wl.batch, dtype=bfloat16())
     context = prompt_len + wl.decode_steps
     prompts = [list(p) for p in synthetic_prompt(cfg, prompt_len, seed=300, batch=wl.batch)]
-    rt.prefill(prompts[0], context)  # compile + capture
-    # one whole untimed batch first: the stacked caches' allocation is not timed
+    # one whole untimed batch first: compiles the batched prefill program and allocates its buffers
     tokens, caches = rt.prefill_batch(prompts, context)
     del caches
     barrier(world)

@@ -10,9 +10,9 @@ lengths), and each sequence reads and writes its own slice of the
 exactly what ``LlamaDecoderStep`` computes; only the weight reads are shared,
 which turns each Linear into a B-row matmul (the tcgen05 GEMM).
 
-``BatchedRuntime`` prefills each sequence with the ordinary batch-1 prefill
-program (llama.py:432-433 is batch 1), stacks the caches, and then steps all
-sequences together, picking each next token by ``argmax_last_axis``
+``BatchedRuntime`` prefills the prompts together (``BatchedPrefill``: the
+reference's prefill, llama.py:432-433, with the batch dimension its layers
+already carry), and then steps all sequences together, picking each next token by ``argmax_last_axis``
 (chomikgrad/lazy.py:132-134; the reference's greedy sampler takes the first
 maximum, generate_tinyllama.py:146-157).
 """
@@ -23,7 +23,7 @@ from typing import Any, List, Optional, Sequence, Tuple
 
 import numpy as np
 
-from chomikgrad.llama import LlamaConfig, LlamaDecoderStep, _rope_rotations
+from chomikgrad.llama import LlamaConfig, LlamaDecoderStep, LlamaForCausalLM, _rope_rotations
 from chomikgrad.tensor import Tensor, compile_graph, no_grad
 
 from .device import DeviceArray
@@ -92,6 +92,50 @@ class BatchedDecoderStep(GraphHelpers, LlamaDecoderStep):
         return (logits, *updated)
 
 
+class BatchedPrefill(GraphHelpers, LlamaForCausalLM):
+    """The prefill of B prompts of equal length as one graph.
+
+    The reference's ``LlamaForCausalLM`` checks for one prompt
+    (llama.py:389-396) although its layers already carry a batch dimension
+    (``_attention`` and ``_mlp`` take (batch, tokens, hidden)).  Here the
+    token matrix is (B, T): every Linear becomes one (B*T)-row GEMM over the
+    shared weights, the causal mask and the RoPE table broadcast over the
+    batch, and each prompt's caches are placed as the reference places them
+    (llama.py:411-418).  Per prompt the graph computes what the batch-1
+    prefill computes.  Returns (B, vocab) logits of each prompt's last token
+    and the (B, kv_heads, cache_length, head_size) caches.
+    """
+
+    def __init__(self, config: LlamaConfig, weights, *, batch: int, sequence_length: int, dtype: np.dtype,
+                 cache_length: int) -> None:
+        super().__init__(config, weights, sequence_length=sequence_length, dtype=dtype, cache_length=cache_length)
+        if batch <= 0:
+            raise ValueError("batch must be positive")
+        self.batch = batch
+
+    def _forward(self, token_matrix: Tensor, selector: Tensor, *, collect_cache: bool) -> Tuple[Tensor, ...]:
+        c, b, t = self.config, self.batch, self.sequence_length
+        if token_matrix.shape != (b, t):
+            raise ValueError(f"batched prefill takes ({b}, {t}) token ids")
+        if selector.shape != (1, t):
+            raise ValueError("position selector has the wrong shape")
+        hidden = self._embed(token_matrix)  # (B, T, H)
+        caches = []
+        for layer in range(c.num_hidden_layers):
+            w = f"model.layers.{layer}"
+            attended, key, value = self._attention(self._rms_norm(hidden, self.weights[f"{w}.input_layernorm.weight"]),
+                                                   layer)
+            hidden = hidden + attended
+            if collect_cache:
+                for part in (key, value):  # (B, kv, T, hd) -> (B, kv, ctx, hd) through the placement matrix
+                    caches.append((part.permute(0, 1, 3, 2) @ self.cache_placement).permute(0, 1, 3, 2))
+            normed = self._rms_norm(hidden, self.weights[f"{w}.post_attention_layernorm.weight"])
+            hidden = hidden + self._mlp(normed, layer)
+        hidden = self._rms_norm(hidden, self.weights["model.norm.weight"])
+        last = (selector @ hidden).reshape(b, c.hidden_size)  # the selector row broadcasts over the prompts
+        return (self._linear(last, self.weights["lm_head.weight"]), *caches)
+
+
 class BatchedRuntime(LlamaRuntime):
     """Prefill B prompts one by one, then decode them together."""
 
@@ -106,19 +150,13 @@ class BatchedRuntime(LlamaRuntime):
         """First token of each prompt (greedy, or sampled with ``rng``) and the stacked (B, ...) caches."""
         if len(prompts) != self.batch or len({len(p) for p in prompts}) != 1:
             raise ValueError(f"{self.batch} prompts of equal length are required")
-        import torch
-
-        firsts, per_seq = [], []
-        for prompt in prompts:
-            logits, caches = self.prefill(prompt, context)
-            firsts.append(self.sample(logits, temperature, top_k, rng))
-            per_seq.append(caches)
-        stacked = []
-        for i in range(len(per_seq[0])):
-            first = per_seq[0][i]
-            flat = torch.cat([seq[i].tensor.reshape(-1) for seq in per_seq])
-            stacked.append(DeviceArray(flat, (self.batch,) + tuple(first.shape[1:]), first.dtype))
-        return firsts, stacked
+        logits, caches = self.prefill_batched(prompts, context)  # one program for all prompts
+        if temperature == 0:
+            return [int(t) for t in self.device.argmax_last_axis(logits)], caches
+        rows = logits.tensor.reshape(logits.shape)  # the program's output buffer is flat
+        firsts = [self.sample(DeviceArray(rows[i:i + 1], (1,) + tuple(logits.shape[1:]), logits.dtype),
+                              temperature, top_k, rng) for i in range(self.batch)]
+        return firsts, caches
 
     def batched_step_inputs(self, tokens: Sequence[int], position: int, context: int) -> List[np.ndarray]:
         c = self.config

@@ -96,6 +96,34 @@ class LlamaRuntime:
             produced = program.run(bindings, synchronize=False)
         return produced[0], list(produced[1:])
 
+    def prefill_batched(self, prompts: Sequence[Sequence[int]], context: int) -> Tuple[Any, List[Any]]:
+        """B prompts of equal length as one program (``batched.BatchedPrefill``): native
+        (B, vocab) logits of each prompt's last token and 2L native (B, kv_heads, context,
+        head_size) caches.  Per prompt the same values as ``prefill``; every Linear runs as one
+        GEMM over all B * T rows."""
+        from .batched import BatchedPrefill
+
+        ids = np.asarray(prompts, dtype=np.int32)
+        if ids.ndim != 2 or ids.shape[0] == 0:
+            raise ValueError("prompts must be a non-empty list of equal-length token lists")
+        key = ("batched",) + ids.shape + (context,)
+        cached = self._prefill.get(key)
+        with no_grad():
+            if cached is None:
+                b, t = ids.shape
+                model = BatchedPrefill(self.config, self.weights, batch=b, sequence_length=t, dtype=self.dtype,
+                                       cache_length=context)
+                source = Tensor(ids, copy=False)
+                outputs = model.prefill(source, Tensor(position_selector(t - 1, t, dtype=self.dtype), copy=False))
+                program = compile_graph(*outputs, compiler=self.compiler_name, dynamic_inputs=(source,))
+                self._prefill[key] = (program, source._node)
+                bindings = None
+            else:
+                program, node = cached
+                bindings = {node: self.device.array(ids)}
+            produced = program.run(bindings, synchronize=False)
+        return produced[0], list(produced[1:])
+
     def step_inputs(self, token: int, position: int, context: int) -> List[np.ndarray]:
         """Host inputs of one decode step, built as generate_tinyllama.py:773-786 builds them."""
         return [np.asarray([[token]], dtype=np.int32), *self._position_host(position, context)]

@@ -46,7 +46,7 @@ import numpy as np
 from chomikgrad.llama import LlamaConfig, LlamaForCausalLM, _prefer_lowering, _rope_rotations, position_selector
 from chomikgrad.tensor import Tensor, compile_graph, no_grad
 
-from .batched import BatchedDecoderStep, BatchedRuntime
+from .batched import BatchedDecoderStep, BatchedPrefill, BatchedRuntime
 from .graphs import MASKED, GraphHelpers
 
 
@@ -243,6 +243,21 @@ class TensorParallelPrefill(_ShardMixin, LlamaForCausalLM):
         return self._reduce(partial), key, value
 
 
+class TensorParallelBatchedPrefill(TensorParallelPrefill):
+    """B prompts of equal length through one rank's prefill as one graph: the forward of
+    ``BatchedPrefill`` over this rank's shards (every Linear one (B*T)-row GEMM)."""
+
+    def __init__(self, config: LlamaConfig, weights: Mapping[str, Tensor], layout: ShardLayout, *, batch: int,
+                 sequence_length: int, dtype, cache_length: int, group: str = "tp") -> None:
+        super().__init__(config, weights, layout, sequence_length=sequence_length, dtype=dtype,
+                         cache_length=cache_length, group=group)
+        if batch <= 0:
+            raise ValueError("batch must be positive")
+        self.batch = batch
+
+    _forward = BatchedPrefill._forward
+
+
 class TensorParallelDecoderStep(_ShardMixin, BatchedDecoderStep):
     """One rank's batched decode step over its shards; caches are (B, kv_heads, ctx, hd) per rank.
 
@@ -387,6 +402,31 @@ class TensorParallelRuntime(BatchedRuntime):
                 selector = position_selector(ids.shape[1] - 1, ids.shape[1], dtype=self.dtype)
                 source = Tensor(ids, copy=False)
                 outputs = model.prefill(source, Tensor(selector, copy=False))
+                program = compile_graph(*outputs, compiler=self.compiler_name, dynamic_inputs=(source,))
+                self._prefill[key] = (program, source._node)
+                bindings = None
+            else:
+                program, node = cached
+                bindings = {node: self.device.array(ids)}
+            produced = program.run(bindings, synchronize=False)
+        return produced[0], list(produced[1:])
+
+    def prefill_batched(self, prompts: Sequence[Sequence[int]], context: int) -> Tuple[Any, List[Any]]:
+        """The prompts through this rank's batched prefill program: the whole (B, vocab) logits
+        and this rank's (B, kv_heads / G, context, head_size) caches."""
+        ids = np.asarray(prompts, dtype=np.int32)
+        if ids.ndim != 2 or ids.shape[0] == 0:
+            raise ValueError("prompts must be a non-empty list of equal-length token lists")
+        key = ("batched",) + ids.shape + (context,)
+        cached = self._prefill.get(key)
+        with no_grad():
+            if cached is None:
+                b, t = ids.shape
+                model = TensorParallelBatchedPrefill(self.config, self.weights, self.layout, batch=b,
+                                                     sequence_length=t, dtype=self.dtype, cache_length=context,
+                                                     group=self.group)
+                source = Tensor(ids, copy=False)
+                outputs = model.prefill(source, Tensor(position_selector(t - 1, t, dtype=self.dtype), copy=False))
                 program = compile_graph(*outputs, compiler=self.compiler_name, dynamic_inputs=(source,))
                 self._prefill[key] = (program, source._node)
                 bindings = None

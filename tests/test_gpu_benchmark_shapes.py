@@ -95,6 +95,32 @@ def test_tinyllama_prefill_of_2048_tokens(gpu):
     assert all(program._sdpa_tc(s) for s in program.plan.steps if s.name == "sdpa")
 
 
+def test_tinyllama_batched_prefill_of_2048_token_prompts(gpu):
+    """The C4 benchmark's program: four 2048-token prompts as one batched prefill (every Linear
+    one GEMM over 8192 rows).  Row 0 is the golden prompt: the reference's logits and first
+    token; every row equals its own batch-1 prefill on the GPU (token and logits, caches)."""
+    g = golden("tinyllama_prefill2048")
+    wl = WORKLOADS["tinyllama-4layer-prefill2048-bf16"]
+    rt = LlamaRuntime(wl.config, synthetic_weights(wl.config, dtype=wl.np_dtype), compiler="cuda-b200")
+    context = int(g["context"])
+    prompts = [[int(t) for t in g["prompt"]]] + [list(p) for p in synthetic_prompt(wl.config, 2048, seed=7, batch=3)]
+    logits, caches = rt.prefill_batched(prompts, context)
+    rows = rt.device.to_numpy(logits)
+    assert rows.shape == (4, wl.config.vocab_size)
+    _bf16_close(rows[:1], g["prefill_logits"])
+    tokens = [int(t) for t in rt.device.argmax_last_axis(logits)]
+    assert tokens[0] == int(g["tokens"][0])
+    batched_caches = [rt.device.to_numpy(c) for c in caches]
+    for s, prompt in enumerate(prompts):
+        one_logits, one_caches = rt.prefill(prompt, context)
+        assert rt.device.argmax(one_logits) == tokens[s]
+        _bf16_close(rows[s:s + 1], rt.device.to_numpy(one_logits))
+        for i, c in enumerate(one_caches):
+            want = np.asarray(rt.device.to_numpy(c), np.float32)
+            np.testing.assert_allclose(np.asarray(batched_caches[i][s:s + 1], np.float32), want, rtol=0,
+                                       atol=1e-3 * max(1.0, float(np.abs(want).max())), err_msg=f"row {s} cache {i}")
+
+
 def test_tinyllama_batch_of_32(gpu):
     from cuda_b200.batched import BatchedRuntime
 

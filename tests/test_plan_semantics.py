@@ -23,7 +23,7 @@ import pytest
 
 from cuda_b200 import _lib
 from cuda_b200 import tensor_parallel as tp
-from cuda_b200.batched import BatchedDecoderStep
+from cuda_b200.batched import BatchedDecoderStep, BatchedPrefill
 from chomikgrad import llama as L
 from chomikgrad.tensor import Tensor, no_grad
 from cuda_b200.models import TINY, WORKLOADS, synthetic_prompt, synthetic_weights
@@ -323,6 +323,74 @@ def test_tensor_parallel_prefill_plans_match_the_one_rank_oracle(vocab_shard):
         for i, (a, b) in enumerate(zip(got[1:], want[1:])):
             b = np.asarray(b, np.float32)[:, kv:kv + lay.kv_heads]
             np.testing.assert_allclose(a, b, rtol=0, atol=1e-4 * max(1.0, float(np.abs(b).max())), err_msg=f"cache {i}")
+
+
+# ------------------------------------------------------------------ batched prefill
+@pytest.mark.parametrize("name", ["tiny-bf16", "tiny-fp32"])
+def test_batched_prefill_plan_matches_each_prompts_prefill(name):
+    """BatchedPrefill (three prompts as one graph, every Linear a GEMM over all rows): the
+    planned program gives each prompt's batch-1 prefill -- the oracle's logits and caches of the
+    reference's LlamaForCausalLM run on that prompt alone."""
+    wl, weights = _weights(name)
+    cfg, dt = wl.config, wl.np_dtype
+    b, seq, ctx = 3, 16, 24
+    ids = np.concatenate([synthetic_prompt(cfg, seq, seed=s) for s in range(b)]).astype(np.int32)
+    selector = L.position_selector(seq - 1, seq, dtype=dt)
+    with no_grad():
+        source = Tensor(ids, copy=False)
+        outs = list(BatchedPrefill(cfg, weights, batch=b, sequence_length=seq, dtype=dt,
+                                   cache_length=ctx).prefill(source, Tensor(selector, copy=False)))
+    plan, _, got = _interpret(outs, [source], gemm_min_rows=16)
+    assert got[0].shape == (b, cfg.vocab_size)
+    for s in range(b):
+        with no_grad():
+            one = L.LlamaForCausalLM(cfg, weights, sequence_length=seq, dtype=dt, cache_length=ctx)
+            want = _oracle(list(one.prefill(Tensor(ids[s:s + 1], copy=False), Tensor(selector, copy=False))))
+        _close(got[0][s:s + 1], want[0], dt, f"logits of prompt {s}")
+        assert int(np.argmax(got[0][s])) == int(np.argmax(want[0]))
+        for i, (a, w) in enumerate(zip(got[1:], want[1:])):
+            w = np.asarray(w, np.float32)
+            np.testing.assert_allclose(np.asarray(a, np.float32)[s:s + 1], w, rtol=0,
+                                       atol=1e-4 * max(1.0, float(np.abs(w).max())), err_msg=f"prompt {s} cache {i}")
+
+
+def test_tensor_parallel_batched_prefill_plans_match_the_one_rank_oracle():
+    """Two ranks' batched prefills (two prompts): every rank's logits are the unsharded batch-1
+    prefill's, prompt by prompt, and its caches are its KV heads of that prompt's caches."""
+    config, size, b, seq, ctx = TINY, 2, 2, 16, 24
+    full_w = {k: v.astype(BF16) for k, v in synthetic_weights(config, dtype=np.float32).items()}
+    ids = np.random.default_rng(5).integers(0, config.vocab_size, (b, seq)).astype(np.int32)
+    selector = L.position_selector(seq - 1, seq, dtype=BF16)
+    wants = []
+    for s in range(b):
+        with no_grad():
+            model = L.LlamaForCausalLM(config, {k: Tensor(v) for k, v in full_w.items()}, sequence_length=seq,
+                                       dtype=BF16, cache_length=ctx)
+            wants.append(_oracle(list(model.prefill(Tensor(ids[s:s + 1]), Tensor(selector)))))
+    interpreters, layouts = [], []
+    for rank in range(size):
+        lay = tp.shard_layout(config, size, rank, vocab_shard=True)
+        with no_grad():
+            m = tp.TensorParallelBatchedPrefill(
+                config, {k: Tensor(v) for k, v in tp.shard_weights(config, full_w, lay).items()}, lay, batch=b,
+                sequence_length=seq, dtype=BF16, cache_length=ctx)
+            source = Tensor(ids)
+            outs = list(m.prefill(source, Tensor(selector)))
+        plan = _plan(outs, [source], gemm_min_rows=16)
+        kinds = Counter(s.name for s in plan.steps)
+        assert kinds["all_reduce"] == 2 * config.num_hidden_layers and kinds["all_gather"] == 1
+        interpreters.append(PlanInterpreter(plan))
+        layouts.append((lay, lay.kv_rows.start // config.head_size))
+    run_ranks(interpreters)
+    for it, (lay, kv) in zip(interpreters, layouts):
+        got = it.outputs()
+        for s, want in enumerate(wants):
+            _close(got[0][s:s + 1], want[0], BF16, f"logits of prompt {s}")
+            assert int(np.argmax(got[0][s])) == int(np.argmax(want[0]))
+            for i, (a, w) in enumerate(zip(got[1:], want[1:])):
+                w = np.asarray(w, np.float32)[:, kv:kv + lay.kv_heads]
+                np.testing.assert_allclose(np.asarray(a, np.float32)[s:s + 1], w, rtol=0,
+                                           atol=1e-4 * max(1.0, float(np.abs(w).max())), err_msg=f"cache {i}")
 
 
 # ------------------------------------------------------------------ the interpreter itself
