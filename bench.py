@@ -96,6 +96,11 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a while to start: the timed region begins after its first
+            # sample, so a short region still gets samples (bounded: 5 s)
+            deadline = time.time() + 5.0
+            while not self.lines and self.proc.poll() is None and time.time() < deadline:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
