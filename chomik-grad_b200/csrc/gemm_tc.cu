@@ -262,9 +262,46 @@ __global__ void __launch_bounds__(256) rms_planes_kernel(const void* a, int a_dt
   __shared__ float red[8];
   const long long r = blockIdx.x;
   const int width = static_cast<int>(k);
-  for (int i = threadIdx.x; i < width; i += blockDim.x) row[i] = load_as_f32(a, r * lda + i, a_dtype);
+  // four elements per thread and access where alignment allows (same arithmetic per element)
+  const bool vec = a_dtype == CB_F32 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && lda % 4 == 0 && k % 4 == 0 &&
+                   (w_dtype == CB_BF16 || w_dtype == CB_F32) && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  if (vec) {
+    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a) + r * lda);
+    for (int q = threadIdx.x; q < width / 4; q += blockDim.x) reinterpret_cast<float4*>(row)[q] = src[q];
+  } else {
+    for (int i = threadIdx.x; i < width; i += blockDim.x) row[i] = load_as_f32(a, r * lda + i, a_dtype);
+  }
   __syncthreads();
   const float d = norm_finish_d(n, norm_block_sum(n, row, width, red));
+  if (vec) {
+    __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(hi + r * k);
+    __nv_bfloat162* l2 = lo != nullptr ? reinterpret_cast<__nv_bfloat162*>(lo + r * k) : nullptr;
+    for (int q = threadIdx.x; q < width / 4; q += blockDim.x) {
+      float wv[4];
+      if (w_dtype == CB_BF16) {
+        const uint2 wb = reinterpret_cast<const uint2*>(w)[q];
+        wv[0] = __uint_as_float(wb.x << 16);
+        wv[1] = __uint_as_float(wb.x & 0xffff0000u);
+        wv[2] = __uint_as_float(wb.y << 16);
+        wv[3] = __uint_as_float(wb.y & 0xffff0000u);
+      } else {
+        const float4 wf = reinterpret_cast<const float4*>(w)[q];
+        wv[0] = wf.x; wv[1] = wf.y; wv[2] = wf.z; wv[3] = wf.w;
+      }
+      const float4 x = reinterpret_cast<const float4*>(row)[q];
+      const float v0 = norm_apply(n, x.x, d, wv[0], dt_out), v1 = norm_apply(n, x.y, d, wv[1], dt_out);
+      const float v2 = norm_apply(n, x.z, d, wv[2], dt_out), v3 = norm_apply(n, x.w, d, wv[3], dt_out);
+      const __nv_bfloat162 h01 = __floats2bfloat162_rn(v0, v1), h23 = __floats2bfloat162_rn(v2, v3);
+      h2[2 * q] = h01;
+      h2[2 * q + 1] = h23;
+      if (l2 != nullptr) {
+        const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+        l2[2 * q] = __floats2bfloat162_rn(__fsub_rn(v0, f01.x), __fsub_rn(v1, f01.y));
+        l2[2 * q + 1] = __floats2bfloat162_rn(__fsub_rn(v2, f23.x), __fsub_rn(v3, f23.y));
+      }
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < width; i += blockDim.x) {
     const float v = norm_apply(n, row[i], d, load_as_f32(w, i, w_dtype), dt_out);
     const __nv_bfloat16 h = __float2bfloat16_rn(v);
