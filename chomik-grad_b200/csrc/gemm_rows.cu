@@ -282,25 +282,52 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           const float4* base = reinterpret_cast<const float4*>(p.partial + tile_flat * p.max_parts * NB * kWTile);
           const int g = r & 31, b0 = r >> 5;
           const int row4 = tile * kWTile + 4 * g;
+          // The parts are summed in part order; the loads of kBatch parts
+          // (and the residual values) are issued together, so a tile split
+          // P ways waits for ceil(P / kBatch) L2 round trips, not P.
+          constexpr int kBatch = 4;
+          auto part_loads = [&](int q, int bs, float4* v) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int bb = bs + 4 * j;
+              v[j] = bb < p.rows ? __ldcg(base + ((static_cast<long long>(q) * NB + bb) * kWTile) / 4 + g)
+                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+          };
+          auto part_add = [](float4* acc, const float4* v) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              acc[j].x += v[j].x;
+              acc[j].y += v[j].y;
+              acc[j].z += v[j].z;
+              acc[j].w += v[j].w;
+            }
+          };
           for (int bs = b0; bs < p.rows; bs += 32) {
+            float res[8][4];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int bb = bs + 4 * j;
+              const float* rr = p.residual != nullptr && bb < p.rows
+                                    ? p.residual + static_cast<long long>(bb) * p.ldr : nullptr;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) res[j][e] = rr != nullptr && row4 + e < n ? rr[row4 + e] : 0.0f;
+            }
             float4 acc[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int q = 0; q < parts; ++q) {
+            int q = 0;
+            for (; q + kBatch <= parts; q += kBatch) {
+              float4 v[kBatch][8];
+#pragma unroll
+              for (int u = 0; u < kBatch; ++u) part_loads(q + u, bs, v[u]);
+#pragma unroll
+              for (int u = 0; u < kBatch; ++u) part_add(acc, v[u]);
+            }
+            for (; q < parts; ++q) {
               float4 v[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int bb = bs + 4 * j;
-                v[j] = bb < p.rows ? __ldcg(base + ((static_cast<long long>(q) * NB + bb) * kWTile) / 4 + g)
-                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-              }
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                acc[j].x += v[j].x;
-                acc[j].y += v[j].y;
-                acc[j].z += v[j].z;
-                acc[j].w += v[j].w;
-              }
+              part_loads(q, bs, v);
+              part_add(acc, v);
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -308,10 +335,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
               if (bb >= p.rows) continue;
               float* o = out + static_cast<long long>(bb) * ldo;
               const float a4[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
-              const float* rr = p.residual != nullptr ? p.residual + static_cast<long long>(bb) * p.ldr : nullptr;
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                if (row4 + e < n) o[row4 + e] = rr != nullptr ? __fadd_rn(rr[row4 + e], a4[e]) : a4[e];
+                if (row4 + e < n) o[row4 + e] = p.residual != nullptr ? __fadd_rn(res[j][e], a4[e]) : a4[e];
             }
           }
           if (r == 0) p.counters[tile_flat] = 0u;

@@ -5,6 +5,7 @@
     python kernel_bench.py sdpa_query [--batch 32 --heads 32 --kv 4 --tokens 768 --hd 64]
     python kernel_bench.py batched   [--workload tinyllama-bf16-bs32 --steps 20 --prompt 64]
     python kernel_bench.py sample    [--rows 1 --width 32000 --top-k 50]
+    python kernel_bench.py gemm_rows [--batch 32]
 
 Each prints CUDA-event times (warm, averaged over --reps launches on the
 current stream).  ``batched`` wraps the timed graph replays in
@@ -181,9 +182,86 @@ def batched(args) -> None:
     print(f"{wl.name}: graph replay {step:.3f} ms per step, {wl.batch / step * 1000:.0f} tokens/s")
 
 
+ROWS_SHAPES = {  # TinyLlama decode Linears: (weights' row counts, k, x prologue)
+    "qkv": ((2048, 256, 256), 2048, "rms"),
+    "o": ((2048,), 2048, "plain"),
+    "gateup": ((5632, 5632), 2048, "rms"),
+    "down": ((2048,), 5632, "swiglu"),
+}
+
+
+def gemm_rows(args) -> None:
+    """cb_gemm_rows at the batched decode step's four Linear shapes, one after another.
+
+    Each shape cycles through enough weight copies (> 256 MB) that every launch
+    streams its weights from HBM, as the step does; x prologues as in the step
+    (RMSNorm before q/k/v and gate/up, SwiGLU before down).  Prints the CUDA-event
+    time per launch and the weight bytes over it.
+    """
+    import torch
+
+    from cuda_b200 import _lib
+
+    lib = _lib.load()
+    rows = args.batch
+    for name, (ns, k, mode) in ROWS_SHAPES.items():
+        wbytes = sum(ns) * k * 2
+        copies = max(2, -(-256 * 2 ** 20 // wbytes))
+        ws = [[(torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16) for n in ns] for _ in range(copies)]
+        x = torch.randn(rows, k, device="cuda")
+        x2 = torch.randn(rows, k, device="cuda")
+        norm_w = torch.ones(k, device="cuda", dtype=torch.bfloat16)
+        outs = [torch.empty(rows, n, device="cuda") for n in ns]
+        residual = torch.randn(rows, ns[0], device="cuda")
+        flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+        launches = []
+        for c in range(copies):
+            a = _lib.GemmRowsArgs()
+            a.x, a.x_dtype, a.ldx = x.data_ptr(), _lib.F32, k
+            a.rows, a.k, a.n_w, a.splits, a.pdl = rows, k, len(ns), 0, 1
+            for i, (w, o) in enumerate(zip(ws[c], outs)):
+                a.w[i], a.w_rows[i], a.out[i], a.ldo[i] = w.data_ptr(), w.shape[0], o.data_ptr(), o.stride(0)
+            if mode == "rms":
+                a.x_mode, a.norm_w, a.norm_w_dtype = _lib.ROWS_X_RMS, norm_w.data_ptr(), _lib.BF16
+                a.divisor, a.eps = float(k), 1e-5
+                a.dt_sq = a.dt_sum = a.dt_mean = a.dt_t = a.dt_d = a.dt_y = _lib.F32
+                a.dt_out = _lib.BF16
+            elif mode == "swiglu":
+                a.x_mode, a.x2, a.x2_dtype, a.ldx2 = _lib.ROWS_X_SWIGLU, x2.data_ptr(), _lib.F32, k
+            if len(ns) == 1:
+                a.residual, a.ldr = residual.data_ptr(), residual.stride(0)
+            scratch = torch.empty(max(lib.cb_gemm_rows_scratch(ctypes.byref(a)), 16), dtype=torch.uint8,
+                                  device="cuda")
+            counters = torch.zeros(max(lib.cb_gemm_rows_counters(ctypes.byref(a)), 1), dtype=torch.int32,
+                                   device="cuda")
+            a.scratch, a.counters, a.error_flag = scratch.data_ptr(), counters.data_ptr(), flag.data_ptr()
+            launches.append((a, scratch, counters))
+        it = iter(range(10 ** 9))
+
+        def run():
+            _lib.call("cb_gemm_rows", ctypes.byref(launches[next(it) % copies][0]),
+                      torch.cuda.current_stream().cuda_stream)
+
+        ms = _timed(run, args.reps)
+        # the same launches replayed from a CUDA graph (no host time between them, as in the decode step)
+        run()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(copies):
+                run()
+        graph_ms = _timed(graph.replay, max(1, args.reps // copies)) / copies
+        assert int(flag.item()) == 0, f"cb_gemm_rows error flag {int(flag.item())}"
+        print(f"gemm_rows {name}: rows {rows} n {ns} k {k} ({mode}): {ms * 1000:.1f} us per launch from the "
+              f"host, {graph_ms * 1000:.1f} us in a graph; {wbytes / 1e6:.1f} MB weights, "
+              f"{wbytes / (graph_ms / 1000) / 1e9:.0f} GB/s in the graph")
+        del ws, launches, graph
+        torch.cuda.empty_cache()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("kernel", choices=("sdpa_tc", "gemm_tc", "sdpa_query", "batched", "sample"))
+    parser.add_argument("kernel", choices=("sdpa_tc", "gemm_tc", "sdpa_query", "batched", "sample", "gemm_rows"))
     parser.add_argument("--reps", type=int, default=20)
     parser.add_argument("--tokens", type=int, default=None)
     parser.add_argument("--heads", type=int, default=32)
@@ -211,7 +289,7 @@ def main() -> None:
     if args.tokens is None:
         args.tokens = 2048 if args.kernel == "sdpa_tc" else 768
     {"sdpa_tc": sdpa_tc, "gemm_tc": gemm_tc, "sdpa_query": sdpa_query, "batched": batched,
-     "sample": sample}[args.kernel](args)
+     "sample": sample, "gemm_rows": gemm_rows}[args.kernel](args)
 
 
 if __name__ == "__main__":
