@@ -15,7 +15,8 @@
 //  * warp 4 streams its range with TMA (the weight chunk and x's bf16 hi/lo
 //    planes, split once by a pre-pass) into a ring of stages;
 //  * warp 5 issues tcgen05.mma (kind::f16, M=128, N=rows padded, K=16)
-//    W.x_hi + W.x_lo into one of two TMEM accumulators, switching at each
+//    W.x_hi + W.x_lo (W.x_hi alone when x is exactly bf16, its lo plane
+//    zero) into one of two TMEM accumulators, switching at each
 //    tile boundary of the range (a "segment"), so the epilogue of one tile
 //    overlaps the MMAs of the next;
 //  * warps 0-3 read each finished accumulator (warp w owns weight rows
@@ -58,6 +59,7 @@ struct RowsParams {
   int kchunks;         // 64-wide K chunks per tile
   long long total;     // tiles * kchunks
   int max_parts;       // partial slots per tile
+  int lo_plane;        // 0: x is exactly bf16 (its lo plane is zero): no lo loads, no lo MMAs
   float* partial;      // (tiles, max_parts, NB, 128) float32
   unsigned* counters;  // one per tile, 0 between launches
   int* error_flag;
@@ -138,11 +140,12 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         const int kx = static_cast<int>(f % p.kchunks) * kChunk;
         unsigned char* st = smem + s * G::kStage;
         tma_load_2d(st + G::kW, &map_xh, kx, 0, full + s);
-        tma_load_2d(st + G::kW + G::kX, &map_xl, kx, 0, full + s);
+        if (p.lo_plane) tma_load_2d(st + G::kW + G::kX, &map_xl, kx, 0, full + s);
       };
       const long long pre = f1 - f0 < G::kStages ? f1 - f0 : G::kStages;
+      const uint32_t stage_bytes = static_cast<uint32_t>(p.lo_plane ? G::kStage : G::kW + G::kX);
       for (long long j = 0; j < pre; ++j) {
-        mbar_arrive_expect_tx(full + j, static_cast<uint32_t>(G::kStage));
+        mbar_arrive_expect_tx(full + j, stage_bytes);
         weight_load(f0 + j, static_cast<int>(j));
       }
       pdl_wait();
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           *abort = 1;
           break;
         }
-        mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(G::kStage));
+        mbar_arrive_expect_tx(full + s, stage_bytes);
         weight_load(f, s);
         x_load(f, s);
       }
@@ -197,7 +200,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           for (int kk = 0; kk < kChunk / kUmmaK; ++kk) {
             const uint64_t dw = sw128_desc(st + kk * kUmmaK * 2);
             umma_bf16(d, dw, sw128_desc(st + G::kW + kk * kUmmaK * 2), idesc, (f != a || kk != 0) ? 1u : 0u);
-            umma_bf16(d, dw, sw128_desc(st + G::kW + G::kX + kk * kUmmaK * 2), idesc, 1u);
+            if (p.lo_plane) umma_bf16(d, dw, sw128_desc(st + G::kW + G::kX + kk * kUmmaK * 2), idesc, 1u);
           }
           umma_commit(empty + s);
         }
@@ -473,6 +476,12 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
   p.kchunks = pl.kchunks;
   p.total = pl.total;
   p.max_parts = pl.max_parts;
+  // x that is exactly bf16 -- given as bf16, or the RMS prologue rounding to
+  // bf16 -- splits into a zero lo plane: its MMAs would add exact zeros.  The
+  // single MMA-issuing thread is what bounds a few-row GEMM's stream (each
+  // tcgen05.mma takes it tens of cycles to issue), so they are skipped.
+  p.lo_plane = !((a.x_mode == CB_ROWS_X_RMS && a.dt_out == CB_BF16) ||
+                 (a.x_mode == CB_ROWS_X_PLAIN && a.x_dtype == CB_BF16));
   // partials after the planes, 16-byte aligned
   const uintptr_t after = reinterpret_cast<uintptr_t>(lo + pl.plane_elems);
   p.partial = reinterpret_cast<float*>((after + 15) & ~static_cast<uintptr_t>(15));

@@ -75,12 +75,17 @@ __device__ __forceinline__ bool mbar_try_wait_short(uint64_t* bar, uint32_t pari
 }
 
 // Wait for the phase with the given parity to complete; false on timeout.
+// The clock is read every 256 polls, starting at the first such read (a
+// %globaltimer read is slow; most waits end within their first polls).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitNs) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
-  for (uint32_t i = 1; i < kWaitPolls; ++i) {
+  uint64_t start = 0;
+  for (uint32_t i = 0; i < kWaitPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_ns() - start > limit_ns) return false;
+    if ((i & 255u) == 255u) {
+      const uint64_t now = global_ns();
+      if (start == 0) start = now;
+      else if (now - start > limit_ns) return false;
+    }
   }
   return false;
 }

@@ -142,21 +142,33 @@ __device__ __forceinline__ void reg_fence(float* x) {
 
 // mbarrier wait that also gives up once *abort != 0 (bounded like mbar_wait;
 // no suspend hint, so a waiter resumes as soon as the phase completes).
+// The clock (%globaltimer) is read only every 64 polls, starting at the first
+// such read: a read costs about half a microsecond, and a wait whose phase has
+// already completed (a ring stage that landed) must cost one poll.
 __device__ inline bool wait_or_abort(uint64_t* bar, uint32_t parity, const volatile int* abort) {
-  const uint64_t start = global_ns();
+  uint64_t start = 0;
   for (uint32_t i = 0; i < kWaitPolls; ++i) {
     if (mbar_try_wait_short(bar, parity)) return true;
-    if ((i & 63u) == 63u && (*abort != 0 || global_ns() - start > kWaitNs)) return false;
+    if ((i & 63u) == 63u) {
+      if (*abort != 0) return false;
+      const uint64_t now = global_ns();
+      if (start == 0) start = now;
+      else if (now - start > kWaitNs) return false;
+    }
   }
   return false;
 }
 
 // Bounded wait without an abort flag (drains, teardown).
 __device__ inline bool wait_short(uint64_t* bar, uint32_t parity) {
-  const uint64_t start = global_ns();
+  uint64_t start = 0;
   for (uint32_t i = 0; i < kWaitPolls; ++i) {
     if (mbar_try_wait_short(bar, parity)) return true;
-    if ((i & 255u) == 255u && global_ns() - start > kWaitNs) return false;
+    if ((i & 255u) == 255u) {
+      const uint64_t now = global_ns();
+      if (start == 0) start = now;
+      else if (now - start > kWaitNs) return false;
+    }
   }
   return false;
 }

@@ -204,7 +204,8 @@ def gemm_rows(args) -> None:
 
     lib = _lib.load()
     rows = args.batch
-    for name, (ns, k, mode) in ROWS_SHAPES.items():
+    shapes = {n: s for n, s in ROWS_SHAPES.items() if n in args.shapes}
+    for name, (ns, k, mode), splits in ((n, s, c) for n, s in shapes.items() for c in args.splits):
         wbytes = sum(ns) * k * 2
         copies = max(2, -(-256 * 2 ** 20 // wbytes))
         ws = [[(torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16) for n in ns] for _ in range(copies)]
@@ -218,7 +219,7 @@ def gemm_rows(args) -> None:
         for c in range(copies):
             a = _lib.GemmRowsArgs()
             a.x, a.x_dtype, a.ldx = x.data_ptr(), _lib.F32, k
-            a.rows, a.k, a.n_w, a.splits, a.pdl = rows, k, len(ns), 0, 1
+            a.rows, a.k, a.n_w, a.splits, a.pdl = rows, k, len(ns), splits, 1
             for i, (w, o) in enumerate(zip(ws[c], outs)):
                 a.w[i], a.w_rows[i], a.out[i], a.ldo[i] = w.data_ptr(), w.shape[0], o.data_ptr(), o.stride(0)
             if mode == "rms":
@@ -252,7 +253,7 @@ def gemm_rows(args) -> None:
                 run()
         graph_ms = _timed(graph.replay, max(1, args.reps // copies)) / copies
         assert int(flag.item()) == 0, f"cb_gemm_rows error flag {int(flag.item())}"
-        print(f"gemm_rows {name}: rows {rows} n {ns} k {k} ({mode}): {ms * 1000:.1f} us per launch from the "
+        print(f"gemm_rows {name}: rows {rows} n {ns} k {k} ({mode}) ctas {splits or 'all'}: {ms * 1000:.1f} us per launch from the "
               f"host, {graph_ms * 1000:.1f} us in a graph; {wbytes / 1e6:.1f} MB weights, "
               f"{wbytes / (graph_ms / 1000) / 1e9:.0f} GB/s in the graph")
         del ws, launches, graph
@@ -263,6 +264,10 @@ def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("kernel", choices=("sdpa_tc", "gemm_tc", "sdpa_query", "batched", "sample", "gemm_rows"))
     parser.add_argument("--reps", type=int, default=20)
+    parser.add_argument("--splits", type=int, nargs="+", default=[0],
+                        help="gemm_rows: CTA counts to time (0: one per SM, the runtime's choice)")
+    parser.add_argument("--shapes", nargs="+", default=list(ROWS_SHAPES), choices=list(ROWS_SHAPES),
+                        help="gemm_rows: which Linear shapes")
     parser.add_argument("--tokens", type=int, default=None)
     parser.add_argument("--heads", type=int, default=32)
     parser.add_argument("--kv", type=int, default=None)
