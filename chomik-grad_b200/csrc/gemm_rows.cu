@@ -10,8 +10,9 @@
 //
 // The weight stream is cut into 64-wide K chunks of 128-row tiles and the
 // flattened (tile, chunk) sequence is split into one contiguous, equal range
-// per CTA (one persistent CTA per SM), so every SM streams the same number
-// of bytes without a break:
+// per CTA (one persistent CTA per SM; two, each with half the ring, for
+// weights of 32 MB and more), so every SM streams the same number of bytes
+// without a break:
 //  * warp 4 streams its range with TMA (the weight chunk and x's bf16 hi/lo
 //    planes, split once by a pre-pass) into a ring of stages;
 //  * warp 5 issues tcgen05.mma (kind::f16, M=128, N=rows padded, K=16)
@@ -37,12 +38,16 @@ using namespace tc;
 constexpr int kRowsThreads = 192;  // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
 constexpr int kWTile = 128;        // weight rows per tile = TMEM lanes
 
-template <int NB>
+// CTAS: resident CTAs per SM.  Two CTAs of half the ring stream a large
+// weight faster than one (each CTA's stage hand-offs bound its own stream:
+// about 32 GB/s per CTA); small GEMMs keep one, whose tiles split into fewer
+// parts.
+template <int NB, int CTAS = 1>
 struct RowsShape {
   static constexpr int kW = kWTile * kChunk * 2;  // weight chunk bytes
   static constexpr int kX = NB * kChunk * 2;      // one x plane chunk
   static constexpr int kStage = kW + 2 * kX;
-  static constexpr int kStages = 200 * 1024 / kStage;
+  static constexpr int kStages = (CTAS == 2 ? 100 : 200) * 1024 / kStage;
   static constexpr int kSmem = kStages * kStage + 1024;
   static constexpr int kAcc = NB < 32 ? 32 : NB;  // columns of one accumulator
   static constexpr int kTmemCols = 2 * kAcc;
@@ -76,12 +81,12 @@ __device__ __forceinline__ void set_flag(int* flag, int code) {
   if (flag != nullptr) atomicCAS(flag, 0, code);
 }
 
-template <int NB>
-__global__ void __launch_bounds__(kRowsThreads, 1)
+template <int NB, int CTAS>
+__global__ void __launch_bounds__(kRowsThreads, CTAS)
     gemm_rows_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
                      const __grid_constant__ CUtensorMap map_w2, const __grid_constant__ CUtensorMap map_xh,
                      const __grid_constant__ CUtensorMap map_xl, const __grid_constant__ RowsParams p) {
-  using G = RowsShape<NB>;
+  using G = RowsShape<NB, CTAS>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -288,7 +293,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
           // The parts are summed in part order; the loads of kBatch parts
           // (and the residual values) are issued together, so a tile split
           // P ways waits for ceil(P / kBatch) L2 round trips, not P.
-          constexpr int kBatch = 4;
+          constexpr int kBatch = CTAS == 2 ? 2 : 4;  // two CTAs per SM: 168 registers per thread
           auto part_loads = [&](int q, int bs, float4* v) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -404,10 +409,13 @@ __global__ void __launch_bounds__(1024) rows_rms_planes_kernel(const void* x, in
     split_store(norm_apply(n, row[i], d, load_as_f32(w, i, w_dtype), dt_out), hi, lo, r * k + i);
 }
 
+constexpr long long kTwoCtaBytes = 32LL << 20;
+
 int padded_rows(long long rows) { return rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256; }
 
 struct RowsPlan {
   int nb, tiles, kchunks, grid, max_parts;
+  int ctas;  // resident CTAs per SM
   long long total, plane_elems, partial_floats;
 };
 
@@ -420,8 +428,13 @@ RowsPlan plan_rows(const cb_gemm_rows_args& a, int sms) {
   r.kchunks = static_cast<int>((a.k + kChunk - 1) / kChunk);
   for (int i = 0; i < a.n_w; ++i) r.tiles += static_cast<int>((a.w_rows[i] + kWTile - 1) / kWTile);
   r.total = static_cast<long long>(r.tiles) * r.kchunks;
-  // one persistent CTA per SM (a.splits > 0: that many CTAs), each streaming an equal range
-  long long grid = a.splits > 0 ? a.splits : sms;
+  // persistent CTAs, each streaming an equal range: two per SM for at least
+  // kTwoCtaBytes of weights (measured: 12-18 % faster at 46-235 MB, slower
+  // at 23 MB and below), else one (a.splits > 0: that many CTAs)
+  long long bytes = 0;
+  for (int i = 0; i < a.n_w; ++i) bytes += a.w_rows[i] * a.k * 2;
+  r.ctas = r.nb <= 64 && bytes >= kTwoCtaBytes ? 2 : 1;
+  long long grid = a.splits > 0 ? a.splits : static_cast<long long>(r.ctas) * sms;
   if (grid > r.total) grid = r.total;
   if (grid < 1) grid = 1;
   r.grid = static_cast<int>(grid);
@@ -435,9 +448,9 @@ RowsPlan plan_rows(const cb_gemm_rows_args& a, int sms) {
   return r;
 }
 
-template <int NB>
+template <int NB, int CTAS>
 int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) {
-  using G = RowsShape<NB>;
+  using G = RowsShape<NB, CTAS>;
   __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(a.scratch);
   __nv_bfloat16* lo = hi + pl.plane_elems;
   if (a.x_mode == CB_ROWS_X_RMS) {
@@ -489,7 +502,7 @@ int launch_rows(const cb_gemm_rows_args& a, const RowsPlan& pl, cudaStream_t s) 
   p.error_flag = a.error_flag;
   p.residual = a.residual;
   p.ldr = a.ldr;
-  auto kernel = gemm_rows_kernel<NB>;
+  auto kernel = gemm_rows_kernel<NB, CTAS>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
   if (e == cudaSuccess)
     e = launch(kernel, dim3(static_cast<unsigned>(pl.grid)), dim3(kRowsThreads), static_cast<size_t>(G::kSmem), s,
@@ -558,11 +571,11 @@ int cb_gemm_rows(const cb_gemm_rows_args* a, cb_stream_t stream) {
   CB_REQUIRE(pl.total < (1LL << 40) && pl.tiles < (1 << 30), "gemm_rows: too many tiles");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (pl.nb) {
-    case 16: return launch_rows<16>(*a, pl, s);
-    case 32: return launch_rows<32>(*a, pl, s);
-    case 64: return launch_rows<64>(*a, pl, s);
-    case 128: return launch_rows<128>(*a, pl, s);
-    default: return launch_rows<256>(*a, pl, s);
+    case 16: return pl.ctas == 2 ? launch_rows<16, 2>(*a, pl, s) : launch_rows<16, 1>(*a, pl, s);
+    case 32: return pl.ctas == 2 ? launch_rows<32, 2>(*a, pl, s) : launch_rows<32, 1>(*a, pl, s);
+    case 64: return pl.ctas == 2 ? launch_rows<64, 2>(*a, pl, s) : launch_rows<64, 1>(*a, pl, s);
+    case 128: return launch_rows<128, 1>(*a, pl, s);
+    default: return launch_rows<256, 1>(*a, pl, s);
   }
 }
 
