@@ -663,37 +663,24 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
   CB_REQUIRE(a->kv_dtype == CB_F32 || a->kv_dtype == CB_BF16, "decode attention: caches must be float32 or bfloat16");
   const size_t smem = static_cast<size_t>(chunk_smem_bytes(group, a->head_size, a->kv_dtype));
   CB_REQUIRE(smem <= 200 * 1024, "decode attention: too many query heads per KV head");
-  // about one wave of resident CTAs (4 per SM): each CTA takes a range of
-  // consecutive chunks of its (sequence, KV head)
   const long long groups = batch * a->kv_heads;
   const bool narrow = group <= 8;  // 128-thread CTAs (two heads per warp past four), twice as many per SM
-  long long per_group = (narrow ? 8LL : 4LL) * sm_count() / groups;
-  if (per_group < 1) per_group = 1;
-  if (per_group > splits) per_group = splits;
-  const long long chunks = (splits + per_group - 1) / per_group;
-  const long long ctas = (splits + chunks - 1) / chunks;
-  const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(a->kv_heads), static_cast<unsigned>(batch));
-  const int per_cta = static_cast<int>(chunks);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaSuccess;
-#define CB_BATCHED_CASE(HD, HPW)                                                                          \
-  {                                                                                                       \
-    auto kernel = a->kv_dtype == CB_BF16                                                                \
-                      ? (narrow ? decode_attention_batched_kernel<HD, HPW, uint16_t, 128>                \
-                                : decode_attention_batched_kernel<HD, HPW, uint16_t, 256>)               \
-                      : (narrow ? decode_attention_batched_kernel<HD, HPW, float, 128>                   \
-                                : decode_attention_batched_kernel<HD, HPW, float, 256>);                 \
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
-    if (e == cudaSuccess) kernel<<<grid, narrow ? 128 : 256, smem, s>>>(*a, qkv_stride, per_cta);          \
-  }
+  const int threads = narrow ? 128 : 256;
+  using BatchedKernel = void (*)(const cb_decode_attention_args, long long, int);
+  BatchedKernel kernel = nullptr;
+#define CB_BATCHED_PICK(HD, HPW)                                                                          \
+  kernel = a->kv_dtype == CB_BF16 ? (narrow ? decode_attention_batched_kernel<HD, HPW, uint16_t, 128>       \
+                                            : decode_attention_batched_kernel<HD, HPW, uint16_t, 256>)      \
+                                  : (narrow ? decode_attention_batched_kernel<HD, HPW, float, 128>          \
+                                            : decode_attention_batched_kernel<HD, HPW, float, 256>);
 #define CB_BATCHED_HD(HD)            \
   case HD:                           \
     if (group <= 4)                  \
-      CB_BATCHED_CASE(HD, 1)         \
+      CB_BATCHED_PICK(HD, 1)         \
     else if (group <= 16)            \
-      CB_BATCHED_CASE(HD, 2)         \
+      CB_BATCHED_PICK(HD, 2)         \
     else                             \
-      CB_BATCHED_CASE(HD, 4)         \
+      CB_BATCHED_PICK(HD, 4)         \
     break;
   switch (a->head_size) {
     CB_BATCHED_HD(32)
@@ -702,7 +689,41 @@ int cb_decode_attention_batched(const cb_decode_attention_args* a, long long bat
     CB_BATCHED_HD(256)
   }
 #undef CB_BATCHED_HD
-#undef CB_BATCHED_CASE
+#undef CB_BATCHED_PICK
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  // Each CTA takes a range of consecutive chunks of its (sequence, KV head).
+  // The range length minimises waves x (chunks per CTA + one chunk's worth of
+  // per-CTA set-up and merge) over the CTAs resident at once -- shared
+  // memory, not threads, bounds them at head size 128 -- so that no second
+  // wave runs a few CTAs while the other SMs idle.
+  static thread_local BatchedKernel cached_kernel = nullptr;
+  static thread_local size_t cached_smem = 0;
+  static thread_local int cached_resident = 0;
+  if (e == cudaSuccess && (kernel != cached_kernel || smem != cached_smem)) {
+    int resident = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kernel, threads, smem);
+    cached_kernel = kernel;
+    cached_smem = smem;
+    cached_resident = resident > 0 ? resident : 1;
+  }
+  const long long capacity = static_cast<long long>(cached_resident) * sm_count();
+  long long chunks = splits, best_cost = -1, best_waves = 0;
+  for (long long c = 1; c <= splits; ++c) {
+    const long long ctas_per_group = (splits + c - 1) / c;
+    if (c > 1 && (splits + c - 2) / (c - 1) == ctas_per_group) continue;  // same CTAs, longer ranges
+    const long long waves = (groups * ctas_per_group + capacity - 1) / capacity;
+    const long long cost = waves * (c + 1);
+    if (best_cost < 0 || cost < best_cost || (cost == best_cost && waves < best_waves)) {
+      best_cost = cost;
+      best_waves = waves;
+      chunks = c;
+    }
+  }
+  const long long ctas = (splits + chunks - 1) / chunks;
+  const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(a->kv_heads), static_cast<unsigned>(batch));
+  const int per_cta = static_cast<int>(chunks);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (e == cudaSuccess) kernel<<<grid, threads, smem, s>>>(*a, qkv_stride, per_cta);
   if (e != cudaSuccess) {
     set_error("cb_decode_attention_batched: %s", cudaGetErrorString(e));
     return CB_ERR_CUDA;
